@@ -1,0 +1,104 @@
+/* strands-decider B200: the C ABI of the sequence-mixing forward.
+ *
+ * The drop-in boundary for the reference's torso engine (strands-decider-rs, `src/engine.rs`): a
+ * Rust host binds these with `extern "C"` declarations in place of
+ * `Engine::load` / `Engine::forward` / `Snapshot`, and the rest of `Decider` (tokenizer, prompt,
+ * head, `ask_all`) stays as it is. Plain pointers and sizes only; host buffers unless a name says
+ * `dev`. Every call returns SD_OK or a negative code; the message of the last failure is in
+ * sd_engine_last_error(engine) (or sd_last_error() for calls without an engine), as the
+ * reference's `Error(String)` (`src/lib.rs:23-44`) carries it. An engine is used by one host thread
+ * at a time (the reference's `&mut self`, `src/engine.rs:529`); engines on different GPUs run
+ * concurrently.
+ */
+#ifndef SD_B200_H
+#define SD_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SD_OK 0
+#define SD_ERR_INVALID (-1) /* bad argument: context, row range, token id (`src/engine.rs:530-537`) */
+#define SD_ERR_IO (-2)      /* a model file is missing or short */
+#define SD_ERR_FORMAT (-3)  /* manifest/tensor format not supported (`src/engine.rs:245-250`) */
+#define SD_ERR_CUDA (-4)    /* a CUDA call failed (including out of memory) */
+#define SD_ERR_KERNEL (-5)  /* a kernel reported an error (a bounded wait ran out, a bad shape) */
+
+#define SD_CONTEXT 4096 /* tokens of KV cache and RoPE table (`src/engine.rs:16`) */
+
+typedef struct sd_engine sd_engine;
+typedef struct sd_snapshot sd_snapshot;
+typedef struct sd_head sd_head;
+typedef struct sd_qweight sd_qweight;
+
+/* Replaces `Engine::load(dir, &Manifest)` (`src/engine.rs:175-303`): reads `manifest.json`, the
+ * weight shards and the embedding rows of a model directory onto GPU `device`. */
+int sd_engine_create(const char* model_dir, int device, sd_engine** out);
+void sd_engine_destroy(sd_engine* e);
+/* `Engine::hidden_size` (`src/engine.rs:305-307`). */
+int sd_engine_hidden_size(const sd_engine* e);
+const char* sd_engine_last_error(const sd_engine* e);
+const char* sd_last_error(void);
+
+/* Replaces `Engine::forward(ids, rows, cache, keep, timed)` (`src/engine.rs:529-662`): runs the torso
+ * over `n_ids` new tokens after the prefix in `cache` (NULL: none), writes the final hidden rows
+ * `rows` (indices into ids) to `hidden_out` [n_rows][hidden_size] f32 and, when `keep`, a snapshot
+ * covering the prefix and these tokens to `*snapshot_out`. `gpu_ms_out` (may be NULL) receives the
+ * device time of the forward, as the reference's timestamp queries measure it. */
+int sd_forward(sd_engine* e, const uint32_t* ids, int32_t n_ids, const int32_t* rows, int32_t n_rows,
+               const sd_snapshot* cache, int32_t keep, float* hidden_out, sd_snapshot** snapshot_out,
+               double* gpu_ms_out);
+
+/* `Snapshot::len` (`src/engine.rs:80-87`): tokens covered. A snapshot is immutable and can seed
+ * any number of forwards on the engine that made it; free it with sd_snapshot_free. */
+int32_t sd_snapshot_len(const sd_snapshot* s);
+void sd_snapshot_free(sd_snapshot* s);
+
+/* Diagnostics: when `host_buf` is set, each following forward writes the residual stream after each
+ * layer (x + y, [n_layers][n_ids][hidden_size] f32) there; `floats` is its capacity. NULL stops. */
+int sd_engine_set_trace(sd_engine* e, float* host_buf, size_t floats);
+int sd_engine_num_layers(const sd_engine* e);
+
+/* Replaces `Head::load` and `Head::probs` (`src/head.rs:25-77`): the pointer head in f64 on the
+ * host. `hidden` is [n_rows][d] = [option 0 .. option n-2, answer]; writes n_rows - 1 probabilities. */
+int sd_head_load(const char* safetensors_path, sd_head** out);
+void sd_head_free(sd_head* h);
+int sd_head_probs(const sd_head* h, const float* hidden, int32_t n_rows, int32_t d, double temperature, double* probs_out);
+
+/* Kernel-level entry points on device memory, on CUDA stream `stream` (a cudaStream_t; NULL: the
+ * legacy default stream). They replace single dispatches of the reference's plan
+ * (`src/engine.rs:396-524`) and serve the isolated benchmarks. */
+
+/* `kernels::attn` (`src/kernels.rs:453-541`): causal GQA attention with the sigmoid output gate.
+ * q_dev [hq][l][hd] f16; k_dev/v_dev [hk][lt][hd] f16 with this call's rows at p..p+l-1; gate at
+ * gate_dev[t * gstride + goff + h * gstep + d] f16 (NULL: ungated); out_dev [l][hq * hd] f16. hd = 256. */
+int sd_attention(const void* q_dev, const void* k_dev, const void* v_dev, const void* gate_dev, int32_t gstride,
+                 int32_t goff, int32_t gstep, void* out_dev, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk,
+                 int32_t hd, void* stream);
+
+/* `Gdn::subgroups` (`src/kernels.rs:257-302`): the gated delta rule over one sequence of l tokens.
+ * q_dev/k_dev [l][qk_stride] f32 (head h at h * 128), v_dev [l][v_stride] f32 (head h at h * 128),
+ * beta_dev/decay_dev [l][h] f32, state_dev [h][128][128] f32 (read when load_state, always written),
+ * o_dev [l][h * 128] f32. */
+int sd_gdn(const void* q_dev, const void* k_dev, int32_t qk_stride, const void* v_dev, int32_t v_stride,
+           const void* beta_dev, const void* decay_dev, void* state_dev, int32_t load_state, void* o_dev, int32_t l,
+           int32_t h, void* stream);
+
+/* A block-quantized int4 group-32 symmetric weight (`src/kernels.rs:545-576`) in the GEMM's tile
+ * layout, made from the reference layout on the device: q_dev [n][k/32][16 bytes], s_dev [n][k/32] f16.
+ * `interleave` stores rows (j, n/2 + j) next to each other (gate_up for the fused SwiGLU). */
+int sd_qweight_create(const void* q_dev, const void* s_dev, int32_t n, int32_t k, int32_t interleave, sd_qweight** out);
+void sd_qweight_free(sd_qweight* w);
+
+/* `matmul_gemv`/`matmul_tiled`/`matmul_coop` (`src/kernels.rs:590-804`): y_dev[m][ldy] =
+ * f16(act_dev[m][k] W^T) (silu = 1 on an interleaved weight: y = silu(gate) * up, [m][n/2]).
+ * ws_dev/ws_bytes: f32 workspace for split-K (m * n floats; 0 bytes disables split-K). */
+int sd_matmul(const sd_qweight* w, const void* act_dev, int32_t m, void* y_dev, int32_t ldy, int32_t silu, void* ws_dev,
+              size_t ws_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,893 @@
+// The torso engine behind the C ABI (include/sd_b200.h): model loading, the per-layer launch
+// sequence, snapshots, and the pointer head. It replaces the reference's `Engine`
+// (src/engine.rs:104-662) and `Head` (src/head.rs).
+//
+// Device layout: the weight shard is uploaded as is (norm weights, conv taps and gate constants are
+// read from it in place); every int4 matmul weight is repacked once into the GEMM's tile layout
+// (gate_up with gate and up rows interleaved, for the SwiGLU epilogue); the embedding table keeps
+// the reference's packed rows. Per gated-delta layer: state [16][128][128] f32 and conv history
+// [3][6144] f16; per attention layer: K and V caches [2][4096][256] f16. Activations live in a pool
+// sized for the longest forward so far.
+#include <sys/stat.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "../../include/sd_b200.h"
+#include "json.h"
+#include "sd_internal.h"
+
+using sd::QWeight;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+void set_global_error(const std::string& s) { g_last_error = s; }
+
+struct LayerW {
+  int kind = 0;  // 0 linear_attention, 1 full_attention, 2 adapter
+  int slot = -1;
+  const float* in_norm = nullptr;
+  const float* post_norm = nullptr;
+  QWeight in_proj, out_proj, qkv, o_proj, gate_up, down, proj;
+  const float *conv = nullptr, *neg_a = nullptr, *dt_bias = nullptr, *gnorm = nullptr;
+  const float *q_norm = nullptr, *k_norm = nullptr, *bias = nullptr;
+};
+
+float half_bits_to_float(uint16_t h) {
+  __half_raw r;
+  r.x = h;
+  return __half2float(__half(r));
+}
+
+uint16_t float_to_half_bits(float f) {
+  __half_raw r = __half(__float2half_rn(f));
+  return r.x;
+}
+
+// `decode_scales` (src/model.rs:219-236): n rows of g codes, each row after a 4-byte header (m as
+// fp16 bits, j as u16); |scale| = fp16(f32(m * 2^(-k j / 4096))) with the power in f64.
+void decode_scales(const uint8_t* src, int n, int g, uint16_t* dst) {
+  const uint8_t* codes = src + 4 * (size_t)n;
+  for (int r = 0; r < n; r++) {
+    const uint16_t mb = (uint16_t)(src[4 * r] | (src[4 * r + 1] << 8));
+    const uint16_t j = (uint16_t)(src[4 * r + 2] | (src[4 * r + 3] << 8));
+    const double m = (double)half_bits_to_float(mb);
+    for (int i = 0; i < g; i++) {
+      const uint8_t c = codes[(size_t)r * g + i];
+      const int k = c & 127;
+      const uint16_t mag = float_to_half_bits((float)(m * std::pow(2.0, -(double)(k * j) / 4096.0)));
+      dst[(size_t)r * g + i] = (uint16_t)(mag | ((uint16_t)(c & 128) << 8));
+    }
+  }
+}
+
+bool read_file(const std::string& path, std::string& out) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return false;
+  std::ostringstream ss;
+  ss << f.rdbuf();
+  out = ss.str();
+  return true;
+}
+
+}  // namespace
+
+struct sd_snapshot {
+  int len = 0;
+  int device = 0;
+  std::vector<float*> state;
+  std::vector<__half*> hist, k, v;
+  ~sd_snapshot() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    for (auto p : state) cudaFree(p);
+    for (auto p : hist) cudaFree(p);
+    for (auto p : k) cudaFree(p);
+    for (auto p : v) cudaFree(p);
+    cudaSetDevice(prev);
+  }
+};
+
+struct sd_qweight {
+  QWeight w;
+  int device = 0;
+};
+
+struct sd_head {
+  std::vector<float> nw, nb, qw, qb, kw, kb;
+  int dim = 0, d = 0;
+};
+
+struct sd_engine {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  sd::Dims dm;
+  int vocab = 0, n_layers = 0, embed_bits = 4;
+  double rope_theta = 1e7;
+  std::vector<double> unrotate;
+  std::vector<uint8_t*> shards;
+  std::vector<std::pair<uint64_t, uint64_t>> shard_ranges;
+  uint8_t* embed_q = nullptr;
+  __half* embed_s = nullptr;
+  const float* final_norm = nullptr;
+  std::vector<LayerW> layers;
+  std::vector<float*> state;
+  std::vector<__half*> hist, kc, vc;
+  float* rope = nullptr;
+  int n_lin = 0, n_full = 0;
+  int in_n = 0, qkv_n = 0;
+  // activation pool
+  int cap = 0;
+  uint32_t* d_ids = nullptr;
+  int* d_rows = nullptr;
+  float *x = nullptr, *qkvc = nullptr, *of = nullptr, *beta = nullptr, *decay = nullptr, *out = nullptr, *ws = nullptr;
+  float* trace_dev = nullptr;
+  size_t ws_bytes = 0;
+  __half *h = nullptr, *big = nullptr, *mid = nullptr, *o = nullptr, *y = nullptr, *q = nullptr;
+  int* d_err = nullptr;
+  // pinned staging
+  uint32_t* p_ids = nullptr;
+  int* p_rows = nullptr;
+  float* p_out = nullptr;
+  int p_cap = 0;
+  float* trace_host = nullptr;
+  size_t trace_floats = 0;
+  std::string err;
+
+  int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    err = buf;
+    set_global_error(err);
+    return code;
+  }
+};
+
+#define CK(call)                                                                                    \
+  do {                                                                                              \
+    cudaError_t _e = (call);                                                                        \
+    if (_e != cudaSuccess) return e->fail(SD_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_e)); \
+  } while (0)
+
+namespace {
+
+void free_pool(sd_engine* e) {
+  cudaFree(e->d_ids); cudaFree(e->d_rows); cudaFree(e->x); cudaFree(e->qkvc); cudaFree(e->of); cudaFree(e->beta);
+  cudaFree(e->decay); cudaFree(e->out); cudaFree(e->ws); cudaFree(e->h); cudaFree(e->big); cudaFree(e->mid);
+  cudaFree(e->o); cudaFree(e->y); cudaFree(e->q); cudaFree(e->trace_dev);
+  e->d_ids = nullptr; e->d_rows = nullptr; e->x = e->qkvc = e->of = e->beta = e->decay = e->out = e->ws = nullptr;
+  e->trace_dev = nullptr;
+  e->h = e->big = e->mid = e->o = e->y = e->q = nullptr;
+  e->cap = 0;
+}
+
+// Activation buffers for `l` tokens, grown to 128 or the next power of two as the reference does
+// (src/engine.rs:364-393).
+int ensure_pool(sd_engine* e, int l) {
+  int cap = l <= 128 ? 128 : 1;
+  while (cap < l) cap <<= 1;
+  if (e->cap >= cap && (!e->trace_host || e->trace_dev)) return SD_OK;
+  free_pool(e);
+  const sd::Dims& d = e->dm;
+  const size_t maxn = std::max({(size_t)2 * d.inter, (size_t)e->in_n, (size_t)e->qkv_n});
+  CK(cudaMalloc(&e->d_ids, cap * sizeof(uint32_t)));
+  CK(cudaMalloc(&e->d_rows, cap * sizeof(int)));
+  CK(cudaMalloc(&e->x, (size_t)cap * d.d * 4));
+  CK(cudaMalloc(&e->h, (size_t)cap * d.d * 2));
+  CK(cudaMalloc(&e->big, (size_t)cap * maxn * 2));
+  CK(cudaMalloc(&e->mid, (size_t)cap * d.inter * 2));
+  CK(cudaMalloc(&e->qkvc, (size_t)cap * d.C() * 4));
+  CK(cudaMalloc(&e->of, (size_t)cap * d.h * d.dv * 4));
+  CK(cudaMalloc(&e->o, (size_t)cap * std::max(d.hq * d.hd, d.h * d.dv) * 2));
+  CK(cudaMalloc(&e->y, (size_t)cap * d.d * 2));
+  CK(cudaMalloc(&e->q, (size_t)d.hq * cap * d.hd * 2));
+  CK(cudaMalloc(&e->beta, (size_t)cap * d.h * 4));
+  CK(cudaMalloc(&e->decay, (size_t)cap * d.h * 4));
+  CK(cudaMalloc(&e->out, (size_t)cap * d.d * 4));
+  // split-K workspace: small-M matmuls only (the planner splits K when the grid is short)
+  e->ws_bytes = (size_t)std::min(cap, 512) * maxn * 4;
+  CK(cudaMalloc(&e->ws, e->ws_bytes));
+  if (e->trace_host) CK(cudaMalloc(&e->trace_dev, (size_t)e->n_layers * cap * d.d * 4));
+  e->cap = cap;
+  return SD_OK;
+}
+
+int ensure_pinned(sd_engine* e, int l, int nrows) {
+  const int need = std::max(l, nrows);
+  if (e->p_cap >= need) return SD_OK;
+  cudaFreeHost(e->p_ids);
+  cudaFreeHost(e->p_rows);
+  cudaFreeHost(e->p_out);
+  int cap = std::max(need, 256);
+  CK(cudaMallocHost(&e->p_ids, cap * sizeof(uint32_t)));
+  CK(cudaMallocHost(&e->p_rows, cap * sizeof(int)));
+  CK(cudaMallocHost(&e->p_out, (size_t)cap * e->dm.d * sizeof(float)));
+  e->p_cap = cap;
+  return SD_OK;
+}
+
+// In-place fast Walsh-Hadamard transform, Sylvester order, unnormalised (src/engine.rs:713-727).
+void fwht(float* x, int n) {
+  for (int h = 1; h < n; h *= 2)
+    for (int i = 0; i < n; i += 2 * h)
+      for (int j = i; j < i + h; j++) {
+        float a = x[j], b = x[j + h];
+        x[j] = a + b;
+        x[j + h] = a - b;
+      }
+}
+
+int load_engine(sd_engine* e, const std::string& dir) {
+  std::string text;
+  if (!read_file(dir + "/manifest.json", text)) return e->fail(SD_ERR_IO, "%s/manifest.json: cannot read", dir.c_str());
+  sd::json::Value m;
+  try {
+    m = sd::json::parse(text);
+  } catch (const std::exception& ex) {
+    return e->fail(SD_ERR_FORMAT, "manifest.json: %s", ex.what());
+  }
+  try {
+    const auto& c = m.at("config");
+    sd::Dims& d = e->dm;
+    d.d = (int)c.at("hidden_size").integer();
+    d.inter = (int)c.at("intermediate_size").integer();
+    d.hq = (int)c.at("num_attention_heads").integer();
+    d.hk = (int)c.at("num_key_value_heads").integer();
+    d.hd = (int)c.at("head_dim").integer();
+    d.h = (int)c.at("linear_num_key_heads").integer();
+    d.dk = (int)c.at("linear_key_head_dim").integer();
+    d.dv = (int)c.at("linear_value_head_dim").integer();
+    d.rd = (int)c.at("rotary_dim").integer();
+    e->rope_theta = c.at("rope_theta").number();
+    if (const auto* u = c.get("unrotate"); u && u->kind == sd::json::Value::Array)
+      for (auto& x : u->arr) e->unrotate.push_back(x.number());
+    if (d.d != 2048 || d.hd != 256 || d.dk != 128 || d.dv != 128 || d.hq % d.hk || d.rd > d.hd || d.rd % 2 ||
+        d.inter % 128)
+      return e->fail(SD_ERR_FORMAT, "unsupported dims (the kernels are built for D=2048, HD=256, DK=DV=128)");
+    const auto& types = c.at("layer_types").arr;
+    e->n_layers = (int)types.size();
+    e->layers.resize(e->n_layers);
+    for (int i = 0; i < e->n_layers; i++) {
+      const std::string& k = types[i].str;
+      if (k == "linear_attention") e->layers[i].kind = 0, e->layers[i].slot = e->n_lin++;
+      else if (k == "full_attention") e->layers[i].kind = 1, e->layers[i].slot = e->n_full++;
+      else if (k == "adapter") e->layers[i].kind = 2;
+      else return e->fail(SD_ERR_FORMAT, "unsupported layer type %s", k.c_str());
+    }
+  } catch (const std::exception& ex) {
+    return e->fail(SD_ERR_FORMAT, "manifest.json config: %s", ex.what());
+  }
+  const auto& tensors = m.at("tensors");
+  for (auto& kv : tensors.obj)
+    if (const auto* hd = kv.second.get("had"); hd && !hd->is_null())
+      return e->fail(SD_ERR_FORMAT, "%s: online Hadamard rotation is not supported", kv.first.c_str());
+
+  // shards, uploaded as is in 64 MiB chunks through pinned memory (src/engine.rs:215-229)
+  const auto& shards = m.at("shards").arr;
+  uint8_t* pinned = nullptr;
+  const size_t chunk = 64ull << 20;
+  CK(cudaMallocHost(&pinned, chunk));
+  std::unique_ptr<uint8_t, void (*)(uint8_t*)> pin_guard(pinned, [](uint8_t* p) { cudaFreeHost(p); });
+  for (size_t i = 0; i < shards.size(); i++) {
+    const uint64_t start = (uint64_t)shards[i].at("start").integer(), bytes = (uint64_t)shards[i].at("bytes").integer();
+    std::string path = dir + "/weights." + std::to_string(i) + ".bin";
+    FILE* f = fopen(path.c_str(), "rb");
+    if (!f) return e->fail(SD_ERR_IO, "%s: cannot open", path.c_str());
+    uint8_t* dev = nullptr;
+    cudaError_t ce = cudaMalloc(&dev, std::max<uint64_t>(bytes, 16));
+    if (ce != cudaSuccess) {
+      fclose(f);
+      return e->fail(SD_ERR_CUDA, "shard %zu: %s", i, cudaGetErrorString(ce));
+    }
+    e->shards.push_back(dev);
+    e->shard_ranges.push_back({start, bytes});
+    for (uint64_t off = 0; off < bytes; off += chunk) {
+      const size_t n = (size_t)std::min<uint64_t>(chunk, bytes - off);
+      if (fread(pinned, 1, n, f) != n) {
+        fclose(f);
+        return e->fail(SD_ERR_IO, "%s: %llu bytes, the manifest says %llu", path.c_str(), (unsigned long long)off,
+                       (unsigned long long)bytes);
+      }
+      CK(cudaMemcpy(dev + off, pinned, n, cudaMemcpyHostToDevice));
+    }
+    fclose(f);
+  }
+  auto tensor_ptr = [&](const std::string& name, const sd::json::Value** meta) -> const uint8_t* {
+    const auto* t = tensors.get(name);
+    if (!t) return nullptr;
+    if (meta) *meta = t;
+    const uint64_t off = (uint64_t)t->at("offset").integer();
+    for (size_t i = 0; i < e->shards.size(); i++)
+      if (off >= e->shard_ranges[i].first && off < e->shard_ranges[i].first + e->shard_ranges[i].second)
+        return e->shards[i] + (off - e->shard_ranges[i].first);
+    return nullptr;
+  };
+  std::string missing;
+  auto f32 = [&](const std::string& name) -> const float* {
+    const float* p = reinterpret_cast<const float*>(tensor_ptr(name, nullptr));
+    if (!p && missing.empty()) missing = name;
+    return p;
+  };
+  int rc = SD_OK;
+  auto mat = [&](const std::string& name, bool interleave, QWeight* w) {
+    const sd::json::Value* t = nullptr;
+    const uint8_t* q = tensor_ptr(name + ".q", &t);
+    const uint8_t* s = tensor_ptr(name + ".s", nullptr);
+    if (!q || !s) {
+      if (missing.empty()) missing = name;
+      return;
+    }
+    const int bits = (int)(t->get("bits") ? t->at("bits").integer() : 4);
+    const int group = (int)(t->get("group") ? t->at("group").integer() : 32);
+    const bool asym = t->get("asym") ? t->at("asym").boolean() : false;
+    const int n = (int)t->at("N").integer(), k = (int)t->at("K").integer();
+    if (bits != 4 || group != 32 || asym || k % 64 || (interleave && n % 2)) {
+      if (rc == SD_OK) rc = e->fail(SD_ERR_FORMAT, "%s: only int4 group-32 symmetric matmul weights are supported", name.c_str());
+      return;
+    }
+    cudaError_t ce = sd::repack_weight(q, reinterpret_cast<const __half*>(s), n, k, interleave, w, e->stream);
+    if (ce != cudaSuccess && rc == SD_OK) rc = e->fail(SD_ERR_CUDA, "%s: %s", name.c_str(), cudaGetErrorString(ce));
+  };
+  for (int i = 0; i < e->n_layers; i++) {
+    LayerW& L = e->layers[i];
+    const std::string pre = "layers." + std::to_string(i) + ".";
+    L.in_norm = f32(pre + "in_norm");
+    if (L.kind == 0) {
+      mat(pre + "in_proj", false, &L.in_proj);
+      mat(pre + "out_proj", false, &L.out_proj);
+      L.conv = f32(pre + "conv");
+      L.neg_a = f32(pre + "neg_exp_A");
+      L.dt_bias = f32(pre + "dt_bias");
+      L.gnorm = f32(pre + "gnorm");
+      e->in_n = std::max(e->in_n, L.in_proj.n);
+    } else if (L.kind == 1) {
+      mat(pre + "qkv", false, &L.qkv);
+      mat(pre + "o_proj", false, &L.o_proj);
+      L.q_norm = f32(pre + "q_norm");
+      L.k_norm = f32(pre + "k_norm");
+      e->qkv_n = std::max(e->qkv_n, L.qkv.n);
+    } else {
+      mat(pre + "proj", false, &L.proj);
+      L.bias = f32(pre + "bias");
+    }
+    if (L.kind != 2) {
+      L.post_norm = f32(pre + "post_norm");
+      mat(pre + "gate_up", true, &L.gate_up);
+      mat(pre + "down", false, &L.down);
+    }
+    if (rc != SD_OK) return rc;
+  }
+  e->final_norm = f32("final_norm");
+  if (!missing.empty()) return e->fail(SD_ERR_FORMAT, "no tensor %s", missing.c_str());
+  const sd::Dims& d = e->dm;
+  for (auto& L : e->layers) {
+    if (L.kind == 0 && L.in_proj.n < d.C() + d.h * d.dv + 2 * d.h)
+      return e->fail(SD_ERR_FORMAT, "in_proj has %d rows, fewer than q,k,v,z,a,b need", L.in_proj.n);
+    if (L.kind == 1 && L.qkv.n < d.hq * d.hd * 2 + 2 * d.hk * d.hd)
+      return e->fail(SD_ERR_FORMAT, "qkv has %d rows, fewer than q,gate,k,v need", L.qkv.n);
+  }
+
+  // embedding parts (src/model.rs:260-283)
+  const auto* emb = m.get("embed");
+  if (!emb || emb->is_null()) return e->fail(SD_ERR_FORMAT, "manifest has no embed");
+  {
+    const sd::json::Value* et = tensors.get("embed.q");
+    e->embed_bits = et && et->get("bits") ? (int)et->at("bits").integer() : 4;
+    const int egroup = et && et->get("group") ? (int)et->at("group").integer() : 32;
+    const bool easym = et && et->get("asym") ? et->at("asym").boolean() : false;
+    if (easym || egroup != 32 || e->embed_bits < 2 || e->embed_bits > 4)
+      return e->fail(SD_ERR_FORMAT, "embedding format not supported (symmetric int2/3/4, group 32)");
+    e->vocab = (int)emb->at("vocab").integer();
+    const auto& parts = emb->at("parts").arr;
+    if (parts.size() != 2 || parts[0].arr[0].str != "embed.q" || parts[1].arr[0].str != "embed.s")
+      return e->fail(SD_ERR_FORMAT, "embed parts must be [embed.q, embed.s]");
+    const size_t qb = (size_t)parts[0].arr[1].integer(), sb = (size_t)parts[1].arr[1].integer();
+    const bool u8 = emb->get("u8") ? emb->at("u8").boolean() : false;
+    const auto* wrb = emb->get("wire_row_bytes");
+    const size_t rb = (wrb && !wrb->is_null()) ? (size_t)wrb->integer() : (size_t)emb->at("row_bytes").integer();
+    if (qb != (size_t)d.d / 32 * 4 * e->embed_bits || sb != (size_t)d.d / 32 * 2)
+      return e->fail(SD_ERR_FORMAT, "embed part sizes do not match the hidden size");
+    std::string path = dir + "/" + emb->at("rows").str;
+    FILE* f = fopen(path.c_str(), "rb");
+    if (!f) return e->fail(SD_ERR_IO, "%s: cannot open", path.c_str());
+    struct stat stbuf;
+    if (fstat(fileno(f), &stbuf) != 0 || (size_t)stbuf.st_size != (size_t)e->vocab * rb) {
+      fclose(f);
+      return e->fail(SD_ERR_IO, "%s: %lld bytes, expected %d rows of %zu", path.c_str(), (long long)stbuf.st_size, e->vocab, rb);
+    }
+    std::vector<uint8_t> hq((size_t)e->vocab * qb), hs((size_t)e->vocab * sb);
+    std::vector<uint8_t> rows(rb * 4096);
+    for (int r0 = 0; r0 < e->vocab; r0 += 4096) {
+      const int n = std::min(4096, e->vocab - r0);
+      if (fread(rows.data(), 1, rb * n, f) != rb * n) {
+        fclose(f);
+        return e->fail(SD_ERR_IO, "%s: short read", path.c_str());
+      }
+      for (int r = 0; r < n; r++) {
+        const uint8_t* row = rows.data() + rb * r;
+        memcpy(hq.data() + (size_t)(r0 + r) * qb, row, qb);
+        if (u8) decode_scales(row + qb, 1, (int)sb / 2, reinterpret_cast<uint16_t*>(hs.data() + (size_t)(r0 + r) * sb));
+        else memcpy(hs.data() + (size_t)(r0 + r) * sb, row + qb, sb);
+      }
+    }
+    fclose(f);
+    CK(cudaMalloc(&e->embed_q, hq.size()));
+    CK(cudaMalloc(&e->embed_s, hs.size()));
+    CK(cudaMemcpy(e->embed_q, hq.data(), hq.size(), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e->embed_s, hs.data(), hs.size(), cudaMemcpyHostToDevice));
+  }
+
+  // recurrent state, conv history, K/V caches (src/engine.rs:251-257), RoPE table (:259-269)
+  for (int i = 0; i < e->n_lin; i++) {
+    float* s = nullptr;
+    __half* h = nullptr;
+    CK(cudaMalloc(&s, (size_t)d.h * d.dk * d.dv * 4));
+    CK(cudaMalloc(&h, (size_t)3 * d.C() * 2));
+    CK(cudaMemset(s, 0, (size_t)d.h * d.dk * d.dv * 4));
+    CK(cudaMemset(h, 0, (size_t)3 * d.C() * 2));
+    e->state.push_back(s);
+    e->hist.push_back(h);
+  }
+  for (int i = 0; i < e->n_full; i++) {
+    __half *k = nullptr, *v = nullptr;
+    CK(cudaMalloc(&k, (size_t)d.hk * SD_CONTEXT * d.hd * 2));
+    CK(cudaMalloc(&v, (size_t)d.hk * SD_CONTEXT * d.hd * 2));
+    CK(cudaMemset(k, 0, (size_t)d.hk * SD_CONTEXT * d.hd * 2));
+    CK(cudaMemset(v, 0, (size_t)d.hk * SD_CONTEXT * d.hd * 2));
+    e->kc.push_back(k);
+    e->vc.push_back(v);
+  }
+  std::vector<float> table((size_t)SD_CONTEXT * d.rd);
+  for (int t = 0; t < SD_CONTEXT; t++)
+    for (int i = 0; i < d.rd / 2; i++) {
+      const double a = (double)t / std::pow(e->rope_theta, (double)(2 * i) / (double)d.rd);
+      table[(size_t)t * d.rd + 2 * i] = (float)std::cos(a);
+      table[(size_t)t * d.rd + 2 * i + 1] = (float)std::sin(a);
+    }
+  CK(cudaMalloc(&e->rope, table.size() * 4));
+  CK(cudaMemcpy(e->rope, table.data(), table.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&e->d_err, sizeof(int)));
+  CK(cudaMemset(e->d_err, 0, sizeof(int)));
+  CK(cudaStreamSynchronize(e->stream));
+  return SD_OK;
+}
+
+// One launch failure or a kernel error word turns into the call's error.
+int check_kernels(sd_engine* e) {
+  cudaError_t ce = cudaStreamSynchronize(e->stream);
+  if (ce != cudaSuccess) return e->fail(SD_ERR_CUDA, "forward: %s", cudaGetErrorString(ce));
+  int herr = 0;
+  CK(cudaMemcpy(&herr, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (herr != 0) {
+    cudaMemset(e->d_err, 0, sizeof(int));
+    return e->fail(SD_ERR_KERNEL, "a kernel reported error %d", herr);
+  }
+  return SD_OK;
+}
+
+#define LK(call)                                                                                       \
+  do {                                                                                                 \
+    cudaError_t _e = (call);                                                                           \
+    if (_e != cudaSuccess) return e->fail(SD_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_e));    \
+  } while (0)
+
+// The layer loop (src/engine.rs:446-522), launched on the engine's stream.
+int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
+  const sd::Dims& d = e->dm;
+  cudaStream_t st = e->stream;
+  const int C = d.C();
+  LK(sd::launch_embed_norm(e->d_ids, l, e->embed_q, e->embed_s, e->embed_bits, d.d, e->vocab, e->layers[0].in_norm, e->x,
+                           e->h, e->d_err, st));
+  for (int i = 0; i < e->n_layers; i++) {
+    const LayerW& L = e->layers[i];
+    if (i > 0) LK(sd::launch_add_norm(e->x, e->y, L.in_norm, l, d.d, true, e->h, st));
+    if (L.kind == 2) {
+      LK(sd::gemm_q4(L.proj, e->h, l, d.d, e->y, d.d, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
+      LK(sd::launch_add_bias(e->y, L.bias, l, d.d, st));
+    } else {
+      if (L.kind == 0) {
+        const int N = L.in_proj.n;
+        __half* hist = e->hist[L.slot];
+        LK(sd::gemm_q4(L.in_proj, e->h, l, d.d, e->big, N, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
+        LK(sd::launch_conv(e->big, N, L.conv, hist, l, C, e->qkvc, st));
+        LK(sd::launch_hist_update(e->big, N, hist, l, C, st));
+        const int aoff = C + d.h * d.dv, boff = aoff + d.h;
+        LK(sd::launch_gdn_gates(e->big, N, aoff, boff, L.neg_a, L.dt_bias, l, d.h, e->beta, e->decay, st));
+        LK(sd::launch_gdn_recurrent(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, e->beta, e->decay,
+                                    e->state[L.slot], has_cache, e->of, l, d.h, st));
+        LK(sd::launch_gnorm(e->of, e->big, N, C, L.gnorm, l, d.h, e->o, st));
+        LK(sd::gemm_q4(L.out_proj, e->o, l, d.h * d.dv, e->y, d.d, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
+      } else {
+        const int N = L.qkv.n;
+        LK(sd::gemm_q4(L.qkv, e->h, l, d.d, e->big, N, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
+        LK(sd::launch_qk_prep(e->big, N, L.q_norm, L.k_norm, e->rope, l, p, SD_CONTEXT, d, e->q, e->kc[L.slot],
+                              e->vc[L.slot], st));
+        LK(sd::launch_attention(e->q, e->kc[L.slot], e->vc[L.slot], e->big, N, d.hd, 2 * d.hd, e->o, l, p, SD_CONTEXT, d.hq,
+                                d.hk, d.hd, st));
+        LK(sd::gemm_q4(L.o_proj, e->o, l, d.hq * d.hd, e->y, d.d, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
+      }
+      LK(sd::launch_add_norm(e->x, e->y, L.post_norm, l, d.d, true, e->h, st));
+      LK(sd::gemm_q4(L.gate_up, e->h, l, d.d, e->mid, d.inter, true, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
+      LK(sd::gemm_q4(L.down, e->mid, l, d.inter, e->y, d.d, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
+    }
+    if (e->trace_dev) LK(sd::launch_trace(e->x, e->y, l * d.d, e->trace_dev + (size_t)i * l * d.d, st));
+  }
+  if (nrows > 0) LK(sd::launch_final_norm(e->x, e->y, e->final_norm, e->d_rows, nrows, d.d, e->out, st));
+  return SD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* sd_last_error(void) { return g_last_error.c_str(); }
+
+int sd_engine_create(const char* model_dir, int device, sd_engine** out) {
+  if (!model_dir || !out) {
+    set_global_error("sd_engine_create: null argument");
+    return SD_ERR_INVALID;
+  }
+  *out = nullptr;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev || device >= sd::kMaxDevices) {
+    set_global_error("sd_engine_create: no CUDA device " + std::to_string(device));
+    return SD_ERR_CUDA;
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) {
+    set_global_error("sd_engine_create: device " + std::to_string(device) + " is not an sm_100 (B200) GPU");
+    return SD_ERR_CUDA;
+  }
+  auto* e = new sd_engine();
+  e->device = device;
+  e->num_sms = prop.multiProcessorCount;
+  cudaSetDevice(device);
+  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess || cudaEventCreate(&e->ev0) != cudaSuccess ||
+      cudaEventCreate(&e->ev1) != cudaSuccess) {
+    set_global_error("sd_engine_create: cannot create a stream");
+    sd_engine_destroy(e);
+    return SD_ERR_CUDA;
+  }
+  int rc = load_engine(e, model_dir);
+  if (rc != SD_OK) {
+    set_global_error(e->err);
+    sd_engine_destroy(e);
+    return rc;
+  }
+  *out = e;
+  return SD_OK;
+}
+
+void sd_engine_destroy(sd_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  free_pool(e);
+  for (auto p : e->shards) cudaFree(p);
+  for (auto& L : e->layers)
+    for (QWeight* w : {&L.in_proj, &L.out_proj, &L.qkv, &L.o_proj, &L.gate_up, &L.down, &L.proj}) cudaFree(w->tiles);
+  for (auto p : e->state) cudaFree(p);
+  for (auto p : e->hist) cudaFree(p);
+  for (auto p : e->kc) cudaFree(p);
+  for (auto p : e->vc) cudaFree(p);
+  cudaFree(e->embed_q);
+  cudaFree(e->embed_s);
+  cudaFree(e->rope);
+  cudaFree(e->d_err);
+  cudaFreeHost(e->p_ids);
+  cudaFreeHost(e->p_rows);
+  cudaFreeHost(e->p_out);
+  if (e->ev0) cudaEventDestroy(e->ev0);
+  if (e->ev1) cudaEventDestroy(e->ev1);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+int sd_engine_hidden_size(const sd_engine* e) { return e ? e->dm.d : 0; }
+int sd_engine_num_layers(const sd_engine* e) { return e ? e->n_layers : 0; }
+const char* sd_engine_last_error(const sd_engine* e) { return e ? e->err.c_str() : g_last_error.c_str(); }
+
+int sd_engine_set_trace(sd_engine* e, float* host_buf, size_t floats) {
+  if (!e) return SD_ERR_INVALID;
+  cudaSetDevice(e->device);
+  e->trace_host = host_buf;
+  e->trace_floats = host_buf ? floats : 0;
+  if (!host_buf) {
+    cudaFree(e->trace_dev);
+    e->trace_dev = nullptr;
+  } else if (e->cap > 0 && !e->trace_dev) {
+    CK(cudaMalloc(&e->trace_dev, (size_t)e->n_layers * e->cap * e->dm.d * 4));
+  }
+  return SD_OK;
+}
+
+int sd_forward(sd_engine* e, const uint32_t* ids, int32_t l, const int32_t* rows, int32_t nrows, const sd_snapshot* cache,
+               int32_t keep, float* hidden_out, sd_snapshot** snapshot_out, double* gpu_ms_out) {
+  if (!e) return SD_ERR_INVALID;
+  const int p = cache ? cache->len : 0;
+  if (l <= 0 || p + l > SD_CONTEXT || !ids) return e->fail(SD_ERR_INVALID, "context of %d tokens: must be 1 to %d", p + l, SD_CONTEXT);
+  if (nrows < 0 || (nrows > 0 && (!rows || !hidden_out))) return e->fail(SD_ERR_INVALID, "rows given without an output buffer");
+  for (int i = 0; i < nrows; i++)
+    if (rows[i] < 0 || rows[i] >= l) return e->fail(SD_ERR_INVALID, "row %d out of range for %d tokens", rows[i], l);
+  for (int i = 0; i < l; i++)
+    if (ids[i] >= (uint32_t)e->vocab) return e->fail(SD_ERR_INVALID, "token id %u out of range (vocab %d)", ids[i], e->vocab);
+  if (cache && cache->device != e->device) return e->fail(SD_ERR_INVALID, "snapshot belongs to another device");
+  if (keep && !snapshot_out) return e->fail(SD_ERR_INVALID, "keep without a snapshot output");
+  if (e->trace_host && e->trace_floats < (size_t)e->n_layers * l * e->dm.d)
+    return e->fail(SD_ERR_INVALID, "trace buffer too small");
+  cudaSetDevice(e->device);
+  int rc = ensure_pool(e, l);
+  if (rc != SD_OK) return rc;
+  rc = ensure_pinned(e, l, nrows);
+  if (rc != SD_OK) return rc;
+  const sd::Dims& d = e->dm;
+  cudaStream_t st = e->stream;
+  memcpy(e->p_ids, ids, l * sizeof(uint32_t));
+  CK(cudaMemcpyAsync(e->d_ids, e->p_ids, l * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+  if (nrows > 0) {
+    memcpy(e->p_rows, rows, nrows * sizeof(int));
+    CK(cudaMemcpyAsync(e->d_rows, e->p_rows, nrows * sizeof(int), cudaMemcpyHostToDevice, st));
+  }
+  CK(cudaEventRecord(e->ev0, st));
+  // restore the prefix, or clear the conv history (src/engine.rs:552-571)
+  const size_t state_bytes = (size_t)d.h * d.dk * d.dv * 4, hist_bytes = (size_t)3 * d.C() * 2;
+  const size_t row_bytes = (size_t)d.hd * 2;
+  if (cache) {
+    for (int i = 0; i < e->n_lin; i++) {
+      CK(cudaMemcpyAsync(e->state[i], cache->state[i], state_bytes, cudaMemcpyDeviceToDevice, st));
+      CK(cudaMemcpyAsync(e->hist[i], cache->hist[i], hist_bytes, cudaMemcpyDeviceToDevice, st));
+    }
+    for (int i = 0; i < e->n_full && p > 0; i++) {
+      CK(cudaMemcpy2DAsync(e->kc[i], SD_CONTEXT * row_bytes, cache->k[i], (size_t)p * row_bytes, (size_t)p * row_bytes, d.hk,
+                           cudaMemcpyDeviceToDevice, st));
+      CK(cudaMemcpy2DAsync(e->vc[i], SD_CONTEXT * row_bytes, cache->v[i], (size_t)p * row_bytes, (size_t)p * row_bytes, d.hk,
+                           cudaMemcpyDeviceToDevice, st));
+    }
+  } else {
+    for (int i = 0; i < e->n_lin; i++) CK(cudaMemsetAsync(e->hist[i], 0, hist_bytes, st));
+  }
+  rc = run_layers(e, l, p, cache != nullptr, nrows);
+  if (rc != SD_OK) return rc;
+  CK(cudaEventRecord(e->ev1, st));
+  if (nrows > 0) CK(cudaMemcpyAsync(e->p_out, e->out, (size_t)nrows * d.d * 4, cudaMemcpyDeviceToHost, st));
+  if (e->trace_dev)
+    CK(cudaMemcpyAsync(e->trace_host, e->trace_dev, (size_t)e->n_layers * l * d.d * 4, cudaMemcpyDeviceToHost, st));
+  // snapshot of the prefix and these tokens (src/engine.rs:592-614)
+  std::unique_ptr<sd_snapshot> snap;
+  if (keep) {
+    snap.reset(new sd_snapshot());
+    snap->device = e->device;
+    const int T = p + l;
+    snap->len = T;
+    for (int i = 0; i < e->n_lin; i++) {
+      float* s = nullptr;
+      __half* h = nullptr;
+      CK(cudaMalloc(&s, state_bytes));
+      snap->state.push_back(s);
+      CK(cudaMalloc(&h, hist_bytes));
+      snap->hist.push_back(h);
+      CK(cudaMemcpyAsync(s, e->state[i], state_bytes, cudaMemcpyDeviceToDevice, st));
+      CK(cudaMemcpyAsync(h, e->hist[i], hist_bytes, cudaMemcpyDeviceToDevice, st));
+    }
+    for (int i = 0; i < e->n_full; i++) {
+      __half *k = nullptr, *v = nullptr;
+      CK(cudaMalloc(&k, (size_t)d.hk * T * row_bytes));
+      snap->k.push_back(k);
+      CK(cudaMalloc(&v, (size_t)d.hk * T * row_bytes));
+      snap->v.push_back(v);
+      CK(cudaMemcpy2DAsync(k, (size_t)T * row_bytes, e->kc[i], SD_CONTEXT * row_bytes, (size_t)T * row_bytes, d.hk,
+                           cudaMemcpyDeviceToDevice, st));
+      CK(cudaMemcpy2DAsync(v, (size_t)T * row_bytes, e->vc[i], SD_CONTEXT * row_bytes, (size_t)T * row_bytes, d.hk,
+                           cudaMemcpyDeviceToDevice, st));
+    }
+  }
+  rc = check_kernels(e);
+  if (rc != SD_OK) return rc;
+  if (gpu_ms_out) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev0, e->ev1);
+    *gpu_ms_out = ms;
+  }
+  if (nrows > 0) {
+    memcpy(hidden_out, e->p_out, (size_t)nrows * d.d * 4);
+    // a rotated torso: the head's basis is unrotate * FWHT(row) (src/engine.rs:652-660)
+    if ((int)e->unrotate.size() == d.d)
+      for (int r = 0; r < nrows; r++) {
+        float* row = hidden_out + (size_t)r * d.d;
+        fwht(row, d.d);
+        for (int c = 0; c < d.d; c++) row[c] = (float)((double)row[c] * e->unrotate[c]);
+      }
+  }
+  if (keep) *snapshot_out = snap.release();
+  return SD_OK;
+}
+
+int32_t sd_snapshot_len(const sd_snapshot* s) { return s ? s->len : 0; }
+void sd_snapshot_free(sd_snapshot* s) { delete s; }
+
+// ---------------------------------------------------------------------------------------------
+// Pointer head (src/head.rs): LayerNorm (eps 1e-5), q/k projections, scaled dot, softmax; f64.
+// ---------------------------------------------------------------------------------------------
+int sd_head_load(const char* path, sd_head** out) {
+  if (!path || !out) return SD_ERR_INVALID;
+  std::string bytes;
+  if (!read_file(path, bytes)) {
+    set_global_error(std::string(path) + ": cannot read");
+    return SD_ERR_IO;
+  }
+  auto bad = [](const char* why) {
+    set_global_error(std::string("head.safetensors: ") + why);
+    return SD_ERR_FORMAT;
+  };
+  if (bytes.size() < 8) return bad("malformed");
+  uint64_t n = 0;
+  memcpy(&n, bytes.data(), 8);
+  if (8 + n > bytes.size()) return bad("malformed");
+  sd::json::Value hdr;
+  try {
+    hdr = sd::json::parse(bytes.substr(8, n));
+  } catch (...) {
+    return bad("malformed");
+  }
+  auto h = std::make_unique<sd_head>();
+  const char* names[6] = {"norm.weight", "norm.bias", "q.weight", "q.bias", "k.weight", "k.bias"};
+  std::vector<float>* dst[6] = {&h->nw, &h->nb, &h->qw, &h->qb, &h->kw, &h->kb};
+  for (int i = 0; i < 6; i++) {
+    const auto* t = hdr.get(names[i]);
+    if (!t) {
+      set_global_error(std::string("head.safetensors: no ") + names[i]);
+      return SD_ERR_FORMAT;
+    }
+    if (t->at("dtype").str != "F32") return bad("tensors must be F32");
+    const auto& off = t->at("data_offsets").arr;
+    const size_t a = (size_t)off[0].integer(), b = (size_t)off[1].integer();
+    if (b < a || 8 + n + b > bytes.size() || (b - a) % 4) return bad("malformed");
+    dst[i]->resize((b - a) / 4);
+    memcpy(dst[i]->data(), bytes.data() + 8 + n + a, b - a);
+    if (i == 2) h->dim = (int)t->at("shape").arr[0].integer();
+  }
+  h->d = (int)h->nw.size();
+  if (h->dim <= 0 || h->qw.size() != (size_t)h->dim * h->d || h->kw.size() != h->qw.size()) return bad("shapes");
+  *out = h.release();
+  return SD_OK;
+}
+
+void sd_head_free(sd_head* h) { delete h; }
+
+int sd_head_probs(const sd_head* h, const float* hidden, int32_t nrows, int32_t d, double temperature, double* probs) {
+  if (!h || !hidden || !probs || nrows < 2 || d != h->d) {
+    set_global_error("sd_head_probs: bad arguments");
+    return SD_ERR_INVALID;
+  }
+  auto project = [&](const float* x, const std::vector<float>& w, const std::vector<float>& b, std::vector<double>& outv) {
+    double mean = 0.0, var = 0.0;
+    for (int j = 0; j < d; j++) mean += (double)x[j];
+    mean /= d;
+    for (int j = 0; j < d; j++) var += ((double)x[j] - mean) * ((double)x[j] - mean);
+    var /= d;
+    const double r = 1.0 / std::sqrt(var + 1e-5);
+    std::vector<double> xn(d);
+    for (int j = 0; j < d; j++) xn[j] = ((double)x[j] - mean) * r * (double)h->nw[j] + (double)h->nb[j];
+    outv.assign(h->dim, 0.0);
+    for (int o = 0; o < h->dim; o++) {
+      double s = 0.0;
+      for (int j = 0; j < d; j++) s += (double)w[(size_t)o * d + j] * xn[j];
+      outv[o] = (double)b[o] + s;
+    }
+  };
+  std::vector<double> q, k;
+  const int nopt = nrows - 1;
+  project(hidden + (size_t)nopt * d, h->qw, h->qb, q);
+  const double scale = std::pow((double)h->dim, -0.5) / std::max(temperature, 1e-6);
+  double mx = -1.79769313486231570e308;
+  for (int i = 0; i < nopt; i++) {
+    project(hidden + (size_t)i * d, h->kw, h->kb, k);
+    double s = 0.0;
+    for (int o = 0; o < h->dim; o++) s += k[o] * q[o];
+    probs[i] = s * scale;
+    mx = std::max(mx, probs[i]);
+  }
+  double z = 0.0;
+  for (int i = 0; i < nopt; i++) {
+    probs[i] = std::exp(probs[i] - mx);
+    z += probs[i];
+  }
+  for (int i = 0; i < nopt; i++) probs[i] /= z;
+  return SD_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Kernel-level entry points
+// ---------------------------------------------------------------------------------------------
+static int op_result(cudaError_t ce, const char* what) {
+  if (ce == cudaSuccess) return SD_OK;
+  set_global_error(std::string(what) + ": " + cudaGetErrorString(ce));
+  return ce == cudaErrorInvalidValue ? SD_ERR_INVALID : SD_ERR_CUDA;
+}
+
+int sd_attention(const void* q, const void* k, const void* v, const void* gate, int32_t gstride, int32_t goff, int32_t gstep,
+                 void* out, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk, int32_t hd, void* stream) {
+  if (!q || !k || !v || !out || l <= 0 || p < 0 || p + l > lt || hk <= 0 || hq % hk) {
+    set_global_error("sd_attention: bad arguments");
+    return SD_ERR_INVALID;
+  }
+  return op_result(sd::launch_attention((const __half*)q, (const __half*)k, (const __half*)v, (const __half*)gate, gstride, goff,
+                                        gstep, (__half*)out, l, p, lt, hq, hk, hd, (cudaStream_t)stream),
+                   "sd_attention");
+}
+
+int sd_gdn(const void* q, const void* k, int32_t qk_stride, const void* v, int32_t v_stride, const void* beta,
+           const void* decay, void* state, int32_t load_state, void* o, int32_t l, int32_t h, void* stream) {
+  if (!q || !k || !v || !beta || !decay || !state || !o || l <= 0 || h <= 0 || qk_stride % 4 || (size_t)q % 16 ||
+      (size_t)k % 16) {
+    set_global_error("sd_gdn: bad arguments");
+    return SD_ERR_INVALID;
+  }
+  return op_result(sd::launch_gdn_recurrent((const float*)q, (const float*)k, qk_stride, (const float*)v, v_stride,
+                                            (const float*)beta, (const float*)decay, (float*)state, load_state != 0, (float*)o,
+                                            l, h, (cudaStream_t)stream),
+                   "sd_gdn");
+}
+
+int sd_qweight_create(const void* q, const void* s, int32_t n, int32_t k, int32_t interleave, sd_qweight** out) {
+  if (!q || !s || !out || n <= 0 || k <= 0 || k % 64 || (interleave && n % 2)) {
+    set_global_error("sd_qweight_create: bad arguments (k must be a multiple of 64)");
+    return SD_ERR_INVALID;
+  }
+  auto w = std::make_unique<sd_qweight>();
+  cudaGetDevice(&w->device);
+  cudaError_t ce = sd::repack_weight((const uint8_t*)q, (const __half*)s, n, k, interleave != 0, &w->w, nullptr);
+  if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+  if (ce != cudaSuccess) return op_result(ce, "sd_qweight_create");
+  *out = w.release();
+  return SD_OK;
+}
+
+void sd_qweight_free(sd_qweight* w) {
+  if (!w) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(w->device);
+  cudaFree(w->w.tiles);
+  cudaSetDevice(prev);
+  delete w;
+}
+
+int sd_matmul(const sd_qweight* w, const void* act, int32_t m, void* y, int32_t ldy, int32_t silu, void* ws, size_t ws_bytes,
+              void* stream) {
+  if (!w || !act || !y || m <= 0 || (silu && !w->w.interleaved)) {
+    set_global_error("sd_matmul: bad arguments");
+    return SD_ERR_INVALID;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  static int* err_word[sd::kMaxDevices] = {};
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (!err_word[dev] && cudaMalloc(&err_word[dev], sizeof(int)) == cudaSuccess) cudaMemset(err_word[dev], 0, sizeof(int));
+  }
+  if (!err_word[dev]) return op_result(cudaErrorMemoryAllocation, "sd_matmul");
+  return op_result(sd::gemm_q4(w->w, (const __half*)act, m, w->w.k, (__half*)y, ldy, silu != 0, (float*)ws, ws_bytes,
+                               err_word[dev], sms, (cudaStream_t)stream),
+                   "sd_matmul");
+}
+
+}  // extern "C"

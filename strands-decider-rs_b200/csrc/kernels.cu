@@ -1,0 +1,382 @@
+// Row-wise and recurrent kernels of the torso: embedding, residual RMSNorm, short conv, gated delta
+// rule, gated RMSNorm, q/k RMSNorm + partial RoPE + KV-cache write. Each restates one of the
+// reference's WGSL kernels (cited per kernel) with the same rounding points: residual stream and
+// recurrent math in f32, f16 where the reference stores f16.
+#include "common.cuh"
+#include "sd_internal.h"
+
+namespace sd {
+
+// Block-wide sum over 256 threads (8 warps).
+__device__ __forceinline__ float block_sum256(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) t += red[i];
+  return t;
+}
+
+__device__ __forceinline__ uint32_t ld32u(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// The unsigned code of element e of block blk in a packed row (src/kernels.rs:63-71).
+__device__ __forceinline__ uint32_t code_of(const uint8_t* row, int bits, int blk, int e) {
+  const uint8_t* b = row + blk * 4 * bits;
+  if (bits == 4) return (ld32u(b + 4 * (e >> 3)) >> (4 * (e & 7))) & 15u;
+  uint32_t lo = (ld32u(b + 4 * (e >> 4)) >> (2 * (e & 15))) & 3u;
+  if (bits == 3) lo |= ((ld32u(b + 8) >> e) & 1u) << 2;
+  return lo;
+}
+
+// embed (src/kernels.rs:63-89) fused with layer 0's input RMSNorm (add_norm without the residual
+// add, src/kernels.rs:93-120): x[t] = dequant(table[ids[t]]) in f32, h[t] = f16(x * inv * w).
+__global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t* __restrict__ ids, const uint8_t* __restrict__ eq,
+                                                         const __half* __restrict__ es, int bits, int d, int vocab,
+                                                         const float* __restrict__ w, float* __restrict__ x,
+                                                         __half* __restrict__ h, int* err) {
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  uint32_t id = ids[t];
+  if (id >= (uint32_t)vocab) {
+    if (threadIdx.x == 0) atomicCAS(err, 0, kErrBadShape);
+    id = 0;
+  }
+  const int nb = d / 32;
+  const uint8_t* row = eq + (size_t)id * nb * 4 * bits;
+  const float half = (float)(1 << (bits - 1));
+  float v[8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int c = threadIdx.x + 256 * i;
+    float val = 0.0f;
+    if (c < d) {
+      const int blk = c >> 5;
+      val = ((float)code_of(row, bits, blk, c & 31) - half) * __half2float(es[(size_t)id * nb + blk]);
+      x[(size_t)t * d + c] = val;
+    }
+    v[i] = val;
+    ss += val * val;
+  }
+  const float inv = rsqrtf(block_sum256(ss, red) / (float)d + 1e-6f);
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int c = threadIdx.x + 256 * i;
+    if (c < d) h[(size_t)t * d + c] = __float2half_rn(v[i] * inv * w[c]);
+  }
+}
+
+// add_norm (src/kernels.rs:93-120): x += y (when add), h = f16(x * rsqrt(mean(x^2) + 1e-6) * w).
+// Thread i owns elements 8i..8i+7 (d = 2048).
+__global__ void __launch_bounds__(256) add_norm_kernel(float* __restrict__ x, const __half* __restrict__ y,
+                                                       const float* __restrict__ w, int d, int add,
+                                                       __half* __restrict__ h) {
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  float* xr = x + (size_t)t * d;
+  const int c0 = threadIdx.x * 8;
+  float v[8];
+  float4 a = *reinterpret_cast<const float4*>(xr + c0), b = *reinterpret_cast<const float4*>(xr + c0 + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  if (add) {
+    uint4 yy = *reinterpret_cast<const uint4*>(y + (size_t)t * d + c0);
+    const __half2* y2 = reinterpret_cast<const __half2*>(&yy);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      float2 f = __half22float2(y2[i]);
+      v[2 * i] += f.x;
+      v[2 * i + 1] += f.y;
+    }
+    *reinterpret_cast<float4*>(xr + c0) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(xr + c0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) ss += v[i] * v[i];
+  const float inv = rsqrtf(block_sum256(ss, red) / (float)d + 1e-6f);
+  float4 w0 = *reinterpret_cast<const float4*>(w + c0), w1 = *reinterpret_cast<const float4*>(w + c0 + 4);
+  const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  uint4 o;
+  __half2* o2 = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; i++) o2[i] = __floats2half2_rn(v[2 * i] * inv * ww[2 * i], v[2 * i + 1] * inv * ww[2 * i + 1]);
+  *reinterpret_cast<uint4*>(h + (size_t)t * d + c0) = o;
+}
+
+// The final norm (src/kernels.rs:93-120 with add and f32 out, src/engine.rs:519-522): for each
+// requested row, x += y, out = x * inv * w in f32.
+__global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, const __half* __restrict__ y,
+                                                         const float* __restrict__ w, const int* __restrict__ rows, int d,
+                                                         float* __restrict__ out) {
+  __shared__ float red[8];
+  const int r = rows[blockIdx.x];
+  float v[8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int c = threadIdx.x + 256 * i;
+    float a = 0.0f;
+    if (c < d) {
+      a = x[(size_t)r * d + c] + __half2float(y[(size_t)r * d + c]);
+      x[(size_t)r * d + c] = a;
+    }
+    v[i] = a;
+    ss += a * a;
+  }
+  const float inv = rsqrtf(block_sum256(ss, red) / (float)d + 1e-6f);
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int c = threadIdx.x + 256 * i;
+    if (c < d) out[(size_t)blockIdx.x * d + c] = v[i] * inv * w[c];
+  }
+}
+
+// conv (src/kernels.rs:152-170): depthwise causal conv, kernel 4, over the q/k/v channels of the
+// in_proj row, reading the 3-row history for t < 0; then SiLU, f32 out.
+__global__ void conv_kernel(const __half* __restrict__ big, int stride, const float4* __restrict__ cw,
+                            const __half* __restrict__ hist, int l, int C, float* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t = blockIdx.y;
+  if (c >= C) return;
+  const float4 k = cw[c];
+  const float kk[4] = {k.x, k.y, k.z, k.w};
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int tt = t + j - 3;
+    const float v = tt >= 0 ? __half2float(big[(size_t)tt * stride + c]) : __half2float(hist[(size_t)(tt + 3) * C + c]);
+    s += kk[j] * v;
+  }
+  out[(size_t)t * C + c] = s / (1.0f + __expf(-s));
+}
+
+// hist_update (src/kernels.rs:173-190): the last 3 pre-conv rows of (old history ++ this call).
+__global__ void hist_update_kernel(const __half* __restrict__ big, int stride, __half* __restrict__ hist, int l, int C) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  __half v[3];
+#pragma unroll
+  for (int r = 0; r < 3; r++) {
+    const int src = l - 3 + r;
+    v[r] = src >= 0 ? big[(size_t)src * stride + c] : hist[(size_t)(src + 3) * C + c];
+  }
+#pragma unroll
+  for (int r = 0; r < 3; r++) hist[(size_t)r * C + c] = v[r];
+}
+
+// The per-token gates of the gated delta rule (src/kernels.rs:289-292): beta = sigmoid(b),
+// decay = exp(negA * softplus(a + dt_bias)) with softplus(x) = x above 20.
+__global__ void gdn_gates_kernel(const __half* __restrict__ big, int stride, int aoff, int boff, const float* __restrict__ neg_a,
+                                 const float* __restrict__ dtb, int l, int h, float* __restrict__ beta,
+                                 float* __restrict__ decay) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= l * h) return;
+  const int t = i / h, hh = i % h;
+  const float a = __half2float(big[(size_t)t * stride + aoff + hh]);
+  const float b = __half2float(big[(size_t)t * stride + boff + hh]);
+  beta[i] = 1.0f / (1.0f + expf(-b));
+  const float x = a + dtb[hh];
+  const float sp = x > 20.0f ? x : logf(1.0f + expf(x));
+  decay[i] = expf(neg_a[hh] * sp);
+}
+
+// Gated delta rule, sequential over tokens (src/kernels.rs:257-302): one CTA per (head, 32 value
+// columns); warp w owns 8 columns, lane l key dims 4l..4l+3, so a 128x8 slice of the state lives in
+// 32 registers per lane. State [h][128][128] f32: loaded when continuing a prefix, always stored.
+__global__ void __launch_bounds__(128) gdn_recurrent_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                            int qk_stride, const float* __restrict__ v, int v_stride,
+                                                            const float* __restrict__ beta, const float* __restrict__ decay,
+                                                            float* __restrict__ state, int load_state,
+                                                            float* __restrict__ o, int l, int h) {
+  constexpr int DK = 128, DV = 128;
+  const int hh = blockIdx.x / (DV / 32);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dv0 = (blockIdx.x % (DV / 32)) * 32 + warp * 8;
+  float4 S[8];
+  float* sb = state + (size_t)hh * DK * DV + (size_t)(lane * 4) * DV + dv0;
+#pragma unroll
+  for (int c = 0; c < 8; c++)
+    S[c] = load_state ? make_float4(sb[c], sb[DV + c], sb[2 * DV + c], sb[3 * DV + c]) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float qs = rsqrtf((float)DK);
+  for (int t = 0; t < l; t++) {
+    const float4 q4 = *reinterpret_cast<const float4*>(q + (size_t)t * qk_stride + hh * DK + lane * 4);
+    const float4 k4 = *reinterpret_cast<const float4*>(k + (size_t)t * qk_stride + hh * DK + lane * 4);
+    const float sq = warp_sum(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
+    const float sk = warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w);
+    const float rq = rsqrtf(sq + 1e-6f) * qs, rk = rsqrtf(sk + 1e-6f);
+    const float4 qn = make_float4(q4.x * rq, q4.y * rq, q4.z * rq, q4.w * rq);
+    const float4 kn = make_float4(k4.x * rk, k4.y * rk, k4.z * rk, k4.w * rk);
+    const float dc = decay[(size_t)t * h + hh], bt = beta[(size_t)t * h + hh];
+    const float* vt = v + (size_t)t * v_stride + hh * DV + dv0;
+    float mine = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      float4 s = S[c];
+      s.x *= dc; s.y *= dc; s.z *= dc; s.w *= dc;
+      const float kv = warp_sum(s.x * kn.x + s.y * kn.y + s.z * kn.z + s.w * kn.w);
+      const float delta = (vt[c] - kv) * bt;
+      s.x += kn.x * delta; s.y += kn.y * delta; s.z += kn.z * delta; s.w += kn.w * delta;
+      const float oc = warp_sum(s.x * qn.x + s.y * qn.y + s.z * qn.z + s.w * qn.w);
+      if (lane == c) mine = oc;
+      S[c] = s;
+    }
+    if (lane < 8) o[(size_t)t * h * DV + hh * DV + dv0 + lane] = mine;
+  }
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    sb[c] = S[c].x;
+    sb[DV + c] = S[c].y;
+    sb[2 * DV + c] = S[c].z;
+    sb[3 * DV + c] = S[c].w;
+  }
+}
+
+// gnorm (src/kernels.rs:377-396): per (token, head) RMSNorm over DV = 128, times w and silu(z),
+// z from the in_proj row at zoff; one warp per (token, head).
+__global__ void __launch_bounds__(128) gnorm_kernel(const float* __restrict__ o, const __half* __restrict__ big, int stride,
+                                                    int zoff, const float* __restrict__ w, int l, int h,
+                                                    __half* __restrict__ out) {
+  constexpr int DV = 128;
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= l * h) return;
+  const int t = row / h, hh = row % h;
+  const float* src = o + (size_t)t * h * DV + hh * DV;
+  float v[4];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    v[i] = src[lane + 32 * i];
+    ss += v[i] * v[i];
+  }
+  const float inv = rsqrtf(warp_sum(ss) / (float)DV + 1e-6f);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int c = lane + 32 * i;
+    const float z = __half2float(big[(size_t)t * stride + zoff + hh * DV + c]);
+    out[(size_t)t * h * DV + hh * DV + c] = __float2half_rn(w[c] * v[i] * inv * z / (1.0f + __expf(-z)));
+  }
+}
+
+// qk_prep (src/kernels.rs:400-448): per (token, head slot) RMSNorm over HD times the q or k norm
+// weight, rotate-half RoPE on the first RD dims from the f32 table, Q out [HQ][L][HD] f16, K and V
+// into the caches [HK][LT][HD] at position p + t.
+__global__ void __launch_bounds__(256) qk_prep_kernel(const __half* __restrict__ big, int stride, const float* __restrict__ qw,
+                                                      const float* __restrict__ kw, const float2* __restrict__ rope, int l,
+                                                      int p, int lt, int hq, int hk, int rd, __half* __restrict__ qo,
+                                                      __half* __restrict__ ko, __half* __restrict__ vo) {
+  constexpr int HD = 256;
+  __shared__ float red[8];
+  __shared__ float nv[HD];
+  const int t = blockIdx.x, s = blockIdx.y, d = threadIdx.x;
+  const bool isq = s < hq;
+  const int pos = p + t;
+  const __half* row = big + (size_t)t * stride;
+  const int koff = hq * HD * 2, voff = koff + hk * HD;
+  if (!isq) {
+    const int kh = s - hq;
+    vo[((size_t)kh * lt + pos) * HD + d] = row[voff + kh * HD + d];
+  }
+  const float v = __half2float(row[isq ? s * 2 * HD + d : koff + (s - hq) * HD + d]);
+  const float tot = block_sum256(v * v, red);
+  const float n = v * rsqrtf(tot / (float)HD + 1e-6f) * (isq ? qw[d] : kw[d]);
+  nv[d] = n;
+  __syncthreads();
+  float r = n;
+  const int rd2 = rd / 2;
+  if (d < rd) {
+    const float2 cs = rope[(size_t)pos * rd2 + (d % rd2)];
+    r = d < rd2 ? n * cs.x - nv[d + rd2] * cs.y : n * cs.x + nv[d - rd2] * cs.y;
+  }
+  if (isq) qo[((size_t)s * l + t) * HD + d] = __float2half_rn(r);
+  else ko[((size_t)(s - hq) * lt + pos) * HD + d] = __float2half_rn(r);
+}
+
+__global__ void trace_kernel(const float* __restrict__ x, const __half* __restrict__ y, int n, float* __restrict__ out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = x[i] + __half2float(y[i]);
+}
+
+// add_bias (src/kernels.rs:138-149): y = f16(y + c[j]).
+__global__ void add_bias_kernel(__half* __restrict__ y, const float* __restrict__ c, int n, int d) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    y[i] = __float2half_rn(__half2float(y[i]) + c[i % d]);
+}
+
+// ---------------------------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------------------------
+static int blocks_for(int64_t n, int per) { return (int)std::min<int64_t>((n + per - 1) / per, 65535); }
+
+cudaError_t launch_embed_norm(const uint32_t* ids, int l, const uint8_t* eq, const __half* es, int bits, int d, int vocab,
+                              const float* w, float* x, __half* h, int* err, cudaStream_t st) {
+  if (d > 2048 || d % 32) return cudaErrorInvalidValue;
+  embed_norm_kernel<<<l, 256, 0, st>>>(ids, eq, es, bits, d, vocab, w, x, h, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add_norm(float* x, const __half* y, const float* w, int l, int d, bool add, __half* h, cudaStream_t st) {
+  if (d != 2048) return cudaErrorInvalidValue;
+  add_norm_kernel<<<l, 256, 0, st>>>(x, y, w, d, add ? 1 : 0, h);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int d, float* out,
+                              cudaStream_t st) {
+  if (nrows <= 0) return cudaSuccess;
+  final_norm_kernel<<<nrows, 256, 0, st>>>(x, y, w, rows, d, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, float* qkvc,
+                        cudaStream_t st) {
+  dim3 grid((C + 255) / 256, l);
+  conv_kernel<<<grid, 256, 0, st>>>(big, stride, reinterpret_cast<const float4*>(conv_w), hist, l, C, qkvc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_hist_update(const __half* big, int stride, __half* hist, int l, int C, cudaStream_t st) {
+  hist_update_kernel<<<(C + 255) / 256, 256, 0, st>>>(big, stride, hist, l, C);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gdn_gates(const __half* big, int stride, int aoff, int boff, const float* neg_a, const float* dt_bias,
+                             int l, int h, float* beta, float* decay, cudaStream_t st) {
+  gdn_gates_kernel<<<blocks_for((int64_t)l * h, 256), 256, 0, st>>>(big, stride, aoff, boff, neg_a, dt_bias, l, h, beta, decay);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gdn_recurrent(const float* q, const float* k, int qk_stride, const float* v, int v_stride,
+                                 const float* beta, const float* decay, float* state, bool load_state, float* o, int l,
+                                 int h, cudaStream_t st) {
+  gdn_recurrent_kernel<<<h * 4, 128, 0, st>>>(q, k, qk_stride, v, v_stride, beta, decay, state, load_state ? 1 : 0, o, l, h);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff, const float* w, int l, int h, __half* out,
+                         cudaStream_t st) {
+  gnorm_kernel<<<(l * h + 3) / 4, 128, 0, st>>>(o, big, stride, zoff, w, l, h, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,
+                           int lt, const Dims& dm, __half* q, __half* kc, __half* vc, cudaStream_t st) {
+  if (dm.hd != 256) return cudaErrorInvalidValue;
+  dim3 grid(l, dm.hq + dm.hk);
+  qk_prep_kernel<<<grid, 256, 0, st>>>(big, stride, qw, kw, reinterpret_cast<const float2*>(rope), l, p, lt, dm.hq, dm.hk,
+                                       dm.rd, q, kc, vc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_trace(const float* x, const __half* y, int n, float* out, cudaStream_t st) {
+  trace_kernel<<<blocks_for(n, 256), 256, 0, st>>>(x, y, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add_bias(__half* y, const float* bias, int l, int d, cudaStream_t st) {
+  add_bias_kernel<<<blocks_for((int64_t)l * d, 256), 256, 0, st>>>(y, bias, l * d, d);
+  return cudaGetLastError();
+}
+
+}  // namespace sd

@@ -1,0 +1,63 @@
+// Internal interfaces between the engine (engine.cu) and the kernel files.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace sd {
+
+constexpr int kMaxDevices = 64;
+
+// A block-quantized int4 weight repacked into the GEMM's tile layout (gemm.cu).
+struct QWeight {
+  uint8_t* tiles = nullptr;
+  size_t bytes = 0;
+  int n = 0, k = 0, npad = 0;
+  bool interleaved = false;
+};
+
+cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool interleave, QWeight* out, cudaStream_t st);
+void gemm_plan(const QWeight& w, int M, int num_sms, int* bn, int* splits, int* kps);
+cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
+                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st);
+int make_act_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
+
+// Model dims the kernels are specialised for (src/kernels.rs:813-835).
+struct Dims {
+  int d = 2048, inter = 6144;
+  int h = 16, dk = 128, dv = 128;  // gated delta
+  int hq = 8, hk = 2, hd = 256, rd = 64;
+  int C() const { return 2 * h * dk + h * dv; }
+};
+
+// kernels.cu
+cudaError_t launch_embed_norm(const uint32_t* ids, int l, const uint8_t* eq, const __half* es, int bits, int d, int vocab,
+                              const float* w, float* x, __half* h, int* err, cudaStream_t st);
+cudaError_t launch_add_norm(float* x, const __half* y, const float* w, int l, int d, bool add, __half* h, cudaStream_t st);
+cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int d, float* out,
+                              cudaStream_t st);
+cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, float* qkvc,
+                        cudaStream_t st);
+cudaError_t launch_hist_update(const __half* big, int stride, __half* hist, int l, int C, cudaStream_t st);
+cudaError_t launch_gdn_gates(const __half* big, int stride, int aoff, int boff, const float* neg_a, const float* dt_bias,
+                             int l, int h, float* beta, float* decay, cudaStream_t st);
+cudaError_t launch_gdn_recurrent(const float* q, const float* k, int qk_stride, const float* v, int v_stride,
+                                 const float* beta, const float* decay, float* state, bool load_state, float* o, int l,
+                                 int h, cudaStream_t st);
+cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff, const float* w, int l, int h, __half* out,
+                         cudaStream_t st);
+cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,
+                           int lt, const Dims& dm, __half* q, __half* kc, __half* vc, cudaStream_t st);
+cudaError_t launch_trace(const float* x, const __half* y, int n, float* out, cudaStream_t st);
+cudaError_t launch_add_bias(__half* y, const float* bias, int l, int d, cudaStream_t st);
+
+// attn.cu: causal GQA attention with the sigmoid output gate (src/kernels.rs:453-541).
+// q [hq][l][hd] (rows for this call), k/v caches [hk][lt][hd] with this call's rows at p..p+l-1,
+// gate at gate[t * gstride + goff + h * gstep + d] (null: ungated), out [l][hq * hd].
+cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, const __half* gate, int gstride, int goff,
+                             int gstep, __half* out, int l, int p, int lt, int hq, int hk, int hd, cudaStream_t st);
+
+}  // namespace sd

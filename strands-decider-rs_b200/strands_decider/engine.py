@@ -1,0 +1,222 @@
+"""ctypes binding of the C ABI in include/sd_b200.h (libsdb200.so, built from ../csrc).
+
+`Engine` mirrors the reference's `Engine` (`src/engine.rs:175,305,529`): `load`, `hidden_size`,
+`forward(ids, rows, cache, keep, timed)` returning an `Output`, and immutable `Snapshot`s. `Head`
+mirrors `src/head.rs`. There is no fallback: without the native library every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG, "libsdb200.so")
+
+SD_OK = 0
+CONTEXT = 4096  # `src/engine.rs:16`
+
+
+class Error(RuntimeError):
+    """The reference's `Error(String)` (`src/lib.rs:23-44`), with the C ABI's status code."""
+
+    def __init__(self, msg: str, code: int = -1):
+        super().__init__(msg)
+        self.code = code
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise Error(f"{LIB_PATH} is missing: build it with `make -C {os.path.join(PKG, 'csrc')}` "
+                        "(or __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        vp, i32, cp = C.c_void_p, C.c_int32, C.c_char_p
+        L.sd_last_error.restype = cp
+        L.sd_engine_create.argtypes = [cp, C.c_int, C.POINTER(vp)]
+        L.sd_engine_destroy.argtypes = [vp]
+        L.sd_engine_hidden_size.argtypes = [vp]
+        L.sd_engine_num_layers.argtypes = [vp]
+        L.sd_engine_last_error.restype = cp
+        L.sd_engine_last_error.argtypes = [vp]
+        L.sd_engine_set_trace.argtypes = [vp, vp, C.c_size_t]
+        L.sd_forward.argtypes = [vp, vp, i32, vp, i32, vp, i32, vp, C.POINTER(vp), C.POINTER(C.c_double)]
+        L.sd_snapshot_len.restype = i32
+        L.sd_snapshot_len.argtypes = [vp]
+        L.sd_snapshot_free.argtypes = [vp]
+        L.sd_head_load.argtypes = [cp, C.POINTER(vp)]
+        L.sd_head_free.argtypes = [vp]
+        L.sd_head_probs.argtypes = [vp, vp, i32, i32, C.c_double, vp]
+        L.sd_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]
+        L.sd_gdn.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, vp]
+        L.sd_qweight_create.argtypes = [vp, vp, i32, i32, i32, C.POINTER(vp)]
+        L.sd_qweight_free.argtypes = [vp]
+        L.sd_matmul.argtypes = [vp, vp, i32, vp, i32, i32, vp, C.c_size_t, vp]
+        _lib = L
+    return _lib
+
+
+def _check(rc: int, what: str, engine=None):
+    if rc != SD_OK:
+        L = lib()
+        msg = (L.sd_engine_last_error(engine) if engine else L.sd_last_error()).decode(errors="replace")
+        raise Error(f"{what}: {msg}", rc)
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data
+
+
+class Snapshot:
+    """The torso state after a prefix (`src/engine.rs:80-87`): immutable, reusable, freed with it."""
+
+    def __init__(self, handle: int):
+        self._h = handle
+
+    @property
+    def len(self) -> int:
+        return lib().sd_snapshot_len(self._h)
+
+    def close(self):
+        if self._h:
+            lib().sd_snapshot_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+@dataclass
+class Output:
+    """`Output` (`src/engine.rs:88-96`): hidden rows [rows, d] f32, GPU time, optional snapshot."""
+    hidden: np.ndarray
+    d: int
+    gpu_ms: float | None
+    snapshot: Snapshot | None
+
+
+class Engine:
+    """The torso on one B200 (`Engine`, `src/engine.rs`)."""
+
+    def __init__(self, handle: int, device: int):
+        self._h = handle
+        self.device = device
+        self.adapter = f"NVIDIA B200 (cuda:{device}, sm_100a)"
+        self._trace = None
+
+    @classmethod
+    def load(cls, model_dir: str, device: int = 0) -> "Engine":
+        """`Engine::load` (`src/engine.rs:175-303`)."""
+        h = C.c_void_p()
+        _check(lib().sd_engine_create(os.fsencode(model_dir), device, C.byref(h)), "Engine::load")
+        return cls(h.value, device)
+
+    def hidden_size(self) -> int:
+        return lib().sd_engine_hidden_size(self._h)
+
+    def num_layers(self) -> int:
+        return lib().sd_engine_num_layers(self._h)
+
+    def forward(self, ids, rows, cache: Snapshot | None = None, keep: bool = False, timed: bool = False,
+                trace: bool = False) -> Output:
+        """`Engine::forward` (`src/engine.rs:529-662`). With ``trace``, ``Output.trace`` holds the
+        residual stream after each layer [n_layers, n_ids, d]."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        rows = np.ascontiguousarray(rows, np.int32)
+        d = self.hidden_size()
+        hidden = np.zeros((len(rows), d), np.float32)
+        snap = C.c_void_p()
+        ms = C.c_double(0.0)
+        L = lib()
+        tr = None
+        if trace:
+            tr = np.zeros((self.num_layers(), len(ids), d), np.float32)
+            _check(L.sd_engine_set_trace(self._h, _ptr(tr), tr.size), "trace", self._h)
+        try:
+            rc = L.sd_forward(self._h, _ptr(ids), len(ids), _ptr(rows) if len(rows) else None, len(rows),
+                              cache._h if cache is not None else None, int(keep), _ptr(hidden) if len(rows) else None,
+                              C.byref(snap), C.byref(ms))
+        finally:
+            if trace:
+                L.sd_engine_set_trace(self._h, None, 0)
+        _check(rc, "Engine::forward", self._h)
+        out = Output(hidden, d, ms.value if timed else None, Snapshot(snap.value) if keep else None)
+        out.trace = tr
+        return out
+
+    def close(self):
+        if self._h:
+            lib().sd_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Head:
+    """The pointer head (`src/head.rs`), in f64 on the host."""
+
+    def __init__(self, handle: int):
+        self._h = handle
+
+    @classmethod
+    def load(cls, path: str) -> "Head":
+        h = C.c_void_p()
+        _check(lib().sd_head_load(os.fsencode(path), C.byref(h)), "Head::load")
+        return cls(h.value)
+
+    def probs(self, hidden: np.ndarray, d: int, temperature: float) -> np.ndarray:
+        hidden = np.ascontiguousarray(hidden, np.float32).reshape(-1, d)
+        out = np.zeros(hidden.shape[0] - 1, np.float64)
+        _check(lib().sd_head_probs(self._h, _ptr(hidden), hidden.shape[0], d, float(temperature), _ptr(out)), "Head::probs")
+        return out
+
+    def __del__(self):
+        try:
+            if self._h:
+                lib().sd_head_free(self._h)
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------------------------------
+# Kernel-level entry points on device memory (pointers as ints, e.g. torch.Tensor.data_ptr())
+# ---------------------------------------------------------------------------------------------
+
+def attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, stream=None):
+    _check(lib().sd_attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, stream), "sd_attention")
+
+
+def gdn(q, k, qk_stride, v, v_stride, beta, decay, state, load_state, o, l, h, stream=None):
+    _check(lib().sd_gdn(q, k, qk_stride, v, v_stride, beta, decay, state, int(load_state), o, l, h, stream), "sd_gdn")
+
+
+class QWeight:
+    def __init__(self, q_dev: int, s_dev: int, n: int, k: int, interleave: bool = False):
+        h = C.c_void_p()
+        _check(lib().sd_qweight_create(q_dev, s_dev, n, k, int(interleave), C.byref(h)), "sd_qweight_create")
+        self._h = h.value
+        self.n, self.k = n, k
+
+    def matmul(self, act_dev: int, m: int, y_dev: int, ldy: int, silu: bool = False, ws_dev: int | None = None,
+               ws_bytes: int = 0, stream=None):
+        _check(lib().sd_matmul(self._h, act_dev, m, y_dev, ldy, int(silu), ws_dev, ws_bytes, stream), "sd_matmul")
+
+    def __del__(self):
+        try:
+            if self._h:
+                lib().sd_qweight_free(self._h)
+        except Exception:
+            pass

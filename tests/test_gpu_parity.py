@@ -1,0 +1,227 @@
+"""The CUDA path through the C ABI against the CPU oracle, on the same seeded inputs.
+
+Tolerances (from the build's parity targets): per-layer hidden states within 2e-2 max-abs; answer
+probabilities within 1e-3 with identical argmax; single kernels as stated per test (f16 outputs:
+a few f16 ulps; f32 recurrences: 1e-4 relative)."""
+import numpy as np
+import pytest
+
+from oracle import oracle
+from strands_decider import model as M
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("m", [1, 7, 33, 130, 300, 700])
+@pytest.mark.parametrize("n,k", [(8256, 2048), (2048, 6144)])
+def test_matmul_matches_oracle(torch, m, n, k):
+    from strands_decider.engine import QWeight
+    rng = np.random.default_rng(m * 7 + n)
+    packed, scales = M._quant_tensor(rng, n, k, 4, 1.0 / np.sqrt(k))
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    want = oracle.matmul(a, packed, scales, n, k, 4, variant=2).astype(np.float32)  # f16 dequant, f32 acc
+    q_d, s_d, a_d = dev(torch, packed), dev(torch, scales.view(np.uint16)), dev(torch, a.view(np.uint16))
+    w = QWeight(q_d.data_ptr(), s_d.data_ptr(), n, k)
+    y = torch.zeros((m, n), dtype=torch.float16, device="cuda")
+    ws = torch.zeros(m * n, dtype=torch.float32, device="cuda")
+    for ws_bytes in (0, ws.numel() * 4):  # without and with split-K
+        y.zero_()
+        w.matmul(a_d.data_ptr(), m, y.data_ptr(), n, ws_dev=ws.data_ptr(), ws_bytes=ws_bytes)
+        torch.cuda.synchronize()
+        got = y.cpu().numpy().astype(np.float32)
+        err = np.abs(got - want)
+        assert err.max() <= 2e-3 + 2e-3 * np.abs(want).max(), (ws_bytes, err.max())
+
+
+@pytest.mark.parametrize("m", [5, 64, 200])
+def test_matmul_swiglu_epilogue(torch, m):
+    from strands_decider.engine import QWeight
+    rng = np.random.default_rng(m)
+    n, k = 2 * 6144, 2048
+    packed, scales = M._quant_tensor(rng, n, k, 4, 1.0 / np.sqrt(k))
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    big = oracle.matmul(a, packed, scales, n, k, 4, variant=2).astype(np.float32)
+    g, u = big[:, :n // 2], big[:, n // 2:]
+    want = (g / (1 + np.exp(-g)) * u).astype(np.float16).astype(np.float32)
+    q_d, s_d, a_d = dev(torch, packed), dev(torch, scales.view(np.uint16)), dev(torch, a.view(np.uint16))
+    w = QWeight(q_d.data_ptr(), s_d.data_ptr(), n, k, interleave=True)
+    y = torch.zeros((m, n // 2), dtype=torch.float16, device="cuda")
+    ws = torch.zeros(m * n, dtype=torch.float32, device="cuda")
+    for ws_bytes in (0, ws.numel() * 4):
+        w.matmul(a_d.data_ptr(), m, y.data_ptr(), n // 2, silu=True, ws_dev=ws.data_ptr(), ws_bytes=ws_bytes)
+        torch.cuda.synchronize()
+        got = y.cpu().numpy().astype(np.float32)
+        assert np.abs(got - want).max() <= 4e-3 + 4e-3 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("l,p", [(300, 0), (37, 500), (1, 100), (129, 0)])
+def test_attention_matches_oracle(torch, l, p):
+    from strands_decider.engine import attention
+    rng = np.random.default_rng(l + p)
+    hq, hk, hd, lt = 8, 2, 256, 4096
+    q = rng.standard_normal((hq, l, hd)).astype(np.float16)
+    kc = np.zeros((hk, lt, hd), np.float16)
+    vc = np.zeros((hk, lt, hd), np.float16)
+    kc[:, :p + l] = rng.standard_normal((hk, p + l, hd))
+    vc[:, :p + l] = rng.standard_normal((hk, p + l, hd))
+    kc[:, p + l:] = np.nan  # rows past the valid keys must never be read
+    vc[:, p + l:] = np.nan
+    gate = rng.standard_normal((l, 5120)).astype(np.float16)
+    want = oracle.attn(q, kc[:, :p + l], vc[:, :p + l], gate, 5120, hd, 2 * hd, p=p).astype(np.float32)
+    out = torch.zeros((l, hq * hd), dtype=torch.float16, device="cuda")
+    qd, kd, vd, gd = (dev(torch, x.view(np.uint16)) for x in (q, kc, vc, gate))
+    attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), gd.data_ptr(), 5120, hd, 2 * hd, out.data_ptr(), l, p, lt, hq, hk, hd)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float32)
+    assert np.isfinite(got).all()
+    assert np.abs(got - want).max() < 4e-3
+
+
+def test_gdn_matches_oracle(torch):
+    from strands_decider.engine import gdn
+    rng = np.random.default_rng(11)
+    l, h = 200, 16
+    q = rng.standard_normal((l, h, 128)).astype(np.float32)
+    k = rng.standard_normal((l, h, 128)).astype(np.float32)
+    v = rng.standard_normal((l, h, 128)).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((l, h))))).astype(np.float32)
+    decay = np.exp(-np.log1p(np.exp(rng.standard_normal((l, h))))).astype(np.float32)
+    s0 = (0.1 * rng.standard_normal((h, 128, 128))).astype(np.float32)
+    for load in (False, True):
+        o_want, s_want = oracle.gdn(q, k, v, beta, decay, s0 if load else None)
+        qd, kd, vd, bd, dd = (dev(torch, x) for x in (q, k, v, beta, decay))
+        sd_ = dev(torch, s0.copy())
+        od = torch.zeros((l, h * 128), dtype=torch.float32, device="cuda")
+        gdn(qd.data_ptr(), kd.data_ptr(), h * 128, vd.data_ptr(), h * 128, bd.data_ptr(), dd.data_ptr(), sd_.data_ptr(), load,
+            od.data_ptr(), l, h)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(od.cpu().numpy(), o_want, rtol=1e-4, atol=1e-4)
+        np.testing.assert_allclose(sd_.cpu().numpy(), s_want, rtol=1e-4, atol=1e-4)
+
+
+@pytest.fixture(scope="module")
+def engines(small_model):
+    from strands_decider.engine import Engine
+    return Engine.load(small_model), oracle.Engine(small_model)
+
+
+@pytest.mark.parametrize("l", [9, 40, 300])
+def test_engine_layers_match_oracle(engines, l):
+    gpu, cpu = engines
+    rng = np.random.default_rng(l)
+    ids = rng.integers(0, 8192, l)
+    rows = sorted(set([0, l // 2, l - 1]))
+    out = gpu.forward(ids, rows, trace=True)
+    want, _, tr = cpu.forward(ids, rows, trace=True)
+    per_layer = np.abs(out.trace - tr).max(axis=(1, 2))
+    assert per_layer.max() < 2e-2, per_layer
+    assert np.abs(out.hidden - want).max() < 2e-2
+
+
+def test_engine_probabilities_match_oracle(engines, small_model):
+    from strands_decider.engine import Head
+    gpu, cpu = engines
+    head = Head.load(f"{small_model}/head.safetensors")
+    tensors = M.read_safetensors(f"{small_model}/head.safetensors")
+    rng = np.random.default_rng(3)
+    worst = 0.0
+    for case in range(6):
+        l = int(rng.integers(20, 400))
+        ids = rng.integers(0, 8192, l)
+        nopt = int(rng.integers(2, 6))
+        rows = sorted(rng.choice(l - 1, nopt, replace=False).tolist()) + [l - 1]
+        a = head.probs(gpu.forward(ids, rows).hidden, 2048, 1.0)
+        b = oracle.head_probs(cpu.forward(ids, rows)[0], tensors, 1.0)
+        worst = max(worst, np.abs(a - b).max())
+        assert np.argmax(a) == np.argmax(b)
+    assert worst < 1e-3, worst
+
+
+def test_prefix_cache_matches_full_forwards(engines):
+    """`tests/engine_parity.rs:59-85` on the GPU engine: max |dp| < 2e-3."""
+    from strands_decider.engine import Head
+    gpu, _ = engines
+    rng = np.random.default_rng(5)
+    state = rng.integers(0, 8000, 150)
+    snap = gpu.forward(state, [], keep=True).snapshot
+    assert snap.len == 150
+    for ql in (24, 48, 7):
+        q = rng.integers(0, 8000, ql)
+        rows = [2, ql // 2, ql - 1]
+        a = gpu.forward(q, rows, cache=snap).hidden
+        b = gpu.forward(np.concatenate([state, q]), [150 + r for r in rows]).hidden
+        assert np.abs(a - b).max() < 2e-2
+    # the snapshot is immutable: the same continuation twice is bit-identical
+    q = rng.integers(0, 8000, 30)
+    a = gpu.forward(q, [29], cache=snap).hidden
+    b = gpu.forward(q, [29], cache=snap).hidden
+    assert np.array_equal(a, b)
+    snap.close()
+
+
+def test_snapshot_of_continuation(engines):
+    gpu, cpu = engines
+    rng = np.random.default_rng(9)
+    s1, s2, q = rng.integers(0, 8000, 60), rng.integers(0, 8000, 40), rng.integers(0, 8000, 25)
+    a = gpu.forward(s1, [], keep=True).snapshot
+    b = gpu.forward(s2, [], cache=a, keep=True).snapshot
+    assert b.len == 100
+    got = gpu.forward(q, [24], cache=b).hidden
+    want = cpu.forward(np.concatenate([s1, s2, q]), [124])[0]
+    assert np.abs(got - want).max() < 2e-2
+
+
+def test_engine_errors(engines):
+    from strands_decider.engine import Error
+    gpu, _ = engines
+    with pytest.raises(Error, match="out of range"):
+        gpu.forward([1, 2, 3], [3])
+    with pytest.raises(Error, match="context of"):
+        gpu.forward(np.zeros(4097, np.int64), [])
+    with pytest.raises(Error, match="token id"):
+        gpu.forward([1, 999999], [0])
+    snap = gpu.forward(np.zeros(4000, np.int64), [], keep=True).snapshot
+    with pytest.raises(Error, match="context of"):
+        gpu.forward(np.zeros(100, np.int64), [0], cache=snap)
+    # the engine still works after the failures
+    assert gpu.forward([5, 6, 7], [2]).hidden.shape == (1, 2048)
+
+
+def test_decider_answers_match_oracle(small_model):
+    """`Decider::ask_all` through the GPU engine against the same pipeline through the oracle."""
+    from strands_decider import Decider, Question
+    from strands_decider import prompt
+    dec = Decider.load(small_model)
+    state = "Help! My payouts have been failing for 3 days! " * 3
+    qs = [Question.noul("Does this convey urgency?"),
+          Question.choice("Which team should handle this?", ["billing", "technical", "sales"]),
+          Question.score("How frustrated is the writer?", ["calm", "frustrated", "very angry"])]
+    answers = dec.ask_all(state, qs)
+    named = [(str(i), q) for i, q in enumerate(qs)]
+    rendered, sids, qencs, options = dec.encode(state, named)
+    cpu = oracle.Engine(small_model)
+    tensors = M.read_safetensors(f"{small_model}/head.safetensors")
+    snap = cpu.forward(sids, [], keep=True)[1]
+    for i, (q, a) in enumerate(zip(qencs, answers)):
+        rows = list(options[i]) + [len(q.ids) - 1]
+        probs = oracle.head_probs(cpu.forward(q.ids, rows, cache=snap)[0], tensors, 1.0)
+        want = prompt.to_answer(rendered[i], probs, 0.0)
+        got_p = dict(a.probabilities) if a.probabilities else {"true": a.noul}
+        want_p = dict(want.probabilities) if want.probabilities else {"true": want.noul}
+        for kk in want_p:
+            assert abs(got_p[kk] - want_p[kk]) <= 1e-3 + 1e-4  # 4-decimal rounding on both sides
+        if a.kind == "choice":
+            assert a.choice == want.choice
+    one = dec.ask(state, qs[1])
+    assert one.kind == "choice"
