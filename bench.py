@@ -1,0 +1,392 @@
+#!/usr/bin/env python
+"""Benchmark of the sequence-mixing forward: answered questions/s on the throughput sweep.
+
+Workload (the reference's headline metric is answered questions/s and prefill tok/s; the sweep is the
+configuration it is quoted on): independent requests of the full random-init 24-layer model, each a
+state of 64-4096 random non-special token ids (clipped so state + longest question fits the
+4096-token context) and 3 questions (noul: 2 options, choice: 3, score: 3) of 42-84 tokens. A request
+runs as the reference's `Decider::run` does (src/lib.rs:185-198): the state once with a snapshot,
+then each question continued from the snapshot, hidden rows at the option tokens and the last token,
+then the pointer head. A step is a batch of --requests-per-step requests per GPU (weak scaling:
+each rank takes its own requests, no collective on the data path).
+
+`value`: device-resident inputs (token ids and rows staged in HBM before the timed region),
+forwards queued with sd_forward_dev, hidden rows left in HBM; CUDA events on the engine's stream.
+`e2e`: the same requests through the C ABI with host buffers (sd_forward: ids host->device, hidden
+rows device->host, synchronous per call) and the pointer head on the host (sd_head_probs).
+`roofline`: the dominant kernel (the dequantizing GEMM), from per-launch CUDA events on the engine's
+stream over a profiled pass of the same steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "strands-decider-rs_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+VOCAB = 248320
+SPECIAL = (6000, 6001, 6002)  # the synthetic tokenizer's added tokens
+N_REQUESTS = 8192
+CONTEXT = 4096
+QLEN = (42, 84)  # question token counts of the reference's fixtures (tests/golden/prompt_cases.json)
+KINDS = (("noul", 2), ("choice", 3), ("score", 3))
+
+
+def request(i: int, seed: int = 0):
+    """Request i of the seeded sweep: (state ids, [(question ids, rows)] x 3, clipped?)."""
+    rng = np.random.default_rng([seed, i])
+    qlens = rng.integers(QLEN[0], QLEN[1] + 1, 3)
+    s = int(rng.integers(64, 4097))
+    clipped = s + int(qlens.max()) > CONTEXT
+    s = min(s, CONTEXT - int(qlens.max()))
+
+    def ids(n):
+        x = rng.integers(0, VOCAB - len(SPECIAL), n)
+        return (x + (x >= SPECIAL[0]) * len(SPECIAL)).astype(np.uint32)
+    qs = []
+    for (_, nopt), ql in zip(KINDS, qlens):
+        ql = int(ql)
+        rows = sorted(rng.choice(np.arange(ql // 2, ql - 1), nopt, replace=False).tolist()) + [ql - 1]
+        qs.append((ids(ql), np.array(rows, np.int32)))
+    return ids(s), qs, clipped
+
+
+def sweep_stats(seed: int = 0, n: int = N_REQUESTS):
+    """Mean state length, tokens per question and clip count over the whole sweep (lengths only)."""
+    tot_state = tot_tokens = clips = 0
+    for i in range(n):
+        rng = np.random.default_rng([seed, i])
+        qlens = rng.integers(QLEN[0], QLEN[1] + 1, 3)
+        s = int(rng.integers(64, 4097))
+        clips += s + int(qlens.max()) > CONTEXT
+        s = min(s, CONTEXT - int(qlens.max()))
+        tot_state += s
+        tot_tokens += s + int(qlens.sum())
+    return tot_state / n, tot_tokens / (3 * n), clips
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        rows = [ln.split(",") for ln in open(self.f.name).read().strip().splitlines() if ln.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        mx = max(float(r[2]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in rows for j in range(4) if "Active" in r[5 + j] and "Not" not in r[5 + j]})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return m["hbm_gbs"], m["bf16_tflops"], m["bf16_tflops_sustained"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(minutes=10), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, x: float) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(world, x: float) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def model_path(world, rank):
+    from strands_decider import model
+    path = os.path.join(ROOT, "_models", "full_s0")
+    if rank == 0:
+        model.ensure_model(path, seed=0)
+    barrier(world)
+    return path
+
+
+def step_requests(step: int, rank: int, world: int, per: int):
+    base = (step * world + rank) * per
+    return [(base + j) % N_REQUESTS for j in range(per)]
+
+
+def cpu_baseline(path: str, seed: int = 0, state_len: int = 96):
+    """The oracle (the CPU restatement of the reference's shader math) on a bounded sample: request 0's
+    three questions after a state cut to `state_len` tokens; throughput scaled to the sweep's mean
+    tokens per question (cost is linear in tokens to within the attention share, about 2%)."""
+    from oracle import oracle
+    eng = oracle.Engine(path)
+    sids, qs, _ = request(0, seed)
+    sids = sids[:state_len]
+    t0 = time.perf_counter()
+    _, snap, _ = eng.forward(sids, [], keep=True)
+    for qids, rows in qs:
+        eng.forward(qids, rows, cache=snap)
+    dt = time.perf_counter() - t0
+    tokens = len(sids) + sum(len(q) for q, _ in qs)
+    return dt, tokens
+
+
+def run_reference(args, world, rank):
+    """`--impl reference`: the reference's own CPU path for the sweep. The reference (Rust + WGSL on
+    wgpu) has no CPU implementation of its own and cannot run here (no Rust toolchain, no graphics
+    stack), so this times the oracle port of its shader math on the host's cores, per step one
+    bounded sample request, scaled to the sweep's mean tokens per question."""
+    if rank != 0:
+        return
+    path = model_path(1, 0)
+    _, mean_tokens_q, _ = sweep_stats(args.seed)
+    cores = os.cpu_count()
+    times = []
+    tokens = 0
+    for s in range(args.warmup + args.steps):
+        dt, tok = cpu_baseline(path, args.seed + s, state_len=64)
+        if s >= args.warmup:
+            times.append(dt)
+            tokens += tok
+    total = sum(times)
+    tok_s = tokens / total
+    qps = tok_s / mean_tokens_q
+    sample = (f"per step: one sweep request with its state cut to 64 tokens + its 3 questions (oracle port, {cores} threads), "
+              f"{tok_s:.1f} tok/s scaled to the sweep's {mean_tokens_q:.0f} tokens per question")
+    line = {"impl": "reference", "metric": "answered questions/s", "value": qps, "unit": "questions/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "sweep (bounded CPU sample)", "model": "random-init 2B hybrid, 24 layers"},
+            "cpu_baseline": {"value": qps, "unit": "questions/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": qps, "unit": "questions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "prefill_tok_s": tok_s}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    from strands_decider.engine import Engine, Head
+
+    path = model_path(world, rank)
+    torch.cuda.set_device(local)
+    eng = Engine.load(path, local)
+    head = Head.load(os.path.join(path, "head.safetensors"))
+    stream = torch.cuda.ExternalStream(eng.stream)
+    per = args.requests_per_step
+    steps_all = args.warmup + args.steps
+    # stage every request of every step in HBM before timing
+    reqs = {}
+    staged = {}
+    for s in range(steps_all + 1):
+        for i in step_requests(s, rank, world, per):
+            if i in reqs:
+                continue
+            sids, qs, _ = request(i, args.seed)
+            reqs[i] = (sids, qs)
+            staged[i] = (torch.from_numpy(sids.view(np.int32)).cuda(),
+                         [(torch.from_numpy(q.view(np.int32)).cuda(), torch.from_numpy(r).cuda()) for q, r in qs])
+    hidden_dev = torch.empty((3, 4, 2048), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def one_step_dev(s):
+        n_q = n_tok = 0
+        for i in step_requests(s, rank, world, per):
+            sd, qd = staged[i]
+            snap = eng.forward_dev(sd.data_ptr(), sd.numel(), None, 0, keep=True)
+            n_tok += sd.numel()
+            for k, (qi, rw) in enumerate(qd):
+                eng.forward_dev(qi.data_ptr(), qi.numel(), rw.data_ptr(), rw.numel(), cache=snap,
+                                hidden_dev=hidden_dev[k].data_ptr())
+                n_q += 1
+                n_tok += qi.numel()
+            snap.close()
+        return n_q, n_tok
+
+    h2d = d2h = 0
+
+    def one_step_host(s):
+        nonlocal h2d, d2h
+        n_q = 0
+        for i in step_requests(s, rank, world, per):
+            sids, qs = reqs[i]
+            snap = eng.forward(sids, [], keep=True).snapshot
+            h2d += sids.nbytes
+            for qids, rows in qs:
+                out = eng.forward(qids, rows, cache=snap)
+                head.probs(out.hidden, 2048, 1.0)
+                h2d += qids.nbytes + rows.nbytes
+                d2h += out.hidden.nbytes
+                n_q += 1
+            snap.close()
+        return n_q
+
+    def timed(fn, first, count):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        eng.synchronize()
+        ev0.record(stream)
+        res = [fn(first + s) for s in range(count)]
+        ev1.record(stream)
+        eng.synchronize()
+        torch.cuda.synchronize()
+        barrier(world)
+        return ev0.elapsed_time(ev1), res
+
+    # warm-up (both paths)
+    for s in range(args.warmup):
+        one_step_dev(s)
+    eng.synchronize()
+    for s in range(min(args.warmup, 1)):
+        one_step_host(s)
+
+    clocks = Clocks(local)
+    l0 = eng.launches()
+    ms_dev, res = timed(one_step_dev, args.warmup, args.steps)
+    launches = eng.launches() - l0
+    clk = clocks.stop()
+    q_dev = sum(r[0] for r in res)
+    tok_dev = sum(r[1] for r in res)
+    h2d = d2h = 0
+    ms_host, res_h = timed(one_step_host, args.warmup, args.steps)
+    q_host = sum(res_h)
+    h2d_step, d2h_step = h2d / args.steps, d2h / args.steps
+
+    # profiled pass over the same steps (per-launch events), for the roofline
+    eng.profile(True)
+    for s in range(args.steps):
+        one_step_dev(args.warmup + s)
+    prof = eng.profile_get()
+    eng.profile(False)
+
+    t_dev = max_over_ranks(world, ms_dev) / 1e3
+    t_host = max_over_ranks(world, ms_host) / 1e3
+    q_all = sum_over_ranks(world, q_dev)
+    tok_all = sum_over_ranks(world, tok_dev)
+    qh_all = sum_over_ranks(world, q_host)
+    if rank != 0:
+        return
+    hbm, tf_burst, tf_sus, src = peaks()
+    g = prof["gemm"]
+    gemm_tflops = g["work"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
+    a = prof["attention"]
+    d = prof["gdn"]
+    mean_state, mean_tok_q, clips = sweep_stats(args.seed)
+    line = {
+        "metric": "answered questions/s", "value": q_all / t_dev, "unit": "questions/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "sweep: requests of a 64-4096-token state (clipped to fit 4096 with the longest question) "
+                               "+ 3 questions of 42-84 tokens (noul/choice/score), random non-special ids",
+                   "model": "random-init 2B hybrid (24 layers: 18 gated-delta + 6 attention, int4 g32 weights, int3 embedding)",
+                   "requests_per_step_per_gpu": per, "requests_timed": int(q_all // 3), "sweep_mean_state_tokens": round(mean_state, 1),
+                   "sweep_clipped_requests": clips, "l2": "inputs larger than L2 (0.8 GB of weights streamed per forward)",
+                   "parallelism": f"replicas x{world} (requests sharded, no collective)"},
+        "prefill_tok_s": tok_all / t_dev,
+        "e2e": {"value": qh_all / t_host, "unit": "questions/s", "h2d_bytes_per_step": int(h2d_step),
+                "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward (host ids in, host hidden rows out) + sd_head_probs"},
+        "gpu_launches": int(launches),
+        "roofline": {"kernel": "gemm_q4_tc (dequantizing tcgen05 GEMM)", "bound": "tensor", "achieved": gemm_tflops,
+                     "peak": tf_sus, "unit": "TFLOP/s", "frac": gemm_tflops / tf_sus, "traffic": None,
+                     "peak_source": f"{src} bf16 sustained (kernel timed inside a long step)",
+                     "share_of_device_time": g["ms"] / max(1e-9, sum(v["ms"] for v in prof.values()))},
+        "kernels": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
+                        "achieved": (v["work"] / (v["ms"] / 1e3) / (1e12 if k in ("gemm", "attention") else 1e9)) if v["ms"] > 0 else 0,
+                        "unit": "TFLOP/s" if k in ("gemm", "attention") else "GB/s"} for k, v in prof.items()},
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        path = model_path(1, 0)
+        dt, tok = cpu_baseline(path, args.seed)
+        tok_s = tok / dt
+        line["cpu_baseline"] = {"value": tok_s / mean_tok_q, "unit": "questions/s", "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"oracle port on request 0 with its state cut to 96 tokens + its 3 questions "
+                                          f"({tok} tokens, {dt:.1f} s, {tok_s:.1f} tok/s) scaled to the sweep's "
+                                          f"{mean_tok_q:.0f} tokens per question"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--requests-per-step", type=int, default=8)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

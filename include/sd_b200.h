@@ -56,10 +56,37 @@ int sd_forward(sd_engine* e, const uint32_t* ids, int32_t n_ids, const int32_t* 
 int32_t sd_snapshot_len(const sd_snapshot* s);
 void sd_snapshot_free(sd_snapshot* s);
 
+/* `Engine::forward` on device memory, asynchronous on the engine's stream (sd_engine_stream): ids_dev
+ * [n_ids] u32 and rows_dev [n_rows] i32 already on the GPU, hidden rows to hidden_dev
+ * [n_rows][hidden_size] f32. Token ids and rows are checked on the device; errors surface at the
+ * next sd_engine_synchronize. A snapshot made here can be used by later calls at once (the work is
+ * stream-ordered). The caller keeps ids_dev/rows_dev alive until the work completes. */
+int sd_forward_dev(sd_engine* e, const uint32_t* ids_dev, int32_t n_ids, const int32_t* rows_dev, int32_t n_rows,
+                   const sd_snapshot* cache, int32_t keep, float* hidden_dev, sd_snapshot** snapshot_out);
+/* Waits for the engine's queued work; returns the first error a kernel reported since the last call. */
+int sd_engine_synchronize(sd_engine* e);
+/* The engine's CUDA stream (a cudaStream_t), for callers that order their own work after it. */
+void* sd_engine_stream(const sd_engine* e);
+/* Kernels of this library the engine has launched since it was created. */
+int64_t sd_engine_launches(const sd_engine* e);
+
 /* Diagnostics: when `host_buf` is set, each following forward writes the residual stream after each
  * layer (x + y, [n_layers][n_ids][hidden_size] f32) there; `floats` is its capacity. NULL stops. */
 int sd_engine_set_trace(sd_engine* e, float* host_buf, size_t floats);
 int sd_engine_num_layers(const sd_engine* e);
+
+/* Per-kernel device time, as the reference's `Engine::profile` (`src/engine.rs:665-711`) gives it per
+ * dispatch label: while enabled, every launch is bracketed by CUDA events on the engine's stream.
+ * sd_engine_profile_get returns, per kind, the summed milliseconds, the launches and the summed
+ * algorithmic work (FLOPs for SD_PROF_GEMM and SD_PROF_ATTN, bytes for the others) since the last
+ * enable. Reading synchronizes. */
+#define SD_PROF_GEMM 0  /* dequantizing matmuls (work: 2 m n k FLOPs) */
+#define SD_PROF_ATTN 1  /* attention (work: 4 hd hq causal pairs FLOPs) */
+#define SD_PROF_GDN 2   /* gated delta rule (work: q,k,v,gates,o,state bytes) */
+#define SD_PROF_OTHER 3 /* norms, conv, gates, q/k prep, embedding (work: bytes moved) */
+#define SD_PROF_KINDS 4
+int sd_engine_profile(sd_engine* e, int32_t enable);
+int sd_engine_profile_get(sd_engine* e, int32_t kind, double* ms, int64_t* launches, double* work);
 
 /* Replaces `Head::load` and `Head::probs` (`src/head.rs:25-77`): the pointer head in f64 on the
  * host. `hidden` is [n_rows][d] = [option 0 .. option n-2, answer]; writes n_rows - 1 probabilities. */
@@ -78,13 +105,15 @@ int sd_attention(const void* q_dev, const void* k_dev, const void* v_dev, const 
                  int32_t goff, int32_t gstep, void* out_dev, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk,
                  int32_t hd, void* stream);
 
-/* `Gdn::subgroups` (`src/kernels.rs:257-302`): the gated delta rule over one sequence of l tokens.
- * q_dev/k_dev [l][qk_stride] f32 (head h at h * 128), v_dev [l][v_stride] f32 (head h at h * 128),
- * beta_dev/decay_dev [l][h] f32, state_dev [h][128][128] f32 (read when load_state, always written),
- * o_dev [l][h * 128] f32. */
+/* `Gdn::subgroups` (`src/kernels.rs:257-302`): the gated delta rule over `batch` sequences of l tokens.
+ * q_dev/k_dev [batch][l][qk_stride] (head h at h * 128), v_dev [batch][l][v_stride] (head h at h * 128),
+ * f32, or f16 when in_f16; seq_qk/seq_v: elements between sequences. beta_dev and g_dev (the log decay:
+ * the decay is exp(g)) [batch][l][h] f32; state_dev [batch][h][128][128] f32 (read when load_state,
+ * always written); o_dev [batch][l][h * 128] f32. `serial` selects the token-serial kernel (f32, one
+ * sequence) instead of the chunked scan. */
 int sd_gdn(const void* q_dev, const void* k_dev, int32_t qk_stride, const void* v_dev, int32_t v_stride,
-           const void* beta_dev, const void* decay_dev, void* state_dev, int32_t load_state, void* o_dev, int32_t l,
-           int32_t h, void* stream);
+           const void* beta_dev, const void* g_dev, void* state_dev, int32_t load_state, void* o_dev, int32_t l,
+           int32_t h, int32_t batch, int64_t seq_qk, int64_t seq_v, int32_t in_f16, int32_t serial, void* stream);
 
 /* A block-quantized int4 group-32 symmetric weight (`src/kernels.rs:545-576`) in the GEMM's tile
  * layout, made from the reference layout on the device: q_dev [n][k/32][16 bytes], s_dev [n][k/32] f16.
@@ -94,7 +123,8 @@ void sd_qweight_free(sd_qweight* w);
 
 /* `matmul_gemv`/`matmul_tiled`/`matmul_coop` (`src/kernels.rs:590-804`): y_dev[m][ldy] =
  * f16(act_dev[m][k] W^T) (silu = 1 on an interleaved weight: y = silu(gate) * up, [m][n/2]).
- * ws_dev/ws_bytes: f32 workspace for split-K (m * n floats; 0 bytes disables split-K). */
+ * ws_dev/ws_bytes: f32 workspace for split-K, one m * n slice per split (splits are reduced to fit;
+ * 0 bytes disables split-K). Results do not depend on the split count's summation order run to run. */
 int sd_matmul(const sd_qweight* w, const void* act_dev, int32_t m, void* y_dev, int32_t ldy, int32_t silu, void* ws_dev,
               size_t ws_bytes, void* stream);
 

@@ -10,18 +10,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "sd_internal.h"
+
 #define SD_DEV __device__ __forceinline__
 
 namespace sd {
-
-// Error codes written to the device error word.
-enum : int {
-  kErrNone = 0,
-  kErrTimeoutFull = 1,    // a consumer gave up waiting for a stage to fill
-  kErrTimeoutEmpty = 2,   // a producer gave up waiting for a stage to drain
-  kErrTimeoutAccum = 3,   // the epilogue gave up waiting for the accumulator
-  kErrBadShape = 4,
-};
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 

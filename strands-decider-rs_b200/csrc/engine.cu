@@ -27,6 +27,8 @@
 
 using sd::QWeight;
 
+struct sd_engine;
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -82,21 +84,16 @@ bool read_file(const std::string& path, std::string& out) {
 
 }  // namespace
 
+// A snapshot is one stream-ordered allocation: [n_lin state][n_lin hist][n_full K][n_full V], K and
+// V compact as [hk][len][hd]. It is freed on its engine's stream, after any work that reads it.
 struct sd_snapshot {
   int len = 0;
   int device = 0;
+  sd_engine* owner = nullptr;
+  uint8_t* base = nullptr;
   std::vector<float*> state;
   std::vector<__half*> hist, k, v;
-  ~sd_snapshot() {
-    int prev = 0;
-    cudaGetDevice(&prev);
-    cudaSetDevice(device);
-    for (auto p : state) cudaFree(p);
-    for (auto p : hist) cudaFree(p);
-    for (auto p : k) cudaFree(p);
-    for (auto p : v) cudaFree(p);
-    cudaSetDevice(prev);
-  }
+  ~sd_snapshot();
 };
 
 struct sd_qweight {
@@ -133,10 +130,10 @@ struct sd_engine {
   int cap = 0;
   uint32_t* d_ids = nullptr;
   int* d_rows = nullptr;
-  float *x = nullptr, *qkvc = nullptr, *of = nullptr, *beta = nullptr, *decay = nullptr, *out = nullptr, *ws = nullptr;
+  float *x = nullptr, *of = nullptr, *beta = nullptr, *decay = nullptr, *out = nullptr, *ws = nullptr;
   float* trace_dev = nullptr;
   size_t ws_bytes = 0;
-  __half *h = nullptr, *big = nullptr, *mid = nullptr, *o = nullptr, *y = nullptr, *q = nullptr;
+  __half *h = nullptr, *big = nullptr, *mid = nullptr, *o = nullptr, *y = nullptr, *q = nullptr, *qkvc = nullptr;
   int* d_err = nullptr;
   // pinned staging
   uint32_t* p_ids = nullptr;
@@ -146,6 +143,16 @@ struct sd_engine {
   float* trace_host = nullptr;
   size_t trace_floats = 0;
   std::string err;
+  // launches of this library's kernels since creation
+  long long launches = 0;
+  // profiling (the reference's `Engine::profile`, src/engine.rs:665-711): events around each launch
+  bool prof_on = false;
+  std::vector<cudaEvent_t> prof_events;
+  size_t prof_used = 0;
+  std::vector<std::pair<int, double>> prof_pending;  // (kind, algorithmic units) per event pair
+  double prof_ms[SD_PROF_KINDS] = {}, prof_units[SD_PROF_KINDS] = {};
+  long long prof_count[SD_PROF_KINDS] = {};
+  std::vector<sd_snapshot*> live;
 
   int fail(int code, const char* fmt, ...) {
     char buf[1024];
@@ -159,6 +166,21 @@ struct sd_engine {
   }
 };
 
+sd_snapshot::~sd_snapshot() {
+  if (!base) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  if (owner) {
+    cudaFreeAsync(base, owner->stream);  // after any queued work that reads it
+    auto& v = owner->live;
+    v.erase(std::remove(v.begin(), v.end(), this), v.end());
+  } else {
+    cudaFree(base);
+  }
+  cudaSetDevice(prev);
+}
+
 #define CK(call)                                                                                    \
   do {                                                                                              \
     cudaError_t _e = (call);                                                                        \
@@ -171,7 +193,8 @@ void free_pool(sd_engine* e) {
   cudaFree(e->d_ids); cudaFree(e->d_rows); cudaFree(e->x); cudaFree(e->qkvc); cudaFree(e->of); cudaFree(e->beta);
   cudaFree(e->decay); cudaFree(e->out); cudaFree(e->ws); cudaFree(e->h); cudaFree(e->big); cudaFree(e->mid);
   cudaFree(e->o); cudaFree(e->y); cudaFree(e->q); cudaFree(e->trace_dev);
-  e->d_ids = nullptr; e->d_rows = nullptr; e->x = e->qkvc = e->of = e->beta = e->decay = e->out = e->ws = nullptr;
+  e->d_ids = nullptr; e->d_rows = nullptr; e->x = e->of = e->beta = e->decay = e->out = e->ws = nullptr;
+  e->qkvc = nullptr;
   e->trace_dev = nullptr;
   e->h = e->big = e->mid = e->o = e->y = e->q = nullptr;
   e->cap = 0;
@@ -192,7 +215,7 @@ int ensure_pool(sd_engine* e, int l) {
   CK(cudaMalloc(&e->h, (size_t)cap * d.d * 2));
   CK(cudaMalloc(&e->big, (size_t)cap * maxn * 2));
   CK(cudaMalloc(&e->mid, (size_t)cap * d.inter * 2));
-  CK(cudaMalloc(&e->qkvc, (size_t)cap * d.C() * 4));
+  CK(cudaMalloc(&e->qkvc, (size_t)cap * d.C() * 2));
   CK(cudaMalloc(&e->of, (size_t)cap * d.h * d.dv * 4));
   CK(cudaMalloc(&e->o, (size_t)cap * std::max(d.hq * d.hd, d.h * d.dv) * 2));
   CK(cudaMalloc(&e->y, (size_t)cap * d.d * 2));
@@ -200,8 +223,9 @@ int ensure_pool(sd_engine* e, int l) {
   CK(cudaMalloc(&e->beta, (size_t)cap * d.h * 4));
   CK(cudaMalloc(&e->decay, (size_t)cap * d.h * 4));
   CK(cudaMalloc(&e->out, (size_t)cap * d.d * 4));
-  // split-K workspace: small-M matmuls only (the planner splits K when the grid is short)
-  e->ws_bytes = (size_t)std::min(cap, 512) * maxn * 4;
+  // split-K workspace (one f32 slice per split): the planner splits K only when the grid is short,
+  // i.e. for small M; 64 MiB covers 32 splits of 64 x 8256 or 16 of 64 x 12288
+  e->ws_bytes = (size_t)64 << 20;
   CK(cudaMalloc(&e->ws, e->ws_bytes));
   if (e->trace_host) CK(cudaMalloc(&e->trace_dev, (size_t)e->n_layers * cap * d.d * 4));
   e->cap = cap;
@@ -468,23 +492,64 @@ int load_engine(sd_engine* e, const std::string& dir) {
   return SD_OK;
 }
 
-// One launch failure or a kernel error word turns into the call's error.
-int check_kernels(sd_engine* e) {
+// Waits for the stream, folds profiled event pairs into the totals, and turns a launch failure or a
+// kernel error word into the call's error.
+int sync_engine(sd_engine* e) {
   cudaError_t ce = cudaStreamSynchronize(e->stream);
   if (ce != cudaSuccess) return e->fail(SD_ERR_CUDA, "forward: %s", cudaGetErrorString(ce));
+  for (size_t i = 0; i < e->prof_pending.size(); i++) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->prof_events[2 * i], e->prof_events[2 * i + 1]);
+    const int kind = e->prof_pending[i].first;
+    e->prof_ms[kind] += ms;
+    e->prof_units[kind] += e->prof_pending[i].second;
+    e->prof_count[kind] += 1;
+  }
+  e->prof_pending.clear();
+  e->prof_used = 0;
   int herr = 0;
   CK(cudaMemcpy(&herr, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (herr != 0) {
     cudaMemset(e->d_err, 0, sizeof(int));
-    return e->fail(SD_ERR_KERNEL, "a kernel reported error %d", herr);
+    return e->fail(SD_ERR_KERNEL, "a kernel reported error %d (%s)", herr,
+                   herr == sd::kErrBadShape ? "token id or row out of range" : "a bounded wait ran out");
   }
   return SD_OK;
 }
 
-#define LK(call)                                                                                       \
-  do {                                                                                                 \
-    cudaError_t _e = (call);                                                                           \
-    if (_e != cudaSuccess) return e->fail(SD_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_e));    \
+cudaEvent_t prof_event(sd_engine* e) {
+  if (e->prof_used >= e->prof_events.size()) {
+    cudaEvent_t ev;
+    cudaEventCreate(&ev);
+    e->prof_events.push_back(ev);
+  }
+  return e->prof_events[e->prof_used++];
+}
+
+// Runs `launch` (which returns a cudaError_t and adds its kernel count to *n), bracketed by
+// profiling events when profiling is on.
+template <class F>
+cudaError_t launch(sd_engine* e, int kind, double units, F&& fn) {
+  cudaEvent_t a = nullptr;
+  if (e->prof_on) {
+    a = prof_event(e);
+    cudaEventRecord(a, e->stream);
+  }
+  int n = 1;
+  cudaError_t ce = fn(&n);
+  e->launches += n;
+  if (e->prof_on) {
+    cudaEvent_t b = prof_event(e);
+    cudaEventRecord(b, e->stream);
+    e->prof_pending.push_back({kind, units});
+  }
+  return ce;
+}
+
+#define LK(kind, units, call)                                                                            \
+  do {                                                                                                   \
+    cudaError_t _e = launch(e, kind, units, [&](int* nl) -> cudaError_t { (void)nl; return (call); });   \
+    if (_e != cudaSuccess) return e->fail(SD_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_e));      \
   } while (0)
 
 // The layer loop (src/engine.rs:446-522), launched on the engine's stream.
@@ -492,43 +557,134 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
   const sd::Dims& d = e->dm;
   cudaStream_t st = e->stream;
   const int C = d.C();
-  LK(sd::launch_embed_norm(e->d_ids, l, e->embed_q, e->embed_s, e->embed_bits, d.d, e->vocab, e->layers[0].in_norm, e->x,
+  const double L = l;
+  auto mm = [&](const QWeight& w, const __half* a, int lda, __half* y, int ldy, bool silu) -> int {
+    const double flops = 2.0 * L * w.n * w.k;
+    LK(SD_PROF_GEMM, flops, sd::gemm_q4(w, a, l, lda, y, ldy, silu, e->ws, e->ws_bytes, e->d_err, e->num_sms, st, nl));
+    return SD_OK;
+  };
+  int rc;
+#define MM(...)                          \
+  do {                                   \
+    if ((rc = mm(__VA_ARGS__)) != SD_OK) \
+      return rc;                         \
+  } while (0)
+  const double row_bytes = (double)d.d * (4 + 2);
+  LK(SD_PROF_OTHER, L * (d.d / 32 * (4.0 * e->embed_bits + 2) + row_bytes),
+     sd::launch_embed_norm(e->d_ids, l, e->embed_q, e->embed_s, e->embed_bits, d.d, e->vocab, e->layers[0].in_norm, e->x,
                            e->h, e->d_err, st));
   for (int i = 0; i < e->n_layers; i++) {
-    const LayerW& L = e->layers[i];
-    if (i > 0) LK(sd::launch_add_norm(e->x, e->y, L.in_norm, l, d.d, true, e->h, st));
-    if (L.kind == 2) {
-      LK(sd::gemm_q4(L.proj, e->h, l, d.d, e->y, d.d, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
-      LK(sd::launch_add_bias(e->y, L.bias, l, d.d, st));
+    const LayerW& Lw = e->layers[i];
+    if (i > 0) LK(SD_PROF_OTHER, L * d.d * 12.0, sd::launch_add_norm(e->x, e->y, Lw.in_norm, l, d.d, true, e->h, st));
+    if (Lw.kind == 2) {
+      MM(Lw.proj, e->h, d.d, e->y, d.d, false);
+      LK(SD_PROF_OTHER, L * d.d * 4.0, sd::launch_add_bias(e->y, Lw.bias, l, d.d, st));
     } else {
-      if (L.kind == 0) {
-        const int N = L.in_proj.n;
-        __half* hist = e->hist[L.slot];
-        LK(sd::gemm_q4(L.in_proj, e->h, l, d.d, e->big, N, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
-        LK(sd::launch_conv(e->big, N, L.conv, hist, l, C, e->qkvc, st));
-        LK(sd::launch_hist_update(e->big, N, hist, l, C, st));
+      if (Lw.kind == 0) {
+        const int N = Lw.in_proj.n;
+        __half* hist = e->hist[Lw.slot];
+        MM(Lw.in_proj, e->h, d.d, e->big, N, false);
+        LK(SD_PROF_OTHER, L * C * 4.0, sd::launch_conv(e->big, N, Lw.conv, hist, l, C, e->qkvc, st));
+        LK(SD_PROF_OTHER, C * 12.0, sd::launch_hist_update(e->big, N, hist, l, C, st));
         const int aoff = C + d.h * d.dv, boff = aoff + d.h;
-        LK(sd::launch_gdn_gates(e->big, N, aoff, boff, L.neg_a, L.dt_bias, l, d.h, e->beta, e->decay, st));
-        LK(sd::launch_gdn_recurrent(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, e->beta, e->decay,
-                                    e->state[L.slot], has_cache, e->of, l, d.h, st));
-        LK(sd::launch_gnorm(e->of, e->big, N, C, L.gnorm, l, d.h, e->o, st));
-        LK(sd::gemm_q4(L.out_proj, e->o, l, d.h * d.dv, e->y, d.d, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
+        LK(SD_PROF_OTHER, L * d.h * 12.0,
+           sd::launch_gdn_gates(e->big, N, aoff, boff, Lw.neg_a, Lw.dt_bias, l, d.h, e->beta, e->decay, st));
+        const double gdn_bytes = L * (C * 2.0 + d.h * 8.0 + d.h * d.dv * 4.0) + 2.0 * d.h * d.dk * d.dv * 4.0;
+        LK(SD_PROF_GDN, gdn_bytes,
+           sd::launch_gdn_chunked(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, 0, 0, true, e->beta,
+                                  e->decay, e->state[Lw.slot], has_cache, e->of, l, d.h, 1, st));
+        LK(SD_PROF_OTHER, L * d.h * d.dv * 8.0, sd::launch_gnorm(e->of, e->big, N, C, Lw.gnorm, l, d.h, e->o, st));
+        MM(Lw.out_proj, e->o, d.h * d.dv, e->y, d.d, false);
       } else {
-        const int N = L.qkv.n;
-        LK(sd::gemm_q4(L.qkv, e->h, l, d.d, e->big, N, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
-        LK(sd::launch_qk_prep(e->big, N, L.q_norm, L.k_norm, e->rope, l, p, SD_CONTEXT, d, e->q, e->kc[L.slot],
-                              e->vc[L.slot], st));
-        LK(sd::launch_attention(e->q, e->kc[L.slot], e->vc[L.slot], e->big, N, d.hd, 2 * d.hd, e->o, l, p, SD_CONTEXT, d.hq,
-                                d.hk, d.hd, st));
-        LK(sd::gemm_q4(L.o_proj, e->o, l, d.hq * d.hd, e->y, d.d, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
+        const int N = Lw.qkv.n;
+        MM(Lw.qkv, e->h, d.d, e->big, N, false);
+        LK(SD_PROF_OTHER, L * (N * 2.0 + (d.hq + 2.0 * d.hk) * d.hd * 2.0),
+           sd::launch_qk_prep(e->big, N, Lw.q_norm, Lw.k_norm, e->rope, l, p, SD_CONTEXT, d, e->q, e->kc[Lw.slot],
+                              e->vc[Lw.slot], st));
+        const double pairs = L * p + L * (L + 1) / 2;  // causal (query, key) pairs
+        LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * pairs,
+           sd::launch_attention(e->q, e->kc[Lw.slot], e->vc[Lw.slot], e->big, N, d.hd, 2 * d.hd, e->o, l, p, SD_CONTEXT,
+                                d.hq, d.hk, d.hd, st));
+        MM(Lw.o_proj, e->o, d.hq * d.hd, e->y, d.d, false);
       }
-      LK(sd::launch_add_norm(e->x, e->y, L.post_norm, l, d.d, true, e->h, st));
-      LK(sd::gemm_q4(L.gate_up, e->h, l, d.d, e->mid, d.inter, true, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
-      LK(sd::gemm_q4(L.down, e->mid, l, d.inter, e->y, d.d, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st));
     }
-    if (e->trace_dev) LK(sd::launch_trace(e->x, e->y, l * d.d, e->trace_dev + (size_t)i * l * d.d, st));
+    if (Lw.kind != 2) {
+      LK(SD_PROF_OTHER, L * d.d * 12.0, sd::launch_add_norm(e->x, e->y, Lw.post_norm, l, d.d, true, e->h, st));
+      MM(Lw.gate_up, e->h, d.d, e->mid, d.inter, true);
+      MM(Lw.down, e->mid, d.inter, e->y, d.d, false);
+    }
+    if (e->trace_dev) LK(SD_PROF_OTHER, L * d.d * 10.0, sd::launch_trace(e->x, e->y, l * d.d, e->trace_dev + (size_t)i * l * d.d, st));
   }
-  if (nrows > 0) LK(sd::launch_final_norm(e->x, e->y, e->final_norm, e->d_rows, nrows, d.d, e->out, st));
+  if (nrows > 0)
+    LK(SD_PROF_OTHER, nrows * d.d * 14.0,
+       sd::launch_final_norm(e->x, e->y, e->final_norm, e->d_rows, nrows, l, d.d, e->out, e->d_err, st));
+#undef MM
+  return SD_OK;
+}
+
+// Restores the prefix or clears the conv history (src/engine.rs:552-571), runs the layers and, with
+// `keep`, copies the state into a new snapshot (src/engine.rs:592-614). Everything is enqueued on the
+// engine's stream; e->d_ids and e->d_rows hold this call's inputs.
+int forward_core(sd_engine* e, int l, const sd_snapshot* cache, int nrows, bool keep, sd_snapshot** snapshot_out) {
+  const sd::Dims& d = e->dm;
+  cudaStream_t st = e->stream;
+  const int p = cache ? cache->len : 0;
+  const size_t state_bytes = (size_t)d.h * d.dk * d.dv * 4, hist_bytes = (size_t)3 * d.C() * 2;
+  const size_t row_bytes = (size_t)d.hd * 2;
+  if (cache) {
+    for (int i = 0; i < e->n_lin; i++) {
+      CK(cudaMemcpyAsync(e->state[i], cache->state[i], state_bytes, cudaMemcpyDeviceToDevice, st));
+      CK(cudaMemcpyAsync(e->hist[i], cache->hist[i], hist_bytes, cudaMemcpyDeviceToDevice, st));
+    }
+    for (int i = 0; i < e->n_full && p > 0; i++) {
+      CK(cudaMemcpy2DAsync(e->kc[i], SD_CONTEXT * row_bytes, cache->k[i], (size_t)p * row_bytes, (size_t)p * row_bytes, d.hk,
+                           cudaMemcpyDeviceToDevice, st));
+      CK(cudaMemcpy2DAsync(e->vc[i], SD_CONTEXT * row_bytes, cache->v[i], (size_t)p * row_bytes, (size_t)p * row_bytes, d.hk,
+                           cudaMemcpyDeviceToDevice, st));
+    }
+  } else {
+    for (int i = 0; i < e->n_lin; i++) CK(cudaMemsetAsync(e->hist[i], 0, hist_bytes, st));
+  }
+  int rc = run_layers(e, l, p, cache != nullptr, nrows);
+  if (rc != SD_OK) return rc;
+  if (keep) {
+    const int T = p + l;
+    const size_t kv_bytes = (size_t)d.hk * T * row_bytes;
+    const size_t total = e->n_lin * (state_bytes + hist_bytes) + 2 * e->n_full * kv_bytes;
+    std::unique_ptr<sd_snapshot> snap(new sd_snapshot());
+    snap->device = e->device;
+    snap->len = T;
+    CK(cudaMallocAsync(reinterpret_cast<void**>(&snap->base), std::max<size_t>(total, 256), st));
+    snap->owner = e;
+    uint8_t* q = snap->base;
+    for (int i = 0; i < e->n_lin; i++, q += state_bytes) snap->state.push_back(reinterpret_cast<float*>(q));
+    for (int i = 0; i < e->n_lin; i++, q += hist_bytes) snap->hist.push_back(reinterpret_cast<__half*>(q));
+    for (int i = 0; i < e->n_full; i++, q += kv_bytes) snap->k.push_back(reinterpret_cast<__half*>(q));
+    for (int i = 0; i < e->n_full; i++, q += kv_bytes) snap->v.push_back(reinterpret_cast<__half*>(q));
+    for (int i = 0; i < e->n_lin; i++) {
+      CK(cudaMemcpyAsync(snap->state[i], e->state[i], state_bytes, cudaMemcpyDeviceToDevice, st));
+      CK(cudaMemcpyAsync(snap->hist[i], e->hist[i], hist_bytes, cudaMemcpyDeviceToDevice, st));
+    }
+    for (int i = 0; i < e->n_full; i++) {
+      CK(cudaMemcpy2DAsync(snap->k[i], (size_t)T * row_bytes, e->kc[i], SD_CONTEXT * row_bytes, (size_t)T * row_bytes, d.hk,
+                           cudaMemcpyDeviceToDevice, st));
+      CK(cudaMemcpy2DAsync(snap->v[i], (size_t)T * row_bytes, e->vc[i], SD_CONTEXT * row_bytes, (size_t)T * row_bytes, d.hk,
+                           cudaMemcpyDeviceToDevice, st));
+    }
+    e->live.push_back(snap.get());
+    *snapshot_out = snap.release();
+  }
+  return SD_OK;
+}
+
+int check_forward_args(sd_engine* e, int l, int nrows, const sd_snapshot* cache, int keep, sd_snapshot** snapshot_out) {
+  const int p = cache ? cache->len : 0;
+  if (l <= 0 || p + l > SD_CONTEXT) return e->fail(SD_ERR_INVALID, "context of %d tokens: must be 1 to %d", p + l, SD_CONTEXT);
+  if (nrows < 0) return e->fail(SD_ERR_INVALID, "negative row count");
+  if (cache && cache->owner != e) return e->fail(SD_ERR_INVALID, "snapshot belongs to another engine");
+  if (keep && !snapshot_out) return e->fail(SD_ERR_INVALID, "keep without a snapshot output");
+  if (e->trace_host && e->trace_floats < (size_t)e->n_layers * l * e->dm.d)
+    return e->fail(SD_ERR_INVALID, "trace buffer too small");
   return SD_OK;
 }
 
@@ -578,6 +734,8 @@ void sd_engine_destroy(sd_engine* e) {
   if (!e) return;
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
+  for (auto* snap : e->live) snap->owner = nullptr;  // freed synchronously later
+  for (auto ev : e->prof_events) cudaEventDestroy(ev);
   free_pool(e);
   for (auto p : e->shards) cudaFree(p);
   for (auto& L : e->layers)
@@ -620,22 +778,16 @@ int sd_engine_set_trace(sd_engine* e, float* host_buf, size_t floats) {
 int sd_forward(sd_engine* e, const uint32_t* ids, int32_t l, const int32_t* rows, int32_t nrows, const sd_snapshot* cache,
                int32_t keep, float* hidden_out, sd_snapshot** snapshot_out, double* gpu_ms_out) {
   if (!e) return SD_ERR_INVALID;
-  const int p = cache ? cache->len : 0;
-  if (l <= 0 || p + l > SD_CONTEXT || !ids) return e->fail(SD_ERR_INVALID, "context of %d tokens: must be 1 to %d", p + l, SD_CONTEXT);
-  if (nrows < 0 || (nrows > 0 && (!rows || !hidden_out))) return e->fail(SD_ERR_INVALID, "rows given without an output buffer");
+  int rc = check_forward_args(e, l, nrows, cache, keep, snapshot_out);
+  if (rc != SD_OK) return rc;
+  if (!ids) return e->fail(SD_ERR_INVALID, "no token ids");
+  if (nrows > 0 && (!rows || !hidden_out)) return e->fail(SD_ERR_INVALID, "rows given without an output buffer");
   for (int i = 0; i < nrows; i++)
     if (rows[i] < 0 || rows[i] >= l) return e->fail(SD_ERR_INVALID, "row %d out of range for %d tokens", rows[i], l);
   for (int i = 0; i < l; i++)
     if (ids[i] >= (uint32_t)e->vocab) return e->fail(SD_ERR_INVALID, "token id %u out of range (vocab %d)", ids[i], e->vocab);
-  if (cache && cache->device != e->device) return e->fail(SD_ERR_INVALID, "snapshot belongs to another device");
-  if (keep && !snapshot_out) return e->fail(SD_ERR_INVALID, "keep without a snapshot output");
-  if (e->trace_host && e->trace_floats < (size_t)e->n_layers * l * e->dm.d)
-    return e->fail(SD_ERR_INVALID, "trace buffer too small");
   cudaSetDevice(e->device);
-  int rc = ensure_pool(e, l);
-  if (rc != SD_OK) return rc;
-  rc = ensure_pinned(e, l, nrows);
-  if (rc != SD_OK) return rc;
+  if ((rc = ensure_pool(e, l)) != SD_OK || (rc = ensure_pinned(e, l, nrows)) != SD_OK) return rc;
   const sd::Dims& d = e->dm;
   cudaStream_t st = e->stream;
   memcpy(e->p_ids, ids, l * sizeof(uint32_t));
@@ -645,60 +797,21 @@ int sd_forward(sd_engine* e, const uint32_t* ids, int32_t l, const int32_t* rows
     CK(cudaMemcpyAsync(e->d_rows, e->p_rows, nrows * sizeof(int), cudaMemcpyHostToDevice, st));
   }
   CK(cudaEventRecord(e->ev0, st));
-  // restore the prefix, or clear the conv history (src/engine.rs:552-571)
-  const size_t state_bytes = (size_t)d.h * d.dk * d.dv * 4, hist_bytes = (size_t)3 * d.C() * 2;
-  const size_t row_bytes = (size_t)d.hd * 2;
-  if (cache) {
-    for (int i = 0; i < e->n_lin; i++) {
-      CK(cudaMemcpyAsync(e->state[i], cache->state[i], state_bytes, cudaMemcpyDeviceToDevice, st));
-      CK(cudaMemcpyAsync(e->hist[i], cache->hist[i], hist_bytes, cudaMemcpyDeviceToDevice, st));
-    }
-    for (int i = 0; i < e->n_full && p > 0; i++) {
-      CK(cudaMemcpy2DAsync(e->kc[i], SD_CONTEXT * row_bytes, cache->k[i], (size_t)p * row_bytes, (size_t)p * row_bytes, d.hk,
-                           cudaMemcpyDeviceToDevice, st));
-      CK(cudaMemcpy2DAsync(e->vc[i], SD_CONTEXT * row_bytes, cache->v[i], (size_t)p * row_bytes, (size_t)p * row_bytes, d.hk,
-                           cudaMemcpyDeviceToDevice, st));
-    }
-  } else {
-    for (int i = 0; i < e->n_lin; i++) CK(cudaMemsetAsync(e->hist[i], 0, hist_bytes, st));
+  sd_snapshot* snap = nullptr;
+  rc = forward_core(e, l, cache, nrows, keep != 0, &snap);
+  if (rc != SD_OK) {
+    cudaStreamSynchronize(st);
+    return rc;
   }
-  rc = run_layers(e, l, p, cache != nullptr, nrows);
-  if (rc != SD_OK) return rc;
   CK(cudaEventRecord(e->ev1, st));
   if (nrows > 0) CK(cudaMemcpyAsync(e->p_out, e->out, (size_t)nrows * d.d * 4, cudaMemcpyDeviceToHost, st));
   if (e->trace_dev)
     CK(cudaMemcpyAsync(e->trace_host, e->trace_dev, (size_t)e->n_layers * l * d.d * 4, cudaMemcpyDeviceToHost, st));
-  // snapshot of the prefix and these tokens (src/engine.rs:592-614)
-  std::unique_ptr<sd_snapshot> snap;
-  if (keep) {
-    snap.reset(new sd_snapshot());
-    snap->device = e->device;
-    const int T = p + l;
-    snap->len = T;
-    for (int i = 0; i < e->n_lin; i++) {
-      float* s = nullptr;
-      __half* h = nullptr;
-      CK(cudaMalloc(&s, state_bytes));
-      snap->state.push_back(s);
-      CK(cudaMalloc(&h, hist_bytes));
-      snap->hist.push_back(h);
-      CK(cudaMemcpyAsync(s, e->state[i], state_bytes, cudaMemcpyDeviceToDevice, st));
-      CK(cudaMemcpyAsync(h, e->hist[i], hist_bytes, cudaMemcpyDeviceToDevice, st));
-    }
-    for (int i = 0; i < e->n_full; i++) {
-      __half *k = nullptr, *v = nullptr;
-      CK(cudaMalloc(&k, (size_t)d.hk * T * row_bytes));
-      snap->k.push_back(k);
-      CK(cudaMalloc(&v, (size_t)d.hk * T * row_bytes));
-      snap->v.push_back(v);
-      CK(cudaMemcpy2DAsync(k, (size_t)T * row_bytes, e->kc[i], SD_CONTEXT * row_bytes, (size_t)T * row_bytes, d.hk,
-                           cudaMemcpyDeviceToDevice, st));
-      CK(cudaMemcpy2DAsync(v, (size_t)T * row_bytes, e->vc[i], SD_CONTEXT * row_bytes, (size_t)T * row_bytes, d.hk,
-                           cudaMemcpyDeviceToDevice, st));
-    }
+  rc = sync_engine(e);
+  if (rc != SD_OK) {
+    delete snap;
+    return rc;
   }
-  rc = check_kernels(e);
-  if (rc != SD_OK) return rc;
   if (gpu_ms_out) {
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, e->ev0, e->ev1);
@@ -714,8 +827,57 @@ int sd_forward(sd_engine* e, const uint32_t* ids, int32_t l, const int32_t* rows
         for (int c = 0; c < d.d; c++) row[c] = (float)((double)row[c] * e->unrotate[c]);
       }
   }
-  if (keep) *snapshot_out = snap.release();
+  if (keep) *snapshot_out = snap;
   return SD_OK;
+}
+
+int sd_forward_dev(sd_engine* e, const uint32_t* ids_dev, int32_t l, const int32_t* rows_dev, int32_t nrows,
+                   const sd_snapshot* cache, int32_t keep, float* hidden_dev, sd_snapshot** snapshot_out) {
+  if (!e) return SD_ERR_INVALID;
+  int rc = check_forward_args(e, l, nrows, cache, keep, snapshot_out);
+  if (rc != SD_OK) return rc;
+  if (!ids_dev || (nrows > 0 && (!rows_dev || !hidden_dev)))
+    return e->fail(SD_ERR_INVALID, "null device buffer");
+  if (e->trace_host) return e->fail(SD_ERR_INVALID, "tracing needs sd_forward");
+  cudaSetDevice(e->device);
+  if ((rc = ensure_pool(e, l)) != SD_OK) return rc;
+  cudaStream_t st = e->stream;
+  CK(cudaMemcpyAsync(e->d_ids, ids_dev, l * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+  if (nrows > 0) CK(cudaMemcpyAsync(e->d_rows, rows_dev, nrows * sizeof(int), cudaMemcpyDeviceToDevice, st));
+  sd_snapshot* snap = nullptr;
+  rc = forward_core(e, l, cache, nrows, keep != 0, &snap);
+  if (rc != SD_OK) return rc;
+  if (nrows > 0) CK(cudaMemcpyAsync(hidden_dev, e->out, (size_t)nrows * e->dm.d * 4, cudaMemcpyDeviceToDevice, st));
+  if (keep) *snapshot_out = snap;
+  return SD_OK;
+}
+
+int sd_engine_synchronize(sd_engine* e) {
+  if (!e) return SD_ERR_INVALID;
+  cudaSetDevice(e->device);
+  return sync_engine(e);
+}
+
+void* sd_engine_stream(const sd_engine* e) { return e ? (void*)e->stream : nullptr; }
+int64_t sd_engine_launches(const sd_engine* e) { return e ? e->launches : 0; }
+
+int sd_engine_profile(sd_engine* e, int32_t enable) {
+  if (!e) return SD_ERR_INVALID;
+  cudaSetDevice(e->device);
+  int rc = sync_engine(e);
+  e->prof_on = enable != 0;
+  for (int k = 0; k < SD_PROF_KINDS; k++) e->prof_ms[k] = e->prof_units[k] = 0.0, e->prof_count[k] = 0;
+  return rc;
+}
+
+int sd_engine_profile_get(sd_engine* e, int32_t kind, double* ms, int64_t* launches, double* work) {
+  if (!e || kind < 0 || kind >= SD_PROF_KINDS) return SD_ERR_INVALID;
+  cudaSetDevice(e->device);
+  int rc = sync_engine(e);
+  if (ms) *ms = e->prof_ms[kind];
+  if (launches) *launches = e->prof_count[kind];
+  if (work) *work = e->prof_units[kind];
+  return rc;
 }
 
 int32_t sd_snapshot_len(const sd_snapshot* s) { return s ? s->len : 0; }
@@ -833,15 +995,22 @@ int sd_attention(const void* q, const void* k, const void* v, const void* gate, 
 }
 
 int sd_gdn(const void* q, const void* k, int32_t qk_stride, const void* v, int32_t v_stride, const void* beta,
-           const void* decay, void* state, int32_t load_state, void* o, int32_t l, int32_t h, void* stream) {
-  if (!q || !k || !v || !beta || !decay || !state || !o || l <= 0 || h <= 0 || qk_stride % 4 || (size_t)q % 16 ||
-      (size_t)k % 16) {
+           const void* g, void* state, int32_t load_state, void* o, int32_t l, int32_t h, int32_t batch, int64_t seq_qk,
+           int64_t seq_v, int32_t in_f16, int32_t serial, void* stream) {
+  const size_t align = in_f16 ? 8 : 16;
+  if (!q || !k || !v || !beta || !g || !state || !o || l <= 0 || h <= 0 || batch <= 0 || qk_stride % 4 ||
+      (size_t)q % align || (size_t)k % align || (serial && (in_f16 || batch != 1))) {
     set_global_error("sd_gdn: bad arguments");
     return SD_ERR_INVALID;
   }
-  return op_result(sd::launch_gdn_recurrent((const float*)q, (const float*)k, qk_stride, (const float*)v, v_stride,
-                                            (const float*)beta, (const float*)decay, (float*)state, load_state != 0, (float*)o,
-                                            l, h, (cudaStream_t)stream),
+  if (serial)
+    return op_result(sd::launch_gdn_recurrent((const float*)q, (const float*)k, qk_stride, (const float*)v, v_stride,
+                                              (const float*)beta, (const float*)g, (float*)state, load_state != 0, (float*)o,
+                                              l, h, (cudaStream_t)stream),
+                     "sd_gdn");
+  return op_result(sd::launch_gdn_chunked(q, k, qk_stride, v, v_stride, seq_qk, seq_v, in_f16 != 0, (const float*)beta,
+                                          (const float*)g, (float*)state, load_state != 0, (float*)o, l, h, batch,
+                                          (cudaStream_t)stream),
                    "sd_gdn");
 }
 

@@ -1,0 +1,510 @@
+// The gated delta rule (the reference's `Gdn` kernels, src/kernels.rs:193-373) as a chunked scan.
+//
+// Per token (src/kernels.rs:282-297): q^ = q rsqrt(|q|^2 + 1e-6) / sqrt(DK), k^ = k rsqrt(|k|^2 + 1e-6),
+// S <- gamma S; delta = beta (v - S^T k^); S += k^ delta^T; o = S^T q^, with gamma = exp(g).
+//
+// Chunked form over C = 64 tokens from the chunk's entry state S0, with G_i = sum_{j<=i} g_j and
+// Gamma_i = exp(G_i):
+//   A[i][j] = beta_i exp(G_i - G_j) (k^_i . k^_j) for j < i;  T = (I + A)^-1 (unit lower triangular)
+//   W = T diag(beta Gamma) K^,  U = T diag(beta) V,  delta = U - W S0
+//   O = diag(Gamma) Q^ S0 + (Q^ K^T o M) delta,  M[i][j] = exp(G_i - G_j) for j <= i
+//   S_C = Gamma_C S0 + K^T diag(exp(G_C - G_i)) delta
+// which unrolls the recurrence exactly; only the summation order and the f16 rounding of the
+// tensor-core operands differ (accumulation is f32; the state is kept in f32).
+//
+// The value columns of the state are independent in the recurrence, so a CTA takes one head and a
+// slice of DVS value columns of one sequence; the intra-chunk products are recomputed per slice.
+// The state slice lives in registers as the accumulator of its own update (warp w owns key rows
+// 16w..16w+15) with an f16 copy in shared memory as the operand of W S0 and Q^ S0.
+#include "common.cuh"
+#include "sd_internal.h"
+
+namespace sd {
+namespace {
+
+constexpr int CH = 64;        // tokens per chunk
+constexpr int DK = 128;       // key (and value) head dim
+constexpr int LQK = DK + 8;   // padded row stride (halves) of 128-wide tiles
+constexpr int L64 = CH + 8;   // padded row stride (halves) of 64-wide tiles
+constexpr int LA = CH + 1;    // row stride (floats) of the f32 64x64 tiles
+
+template <int DVS>
+struct GdnSmem {
+  static constexpr int LV = DVS + 8;
+  __half q[CH * LQK];
+  __half k[CH * LQK];
+  __half w[CH * LQK];
+  __half v[CH * LV];
+  __half t1[CH * L64];
+  __half t2[CH * L64];
+  __half p[CH * L64];
+  __half d[CH * LV];
+  __half ds[CH * LV];
+  __half s[DK * LV];
+  float a[CH * LA];
+  float x[CH * LA];
+  float y[3 * 16 * 17];
+  float beta[CH], g[CH], G[CH];
+  // the next chunk's raw f16 inputs, prefetched with cp.async while this chunk computes
+  __half rq[CH * DK];
+  __half rk[CH * DK];
+  __half rv[CH * DVS];
+  float rbeta[CH], rg[CH];
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Fragment addresses (lane-dependent) for the m16n8k16 operands from padded row-major tiles.
+// A from [m][k]; B from [n][k] (non-transposed) or [k][n] (transposed); A from [k][m] (transposed).
+__device__ __forceinline__ uint32_t a_addr(const __half* base, int ld, int m0, int k0, int lane) {
+  const int mat = lane >> 3;
+  return smem_u32(base + (m0 + (mat & 1) * 8 + (lane & 7)) * ld + k0 + (mat >> 1) * 8);
+}
+__device__ __forceinline__ uint32_t bn_addr(const __half* base, int ld, int n0, int k0, int lane) {
+  const int mat = lane >> 3;
+  return smem_u32(base + (n0 + (mat >> 1) * 8 + (lane & 7)) * ld + k0 + (mat & 1) * 8);
+}
+__device__ __forceinline__ uint32_t bt_addr(const __half* base, int ld, int k0, int n0, int lane) {
+  const int mat = lane >> 3;
+  return smem_u32(base + (k0 + (mat & 1) * 8 + (lane & 7)) * ld + n0 + (mat >> 1) * 8);
+}
+__device__ __forceinline__ uint32_t at_addr(const __half* base, int ld, int k0, int m0, int lane) {
+  const int mat = lane >> 3;
+  return smem_u32(base + (k0 + (mat >> 1) * 8 + (lane & 7)) * ld + m0 + (mat & 1) * 8);
+}
+
+__device__ __forceinline__ void cp_async(void* dst, const void* src, int bytes_valid, int size) {
+  if (size == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(bytes_valid) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(bytes_valid) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p);
+template <>
+__device__ __forceinline__ float4 load4<float>(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+template <>
+__device__ __forceinline__ float4 load4<__half>(const __half* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+template <typename T>
+__device__ __forceinline__ float load1(const T* p) {
+  return (float)*p;
+}
+
+}  // namespace
+
+template <typename TIn>
+struct GdnArgs {
+  const TIn *q, *k, *v;
+  int qk_stride, v_stride;      // elements between tokens
+  long long seq_qk, seq_v;      // elements between sequences
+  const float *beta, *g;        // [seq][l][h]
+  float* state;                 // [seq][h][128][128]
+  float* o;                     // [seq][l][h * 128]
+  int load_state, l, h;
+};
+
+template <int DVS, typename TIn>
+__global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a) {
+  constexpr int LV = GdnSmem<DVS>::LV;
+  constexpr int NT = DVS / 16;  // n8 tiles per warp for the 64 x DVS products
+  extern __shared__ __align__(16) uint8_t gdn_smem_raw[];
+  GdnSmem<DVS>& sm = *reinterpret_cast<GdnSmem<DVS>*>(gdn_smem_raw);
+  const int NS = DK / DVS;
+  const int h = blockIdx.x / NS, c0 = (blockIdx.x % NS) * DVS, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g8 = lane >> 2, tq = lane & 3;
+  const int H = a.h;
+  const TIn* qg = a.q + b * a.seq_qk + h * DK;
+  const TIn* kg = a.k + b * a.seq_qk + h * DK;
+  const TIn* vg = a.v + b * a.seq_v + h * DK + c0;
+  const float* betag = a.beta + (long long)b * a.l * H + h;
+  const float* gg = a.g + (long long)b * a.l * H + h;
+  float* og = a.o + (long long)b * a.l * H * DK + h * DK + c0;
+  float* stg = a.state + ((long long)b * H + h) * DK * DK + c0;
+
+  // State slice: warp w owns key rows 16w..16w+15, all DVS columns (m16n8 accumulator layout).
+  float sacc[DVS / 8][4];
+#pragma unroll
+  for (int nt = 0; nt < DVS / 8; nt++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
+      sacc[nt][r] = a.load_state ? stg[row * DK + col] : 0.0f;
+    }
+  auto write_state_f16 = [&]() {
+#pragma unroll
+    for (int nt = 0; nt < DVS / 8; nt++) {
+      const int row = warp * 16 + g8, col = nt * 8 + 2 * tq;
+      *reinterpret_cast<__half2*>(&sm.s[row * LV + col]) = __floats2half2_rn(sacc[nt][0], sacc[nt][1]);
+      *reinterpret_cast<__half2*>(&sm.s[(row + 8) * LV + col]) = __floats2half2_rn(sacc[nt][2], sacc[nt][3]);
+    }
+  };
+  write_state_f16();
+
+  const float qscale = rsqrtf((float)DK);
+  const int mt = warp & 3;             // m16 tile of the 64-row products
+  const int nbase = (warp >> 2) * (DVS / 2);  // first value column of this warp's 64 x DVS products
+
+  // f16 inputs are prefetched one chunk ahead into the staging buffers; f32 inputs are read directly
+  constexpr bool kStage = sizeof(TIn) == 2;
+  auto prefetch = [&](int t0) {
+    const int n = min(CH, a.l - t0);
+    for (int e = threadIdx.x; e < CH * (DK / 8); e += 256) {  // q, k: 16 chunks of 16 bytes per row
+      const int r = e >> 4, c = (e & 15) * 8;
+      const int rr = r < n ? r : 0;
+      cp_async(&sm.rq[r * DK + c], qg + (long long)(t0 + rr) * a.qk_stride + c, r < n ? 16 : 0, 16);
+      cp_async(&sm.rk[r * DK + c], kg + (long long)(t0 + rr) * a.qk_stride + c, r < n ? 16 : 0, 16);
+    }
+    for (int e = threadIdx.x; e < CH * (DVS / 8); e += 256) {
+      const int r = e / (DVS / 8), c = (e % (DVS / 8)) * 8;
+      const int rr = r < n ? r : 0;
+      cp_async(&sm.rv[r * DVS + c], vg + (long long)(t0 + rr) * a.v_stride + c, r < n ? 16 : 0, 16);
+    }
+    if (threadIdx.x < 2 * CH) {
+      const int r = threadIdx.x & (CH - 1), rr = r < n ? r : 0;
+      const bool isb = threadIdx.x < CH;
+      cp_async(isb ? &sm.rbeta[r] : &sm.rg[r], (isb ? betag : gg) + (long long)(t0 + rr) * H, r < n ? 4 : 0, 4);
+    }
+    cp_async_commit();
+  };
+  if constexpr (kStage) prefetch(0);
+
+  for (int t0 = 0; t0 < a.l; t0 += CH) {
+    const int n = min(CH, a.l - t0);
+    // 1. normalised q^, k^ (one warp per token row), the value slice, the gates
+    if constexpr (kStage) {
+      cp_async_wait_all();
+      __syncthreads();
+    }
+    for (int r = warp; r < CH; r += 8) {
+      float4 qv = make_float4(0.f, 0.f, 0.f, 0.f), kv = qv;
+      if constexpr (kStage) {
+        qv = load4<__half>(&sm.rq[r * DK + lane * 4]);
+        kv = load4<__half>(&sm.rk[r * DK + lane * 4]);
+      } else if (r < n) {
+        qv = load4(qg + (long long)(t0 + r) * a.qk_stride + lane * 4);
+        kv = load4(kg + (long long)(t0 + r) * a.qk_stride + lane * 4);
+      }
+      const float sq = warp_sum(qv.x * qv.x + qv.y * qv.y + qv.z * qv.z + qv.w * qv.w);
+      const float sk = warp_sum(kv.x * kv.x + kv.y * kv.y + kv.z * kv.z + kv.w * kv.w);
+      const float rq = rsqrtf(sq + 1e-6f) * qscale, rk = rsqrtf(sk + 1e-6f);
+      __half2* qd = reinterpret_cast<__half2*>(&sm.q[r * LQK + lane * 4]);
+      __half2* kd = reinterpret_cast<__half2*>(&sm.k[r * LQK + lane * 4]);
+      qd[0] = __floats2half2_rn(qv.x * rq, qv.y * rq);
+      qd[1] = __floats2half2_rn(qv.z * rq, qv.w * rq);
+      kd[0] = __floats2half2_rn(kv.x * rk, kv.y * rk);
+      kd[1] = __floats2half2_rn(kv.z * rk, kv.w * rk);
+      for (int j = lane; j < DVS; j += 32) {
+        if constexpr (kStage) sm.v[r * LV + j] = sm.rv[r * DVS + j];
+        else sm.v[r * LV + j] = __float2half_rn(r < n ? load1(vg + (long long)(t0 + r) * a.v_stride + j) : 0.0f);
+      }
+    }
+    if (threadIdx.x < CH) {
+      const int r = threadIdx.x;
+      if constexpr (kStage) {
+        sm.beta[r] = sm.rbeta[r];
+        sm.g[r] = sm.rg[r];
+      } else {
+        sm.beta[r] = r < n ? betag[(long long)(t0 + r) * H] : 0.0f;
+        sm.g[r] = r < n ? gg[(long long)(t0 + r) * H] : 0.0f;
+      }
+    }
+    __syncthreads();
+    if constexpr (kStage) {
+      if (t0 + CH < a.l) prefetch(t0 + CH);  // the staging buffers are free again
+    }
+    if (warp == 0) {  // inclusive prefix sum of the log decays
+      const float x0 = sm.g[2 * lane], x1 = sm.g[2 * lane + 1];
+      float s = x0 + x1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += u;
+      }
+      const float before = s - (x0 + x1);
+      sm.G[2 * lane] = before + x0;
+      sm.G[2 * lane + 1] = s;
+    }
+    __syncthreads();
+
+    // 2. K^ K^T -> A (masked, scaled, f32) and Q^ K^T -> P (masked, decayed, f16)
+    {
+      const int nb = (warp >> 2) * 32;
+      float kk[4][4], qk[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) kk[i][j] = qk[i][j] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ks++) {
+        uint32_t ak[4], aq[4];
+        ldsm_x4(a_addr(sm.k, LQK, mt * 16, ks * 16, lane), ak);
+        ldsm_x4(a_addr(sm.q, LQK, mt * 16, ks * 16, lane), aq);
+#pragma unroll
+        for (int j2 = 0; j2 < 2; j2++) {
+          uint32_t bk[4];
+          ldsm_x4(bn_addr(sm.k, LQK, nb + j2 * 16, ks * 16, lane), bk);
+          mma16816(kk[2 * j2], ak, bk[0], bk[1]);
+          mma16816(kk[2 * j2 + 1], ak, bk[2], bk[3]);
+          mma16816(qk[2 * j2], aq, bk[0], bk[1]);
+          mma16816(qk[2 * j2 + 1], aq, bk[2], bk[3]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          const int i = mt * 16 + g8 + (r >> 1) * 8, j = nb + nt * 8 + 2 * tq + (r & 1);
+          const float e = j <= i ? __expf(sm.G[i] - sm.G[j]) : 0.0f;
+          sm.a[i * LA + j] = j < i ? sm.beta[i] * e * kk[nt][r] : 0.0f;
+          sm.p[i * L64 + j] = __float2half_rn(e * qk[nt][r]);
+        }
+    }
+    __syncthreads();
+
+    // 3. T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution (warp bb, lane =
+    // column), then the off-diagonal blocks level by level: X_ij = -X_ii sum_{m=j}^{i-1} A_im X_mj.
+    if (warp < 4 && lane < 16) {
+      const int o = warp * 16, c = lane;
+      float xc[16];
+#pragma unroll
+      for (int r = 0; r < 16; r++) {
+        float val = r == c ? 1.0f : 0.0f;
+#pragma unroll
+        for (int j = 0; j < r; j++)
+          if (j >= c) val -= sm.a[(o + r) * LA + o + j] * xc[j];
+        xc[r] = r >= c ? val : 0.0f;
+      }
+#pragma unroll
+      for (int r = 0; r < 16; r++) sm.x[(o + r) * LA + o + c] = xc[r];
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int dl = 1; dl < 4; dl++) {
+      const int npair = 4 - dl;
+      for (int e = threadIdx.x; e < npair * 256; e += 256) {
+        const int pr = e >> 8, r = (e >> 4) & 15, c = e & 15;
+        const int bi = dl + pr, bj = pr;
+        float s = 0.0f;
+        for (int m = bj; m < bi; m++)
+#pragma unroll
+          for (int q = 0; q < 16; q++) s += sm.a[(bi * 16 + r) * LA + m * 16 + q] * sm.x[(m * 16 + q) * LA + bj * 16 + c];
+        sm.y[pr * 272 + r * 17 + c] = s;
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < npair * 256; e += 256) {
+        const int pr = e >> 8, r = (e >> 4) & 15, c = e & 15;
+        const int bi = dl + pr, bj = pr;
+        float s = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 16; q++) s += sm.x[(bi * 16 + r) * LA + bi * 16 + q] * sm.y[pr * 272 + q * 17 + c];
+        sm.x[(bi * 16 + r) * LA + bj * 16 + c] = -s;
+      }
+      __syncthreads();
+    }
+    // T1 = T diag(beta Gamma), T2 = T diag(beta) (lower triangular, f16)
+    for (int e = threadIdx.x; e < CH * CH; e += 256) {
+      const int i = e >> 6, j = e & 63;
+      const float t = j <= i ? sm.x[i * LA + j] : 0.0f;
+      const float bj = sm.beta[j];
+      sm.t1[i * L64 + j] = __float2half_rn(t * bj * __expf(sm.G[j]));
+      sm.t2[i * L64 + j] = __float2half_rn(t * bj);
+    }
+    __syncthreads();
+
+    // 4. W = T1 K^ (64 x 128, to shared memory) and U = T2 V (64 x DVS, in registers)
+    float uacc[NT][4];
+    {
+      const int nw = (warp >> 2) * 64;
+      float wacc[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; i++) wacc[i][0] = wacc[i][1] = wacc[i][2] = wacc[i][3] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NT; i++) uacc[i][0] = uacc[i][1] = uacc[i][2] = uacc[i][3] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < CH / 16; ks++) {
+        uint32_t at1[4], at2[4];
+        ldsm_x4(a_addr(sm.t1, L64, mt * 16, ks * 16, lane), at1);
+        ldsm_x4(a_addr(sm.t2, L64, mt * 16, ks * 16, lane), at2);
+#pragma unroll
+        for (int j2 = 0; j2 < 4; j2++) {
+          uint32_t bk[4];
+          ldsm_x4_t(bt_addr(sm.k, LQK, ks * 16, nw + j2 * 16, lane), bk);
+          mma16816(wacc[2 * j2], at1, bk[0], bk[1]);
+          mma16816(wacc[2 * j2 + 1], at1, bk[2], bk[3]);
+        }
+#pragma unroll
+        for (int j2 = 0; j2 < NT / 2; j2++) {
+          uint32_t bv[4];
+          ldsm_x4_t(bt_addr(sm.v, LV, ks * 16, nbase + j2 * 16, lane), bv);
+          mma16816(uacc[2 * j2], at2, bv[0], bv[1]);
+          mma16816(uacc[2 * j2 + 1], at2, bv[2], bv[3]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 8; nt++) {
+        const int row = mt * 16 + g8, col = nw + nt * 8 + 2 * tq;
+        *reinterpret_cast<__half2*>(&sm.w[row * LQK + col]) = __floats2half2_rn(wacc[nt][0], wacc[nt][1]);
+        *reinterpret_cast<__half2*>(&sm.w[(row + 8) * LQK + col]) = __floats2half2_rn(wacc[nt][2], wacc[nt][3]);
+      }
+    }
+    __syncthreads();
+
+    // 5. delta = U - W S0 and Gamma Q^ S0
+    float oacc[NT][4];
+    {
+      float wsacc[NT][4];
+#pragma unroll
+      for (int i = 0; i < NT; i++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) wsacc[i][r] = oacc[i][r] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ks++) {
+        uint32_t aw[4], aq[4];
+        ldsm_x4(a_addr(sm.w, LQK, mt * 16, ks * 16, lane), aw);
+        ldsm_x4(a_addr(sm.q, LQK, mt * 16, ks * 16, lane), aq);
+#pragma unroll
+        for (int j2 = 0; j2 < NT / 2; j2++) {
+          uint32_t bs[4];
+          ldsm_x4_t(bt_addr(sm.s, LV, ks * 16, nbase + j2 * 16, lane), bs);
+          mma16816(wsacc[2 * j2], aw, bs[0], bs[1]);
+          mma16816(wsacc[2 * j2 + 1], aw, bs[2], bs[3]);
+          mma16816(oacc[2 * j2], aq, bs[0], bs[1]);
+          mma16816(oacc[2 * j2 + 1], aq, bs[2], bs[3]);
+        }
+      }
+      const float glast = sm.G[CH - 1];
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+          const int i = mt * 16 + g8 + hf * 8, col = nbase + nt * 8 + 2 * tq;
+          const float d0 = uacc[nt][2 * hf] - wsacc[nt][2 * hf], d1 = uacc[nt][2 * hf + 1] - wsacc[nt][2 * hf + 1];
+          const float gi = __expf(sm.G[i]), sc = __expf(glast - sm.G[i]);
+          *reinterpret_cast<__half2*>(&sm.d[i * LV + col]) = __floats2half2_rn(d0, d1);
+          *reinterpret_cast<__half2*>(&sm.ds[i * LV + col]) = __floats2half2_rn(d0 * sc, d1 * sc);
+          oacc[nt][2 * hf] *= gi;
+          oacc[nt][2 * hf + 1] *= gi;
+        }
+    }
+    __syncthreads();
+
+    // 6. O = Gamma Q^ S0 + P delta, stored for the valid tokens
+    {
+#pragma unroll
+      for (int ks = 0; ks < CH / 16; ks++) {
+        uint32_t ap[4];
+        ldsm_x4(a_addr(sm.p, L64, mt * 16, ks * 16, lane), ap);
+#pragma unroll
+        for (int j2 = 0; j2 < NT / 2; j2++) {
+          uint32_t bd[4];
+          ldsm_x4_t(bt_addr(sm.d, LV, ks * 16, nbase + j2 * 16, lane), bd);
+          mma16816(oacc[2 * j2], ap, bd[0], bd[1]);
+          mma16816(oacc[2 * j2 + 1], ap, bd[2], bd[3]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+          const int i = mt * 16 + g8 + hf * 8, col = nbase + nt * 8 + 2 * tq;
+          if (i < n)
+            *reinterpret_cast<float2*>(og + (long long)(t0 + i) * H * DK + col) =
+                make_float2(oacc[nt][2 * hf], oacc[nt][2 * hf + 1]);
+        }
+    }
+
+    // 7. S = Gamma_C S0 + K^T (decayed delta)
+    {
+      const float gc = __expf(sm.G[CH - 1]);
+#pragma unroll
+      for (int nt = 0; nt < DVS / 8; nt++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) sacc[nt][r] *= gc;
+#pragma unroll
+      for (int ks = 0; ks < CH / 16; ks++) {
+        uint32_t akt[4];
+        ldsm_x4_t(at_addr(sm.k, LQK, ks * 16, warp * 16, lane), akt);
+#pragma unroll
+        for (int j2 = 0; j2 < DVS / 16; j2++) {
+          uint32_t bd[4];
+          ldsm_x4_t(bt_addr(sm.ds, LV, ks * 16, j2 * 16, lane), bd);
+          mma16816(sacc[2 * j2], akt, bd[0], bd[1]);
+          mma16816(sacc[2 * j2 + 1], akt, bd[2], bd[3]);
+        }
+      }
+    }
+    __syncthreads();  // every warp is done reading the old f16 state and this chunk's tiles
+    write_state_f16();
+    __syncthreads();
+  }
+  // final state (f32)
+#pragma unroll
+  for (int nt = 0; nt < DVS / 8; nt++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
+      stg[row * DK + col] = sacc[nt][r];
+    }
+}
+
+template <int DVS, typename TIn>
+static cudaError_t launch_chunk(const GdnArgs<TIn>& a, int batch, cudaStream_t st) {
+  auto kern = gdn_chunk_kernel<DVS, TIn>;
+  const int smem = (int)sizeof(GdnSmem<DVS>);
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  dim3 grid(a.h * (DK / DVS), batch);
+  kern<<<grid, 256, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+// The chunked scan over `batch` sequences. DVS (value columns per CTA) trades redundant intra-chunk
+// work for parallelism: 32 for a single sequence (64 CTAs for 16 heads), 64 for batches.
+cudaError_t launch_gdn_chunked(const void* q, const void* k, int qk_stride, const void* v, int v_stride, long long seq_qk,
+                               long long seq_v, bool in_f16, const float* beta, const float* g, float* state, bool load_state,
+                               float* o, int l, int h, int batch, cudaStream_t st) {
+  if (l <= 0 || h <= 0 || batch <= 0) return cudaErrorInvalidValue;
+  const bool wide = (long long)batch * h >= 128;
+  if (in_f16) {
+    GdnArgs<__half> a{(const __half*)q, (const __half*)k, (const __half*)v, qk_stride, v_stride, seq_qk, seq_v,
+                      beta, g, state, o, load_state ? 1 : 0, l, h};
+    return wide ? launch_chunk<64>(a, batch, st) : launch_chunk<32>(a, batch, st);
+  }
+  GdnArgs<float> a{(const float*)q, (const float*)k, (const float*)v, qk_stride, v_stride, seq_qk, seq_v,
+                   beta, g, state, o, load_state ? 1 : 0, l, h};
+  return wide ? launch_chunk<64>(a, batch, st) : launch_chunk<32>(a, batch, st);
+}
+
+}  // namespace sd

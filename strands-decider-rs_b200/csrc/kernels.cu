@@ -109,10 +109,14 @@ __global__ void __launch_bounds__(256) add_norm_kernel(float* __restrict__ x, co
 // The final norm (src/kernels.rs:93-120 with add and f32 out, src/engine.rs:519-522): for each
 // requested row, x += y, out = x * inv * w in f32.
 __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, const __half* __restrict__ y,
-                                                         const float* __restrict__ w, const int* __restrict__ rows, int d,
-                                                         float* __restrict__ out) {
+                                                         const float* __restrict__ w, const int* __restrict__ rows, int l,
+                                                         int d, float* __restrict__ out, int* err) {
   __shared__ float red[8];
   const int r = rows[blockIdx.x];
+  if (r < 0 || r >= l) {  // rows given on the device are checked here
+    if (threadIdx.x == 0) atomicCAS(err, 0, kErrBadShape);
+    return;
+  }
   float v[8];
   float ss = 0.0f;
 #pragma unroll
@@ -135,9 +139,11 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
 }
 
 // conv (src/kernels.rs:152-170): depthwise causal conv, kernel 4, over the q/k/v channels of the
-// in_proj row, reading the 3-row history for t < 0; then SiLU, f32 out.
+// in_proj row, reading the 3-row history for t < 0; then SiLU. The output is stored as f16 (the
+// reference keeps f32): the chunked scan that reads it rounds q, k and v to f16 tensor-core operands
+// anyway, after normalising q and k in f32.
 __global__ void conv_kernel(const __half* __restrict__ big, int stride, const float4* __restrict__ cw,
-                            const __half* __restrict__ hist, int l, int C, float* __restrict__ out) {
+                            const __half* __restrict__ hist, int l, int C, __half* __restrict__ out) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int t = blockIdx.y;
   if (c >= C) return;
@@ -150,7 +156,7 @@ __global__ void conv_kernel(const __half* __restrict__ big, int stride, const fl
     const float v = tt >= 0 ? __half2float(big[(size_t)tt * stride + c]) : __half2float(hist[(size_t)(tt + 3) * C + c]);
     s += kk[j] * v;
   }
-  out[(size_t)t * C + c] = s / (1.0f + __expf(-s));
+  out[(size_t)t * C + c] = __float2half_rn(s / (1.0f + __expf(-s)));
 }
 
 // hist_update (src/kernels.rs:173-190): the last 3 pre-conv rows of (old history ++ this call).
@@ -167,11 +173,11 @@ __global__ void hist_update_kernel(const __half* __restrict__ big, int stride, _
   for (int r = 0; r < 3; r++) hist[(size_t)r * C + c] = v[r];
 }
 
-// The per-token gates of the gated delta rule (src/kernels.rs:289-292): beta = sigmoid(b),
-// decay = exp(negA * softplus(a + dt_bias)) with softplus(x) = x above 20.
+// The per-token gates of the gated delta rule (src/kernels.rs:289-292): beta = sigmoid(b) and the log
+// decay g = negA * softplus(a + dt_bias), softplus(x) = x above 20 (the decay is exp(g)).
 __global__ void gdn_gates_kernel(const __half* __restrict__ big, int stride, int aoff, int boff, const float* __restrict__ neg_a,
                                  const float* __restrict__ dtb, int l, int h, float* __restrict__ beta,
-                                 float* __restrict__ decay) {
+                                 float* __restrict__ gl) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= l * h) return;
   const int t = i / h, hh = i % h;
@@ -180,7 +186,7 @@ __global__ void gdn_gates_kernel(const __half* __restrict__ big, int stride, int
   beta[i] = 1.0f / (1.0f + expf(-b));
   const float x = a + dtb[hh];
   const float sp = x > 20.0f ? x : logf(1.0f + expf(x));
-  decay[i] = expf(neg_a[hh] * sp);
+  gl[i] = neg_a[hh] * sp;
 }
 
 // Gated delta rule, sequential over tokens (src/kernels.rs:257-302): one CTA per (head, 32 value
@@ -188,7 +194,7 @@ __global__ void gdn_gates_kernel(const __half* __restrict__ big, int stride, int
 // 32 registers per lane. State [h][128][128] f32: loaded when continuing a prefix, always stored.
 __global__ void __launch_bounds__(128) gdn_recurrent_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                                             int qk_stride, const float* __restrict__ v, int v_stride,
-                                                            const float* __restrict__ beta, const float* __restrict__ decay,
+                                                            const float* __restrict__ beta, const float* __restrict__ gl,
                                                             float* __restrict__ state, int load_state,
                                                             float* __restrict__ o, int l, int h) {
   constexpr int DK = 128, DV = 128;
@@ -209,7 +215,7 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(const float* __restr
     const float rq = rsqrtf(sq + 1e-6f) * qs, rk = rsqrtf(sk + 1e-6f);
     const float4 qn = make_float4(q4.x * rq, q4.y * rq, q4.z * rq, q4.w * rq);
     const float4 kn = make_float4(k4.x * rk, k4.y * rk, k4.z * rk, k4.w * rk);
-    const float dc = decay[(size_t)t * h + hh], bt = beta[(size_t)t * h + hh];
+    const float dc = expf(gl[(size_t)t * h + hh]), bt = beta[(size_t)t * h + hh];
     const float* vt = v + (size_t)t * v_stride + hh * DV + dv0;
     float mine = 0.0f;
 #pragma unroll
@@ -322,14 +328,14 @@ cudaError_t launch_add_norm(float* x, const __half* y, const float* w, int l, in
   return cudaGetLastError();
 }
 
-cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int d, float* out,
-                              cudaStream_t st) {
+cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int l, int d, float* out,
+                              int* err, cudaStream_t st) {
   if (nrows <= 0) return cudaSuccess;
-  final_norm_kernel<<<nrows, 256, 0, st>>>(x, y, w, rows, d, out);
+  final_norm_kernel<<<nrows, 256, 0, st>>>(x, y, w, rows, l, d, out, err);
   return cudaGetLastError();
 }
 
-cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, float* qkvc,
+cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, __half* qkvc,
                         cudaStream_t st) {
   dim3 grid((C + 255) / 256, l);
   conv_kernel<<<grid, 256, 0, st>>>(big, stride, reinterpret_cast<const float4*>(conv_w), hist, l, C, qkvc);
@@ -342,15 +348,15 @@ cudaError_t launch_hist_update(const __half* big, int stride, __half* hist, int 
 }
 
 cudaError_t launch_gdn_gates(const __half* big, int stride, int aoff, int boff, const float* neg_a, const float* dt_bias,
-                             int l, int h, float* beta, float* decay, cudaStream_t st) {
-  gdn_gates_kernel<<<blocks_for((int64_t)l * h, 256), 256, 0, st>>>(big, stride, aoff, boff, neg_a, dt_bias, l, h, beta, decay);
+                             int l, int h, float* beta, float* gl, cudaStream_t st) {
+  gdn_gates_kernel<<<blocks_for((int64_t)l * h, 256), 256, 0, st>>>(big, stride, aoff, boff, neg_a, dt_bias, l, h, beta, gl);
   return cudaGetLastError();
 }
 
 cudaError_t launch_gdn_recurrent(const float* q, const float* k, int qk_stride, const float* v, int v_stride,
-                                 const float* beta, const float* decay, float* state, bool load_state, float* o, int l,
+                                 const float* beta, const float* gl, float* state, bool load_state, float* o, int l,
                                  int h, cudaStream_t st) {
-  gdn_recurrent_kernel<<<h * 4, 128, 0, st>>>(q, k, qk_stride, v, v_stride, beta, decay, state, load_state ? 1 : 0, o, l, h);
+  gdn_recurrent_kernel<<<h * 4, 128, 0, st>>>(q, k, qk_stride, v, v_stride, beta, gl, state, load_state ? 1 : 0, o, l, h);
   return cudaGetLastError();
 }
 

@@ -11,6 +11,15 @@ namespace sd {
 
 constexpr int kMaxDevices = 64;
 
+// Error codes a kernel writes to its launch's device error word (the first one sticks).
+enum : int {
+  kErrNone = 0,
+  kErrTimeoutFull = 1,   // a consumer gave up waiting for a stage to fill
+  kErrTimeoutEmpty = 2,  // a producer gave up waiting for a stage to drain
+  kErrTimeoutAccum = 3,  // the epilogue gave up waiting for the accumulator
+  kErrBadShape = 4,      // a token id or row index out of range
+};
+
 // A block-quantized int4 weight repacked into the GEMM's tile layout (gemm.cu).
 struct QWeight {
   uint8_t* tiles = nullptr;
@@ -21,8 +30,10 @@ struct QWeight {
 
 cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool interleave, QWeight* out, cudaStream_t st);
 void gemm_plan(const QWeight& w, int M, int num_sms, int* bn, int* splits, int* kps);
+// y[M][ldy] = act[M][K] W^T, or SwiGLU of interleaved gate/up rows into y[M][N/2] when silu; ws is
+// the f32 split-K workspace (M * N floats; smaller disables split-K); *nlaunch gets the kernel count.
 cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
-                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st);
+                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch = nullptr);
 int make_act_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
 
 // Model dims the kernels are specialised for (src/kernels.rs:813-835).
@@ -37,16 +48,23 @@ struct Dims {
 cudaError_t launch_embed_norm(const uint32_t* ids, int l, const uint8_t* eq, const __half* es, int bits, int d, int vocab,
                               const float* w, float* x, __half* h, int* err, cudaStream_t st);
 cudaError_t launch_add_norm(float* x, const __half* y, const float* w, int l, int d, bool add, __half* h, cudaStream_t st);
-cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int d, float* out,
-                              cudaStream_t st);
-cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, float* qkvc,
+cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int l, int d, float* out,
+                              int* err, cudaStream_t st);
+cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, __half* qkvc,
                         cudaStream_t st);
 cudaError_t launch_hist_update(const __half* big, int stride, __half* hist, int l, int C, cudaStream_t st);
+// gates: beta = sigmoid(b), g = log decay = negA softplus(a + dt_bias), both [l][h]
 cudaError_t launch_gdn_gates(const __half* big, int stride, int aoff, int boff, const float* neg_a, const float* dt_bias,
-                             int l, int h, float* beta, float* decay, cudaStream_t st);
+                             int l, int h, float* beta, float* g, cudaStream_t st);
+// token-serial gated delta rule (one sequence), decay exp(g) per token as the reference computes it
 cudaError_t launch_gdn_recurrent(const float* q, const float* k, int qk_stride, const float* v, int v_stride,
-                                 const float* beta, const float* decay, float* state, bool load_state, float* o, int l,
+                                 const float* beta, const float* g, float* state, bool load_state, float* o, int l,
                                  int h, cudaStream_t st);
+// chunked gated delta rule (gdn.cu) over `batch` sequences: q/k/v f32 or f16 rows (head h at
+// h * 128), gates [batch][l][h], state [batch][h][128][128], o [batch][l][h * 128] f32
+cudaError_t launch_gdn_chunked(const void* q, const void* k, int qk_stride, const void* v, int v_stride, long long seq_qk,
+                               long long seq_v, bool in_f16, const float* beta, const float* g, float* state, bool load_state,
+                               float* o, int l, int h, int batch, cudaStream_t st);
 cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff, const float* w, int l, int h, __half* out,
                          cudaStream_t st);
 cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,

@@ -47,6 +47,14 @@ def lib() -> C.CDLL:
         L.sd_engine_last_error.argtypes = [vp]
         L.sd_engine_set_trace.argtypes = [vp, vp, C.c_size_t]
         L.sd_forward.argtypes = [vp, vp, i32, vp, i32, vp, i32, vp, C.POINTER(vp), C.POINTER(C.c_double)]
+        L.sd_forward_dev.argtypes = [vp, vp, i32, vp, i32, vp, i32, vp, C.POINTER(vp)]
+        L.sd_engine_synchronize.argtypes = [vp]
+        L.sd_engine_stream.restype = vp
+        L.sd_engine_stream.argtypes = [vp]
+        L.sd_engine_launches.restype = C.c_int64
+        L.sd_engine_launches.argtypes = [vp]
+        L.sd_engine_profile.argtypes = [vp, i32]
+        L.sd_engine_profile_get.argtypes = [vp, i32, C.POINTER(C.c_double), C.POINTER(C.c_int64), C.POINTER(C.c_double)]
         L.sd_snapshot_len.restype = i32
         L.sd_snapshot_len.argtypes = [vp]
         L.sd_snapshot_free.argtypes = [vp]
@@ -54,7 +62,7 @@ def lib() -> C.CDLL:
         L.sd_head_free.argtypes = [vp]
         L.sd_head_probs.argtypes = [vp, vp, i32, i32, C.c_double, vp]
         L.sd_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]
-        L.sd_gdn.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, vp]
+        L.sd_gdn.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, i32, C.c_int64, C.c_int64, i32, i32, vp]
         L.sd_qweight_create.argtypes = [vp, vp, i32, i32, i32, C.POINTER(vp)]
         L.sd_qweight_free.argtypes = [vp]
         L.sd_matmul.argtypes = [vp, vp, i32, vp, i32, i32, vp, C.c_size_t, vp]
@@ -153,6 +161,38 @@ class Engine:
         out.trace = tr
         return out
 
+    def forward_dev(self, ids_dev: int, n_ids: int, rows_dev: int | None, n_rows: int, cache: Snapshot | None = None,
+                    keep: bool = False, hidden_dev: int | None = None) -> Snapshot | None:
+        """`sd_forward_dev`: the forward on device buffers, queued on the engine's stream."""
+        snap = C.c_void_p()
+        _check(lib().sd_forward_dev(self._h, ids_dev, n_ids, rows_dev, n_rows, cache._h if cache is not None else None,
+                                    int(keep), hidden_dev, C.byref(snap)), "sd_forward_dev", self._h)
+        return Snapshot(snap.value) if keep else None
+
+    def synchronize(self):
+        _check(lib().sd_engine_synchronize(self._h), "sd_engine_synchronize", self._h)
+
+    @property
+    def stream(self) -> int:
+        return lib().sd_engine_stream(self._h) or 0
+
+    def launches(self) -> int:
+        return int(lib().sd_engine_launches(self._h))
+
+    PROFILE_KINDS = ("gemm", "attention", "gdn", "other")
+
+    def profile(self, enable: bool):
+        """Per-kernel-kind device time (the reference's `Engine::profile`, `src/engine.rs:665-711`)."""
+        _check(lib().sd_engine_profile(self._h, int(enable)), "sd_engine_profile", self._h)
+
+    def profile_get(self) -> dict:
+        out = {}
+        for i, name in enumerate(self.PROFILE_KINDS):
+            ms, n, work = C.c_double(), C.c_int64(), C.c_double()
+            _check(lib().sd_engine_profile_get(self._h, i, C.byref(ms), C.byref(n), C.byref(work)), "profile", self._h)
+            out[name] = {"ms": ms.value, "launches": n.value, "work": work.value}
+        return out
+
     def close(self):
         if self._h:
             lib().sd_engine_destroy(self._h)
@@ -199,8 +239,11 @@ def attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, st
     _check(lib().sd_attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, stream), "sd_attention")
 
 
-def gdn(q, k, qk_stride, v, v_stride, beta, decay, state, load_state, o, l, h, stream=None):
-    _check(lib().sd_gdn(q, k, qk_stride, v, v_stride, beta, decay, state, int(load_state), o, l, h, stream), "sd_gdn")
+def gdn(q, k, qk_stride, v, v_stride, beta, g, state, load_state, o, l, h, batch=1, seq_qk=0, seq_v=0, in_f16=False,
+        serial=False, stream=None):
+    """`sd_gdn`: g is the log decay (decay = exp(g))."""
+    _check(lib().sd_gdn(q, k, qk_stride, v, v_stride, beta, g, state, int(load_state), o, l, h, batch, seq_qk, seq_v,
+                        int(in_f16), int(serial), stream), "sd_gdn")
 
 
 class QWeight:

@@ -46,6 +46,7 @@ PROD = dict(
     rotary_dim=64,
 )
 PROD_VOCAB = 248320
+WRITER_VERSION = 2  # bumped whenever the seeded weights change
 PROD_LAYERS = 24
 HEAD_DIM_OUT = 256
 
@@ -350,18 +351,20 @@ def write_synthetic(path: str, seed: int = 0, n_layers: int = PROD_LAYERS, vocab
     cfg_d = asdict(cfg)
     manifest = {"config": cfg_d, "shards": [{"path": "weights.0.bin", "start": 0, "bytes": total}],
                 "tensors": tensors, "embed": embed, "tokenizer": "tokenizer.json",
-                "synthetic": {"seed": seed, "n_layers": len(types), "vocab": vocab}}
+                "synthetic": {"seed": seed, "n_layers": len(types), "vocab": vocab, "writer": WRITER_VERSION}}
     with open(os.path.join(path, "manifest.json"), "w") as f:
         json.dump(manifest, f, indent=1)
 
-    # Pointer head: LayerNorm then q/k projections to HEAD_DIM_OUT (`src/head.rs:55-66`).
+    # Pointer head: LayerNorm then q/k projections to HEAD_DIM_OUT (`src/head.rs:55-66`), sized so the
+    # option logits (q.k / sqrt(dim)) have a standard deviation near 1.4: the spread of the reference's
+    # example answer (0.874 / 0.065 / 0.062, logit gaps near 2.6, `README.md` of the reference).
     hrng = np.random.default_rng(seed + 2)
     head = {
         "norm.weight": (1.0 + 0.1 * hrng.standard_normal(d)).astype(np.float32),
         "norm.bias": (0.1 * hrng.standard_normal(d)).astype(np.float32),
-        "q.weight": (hrng.standard_normal((HEAD_DIM_OUT, d)) / np.sqrt(d) * 2.0).astype(np.float32),
+        "q.weight": (hrng.standard_normal((HEAD_DIM_OUT, d)) / np.sqrt(d) * 1.2).astype(np.float32),
         "q.bias": (0.1 * hrng.standard_normal(HEAD_DIM_OUT)).astype(np.float32),
-        "k.weight": (hrng.standard_normal((HEAD_DIM_OUT, d)) / np.sqrt(d) * 2.0).astype(np.float32),
+        "k.weight": (hrng.standard_normal((HEAD_DIM_OUT, d)) / np.sqrt(d) * 1.2).astype(np.float32),
         "k.bias": (0.1 * hrng.standard_normal(HEAD_DIM_OUT)).astype(np.float32),
     }
     write_safetensors(os.path.join(path, "head.safetensors"), head)
@@ -406,7 +409,8 @@ def read_safetensors(path: str) -> dict[str, np.ndarray]:
 
 def ensure_model(path: str, **kw) -> str:
     """Writes the synthetic model at ``path`` unless a complete one with the same settings is there."""
-    want = {"seed": kw.get("seed", 0), "n_layers": kw.get("n_layers", PROD_LAYERS), "vocab": kw.get("vocab", PROD_VOCAB)}
+    want = {"seed": kw.get("seed", 0), "n_layers": kw.get("n_layers", PROD_LAYERS), "vocab": kw.get("vocab", PROD_VOCAB),
+            "writer": WRITER_VERSION}
     mpath = os.path.join(path, "manifest.json")
     if os.path.exists(mpath) and os.path.exists(os.path.join(path, "tokenizer.json")):
         try:
