@@ -109,11 +109,14 @@ int sd_attention(const void* q_dev, const void* k_dev, const void* v_dev, const 
  * q_dev/k_dev [batch][l][qk_stride] (head h at h * 128), v_dev [batch][l][v_stride] (head h at h * 128),
  * f32, or f16 when in_f16; seq_qk/seq_v: elements between sequences. beta_dev and g_dev (the log decay:
  * the decay is exp(g)) [batch][l][h] f32; state_dev [batch][h][128][128] f32 (read when load_state,
- * always written); o_dev [batch][l][h * 128] f32. `serial` selects the token-serial kernel (f32, one
- * sequence) instead of the chunked scan. */
+ * always written); o_dev [batch][l][h * 128] f32. algo 0: the chunked scan (64-token chunks, one
+ * pass); 1: the token-serial recurrence (f32, batch 1); 2: the two-phase chunked scan (f16, batch 1;
+ * needs scratch_dev of sd_gdn_scratch_bytes(l, h) bytes). */
 int sd_gdn(const void* q_dev, const void* k_dev, int32_t qk_stride, const void* v_dev, int32_t v_stride,
            const void* beta_dev, const void* g_dev, void* state_dev, int32_t load_state, void* o_dev, int32_t l,
-           int32_t h, int32_t batch, int64_t seq_qk, int64_t seq_v, int32_t in_f16, int32_t serial, void* stream);
+           int32_t h, int32_t batch, int64_t seq_qk, int64_t seq_v, int32_t in_f16, int32_t algo, void* scratch_dev,
+           size_t scratch_bytes, void* stream);
+size_t sd_gdn_scratch_bytes(int32_t l, int32_t h);
 
 /* A block-quantized int4 group-32 symmetric weight (`src/kernels.rs:545-576`) in the GEMM's tile
  * layout, made from the reference layout on the device: q_dev [n][k/32][16 bytes], s_dev [n][k/32] f16.

@@ -8,6 +8,7 @@
 // the reference's packed rows. Per gated-delta layer: state [16][128][128] f32 and conv history
 // [3][6144] f16; per attention layer: K and V caches [2][4096][256] f16. Activations live in a pool
 // sized for the longest forward so far.
+#include <immintrin.h>
 #include <sys/stat.h>
 
 #include <cmath>
@@ -133,6 +134,8 @@ struct sd_engine {
   float *x = nullptr, *of = nullptr, *beta = nullptr, *decay = nullptr, *out = nullptr, *ws = nullptr;
   float* trace_dev = nullptr;
   size_t ws_bytes = 0;
+  void* gdn_scratch = nullptr;  // per-chunk records of the two-phase scan
+  size_t gdn_scratch_bytes = 0;
   __half *h = nullptr, *big = nullptr, *mid = nullptr, *o = nullptr, *y = nullptr, *q = nullptr, *qkvc = nullptr;
   int* d_err = nullptr;
   // pinned staging
@@ -192,7 +195,8 @@ namespace {
 void free_pool(sd_engine* e) {
   cudaFree(e->d_ids); cudaFree(e->d_rows); cudaFree(e->x); cudaFree(e->qkvc); cudaFree(e->of); cudaFree(e->beta);
   cudaFree(e->decay); cudaFree(e->out); cudaFree(e->ws); cudaFree(e->h); cudaFree(e->big); cudaFree(e->mid);
-  cudaFree(e->o); cudaFree(e->y); cudaFree(e->q); cudaFree(e->trace_dev);
+  cudaFree(e->o); cudaFree(e->y); cudaFree(e->q); cudaFree(e->trace_dev); cudaFree(e->gdn_scratch);
+  e->gdn_scratch = nullptr;
   e->d_ids = nullptr; e->d_rows = nullptr; e->x = e->of = e->beta = e->decay = e->out = e->ws = nullptr;
   e->qkvc = nullptr;
   e->trace_dev = nullptr;
@@ -227,6 +231,8 @@ int ensure_pool(sd_engine* e, int l) {
   // i.e. for small M; 64 MiB covers 32 splits of 64 x 8256 or 16 of 64 x 12288
   e->ws_bytes = (size_t)64 << 20;
   CK(cudaMalloc(&e->ws, e->ws_bytes));
+  e->gdn_scratch_bytes = sd::gdn_two_phase_scratch(cap, d.h);
+  CK(cudaMalloc(&e->gdn_scratch, e->gdn_scratch_bytes));
   if (e->trace_host) CK(cudaMalloc(&e->trace_dev, (size_t)e->n_layers * cap * d.d * 4));
   e->cap = cap;
   return SD_OK;
@@ -590,9 +596,16 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
         LK(SD_PROF_OTHER, L * d.h * 12.0,
            sd::launch_gdn_gates(e->big, N, aoff, boff, Lw.neg_a, Lw.dt_bias, l, d.h, e->beta, e->decay, st));
         const double gdn_bytes = L * (C * 2.0 + d.h * 8.0 + d.h * d.dv * 4.0) + 2.0 * d.h * d.dk * d.dv * 4.0;
-        LK(SD_PROF_GDN, gdn_bytes,
-           sd::launch_gdn_chunked(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, 0, 0, true, e->beta,
-                                  e->decay, e->state[Lw.slot], has_cache, e->of, l, d.h, 1, st));
+        // one chunk: the single-pass scan; longer: the two-phase scan (chunks in parallel, then the state walk)
+        if (l <= 64)
+          LK(SD_PROF_GDN, gdn_bytes,
+             sd::launch_gdn_chunked(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, 0, 0, true, e->beta,
+                                    e->decay, e->state[Lw.slot], has_cache, e->of, l, d.h, 1, st));
+        else
+          LK(SD_PROF_GDN, gdn_bytes,
+             (*nl = 2, sd::launch_gdn_two_phase(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, e->beta,
+                                                e->decay, e->state[Lw.slot], has_cache, e->of, l, d.h, e->gdn_scratch,
+                                                e->gdn_scratch_bytes, st)));
         LK(SD_PROF_OTHER, L * d.h * d.dv * 8.0, sd::launch_gnorm(e->of, e->big, N, C, Lw.gnorm, l, d.h, e->o, st));
         MM(Lw.out_proj, e->o, d.h * d.dv, e->y, d.d, false);
       } else {
@@ -937,31 +950,53 @@ int sd_head_probs(const sd_head* h, const float* hidden, int32_t nrows, int32_t 
     set_global_error("sd_head_probs: bad arguments");
     return SD_ERR_INVALID;
   }
-  auto project = [&](const float* x, const std::vector<float>& w, const std::vector<float>& b, std::vector<double>& outv) {
-    double mean = 0.0, var = 0.0;
-    for (int j = 0; j < d; j++) mean += (double)x[j];
-    mean /= d;
-    for (int j = 0; j < d; j++) var += ((double)x[j] - mean) * ((double)x[j] - mean);
-    var /= d;
-    const double r = 1.0 / std::sqrt(var + 1e-5);
-    std::vector<double> xn(d);
-    for (int j = 0; j < d; j++) xn[j] = ((double)x[j] - mean) * r * (double)h->nw[j] + (double)h->nb[j];
-    outv.assign(h->dim, 0.0);
+  // LayerNorm (eps 1e-5) then the q or k projection, in f64 (src/head.rs:55-66): xn = (x - mean) r
+  // norm.weight + norm.bias, out[o] = bias[o] + sum_j w[o][j] xn[j] with the f32 weights promoted; all
+  // `n` rows at once, so each weight row is read once for all of them
+  auto project = [&](const float* x, int n, const std::vector<float>& w, const std::vector<float>& b,
+                     std::vector<double>& outv) {
+    std::vector<double> xn((size_t)n * d);
+    for (int i = 0; i < n; i++) {
+      const float* xi = x + (size_t)i * d;
+      double mean = 0.0, var = 0.0;
+      for (int j = 0; j < d; j++) mean += (double)xi[j];
+      mean /= d;
+      for (int j = 0; j < d; j++) var += ((double)xi[j] - mean) * ((double)xi[j] - mean);
+      var /= d;
+      const double r = 1.0 / std::sqrt(var + 1e-5);
+      for (int j = 0; j < d; j++) xn[(size_t)i * d + j] = ((double)xi[j] - mean) * r * (double)h->nw[j] + (double)h->nb[j];
+    }
+    outv.assign((size_t)n * h->dim, 0.0);
     for (int o = 0; o < h->dim; o++) {
-      double s = 0.0;
-      for (int j = 0; j < d; j++) s += (double)w[(size_t)o * d + j] * xn[j];
-      outv[o] = (double)b[o] + s;
+      const float* wp = w.data() + (size_t)o * d;
+      for (int i = 0; i < n; i++) {
+        const double* xp = xn.data() + (size_t)i * d;
+        // four 4-wide f64 partial sums over j (AVX2 + FMA); the tail in scalar
+        __m256d a0 = _mm256_setzero_pd(), a1 = a0, a2 = a0, a3 = a0;
+        int j = 0;
+        for (; j + 16 <= d; j += 16) {
+          a0 = _mm256_fmadd_pd(_mm256_cvtps_pd(_mm_loadu_ps(wp + j)), _mm256_loadu_pd(xp + j), a0);
+          a1 = _mm256_fmadd_pd(_mm256_cvtps_pd(_mm_loadu_ps(wp + j + 4)), _mm256_loadu_pd(xp + j + 4), a1);
+          a2 = _mm256_fmadd_pd(_mm256_cvtps_pd(_mm_loadu_ps(wp + j + 8)), _mm256_loadu_pd(xp + j + 8), a2);
+          a3 = _mm256_fmadd_pd(_mm256_cvtps_pd(_mm_loadu_ps(wp + j + 12)), _mm256_loadu_pd(xp + j + 12), a3);
+        }
+        double part[4];
+        _mm256_storeu_pd(part, _mm256_add_pd(_mm256_add_pd(a0, a1), _mm256_add_pd(a2, a3)));
+        double sum = (part[0] + part[1]) + (part[2] + part[3]);
+        for (; j < d; j++) sum += (double)wp[j] * xp[j];
+        outv[(size_t)i * h->dim + o] = (double)b[o] + sum;
+      }
     }
   };
   std::vector<double> q, k;
   const int nopt = nrows - 1;
-  project(hidden + (size_t)nopt * d, h->qw, h->qb, q);
+  project(hidden + (size_t)nopt * d, 1, h->qw, h->qb, q);
+  project(hidden, nopt, h->kw, h->kb, k);
   const double scale = std::pow((double)h->dim, -0.5) / std::max(temperature, 1e-6);
   double mx = -1.79769313486231570e308;
   for (int i = 0; i < nopt; i++) {
-    project(hidden + (size_t)i * d, h->kw, h->kb, k);
     double s = 0.0;
-    for (int o = 0; o < h->dim; o++) s += k[o] * q[o];
+    for (int o = 0; o < h->dim; o++) s += k[(size_t)i * h->dim + o] * q[o];
     probs[i] = s * scale;
     mx = std::max(mx, probs[i]);
   }
@@ -996,23 +1031,31 @@ int sd_attention(const void* q, const void* k, const void* v, const void* gate, 
 
 int sd_gdn(const void* q, const void* k, int32_t qk_stride, const void* v, int32_t v_stride, const void* beta,
            const void* g, void* state, int32_t load_state, void* o, int32_t l, int32_t h, int32_t batch, int64_t seq_qk,
-           int64_t seq_v, int32_t in_f16, int32_t serial, void* stream) {
+           int64_t seq_v, int32_t in_f16, int32_t algo, void* scratch, size_t scratch_bytes, void* stream) {
   const size_t align = in_f16 ? 8 : 16;
   if (!q || !k || !v || !beta || !g || !state || !o || l <= 0 || h <= 0 || batch <= 0 || qk_stride % 4 ||
-      (size_t)q % align || (size_t)k % align || (serial && (in_f16 || batch != 1))) {
+      (size_t)q % align || (size_t)k % align || algo < 0 || algo > 2 || (algo == 1 && (in_f16 || batch != 1)) ||
+      (algo == 2 && (!in_f16 || batch != 1 || !scratch || scratch_bytes < sd::gdn_two_phase_scratch(l, h)))) {
     set_global_error("sd_gdn: bad arguments");
     return SD_ERR_INVALID;
   }
-  if (serial)
+  cudaStream_t st = (cudaStream_t)stream;
+  if (algo == 1)
     return op_result(sd::launch_gdn_recurrent((const float*)q, (const float*)k, qk_stride, (const float*)v, v_stride,
                                               (const float*)beta, (const float*)g, (float*)state, load_state != 0, (float*)o,
-                                              l, h, (cudaStream_t)stream),
+                                              l, h, st),
+                     "sd_gdn");
+  if (algo == 2)
+    return op_result(sd::launch_gdn_two_phase((const __half*)q, (const __half*)k, qk_stride, (const __half*)v, v_stride,
+                                              (const float*)beta, (const float*)g, (float*)state, load_state != 0, (float*)o,
+                                              l, h, scratch, scratch_bytes, st),
                      "sd_gdn");
   return op_result(sd::launch_gdn_chunked(q, k, qk_stride, v, v_stride, seq_qk, seq_v, in_f16 != 0, (const float*)beta,
-                                          (const float*)g, (float*)state, load_state != 0, (float*)o, l, h, batch,
-                                          (cudaStream_t)stream),
+                                          (const float*)g, (float*)state, load_state != 0, (float*)o, l, h, batch, st),
                    "sd_gdn");
 }
+
+size_t sd_gdn_scratch_bytes(int32_t l, int32_t h) { return l > 0 && h > 0 ? sd::gdn_two_phase_scratch(l, h) : 0; }
 
 int sd_qweight_create(const void* q, const void* s, int32_t n, int32_t k, int32_t interleave, sd_qweight** out) {
   if (!q || !s || !out || n <= 0 || k <= 0 || k % 64 || (interleave && n % 2)) {

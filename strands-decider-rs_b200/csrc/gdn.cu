@@ -472,6 +472,428 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Two-phase form for a few long sequences (the engine's case: one sequence, 16 heads). Phase 1
+// computes, for every (chunk, head) in parallel, everything that does not depend on the state; phase
+// 2 walks the chunks of each (head, value slice) in order with only the state-dependent products.
+// Per chunk and head, phase 1 writes (ChunkRec): K^ and Gamma Q^ (f16 64x128), W (f16 64x128),
+// U (f32 64x128), P (f16 64x64), exp(G_C - G_i) (f32 64) and Gamma_C.
+// ---------------------------------------------------------------------------------------------
+struct ChunkRec {
+  __half k[CH * DK];
+  __half qg[CH * DK];
+  __half w[CH * DK];
+  float u[CH * DK];
+  __half p[CH * CH];
+  float dsc[CH];
+  float gc;
+  float pad[3];
+};
+static_assert(sizeof(ChunkRec) % 16 == 0, "records are copied in 16-byte pieces");
+
+struct PrepSmem {
+  __half q[CH * LQK];
+  __half k[CH * LQK];
+  __half v[CH * LQK];
+  __half t1[CH * L64];
+  __half t2[CH * L64];
+  float a[CH * LA];
+  float x[CH * LA];
+  float y[3 * 16 * 17];
+  float beta[CH], g[CH], G[CH];
+};
+
+// Phase 1: grid (chunks, heads). Inputs f16 rows as in the chunked kernel (one sequence).
+__global__ void __launch_bounds__(256, 1) gdn_prep_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
+                                                          int qk_stride, const __half* __restrict__ v, int v_stride,
+                                                          const float* __restrict__ beta, const float* __restrict__ gl, int l,
+                                                          int H, ChunkRec* __restrict__ rec) {
+  extern __shared__ __align__(16) uint8_t prep_smem_raw[];
+  PrepSmem& sm = *reinterpret_cast<PrepSmem*>(prep_smem_raw);
+  const int c = blockIdx.x, h = blockIdx.y;
+  const int t0 = c * CH, n = min(CH, l - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g8 = lane >> 2, tq = lane & 3;
+  const int mt = warp & 3;
+  ChunkRec& R = rec[(size_t)h * ((l + CH - 1) / CH) + c];
+  const float qscale = rsqrtf((float)DK);
+
+  // 1. q^, k^ (normalised), v: each warp loads its 8 rows at once, then reduces
+  {
+    uint2 qr[8], kr[8], vr[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int r = warp + 8 * i;
+      qr[i] = kr[i] = vr[i] = make_uint2(0, 0);
+      if (r < n) {
+        qr[i] = *reinterpret_cast<const uint2*>(q + (long long)(t0 + r) * qk_stride + h * DK + lane * 4);
+        kr[i] = *reinterpret_cast<const uint2*>(k + (long long)(t0 + r) * qk_stride + h * DK + lane * 4);
+        vr[i] = *reinterpret_cast<const uint2*>(v + (long long)(t0 + r) * v_stride + h * DK + lane * 4);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int r = warp + 8 * i;
+      const float4 qv = load4<__half>(reinterpret_cast<const __half*>(&qr[i]));
+      const float4 kv = load4<__half>(reinterpret_cast<const __half*>(&kr[i]));
+      const float sq = warp_sum(qv.x * qv.x + qv.y * qv.y + qv.z * qv.z + qv.w * qv.w);
+      const float sk = warp_sum(kv.x * kv.x + kv.y * kv.y + kv.z * kv.z + kv.w * kv.w);
+      const float rq = rsqrtf(sq + 1e-6f) * qscale, rk = rsqrtf(sk + 1e-6f);
+      __half2* qd = reinterpret_cast<__half2*>(&sm.q[r * LQK + lane * 4]);
+      __half2* kd = reinterpret_cast<__half2*>(&sm.k[r * LQK + lane * 4]);
+      qd[0] = __floats2half2_rn(qv.x * rq, qv.y * rq);
+      qd[1] = __floats2half2_rn(qv.z * rq, qv.w * rq);
+      kd[0] = __floats2half2_rn(kv.x * rk, kv.y * rk);
+      kd[1] = __floats2half2_rn(kv.z * rk, kv.w * rk);
+      *reinterpret_cast<uint2*>(&sm.v[r * LQK + lane * 4]) = vr[i];
+    }
+  }
+  if (threadIdx.x < CH) {
+    const int r = threadIdx.x;
+    sm.beta[r] = r < n ? beta[(long long)(t0 + r) * H + h] : 0.0f;
+    sm.g[r] = r < n ? gl[(long long)(t0 + r) * H + h] : 0.0f;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const float x0 = sm.g[2 * lane], x1 = sm.g[2 * lane + 1];
+    float s = x0 + x1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float u = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += u;
+    }
+    const float before = s - (x0 + x1);
+    sm.G[2 * lane] = before + x0;
+    sm.G[2 * lane + 1] = s;
+  }
+  __syncthreads();
+  // K^ and Gamma Q^ to the record
+  for (int e = threadIdx.x; e < CH * DK / 8; e += 256) {
+    const int r = e >> 4, c8 = (e & 15) * 8;
+    *reinterpret_cast<uint4*>(&R.k[r * DK + c8]) = *reinterpret_cast<const uint4*>(&sm.k[r * LQK + c8]);
+    const __half2 gi = __float2half2_rn(__expf(sm.G[r]));
+    uint4 qv = *reinterpret_cast<const uint4*>(&sm.q[r * LQK + c8]);
+    __half2* q2 = reinterpret_cast<__half2*>(&qv);
+#pragma unroll
+    for (int j = 0; j < 4; j++) q2[j] = __hmul2(q2[j], gi);
+    *reinterpret_cast<uint4*>(&R.qg[r * DK + c8]) = qv;
+  }
+  if (threadIdx.x < CH) R.dsc[threadIdx.x] = __expf(sm.G[CH - 1] - sm.G[threadIdx.x]);
+  if (threadIdx.x == 0) R.gc = __expf(sm.G[CH - 1]);
+
+  // 2. A and P
+  {
+    const int nb = (warp >> 2) * 32;
+    float kk[4][4], qk[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) kk[i][j] = qk[i][j] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < DK / 16; ks++) {
+      uint32_t ak[4], aq[4];
+      ldsm_x4(a_addr(sm.k, LQK, mt * 16, ks * 16, lane), ak);
+      ldsm_x4(a_addr(sm.q, LQK, mt * 16, ks * 16, lane), aq);
+#pragma unroll
+      for (int j2 = 0; j2 < 2; j2++) {
+        uint32_t bk[4];
+        ldsm_x4(bn_addr(sm.k, LQK, nb + j2 * 16, ks * 16, lane), bk);
+        mma16816(kk[2 * j2], ak, bk[0], bk[1]);
+        mma16816(kk[2 * j2 + 1], ak, bk[2], bk[3]);
+        mma16816(qk[2 * j2], aq, bk[0], bk[1]);
+        mma16816(qk[2 * j2 + 1], aq, bk[2], bk[3]);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const int i = mt * 16 + g8 + (r >> 1) * 8, j = nb + nt * 8 + 2 * tq + (r & 1);
+        const float e = j <= i ? __expf(sm.G[i] - sm.G[j]) : 0.0f;
+        sm.a[i * LA + j] = j < i ? sm.beta[i] * e * kk[nt][r] : 0.0f;
+        R.p[i * CH + j] = __float2half_rn(e * qk[nt][r]);
+      }
+  }
+  __syncthreads();
+  // 3. T = (I + A)^-1 (blocked by 16)
+  if (warp < 4 && lane < 16) {
+    const int o = warp * 16, cc = lane;
+    float xc[16];
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+      float v0 = r == cc ? 1.0f : 0.0f, v1 = 0.0f;
+#pragma unroll
+      for (int j = 0; j < r; j++)
+        if (j >= cc) {
+          if (j & 1) v1 -= sm.a[(o + r) * LA + o + j] * xc[j];
+          else v0 -= sm.a[(o + r) * LA + o + j] * xc[j];
+        }
+      xc[r] = r >= cc ? v0 + v1 : 0.0f;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; r++) sm.x[(o + r) * LA + o + cc] = xc[r];
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int dl = 1; dl < 4; dl++) {
+    const int npair = 4 - dl;
+    for (int e = threadIdx.x; e < npair * 256; e += 256) {
+      const int pr = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      const int bi = dl + pr, bj = pr;
+      float s0 = 0.0f, s1 = 0.0f;
+      for (int m = bj; m < bi; m++)
+#pragma unroll
+        for (int qq = 0; qq < 16; qq += 2) {
+          s0 += sm.a[(bi * 16 + r) * LA + m * 16 + qq] * sm.x[(m * 16 + qq) * LA + bj * 16 + cc];
+          s1 += sm.a[(bi * 16 + r) * LA + m * 16 + qq + 1] * sm.x[(m * 16 + qq + 1) * LA + bj * 16 + cc];
+        }
+      sm.y[pr * 272 + r * 17 + cc] = s0 + s1;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < npair * 256; e += 256) {
+      const int pr = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      const int bi = dl + pr, bj = pr;
+      float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+      for (int qq = 0; qq < 16; qq += 2) {
+        s0 += sm.x[(bi * 16 + r) * LA + bi * 16 + qq] * sm.y[pr * 272 + qq * 17 + cc];
+        s1 += sm.x[(bi * 16 + r) * LA + bi * 16 + qq + 1] * sm.y[pr * 272 + (qq + 1) * 17 + cc];
+      }
+      sm.x[(bi * 16 + r) * LA + bj * 16 + cc] = -(s0 + s1);
+    }
+    __syncthreads();
+  }
+  for (int e = threadIdx.x; e < CH * CH; e += 256) {
+    const int i = e >> 6, j = e & 63;
+    const float t = j <= i ? sm.x[i * LA + j] : 0.0f;
+    const float bj = sm.beta[j];
+    sm.t1[i * L64 + j] = __float2half_rn(t * bj * __expf(sm.G[j]));
+    sm.t2[i * L64 + j] = __float2half_rn(t * bj);
+  }
+  __syncthreads();
+  // 4. W = T1 K^ (f16) and U = T2 V (f32), 64 x 128 each
+  {
+    const int nw = (warp >> 2) * 64;
+    float wacc[8][4], uacc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+      for (int r = 0; r < 4; r++) wacc[i][r] = uacc[i][r] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < CH / 16; ks++) {
+      uint32_t at1[4], at2[4];
+      ldsm_x4(a_addr(sm.t1, L64, mt * 16, ks * 16, lane), at1);
+      ldsm_x4(a_addr(sm.t2, L64, mt * 16, ks * 16, lane), at2);
+#pragma unroll
+      for (int j2 = 0; j2 < 4; j2++) {
+        uint32_t bk[4], bv[4];
+        ldsm_x4_t(bt_addr(sm.k, LQK, ks * 16, nw + j2 * 16, lane), bk);
+        ldsm_x4_t(bt_addr(sm.v, LQK, ks * 16, nw + j2 * 16, lane), bv);
+        mma16816(wacc[2 * j2], at1, bk[0], bk[1]);
+        mma16816(wacc[2 * j2 + 1], at1, bk[2], bk[3]);
+        mma16816(uacc[2 * j2], at2, bv[0], bv[1]);
+        mma16816(uacc[2 * j2 + 1], at2, bv[2], bv[3]);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+      for (int hf = 0; hf < 2; hf++) {
+        const int row = mt * 16 + g8 + hf * 8, col = nw + nt * 8 + 2 * tq;
+        *reinterpret_cast<__half2*>(&R.w[row * DK + col]) = __floats2half2_rn(wacc[nt][2 * hf], wacc[nt][2 * hf + 1]);
+        *reinterpret_cast<float2*>(&R.u[row * DK + col]) = make_float2(uacc[nt][2 * hf], uacc[nt][2 * hf + 1]);
+      }
+  }
+}
+
+template <int DVS>
+struct ScanSmem {
+  static constexpr int LV = DVS + 8;
+  // double-buffered chunk records (the slice of U only)
+  __half k[2][CH * LQK];
+  __half qg[2][CH * LQK];
+  __half w[2][CH * LQK];
+  __half p[2][CH * L64];
+  float u[2][CH * DVS];
+  float dsc[2][CH];
+  float gc[2][4];
+  __half s[DK * LV];
+  __half d[CH * LV];
+  __half ds[CH * LV];
+};
+
+// Phase 2: grid (heads x 128/DVS). Walks the chunks in order; the next chunk's record is prefetched.
+template <int DVS>
+__global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const ChunkRec* __restrict__ rec, int nchunks, int l, int H,
+                                                          float* __restrict__ state, int load_state, float* __restrict__ o) {
+  constexpr int LV = ScanSmem<DVS>::LV;
+  constexpr int NT = DVS / 16;
+  extern __shared__ __align__(16) uint8_t scan_smem_raw[];
+  ScanSmem<DVS>& sm = *reinterpret_cast<ScanSmem<DVS>*>(scan_smem_raw);
+  const int NS = DK / DVS;
+  const int h = blockIdx.x / NS, c0 = (blockIdx.x % NS) * DVS;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g8 = lane >> 2, tq = lane & 3;
+  const int mt = warp & 3, nbase = (warp >> 2) * (DVS / 2);
+  float* stg = state + (long long)h * DK * DK + c0;
+  float* og = o + h * DK + c0;
+  const ChunkRec* rh = rec + (size_t)h * nchunks;
+
+  auto prefetch = [&](int c, int b) {
+    const ChunkRec& R = rh[c];
+    for (int e = threadIdx.x; e < CH * DK / 8; e += 256) {
+      const int r = e >> 4, c8 = (e & 15) * 8;
+      cp_async(&sm.k[b][r * LQK + c8], &R.k[r * DK + c8], 16, 16);
+      cp_async(&sm.qg[b][r * LQK + c8], &R.qg[r * DK + c8], 16, 16);
+      cp_async(&sm.w[b][r * LQK + c8], &R.w[r * DK + c8], 16, 16);
+    }
+    for (int e = threadIdx.x; e < CH * CH / 8; e += 256) {
+      const int r = e >> 3, c8 = (e & 7) * 8;
+      cp_async(&sm.p[b][r * L64 + c8], &R.p[r * CH + c8], 16, 16);
+    }
+    for (int e = threadIdx.x; e < CH * DVS / 4; e += 256) {
+      const int r = e / (DVS / 4), c4 = (e % (DVS / 4)) * 4;
+      cp_async(&sm.u[b][r * DVS + c4], &R.u[r * DK + c0 + c4], 16, 16);
+    }
+    if (threadIdx.x < CH / 4) cp_async(&sm.dsc[b][threadIdx.x * 4], &R.dsc[threadIdx.x * 4], 16, 16);
+    if (threadIdx.x == CH / 4) cp_async(&sm.gc[b][0], &R.gc, 16, 16);
+    cp_async_commit();
+  };
+
+  float sacc[DVS / 8][4];
+#pragma unroll
+  for (int nt = 0; nt < DVS / 8; nt++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
+      sacc[nt][r] = load_state ? stg[row * DK + col] : 0.0f;
+    }
+  auto write_state_f16 = [&]() {
+#pragma unroll
+    for (int nt = 0; nt < DVS / 8; nt++) {
+      const int row = warp * 16 + g8, col = nt * 8 + 2 * tq;
+      *reinterpret_cast<__half2*>(&sm.s[row * LV + col]) = __floats2half2_rn(sacc[nt][0], sacc[nt][1]);
+      *reinterpret_cast<__half2*>(&sm.s[(row + 8) * LV + col]) = __floats2half2_rn(sacc[nt][2], sacc[nt][3]);
+    }
+  };
+  write_state_f16();
+  prefetch(0, 0);
+  for (int c = 0; c < nchunks; c++) {
+    const int b = c & 1;
+    const int t0 = c * CH, n = min(CH, l - t0);
+    cp_async_wait_all();
+    __syncthreads();  // chunk c's record landed; the other buffer is free
+    if (c + 1 < nchunks) prefetch(c + 1, b ^ 1);
+    // delta = U - W S, O = (Gamma Q^) S
+    float dacc[NT][4], oacc[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; i++)
+#pragma unroll
+      for (int r = 0; r < 4; r++) dacc[i][r] = oacc[i][r] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < DK / 16; ks++) {
+      uint32_t aw[4], aq[4];
+      ldsm_x4(a_addr(sm.w[b], LQK, mt * 16, ks * 16, lane), aw);
+      ldsm_x4(a_addr(sm.qg[b], LQK, mt * 16, ks * 16, lane), aq);
+#pragma unroll
+      for (int j2 = 0; j2 < NT / 2; j2++) {
+        uint32_t bs[4];
+        ldsm_x4_t(bt_addr(sm.s, LV, ks * 16, nbase + j2 * 16, lane), bs);
+        mma16816(dacc[2 * j2], aw, bs[0], bs[1]);
+        mma16816(dacc[2 * j2 + 1], aw, bs[2], bs[3]);
+        mma16816(oacc[2 * j2], aq, bs[0], bs[1]);
+        mma16816(oacc[2 * j2 + 1], aq, bs[2], bs[3]);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int hf = 0; hf < 2; hf++) {
+        const int i = mt * 16 + g8 + hf * 8, col = nbase + nt * 8 + 2 * tq;
+        const float2 u = *reinterpret_cast<const float2*>(&sm.u[b][i * DVS + col]);
+        const float d0 = u.x - dacc[nt][2 * hf], d1 = u.y - dacc[nt][2 * hf + 1];
+        const float sc = sm.dsc[b][i];
+        *reinterpret_cast<__half2*>(&sm.d[i * LV + col]) = __floats2half2_rn(d0, d1);
+        *reinterpret_cast<__half2*>(&sm.ds[i * LV + col]) = __floats2half2_rn(d0 * sc, d1 * sc);
+      }
+    __syncthreads();
+    // O += P delta
+#pragma unroll
+    for (int ks = 0; ks < CH / 16; ks++) {
+      uint32_t ap[4];
+      ldsm_x4(a_addr(sm.p[b], L64, mt * 16, ks * 16, lane), ap);
+#pragma unroll
+      for (int j2 = 0; j2 < NT / 2; j2++) {
+        uint32_t bd[4];
+        ldsm_x4_t(bt_addr(sm.d, LV, ks * 16, nbase + j2 * 16, lane), bd);
+        mma16816(oacc[2 * j2], ap, bd[0], bd[1]);
+        mma16816(oacc[2 * j2 + 1], ap, bd[2], bd[3]);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int hf = 0; hf < 2; hf++) {
+        const int i = mt * 16 + g8 + hf * 8, col = nbase + nt * 8 + 2 * tq;
+        if (i < n)
+          *reinterpret_cast<float2*>(og + (long long)(t0 + i) * H * DK + col) = make_float2(oacc[nt][2 * hf], oacc[nt][2 * hf + 1]);
+      }
+    // S = Gamma_C S + K^T (decayed delta)
+    const float gc = sm.gc[b][0];
+#pragma unroll
+    for (int nt = 0; nt < DVS / 8; nt++)
+#pragma unroll
+      for (int r = 0; r < 4; r++) sacc[nt][r] *= gc;
+#pragma unroll
+    for (int ks = 0; ks < CH / 16; ks++) {
+      uint32_t akt[4];
+      ldsm_x4_t(at_addr(sm.k[b], LQK, ks * 16, warp * 16, lane), akt);
+#pragma unroll
+      for (int j2 = 0; j2 < DVS / 16; j2++) {
+        uint32_t bd[4];
+        ldsm_x4_t(bt_addr(sm.ds, LV, ks * 16, j2 * 16, lane), bd);
+        mma16816(sacc[2 * j2], akt, bd[0], bd[1]);
+        mma16816(sacc[2 * j2 + 1], akt, bd[2], bd[3]);
+      }
+    }
+    __syncthreads();  // done with the old f16 state, delta and this chunk's buffers
+    write_state_f16();
+  }
+#pragma unroll
+  for (int nt = 0; nt < DVS / 8; nt++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
+      stg[row * DK + col] = sacc[nt][r];
+    }
+}
+
+size_t gdn_two_phase_scratch(int l, int h) { return (size_t)((l + CH - 1) / CH) * h * sizeof(ChunkRec); }
+
+// One sequence, f16 q/k/v rows: phase 1 over all (chunk, head), then the scan over (head, slice).
+cudaError_t launch_gdn_two_phase(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
+                                 const float* beta, const float* g, float* state, bool load_state, float* o, int l, int h,
+                                 void* scratch, size_t scratch_bytes, cudaStream_t st) {
+  if (l <= 0 || h <= 0 || scratch_bytes < gdn_two_phase_scratch(l, h)) return cudaErrorInvalidValue;
+  constexpr int DVS = 32;
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gdn_scan_kernel<DVS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(ScanSmem<DVS>));
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  const int nchunks = (l + CH - 1) / CH;
+  ChunkRec* rec = reinterpret_cast<ChunkRec*>(scratch);
+  gdn_prep_kernel<<<dim3(nchunks, h), 256, sizeof(PrepSmem), st>>>(q, k, qk_stride, v, v_stride, beta, g, l, h, rec);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  gdn_scan_kernel<DVS><<<h * (DK / DVS), 256, sizeof(ScanSmem<DVS>), st>>>(rec, nchunks, l, h, state, load_state ? 1 : 0, o);
+  return cudaGetLastError();
+}
+
 template <int DVS, typename TIn>
 static cudaError_t launch_chunk(const GdnArgs<TIn>& a, int batch, cudaStream_t st) {
   auto kern = gdn_chunk_kernel<DVS, TIn>;

@@ -65,6 +65,12 @@ cudaError_t launch_gdn_recurrent(const float* q, const float* k, int qk_stride, 
 cudaError_t launch_gdn_chunked(const void* q, const void* k, int qk_stride, const void* v, int v_stride, long long seq_qk,
                                long long seq_v, bool in_f16, const float* beta, const float* g, float* state, bool load_state,
                                float* o, int l, int h, int batch, cudaStream_t st);
+// two-phase chunked scan for one long sequence (f16 rows): all chunks' intra-chunk work in parallel,
+// then the state scan; `scratch` holds gdn_two_phase_scratch(l, h) bytes of per-chunk records
+size_t gdn_two_phase_scratch(int l, int h);
+cudaError_t launch_gdn_two_phase(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
+                                 const float* beta, const float* g, float* state, bool load_state, float* o, int l, int h,
+                                 void* scratch, size_t scratch_bytes, cudaStream_t st);
 cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff, const float* w, int l, int h, __half* out,
                          cudaStream_t st);
 cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,

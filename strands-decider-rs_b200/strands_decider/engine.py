@@ -62,7 +62,10 @@ def lib() -> C.CDLL:
         L.sd_head_free.argtypes = [vp]
         L.sd_head_probs.argtypes = [vp, vp, i32, i32, C.c_double, vp]
         L.sd_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]
-        L.sd_gdn.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, i32, C.c_int64, C.c_int64, i32, i32, vp]
+        L.sd_gdn.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, i32, C.c_int64, C.c_int64, i32, i32, vp,
+                             C.c_size_t, vp]
+        L.sd_gdn_scratch_bytes.restype = C.c_size_t
+        L.sd_gdn_scratch_bytes.argtypes = [i32, i32]
         L.sd_qweight_create.argtypes = [vp, vp, i32, i32, i32, C.POINTER(vp)]
         L.sd_qweight_free.argtypes = [vp]
         L.sd_matmul.argtypes = [vp, vp, i32, vp, i32, i32, vp, C.c_size_t, vp]
@@ -239,11 +242,20 @@ def attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, st
     _check(lib().sd_attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, stream), "sd_attention")
 
 
+GDN_CHUNKED, GDN_SERIAL, GDN_TWO_PHASE = 0, 1, 2
+
+
 def gdn(q, k, qk_stride, v, v_stride, beta, g, state, load_state, o, l, h, batch=1, seq_qk=0, seq_v=0, in_f16=False,
-        serial=False, stream=None):
-    """`sd_gdn`: g is the log decay (decay = exp(g))."""
+        serial=False, algo=None, scratch=None, scratch_bytes=0, stream=None):
+    """`sd_gdn`: g is the log decay (decay = exp(g)); algo 0 chunked, 1 token-serial, 2 two-phase."""
+    if algo is None:
+        algo = GDN_SERIAL if serial else GDN_CHUNKED
     _check(lib().sd_gdn(q, k, qk_stride, v, v_stride, beta, g, state, int(load_state), o, l, h, batch, seq_qk, seq_v,
-                        int(in_f16), int(serial), stream), "sd_gdn")
+                        int(in_f16), int(algo), scratch, scratch_bytes, stream), "sd_gdn")
+
+
+def gdn_scratch_bytes(l: int, h: int) -> int:
+    return int(lib().sd_gdn_scratch_bytes(l, h))
 
 
 class QWeight:

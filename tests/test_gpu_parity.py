@@ -142,6 +142,30 @@ def test_gdn_chunked_matches_oracle(torch, b, l, in_f16, load):
         assert np.abs(got_o[i] - o_want).max() < 3e-2
 
 
+@pytest.mark.parametrize("l,load", [(333, False), (64, True), (65, True), (1000, True)])
+def test_gdn_two_phase_matches_oracle(torch, l, load):
+    """The two-phase scan (all chunks' intra-chunk products in parallel, then the state walk) against
+    the oracle's recurrence, one sequence with f16 inputs: relative error below 5e-3."""
+    from strands_decider.engine import GDN_TWO_PHASE, gdn, gdn_scratch_bytes
+    h = 16
+    q, k, v, beta, g, s0 = _gdn_inputs(np.random.default_rng(l * 3 + load), 1, l, h)
+    q, k, v = (x.astype(np.float16) for x in (q, k, v))
+    qd, kd, vd, bd, gd = (dev(torch, x) for x in (q, k, v, beta, g))
+    sd_ = dev(torch, s0.copy())
+    od = torch.zeros((l, h * 128), dtype=torch.float32, device="cuda")
+    nb = gdn_scratch_bytes(l, h)
+    scratch = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    gdn(qd.data_ptr(), kd.data_ptr(), h * 128, vd.data_ptr(), h * 128, bd.data_ptr(), gd.data_ptr(), sd_.data_ptr(), load,
+        od.data_ptr(), l, h, in_f16=True, algo=GDN_TWO_PHASE, scratch=scratch.data_ptr(), scratch_bytes=nb)
+    torch.cuda.synchronize()
+    o_want, s_want = oracle.gdn(q[0].astype(np.float32), k[0].astype(np.float32), v[0].astype(np.float32), beta[0],
+                                np.exp(g[0]), s0[0] if load else None)
+    got_o, got_s = od.cpu().numpy(), sd_.cpu().numpy()[0]
+    eo = np.linalg.norm(got_o - o_want) / np.linalg.norm(o_want)
+    es = np.linalg.norm(got_s - s_want) / np.linalg.norm(s_want)
+    assert eo < 5e-3 and es < 5e-3, (eo, es)
+
+
 @pytest.fixture(scope="module")
 def engines(small_model):
     from strands_decider.engine import Engine
