@@ -1,9 +1,9 @@
 /* strands-decider B200: the C ABI of the sequence-mixing forward.
  *
  * The drop-in boundary for the reference's torso engine (strands-decider-rs, `src/engine.rs`): a
- * Rust host binds these with `extern "C"` declarations in place of
- * `Engine::load` / `Engine::forward` / `Snapshot`, and the rest of `Decider` (tokenizer, prompt,
- * head, `ask_all`) stays as it is. Plain pointers and sizes only; host buffers unless a name says
+ * Rust host binds these with `extern "C"` declarations in place of `Engine::load` /
+ * `Engine::forward` / `Snapshot`, and the rest of `Decider` (tokenizer, prompt, head, `ask_all`)
+ * stays as it is. Plain pointers and sizes only; host buffers unless a name says
  * `dev`. Every call returns SD_OK or a negative code; the message of the last failure is in
  * sd_engine_last_error(engine) (or sd_last_error() for calls without an engine), as the
  * reference's `Error(String)` (`src/lib.rs:23-44`) carries it. An engine is used by one host thread
@@ -117,6 +117,23 @@ int sd_gdn(const void* q_dev, const void* k_dev, int32_t qk_stride, const void* 
            int32_t h, int32_t batch, int64_t seq_qk, int64_t seq_v, int32_t in_f16, int32_t algo, void* scratch_dev,
            size_t scratch_bytes, void* stream);
 size_t sd_gdn_scratch_bytes(int32_t l, int32_t h);
+
+/* The two-phase scan of sd_gdn (algo 2: one sequence, f16 q/k/v) for callers that must not allocate
+ * device memory while they run, such as a serving process whose GPU memory is all reserved when it
+ * starts, or a latency path that cannot take cudaMalloc's implicit device synchronisation. This entry
+ * point has no counterpart in the reference. It calls no cudaMalloc, cudaFree or other allocating
+ * routine: its per-chunk scratch is one fixed 24 MiB device array inside the library, which every
+ * GPU that loads the library holds until the process exits. Limit: ceil(l / 64) * h chunk records
+ * must fit that array (sd_gdn_noalloc_max_tokens(h) tokens; 1088 for 16 heads); larger calls fail
+ * with SD_ERR_INVALID and say why. The first call on a device looks the array's address up for that
+ * device (make it before any stream capture). All calls on a device share the array, and each call
+ * writes every record it reads, so nothing carries over between calls; two calls whose work
+ * overlaps on the GPU (different streams, no ordering between them) race on it. */
+int sd_gdn_noalloc(const void* q_dev, const void* k_dev, int32_t qk_stride, const void* v_dev, int32_t v_stride,
+                   const void* beta_dev, const void* g_dev, void* state_dev, int32_t load_state, void* o_dev, int32_t l,
+                   int32_t h, void* stream);
+/* The longest sequence sd_gdn_noalloc accepts for h heads. */
+int32_t sd_gdn_noalloc_max_tokens(int32_t h);
 
 /* A block-quantized int4 group-32 symmetric weight (`src/kernels.rs:545-576`) in the GEMM's tile
  * layout, made from the reference layout on the device: q_dev [n][k/32][16 bytes], s_dev [n][k/32] f16.

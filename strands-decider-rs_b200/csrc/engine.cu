@@ -31,10 +31,15 @@ using sd::QWeight;
 struct sd_engine;
 
 namespace {
-
 thread_local std::string g_last_error;
-
 void set_global_error(const std::string& s) { g_last_error = s; }
+}  // namespace
+
+namespace sd {
+void set_last_error(const std::string& s) { set_global_error(s); }
+}  // namespace sd
+
+namespace {
 
 struct LayerW {
   int kind = 0;  // 0 linear_attention, 1 full_attention, 2 adapter

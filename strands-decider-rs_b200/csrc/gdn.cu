@@ -16,6 +16,10 @@
 // slice of DVS value columns of one sequence; the intra-chunk products are recomputed per slice.
 // The state slice lives in registers as the accumulator of its own update (warp w owns key rows
 // 16w..16w+15) with an f16 copy in shared memory as the operand of W S0 and Q^ S0.
+#include <mutex>
+#include <string>
+
+#include "../../include/sd_b200.h"
 #include "common.cuh"
 #include "sd_internal.h"
 
@@ -930,3 +934,71 @@ cudaError_t launch_gdn_chunked(const void* q, const void* k, int qk_stride, cons
 }
 
 }  // namespace sd
+
+// ---------------------------------------------------------------------------------------------
+// The two-phase scan without allocation. Its per-chunk records live in one fixed device array
+// compiled into the library: every GPU that loads the library holds these 24 MiB until the process
+// exits, and every call on a device uses the same array.
+// ---------------------------------------------------------------------------------------------
+namespace sd {
+namespace {
+constexpr size_t kNoAllocScratchBytes = (size_t)24 << 20;
+constexpr int kNoAllocRecords = (int)(kNoAllocScratchBytes / sizeof(ChunkRec));
+static __device__ __align__(256) unsigned char g_gdn_noalloc_scratch[kNoAllocScratchBytes];
+
+// The array's device address on the current device. Host code cannot use the symbol itself (on the
+// host it names a stand-in, not device memory), so the address is looked up once per device, with
+// that device current, and cached.
+cudaError_t noalloc_scratch(void** out) {
+  static void* addr[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> g(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_gdn_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return cudaSuccess;
+}
+}  // namespace
+}  // namespace sd
+
+extern "C" int32_t sd_gdn_noalloc_max_tokens(int32_t h) {
+  if (h <= 0 || h > sd::kNoAllocRecords) return 0;
+  return (sd::kNoAllocRecords / h) * 64;
+}
+
+extern "C" int sd_gdn_noalloc(const void* q, const void* k, int32_t qk_stride, const void* v, int32_t v_stride,
+                              const void* beta, const void* g, void* state, int32_t load_state, void* o, int32_t l,
+                              int32_t h, void* stream) {
+  if (!q || !k || !v || !beta || !g || !state || !o || l <= 0 || h <= 0 || qk_stride % 4 || (size_t)q % 8 ||
+      (size_t)k % 8) {
+    sd::set_last_error("sd_gdn_noalloc: bad arguments");
+    return SD_ERR_INVALID;
+  }
+  const long long records = (long long)((l + 63) / 64) * h;
+  if (records > sd::kNoAllocRecords) {
+    sd::set_last_error("sd_gdn_noalloc: " + std::to_string(h) + " heads x " + std::to_string((l + 63) / 64) +
+                       " chunks of 64 tokens need " + std::to_string(records) + " chunk records; the fixed scratch holds " +
+                       std::to_string(sd::kNoAllocRecords) + " (at most " + std::to_string(sd_gdn_noalloc_max_tokens(h)) +
+                       " tokens for " + std::to_string(h) + " heads)");
+    return SD_ERR_INVALID;
+  }
+  void* scratch = nullptr;
+  cudaError_t e = sd::noalloc_scratch(&scratch);
+  if (e == cudaSuccess)
+    e = sd::launch_gdn_two_phase((const __half*)q, (const __half*)k, qk_stride, (const __half*)v, v_stride,
+                                 (const float*)beta, (const float*)g, (float*)state, load_state != 0, (float*)o, l, h, scratch,
+                                 sd::kNoAllocScratchBytes, (cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    sd::set_last_error(std::string("sd_gdn_noalloc: ") + cudaGetErrorString(e));
+    return SD_ERR_CUDA;
+  }
+  return SD_OK;
+}

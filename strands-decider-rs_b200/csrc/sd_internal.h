@@ -6,10 +6,14 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <string>
 
 namespace sd {
 
 constexpr int kMaxDevices = 64;
+
+// Sets the message sd_last_error() returns on this thread.
+void set_last_error(const std::string& s);
 
 // Error codes a kernel writes to its launch's device error word (the first one sticks).
 enum : int {

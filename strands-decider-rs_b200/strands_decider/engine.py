@@ -64,6 +64,9 @@ def lib() -> C.CDLL:
         L.sd_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]
         L.sd_gdn.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, i32, C.c_int64, C.c_int64, i32, i32, vp,
                              C.c_size_t, vp]
+        L.sd_gdn_noalloc.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, vp]
+        L.sd_gdn_noalloc_max_tokens.restype = i32
+        L.sd_gdn_noalloc_max_tokens.argtypes = [i32]
         L.sd_gdn_scratch_bytes.restype = C.c_size_t
         L.sd_gdn_scratch_bytes.argtypes = [i32, i32]
         L.sd_qweight_create.argtypes = [vp, vp, i32, i32, i32, C.POINTER(vp)]
@@ -256,6 +259,16 @@ def gdn(q, k, qk_stride, v, v_stride, beta, g, state, load_state, o, l, h, batch
 
 def gdn_scratch_bytes(l: int, h: int) -> int:
     return int(lib().sd_gdn_scratch_bytes(l, h))
+
+
+def gdn_noalloc(q, k, qk_stride, v, v_stride, beta, g, state, load_state, o, l, h, stream=None):
+    """`sd_gdn_noalloc`: the two-phase scan on the library's fixed scratch array (no allocation)."""
+    _check(lib().sd_gdn_noalloc(q, k, qk_stride, v, v_stride, beta, g, state, int(load_state), o, l, h, stream),
+           "sd_gdn_noalloc")
+
+
+def gdn_noalloc_max_tokens(h: int) -> int:
+    return int(lib().sd_gdn_noalloc_max_tokens(h))
 
 
 class QWeight:
