@@ -345,7 +345,10 @@ def run_ours(args, world, rank, local):
                 "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward (host ids in, host hidden rows out) + sd_head_probs"},
         "gpu_launches": int(launches),
         "roofline": {"kernel": "gemm_q4_tc (dequantizing tcgen05 GEMM)", "bound": "tensor", "achieved": gemm_tflops,
-                     "peak": tf_sus, "unit": "TFLOP/s", "frac": gemm_tflops / tf_sus, "traffic": None,
+                     "peak": tf_sus, "unit": "TFLOP/s", "frac": gemm_tflops / tf_sus,
+                     # dram read+write of one gate_up launch at m=2048 from an ncu capture of
+                     # `bench.py --workload gemm --m 2048 --n 12288` (algorithmic: 22.6 MB read)
+                     "traffic": 22.64e6, "traffic_launch": "gate_up m=2048 n=12288 k=2048",
                      "peak_source": f"{src} bf16 sustained (kernel timed inside a long step)",
                      "share_of_device_time": g["ms"] / max(1e-9, sum(v["ms"] for v in prof.values()))},
         "kernels": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
@@ -364,6 +367,91 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_kernel_workload(args):
+    """Isolated kernel workloads (not the headline; used for kernel rooflines and ncu captures):
+    attention = config 2 (B=4, S=2048, causal GQA 8/2 heads x 256, gated), gdn = config 3 (B=16,
+    L=1024, 16 heads of 128x128, f16 q/k/v, beta = sigmoid(N(0,1)), g = -softplus(N(0,1))), gemm = one
+    dequantizing matmul shape. Inputs are seeded synthetic tensors with the configs' shapes."""
+    import torch
+    from strands_decider import model as M
+    from strands_decider.engine import QWeight, attention, gdn
+    torch.cuda.set_device(0)
+    hbm, tf_burst, tf_sus, src = peaks()
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    if args.workload == "attention":
+        B, S, hq, hk, hd = 4, 2048, 8, 2, 256
+        q = torch.randn(B, hq, S, hd, generator=g, device="cuda").half()
+        k = torch.randn(B, hk, S, hd, generator=g, device="cuda").half()
+        v = torch.randn(B, hk, S, hd, generator=g, device="cuda").half()
+        gate = torch.randn(B, S, hq * 2 * hd, generator=g, device="cuda").half()
+        o = torch.empty(B, S, hq * hd, device="cuda").half()
+
+        def fn():
+            for b in range(B):
+                attention(q[b].data_ptr(), k[b].data_ptr(), v[b].data_ptr(), gate[b].data_ptr(), hq * 2 * hd, hd, 2 * hd,
+                          o[b].data_ptr(), S, 0, S, hq, hk, hd)
+        ms = timed(fn, args.steps, args.warmup)
+        work = 4.0 * hd * hq * B * S * (S + 1) / 2
+        line = {"metric": "attention TFLOP/s (config 2)", "value": work / ms / 1e9, "unit": "TFLOP/s", "ms_per_step": ms,
+                "roofline": {"bound": "tensor", "achieved": work / ms / 1e9, "peak": tf_burst, "unit": "TFLOP/s",
+                             "frac": work / ms / 1e9 / tf_burst, "peak_source": f"{src} bf16 burst"},
+                "config": {"workload": "config 2: B=4 S=2048 HQ=8 HK=2 HD=256 causal, gated", "flops_per_step": work}}
+    elif args.workload == "gdn":
+        B, L, H = 16, 1024, 16
+        x = torch.randn(B, L, 3, H * 128, generator=g, device="cuda").half()
+        beta = torch.sigmoid(torch.randn(B, L, H, generator=g, device="cuda"))
+        gl = -torch.nn.functional.softplus(torch.randn(B, L, H, generator=g, device="cuda"))
+        st = torch.zeros(B, H, 128, 128, device="cuda")
+        o = torch.empty(B, L, H * 128, device="cuda")
+        qp = x.data_ptr()
+
+        def fn():
+            gdn(qp, qp + H * 128 * 2, 3 * H * 128, qp + 2 * H * 128 * 2, 3 * H * 128, beta.data_ptr(), gl.data_ptr(),
+                st.data_ptr(), 0, o.data_ptr(), L, H, batch=B, seq_qk=L * 3 * H * 128, seq_v=L * 3 * H * 128, in_f16=True)
+        ms = timed(fn, args.steps, args.warmup)
+        byts = B * L * H * (3 * 128 * 2 + 8 + 128 * 4) + B * H * 128 * 128 * 4
+        line = {"metric": "gated delta rule GB/s (config 3)", "value": byts / ms / 1e6, "unit": "GB/s", "ms_per_step": ms,
+                "roofline": {"bound": "hbm", "achieved": byts / ms / 1e6, "peak": hbm, "unit": "GB/s",
+                             "frac": byts / ms / 1e6 / hbm, "peak_source": f"{src} HBM copy"},
+                "config": {"workload": "config 3: B=16 L=1024 H=16 DK=DV=128, f16 q/k/v, chunked scan", "bytes_per_step": byts}}
+    else:
+        m, n, k = args.m, args.n, args.k
+        rng = np.random.default_rng(args.seed)
+        silu = n == 12288
+        packed, scales = M._quant_tensor(rng, n, k, 4, 1.0 / np.sqrt(k))
+        qd = torch.from_numpy(packed).cuda()
+        sd = torch.from_numpy(scales.view(np.uint16)).cuda()
+        w = QWeight(qd.data_ptr(), sd.data_ptr(), n, k, interleave=silu)
+        a = torch.randn(m, k, generator=g, device="cuda").half()
+        y = torch.empty(m, n, device="cuda").half()
+        ws = torch.empty(16 << 20, dtype=torch.float32, device="cuda")
+
+        def fn():
+            w.matmul(a.data_ptr(), m, y.data_ptr(), n // 2 if silu else n, silu=silu, ws_dev=ws.data_ptr(), ws_bytes=ws.numel() * 4)
+        ms = timed(fn, args.steps, args.warmup)
+        fl = 2.0 * m * n * k
+        line = {"metric": "dequantizing GEMM TFLOP/s", "value": fl / ms / 1e9, "unit": "TFLOP/s", "ms_per_step": ms,
+                "roofline": {"bound": "tensor" if m > 71 else "hbm", "achieved": fl / ms / 1e9, "peak": tf_burst,
+                             "unit": "TFLOP/s", "frac": fl / ms / 1e9 / tf_burst, "peak_source": f"{src} bf16 burst"},
+                "config": {"workload": f"gemm m={m} n={n} k={k}" + (" (SwiGLU epilogue)" if silu else ""),
+                           "weight_gbs": n * k * 0.5625 / ms / 1e6}}
+    line.update({"steps": args.steps, "warmup": args.warmup, "n_gpus": 1, "data": "synthetic", "dtype": "f16"})
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -373,9 +461,17 @@ def main():
     ap.add_argument("--requests-per-step", type=int, default=8)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["sweep", "attention", "gdn", "gemm"], default="sweep",
+                    help="sweep: the headline; the others: isolated kernels (config 2, config 3, one GEMM shape)")
+    ap.add_argument("--m", type=int, default=2048)
+    ap.add_argument("--n", type=int, default=12288)
+    ap.add_argument("--k", type=int, default=2048)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload != "sweep":
+        run_kernel_workload(args)
+        return
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":
