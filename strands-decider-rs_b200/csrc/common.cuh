@@ -51,20 +51,43 @@ SD_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with parity `parity` to complete. Gives up after kWaitLimitNs, or at once when
-// another thread of the CTA has already given up (*abort set): records `code` in *err and returns
-// false.
+// Waits for the phase with parity `parity` to complete. Gives up after kWaitLimitNs, or soon after
+// another thread of the CTA has given up (*abort set): records `code` in *err and returns false. The
+// clock and the abort flag are read every 32 polls, and long waits back off, so waiting threads
+// take little of the shared-memory bandwidth the tensor core reads its operands through.
 SD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  unsigned long long t0 = global_ns();
-  while (true) {
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; i++) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (global_ns() - t0 > kWaitLimitNs) {
-      *abort = 1;
-      atomicCAS(err, 0, code);
-      return false;
+    if ((i & 31) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        atomicCAS(err, 0, code);
+        return false;
+      }
+      if (i >= 256) __nanosleep(64);
     }
+  }
+}
+
+// mbar_wait for a whole warp: every lane polls (one try_wait instruction for the warp), so each
+// lane has the barrier's acquire ordering. The lanes leave together: a lane that gave up (timeout or
+// abort) makes the whole warp give up.
+SD_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+  const bool ok = mbar_wait(bar, parity, abort, err, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Waits (bounded, ignoring the abort flag) for a phase that asynchronous copies or MMAs this CTA
+// issued will complete, before the CTA exits: used on the way out, after an abort too, so that no
+// copy lands in shared memory and no MMA writes TMEM after the CTA has released them.
+SD_DEV void mbar_drain(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) return;
   }
 }
 
@@ -117,6 +140,32 @@ SD_DEV void tc_commit(uint64_t* bar) {
                : "memory");
 }
 SD_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+SD_DEV void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: A (M rows = TMEM lanes, K packed two f16 per
+// 32-bit column) read from tensor memory.
+SD_DEV void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns from registers: thread i of the warp writes lane
+// (base lane + i). Asynchronous: tc_wait_st before the data is signalled to another thread.
+SD_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
 
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane (base lane + i).
 SD_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {

@@ -1092,6 +1092,14 @@ int sd_matmul(const sd_qweight* w, const void* act, int32_t m, void* y, int32_t 
     set_global_error("sd_matmul: bad arguments");
     return SD_ERR_INVALID;
   }
+  // the epilogue stores 16-byte vectors: 16-byte aligned buffers, rows of whole vectors
+  const int nout = silu ? w->w.n / 2 : w->w.n;
+  if (ldy < nout || ldy % 8 || w->w.n % 8 || (silu && w->w.n % 32) || ((uintptr_t)act | (uintptr_t)y) % 16 ||
+      (uintptr_t)ws % 16) {
+    set_global_error("sd_matmul: ldy must be >= the output width and a multiple of 8, n a multiple of 8 (32 with "
+                     "silu), and act, y and ws 16-byte aligned");
+    return SD_ERR_INVALID;
+  }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -2,11 +2,26 @@
 // stored as the reference's int4 group-32 symmetric blocks (src/kernels.rs:545-576, `matmul_tiled`
 // at src/kernels.rs:640-709 and `matmul_coop` at :716-804 are the kernels it replaces).
 //
-// Roles (6 warps): warp 0 issues the TMA load of each activation tile and the bulk copy of each
-// packed weight tile; warp 1 owns the TMEM accumulator and issues tcgen05.mma; warps 2-5 dequantize
-// the packed weight tile into a 128-byte-swizzled f16 tile (the MMA's A operand), then run the
-// epilogue out of TMEM. The weights are the MMA's M side (128 rows per tile) and the tokens its N
-// side (BN columns), so one dequantized tile serves up to 256 tokens.
+// The weights are the MMA's M side (128 rows per tile) and the tokens its N side (BN columns, up to
+// 192), so one dequantized weight tile serves up to 192 tokens. The dequantized weights never touch
+// shared memory: they go from registers into tensor memory, which tcgen05.mma reads its A operand
+// from; only the activations (the B operand) are staged in shared memory. Persistent and
+// warp-specialised:
+//   raw producer  bulk-copies the packed weight k-tiles of each stage (codes + scales, 4608 bytes a
+//                 k-tile, contiguous in the tile layout) into the raw ring, one copy and one barrier;
+//   act producer  TMA-loads the activation k-tiles of a stage (BN x 64 f16 each, 128-byte swizzle);
+//   dequantizers  NG groups of four warps, taking stages in turn: each thread reads one weight row of
+//                 each k-tile of the stage from the raw ring (freeing the slot once read), dequantizes
+//                 its 64 values and stores them into its TMEM lane (32 columns of f16 pairs);
+//   MMA issuer    one thread: tcgen05.mma (M 128, N BN, K 16, A from TMEM, B from shared memory)
+//                 into a TMEM accumulator;
+//   epilogue      four warps read the accumulator out of TMEM (each its 32-lane quarter), transpose it
+//                 through shared memory and store f16 token rows (or the SwiGLU of gate/up row pairs,
+//                 or f32 split-K partials).
+// A stage holds KS k-tiles of both operands behind one barrier (the act producer's byte count plus one
+// arrival per dequantizing warp) and is released by one tcgen05.commit, so the MMA thread waits once
+// and commits once per 4 KS MMAs. The raw ring runs ahead on its own barriers. TMEM holds two
+// accumulators (one tile's epilogue overlaps the next tile's main loop) and the A ring.
 //
 // Numerics: the dequantized weight is (q - 8) * scale rounded to f16, as the reference's tiled
 // kernel computes it (src/kernels.rs:671); products accumulate in f32; the output is rounded to f16.
@@ -24,27 +39,46 @@ constexpr int kBK = 64;
 constexpr int kTileCodes = kBM * kBK / 2;          // 4096 bytes of int4 codes
 constexpr int kTileScales = kBM * (kBK / 32) * 2;  // 512 bytes of f16 scales
 constexpr int kTileBytes = kTileCodes + kTileScales;
+constexpr int kHalfCodes = kTileCodes / 2;  // codes of k-group 0 of every row, then of k-group 1
+constexpr int kACols = kBK / 2;             // TMEM columns of one dequantized k-tile (f16 pairs)
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 5 : (BN >= 64 ? 7 : 8));
+  // k-tiles per stage, stages, dequantization groups (no more than stages), raw ring slots of one
+  // stage's packed weights each (deeper for short prompts, whose weights stream from HBM once)
+  static constexpr int KS = BN >= 192 ? 1 : 2;
+  static constexpr int S = BN >= 64 ? 4 : 6;
+  static constexpr int NG = 4;
+  static constexpr int SR = BN >= 192 ? 16 : (BN >= 128 ? 8 : 12);
+  static constexpr int kRawSlot = KS * kTileBytes;
+  static constexpr int kWarps = 2 + 4 * NG + 4 + 1;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kWarpAct = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 2 + 4 * NG, kWarpRaw = kWarpEpi0 + 4;
   static constexpr int kAccCols = BN < 32 ? 32 : BN;  // one accumulator buffer
-  static constexpr int kTmemCols = 2 * kAccCols;      // double-buffered: epilogue overlaps the next tile
-  static constexpr size_t kA = (size_t)kBM * kBK * 2;
-  static constexpr size_t kB = (size_t)BN * kBK * 2;
-  static constexpr size_t kOffB = kStages * kA;
-  static constexpr size_t kOffRaw = kOffB + kStages * kB;
-  static constexpr size_t kOffStage = kOffRaw + (size_t)kStages * kTileBytes;
-  static constexpr int kStageBytesPerWarp = 32 * 40 * 2;  // 32 x 32 f16 (row stride 40) or 16 x 32 f32 (row stride 36)
-  static constexpr size_t kOffBar = kOffStage + 4 * kStageBytesPerWarp;
-  static constexpr size_t kBytes = kOffBar + (3 * kStages + 4) * 8 + 16;
+  static constexpr int kACol0 = 2 * kAccCols;         // the A ring follows the two accumulators
+  static constexpr int kTmemUsed = kACol0 + S * KS * kACols;
+  static constexpr int kTmemCols = kTmemUsed <= 256 ? 256 : 512;
+  static constexpr size_t kB = (size_t)BN * kBK * 2;  // one k-tile of activations, f16
+  static constexpr size_t kStage = KS * kB;
+  static constexpr size_t kOffRaw = S * kStage;
+  static constexpr size_t kOffStg = kOffRaw + (size_t)SR * kRawSlot;
+  static constexpr int kStgBytesPerWarp = 32 * 40 * 2;  // 32 x 32 f16 (row stride 40) or 16 x 32 f32 (row stride 36)
+  static constexpr size_t kOffBar = kOffStg + 4 * kStgBytesPerWarp;
+  static constexpr int kBars = 2 * SR + 2 * S + 4 + 1;
+  static constexpr size_t kBytes = kOffBar + kBars * 8 + 16;
   static constexpr size_t kSmem = kBytes + 1024;  // room to align the base to 1024 bytes
   static_assert(kSmem <= 232448, "shared memory per CTA");
+  static_assert(kTmemUsed <= 512, "tensor memory columns");
+  static_assert(kThreads <= 1024, "threads per CTA");
+  static_assert(BN % 32 == 0 && BN <= 256, "the epilogue reads 32 token columns at a time");
+  static_assert(S >= 2 && NG <= S, "stage ring: a group waits for the stage NG before its own");
+  // A raw ring slot is reused every SR stages; the groups take stages in turn, so this keeps every use
+  // of a slot with one group. Otherwise a group could poll a slot whose previous use (another group's
+  // stage) has not landed yet and take that older phase, of the same parity, for its own.
+  static_assert(SR % NG == 0, "raw ring: each slot belongs to one group");
 };
 
 enum Epi { kEpiStore = 0, kEpiSilu = 1, kEpiPartial = 2 };
-
-constexpr int kGemmThreads = 448;  // 14 warps: producer, MMA, 8 dequant, 4 epilogue
 
 struct TileGrid {
   int ntiles, mtiles, splits, kps, KT;
@@ -60,46 +94,50 @@ struct TileGrid {
   }
 };
 
-// Persistent, warp-specialised: each CTA walks tiles blockIdx.x, +gridDim.x, ...; the smem ring runs
-// across tile boundaries and the accumulator is double-buffered in TMEM, so one tile's epilogue
-// overlaps the next tile's loads, dequantization and MMAs.
+// Persistent: each CTA walks tiles blockIdx.x, +gridDim.x, ...; the rings run across tile boundaries.
+// Every role walks the same sequence: tiles with work, their stages (KS k-tiles each, the last one of a
+// tile possibly fewer) and k-tiles, so stage and k-tile counters agree between roles.
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     gemm_q4_tc(const __grid_constant__ CUtensorMap act_map, const uint8_t* __restrict__ wt, int M, int N, TileGrid tg,
                __half* __restrict__ y, int ldy, float* __restrict__ ws, int* err) {
   using Cfg = GemmCfg<BN>;
-  constexpr int S = Cfg::kStages;
+  constexpr int KS = Cfg::KS, S = Cfg::S, SR = Cfg::SR, NG = Cfg::NG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sa = base;
-  uint8_t* sb = base + Cfg::kOffB;
   uint8_t* sraw = base + Cfg::kOffRaw;
-  uint8_t* sstage = base + Cfg::kOffStage;
-  uint64_t* full_raw = reinterpret_cast<uint64_t*>(base + Cfg::kOffBar);
-  uint64_t* full_a = full_raw + S;
-  uint64_t* empty = full_a + S;
-  uint64_t* acc_full = empty + S;  // [2]
+  uint8_t* sstg = base + Cfg::kOffStg;
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(base + Cfg::kOffBar);
+  uint64_t* raw_empty = raw_full + SR;
+  uint64_t* full = raw_empty + SR;     // [S] operands of a stage landed / written
+  uint64_t* empty = full + S;          // [S] the stage's MMAs completed
+  uint64_t* acc_full = empty + S;      // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* mma_done = acc_empty + 2;  // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntile_total = tg.count();
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < SR; s++) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 4);  // the four warps of a dequantization group
+    }
     for (int s = 0; s < S; s++) {
-      mbar_init(&full_raw[s], 1);
-      mbar_init(&full_a[s], 256);
+      mbar_init(&full[s], 4 + 1);  // a dequantization group's warps + the act producer's byte count
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 4);  // the four epilogue warps
     }
+    mbar_init(mma_done, 1);
     *abort = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == Cfg::kWarpMma) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -109,103 +147,145 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int KT = tg.KT;
 
-  if (warp == 0) {
-    // producer: activation tile by TMA, packed weight tile by bulk copy, one stage per k-tile
+  if (warp == Cfg::kWarpRaw) {
+    // one thread: the packed weight k-tiles of every stage, one copy per stage into the raw ring
     if (lane == 0) {
-      prefetch_tmap(&act_map);
-      int it = 0;
+      int si = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < ntile_total && ok; t += gridDim.x) {
         int nt, mt, sp, kt0, nk;
         tg.decode(t, nt, mt, sp, kt0, nk);
         const uint8_t* wtile = wt + (size_t)nt * KT * kTileBytes;
-        for (int i = 0; i < nk; i++, it++) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1;
-          if (it >= S && !mbar_wait(&empty[s], ph ^ 1, abort, err, kErrTimeoutEmpty)) {
+        for (int i = 0; i < nk; i += KS, si++) {
+          const int rs = si % SR, kc = min(KS, nk - i);
+          if (si >= SR && !mbar_wait(&raw_empty[rs], ((si / SR) & 1) ^ 1, abort, err, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_raw[s], (uint32_t)(Cfg::kB + kTileBytes));
-          tma_load_2d(sb + s * Cfg::kB, &act_map, &full_raw[s], (kt0 + i) * kBK, mt * BN);
-          bulk_load(sraw + s * kTileBytes, wtile + (size_t)(kt0 + i) * kTileBytes, kTileBytes, &full_raw[s]);
+          mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)(kc * kTileBytes));
+          bulk_load(sraw + rs * Cfg::kRawSlot, wtile + (size_t)(kt0 + i) * kTileBytes, kc * kTileBytes, &raw_full[rs]);
         }
       }
+      for (int j = max(0, si - SR); j < si; j++) mbar_drain(&raw_full[j % SR], (j / SR) & 1);
     }
-  } else if (warp == 1) {
-    // MMA issuer: accumulator buffer (local tile index & 1)
+  } else if (warp == Cfg::kWarpAct) {
+    // one thread: the activation k-tiles of each stage, one barrier per stage
+    if (lane == 0) {
+      prefetch_tmap(&act_map);
+      int si = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntile_total && ok; t += gridDim.x) {
+        int nt, mt, sp, kt0, nk;
+        tg.decode(t, nt, mt, sp, kt0, nk);
+        for (int i = 0; i < nk; i += KS, si++) {
+          const int s = si % S, kc = min(KS, nk - i);
+          if (si >= S && !mbar_wait(&empty[s], ((si / S) & 1) ^ 1, abort, err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sb = base + s * Cfg::kStage;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(kc * Cfg::kB));
+          for (int j = 0; j < kc; j++) tma_load_2d(sb + j * Cfg::kB, &act_map, &full[s], (kt0 + i + j) * kBK, mt * BN);
+        }
+      }
+      for (int j = max(0, si - S); j < si; j++) mbar_drain(&full[j % S], (j / S) & 1);
+    }
+  } else if (warp == Cfg::kWarpMma) {
+    // one thread: one wait and one commit per stage; accumulator buffer = local tile index & 1
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(kBM, BN);
-      int it = 0, lt = -1;
+      int si = 0, lt = -1;
       bool ok = true;
       for (int t = blockIdx.x; t < ntile_total && ok; t += gridDim.x) {
         int nt, mt, sp, kt0, nk;
         tg.decode(t, nt, mt, sp, kt0, nk);
         if (nk == 0) continue;
-        lt++;  // tiles with work, in order: the accumulator buffer is lt & 1
+        lt++;  // tiles with work, in order
         const int buf = lt & 1;
         if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) & 1) ^ 1, abort, err, kErrTimeoutEmpty)) break;
         tc_fence_after();
         const uint32_t acc = tmem + buf * Cfg::kAccCols;
-        for (int i = 0; i < nk; i++, it++) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1;
-          if (!mbar_wait(&full_a[s], ph, abort, err, kErrTimeoutFull)) {
+        for (int i = 0; i < nk; i += KS, si++) {
+          const int s = si % S, kc = min(KS, nk - i);
+          if (!mbar_wait(&full[s], (si / S) & 1, abort, err, kErrTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t ad = sw128_desc(sa + s * Cfg::kA);
-          const uint64_t bd = sw128_desc(sb + s * Cfg::kB);
+          const uint8_t* sb = base + s * Cfg::kStage;
+          const uint32_t a0 = tmem + Cfg::kACol0 + s * KS * kACols;
+          for (int j = 0; j < kc; j++) {
+            const uint64_t bd = sw128_desc(sb + j * Cfg::kB);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; kk++)  // 16 f16 = 32 bytes per step: +2 in the address field
-            tc_mma_f16(acc, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0);
+            for (int kk = 0; kk < kBK / 16; kk++)  // K 16 per MMA: 8 TMEM columns of A, +32 bytes (+2) of B
+              tc_mma_f16_ts(acc, a0 + j * kACols + kk * 8, bd + 2 * kk, idesc, (i | j | kk) != 0);
+          }
           tc_commit(&empty[s]);
         }
+        if (!ok) break;
         tc_commit(&acc_full[buf]);
       }
+      // every MMA issued has completed before TMEM is released
+      tc_commit(mma_done);
+      mbar_drain(mma_done, 0);
     }
-  } else if (warp < 10) {
-    // dequantization: 256 threads, thread pair (r, r + 128) splits row r's 8 chunks 4 + 4
-    const int tid = threadIdx.x - 64;
-    const int r = tid & 127, half = tid >> 7;
-    int it = 0;
+  } else if (warp < Cfg::kWarpEpi0) {
+    // dequantization: group g takes the stages with si % NG == g; thread i of warp w owns weight row
+    // (w % 4) * 32 + i, the TMEM lane this warp may write
+    const int g = (warp - Cfg::kWarpDq0) >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16) + Cfg::kACol0;
+    int si = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntile_total && ok; t += gridDim.x) {
       int nt, mt, sp, kt0, nk;
       tg.decode(t, nt, mt, sp, kt0, nk);
-      for (int i = 0; i < nk; i++, it++) {
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1;
-        if (!mbar_wait(&full_raw[s], ph, abort, err, kErrTimeoutFull)) {
+      for (int i = 0; i < nk && ok; i += KS, si++) {
+        if (si % NG != g) continue;
+        const int s = si % S, rs = si % SR, kc = min(KS, nk - i);
+        if (!mbar_wait_warp(&raw_full[rs], (si / SR) & 1, abort, err, kErrTimeoutFull)) {
           ok = false;
           break;
         }
-        const uint8_t* raw = sraw + s * kTileBytes;
-        const uint4 c = *reinterpret_cast<const uint4*>(raw + r * 32 + half * 16);
-        const __half sc = reinterpret_cast<const __half*>(raw + kTileCodes)[r * 2 + half];
-        const __half2 sc2 = __half2half2(sc);
-        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-        uint8_t* arow = sa + s * Cfg::kA + r * 128;
+        for (int j = 0; j < kc; j++) {
+          const uint8_t* raw = sraw + rs * Cfg::kRawSlot + j * kTileBytes;
+          const uint4 c0 = *reinterpret_cast<const uint4*>(raw + r * 16);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(raw + kHalfCodes + r * 16);
+          const __half2 sc = *reinterpret_cast<const __half2*>(raw + kTileCodes + r * 4);
+          const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          uint32_t v[32];  // column c: elements (2c, 2c + 1) of this row's 64
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const int ch = half * 4 + j;
-          uint4 o;
-          o.x = h2_as_u32(dq_pair(w[j], 0, sc2));
-          o.y = h2_as_u32(dq_pair(w[j], 1, sc2));
-          o.z = h2_as_u32(dq_pair(w[j], 2, sc2));
-          o.w = h2_as_u32(dq_pair(w[j], 3, sc2));
-          *reinterpret_cast<uint4*>(arow + ((ch ^ (r & 7)) << 4)) = o;
+          for (int ch = 0; ch < 8; ch++) {
+            const __half2 sc2 = ch < 4 ? __low2half2(sc) : __high2half2(sc);
+#pragma unroll
+            for (int e = 0; e < 4; e++) v[ch * 4 + e] = h2_as_u32(dq_pair(w[ch], e, sc2));
+          }
+          if (j == kc - 1) {
+            // the stage's codes are in registers (the results depend on them): refill the raw slot
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rs]);
+          }
+          if (j == 0 && si >= S) {
+            if (!mbar_wait_warp(&empty[s], ((si / S) & 1) ^ 1, abort, err, kErrTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();  // the MMAs that read this slot are complete
+          }
+          tmem_st32(lane_base + (s * KS + j) * kACols, v);
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&full_a[s]);
+        if (!ok) break;
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
       }
     }
-  } else {
+  } else if (warp < Cfg::kWarpRaw) {
     // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (weight rows of the tile), transposes
     // through shared memory and stores token rows with 16-byte stores
     const int q = warp & 3;
-    uint8_t* stg = sstage + (warp - 10) * Cfg::kStageBytesPerWarp;
+    uint8_t* stg = sstg + (warp - Cfg::kWarpEpi0) * Cfg::kStgBytesPerWarp;
     int lt = -1;
     for (int t = blockIdx.x; t < ntile_total; t += gridDim.x) {
       int nt, mt, sp, kt0, nk;
@@ -213,7 +293,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (nk == 0) continue;
       lt++;
       const int buf = lt & 1;
-      if (!mbar_wait(&acc_full[buf], (lt >> 1) & 1, abort, err, kErrTimeoutAccum)) break;
+      if (!mbar_wait_warp(&acc_full[buf], (lt >> 1) & 1, abort, err, kErrTimeoutAccum)) break;
       tc_fence_after();
       const uint32_t acc = tmem + buf * Cfg::kAccCols + ((uint32_t)(q * 32) << 16);
       const int n0 = nt * kBM + q * 32;  // first weight row of this warp
@@ -242,12 +322,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
             }
           } else {
-            // rows interleaved as (gate j, up j): even lanes hold gate, odd lanes up
+            // rows interleaved as (gate j, up j): even lanes hold gate, odd lanes up. For the token
+            // pair (2p, 2p+1) the even lane computes token 2p and the odd lane token 2p+1, after one
+            // exchange: the even lane sends its gate of token 2p+1, the odd lane its up of token 2p.
+            const int odd = lane & 1;
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-              const float g = __half2float(__float2half_rn(__uint_as_float(v[j])));
-              const float u = __shfl_xor_sync(0xffffffffu, g, 1);
-              if ((lane & 1) == 0) st[j * 40 + (lane >> 1)] = __float2half_rn(g / (1.0f + __expf(-g)) * u);
+            for (int p = 0; p < 16; p++) {
+              const float a0 = __half2float(__float2half_rn(__uint_as_float(v[2 * p])));
+              const float a1 = __half2float(__float2half_rn(__uint_as_float(v[2 * p + 1])));
+              const float other = __shfl_xor_sync(0xffffffffu, odd ? a0 : a1, 1);
+              const float g = odd ? other : a0;
+              const float u = odd ? a1 : other;
+              st[(2 * p + odd) * 40 + (lane >> 1)] = __float2half_rn(__fdividef(g, 1.0f + __expf(-g)) * u);
             }
             __syncwarp();
             const int m = mbase + lane;
@@ -288,12 +374,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == Cfg::kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
@@ -319,14 +406,15 @@ __global__ void gemm_finish(const float* __restrict__ ws, int splits, int M, int
       }
       const float g = __half2float(__float2half_rn(gs));
       const float u = __half2float(__float2half_rn(us));
-      y[m * ldy + j] = __float2half_rn(g / (1.0f + __expf(-g)) * u);
+      y[m * ldy + j] = __float2half_rn(__fdividef(g, 1.0f + __expf(-g)) * u);
     }
   }
 }
 
 // Reference layout (n rows of k/32 blocks of 16 bytes; scales [n][k/32]) -> tile layout
-// [npad/128][k/64][4096 code bytes + 512 scale bytes], with the nibbles of each 8-element word
-// reordered to (even elements low half, odd elements high half). `interleave` maps output row 2j
+// [npad/128][k/64][2048 code bytes of k-group 0 (16 per row) + 2048 of k-group 1 + 512 scale bytes
+// (2 per row)], so that 32 consecutive rows read by a warp are contiguous, with the nibbles of each
+// 8-element word reordered to (even elements low half, odd elements high half). `interleave` maps output row 2j
 // to source row j and 2j+1 to source row n/2 + j (gate_up: gate j next to up j).
 __global__ void repack_q4(const uint8_t* __restrict__ q, const __half* __restrict__ s, int n, int k, int npad, int interleave,
                           uint8_t* __restrict__ out) {
@@ -337,10 +425,11 @@ __global__ void repack_q4(const uint8_t* __restrict__ q, const __half* __restric
     int src = row;
     if (interleave) src = (row & 1) ? (n / 2 + (row >> 1)) : (row >> 1);
     uint8_t* tile = out + ((size_t)(row / kBM) * KT + kt) * kTileBytes;
-    uint32_t* dst = reinterpret_cast<uint32_t*>(tile + (row % kBM) * 32);
+    uint32_t* dst0 = reinterpret_cast<uint32_t*>(tile + (row % kBM) * 16);               // k-group 0
+    uint32_t* dst1 = reinterpret_cast<uint32_t*>(tile + kHalfCodes + (row % kBM) * 16);  // k-group 1
     __half* dsc = reinterpret_cast<__half*>(tile + kTileCodes) + (row % kBM) * 2;
     if (row >= n) {
-      for (int i = 0; i < 8; i++) dst[i] = 0;
+      for (int i = 0; i < 4; i++) dst0[i] = dst1[i] = 0;
       dsc[0] = dsc[1] = __float2half(0.0f);
       continue;
     }
@@ -353,7 +442,7 @@ __global__ void repack_q4(const uint8_t* __restrict__ q, const __half* __restric
         const int pos = (e & 1) ? (4 + (e >> 1)) : (e >> 1);
         o |= nib << (4 * pos);
       }
-      dst[i] = o;
+      (i < 4 ? dst0 : dst1)[i & 3] = o;
     }
     dsc[0] = s[(size_t)src * (k / 32) + 2 * kt];
     dsc[1] = s[(size_t)src * (k / 32) + 2 * kt + 1];
@@ -410,7 +499,7 @@ static cudaError_t launch_bn(const CUtensorMap& map, const QWeight& w, int M, co
     attr_set[dev] = true;
   }
   const int grid = std::min(tg.count(), num_sms);
-  kern<<<grid, kGemmThreads, Cfg::kSmem, st>>>(map, w.tiles, M, w.n, tg, y, ldy, ws, err);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmem, st>>>(map, w.tiles, M, w.n, tg, y, ldy, ws, err);
   return cudaGetLastError();
 }
 
@@ -421,28 +510,41 @@ static cudaError_t launch_epi(int bn, const CUtensorMap& map, const QWeight& w, 
     case 32: return launch_bn<32, EPI>(map, w, M, tg, num_sms, y, ldy, ws, err, st);
     case 64: return launch_bn<64, EPI>(map, w, M, tg, num_sms, y, ldy, ws, err, st);
     case 128: return launch_bn<128, EPI>(map, w, M, tg, num_sms, y, ldy, ws, err, st);
-    default: return launch_bn<256, EPI>(map, w, M, tg, num_sms, y, ldy, ws, err, st);
+    default: return launch_bn<192, EPI>(map, w, M, tg, num_sms, y, ldy, ws, err, st);
   }
 }
 
-// Token tile width and split-K: 256-wide token tiles for long prompts, narrower ones (with the K
-// dimension split across CTAs) when the weight tiles alone would leave most SMs idle.
+// Token tile width and split-K: 192-wide token tiles for long prompts, narrower ones for short ones.
+// The K dimension is split across CTAs when that shortens the longest CTA's walk: the cost of a
+// split count is (waves of work units over the SMs) x (k-tiles per unit), plus one k-tile for the
+// finishing pass that sums the splits.
+// k-tiles per split: even where K allows, so that two-k-tile stages are not cut short
+static int split_kps(int KT, int splits) {
+  int kps = (KT + splits - 1) / splits;
+  if (KT % 2 == 0) kps += kps & 1;
+  return kps;
+}
+
 void gemm_plan(const QWeight& w, int M, int num_sms, int* bn_out, int* splits_out, int* kps_out) {
-  int bn = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
+  // past 128 tokens: 128- or 192-wide tiles, whichever covers M with less work, counting a tile as
+  // at least 160 columns (below that the dequantization of its weight tile, not the MMA, sets its pace)
+  int bn = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+  if (M > 128 && (long)((M + 191) / 192) * 192 <= (long)((M + 127) / 128) * 160) bn = 192;
   const int ntiles = w.npad / kBM;
   const int mtiles = (M + bn - 1) / bn;
   const int KT = w.k / kBK;
-  int splits = 1;
   const int tiles = ntiles * mtiles;
-  if (tiles < num_sms) {
-    splits = (num_sms + tiles - 1) / tiles;
-    splits = std::min(splits, std::max(1, KT / 4));  // at least 4 k-tiles per split
+  int best = 1;
+  long best_cost = (long)((tiles + num_sms - 1) / num_sms) * KT;
+  for (int s = 2; s <= std::max(1, KT / 4); s++) {  // at least 4 k-tiles per split
+    const int kps = split_kps(KT, s);
+    if ((KT + kps - 1) / kps != s) continue;
+    const long cost = (long)((tiles * (long)s + num_sms - 1) / num_sms) * kps + 1;
+    if (cost < best_cost) best_cost = cost, best = s;
   }
-  const int kps = (KT + splits - 1) / splits;
-  splits = (KT + kps - 1) / kps;
   *bn_out = bn;
-  *splits_out = splits;
-  *kps_out = kps;
+  *splits_out = best;
+  *kps_out = split_kps(KT, best);
 }
 
 cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
@@ -456,7 +558,7 @@ cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half*
   if (splits > 1 && splits * slice > ws_bytes) {  // fewer splits that fit the workspace
     const int fit = (int)std::min<size_t>(splits, ws_bytes / std::max<size_t>(slice, 1));
     splits = std::max(1, fit);
-    kps = (KT + splits - 1) / splits;
+    kps = split_kps(KT, splits);
     splits = (KT + kps - 1) / kps;
     if (splits * slice > ws_bytes) splits = 1, kps = KT;
   }

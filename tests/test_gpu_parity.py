@@ -23,8 +23,8 @@ def dev(torch, a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.mark.parametrize("m", [1, 7, 33, 130, 300, 700])
-@pytest.mark.parametrize("n,k", [(8256, 2048), (2048, 6144)])
+@pytest.mark.parametrize("m", [1, 7, 33, 100, 130, 300, 700])
+@pytest.mark.parametrize("n,k", [(8256, 2048), (2048, 6144), (384, 192)])  # 192: an odd k-tile count
 def test_matmul_matches_oracle(torch, m, n, k):
     from strands_decider.engine import QWeight
     rng = np.random.default_rng(m * 7 + n)
@@ -44,7 +44,7 @@ def test_matmul_matches_oracle(torch, m, n, k):
         assert err.max() <= 2e-3 + 2e-3 * np.abs(want).max(), (ws_bytes, err.max())
 
 
-@pytest.mark.parametrize("m", [5, 64, 200])
+@pytest.mark.parametrize("m", [5, 64, 100, 200, 328])
 def test_matmul_swiglu_epilogue(torch, m):
     from strands_decider.engine import QWeight
     rng = np.random.default_rng(m)
