@@ -105,6 +105,14 @@ int sd_attention(const void* q_dev, const void* k_dev, const void* v_dev, const 
                  int32_t goff, int32_t gstep, void* out_dev, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk,
                  int32_t hd, void* stream);
 
+/* sd_attention with the keys split across `splits` CTAs per (query block, head) (0: the engine's
+ * choice, which splits only when the query blocks x heads leave SMs idle, as for a short continuation
+ * over a long prefix); each split's partial result is merged by a second kernel. ws_dev: f32
+ * workspace of splits x hq x l x (hd + 2) floats (16-byte aligned; unused with one split). */
+int sd_attention_split(const void* q_dev, const void* k_dev, const void* v_dev, const void* gate_dev, int32_t gstride,
+                       int32_t goff, int32_t gstep, void* out_dev, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk,
+                       int32_t hd, int32_t splits, void* ws_dev, size_t ws_bytes, void* stream);
+
 /* `Gdn::subgroups` (`src/kernels.rs:257-302`): the gated delta rule over `batch` sequences of l tokens.
  * q_dev/k_dev [batch][l][qk_stride] (head h at h * 128), v_dev [batch][l][v_stride] (head h at h * 128),
  * f32, or f16 when in_f16; seq_qk/seq_v: elements between sequences. beta_dev and g_dev (the log decay:

@@ -6,7 +6,12 @@
 // Flash-style: one CTA per (64 queries, q head), 4 warps of 16 query rows; keys in blocks of 32 with
 // an online softmax in registers. Q, K and V tiles are staged in padded shared memory (row stride
 // 264 halves, so ldmatrix rows fall in distinct banks); K/V blocks are double-buffered with cp.async
-// and rows past the last valid key are zero-filled.
+// and rows past the last valid key are zero-filled. When the (query block, head) grid is too small to
+// fill the GPU (a short continuation over a long prefix) the keys are split across CTAs as well: each
+// split writes its unnormalised output with its row max and sum (f32), and attn_combine merges the
+// splits (rescaled to the largest max) and applies the gate.
+#include <algorithm>
+
 #include "common.cuh"
 #include "sd_internal.h"
 
@@ -56,7 +61,7 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 __global__ void __launch_bounds__(128, 2)
     attn_fwd_kernel(const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
                     const __half* __restrict__ gate, int gstride, int goff, int gstep, __half* __restrict__ out, int l, int p,
-                    int lt, int hq, int hk) {
+                    int lt, int hq, int hk, float* __restrict__ part_o, float* __restrict__ part_ml) {
   extern __shared__ __align__(16) uint8_t smem[];
   __half* sq = reinterpret_cast<__half*>(smem);
   __half* skv = reinterpret_cast<__half*>(smem + kSmemQ);  // [2][K | V]
@@ -67,6 +72,9 @@ __global__ void __launch_bounds__(128, 2)
   const int nq = min(BQ, l - t0);
   const int kend = p + t0 + nq;  // keys [0, kend)
   const int nkb = (kend + BKV - 1) / BKV;
+  // this CTA's share of the key blocks (all of them unless the keys are split: blockIdx.z of gridDim.z)
+  const int per = (nkb + gridDim.z - 1) / gridDim.z;
+  const int kb0 = min(nkb, (int)blockIdx.z * per), kb1 = min(nkb, kb0 + per);
 
   // Q tile, scaled by 1/sqrt(256) = 1/16 (exact in f16) and rounded to f16.
   for (int e = threadIdx.x; e < BQ * HD / 8; e += 128) {
@@ -103,10 +111,10 @@ __global__ void __launch_bounds__(128, 2)
   const int row0 = warp * 16 + g;          // CTA rows of this thread: row0, row0 + 8
   const int lim0 = p + t0 + row0, lim1 = lim0 + 8;  // last key each may see
 
-  load_kv(0, 0);
-  for (int kb = 0; kb < nkb; kb++) {
-    const int buf = kb & 1;
-    if (kb + 1 < nkb) {
+  if (kb0 < kb1) load_kv(kb0, 0);
+  for (int kb = kb0; kb < kb1; kb++) {
+    const int buf = (kb - kb0) & 1;
+    if (kb + 1 < kb1) {
       load_kv(kb + 1, buf ^ 1);
       cp_async_wait<1>();
     } else {
@@ -156,14 +164,17 @@ __global__ void __launch_bounds__(128, 2)
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    // the running max; a row with no visible key yet (possible in a split that starts past it) keeps
+    // -1e30, and its probabilities are taken against 0, so they are exp(-1e30) = 0, not exp(0)
     const float mn0 = fmaxf(mrow[0], mx0), mn1 = fmaxf(mrow[1], mx1);
-    const float al0 = __expf(mrow[0] - mn0), al1 = __expf(mrow[1] - mn1);
+    const float mr0 = mn0 < -1e29f ? 0.0f : mn0, mr1 = mn1 < -1e29f ? 0.0f : mn1;
+    const float al0 = __expf(mrow[0] - mr0), al1 = __expf(mrow[1] - mr1);
     float sum0 = 0.0f, sum1 = 0.0f;
     uint32_t pa[4][2];
 #pragma unroll
     for (int nt = 0; nt < 4; nt++) {
-      const float p0 = __expf(s[nt][0] - mn0), p1 = __expf(s[nt][1] - mn0);
-      const float p2 = __expf(s[nt][2] - mn1), p3 = __expf(s[nt][3] - mn1);
+      const float p0 = __expf(s[nt][0] - mr0), p1 = __expf(s[nt][1] - mr0);
+      const float p2 = __expf(s[nt][2] - mr1), p3 = __expf(s[nt][3] - mr1);
       sum0 += p0 + p1;
       sum1 += p2 + p3;
       pa[nt][0] = pack_h2(p0, p1);
@@ -202,6 +213,21 @@ __global__ void __launch_bounds__(128, 2)
     __syncthreads();
   }
 
+  if (gridDim.z > 1) {
+    // split keys: the unnormalised output and (max, sum) of each row, for attn_combine
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+      const int r = row0 + half * 8;
+      if (r >= nq) continue;
+      const size_t row = ((size_t)blockIdx.z * hq + h) * l + t0 + r;
+#pragma unroll
+      for (int nt = 0; nt < HD / 8; nt++)
+        *reinterpret_cast<float2*>(part_o + row * HD + nt * 8 + 2 * tq) = make_float2(o[nt][2 * half], o[nt][2 * half + 1]);
+      if (tq == 0) *reinterpret_cast<float2*>(part_ml + row * 2) = make_float2(mrow[half], lrow[half]);
+    }
+    return;
+  }
+
   // out = O / l * sigmoid(gate), f16
   const float il0 = 1.0f / lrow[0], il1 = 1.0f / lrow[1];
 #pragma unroll
@@ -225,9 +251,58 @@ __global__ void __launch_bounds__(128, 2)
   }
 }
 
+// Merges the key splits of one (token, head) row per warp: out = sum_z e^(m_z - M) O_z /
+// sum_z e^(m_z - M) l_z, then the sigmoid gate, f16. Lane i holds dimensions 8i .. 8i + 7.
+__global__ void attn_combine(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits, int l, int hq,
+                             const __half* __restrict__ gate, int gstride, int goff, int gstep, __half* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= l * hq) return;
+  const int h = row / l, t = row % l;
+  float mmax = -1e30f;
+  for (int z = 0; z < splits; z++) mmax = fmaxf(mmax, part_ml[(((size_t)z * hq + h) * l + t) * 2]);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}, lsum = 0.0f;
+  for (int z = 0; z < splits; z++) {
+    const size_t r = ((size_t)z * hq + h) * l + t;
+    const float2 ml = *reinterpret_cast<const float2*>(part_ml + r * 2);
+    const float w = ml.y > 0.0f ? __expf(ml.x - mmax) : 0.0f;
+    lsum += w * ml.y;
+    const float4 a = *reinterpret_cast<const float4*>(part_o + r * HD + lane * 8);
+    const float4 b = *reinterpret_cast<const float4*>(part_o + r * HD + lane * 8 + 4);
+    acc[0] += w * a.x, acc[1] += w * a.y, acc[2] += w * a.z, acc[3] += w * a.w;
+    acc[4] += w * b.x, acc[5] += w * b.y, acc[6] += w * b.z, acc[7] += w * b.w;
+  }
+  const float il = 1.0f / lsum;
+  uint32_t hv[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float x0 = acc[2 * i] * il, x1 = acc[2 * i + 1] * il;
+    if (gate) {
+      const float2 gf = __half22float2(
+          *reinterpret_cast<const __half2*>(gate + (size_t)t * gstride + goff + h * gstep + lane * 8 + 2 * i));
+      x0 = x0 / (1.0f + __expf(-gf.x));
+      x1 = x1 / (1.0f + __expf(-gf.y));
+    }
+    hv[i] = pack_h2(x0, x1);
+  }
+  *reinterpret_cast<uint4*>(out + (size_t)t * hq * HD + h * HD + lane * 8) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+}
+
+size_t attention_split_bytes(int l, int hq, int splits) { return (size_t)splits * hq * l * (HD + 2) * sizeof(float); }
+
+// Key splits for a short continuation: none while the (query block, head) grid fills the SMs, else
+// enough to reach about two CTAs per SM, with at least four key blocks (128 keys) per split.
+int attention_splits(int l, int p, int hq, int num_sms) {
+  const int ctas = (l + BQ - 1) / BQ * hq;
+  if (ctas >= num_sms) return 1;
+  const int nkb = (p + l + BKV - 1) / BKV;
+  return std::max(1, std::min({(2 * num_sms + ctas - 1) / ctas, nkb / 4, 32}));
+}
+
 cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, const __half* gate, int gstride, int goff,
-                             int gstep, __half* out, int l, int p, int lt, int hq, int hk, int hd, cudaStream_t st) {
-  if (hd != HD || hq % hk != 0 || l <= 0) return cudaErrorInvalidValue;
+                             int gstep, __half* out, int l, int p, int lt, int hq, int hk, int hd, int splits, float* ws,
+                             size_t ws_bytes, cudaStream_t st) {
+  if (hd != HD || hq % hk != 0 || l <= 0 || splits < 1) return cudaErrorInvalidValue;
+  if (splits > 1 && (!ws || ws_bytes < attention_split_bytes(l, hq, splits))) return cudaErrorInvalidValue;
   static bool attr[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -237,8 +312,13 @@ cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, 
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  dim3 grid((l + BQ - 1) / BQ, hq);
-  attn_fwd_kernel<<<grid, 128, kSmem, st>>>(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk);
+  dim3 grid((l + BQ - 1) / BQ, hq, splits);
+  float* part_o = ws;
+  float* part_ml = ws ? ws + (size_t)splits * hq * l * HD : nullptr;
+  attn_fwd_kernel<<<grid, 128, kSmem, st>>>(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, part_o, part_ml);
+  if (splits == 1) return cudaGetLastError();
+  const int rows = l * hq;
+  attn_combine<<<(rows + 3) / 4, 128, 0, st>>>(part_o, part_ml, splits, l, hq, gate, gstride, goff, gstep, out);
   return cudaGetLastError();
 }
 

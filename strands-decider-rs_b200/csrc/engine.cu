@@ -620,9 +620,12 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
            sd::launch_qk_prep(e->big, N, Lw.q_norm, Lw.k_norm, e->rope, l, p, SD_CONTEXT, d, e->q, e->kc[Lw.slot],
                               e->vc[Lw.slot], st));
         const double pairs = L * p + L * (L + 1) / 2;  // causal (query, key) pairs
+        int splits = sd::attention_splits(l, p, d.hq, e->num_sms);  // keys split for short continuations
+        while (splits > 1 && sd::attention_split_bytes(l, d.hq, splits) > e->ws_bytes) splits--;
         LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * pairs,
-           sd::launch_attention(e->q, e->kc[Lw.slot], e->vc[Lw.slot], e->big, N, d.hd, 2 * d.hd, e->o, l, p, SD_CONTEXT,
-                                d.hq, d.hk, d.hd, st));
+           (*nl = splits > 1 ? 2 : 1,  // with split keys, a second kernel merges the splits
+            sd::launch_attention(e->q, e->kc[Lw.slot], e->vc[Lw.slot], e->big, N, d.hd, 2 * d.hd, e->o, l, p, SD_CONTEXT,
+                                 d.hq, d.hk, d.hd, splits, e->ws, e->ws_bytes, st)));
         MM(Lw.o_proj, e->o, d.hq * d.hd, e->y, d.d, false);
       }
     }
@@ -1030,8 +1033,34 @@ int sd_attention(const void* q, const void* k, const void* v, const void* gate, 
     return SD_ERR_INVALID;
   }
   return op_result(sd::launch_attention((const __half*)q, (const __half*)k, (const __half*)v, (const __half*)gate, gstride, goff,
-                                        gstep, (__half*)out, l, p, lt, hq, hk, hd, (cudaStream_t)stream),
+                                        gstep, (__half*)out, l, p, lt, hq, hk, hd, 1, nullptr, 0, (cudaStream_t)stream),
                    "sd_attention");
+}
+
+int sd_attention_split(const void* q, const void* k, const void* v, const void* gate, int32_t gstride, int32_t goff,
+                       int32_t gstep, void* out, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk, int32_t hd,
+                       int32_t splits, void* ws, size_t ws_bytes, void* stream) {
+  if (!q || !k || !v || !out || l <= 0 || p < 0 || p + l > lt || hk <= 0 || hq % hk || splits < 0 || (size_t)ws % 16) {
+    set_global_error("sd_attention_split: bad arguments");
+    return SD_ERR_INVALID;
+  }
+  if (splits == 0) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    splits = sd::attention_splits(l, p, hq, sms);
+  }
+  if (splits > 1 && (!ws || ws_bytes < sd::attention_split_bytes(l, hq, splits))) {
+    char msg[160];
+    snprintf(msg, sizeof msg, "sd_attention_split: the workspace needs %zu bytes for %d splits",
+             sd::attention_split_bytes(l, hq, splits), (int)splits);
+    set_global_error(msg);
+    return SD_ERR_INVALID;
+  }
+  return op_result(sd::launch_attention((const __half*)q, (const __half*)k, (const __half*)v, (const __half*)gate, gstride, goff,
+                                        gstep, (__half*)out, l, p, lt, hq, hk, hd, splits, (float*)ws, ws_bytes,
+                                        (cudaStream_t)stream),
+                   "sd_attention_split");
 }
 
 int sd_gdn(const void* q, const void* k, int32_t qk_stride, const void* v, int32_t v_stride, const void* beta,

@@ -80,6 +80,12 @@ struct GemmCfg {
 
 enum Epi { kEpiStore = 0, kEpiSilu = 1, kEpiPartial = 2 };
 
+// The SwiGLU of one output: gate and up are each rounded to f16 first, as the reference stores them.
+SD_DEV float swiglu(float gate, float up) {
+  const float g = __half2float(__float2half_rn(gate)), u = __half2float(__float2half_rn(up));
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
 struct TileGrid {
   int ntiles, mtiles, splits, kps, KT;
   __host__ __device__ int count() const { return ntiles * mtiles * splits; }
@@ -328,12 +334,11 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
             const int odd = lane & 1;
 #pragma unroll
             for (int p = 0; p < 16; p++) {
-              const float a0 = __half2float(__float2half_rn(__uint_as_float(v[2 * p])));
-              const float a1 = __half2float(__float2half_rn(__uint_as_float(v[2 * p + 1])));
+              const float a0 = __uint_as_float(v[2 * p]), a1 = __uint_as_float(v[2 * p + 1]);
               const float other = __shfl_xor_sync(0xffffffffu, odd ? a0 : a1, 1);
               const float g = odd ? other : a0;
               const float u = odd ? a1 : other;
-              st[(2 * p + odd) * 40 + (lane >> 1)] = __float2half_rn(__fdividef(g, 1.0f + __expf(-g)) * u);
+              st[(2 * p + odd) * 40 + (lane >> 1)] = __float2half_rn(swiglu(g, u));
             }
             __syncwarp();
             const int m = mbase + lane;
@@ -404,9 +409,7 @@ __global__ void gemm_finish(const float* __restrict__ ws, int splits, int M, int
         gs += ws[z * slice + m * N + 2 * j];
         us += ws[z * slice + m * N + 2 * j + 1];
       }
-      const float g = __half2float(__float2half_rn(gs));
-      const float u = __half2float(__float2half_rn(us));
-      y[m * ldy + j] = __float2half_rn(__fdividef(g, 1.0f + __expf(-g)) * u);
+      y[m * ldy + j] = __float2half_rn(swiglu(gs, us));
     }
   }
 }

@@ -86,6 +86,10 @@ cudaError_t launch_add_bias(__half* y, const float* bias, int l, int d, cudaStre
 // q [hq][l][hd] (rows for this call), k/v caches [hk][lt][hd] with this call's rows at p..p+l-1,
 // gate at gate[t * gstride + goff + h * gstep + d] (null: ungated), out [l][hq * hd].
 cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, const __half* gate, int gstride, int goff,
-                             int gstep, __half* out, int l, int p, int lt, int hq, int hk, int hd, cudaStream_t st);
+                             int gstep, __half* out, int l, int p, int lt, int hq, int hk, int hd, int splits, float* ws,
+                             size_t ws_bytes, cudaStream_t st);
+// Key splits launch_attention should use for l queries after p cached keys, and the workspace they need.
+int attention_splits(int l, int p, int hq, int num_sms);
+size_t attention_split_bytes(int l, int hq, int splits);
 
 }  // namespace sd

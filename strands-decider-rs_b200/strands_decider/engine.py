@@ -62,6 +62,8 @@ def lib() -> C.CDLL:
         L.sd_head_free.argtypes = [vp]
         L.sd_head_probs.argtypes = [vp, vp, i32, i32, C.c_double, vp]
         L.sd_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]
+        L.sd_attention_split.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp,
+                                         C.c_size_t, vp]
         L.sd_gdn.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, i32, C.c_int64, C.c_int64, i32, i32, vp,
                              C.c_size_t, vp]
         L.sd_gdn_noalloc.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, vp]
@@ -241,8 +243,14 @@ class Head:
 # Kernel-level entry points on device memory (pointers as ints, e.g. torch.Tensor.data_ptr())
 # ---------------------------------------------------------------------------------------------
 
-def attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, stream=None):
-    _check(lib().sd_attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, stream), "sd_attention")
+def attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, stream=None, splits=None, ws=None,
+              ws_bytes=0):
+    """`sd_attention`; with ``splits`` (0: the engine's choice), `sd_attention_split` on workspace ``ws``."""
+    if splits is None:
+        _check(lib().sd_attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, stream), "sd_attention")
+    else:
+        _check(lib().sd_attention_split(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, splits, ws,
+                                        ws_bytes, stream), "sd_attention_split")
 
 
 GDN_CHUNKED, GDN_SERIAL, GDN_TWO_PHASE = 0, 1, 2

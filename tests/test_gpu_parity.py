@@ -65,8 +65,9 @@ def test_matmul_swiglu_epilogue(torch, m):
         assert np.abs(got - want).max() <= 4e-3 + 4e-3 * np.abs(want).max()
 
 
-@pytest.mark.parametrize("l,p", [(300, 0), (37, 500), (1, 100), (129, 0)])
-def test_attention_matches_oracle(torch, l, p):
+@pytest.mark.parametrize("l,p", [(300, 0), (37, 500), (1, 100), (129, 0), (60, 2048)])
+@pytest.mark.parametrize("splits", [None, 0, 3, 7])  # None: sd_attention; else sd_attention_split (0: auto)
+def test_attention_matches_oracle(torch, l, p, splits):
     from strands_decider.engine import attention
     rng = np.random.default_rng(l + p)
     hq, hk, hd, lt = 8, 2, 256, 4096
@@ -81,7 +82,9 @@ def test_attention_matches_oracle(torch, l, p):
     want = oracle.attn(q, kc[:, :p + l], vc[:, :p + l], gate, 5120, hd, 2 * hd, p=p).astype(np.float32)
     out = torch.zeros((l, hq * hd), dtype=torch.float16, device="cuda")
     qd, kd, vd, gd = (dev(torch, x.view(np.uint16)) for x in (q, kc, vc, gate))
-    attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), gd.data_ptr(), 5120, hd, 2 * hd, out.data_ptr(), l, p, lt, hq, hk, hd)
+    ws = torch.empty(32 << 20, dtype=torch.uint8, device="cuda")
+    attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), gd.data_ptr(), 5120, hd, 2 * hd, out.data_ptr(), l, p, lt, hq, hk, hd,
+              splits=splits, ws=ws.data_ptr(), ws_bytes=ws.numel())
     torch.cuda.synchronize()
     got = out.cpu().numpy().astype(np.float32)
     assert np.isfinite(got).all()
