@@ -241,22 +241,23 @@ def run_ours(args, world, rank, local):
                 continue
             sids, qs, _ = request(i, args.seed)
             reqs[i] = (sids, qs)
+            # the state's ids and the questions' ids (back to back) in HBM; lengths and rows on the host
             staged[i] = (torch.from_numpy(sids.view(np.int32)).cuda(),
-                         [(torch.from_numpy(q.view(np.int32)).cuda(), torch.from_numpy(r).cuda()) for q, r in qs])
-    hidden_dev = torch.empty((3, 4, 2048), dtype=torch.float32, device="cuda")
+                         torch.from_numpy(np.concatenate([q for q, _ in qs]).view(np.int32)).cuda(),
+                         [len(q) for q, _ in qs], [list(r) for _, r in qs])
+    hidden_dev = torch.empty((16, 2048), dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
 
+    # a request as the Decider runs it (`Decider::run`, src/lib.rs:156-208): the state once, kept as
+    # a snapshot, then its questions continued from the snapshot in one batched fork
     def one_step_dev(s):
         n_q = n_tok = 0
         for i in step_requests(s, rank, world, per):
-            sd, qd = staged[i]
+            sd, qd, lens, rows = staged[i]
             snap = eng.forward_dev(sd.data_ptr(), sd.numel(), None, 0, keep=True)
-            n_tok += sd.numel()
-            for k, (qi, rw) in enumerate(qd):
-                eng.forward_dev(qi.data_ptr(), qi.numel(), rw.data_ptr(), rw.numel(), cache=snap,
-                                hidden_dev=hidden_dev[k].data_ptr())
-                n_q += 1
-                n_tok += qi.numel()
+            eng.forward_fork_dev(snap, qd.data_ptr(), lens, rows, hidden_dev.data_ptr())
+            n_q += len(lens)
+            n_tok += sd.numel() + qd.numel()
             snap.close()
         return n_q, n_tok
 
@@ -269,11 +270,11 @@ def run_ours(args, world, rank, local):
             sids, qs = reqs[i]
             snap = eng.forward(sids, [], keep=True).snapshot
             h2d += sids.nbytes
-            for qids, rows in qs:
-                out = eng.forward(qids, rows, cache=snap)
-                head.probs(out.hidden, 2048, 1.0)
+            outs = eng.forward_fork(snap, [q for q, _ in qs], [r for _, r in qs])
+            for (qids, rows), hidden in zip(qs, outs):
+                head.probs(hidden, 2048, 1.0)
                 h2d += qids.nbytes + rows.nbytes
-                d2h += out.hidden.nbytes
+                d2h += hidden.nbytes
                 n_q += 1
             snap.close()
         return n_q
@@ -342,7 +343,7 @@ def run_ours(args, world, rank, local):
                    "parallelism": f"replicas x{world} (requests sharded, no collective)"},
         "prefill_tok_s": tok_all / t_dev,
         "e2e": {"value": qh_all / t_host, "unit": "questions/s", "h2d_bytes_per_step": int(h2d_step),
-                "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward (host ids in, host hidden rows out) + sd_head_probs"},
+                "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward (state, kept) + sd_forward_fork (the questions; host ids in, host hidden rows out) + sd_head_probs"},
         "gpu_launches": int(launches),
         "roofline": {"kernel": "gemm_q4_tc (dequantizing tcgen05 GEMM)", "bound": "tensor", "achieved": gemm_tflops,
                      "peak": tf_sus, "unit": "TFLOP/s", "frac": gemm_tflops / tf_sus,

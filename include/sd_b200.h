@@ -51,6 +51,22 @@ int sd_forward(sd_engine* e, const uint32_t* ids, int32_t n_ids, const int32_t* 
                const sd_snapshot* cache, int32_t keep, float* hidden_out, sd_snapshot** snapshot_out,
                double* gpu_ms_out);
 
+/* The batched fork: `nq` questions, each a forward of lens[b] new tokens continuing the snapshot
+ * `cache`, in one pass (it replaces the serial loop of `Decider::ask_all`, `src/lib.rs:192-198`,
+ * whose every question is an `Engine::forward(ids, rows, Some(&snapshot), false, ..)`). ids: the
+ * questions' tokens back to back (sum of lens); rows: each question's rows (indices into its own
+ * tokens, nrows[b] of them), back to back; hidden_out: [sum of nrows][hidden_size] f32 in the same
+ * order. The results equal nq separate sd_forward calls up to f32 summation order. The snapshot is
+ * read in place and not changed. gpu_ms_out (may be NULL): device time of the pass. */
+int sd_forward_fork(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids, const int32_t* lens, int32_t nq,
+                    const int32_t* rows, const int32_t* nrows, float* hidden_out, double* gpu_ms_out);
+/* sd_forward_fork with the token ids already on the GPU (ids_dev) and the hidden rows written to
+ * hidden_dev [sum of nrows][hidden_size] f32, asynchronous on the engine's stream (lens, rows and
+ * nrows stay host arrays: they shape the pass). Token ids are checked on the device; errors surface
+ * at the next sd_engine_synchronize. */
+int sd_forward_fork_dev(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids_dev, const int32_t* lens, int32_t nq,
+                        const int32_t* rows, const int32_t* nrows, float* hidden_dev);
+
 /* `Snapshot::len` (`src/engine.rs:80-87`): tokens covered. A snapshot is immutable and can seed
  * any number of forwards on the engine that made it; free it with sd_snapshot_free. */
 int32_t sd_snapshot_len(const sd_snapshot* s);

@@ -9,7 +9,9 @@
 // and rows past the last valid key are zero-filled. When the (query block, head) grid is too small to
 // fill the GPU (a short continuation over a long prefix) the keys are split across CTAs as well: each
 // split writes its unnormalised output with its row max and sum (f32), and attn_combine merges the
-// splits (rescaled to the largest max) and applies the gate.
+// splits (rescaled to the largest max) and applies the gate. In packed mode (AttnPacked) the queries are
+// several sequences packed back to back, each continuing one cached prefix: the keys of a sequence are
+// the prefix's (from the cache) and then its own (from tail buffers), never another sequence's.
 #include <algorithm>
 
 #include "common.cuh"
@@ -61,16 +63,26 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 __global__ void __launch_bounds__(128, 2)
     attn_fwd_kernel(const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
                     const __half* __restrict__ gate, int gstride, int goff, int gstep, __half* __restrict__ out, int l, int p,
-                    int lt, int hq, int hk, float* __restrict__ part_o, float* __restrict__ part_ml) {
+                    int lt, int hq, int hk, float* __restrict__ part_o, float* __restrict__ part_ml, const AttnPacked pk) {
   extern __shared__ __align__(16) uint8_t smem[];
   __half* sq = reinterpret_cast<__half*>(smem);
   __half* skv = reinterpret_cast<__half*>(smem + kSmemQ);  // [2][K | V]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = gridDim.x - 1 - blockIdx.x;  // longest (latest) query blocks first
   const int h = blockIdx.y, kh = h / (hq / hk);
-  const int t0 = qb * BQ;
-  const int nq = min(BQ, l - t0);
-  const int kend = p + t0 + nq;  // keys [0, kend)
+  // t0: first query of the block within its sequence; tok0: its row in q, gate, out (and the tails)
+  int t0, nq, tok0;
+  if (pk.blk) {
+    const int sq = pk.blk[2 * blockIdx.x];
+    t0 = pk.blk[2 * blockIdx.x + 1];
+    nq = min(BQ, pk.seq_len[sq] - t0);
+    tok0 = pk.seq_off[sq] + t0;
+  } else {
+    t0 = (gridDim.x - 1 - blockIdx.x) * BQ;  // longest (latest) query blocks first
+    nq = min(BQ, l - t0);
+    tok0 = t0;
+  }
+  const int tail0 = tok0 - t0 - p;  // tail row of key p (packed mode)
+  const int kend = p + t0 + nq;     // keys [0, kend)
   const int nkb = (kend + BKV - 1) / BKV;
   // this CTA's share of the key blocks (all of them unless the keys are split: blockIdx.z of gridDim.z)
   const int per = (nkb + gridDim.z - 1) / gridDim.z;
@@ -81,7 +93,7 @@ __global__ void __launch_bounds__(128, 2)
     const int r = e / (HD / 8), c8 = (e % (HD / 8)) * 8;
     uint4 val = make_uint4(0, 0, 0, 0);
     if (r < nq) {
-      val = *reinterpret_cast<const uint4*>(q + ((size_t)h * l + t0 + r) * HD + c8);
+      val = *reinterpret_cast<const uint4*>(q + ((size_t)h * l + tok0 + r) * HD + c8);
       __half2* v2 = reinterpret_cast<__half2*>(&val);
 #pragma unroll
       for (int i = 0; i < 4; i++) v2[i] = __hmul2(v2[i], __float2half2_rn(0.0625f));
@@ -96,9 +108,14 @@ __global__ void __launch_bounds__(128, 2)
       const int r = e / (HD / 8), c8 = (e % (HD / 8)) * 8;
       const int j = kb * BKV + r;
       const bool ok = j < kend;
-      const size_t off = ((size_t)kh * lt + (ok ? j : 0)) * HD + c8;
-      cp_async16(smem_u32(dk + r * LDS + c8), k + off, ok);
-      cp_async16(smem_u32(dv + r * LDS + c8), v + off, ok);
+      const __half *ks = k, *vs = v;
+      size_t off = ((size_t)kh * lt + (ok ? j : 0)) * HD + c8;
+      if (pk.blk && ok && j >= p) {  // this sequence's own keys
+        ks = pk.kt, vs = pk.vt;
+        off = ((size_t)kh * pk.T + tail0 + j) * HD + c8;
+      }
+      cp_async16(smem_u32(dk + r * LDS + c8), ks + off, ok);
+      cp_async16(smem_u32(dv + r * LDS + c8), vs + off, ok);
     }
     cp_async_commit();
   };
@@ -219,7 +236,7 @@ __global__ void __launch_bounds__(128, 2)
     for (int half = 0; half < 2; half++) {
       const int r = row0 + half * 8;
       if (r >= nq) continue;
-      const size_t row = ((size_t)blockIdx.z * hq + h) * l + t0 + r;
+      const size_t row = ((size_t)blockIdx.z * hq + h) * l + tok0 + r;
 #pragma unroll
       for (int nt = 0; nt < HD / 8; nt++)
         *reinterpret_cast<float2*>(part_o + row * HD + nt * 8 + 2 * tq) = make_float2(o[nt][2 * half], o[nt][2 * half + 1]);
@@ -234,7 +251,7 @@ __global__ void __launch_bounds__(128, 2)
   for (int half = 0; half < 2; half++) {
     const int r = row0 + half * 8;
     if (r >= nq) continue;
-    const int t = t0 + r;
+    const int t = tok0 + r;
     const float il = half ? il1 : il0;
 #pragma unroll
     for (int nt = 0; nt < HD / 8; nt++) {
@@ -289,13 +306,18 @@ __global__ void attn_combine(const float* __restrict__ part_o, const float* __re
 
 size_t attention_split_bytes(int l, int hq, int splits) { return (size_t)splits * hq * l * (HD + 2) * sizeof(float); }
 
-// Key splits for a short continuation: none while the (query block, head) grid fills the SMs, else
-// enough to reach about two CTAs per SM, with at least four key blocks (128 keys) per split.
-int attention_splits(int l, int p, int hq, int num_sms) {
-  const int ctas = (l + BQ - 1) / BQ * hq;
+// Key splits for `qblocks` query blocks over at most `keys` keys: none while the (query block, head)
+// grid fills the SMs, else enough to reach about two CTAs per SM, with at least four key blocks (128
+// keys) per split.
+static int splits_for(int qblocks, int keys, int hq, int num_sms) {
+  const int ctas = qblocks * hq;
   if (ctas >= num_sms) return 1;
-  const int nkb = (p + l + BKV - 1) / BKV;
+  const int nkb = (keys + BKV - 1) / BKV;
   return std::max(1, std::min({(2 * num_sms + ctas - 1) / ctas, nkb / 4, 32}));
+}
+int attention_splits(int l, int p, int hq, int num_sms) { return splits_for((l + BQ - 1) / BQ, p + l, hq, num_sms); }
+int attention_splits_packed(int nblk, int p, int max_len, int hq, int num_sms) {
+  return splits_for(nblk, p + max_len, hq, num_sms);
 }
 
 cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, const __half* gate, int gstride, int goff,
@@ -315,10 +337,35 @@ cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, 
   dim3 grid((l + BQ - 1) / BQ, hq, splits);
   float* part_o = ws;
   float* part_ml = ws ? ws + (size_t)splits * hq * l * HD : nullptr;
-  attn_fwd_kernel<<<grid, 128, kSmem, st>>>(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, part_o, part_ml);
+  attn_fwd_kernel<<<grid, 128, kSmem, st>>>(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, part_o, part_ml,
+                                            AttnPacked{});
   if (splits == 1) return cudaGetLastError();
   const int rows = l * hq;
   attn_combine<<<(rows + 3) / 4, 128, 0, st>>>(part_o, part_ml, splits, l, hq, gate, gstride, goff, gstep, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention_packed(const __half* q, const __half* k, const __half* v, const __half* gate, int gstride,
+                                    int goff, int gstep, __half* out, int T, int p, int lt, int hq, int hk, int hd,
+                                    const AttnPacked& pk, int nblk, int splits, float* ws, size_t ws_bytes, cudaStream_t st) {
+  if (hd != HD || hq % hk != 0 || T <= 0 || nblk <= 0 || splits < 1 || !pk.blk) return cudaErrorInvalidValue;
+  if (splits > 1 && (!ws || ws_bytes < attention_split_bytes(T, hq, splits))) return cudaErrorInvalidValue;
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  dim3 grid(nblk, hq, splits);
+  float* part_o = ws;
+  float* part_ml = ws ? ws + (size_t)splits * hq * T * HD : nullptr;
+  attn_fwd_kernel<<<grid, 128, kSmem, st>>>(q, k, v, gate, gstride, goff, gstep, out, T, p, lt, hq, hk, part_o, part_ml, pk);
+  if (splits == 1) return cudaGetLastError();
+  const int rows = T * hq;
+  attn_combine<<<(rows + 3) / 4, 128, 0, st>>>(part_o, part_ml, splits, T, hq, gate, gstride, goff, gstep, out);
   return cudaGetLastError();
 }
 

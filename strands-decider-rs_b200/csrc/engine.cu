@@ -143,6 +143,18 @@ struct sd_engine {
   size_t gdn_scratch_bytes = 0;
   __half *h = nullptr, *big = nullptr, *mid = nullptr, *o = nullptr, *y = nullptr, *q = nullptr, *qkvc = nullptr;
   int* d_err = nullptr;
+  // batched fork: per-token / per-sequence index arrays and the packed tokens' K and V (one attention
+  // layer at a time), grown as needed
+  int* fk_meta = nullptr;
+  size_t fk_meta_ints = 0;
+  __half* fk_kv = nullptr;
+  size_t fk_kv_halves = 0;
+  // pinned staging of fk_meta: a ring of slots, each reused once the copy out of it (event) is done
+  static constexpr int kForkSlots = 4;
+  int* fk_pin[kForkSlots] = {};
+  size_t fk_pin_ints[kForkSlots] = {};
+  cudaEvent_t fk_ev[kForkSlots] = {};
+  int fk_next = 0;
   // pinned staging
   uint32_t* p_ids = nullptr;
   int* p_rows = nullptr;
@@ -563,8 +575,23 @@ cudaError_t launch(sd_engine* e, int kind, double units, F&& fn) {
     if (_e != cudaSuccess) return e->fail(SD_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_e));      \
   } while (0)
 
-// The layer loop (src/engine.rs:446-522), launched on the engine's stream.
-int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
+// A batched fork (sd_forward_fork): several sequences packed back to back, each continuing the
+// snapshot `snap`, whose states and prefix K/V are read in place and never written. Device arrays:
+// tpos (position of each packed token), tstart (first token of each token's sequence), seq_off /
+// seq_len per sequence, blk (sequence, first query) per 64-query attention block.
+struct Fork {
+  const sd_snapshot* snap;
+  const uint32_t* ids;  // [l] token ids
+  const int* rows;      // output rows (indices into the packed tokens)
+  const int *tpos, *tstart, *seq_off, *seq_len, *blk;
+  int nseq, nblk, max_len;
+  double tail_pairs;  // sum over sequences of len (len + 1) / 2: causal pairs among their own tokens
+  __half *kt, *vt;    // [hk][l][hd] K and V of the packed tokens
+};
+
+// The layer loop (src/engine.rs:446-522), launched on the engine's stream. With `fk`, the l tokens are
+// a batched fork's packed sequences (each at position p + its index within its sequence).
+int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork* fk = nullptr) {
   const sd::Dims& d = e->dm;
   cudaStream_t st = e->stream;
   const int C = d.C();
@@ -582,7 +609,7 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
   } while (0)
   const double row_bytes = (double)d.d * (4 + 2);
   LK(SD_PROF_OTHER, L * (d.d / 32 * (4.0 * e->embed_bits + 2) + row_bytes),
-     sd::launch_embed_norm(e->d_ids, l, e->embed_q, e->embed_s, e->embed_bits, d.d, e->vocab, e->layers[0].in_norm, e->x,
+     sd::launch_embed_norm(fk ? fk->ids : e->d_ids, l, e->embed_q, e->embed_s, e->embed_bits, d.d, e->vocab, e->layers[0].in_norm, e->x,
                            e->h, e->d_err, st));
   for (int i = 0; i < e->n_layers; i++) {
     const LayerW& Lw = e->layers[i];
@@ -593,16 +620,23 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
     } else {
       if (Lw.kind == 0) {
         const int N = Lw.in_proj.n;
-        __half* hist = e->hist[Lw.slot];
+        __half* hist = fk ? fk->snap->hist[Lw.slot] : e->hist[Lw.slot];
         MM(Lw.in_proj, e->h, d.d, e->big, N, false);
-        LK(SD_PROF_OTHER, L * C * 4.0, sd::launch_conv(e->big, N, Lw.conv, hist, l, C, e->qkvc, st));
-        LK(SD_PROF_OTHER, C * 12.0, sd::launch_hist_update(e->big, N, hist, l, C, st));
+        LK(SD_PROF_OTHER, L * C * 4.0,
+           sd::launch_conv(e->big, N, Lw.conv, hist, l, C, e->qkvc, fk ? fk->tstart : nullptr, st));
+        if (!fk) LK(SD_PROF_OTHER, C * 12.0, sd::launch_hist_update(e->big, N, hist, l, C, st));
         const int aoff = C + d.h * d.dv, boff = aoff + d.h;
         LK(SD_PROF_OTHER, L * d.h * 12.0,
            sd::launch_gdn_gates(e->big, N, aoff, boff, Lw.neg_a, Lw.dt_bias, l, d.h, e->beta, e->decay, st));
         const double gdn_bytes = L * (C * 2.0 + d.h * 8.0 + d.h * d.dv * 4.0) + 2.0 * d.h * d.dk * d.dv * 4.0;
-        // one chunk: the single-pass scan; longer: the two-phase scan (chunks in parallel, then the state walk)
-        if (l <= 64)
+        // one chunk: the single-pass scan; longer: the two-phase scan (chunks in parallel, then the state walk);
+        // a fork: the single-pass scan over every sequence, from the snapshot's state
+        if (fk)
+          LK(SD_PROF_GDN, gdn_bytes,
+             sd::launch_gdn_chunked_packed(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, e->beta,
+                                           e->decay, fk->snap->state[Lw.slot], e->of, fk->seq_off, fk->seq_len, fk->nseq,
+                                           d.h, st));
+        else if (l <= 64)
           LK(SD_PROF_GDN, gdn_bytes,
              sd::launch_gdn_chunked(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, 0, 0, true, e->beta,
                                     e->decay, e->state[Lw.slot], has_cache, e->of, l, d.h, 1, st));
@@ -616,8 +650,22 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
       } else {
         const int N = Lw.qkv.n;
         MM(Lw.qkv, e->h, d.d, e->big, N, false);
+        if (fk) {
+          LK(SD_PROF_OTHER, L * (N * 2.0 + (d.hq + 2.0 * d.hk) * d.hd * 2.0),
+             sd::launch_qk_prep(e->big, N, Lw.q_norm, Lw.k_norm, e->rope, l, p, l, d, fk->tpos, e->q, fk->kt, fk->vt, st));
+          const double pairs = L * p + fk->tail_pairs;  // causal (query, key) pairs of every sequence
+          sd::AttnPacked pk;
+          pk.blk = fk->blk, pk.seq_off = fk->seq_off, pk.seq_len = fk->seq_len, pk.kt = fk->kt, pk.vt = fk->vt, pk.T = l;
+          int splits = sd::attention_splits_packed(fk->nblk, p, fk->max_len, d.hq, e->num_sms);
+          while (splits > 1 && sd::attention_split_bytes(l, d.hq, splits) > e->ws_bytes) splits--;
+          LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * pairs,
+             (*nl = splits > 1 ? 2 : 1,
+              sd::launch_attention_packed(e->q, fk->snap->k[Lw.slot], fk->snap->v[Lw.slot], e->big, N, d.hd, 2 * d.hd, e->o,
+                                          l, p, p, d.hq, d.hk, d.hd, pk, fk->nblk, splits, e->ws, e->ws_bytes, st)));
+          MM(Lw.o_proj, e->o, d.hq * d.hd, e->y, d.d, false);
+        } else {
         LK(SD_PROF_OTHER, L * (N * 2.0 + (d.hq + 2.0 * d.hk) * d.hd * 2.0),
-           sd::launch_qk_prep(e->big, N, Lw.q_norm, Lw.k_norm, e->rope, l, p, SD_CONTEXT, d, e->q, e->kc[Lw.slot],
+           sd::launch_qk_prep(e->big, N, Lw.q_norm, Lw.k_norm, e->rope, l, p, SD_CONTEXT, d, nullptr, e->q, e->kc[Lw.slot],
                               e->vc[Lw.slot], st));
         const double pairs = L * p + L * (L + 1) / 2;  // causal (query, key) pairs
         int splits = sd::attention_splits(l, p, d.hq, e->num_sms);  // keys split for short continuations
@@ -627,6 +675,7 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
             sd::launch_attention(e->q, e->kc[Lw.slot], e->vc[Lw.slot], e->big, N, d.hd, 2 * d.hd, e->o, l, p, SD_CONTEXT,
                                  d.hq, d.hk, d.hd, splits, e->ws, e->ws_bytes, st)));
         MM(Lw.o_proj, e->o, d.hq * d.hd, e->y, d.d, false);
+        }
       }
     }
     if (Lw.kind != 2) {
@@ -638,7 +687,7 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows) {
   }
   if (nrows > 0)
     LK(SD_PROF_OTHER, nrows * d.d * 14.0,
-       sd::launch_final_norm(e->x, e->y, e->final_norm, e->d_rows, nrows, l, d.d, e->out, e->d_err, st));
+       sd::launch_final_norm(e->x, e->y, e->final_norm, fk ? fk->rows : e->d_rows, nrows, l, d.d, e->out, e->d_err, st));
 #undef MM
   return SD_OK;
 }
@@ -709,6 +758,112 @@ int check_forward_args(sd_engine* e, int l, int nrows, const sd_snapshot* cache,
   return SD_OK;
 }
 
+// Validates a batched fork and enqueues it on the engine's stream: one upload (through a pinned ring
+// slot) carries the index arrays (tpos, tstart, seq_off, seq_len, blk), the global rows and, from the
+// host, the ids; ids already on the device are read in place. Then the layers. `timed` brackets the
+// layers with the engine's events. *R_out: rows.
+int fork_enqueue(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids_host, const uint32_t* ids_dev,
+                 const int32_t* lens, int32_t nq, const int32_t* rows, const int32_t* nrows, bool has_out, bool timed,
+                 long long* R_out) {
+  if (!cache) return e->fail(SD_ERR_INVALID, "sd_forward_fork: no snapshot (the questions continue one)");
+  if (cache->owner != e) return e->fail(SD_ERR_INVALID, "snapshot belongs to another engine");
+  if (nq <= 0 || (!ids_host && !ids_dev) || !lens || !nrows) return e->fail(SD_ERR_INVALID, "sd_forward_fork: no questions");
+  if (e->trace_host) return e->fail(SD_ERR_INVALID, "sd_forward_fork: per-layer tracing is for sd_forward only");
+  const int p = cache->len;
+  long long T = 0, R = 0;
+  int max_len = 0, nblk = 0;
+  double tail_pairs = 0;
+  for (int b = 0; b < nq; b++) {
+    if (lens[b] <= 0 || p + lens[b] > SD_CONTEXT)
+      return e->fail(SD_ERR_INVALID, "question %d: context of %d tokens: must be %d to %d", b, p + lens[b], p + 1, SD_CONTEXT);
+    if (nrows[b] < 0) return e->fail(SD_ERR_INVALID, "question %d: negative row count", b);
+    T += lens[b];
+    R += nrows[b];
+    max_len = std::max(max_len, (int)lens[b]);
+    tail_pairs += (double)lens[b] * (lens[b] + 1) / 2;
+    nblk += (lens[b] + 63) / 64;
+  }
+  if (T > (1 << 16)) return e->fail(SD_ERR_INVALID, "sd_forward_fork: %lld tokens in one call (at most 65536)", T);
+  if (R > 0 && (!rows || !has_out)) return e->fail(SD_ERR_INVALID, "rows given without an output buffer");
+  if (ids_host)
+    for (long long i = 0; i < T; i++)
+      if (ids_host[i] >= (uint32_t)e->vocab)
+        return e->fail(SD_ERR_INVALID, "token id %u out of range (vocab %d)", ids_host[i], e->vocab);
+  // staged layout (ints): tpos[T], tstart[T], seq_off[nq], seq_len[nq], blk[2 nblk], rows[R], ids[T] (host ids)
+  const size_t n_idx = 2 * (size_t)T + 2 * (size_t)nq + 2 * (size_t)nblk;
+  const size_t n_all = n_idx + (size_t)R + (ids_host ? (size_t)T : 0);
+  cudaSetDevice(e->device);
+  int rc;
+  if ((rc = ensure_pool(e, (int)T)) != SD_OK) return rc;
+  const sd::Dims& d = e->dm;
+  cudaStream_t st = e->stream;
+  const int slot = e->fk_next;
+  e->fk_next = (slot + 1) % sd_engine::kForkSlots;
+  if (e->fk_ev[slot]) CK(cudaEventSynchronize(e->fk_ev[slot]));  // its previous upload is done
+  else CK(cudaEventCreateWithFlags(&e->fk_ev[slot], cudaEventDisableTiming));
+  if (e->fk_pin_ints[slot] < n_all) {
+    cudaFreeHost(e->fk_pin[slot]);
+    e->fk_pin[slot] = nullptr, e->fk_pin_ints[slot] = 0;
+    const size_t cap = std::max<size_t>(n_all, 8192);
+    CK(cudaMallocHost(&e->fk_pin[slot], cap * sizeof(int)));
+    e->fk_pin_ints[slot] = cap;
+  }
+  int* tpos = e->fk_pin[slot];
+  int* tstart = tpos + T;
+  int* soff = tstart + T;
+  int* slen = soff + nq;
+  int* blk = slen + nq;
+  int* grows = tpos + n_idx;
+  {
+    int t = 0, k = 0;
+    long long r = 0;
+    for (int b = 0; b < nq; b++) {
+      soff[b] = t, slen[b] = lens[b];
+      for (int j = 0; j < lens[b]; j++) tpos[t + j] = p + j, tstart[t + j] = t;
+      for (int q0 = 0; q0 < lens[b]; q0 += 64, k++) blk[2 * k] = b, blk[2 * k + 1] = q0;
+      for (int j = 0; j < nrows[b]; j++, r++) {
+        if (rows[r] < 0 || rows[r] >= lens[b])
+          return e->fail(SD_ERR_INVALID, "question %d: row %d out of range for %d tokens", b, rows[r], lens[b]);
+        grows[r] = t + rows[r];
+      }
+      t += lens[b];
+    }
+  }
+  if (ids_host) memcpy(grows + R, ids_host, T * sizeof(uint32_t));
+  if (e->fk_meta_ints < n_all) {
+    CK(cudaStreamSynchronize(st));  // the old arrays may still be read by queued work
+    cudaFree(e->fk_meta);
+    e->fk_meta = nullptr, e->fk_meta_ints = 0;
+    const size_t cap = std::max<size_t>(n_all, 8192);
+    CK(cudaMalloc(&e->fk_meta, cap * sizeof(int)));
+    e->fk_meta_ints = cap;
+  }
+  const size_t kv = 2 * (size_t)d.hk * T * d.hd;
+  if (e->fk_kv_halves < kv) {
+    CK(cudaStreamSynchronize(st));
+    cudaFree(e->fk_kv);
+    e->fk_kv = nullptr, e->fk_kv_halves = 0;
+    const size_t cap = std::max<size_t>(kv, (size_t)2 * d.hk * 1024 * d.hd);
+    CK(cudaMalloc(&e->fk_kv, cap * sizeof(__half)));
+    e->fk_kv_halves = cap;
+  }
+  CK(cudaMemcpyAsync(e->fk_meta, e->fk_pin[slot], n_all * sizeof(int), cudaMemcpyHostToDevice, st));
+  CK(cudaEventRecord(e->fk_ev[slot], st));
+  if (timed) CK(cudaEventRecord(e->ev0, st));
+  const int* dm = e->fk_meta;
+  const uint32_t* ids = ids_host ? reinterpret_cast<const uint32_t*>(dm + n_idx + R) : ids_dev;
+  Fork fk{cache, ids, dm + n_idx, dm, dm + T, dm + 2 * T, dm + 2 * T + nq, dm + 2 * T + 2 * nq, nq, nblk, max_len,
+          tail_pairs, e->fk_kv, e->fk_kv + (size_t)d.hk * T * d.hd};
+  rc = run_layers(e, (int)T, p, true, (int)R, &fk);
+  if (rc != SD_OK) {
+    cudaStreamSynchronize(st);
+    return rc;
+  }
+  if (timed) CK(cudaEventRecord(e->ev1, st));
+  *R_out = R;
+  return SD_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -772,6 +927,12 @@ void sd_engine_destroy(sd_engine* e) {
   cudaFreeHost(e->p_ids);
   cudaFreeHost(e->p_rows);
   cudaFreeHost(e->p_out);
+  cudaFree(e->fk_meta);
+  cudaFree(e->fk_kv);
+  for (int i = 0; i < sd_engine::kForkSlots; i++) {
+    cudaFreeHost(e->fk_pin[i]);
+    if (e->fk_ev[i]) cudaEventDestroy(e->fk_ev[i]);
+  }
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -849,6 +1010,44 @@ int sd_forward(sd_engine* e, const uint32_t* ids, int32_t l, const int32_t* rows
       }
   }
   if (keep) *snapshot_out = snap;
+  return SD_OK;
+}
+
+int sd_forward_fork(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids, const int32_t* lens, int32_t nq,
+                    const int32_t* rows, const int32_t* nrows, float* hidden_out, double* gpu_ms_out) {
+  if (!e) return SD_ERR_INVALID;
+  long long R = 0;
+  int rc = fork_enqueue(e, cache, ids, nullptr, lens, nq, rows, nrows, hidden_out != nullptr, true, &R);
+  if (rc != SD_OK) return rc;
+  const sd::Dims& d = e->dm;
+  cudaStream_t st = e->stream;
+  if ((rc = ensure_pinned(e, 1, (int)R)) != SD_OK) return rc;
+  if (R > 0) CK(cudaMemcpyAsync(e->p_out, e->out, (size_t)R * d.d * 4, cudaMemcpyDeviceToHost, st));
+  if ((rc = sync_engine(e)) != SD_OK) return rc;
+  if (gpu_ms_out) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev0, e->ev1);
+    *gpu_ms_out = ms;
+  }
+  if (R > 0) {
+    memcpy(hidden_out, e->p_out, (size_t)R * d.d * 4);
+    if ((int)e->unrotate.size() == d.d)  // a rotated torso (src/engine.rs:652-660)
+      for (long long r = 0; r < R; r++) {
+        float* row = hidden_out + (size_t)r * d.d;
+        fwht(row, d.d);
+        for (int c = 0; c < d.d; c++) row[c] = (float)((double)row[c] * e->unrotate[c]);
+      }
+  }
+  return SD_OK;
+}
+
+int sd_forward_fork_dev(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids_dev, const int32_t* lens, int32_t nq,
+                        const int32_t* rows, const int32_t* nrows, float* hidden_dev) {
+  if (!e) return SD_ERR_INVALID;
+  long long R = 0;
+  int rc = fork_enqueue(e, cache, nullptr, ids_dev, lens, nq, rows, nrows, hidden_dev != nullptr, false, &R);
+  if (rc != SD_OK) return rc;
+  if (R > 0) CK(cudaMemcpyAsync(hidden_dev, e->out, (size_t)R * e->dm.d * 4, cudaMemcpyDeviceToDevice, e->stream));
   return SD_OK;
 }
 

@@ -130,6 +130,11 @@ struct GdnArgs {
   float* state;                 // [seq][h][128][128]
   float* o;                     // [seq][l][h * 128]
   int load_state, l, h;
+  // packed sequences of different lengths (seq_off non-null): sequence b is tokens seq_off[b] ..
+  // + seq_len[b] of q, k, v, beta, g and o (token-major, no per-sequence stride)
+  const int *seq_off = nullptr, *seq_len = nullptr;
+  long long state_bstride = -1;  // elements between sequences' states (-1: h * 128 * 128; 0: one shared state)
+  int store_state = 1;           // write the final state back
 };
 
 template <int DVS, typename TIn>
@@ -142,13 +147,17 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
   const int h = blockIdx.x / NS, c0 = (blockIdx.x % NS) * DVS, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g8 = lane >> 2, tq = lane & 3;
   const int H = a.h;
-  const TIn* qg = a.q + b * a.seq_qk + h * DK;
-  const TIn* kg = a.k + b * a.seq_qk + h * DK;
-  const TIn* vg = a.v + b * a.seq_v + h * DK + c0;
-  const float* betag = a.beta + (long long)b * a.l * H + h;
-  const float* gg = a.g + (long long)b * a.l * H + h;
-  float* og = a.o + (long long)b * a.l * H * DK + h * DK + c0;
-  float* stg = a.state + ((long long)b * H + h) * DK * DK + c0;
+  const bool packed = a.seq_off != nullptr;
+  const long long t_base = packed ? a.seq_off[b] : (long long)b * a.l;  // first token (in beta, g, o)
+  const int L = packed ? a.seq_len[b] : a.l;
+  const TIn* qg = a.q + (packed ? t_base * a.qk_stride : b * a.seq_qk) + h * DK;
+  const TIn* kg = a.k + (packed ? t_base * a.qk_stride : b * a.seq_qk) + h * DK;
+  const TIn* vg = a.v + (packed ? t_base * a.v_stride : b * a.seq_v) + h * DK + c0;
+  const float* betag = a.beta + t_base * H + h;
+  const float* gg = a.g + t_base * H + h;
+  float* og = a.o + t_base * H * DK + h * DK + c0;
+  const long long sb = a.state_bstride < 0 ? (long long)H * DK * DK : a.state_bstride;
+  float* stg = a.state + b * sb + (long long)h * DK * DK + c0;
 
   // State slice: warp w owns key rows 16w..16w+15, all DVS columns (m16n8 accumulator layout).
   float sacc[DVS / 8][4];
@@ -176,7 +185,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
   // f16 inputs are prefetched one chunk ahead into the staging buffers; f32 inputs are read directly
   constexpr bool kStage = sizeof(TIn) == 2;
   auto prefetch = [&](int t0) {
-    const int n = min(CH, a.l - t0);
+    const int n = min(CH, L - t0);
     for (int e = threadIdx.x; e < CH * (DK / 8); e += 256) {  // q, k: 16 chunks of 16 bytes per row
       const int r = e >> 4, c = (e & 15) * 8;
       const int rr = r < n ? r : 0;
@@ -197,8 +206,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
   };
   if constexpr (kStage) prefetch(0);
 
-  for (int t0 = 0; t0 < a.l; t0 += CH) {
-    const int n = min(CH, a.l - t0);
+  for (int t0 = 0; t0 < L; t0 += CH) {
+    const int n = min(CH, L - t0);
     // 1. normalised q^, k^ (one warp per token row), the value slice, the gates
     if constexpr (kStage) {
       cp_async_wait_all();
@@ -239,7 +248,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
     }
     __syncthreads();
     if constexpr (kStage) {
-      if (t0 + CH < a.l) prefetch(t0 + CH);  // the staging buffers are free again
+      if (t0 + CH < L) prefetch(t0 + CH);  // the staging buffers are free again
     }
     if (warp == 0) {  // inclusive prefix sum of the log decays
       const float x0 = sm.g[2 * lane], x1 = sm.g[2 * lane + 1];
@@ -467,13 +476,15 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
     __syncthreads();
   }
   // final state (f32)
+  if (a.store_state) {
 #pragma unroll
-  for (int nt = 0; nt < DVS / 8; nt++)
+    for (int nt = 0; nt < DVS / 8; nt++)
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-      const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
-      stg[row * DK + col] = sacc[nt][r];
-    }
+      for (int r = 0; r < 4; r++) {
+        const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
+        stg[row * DK + col] = sacc[nt][r];
+      }
+  }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -931,6 +942,21 @@ cudaError_t launch_gdn_chunked(const void* q, const void* k, int qk_stride, cons
   GdnArgs<float> a{(const float*)q, (const float*)k, (const float*)v, qk_stride, v_stride, seq_qk, seq_v,
                    beta, g, state, o, load_state ? 1 : 0, l, h};
   return wide ? launch_chunk<64>(a, batch, st) : launch_chunk<32>(a, batch, st);
+}
+
+// The chunked scan over `nseq` packed sequences of different lengths (sequence b: tokens seq_off[b] ..
+// + seq_len[b], device arrays), all starting from one shared state, which is read and not written:
+// continuations of one prefix, as a batched fork runs them.
+cudaError_t launch_gdn_chunked_packed(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
+                                      const float* beta, const float* g, const float* state, float* o, const int* seq_off,
+                                      const int* seq_len, int nseq, int h, cudaStream_t st) {
+  if (nseq <= 0 || h <= 0) return cudaErrorInvalidValue;
+  GdnArgs<__half> a{q, k, v, qk_stride, v_stride, 0, 0, beta, g, const_cast<float*>(state), o, 1, 0, h};
+  a.seq_off = seq_off;
+  a.seq_len = seq_len;
+  a.state_bstride = 0;
+  a.store_state = 0;
+  return (long long)nseq * h >= 128 ? launch_chunk<64>(a, nseq, st) : launch_chunk<32>(a, nseq, st);
 }
 
 }  // namespace sd

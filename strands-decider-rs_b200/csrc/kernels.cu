@@ -138,25 +138,76 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
   }
 }
 
-// conv (src/kernels.rs:152-170): depthwise causal conv, kernel 4, over the q/k/v channels of the
-// in_proj row, reading the 3-row history for t < 0; then SiLU. The output is stored as f16 (the
-// reference keeps f32): the chunked scan that reads it rounds q, k and v to f16 tensor-core operands
-// anyway, after normalising q and k in f32.
-__global__ void conv_kernel(const __half* __restrict__ big, int stride, const float4* __restrict__ cw,
-                            const __half* __restrict__ hist, int l, int C, __half* __restrict__ out) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  const int t = blockIdx.y;
-  if (c >= C) return;
-  const float4 k = cw[c];
-  const float kk[4] = {k.x, k.y, k.z, k.w};
-  float s = 0.0f;
+// conv (src/kernels.rs:152-171): depthwise causal conv (4 taps) over the C = q,k,v channels of the
+// in_proj output, then SiLU, f16 out. Each thread owns 8 channels (16-byte loads and stores) and a run
+// of kConvT consecutive tokens, sliding a 3-row window along it. The rows before a sequence's first
+// token come from its history (the last 3 pre-conv rows of the prefix, `hist` [3][C]). With `tstart`
+// (the first token of each token's sequence, for several sequences packed back to back) the window
+// restarts from the history at every sequence start; without it all l tokens are one sequence. The
+// output is stored as f16 (the reference keeps f32): the chunked scan that reads it rounds q, k and v
+// to f16 tensor-core operands anyway, after normalising q and k in f32.
+constexpr int kConvT = 16;
+__global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ big, int stride, const float4* __restrict__ cw,
+                                                   const __half* __restrict__ hist, int l, int C, const int* __restrict__ tstart,
+                                                   __half* __restrict__ out) {
+  const int c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int t0 = blockIdx.y * kConvT;
+  if (c8 >= C || t0 >= l) return;
+  float w[8][4];
 #pragma unroll
-  for (int j = 0; j < 4; j++) {
-    const int tt = t + j - 3;
-    const float v = tt >= 0 ? __half2float(big[(size_t)tt * stride + c]) : __half2float(hist[(size_t)(tt + 3) * C + c]);
-    s += kk[j] * v;
+  for (int i = 0; i < 8; i++) {
+    const float4 k = cw[c8 + i];
+    w[i][0] = k.x, w[i][1] = k.y, w[i][2] = k.z, w[i][3] = k.w;
   }
-  out[(size_t)t * C + c] = __float2half_rn(s / (1.0f + __expf(-s)));
+  auto unpack = [](uint4 u, float (&f)[8]) {
+    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float2 v = __half22float2(h2[i]);
+      f[2 * i] = v.x, f[2 * i + 1] = v.y;
+    }
+  };
+  auto row = [&](int t, int s0, float (&f)[8]) {  // pre-conv row t of the sequence starting at s0
+    if (t >= s0) unpack(*reinterpret_cast<const uint4*>(big + (size_t)t * stride + c8), f);
+    else unpack(*reinterpret_cast<const uint4*>(hist + (size_t)(3 + t - s0) * C + c8), f);
+  };
+  float win[3][8];
+  int s0 = tstart ? tstart[t0] : 0;
+#pragma unroll
+  for (int j = 0; j < 3; j++) row(t0 - 3 + j, s0, win[j]);
+  const int t1 = min(l, t0 + kConvT);
+  for (int t = t0; t < t1; t++) {
+    if (tstart && t > t0 && tstart[t] != s0) {  // a new sequence starts at t: its history
+      s0 = tstart[t];
+#pragma unroll
+      for (int j = 0; j < 3; j++) row(t - 3 + j, s0, win[j]);
+    }
+    float x[8];
+    row(t, s0, x);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      float r[2];
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        float acc = 0.0f;
+        acc += w[i + u][0] * win[0][i + u];
+        acc += w[i + u][1] * win[1][i + u];
+        acc += w[i + u][2] * win[2][i + u];
+        acc += w[i + u][3] * x[i + u];
+        r[u] = acc / (1.0f + __expf(-acc));
+      }
+      const __half2 hv = __floats2half2_rn(r[0], r[1]);
+      o[i / 2] = *reinterpret_cast<const uint32_t*>(&hv);
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)t * C + c8) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      win[0][i] = win[1][i];
+      win[1][i] = win[2][i];
+      win[2][i] = x[i];
+    }
+  }
 }
 
 // hist_update (src/kernels.rs:173-190): the last 3 pre-conv rows of (old history ++ this call).
@@ -268,22 +319,24 @@ __global__ void __launch_bounds__(128) gnorm_kernel(const float* __restrict__ o,
 
 // qk_prep (src/kernels.rs:400-448): per (token, head slot) RMSNorm over HD times the q or k norm
 // weight, rotate-half RoPE on the first RD dims from the f32 table, Q out [HQ][L][HD] f16, K and V
-// into the caches [HK][LT][HD] at position p + t.
+// into the caches [HK][LT][HD] at position p + t. With `tpos` (packed sequences continuing one
+// prefix) token t sits at position tpos[t] and its K and V go to row t of [HK][LT][HD] tail buffers.
 __global__ void __launch_bounds__(256) qk_prep_kernel(const __half* __restrict__ big, int stride, const float* __restrict__ qw,
                                                       const float* __restrict__ kw, const float2* __restrict__ rope, int l,
-                                                      int p, int lt, int hq, int hk, int rd, __half* __restrict__ qo,
-                                                      __half* __restrict__ ko, __half* __restrict__ vo) {
+                                                      int p, int lt, int hq, int hk, int rd, const int* __restrict__ tpos,
+                                                      __half* __restrict__ qo, __half* __restrict__ ko, __half* __restrict__ vo) {
   constexpr int HD = 256;
   __shared__ float red[8];
   __shared__ float nv[HD];
   const int t = blockIdx.x, s = blockIdx.y, d = threadIdx.x;
   const bool isq = s < hq;
-  const int pos = p + t;
+  const int pos = tpos ? tpos[t] : p + t;  // RoPE position
+  const int krow = tpos ? t : pos;         // K/V row
   const __half* row = big + (size_t)t * stride;
   const int koff = hq * HD * 2, voff = koff + hk * HD;
   if (!isq) {
     const int kh = s - hq;
-    vo[((size_t)kh * lt + pos) * HD + d] = row[voff + kh * HD + d];
+    vo[((size_t)kh * lt + krow) * HD + d] = row[voff + kh * HD + d];
   }
   const float v = __half2float(row[isq ? s * 2 * HD + d : koff + (s - hq) * HD + d]);
   const float tot = block_sum256(v * v, red);
@@ -297,7 +350,7 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const __half* __restrict__
     r = d < rd2 ? n * cs.x - nv[d + rd2] * cs.y : n * cs.x + nv[d - rd2] * cs.y;
   }
   if (isq) qo[((size_t)s * l + t) * HD + d] = __float2half_rn(r);
-  else ko[((size_t)(s - hq) * lt + pos) * HD + d] = __float2half_rn(r);
+  else ko[((size_t)(s - hq) * lt + krow) * HD + d] = __float2half_rn(r);
 }
 
 __global__ void trace_kernel(const float* __restrict__ x, const __half* __restrict__ y, int n, float* __restrict__ out) {
@@ -336,9 +389,10 @@ cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const i
 }
 
 cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, __half* qkvc,
-                        cudaStream_t st) {
-  dim3 grid((C + 255) / 256, l);
-  conv_kernel<<<grid, 256, 0, st>>>(big, stride, reinterpret_cast<const float4*>(conv_w), hist, l, C, qkvc);
+                        const int* tstart, cudaStream_t st) {
+  if (C % 8 || stride % 8) return cudaErrorInvalidValue;
+  dim3 grid((C / 8 + 127) / 128, (l + kConvT - 1) / kConvT);
+  conv_kernel<<<grid, 128, 0, st>>>(big, stride, reinterpret_cast<const float4*>(conv_w), hist, l, C, tstart, qkvc);
   return cudaGetLastError();
 }
 
@@ -367,11 +421,11 @@ cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff
 }
 
 cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,
-                           int lt, const Dims& dm, __half* q, __half* kc, __half* vc, cudaStream_t st) {
+                           int lt, const Dims& dm, const int* tpos, __half* q, __half* kc, __half* vc, cudaStream_t st) {
   if (dm.hd != 256) return cudaErrorInvalidValue;
   dim3 grid(l, dm.hq + dm.hk);
   qk_prep_kernel<<<grid, 256, 0, st>>>(big, stride, qw, kw, reinterpret_cast<const float2*>(rope), l, p, lt, dm.hq, dm.hk,
-                                       dm.rd, q, kc, vc);
+                                       dm.rd, tpos, q, kc, vc);
   return cudaGetLastError();
 }
 

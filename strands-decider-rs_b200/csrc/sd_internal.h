@@ -55,7 +55,7 @@ cudaError_t launch_add_norm(float* x, const __half* y, const float* w, int l, in
 cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int l, int d, float* out,
                               int* err, cudaStream_t st);
 cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, __half* qkvc,
-                        cudaStream_t st);
+                        const int* tstart, cudaStream_t st);
 cudaError_t launch_hist_update(const __half* big, int stride, __half* hist, int l, int C, cudaStream_t st);
 // gates: beta = sigmoid(b), g = log decay = negA softplus(a + dt_bias), both [l][h]
 cudaError_t launch_gdn_gates(const __half* big, int stride, int aoff, int boff, const float* neg_a, const float* dt_bias,
@@ -69,6 +69,9 @@ cudaError_t launch_gdn_recurrent(const float* q, const float* k, int qk_stride, 
 cudaError_t launch_gdn_chunked(const void* q, const void* k, int qk_stride, const void* v, int v_stride, long long seq_qk,
                                long long seq_v, bool in_f16, const float* beta, const float* g, float* state, bool load_state,
                                float* o, int l, int h, int batch, cudaStream_t st);
+cudaError_t launch_gdn_chunked_packed(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
+                                      const float* beta, const float* g, const float* state, float* o, const int* seq_off,
+                                      const int* seq_len, int nseq, int h, cudaStream_t st);
 // two-phase chunked scan for one long sequence (f16 rows): all chunks' intra-chunk work in parallel,
 // then the state scan; `scratch` holds gdn_two_phase_scratch(l, h) bytes of per-chunk records
 size_t gdn_two_phase_scratch(int l, int h);
@@ -78,17 +81,30 @@ cudaError_t launch_gdn_two_phase(const __half* q, const __half* k, int qk_stride
 cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff, const float* w, int l, int h, __half* out,
                          cudaStream_t st);
 cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,
-                           int lt, const Dims& dm, __half* q, __half* kc, __half* vc, cudaStream_t st);
+                           int lt, const Dims& dm, const int* tpos, __half* q, __half* kc, __half* vc, cudaStream_t st);
 cudaError_t launch_trace(const float* x, const __half* y, int n, float* out, cudaStream_t st);
 cudaError_t launch_add_bias(__half* y, const float* bias, int l, int d, cudaStream_t st);
 
 // attn.cu: causal GQA attention with the sigmoid output gate (src/kernels.rs:453-541).
 // q [hq][l][hd] (rows for this call), k/v caches [hk][lt][hd] with this call's rows at p..p+l-1,
 // gate at gate[t * gstride + goff + h * gstep + d] (null: ungated), out [l][hq * hd].
+// Packed mode of the attention kernel: query blocks of several sequences continuing one prefix.
+struct AttnPacked {
+  const int* blk = nullptr;      // [blocks][2]: sequence, first query (within the sequence) of each block
+  const int* seq_off = nullptr;  // first packed token of each sequence
+  const int* seq_len = nullptr;
+  const __half* kt = nullptr;    // [hk][T][hd] keys and values of the packed tokens
+  const __half* vt = nullptr;
+  int T = 0;
+};
 cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, const __half* gate, int gstride, int goff,
                              int gstep, __half* out, int l, int p, int lt, int hq, int hk, int hd, int splits, float* ws,
                              size_t ws_bytes, cudaStream_t st);
 // Key splits launch_attention should use for l queries after p cached keys, and the workspace they need.
+cudaError_t launch_attention_packed(const __half* q, const __half* k, const __half* v, const __half* gate, int gstride,
+                                    int goff, int gstep, __half* out, int T, int p, int lt, int hq, int hk, int hd,
+                                    const AttnPacked& pk, int nblk, int splits, float* ws, size_t ws_bytes, cudaStream_t st);
+int attention_splits_packed(int nblk, int p, int max_len, int hq, int num_sms);
 int attention_splits(int l, int p, int hq, int num_sms);
 size_t attention_split_bytes(int l, int hq, int splits);
 

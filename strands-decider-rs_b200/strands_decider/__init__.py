@@ -18,7 +18,7 @@ from .tokenizer import Tokenizer
 
 __all__ = ["Decider", "Question", "Answer", "Request", "Response", "Timings", "Engine", "Snapshot", "Error", "CONTEXT"]
 
-MAX_BATCH = 32  # questions per forward chunk in the official engine; only the token count uses it (`src/lib.rs:107-108`)
+MAX_BATCH = 32  # questions per batched fork; the reference's constant, which there only sets the token count (`src/lib.rs:107-108`)
 
 
 @dataclass
@@ -139,7 +139,8 @@ class Decider:
 
     def _run(self, state, named) -> Response:
         """`Decider::run` (`src/lib.rs:156-208`): one forward for a single question; otherwise the
-        state once with a snapshot, then each question continued from it."""
+        state once with a snapshot, then the questions continued from it, MAX_BATCH at a time in one
+        batched fork each (`sd_forward_fork`; the reference runs them one after another)."""
         t0 = time.perf_counter()
         rendered, sids, qencs, options = self.encode(state, named)
         t1 = time.perf_counter()
@@ -155,11 +156,13 @@ class Decider:
         else:
             prefix = self.engine.forward(sids, [], keep=True).snapshot
             try:
-                for i, q in enumerate(qencs):
-                    rows = list(options[i]) + [len(q.ids) - 1]
-                    out = self.engine.forward(q.ids, rows, cache=prefix)
-                    probs = self.head.probs(out.hidden, d, self._temperature(rendered[i]))
-                    answers.append((named[i][0], prompt.to_answer(rendered[i], probs, smooth)))
+                for c in range(0, len(qencs), MAX_BATCH):
+                    idx = range(c, min(len(qencs), c + MAX_BATCH))
+                    hidden = self.engine.forward_fork(prefix, [qencs[i].ids for i in idx],
+                                                      [list(options[i]) + [len(qencs[i].ids) - 1] for i in idx])
+                    for i, h in zip(idx, hidden):
+                        probs = self.head.probs(h, d, self._temperature(rendered[i]))
+                        answers.append((named[i][0], prompt.to_answer(rendered[i], probs, smooth)))
             finally:
                 prefix.close()
         input_tokens = 0

@@ -48,6 +48,8 @@ def lib() -> C.CDLL:
         L.sd_engine_set_trace.argtypes = [vp, vp, C.c_size_t]
         L.sd_forward.argtypes = [vp, vp, i32, vp, i32, vp, i32, vp, C.POINTER(vp), C.POINTER(C.c_double)]
         L.sd_forward_dev.argtypes = [vp, vp, i32, vp, i32, vp, i32, vp, C.POINTER(vp)]
+        L.sd_forward_fork.argtypes = [vp, vp, vp, vp, i32, vp, vp, vp, C.POINTER(C.c_double)]
+        L.sd_forward_fork_dev.argtypes = [vp, vp, vp, vp, i32, vp, vp, vp]
         L.sd_engine_synchronize.argtypes = [vp]
         L.sd_engine_stream.restype = vp
         L.sd_engine_stream.argtypes = [vp]
@@ -168,6 +170,34 @@ class Engine:
         out = Output(hidden, d, ms.value if timed else None, Snapshot(snap.value) if keep else None)
         out.trace = tr
         return out
+
+    def forward_fork(self, cache: Snapshot, ids_list, rows_list, timed: bool = False):
+        """`sd_forward_fork`: every question (ids_list[b], its rows rows_list[b]) continued from the
+        snapshot ``cache`` in one pass. Returns the hidden rows of each question ([rows, d] f32 each)
+        and, with ``timed``, the pass's device time in ms."""
+        lens = np.array([len(x) for x in ids_list], np.int32)
+        nrows = np.array([len(r) for r in rows_list], np.int32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(x, np.uint32) for x in ids_list]), np.uint32)
+        rows = np.ascontiguousarray(np.concatenate([np.asarray(r, np.int32) for r in rows_list] + [np.zeros(0, np.int32)]),
+                                    np.int32)
+        d = self.hidden_size()
+        hidden = np.zeros((int(nrows.sum()), d), np.float32)
+        ms = C.c_double(0.0)
+        _check(lib().sd_forward_fork(self._h, cache._h, _ptr(ids), _ptr(lens), len(lens), _ptr(rows) if len(rows) else None,
+                                     _ptr(nrows), _ptr(hidden) if len(rows) else None, C.byref(ms)),
+               "sd_forward_fork", self._h)
+        outs = np.split(hidden, np.cumsum(nrows)[:-1]) if len(nrows) > 1 else [hidden]
+        return (outs, ms.value) if timed else outs
+
+    def forward_fork_dev(self, cache: Snapshot, ids_dev: int, lens, rows_list, hidden_dev: int | None):
+        """`sd_forward_fork_dev`: the fork with the questions' ids on the GPU (back to back, lens[b]
+        each), hidden rows to ``hidden_dev``, queued on the engine's stream."""
+        lens = np.ascontiguousarray(lens, np.int32)
+        nrows = np.array([len(r) for r in rows_list], np.int32)
+        rows = np.ascontiguousarray(np.concatenate([np.asarray(r, np.int32) for r in rows_list] + [np.zeros(0, np.int32)]),
+                                    np.int32)
+        _check(lib().sd_forward_fork_dev(self._h, cache._h, ids_dev, _ptr(lens), len(lens), _ptr(rows) if len(rows) else None,
+                                         _ptr(nrows), hidden_dev), "sd_forward_fork_dev", self._h)
 
     def forward_dev(self, ids_dev: int, n_ids: int, rows_dev: int | None, n_rows: int, cache: Snapshot | None = None,
                     keep: bool = False, hidden_dev: int | None = None) -> Snapshot | None:
