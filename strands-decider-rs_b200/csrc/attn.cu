@@ -304,6 +304,14 @@ __global__ void attn_combine(const float* __restrict__ part_o, const float* __re
   *reinterpret_cast<uint4*>(out + (size_t)t * hq * HD + h * HD + lane * 8) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
 }
 
+// Loads the attention kernels on the current device (see preload_gemm).
+cudaError_t preload_attention() {
+  cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes a;
+  return cudaFuncGetAttributes(&a, attn_combine);
+}
+
 size_t attention_split_bytes(int l, int hq, int splits) { return (size_t)splits * hq * l * (HD + 2) * sizeof(float); }
 
 // Key splits for `qblocks` query blocks over at most `keys` keys: none while the (query block, head)

@@ -39,35 +39,36 @@ SD_DEV void mbar_arrive(uint64_t* bar) {
 SD_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+// Tests the phase with parity `parity`; while it is not complete the thread is suspended in hardware
+// (for at most kSuspendNs, woken when the phase completes), so waiting warps take no issue slots
+// from the warps that share their scheduler (the MMA issuer above all).
+constexpr uint32_t kSuspendNs = 20000;
 SD_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
 
 // Waits for the phase with parity `parity` to complete. Gives up after kWaitLimitNs, or soon after
-// another thread of the CTA has given up (*abort set): records `code` in *err and returns false. The
-// clock and the abort flag are read every 32 polls, and long waits back off, so waiting threads
-// take little of the shared-memory bandwidth the tensor core reads its operands through.
+// another thread of the CTA has given up (*abort set): records `code` in *err and returns false. Each
+// poll sleeps in hardware until the phase completes (or kSuspendNs), then the clock and the abort flag
+// are read.
 SD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
-  for (uint32_t i = 1;; i++) {
+  while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 31) == 0) {
-      if (*abort) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        atomicCAS(err, 0, code);
-        return false;
-      }
-      if (i >= 256) __nanosleep(64);
+    if (*abort) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      atomicCAS(err, 0, code);
+      return false;
     }
   }
 }

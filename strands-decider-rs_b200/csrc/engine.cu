@@ -159,7 +159,8 @@ struct sd_engine {
   uint32_t* p_ids = nullptr;
   int* p_rows = nullptr;
   float* p_out = nullptr;
-  int p_cap = 0;
+  int p_cap = 0;      // tokens of p_ids
+  int p_row_cap = 0;  // rows of p_rows and p_out
   float* trace_host = nullptr;
   size_t trace_floats = 0;
   std::string err;
@@ -255,17 +256,24 @@ int ensure_pool(sd_engine* e, int l) {
   return SD_OK;
 }
 
+// Pinned staging: ids for l tokens, rows and output rows for nrows rows (grown as needed).
 int ensure_pinned(sd_engine* e, int l, int nrows) {
-  const int need = std::max(l, nrows);
-  if (e->p_cap >= need) return SD_OK;
-  cudaFreeHost(e->p_ids);
-  cudaFreeHost(e->p_rows);
-  cudaFreeHost(e->p_out);
-  int cap = std::max(need, 256);
-  CK(cudaMallocHost(&e->p_ids, cap * sizeof(uint32_t)));
-  CK(cudaMallocHost(&e->p_rows, cap * sizeof(int)));
-  CK(cudaMallocHost(&e->p_out, (size_t)cap * e->dm.d * sizeof(float)));
-  e->p_cap = cap;
+  if (e->p_cap < l) {
+    cudaFreeHost(e->p_ids);
+    e->p_ids = nullptr, e->p_cap = 0;
+    const int cap = std::max(l, 256);
+    CK(cudaMallocHost(&e->p_ids, cap * sizeof(uint32_t)));
+    e->p_cap = cap;
+  }
+  if (e->p_row_cap < nrows) {
+    cudaFreeHost(e->p_rows);
+    cudaFreeHost(e->p_out);
+    e->p_rows = nullptr, e->p_out = nullptr, e->p_row_cap = 0;
+    const int cap = std::max(nrows, 64);
+    CK(cudaMallocHost(&e->p_rows, cap * sizeof(int)));
+    CK(cudaMallocHost(&e->p_out, (size_t)cap * e->dm.d * sizeof(float)));
+    e->p_row_cap = cap;
+  }
   return SD_OK;
 }
 
@@ -898,6 +906,20 @@ int sd_engine_create(const char* model_dir, int device, sd_engine** out) {
   }
   int rc = load_engine(e, model_dir);
   if (rc != SD_OK) {
+    set_global_error(e->err);
+    sd_engine_destroy(e);
+    return rc;
+  }
+  cudaError_t ce;
+  if ((ce = sd::preload_gemm()) != cudaSuccess || (ce = sd::preload_attention()) != cudaSuccess ||
+      (ce = sd::preload_gdn()) != cudaSuccess || (ce = sd::preload_kernels()) != cudaSuccess) {
+    set_global_error(std::string("sd_engine_create: loading the kernels: ") + cudaGetErrorString(ce));
+    sd_engine_destroy(e);
+    return SD_ERR_CUDA;
+  }
+  // pinned staging for the largest context up front (a resize inside a timed forward would cost a
+  // pinned allocation)
+  if ((rc = ensure_pinned(e, SD_CONTEXT, 64)) != SD_OK) {
     set_global_error(e->err);
     sd_engine_destroy(e);
     return rc;

@@ -944,6 +944,26 @@ cudaError_t launch_gdn_chunked(const void* q, const void* k, int qk_stride, cons
   return wide ? launch_chunk<64>(a, batch, st) : launch_chunk<32>(a, batch, st);
 }
 
+// Loads the gated-delta kernels on the current device (see preload_gemm).
+cudaError_t preload_gdn() {
+  cudaFuncAttributes a;
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(gdn_chunk_kernel<32, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(GdnSmem<32>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_chunk_kernel<64, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(GdnSmem<64>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_chunk_kernel<32, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(GdnSmem<32>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_chunk_kernel<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(GdnSmem<64>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem))) !=
+          cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_scan_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(ScanSmem<32>))) != cudaSuccess)
+    return e;
+  return cudaFuncGetAttributes(&a, gdn_scan_kernel<32>);
+}
+
 // The chunked scan over `nseq` packed sequences of different lengths (sequence b: tokens seq_off[b] ..
 // + seq_len[b], device arrays), all starting from one shared state, which is read and not written:
 // continuations of one prefix, as a batched fork runs them.

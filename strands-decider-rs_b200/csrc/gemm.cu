@@ -517,37 +517,42 @@ static cudaError_t launch_epi(int bn, const CUtensorMap& map, const QWeight& w, 
   }
 }
 
-// Token tile width and split-K: 192-wide token tiles for long prompts, narrower ones for short ones.
-// The K dimension is split across CTAs when that shortens the longest CTA's walk: the cost of a
-// split count is (waves of work units over the SMs) x (k-tiles per unit), plus one k-tile for the
-// finishing pass that sums the splits.
-// k-tiles per split: even where K allows, so that two-k-tile stages are not cut short
-static int split_kps(int KT, int splits) {
+// Token tile width and split-K, from a time estimate: (waves of work units over the SMs) x (k-tiles
+// per unit) x the steady-state time of a k-tile at that width (measured on B200 with one full wave of
+// 128-row weight tiles: 0.33 us at 32 or 64 tokens, 0.35 us at 128, 0.385 us at 192), plus, with K
+// split, the finishing pass: a launch and the f32 partials written and read back (8 bytes per output
+// per split at about 5 TB/s). Past 128 tokens both 128- and 192-wide tiles are costed (192 does more
+// per k-tile, 128 can fill the last wave better).
+static int split_kps(int KT, int splits) {  // k-tiles per split: even where K allows (two-k-tile stages)
   int kps = (KT + splits - 1) / splits;
   if (KT % 2 == 0) kps += kps & 1;
   return kps;
 }
 
+static double kt_us(int bn) { return bn >= 192 ? 0.385 : (bn >= 128 ? 0.35 : 0.33); }
+
 void gemm_plan(const QWeight& w, int M, int num_sms, int* bn_out, int* splits_out, int* kps_out) {
-  // past 128 tokens: 128- or 192-wide tiles, whichever covers M with less work, counting a tile as
-  // at least 160 columns (below that the dequantization of its weight tile, not the MMA, sets its pace)
-  int bn = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
-  if (M > 128 && (long)((M + 191) / 192) * 192 <= (long)((M + 127) / 128) * 160) bn = 192;
   const int ntiles = w.npad / kBM;
-  const int mtiles = (M + bn - 1) / bn;
   const int KT = w.k / kBK;
-  const int tiles = ntiles * mtiles;
-  int best = 1;
-  long best_cost = (long)((tiles + num_sms - 1) / num_sms) * KT;
-  for (int s = 2; s <= std::max(1, KT / 4); s++) {  // at least 4 k-tiles per split
-    const int kps = split_kps(KT, s);
-    if ((KT + kps - 1) / kps != s) continue;
-    const long cost = (long)((tiles * (long)s + num_sms - 1) / num_sms) * kps + 1;
-    if (cost < best_cost) best_cost = cost, best = s;
+  int cands[2] = {M <= 32 ? 32 : (M <= 64 ? 64 : 128), 0};
+  if (M > 128) cands[1] = 192;
+  double best_cost = 1e30;
+  int best_bn = cands[0], best_s = 1;
+  for (int bn : cands) {
+    if (!bn) continue;
+    const long tiles = (long)ntiles * ((M + bn - 1) / bn);
+    for (int s = 1; s <= std::max(1, KT / 4); s++) {  // at least 4 k-tiles per split
+      const int kps = split_kps(KT, s);
+      if ((KT + kps - 1) / kps != s) continue;
+      const long waves = (tiles * s + num_sms - 1) / num_sms;
+      double cost = waves * kps * kt_us(bn);
+      if (s > 1) cost += 3.0 + (double)s * M * w.n * 8.0 / 5e6;
+      if (cost < best_cost) best_cost = cost, best_bn = bn, best_s = s;
+    }
   }
-  *bn_out = bn;
-  *splits_out = best;
-  *kps_out = split_kps(KT, best);
+  *bn_out = best_bn;
+  *splits_out = best_s;
+  *kps_out = split_kps(KT, best_s);
 }
 
 cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
@@ -578,6 +583,27 @@ cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half*
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4096);
   gemm_finish<<<blocks, 256, 0, st>>>(ws, splits, M, w.n, y, ldy, silu ? 1 : 0);
   return cudaGetLastError();
+}
+
+template <int BN>
+static cudaError_t preload_bn() {
+  for (auto kern : {gemm_q4_tc<BN, kEpiStore>, gemm_q4_tc<BN, kEpiSilu>, gemm_q4_tc<BN, kEpiPartial>}) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<BN>::kSmem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// Loads every GEMM kernel on the current device (and sets its shared-memory size), so that no launch
+// later pays the first-use module load.
+cudaError_t preload_gemm() {
+  cudaError_t e;
+  if ((e = preload_bn<32>()) != cudaSuccess || (e = preload_bn<64>()) != cudaSuccess || (e = preload_bn<128>()) != cudaSuccess ||
+      (e = preload_bn<192>()) != cudaSuccess)
+    return e;
+  cudaFuncAttributes a;
+  if ((e = cudaFuncGetAttributes(&a, gemm_finish)) != cudaSuccess) return e;
+  return cudaFuncGetAttributes(&a, repack_q4);
 }
 
 cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool interleave, QWeight* out, cudaStream_t st) {

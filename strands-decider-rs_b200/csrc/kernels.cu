@@ -429,6 +429,20 @@ cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const
   return cudaGetLastError();
 }
 
+// Loads the row-wise kernels on the current device (see preload_gemm).
+cudaError_t preload_kernels() {
+  cudaFuncAttributes a;
+  const void* fns[] = {(const void*)embed_norm_kernel, (const void*)add_norm_kernel,   (const void*)final_norm_kernel,
+                       (const void*)conv_kernel,       (const void*)hist_update_kernel, (const void*)gdn_gates_kernel,
+                       (const void*)gdn_recurrent_kernel, (const void*)gnorm_kernel,  (const void*)qk_prep_kernel,
+                       (const void*)trace_kernel,      (const void*)add_bias_kernel};
+  for (const void* f : fns) {
+    cudaError_t e = cudaFuncGetAttributes(&a, f);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t launch_trace(const float* x, const __half* y, int n, float* out, cudaStream_t st) {
   trace_kernel<<<blocks_for(n, 256), 256, 0, st>>>(x, y, n, out);
   return cudaGetLastError();

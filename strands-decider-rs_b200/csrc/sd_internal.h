@@ -108,4 +108,11 @@ int attention_splits_packed(int nblk, int p, int max_len, int hq, int num_sms);
 int attention_splits(int l, int p, int hq, int num_sms);
 size_t attention_split_bytes(int l, int hq, int splits);
 
+// Load every kernel of a file on the current device (first-use module loads happen at engine
+// creation, not inside a timed forward).
+cudaError_t preload_gemm();
+cudaError_t preload_attention();
+cudaError_t preload_gdn();
+cudaError_t preload_kernels();
+
 }  // namespace sd
