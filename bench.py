@@ -349,7 +349,7 @@ def run_ours(args, world, rank, local):
                      "peak": tf_sus, "unit": "TFLOP/s", "frac": gemm_tflops / tf_sus,
                      # dram read+write of one gate_up launch at m=2048 from an ncu capture of
                      # `bench.py --workload gemm --m 2048 --n 12288` (algorithmic: 22.6 MB read)
-                     "traffic": 22.64e6, "traffic_launch": "gate_up m=2048 n=12288 k=2048",
+                     "traffic": 22.586e6, "traffic_launch": "gate_up m=2048 n=12288 k=2048",
                      "peak_source": f"{src} bf16 sustained (kernel timed inside a long step)",
                      "share_of_device_time": g["ms"] / max(1e-9, sum(v["ms"] for v in prof.values()))},
         "kernels": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
