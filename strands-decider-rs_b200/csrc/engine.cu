@@ -143,6 +143,9 @@ struct sd_engine {
   size_t gdn_scratch_bytes = 0;
   __half *h = nullptr, *big = nullptr, *mid = nullptr, *o = nullptr, *y = nullptr, *q = nullptr, *qkvc = nullptr;
   int* d_err = nullptr;
+  // snapshots: stream-ordered allocations from the engine's own pool, which keeps freed memory
+  // (release threshold unlimited), so a snapshot after a synchronisation does not map memory anew
+  cudaMemPool_t snap_pool = nullptr;
   // batched fork: per-token / per-sequence index arrays and the packed tokens' K and V (one attention
   // layer at a time), grown as needed
   int* fk_meta = nullptr;
@@ -732,7 +735,7 @@ int forward_core(sd_engine* e, int l, const sd_snapshot* cache, int nrows, bool 
     std::unique_ptr<sd_snapshot> snap(new sd_snapshot());
     snap->device = e->device;
     snap->len = T;
-    CK(cudaMallocAsync(reinterpret_cast<void**>(&snap->base), std::max<size_t>(total, 256), st));
+    CK(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&snap->base), std::max<size_t>(total, 256), e->snap_pool, st));
     snap->owner = e;
     uint8_t* q = snap->base;
     for (int i = 0; i < e->n_lin; i++, q += state_bytes) snap->state.push_back(reinterpret_cast<float*>(q));
@@ -904,6 +907,19 @@ int sd_engine_create(const char* model_dir, int device, sd_engine** out) {
     sd_engine_destroy(e);
     return SD_ERR_CUDA;
   }
+  {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    uint64_t keep_all = UINT64_MAX;
+    if (cudaMemPoolCreate(&e->snap_pool, &props) != cudaSuccess ||
+        cudaMemPoolSetAttribute(e->snap_pool, cudaMemPoolAttrReleaseThreshold, &keep_all) != cudaSuccess) {
+      set_global_error("sd_engine_create: cannot create the snapshot memory pool");
+      sd_engine_destroy(e);
+      return SD_ERR_CUDA;
+    }
+  }
   int rc = load_engine(e, model_dir);
   if (rc != SD_OK) {
     set_global_error(e->err);
@@ -957,6 +973,7 @@ void sd_engine_destroy(sd_engine* e) {
   }
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
+  if (e->snap_pool) cudaMemPoolDestroy(e->snap_pool);  // deferred while snapshots still hold memory
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }

@@ -139,74 +139,74 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
 }
 
 // conv (src/kernels.rs:152-171): depthwise causal conv (4 taps) over the C = q,k,v channels of the
-// in_proj output, then SiLU, f16 out. Each thread owns 8 channels (16-byte loads and stores) and a run
-// of kConvT consecutive tokens, sliding a 3-row window along it. The rows before a sequence's first
-// token come from its history (the last 3 pre-conv rows of the prefix, `hist` [3][C]). With `tstart`
-// (the first token of each token's sequence, for several sequences packed back to back) the window
-// restarts from the history at every sequence start; without it all l tokens are one sequence. The
-// output is stored as f16 (the reference keeps f32): the chunked scan that reads it rounds q, k and v
-// to f16 tensor-core operands anyway, after normalising q and k in f32.
-constexpr int kConvT = 16;
+// in_proj output, then SiLU, f16 out. Each thread owns 8 channels (16-byte loads and stores) and
+// kConvT consecutive tokens: it loads the kConvT + 3 input rows and the 3 history rows (the last 3
+// pre-conv rows before the sequence, `hist` [3][C]) up front, so all its loads are in flight at
+// once, then computes its outputs from registers. With `tstart` (the first token of each token's
+// sequence, for several sequences packed back to back) a tap before its token's sequence start reads
+// the history; without it all l tokens are one sequence. The output is stored as f16 (the reference
+// keeps f32): the chunked scan that reads it rounds q, k and v to f16 tensor-core operands anyway,
+// after normalising q and k in f32.
+constexpr int kConvT = 8;
 __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ big, int stride, const float4* __restrict__ cw,
                                                    const __half* __restrict__ hist, int l, int C, const int* __restrict__ tstart,
                                                    __half* __restrict__ out) {
   const int c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   const int t0 = blockIdx.y * kConvT;
   if (c8 >= C || t0 >= l) return;
+  uint4 raw[kConvT + 3];  // input rows t0 - 3 .. t0 + kConvT - 1 (zero outside 0 .. l - 1)
+#pragma unroll
+  for (int r = 0; r < kConvT + 3; r++) {
+    const int t = t0 - 3 + r;
+    raw[r] = (t >= 0 && t < l) ? *reinterpret_cast<const uint4*>(big + (size_t)t * stride + c8) : make_uint4(0, 0, 0, 0);
+  }
+  uint4 hs[3];
+#pragma unroll
+  for (int j = 0; j < 3; j++) hs[j] = *reinterpret_cast<const uint4*>(hist + (size_t)j * C + c8);
+  int st[kConvT];
+#pragma unroll
+  for (int i = 0; i < kConvT; i++) st[i] = (tstart && t0 + i < l) ? tstart[t0 + i] : 0;
   float w[8][4];
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
-    const float4 k = cw[c8 + i];
-    w[i][0] = k.x, w[i][1] = k.y, w[i][2] = k.z, w[i][3] = k.w;
+  for (int c = 0; c < 8; c++) {
+    const float4 k = cw[c8 + c];
+    w[c][0] = k.x, w[c][1] = k.y, w[c][2] = k.z, w[c][3] = k.w;
   }
-  auto unpack = [](uint4 u, float (&f)[8]) {
-    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const float2 v = __half22float2(h2[i]);
-      f[2 * i] = v.x, f[2 * i + 1] = v.y;
+  for (int i = 0; i < kConvT; i++) {
+    const int t = t0 + i;
+    if (t >= l) break;
+    uint4 src[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int tt = t - 3 + j, hr = 3 + tt - st[i];  // history row when tt is before the sequence
+      src[j] = tt >= st[i] ? raw[i + j] : (hr == 0 ? hs[0] : (hr == 1 ? hs[1] : hs[2]));
     }
-  };
-  auto row = [&](int t, int s0, float (&f)[8]) {  // pre-conv row t of the sequence starting at s0
-    if (t >= s0) unpack(*reinterpret_cast<const uint4*>(big + (size_t)t * stride + c8), f);
-    else unpack(*reinterpret_cast<const uint4*>(hist + (size_t)(3 + t - s0) * C + c8), f);
-  };
-  float win[3][8];
-  int s0 = tstart ? tstart[t0] : 0;
+    float x[4][8];
 #pragma unroll
-  for (int j = 0; j < 3; j++) row(t0 - 3 + j, s0, win[j]);
-  const int t1 = min(l, t0 + kConvT);
-  for (int t = t0; t < t1; t++) {
-    if (tstart && t > t0 && tstart[t] != s0) {  // a new sequence starts at t: its history
-      s0 = tstart[t];
+    for (int j = 0; j < 4; j++) {
+      const __half2* h2 = reinterpret_cast<const __half2*>(&src[j]);
 #pragma unroll
-      for (int j = 0; j < 3; j++) row(t - 3 + j, s0, win[j]);
+      for (int c = 0; c < 4; c++) {
+        const float2 f = __half22float2(h2[c]);
+        x[j][2 * c] = f.x, x[j][2 * c + 1] = f.y;
+      }
     }
-    float x[8];
-    row(t, s0, x);
     uint32_t o[4];
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
+    for (int c = 0; c < 8; c += 2) {
       float r[2];
 #pragma unroll
       for (int u = 0; u < 2; u++) {
         float acc = 0.0f;
-        acc += w[i + u][0] * win[0][i + u];
-        acc += w[i + u][1] * win[1][i + u];
-        acc += w[i + u][2] * win[2][i + u];
-        acc += w[i + u][3] * x[i + u];
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc += w[c + u][j] * x[j][c + u];
         r[u] = acc / (1.0f + __expf(-acc));
       }
       const __half2 hv = __floats2half2_rn(r[0], r[1]);
-      o[i / 2] = *reinterpret_cast<const uint32_t*>(&hv);
+      o[c / 2] = *reinterpret_cast<const uint32_t*>(&hv);
     }
     *reinterpret_cast<uint4*>(out + (size_t)t * C + c8) = make_uint4(o[0], o[1], o[2], o[3]);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      win[0][i] = win[1][i];
-      win[1][i] = win[2][i];
-      win[2][i] = x[i];
-    }
   }
 }
 
@@ -300,21 +300,22 @@ __global__ void __launch_bounds__(128) gnorm_kernel(const float* __restrict__ o,
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= l * h) return;
   const int t = row / h, hh = row % h;
-  const float* src = o + (size_t)t * h * DV + hh * DV;
-  float v[4];
-  float ss = 0.0f;
+  const int c = lane * 4;  // this lane's 4 consecutive channels
+  const float4 v = *reinterpret_cast<const float4*>(o + (size_t)t * h * DV + hh * DV + c);
+  const uint2 zz = *reinterpret_cast<const uint2*>(big + (size_t)t * stride + zoff + hh * DV + c);
+  const float4 ww = *reinterpret_cast<const float4*>(w + c);
+  const float inv = rsqrtf(warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w) / (float)DV + 1e-6f);
+  const float2 z01 = __half22float2(*reinterpret_cast<const __half2*>(&zz.x));
+  const float2 z23 = __half22float2(*reinterpret_cast<const __half2*>(&zz.y));
+  const float vv[4] = {v.x, v.y, v.z, v.w}, wv[4] = {ww.x, ww.y, ww.z, ww.w}, z[4] = {z01.x, z01.y, z23.x, z23.y};
+  float r[4];
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    v[i] = src[lane + 32 * i];
-    ss += v[i] * v[i];
-  }
-  const float inv = rsqrtf(warp_sum(ss) / (float)DV + 1e-6f);
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int c = lane + 32 * i;
-    const float z = __half2float(big[(size_t)t * stride + zoff + hh * DV + c]);
-    out[(size_t)t * h * DV + hh * DV + c] = __float2half_rn(w[c] * v[i] * inv * z / (1.0f + __expf(-z)));
-  }
+  for (int i = 0; i < 4; i++) r[i] = wv[i] * vv[i] * inv * z[i] / (1.0f + __expf(-z[i]));
+  const __half2 a = __floats2half2_rn(r[0], r[1]), b = __floats2half2_rn(r[2], r[3]);
+  uint2 res;
+  res.x = *reinterpret_cast<const uint32_t*>(&a);
+  res.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(out + (size_t)t * h * DV + hh * DV + c) = res;
 }
 
 // qk_prep (src/kernels.rs:400-448): per (token, head slot) RMSNorm over HD times the q or k norm
