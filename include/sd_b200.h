@@ -110,6 +110,36 @@ int sd_head_load(const char* safetensors_path, sd_head** out);
 void sd_head_free(sd_head* h);
 int sd_head_probs(const sd_head* h, const float* hidden, int32_t n_rows, int32_t d, double temperature, double* probs_out);
 
+/* The Decider on the engine (the reference's `Decider`, `src/lib.rs:100-209`): tokenizer, prompt,
+ * torso, pointer head and answers in the library (C++). */
+typedef struct sd_decider sd_decider;
+typedef struct sd_tokenizer sd_tokenizer;
+/* `Decider::load` (`src/lib.rs:120-134`): tokenizer.json, the torso (sd_engine_create on `device`),
+ * head.safetensors and hobson_config.json of a model directory. Failure: sd_host_last_error(). */
+int sd_decider_load(const char* model_dir, int device, sd_decider** out);
+void sd_decider_free(sd_decider* d);
+/* `Decider::evaluate` / `ask_all` (`src/lib.rs:141-208`) on a System One request
+ * (`Request::from_json`, `src/lib.rs:46-63`: {"state": content, "questions": {name: question}}):
+ * writes the response body (`Response::to_json`, `src/lib.rs:78-87`: model, answers by name, usage) to
+ * *response_json, a NUL-terminated string the caller frees with sd_string_free. Several questions
+ * share one encoding of the state: a snapshot, then one batched fork per 32 questions. */
+int sd_decider_ask_all(sd_decider* d, const char* request_json, char** response_json);
+const char* sd_decider_last_error(const sd_decider* d);
+const char* sd_host_last_error(void);
+void sd_string_free(char* s);
+
+/* `Tokenizer::from_json` / `encode` (`src/tokenizer.rs:84-155`) on their own: `text` (len bytes of
+ * UTF-8) to ids and byte offsets ([n][2], into the NFC text); at most `cap` are written, *n_out is the
+ * full count. */
+int sd_tokenizer_load(const char* tokenizer_json_path, sd_tokenizer** out);
+void sd_tokenizer_free(sd_tokenizer* t);
+int sd_tokenizer_encode(const sd_tokenizer* t, const char* text, size_t len, uint32_t* ids, uint32_t* offsets, int64_t cap,
+                        int64_t* n_out);
+/* Prompt rendering (`src/prompt.rs:159-200`) of {"state": content, "questions": [question, ...]}:
+ * writes {"state": text, "questions": [{"text": text, "spans": [[begin, end], ...]}]} (byte ranges of
+ * the option lines) to *out_json (free with sd_string_free). */
+int sd_prompt_render(const char* request_json, char** out_json);
+
 /* Kernel-level entry points on device memory, on CUDA stream `stream` (a cudaStream_t; NULL: the
  * legacy default stream). They replace single dispatches of the reference's plan
  * (`src/engine.rs:396-524`) and serve the isolated benchmarks. */

@@ -1,0 +1,319 @@
+// The Decider (the reference's src/lib.rs:100-209) in C++ over the engine's C ABI: tokenizer, prompt,
+// torso (sd_forward / sd_forward_fork), pointer head, answers. Exposed as sd_decider_* (JSON request in,
+// the System One response body out), plus the tokenizer and prompt rendering on their own.
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "prompt.h"
+#include "pyjson.h"
+#include "sd_b200.h"
+#include "tokenizer.h"
+#include "unicode.h"
+
+namespace {
+
+thread_local std::string g_host_error;
+
+constexpr size_t kMaxBatch = 32;  // questions per fork; the reference's MAX_BATCH (src/lib.rs:107-108)
+
+int host_fail(std::string* slot, const std::string& msg) {
+  if (slot) *slot = msg;
+  g_host_error = msg;
+  return SD_ERR_INVALID;
+}
+
+bool read_file(const std::string& path, std::string& out, std::string& err) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) {
+    err = path + ": cannot open";
+    return false;
+  }
+  std::ostringstream ss;
+  ss << f.rdbuf();
+  out = ss.str();
+  return true;
+}
+
+char* dup_string(const std::string& s) {
+  char* p = static_cast<char*>(malloc(s.size() + 1));
+  if (p) memcpy(p, s.c_str(), s.size() + 1);
+  return p;
+}
+
+struct Config {  // hobson_config.json (src/lib.rs:89-98)
+  size_t max_length = 0;
+  double temperature = 1.0;
+  std::map<std::string, double> temperature_by_kind;
+  double ordinal_smoothing = 0.0;
+};
+
+}  // namespace
+
+struct sd_tokenizer {
+  std::unique_ptr<sd::Tokenizer> tok;
+};
+
+struct sd_decider {
+  sd_engine* engine = nullptr;
+  sd_head* head = nullptr;
+  std::unique_ptr<sd::Tokenizer> tok;
+  Config cfg;
+  std::string err;
+
+  ~sd_decider() {
+    sd_head_free(head);
+    sd_engine_destroy(engine);
+  }
+
+  double temperature(sd::prompt::Kind k) const {
+    auto it = cfg.temperature_by_kind.find(sd::prompt::kind_name(k));
+    return it == cfg.temperature_by_kind.end() ? cfg.temperature : it->second;
+  }
+
+  // `Decider::run` (src/lib.rs:156-208): the answers, in question order, and the usage count.
+  sd::pj::Value run(const sd::pj::Value& state, const std::vector<std::pair<std::string, sd::prompt::Question>>& named) {
+    using namespace sd;
+    if (!state.is_content()) throw std::runtime_error("state must be a string, object or array");
+    if (named.empty()) throw std::runtime_error("ask at least one question");
+    for (const auto& q : named) q.second.validate();
+    std::vector<prompt::Rendered> rendered;
+    for (const auto& q : named) rendered.push_back(prompt::render_question(q.second));
+    const Encoding st = tok->encode(prompt::render_state(state));
+    std::vector<Encoding> qs;
+    size_t longest = 0;
+    for (const auto& r : rendered) {
+      qs.push_back(tok->encode(r.text));
+      longest = std::max(longest, qs.back().ids.size());
+    }
+    const size_t ns = st.ids.size();
+    if (ns + longest > cfg.max_length)
+      throw std::runtime_error("prompt of " + std::to_string(ns + longest) + " tokens (" + std::to_string(ns) + " state + " +
+                               std::to_string(longest) + " question) exceeds the context window of " +
+                               std::to_string(cfg.max_length) + " tokens");
+    std::vector<std::vector<size_t>> options;
+    for (size_t i = 0; i < qs.size(); i++) options.push_back(prompt::option_token_index(qs[i].offsets, rendered[i].spans));
+    const int d = sd_engine_hidden_size(engine);
+    pj::Value answers = pj::Value::object();
+    auto answer = [&](size_t i, const float* hidden, size_t nrows) {
+      std::vector<double> probs(nrows - 1);
+      if (sd_head_probs(head, hidden, (int32_t)nrows, d, temperature(rendered[i].kind), probs.data()) != SD_OK)
+        throw std::runtime_error(sd_last_error());
+      answers.set(named[i].first, prompt::to_answer(rendered[i], probs, cfg.ordinal_smoothing));
+    };
+    auto check = [&](int rc) {
+      if (rc != SD_OK) throw std::runtime_error(sd_engine_last_error(engine));
+    };
+    if (qs.size() == 1) {
+      std::vector<uint32_t> ids(st.ids);
+      ids.insert(ids.end(), qs[0].ids.begin(), qs[0].ids.end());
+      std::vector<int32_t> rows;
+      for (size_t o : options[0]) rows.push_back((int32_t)(ns + o));
+      rows.push_back((int32_t)ids.size() - 1);
+      std::vector<float> hidden(rows.size() * (size_t)d);
+      check(sd_forward(engine, ids.data(), (int32_t)ids.size(), rows.data(), (int32_t)rows.size(), nullptr, 0, hidden.data(),
+                       nullptr, nullptr));
+      answer(0, hidden.data(), rows.size());
+    } else {
+      sd_snapshot* prefix = nullptr;
+      check(sd_forward(engine, st.ids.data(), (int32_t)ns, nullptr, 0, nullptr, 1, nullptr, &prefix, nullptr));
+      try {
+        for (size_t c = 0; c < qs.size(); c += kMaxBatch) {
+          const size_t e = std::min(qs.size(), c + kMaxBatch);
+          std::vector<uint32_t> ids;
+          std::vector<int32_t> lens, rows, nrows;
+          for (size_t i = c; i < e; i++) {
+            ids.insert(ids.end(), qs[i].ids.begin(), qs[i].ids.end());
+            lens.push_back((int32_t)qs[i].ids.size());
+            for (size_t o : options[i]) rows.push_back((int32_t)o);
+            rows.push_back((int32_t)qs[i].ids.size() - 1);
+            nrows.push_back((int32_t)options[i].size() + 1);
+          }
+          std::vector<float> hidden(rows.size() * (size_t)d);
+          check(sd_forward_fork(engine, prefix, ids.data(), lens.data(), (int32_t)lens.size(), rows.data(), nrows.data(),
+                                hidden.data(), nullptr));
+          size_t at = 0;
+          for (size_t i = c; i < e; i++) {
+            answer(i, hidden.data() + at * d, (size_t)nrows[i - c]);
+            at += nrows[i - c];
+          }
+        }
+      } catch (...) {
+        sd_snapshot_free(prefix);
+        throw;
+      }
+      sd_snapshot_free(prefix);
+    }
+    // usage as the official engine counts it: chunks of questions, each with the state once
+    size_t input_tokens = 0;
+    for (size_t c = 0; c < qs.size(); c += kMaxBatch) {
+      const size_t e = std::min(qs.size(), c + kMaxBatch);
+      input_tokens += ns;
+      for (size_t i = c; i < e; i++) input_tokens += qs[i].ids.size();
+    }
+    pj::Value usage = pj::Value::object();
+    usage.set("input_tokens", pj::Value::integer((long long)input_tokens));
+    usage.set("output_tokens", pj::Value::integer((long long)named.size()));
+    pj::Value resp = pj::Value::object();  // Response::to_json (src/lib.rs:78-87)
+    resp.set("model", pj::Value::str("strands-decider-rs-0.1.0"));
+    resp.set("answers", answers);
+    resp.set("usage", usage);
+    return resp;
+  }
+};
+
+extern "C" {
+
+const char* sd_host_last_error(void) { return g_host_error.c_str(); }
+
+void sd_string_free(char* s) { free(s); }
+
+int sd_tokenizer_load(const char* path, sd_tokenizer** out) {
+  if (!path || !out) return host_fail(nullptr, "sd_tokenizer_load: null argument");
+  std::string text, err;
+  if (!read_file(path, text, err)) return host_fail(nullptr, err);
+  try {
+    auto t = new sd_tokenizer();
+    t->tok = sd::Tokenizer::from_json(text);
+    *out = t;
+    return SD_OK;
+  } catch (const std::exception& e) {
+    return host_fail(nullptr, e.what());
+  }
+}
+
+void sd_tokenizer_free(sd_tokenizer* t) { delete t; }
+
+int sd_tokenizer_encode(const sd_tokenizer* t, const char* text, size_t len, uint32_t* ids, uint32_t* offsets, int64_t cap,
+                        int64_t* n_out) {
+  if (!t || (!text && len) || !n_out) return host_fail(nullptr, "sd_tokenizer_encode: null argument");
+  try {
+    const sd::Encoding enc = t->tok->encode(std::string(text ? text : "", len));
+    *n_out = (int64_t)enc.ids.size();
+    for (int64_t i = 0; i < (int64_t)enc.ids.size() && i < cap; i++) {
+      if (ids) ids[i] = enc.ids[i];
+      if (offsets) offsets[2 * i] = enc.offsets[i].first, offsets[2 * i + 1] = enc.offsets[i].second;
+    }
+    return SD_OK;
+  } catch (const std::exception& e) {
+    return host_fail(nullptr, e.what());
+  }
+}
+
+int sd_prompt_render(const char* request_json, char** out_json) {
+  if (!request_json || !out_json) return host_fail(nullptr, "sd_prompt_render: null argument");
+  try {
+    using namespace sd;
+    const pj::Value req = pj::parse(request_json);
+    const pj::Value* state = req.get("state");
+    const pj::Value* qs = req.get("questions");
+    pj::Value out = pj::Value::object();
+    out.set("state", pj::Value::str(prompt::render_state(state ? *state : pj::Value())));
+    pj::Value arr = pj::Value::array();
+    if (qs && qs->kind == pj::Value::Array)
+      for (const pj::Value& q : qs->arr) {
+        const prompt::Rendered r = prompt::render_question(prompt::Question::from_json(q));
+        pj::Value o = pj::Value::object();
+        o.set("text", pj::Value::str(r.text));
+        pj::Value spans = pj::Value::array();
+        for (const auto& sp : r.spans) {
+          pj::Value p = pj::Value::array();
+          p.arr.push_back(pj::Value::integer(sp.first));
+          p.arr.push_back(pj::Value::integer(sp.second));
+          spans.arr.push_back(p);
+        }
+        o.set("spans", spans);
+        arr.arr.push_back(o);
+      }
+    out.set("questions", arr);
+    *out_json = dup_string(pj::dumps(out));
+    return SD_OK;
+  } catch (const std::exception& e) {
+    return host_fail(nullptr, e.what());
+  }
+}
+
+int sd_decider_load(const char* model_dir, int device, sd_decider** out) {
+  if (!model_dir || !out) return host_fail(nullptr, "sd_decider_load: null argument");
+  const std::string dir(model_dir);
+  std::unique_ptr<sd_decider> d(new sd_decider());
+  std::string text, err;
+  if (!read_file(dir + "/tokenizer.json", text, err)) return host_fail(nullptr, err);
+  try {
+    d->tok = sd::Tokenizer::from_json(text);
+  } catch (const std::exception& e) {
+    return host_fail(nullptr, e.what());
+  }
+  int rc = sd_engine_create(model_dir, device, &d->engine);
+  if (rc != SD_OK) return host_fail(nullptr, sd_last_error()), rc;
+  rc = sd_head_load((dir + "/head.safetensors").c_str(), &d->head);
+  if (rc != SD_OK) return host_fail(nullptr, sd_last_error()), rc;
+  if (!read_file(dir + "/hobson_config.json", text, err)) return host_fail(nullptr, err);
+  try {
+    const sd::pj::Value c = sd::pj::parse(text);
+    const sd::pj::Value* ml = c.get("max_length");
+    const sd::pj::Value* t = c.get("temperature");
+    if (!ml || ml->kind != sd::pj::Value::Int || ml->i < 0) throw std::runtime_error("missing or bad field `max_length`");
+    if (!t || !t->is_number()) throw std::runtime_error("missing or bad field `temperature`");
+    d->cfg.max_length = (size_t)ml->i;
+    d->cfg.temperature = t->as_double();
+    if (const sd::pj::Value* tk = c.get("temperature_by_kind")) {
+      if (tk->kind != sd::pj::Value::Object) throw std::runtime_error("bad field `temperature_by_kind`");
+      for (const auto& kv : tk->obj) {
+        if (!kv.second.is_number()) throw std::runtime_error("bad field `temperature_by_kind`");
+        d->cfg.temperature_by_kind[kv.first] = kv.second.as_double();
+      }
+    }
+    if (const sd::pj::Value* os = c.get("ordinal_smoothing")) {
+      if (!os->is_number()) throw std::runtime_error("bad field `ordinal_smoothing`");
+      d->cfg.ordinal_smoothing = os->as_double();
+    }
+  } catch (const std::exception& e) {
+    return host_fail(nullptr, std::string("hobson_config.json: ") + e.what());
+  }
+  *out = d.release();
+  return SD_OK;
+}
+
+void sd_decider_free(sd_decider* d) { delete d; }
+
+const char* sd_decider_last_error(const sd_decider* d) { return d ? d->err.c_str() : g_host_error.c_str(); }
+
+int sd_decider_ask_all(sd_decider* d, const char* request_json, char** response_json) {
+  if (!d || !request_json || !response_json) return host_fail(d ? &d->err : nullptr, "sd_decider_ask_all: null argument");
+  *response_json = nullptr;
+  try {
+    using namespace sd;
+    // `Request::from_json` (src/lib.rs:46-63)
+    const pj::Value req = pj::parse(request_json);
+    const pj::Value* state = req.get("state");
+    if (!state || !state->is_content()) throw std::runtime_error("state must be a string, object or array");
+    const pj::Value* images = req.get("images");
+    if (images && images->kind == pj::Value::Array && !images->arr.empty())
+      throw std::runtime_error("this engine has no vision tower; images are not supported");
+    const pj::Value* qs = req.get("questions");
+    if (!qs || qs->kind != pj::Value::Object || qs->obj.empty()) throw std::runtime_error("questions must be a non-empty object");
+    std::vector<std::pair<std::string, prompt::Question>> named;
+    for (const auto& kv : qs->obj) {
+      try {
+        named.emplace_back(kv.first, prompt::Question::from_json(kv.second));
+      } catch (const std::exception& e) {
+        throw std::runtime_error("question " + kv.first + ": " + e.what());
+      }
+    }
+    *response_json = dup_string(pj::dumps(d->run(*state, named)));
+    return SD_OK;
+  } catch (const std::exception& e) {
+    return host_fail(&d->err, e.what());
+  }
+}
+
+}  // extern "C"

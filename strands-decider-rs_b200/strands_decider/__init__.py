@@ -12,11 +12,12 @@ import time
 from dataclasses import dataclass, field
 
 from . import prompt
-from .engine import CONTEXT, Engine, Error, Head, Snapshot
+from .engine import CONTEXT, Engine, Error, Head, NativeDecider, Snapshot
 from .prompt import Answer, Question
 from .tokenizer import Tokenizer
 
-__all__ = ["Decider", "Question", "Answer", "Request", "Response", "Timings", "Engine", "Snapshot", "Error", "CONTEXT"]
+__all__ = ["Decider", "NativeDecider", "Question", "Answer", "Request", "Response", "Timings", "Engine", "Snapshot", "Error",
+           "CONTEXT"]
 
 MAX_BATCH = 32  # questions per batched fork; the reference's constant, which there only sets the token count (`src/lib.rs:107-108`)
 
@@ -61,7 +62,7 @@ class Response:
 
     def to_json(self) -> dict:
         """The System One response body (`src/lib.rs:78-87`)."""
-        return {"model": "strands-decider-b200",
+        return {"model": "strands-decider-rs-0.1.0",  # the reference's crate name and version (`Cargo.toml:2-3`)
                 "answers": {k: a.to_json() for k, a in self.answers},
                 "usage": {"input_tokens": self.input_tokens, "output_tokens": len(self.answers)}}
 

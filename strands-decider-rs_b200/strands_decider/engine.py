@@ -7,6 +7,7 @@ mirrors `src/head.rs`. There is no fallback: without the native library every ca
 from __future__ import annotations
 
 import ctypes as C
+import json
 import os
 from dataclasses import dataclass
 
@@ -76,6 +77,13 @@ def lib() -> C.CDLL:
         L.sd_qweight_create.argtypes = [vp, vp, i32, i32, i32, C.POINTER(vp)]
         L.sd_qweight_free.argtypes = [vp]
         L.sd_matmul.argtypes = [vp, vp, i32, vp, i32, i32, vp, C.c_size_t, vp]
+        L.sd_decider_load.argtypes = [cp, C.c_int, C.POINTER(vp)]
+        L.sd_decider_free.argtypes = [vp]
+        L.sd_decider_ask_all.argtypes = [vp, cp, C.POINTER(vp)]
+        L.sd_decider_last_error.argtypes = [vp]
+        L.sd_decider_last_error.restype = cp
+        L.sd_host_last_error.restype = cp
+        L.sd_string_free.argtypes = [vp]
         _lib = L
     return _lib
 
@@ -326,3 +334,34 @@ class QWeight:
                 lib().sd_qweight_free(self._h)
         except Exception:
             pass
+
+
+class NativeDecider:
+    """The Decider of the library itself (`sd_decider_*`: tokenizer, prompt, torso, head and answers in
+    C++), driven with System One JSON: `ask_all(request) -> response` as `Decider::evaluate` and
+    `Response::to_json` (`src/lib.rs:46-87,147-150`)."""
+
+    def __init__(self, handle: int):
+        self._h = handle
+
+    @classmethod
+    def load(cls, model_dir: str, device: int = 0) -> "NativeDecider":
+        h = C.c_void_p()
+        if lib().sd_decider_load(os.fsencode(model_dir), device, C.byref(h)) != SD_OK:
+            raise Error(f"Decider::load: {lib().sd_host_last_error().decode(errors='replace')}")
+        return cls(h.value)
+
+    def ask_all(self, request: dict) -> dict:
+        out = C.c_void_p()
+        L = lib()
+        if L.sd_decider_ask_all(self._h, json.dumps(request).encode(), C.byref(out)) != SD_OK:
+            raise Error(L.sd_decider_last_error(self._h).decode(errors="replace"))
+        try:
+            return json.loads(C.string_at(out.value).decode())
+        finally:
+            L.sd_string_free(out)
+
+    def close(self):
+        if self._h:
+            lib().sd_decider_free(self._h)
+            self._h = None
