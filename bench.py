@@ -8,12 +8,17 @@ state of 64-4096 random non-special token ids (clipped so state + longest questi
 runs as the reference's `Decider::run` does (src/lib.rs:185-198): the state once with a snapshot,
 then each question continued from the snapshot, hidden rows at the option tokens and the last token,
 then the pointer head. A step is a batch of --requests-per-step requests per GPU (weak scaling:
-each rank takes its own requests, no collective on the data path).
+each rank takes its own requests, no collective on the data path): the states of all of them in one
+packed pass, a snapshot each (sd_forward_batch), then their questions in one batched fork, each
+continuing its own request's snapshot (sd_forward_fork_multi), as a server answers concurrent
+requests.
 
 `value`: device-resident inputs (token ids and rows staged in HBM before the timed region),
-forwards queued with sd_forward_dev, hidden rows left in HBM; CUDA events on the engine's stream.
-`e2e`: the same requests through the C ABI with host buffers (sd_forward: ids host->device, hidden
-rows device->host, synchronous per call) and the pointer head on the host (sd_head_probs).
+passes queued with sd_forward_batch_dev / sd_forward_fork_multi_dev, hidden rows left in HBM; CUDA
+events on the engine's stream.
+`e2e`: the same requests through the C ABI with host buffers (sd_forward_batch / sd_forward_fork_multi:
+ids host->device, hidden rows device->host, synchronous per call) and the pointer head on the host
+(sd_head_probs).
 `roofline`: the dominant kernel (the dequantizing GEMM), from per-launch CUDA events on the engine's
 stream over a profiled pass of the same steps.
 """
@@ -87,17 +92,30 @@ class Clocks:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
+        # nvidia-smi takes a moment to start: wait (at most 10 s) for its first sample, which is taken
+        # before the timed region and dropped
+        self.skip = 0
+        t0 = time.time()
+        while self.p is not None and self.p.poll() is None and time.time() - t0 < 10:
+            if self._rows():
+                self.skip = len(self._rows())
+                break
+            time.sleep(0.05)
+
+    def _rows(self):
+        self.f.flush()
+        return [ln.split(",") for ln in open(self.f.name).read().strip().splitlines() if ln.count(",") >= 8]
 
     def stop(self) -> dict:
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
         self.p.wait()
-        self.f.flush()
-        rows = [ln.split(",") for ln in open(self.f.name).read().strip().splitlines() if ln.count(",") >= 8]
+        rows = self._rows()
+        rows = rows[self.skip:] or rows[-1:]  # the samples of the timed region (the last one if it was shorter)
         os.unlink(self.f.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
@@ -245,39 +263,60 @@ def run_ours(args, world, rank, local):
             staged[i] = (torch.from_numpy(sids.view(np.int32)).cuda(),
                          torch.from_numpy(np.concatenate([q for q, _ in qs]).view(np.int32)).cuda(),
                          [len(q) for q, _ in qs], [list(r) for _, r in qs])
-    hidden_dev = torch.empty((16, 2048), dtype=torch.float32, device="cuda")
+    # the states and the questions of a step's requests back to back in HBM, for the passes across requests
+    step_s, step_q = {}, {}
+    for s in range(steps_all + 1):
+        ii = step_requests(s, rank, world, per)
+        step_s[s] = torch.cat([staged[i][0] for i in ii])
+        step_q[s] = torch.cat([staged[i][1] for i in ii])
+    hidden_dev = torch.empty((per * 12, 2048), dtype=torch.float32, device="cuda")
+    # working memory for the largest pass of any step, up front (as a server sizes it at start-up)
+    eng.reserve(max(max(t.numel() for t in step_s.values()), max(t.numel() for t in step_q.values())), per * 3, per * 12)
     torch.cuda.synchronize()
 
     # a request as the Decider runs it (`Decider::run`, src/lib.rs:156-208): the state once, kept as
-    # a snapshot, then its questions continued from the snapshot in one batched fork
+    # a snapshot, then its questions continued from the snapshot. The states of all the step's
+    # requests run as one packed pass (sd_forward_batch, a snapshot each), then their questions as
+    # one batched fork (each continuing its own request's snapshot)
     def one_step_dev(s):
-        n_q = n_tok = 0
-        for i in step_requests(s, rank, world, per):
-            sd, qd, lens, rows = staged[i]
-            snap = eng.forward_dev(sd.data_ptr(), sd.numel(), None, 0, keep=True)
-            eng.forward_fork_dev(snap, qd.data_ptr(), lens, rows, hidden_dev.data_ptr())
-            n_q += len(lens)
-            n_tok += sd.numel() + qd.numel()
+        ii = step_requests(s, rank, world, per)
+        slens = [staged[i][0].numel() for i in ii]
+        snaps = eng.forward_batch_dev(None, step_s[s].data_ptr(), slens, [[]] * len(ii), None, keep=True)
+        caches, lens, rows = [], [], []
+        n_tok = sum(slens)
+        for i, snap in zip(ii, snaps):
+            _, qd, ql, qr = staged[i]
+            caches += [snap] * len(ql)
+            lens += ql
+            rows += qr
+            n_tok += qd.numel()
+        eng.forward_fork_dev(caches, step_q[s].data_ptr(), lens, rows, hidden_dev.data_ptr())
+        for snap in snaps:
             snap.close()
-        return n_q, n_tok
+        return len(lens), n_tok
 
     h2d = d2h = 0
 
     def one_step_host(s):
         nonlocal h2d, d2h
-        n_q = 0
-        for i in step_requests(s, rank, world, per):
-            sids, qs = reqs[i]
-            snap = eng.forward(sids, [], keep=True).snapshot
-            h2d += sids.nbytes
-            outs = eng.forward_fork(snap, [q for q, _ in qs], [r for _, r in qs])
-            for (qids, rows), hidden in zip(qs, outs):
-                head.probs(hidden, 2048, 1.0)
-                h2d += qids.nbytes + rows.nbytes
-                d2h += hidden.nbytes
-                n_q += 1
+        ii = step_requests(s, rank, world, per)
+        states = [reqs[i][0] for i in ii]
+        _, snaps = eng.forward_batch(None, states, [[]] * len(ii), keep=True)
+        h2d += sum(x.nbytes for x in states)
+        caches, qids, qrows = [], [], []
+        for i, snap in zip(ii, snaps):
+            qs = reqs[i][1]
+            caches += [snap] * len(qs)
+            qids += [q for q, _ in qs]
+            qrows += [r for _, r in qs]
+        outs = eng.forward_fork(caches, qids, qrows)
+        for q, r, hidden in zip(qids, qrows, outs):
+            head.probs(hidden, 2048, 1.0)
+            h2d += q.nbytes + r.nbytes
+            d2h += hidden.nbytes
+        for snap in snaps:
             snap.close()
-        return n_q
+        return len(outs)
 
     def timed(fn, first, count):
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -343,7 +382,7 @@ def run_ours(args, world, rank, local):
                    "parallelism": f"replicas x{world} (requests sharded, no collective)"},
         "prefill_tok_s": tok_all / t_dev,
         "e2e": {"value": qh_all / t_host, "unit": "questions/s", "h2d_bytes_per_step": int(h2d_step),
-                "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward (state, kept) + sd_forward_fork (the questions; host ids in, host hidden rows out) + sd_head_probs"},
+                "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward_batch (the step's states, one snapshot each) + sd_forward_fork_multi (the step's questions, each from its request's snapshot; host ids in, host hidden rows out) + sd_head_probs"},
         "gpu_launches": int(launches),
         "roofline": {"kernel": "gemm_q4_tc (dequantizing tcgen05 GEMM)", "bound": "tensor", "achieved": gemm_tflops,
                      "peak": tf_sus, "unit": "TFLOP/s", "frac": gemm_tflops / tf_sus,
@@ -456,7 +495,7 @@ def run_kernel_workload(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--requests-per-step", type=int, default=8)

@@ -37,6 +37,11 @@ typedef struct sd_qweight sd_qweight;
  * weight shards and the embedding rows of a model directory onto GPU `device`. */
 int sd_engine_create(const char* model_dir, int device, sd_engine** out);
 void sd_engine_destroy(sd_engine* e);
+/* Sizes the engine's working memory (activations, staging, pinned buffers) for passes of up to
+ * max_tokens tokens, max_seqs sequences and max_rows hidden rows, so that no later call within those
+ * bounds allocates (an allocation waits for the engine's queued work). A server calls it once at
+ * start-up; without it the buffers grow on demand. */
+int sd_engine_reserve(sd_engine* e, int32_t max_tokens, int32_t max_seqs, int32_t max_rows);
 /* `Engine::hidden_size` (`src/engine.rs:305-307`). */
 int sd_engine_hidden_size(const sd_engine* e);
 const char* sd_engine_last_error(const sd_engine* e);
@@ -66,6 +71,30 @@ int sd_forward_fork(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids,
  * at the next sd_engine_synchronize. */
 int sd_forward_fork_dev(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids_dev, const int32_t* lens, int32_t nq,
                         const int32_t* rows, const int32_t* nrows, float* hidden_dev);
+/* The batched fork across requests: question b continues caches[b] (any snapshots of this engine,
+ * of any lengths; several questions may share one), so the questions of many `Decider::ask_all`
+ * calls run as one pass, which is how a server answers concurrent requests. Otherwise as
+ * sd_forward_fork / sd_forward_fork_dev (at most 4096 questions and 65536 tokens per call). */
+int sd_forward_fork_multi(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids, const int32_t* lens,
+                          int32_t nq, const int32_t* rows, const int32_t* nrows, float* hidden_out, double* gpu_ms_out);
+int sd_forward_fork_multi_dev(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids_dev, const int32_t* lens,
+                              int32_t nq, const int32_t* rows, const int32_t* nrows, float* hidden_dev);
+/* Many `Engine::forward` calls in one pass: sequence b is lens[b] new tokens continuing caches[b]
+ * (NULL entry, or a NULL caches array: a fresh sequence, as `Engine::forward(.., None, ..)`), its
+ * rows (nrows[b] of them, indices into its own tokens) written to hidden_out in order; with `keep`,
+ * snapshots_out[b] receives a snapshot covering caches[b]'s tokens and these (free each with
+ * sd_snapshot_free). The results equal nseq separate sd_forward calls up to f32 summation order;
+ * the source snapshots are read and not changed. This is how a server prefills the states of
+ * concurrent requests: the GEMMs see every sequence's rows at once, and the gated-delta scans and
+ * attention of all sequences run side by side. At most 4096 sequences and 65536 tokens per call. */
+int sd_forward_batch(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids, const int32_t* lens, int32_t nseq,
+                     const int32_t* rows, const int32_t* nrows, int32_t keep, float* hidden_out, sd_snapshot** snapshots_out,
+                     double* gpu_ms_out);
+/* sd_forward_batch with the ids on the GPU and the rows to hidden_dev, asynchronous on the engine's
+ * stream (the new snapshots are returned at once and usable by later calls on the engine). */
+int sd_forward_batch_dev(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids_dev, const int32_t* lens,
+                         int32_t nseq, const int32_t* rows, const int32_t* nrows, int32_t keep, float* hidden_dev,
+                         sd_snapshot** snapshots_out);
 
 /* `Snapshot::len` (`src/engine.rs:80-87`): tokens covered. A snapshot is immutable and can seed
  * any number of forwards on the engine that made it; free it with sd_snapshot_free. */
@@ -124,6 +153,12 @@ void sd_decider_free(sd_decider* d);
  * *response_json, a NUL-terminated string the caller frees with sd_string_free. Several questions
  * share one encoding of the state: a snapshot, then one batched fork per 32 questions. */
 int sd_decider_ask_all(sd_decider* d, const char* request_json, char** response_json);
+/* Many requests at once (a JSON array of requests as sd_decider_ask_all takes them), as a server
+ * answers concurrent ones: the requests' states in packed passes (sd_forward_batch), then all their
+ * questions in packed forks (sd_forward_fork_multi). Writes a JSON array in the same order: each
+ * request's response body, equal to its own sd_decider_ask_all up to f32 summation order, or
+ * {"error": message} for a request that failed. The call itself fails only on a malformed array. */
+int sd_decider_ask_batch(sd_decider* d, const char* requests_json, char** responses_json);
 const char* sd_decider_last_error(const sd_decider* d);
 const char* sd_host_last_error(void);
 void sd_string_free(char* s);

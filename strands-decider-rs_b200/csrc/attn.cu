@@ -76,6 +76,12 @@ __global__ void __launch_bounds__(128, 2)
     t0 = pk.blk[2 * blockIdx.x + 1];
     nq = min(BQ, pk.seq_len[sq] - t0);
     tok0 = pk.seq_off[sq] + t0;
+    if (pk.kp) {  // this sequence's own prefix: its length and its K/V rows
+      p = pk.plen[sq];
+      lt = p;
+      k = pk.kp[sq];
+      v = pk.vp[sq];
+    }
   } else {
     t0 = (gridDim.x - 1 - blockIdx.x) * BQ;  // longest (latest) query blocks first
     nq = min(BQ, l - t0);
@@ -110,9 +116,9 @@ __global__ void __launch_bounds__(128, 2)
       const bool ok = j < kend;
       const __half *ks = k, *vs = v;
       size_t off = ((size_t)kh * lt + (ok ? j : 0)) * HD + c8;
-      if (pk.blk && ok && j >= p) {  // this sequence's own keys
+      if (pk.blk && j >= p) {  // this sequence's own keys (past the last one: row 0 of the tails, not read)
         ks = pk.kt, vs = pk.vt;
-        off = ((size_t)kh * pk.T + tail0 + j) * HD + c8;
+        off = ((size_t)kh * pk.T + (ok ? tail0 + j : 0)) * HD + c8;
       }
       cp_async16(smem_u32(dk + r * LDS + c8), ks + off, ok);
       cp_async16(smem_u32(dv + r * LDS + c8), vs + off, ok);

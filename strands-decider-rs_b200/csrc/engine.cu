@@ -586,17 +586,33 @@ cudaError_t launch(sd_engine* e, int kind, double units, F&& fn) {
     if (_e != cudaSuccess) return e->fail(SD_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_e));      \
   } while (0)
 
-// A batched fork (sd_forward_fork): several sequences packed back to back, each continuing the
-// snapshot `snap`, whose states and prefix K/V are read in place and never written. Device arrays:
-// tpos (position of each packed token), tstart (first token of each token's sequence), seq_off /
-// seq_len per sequence, blk (sequence, first query) per 64-query attention block.
+// A packed pass (sd_forward_batch and the batched forks built on it): several sequences back to back,
+// sequence b continuing snapshot b (the same one for every question of one request, one per request
+// when several requests run together, or none: a fresh sequence), whose states, conv histories and
+// prefix K/V are read in place and never written; with `keep`, each sequence's new state, history
+// and K/V go to a new snapshot of its own. Device arrays: per-layer tables of each sequence's
+// snapshot buffers (null entries: no source snapshot); tpos (position of each packed token), tstart
+// (first token of each token's sequence), tseq (its sequence); seq_off / seq_len / plen (prefix
+// length) per sequence; blk (sequence, first query) per 64-query attention block; for the two-phase
+// scan of long sequences, chunk_tab (first token, tokens) per 64-token chunk, chunk0 (first chunk)
+// per sequence and order (sequences, longest first).
 struct Fork {
-  const sd_snapshot* snap;
   const uint32_t* ids;  // [l] token ids
   const int* rows;      // output rows (indices into the packed tokens)
-  const int *tpos, *tstart, *seq_off, *seq_len, *blk;
-  int nseq, nblk, max_len;
-  double tail_pairs;  // sum over sequences of len (len + 1) / 2: causal pairs among their own tokens
+  const float* const* states;   // [n_lin][nseq] GDN states
+  const __half* const* hists;   // [n_lin][nseq] conv histories
+  const __half* const* kp;      // [n_full][nseq] prefix keys ([hk][plen][hd])
+  const __half* const* vp;      // [n_full][nseq] prefix values
+  // keep: the new snapshots' buffers, [n_lin][nseq] / [n_full][nseq] (null: nothing kept)
+  float* const* s_out = nullptr;
+  __half* const* h_out = nullptr;
+  __half* const* k_out = nullptr;
+  __half* const* v_out = nullptr;
+  const int *tpos, *tstart, *tseq, *seq_off, *seq_len, *plen, *blk;
+  const int *chunk_tab = nullptr, *chunk0 = nullptr, *order = nullptr;
+  int nseq, nblk, max_len, max_p, max_rows, chunks = 0;
+  bool two_phase = false;
+  double pairs;       // causal (query, key) pairs of every sequence: len p + len (len + 1) / 2
   __half *kt, *vt;    // [hk][l][hd] K and V of the packed tokens
 };
 
@@ -631,22 +647,36 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
     } else {
       if (Lw.kind == 0) {
         const int N = Lw.in_proj.n;
-        __half* hist = fk ? fk->snap->hist[Lw.slot] : e->hist[Lw.slot];
+        __half* hist = fk ? nullptr : e->hist[Lw.slot];
         MM(Lw.in_proj, e->h, d.d, e->big, N, false);
         LK(SD_PROF_OTHER, L * C * 4.0,
-           sd::launch_conv(e->big, N, Lw.conv, hist, l, C, e->qkvc, fk ? fk->tstart : nullptr, st));
+           sd::launch_conv(e->big, N, Lw.conv, hist, l, C, e->qkvc, fk ? fk->tstart : nullptr,
+                           fk ? fk->hists + (size_t)Lw.slot * fk->nseq : nullptr, fk ? fk->tseq : nullptr, st));
         if (!fk) LK(SD_PROF_OTHER, C * 12.0, sd::launch_hist_update(e->big, N, hist, l, C, st));
+        else if (fk->h_out)
+          LK(SD_PROF_OTHER, fk->nseq * C * 12.0,
+             sd::launch_hist_pack(e->big, N, C, fk->seq_off, fk->seq_len, fk->hists + (size_t)Lw.slot * fk->nseq,
+                                  fk->h_out + (size_t)Lw.slot * fk->nseq, fk->nseq, st));
         const int aoff = C + d.h * d.dv, boff = aoff + d.h;
         LK(SD_PROF_OTHER, L * d.h * 12.0,
            sd::launch_gdn_gates(e->big, N, aoff, boff, Lw.neg_a, Lw.dt_bias, l, d.h, e->beta, e->decay, st));
         const double gdn_bytes = L * (C * 2.0 + d.h * 8.0 + d.h * d.dv * 4.0) + 2.0 * d.h * d.dk * d.dv * 4.0;
         // one chunk: the single-pass scan; longer: the two-phase scan (chunks in parallel, then the state walk);
-        // a fork: the single-pass scan over every sequence, from the snapshot's state
-        if (fk)
+        // packed sequences, each from its snapshot's state (or zeros): short ones with the single-pass
+        // scan, long ones with the two-phase scan
+        if (fk && fk->two_phase)
+          LK(SD_PROF_GDN, gdn_bytes,
+             (*nl = 2, sd::launch_gdn_two_phase_packed(
+                           e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, e->beta, e->decay,
+                           fk->states + (size_t)Lw.slot * fk->nseq, fk->s_out ? fk->s_out + (size_t)Lw.slot * fk->nseq : nullptr,
+                           e->of, fk->seq_off, fk->seq_len, fk->chunk0, fk->order, fk->chunk_tab, fk->nseq, fk->chunks, d.h,
+                           e->gdn_scratch, e->gdn_scratch_bytes, st)));
+        else if (fk)
           LK(SD_PROF_GDN, gdn_bytes,
              sd::launch_gdn_chunked_packed(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, e->beta,
-                                           e->decay, fk->snap->state[Lw.slot], e->of, fk->seq_off, fk->seq_len, fk->nseq,
-                                           d.h, st));
+                                           e->decay, fk->states + (size_t)Lw.slot * fk->nseq,
+                                           fk->s_out ? fk->s_out + (size_t)Lw.slot * fk->nseq : nullptr, e->of, fk->seq_off,
+                                           fk->seq_len, fk->nseq, d.h, st));
         else if (l <= 64)
           LK(SD_PROF_GDN, gdn_bytes,
              sd::launch_gdn_chunked(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, 0, 0, true, e->beta,
@@ -664,15 +694,21 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
         if (fk) {
           LK(SD_PROF_OTHER, L * (N * 2.0 + (d.hq + 2.0 * d.hk) * d.hd * 2.0),
              sd::launch_qk_prep(e->big, N, Lw.q_norm, Lw.k_norm, e->rope, l, p, l, d, fk->tpos, e->q, fk->kt, fk->vt, st));
-          const double pairs = L * p + fk->tail_pairs;  // causal (query, key) pairs of every sequence
           sd::AttnPacked pk;
           pk.blk = fk->blk, pk.seq_off = fk->seq_off, pk.seq_len = fk->seq_len, pk.kt = fk->kt, pk.vt = fk->vt, pk.T = l;
-          int splits = sd::attention_splits_packed(fk->nblk, p, fk->max_len, d.hq, e->num_sms);
+          pk.kp = fk->kp + (size_t)Lw.slot * fk->nseq, pk.vp = fk->vp + (size_t)Lw.slot * fk->nseq, pk.plen = fk->plen;
+          int splits = sd::attention_splits_packed(fk->nblk, fk->max_p, fk->max_len, d.hq, e->num_sms);
           while (splits > 1 && sd::attention_split_bytes(l, d.hq, splits) > e->ws_bytes) splits--;
-          LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * pairs,
+          LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * fk->pairs,
              (*nl = splits > 1 ? 2 : 1,
-              sd::launch_attention_packed(e->q, fk->snap->k[Lw.slot], fk->snap->v[Lw.slot], e->big, N, d.hd, 2 * d.hd, e->o,
-                                          l, p, p, d.hq, d.hk, d.hd, pk, fk->nblk, splits, e->ws, e->ws_bytes, st)));
+              sd::launch_attention_packed(e->q, nullptr, nullptr, e->big, N, d.hd, 2 * d.hd, e->o, l, fk->max_p, fk->max_p,
+                                          d.hq, d.hk, d.hd, pk, fk->nblk, splits, e->ws, e->ws_bytes, st)));
+          if (fk->k_out)  // the sequences' keys and values (prefix and own) into their new snapshots
+            LK(SD_PROF_OTHER, 8.0 * d.hk * d.hd * (L + fk->max_p),
+               sd::launch_kv_pack(fk->kt, fk->vt, l, d.hk, d.hd, fk->seq_off, fk->seq_len, fk->plen,
+                                  fk->kp + (size_t)Lw.slot * fk->nseq, fk->vp + (size_t)Lw.slot * fk->nseq,
+                                  fk->k_out + (size_t)Lw.slot * fk->nseq, fk->v_out + (size_t)Lw.slot * fk->nseq, fk->nseq,
+                                  fk->max_rows, st));
           MM(Lw.o_proj, e->o, d.hq * d.hd, e->y, d.d, false);
         } else {
         LK(SD_PROF_OTHER, L * (N * 2.0 + (d.hq + 2.0 * d.hk) * d.hd * 2.0),
@@ -703,6 +739,26 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
   return SD_OK;
 }
 
+// A new snapshot of T tokens (uninitialised), one stream-ordered allocation from the engine's pool.
+int alloc_snapshot(sd_engine* e, int T, std::unique_ptr<sd_snapshot>* out) {
+  const sd::Dims& d = e->dm;
+  const size_t state_bytes = (size_t)d.h * d.dk * d.dv * 4, hist_bytes = (size_t)3 * d.C() * 2;
+  const size_t kv_bytes = (size_t)d.hk * T * d.hd * 2;
+  const size_t total = e->n_lin * (state_bytes + hist_bytes) + 2 * e->n_full * kv_bytes;
+  std::unique_ptr<sd_snapshot> snap(new sd_snapshot());
+  snap->device = e->device;
+  snap->len = T;
+  CK(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&snap->base), std::max<size_t>(total, 256), e->snap_pool, e->stream));
+  snap->owner = e;
+  uint8_t* q = snap->base;
+  for (int i = 0; i < e->n_lin; i++, q += state_bytes) snap->state.push_back(reinterpret_cast<float*>(q));
+  for (int i = 0; i < e->n_lin; i++, q += hist_bytes) snap->hist.push_back(reinterpret_cast<__half*>(q));
+  for (int i = 0; i < e->n_full; i++, q += kv_bytes) snap->k.push_back(reinterpret_cast<__half*>(q));
+  for (int i = 0; i < e->n_full; i++, q += kv_bytes) snap->v.push_back(reinterpret_cast<__half*>(q));
+  *out = std::move(snap);
+  return SD_OK;
+}
+
 // Restores the prefix or clears the conv history (src/engine.rs:552-571), runs the layers and, with
 // `keep`, copies the state into a new snapshot (src/engine.rs:592-614). Everything is enqueued on the
 // engine's stream; e->d_ids and e->d_rows hold this call's inputs.
@@ -730,18 +786,8 @@ int forward_core(sd_engine* e, int l, const sd_snapshot* cache, int nrows, bool 
   if (rc != SD_OK) return rc;
   if (keep) {
     const int T = p + l;
-    const size_t kv_bytes = (size_t)d.hk * T * row_bytes;
-    const size_t total = e->n_lin * (state_bytes + hist_bytes) + 2 * e->n_full * kv_bytes;
-    std::unique_ptr<sd_snapshot> snap(new sd_snapshot());
-    snap->device = e->device;
-    snap->len = T;
-    CK(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&snap->base), std::max<size_t>(total, 256), e->snap_pool, st));
-    snap->owner = e;
-    uint8_t* q = snap->base;
-    for (int i = 0; i < e->n_lin; i++, q += state_bytes) snap->state.push_back(reinterpret_cast<float*>(q));
-    for (int i = 0; i < e->n_lin; i++, q += hist_bytes) snap->hist.push_back(reinterpret_cast<__half*>(q));
-    for (int i = 0; i < e->n_full; i++, q += kv_bytes) snap->k.push_back(reinterpret_cast<__half*>(q));
-    for (int i = 0; i < e->n_full; i++, q += kv_bytes) snap->v.push_back(reinterpret_cast<__half*>(q));
+    std::unique_ptr<sd_snapshot> snap;
+    if ((rc = alloc_snapshot(e, T, &snap)) != SD_OK) return rc;
     for (int i = 0; i < e->n_lin; i++) {
       CK(cudaMemcpyAsync(snap->state[i], e->state[i], state_bytes, cudaMemcpyDeviceToDevice, st));
       CK(cudaMemcpyAsync(snap->hist[i], e->hist[i], hist_bytes, cudaMemcpyDeviceToDevice, st));
@@ -769,83 +815,34 @@ int check_forward_args(sd_engine* e, int l, int nrows, const sd_snapshot* cache,
   return SD_OK;
 }
 
-// Validates a batched fork and enqueues it on the engine's stream: one upload (through a pinned ring
-// slot) carries the index arrays (tpos, tstart, seq_off, seq_len, blk), the global rows and, from the
-// host, the ids; ids already on the device are read in place. Then the layers. `timed` brackets the
-// layers with the engine's events. *R_out: rows.
-int fork_enqueue(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids_host, const uint32_t* ids_dev,
-                 const int32_t* lens, int32_t nq, const int32_t* rows, const int32_t* nrows, bool has_out, bool timed,
-                 long long* R_out) {
-  if (!cache) return e->fail(SD_ERR_INVALID, "sd_forward_fork: no snapshot (the questions continue one)");
-  if (cache->owner != e) return e->fail(SD_ERR_INVALID, "snapshot belongs to another engine");
-  if (nq <= 0 || (!ids_host && !ids_dev) || !lens || !nrows) return e->fail(SD_ERR_INVALID, "sd_forward_fork: no questions");
-  if (e->trace_host) return e->fail(SD_ERR_INVALID, "sd_forward_fork: per-layer tracing is for sd_forward only");
-  const int p = cache->len;
-  long long T = 0, R = 0;
-  int max_len = 0, nblk = 0;
-  double tail_pairs = 0;
-  for (int b = 0; b < nq; b++) {
-    if (lens[b] <= 0 || p + lens[b] > SD_CONTEXT)
-      return e->fail(SD_ERR_INVALID, "question %d: context of %d tokens: must be %d to %d", b, p + lens[b], p + 1, SD_CONTEXT);
-    if (nrows[b] < 0) return e->fail(SD_ERR_INVALID, "question %d: negative row count", b);
-    T += lens[b];
-    R += nrows[b];
-    max_len = std::max(max_len, (int)lens[b]);
-    tail_pairs += (double)lens[b] * (lens[b] + 1) / 2;
-    nblk += (lens[b] + 63) / 64;
-  }
-  if (T > (1 << 16)) return e->fail(SD_ERR_INVALID, "sd_forward_fork: %lld tokens in one call (at most 65536)", T);
-  if (R > 0 && (!rows || !has_out)) return e->fail(SD_ERR_INVALID, "rows given without an output buffer");
-  if (ids_host)
-    for (long long i = 0; i < T; i++)
-      if (ids_host[i] >= (uint32_t)e->vocab)
-        return e->fail(SD_ERR_INVALID, "token id %u out of range (vocab %d)", ids_host[i], e->vocab);
-  // staged layout (ints): tpos[T], tstart[T], seq_off[nq], seq_len[nq], blk[2 nblk], rows[R], ids[T] (host ids)
-  const size_t n_idx = 2 * (size_t)T + 2 * (size_t)nq + 2 * (size_t)nblk;
-  const size_t n_all = n_idx + (size_t)R + (ids_host ? (size_t)T : 0);
-  cudaSetDevice(e->device);
-  int rc;
-  if ((rc = ensure_pool(e, (int)T)) != SD_OK) return rc;
+// Staged ints of a packed pass (pointer tables as two ints a pointer, index arrays, rows, the two-phase
+// scan's tables when chunks >= 0, host ids).
+size_t packed_ints(const sd_engine* e, long long T, long long nq, long long nblk, long long R, bool keep, long long chunks,
+                   bool host_ids) {
+  const size_t per_set = (size_t)(2 * e->n_lin + 2 * e->n_full) * nq;
+  return 2 * per_set * (keep ? 2 : 1) + 3 * (size_t)T + 3 * (size_t)nq + 2 * (size_t)nblk + (size_t)R +
+         (chunks >= 0 ? 2 * (size_t)chunks + 2 * (size_t)nq : 0) + (host_ids ? (size_t)T : 0);
+}
+
+// Grows the packed pass's device buffers (staged index arrays, the packed tokens' K/V, the two-phase
+// scan's records) to hold a pass of T tokens, `ints` staged ints and `chunks` records per head, by at
+// least a quarter at a time. A resize first waits for the queued work that may use the old buffers.
+int ensure_packed(sd_engine* e, long long T, size_t ints, long long chunks) {
   const sd::Dims& d = e->dm;
   cudaStream_t st = e->stream;
-  const int slot = e->fk_next;
-  e->fk_next = (slot + 1) % sd_engine::kForkSlots;
-  if (e->fk_ev[slot]) CK(cudaEventSynchronize(e->fk_ev[slot]));  // its previous upload is done
-  else CK(cudaEventCreateWithFlags(&e->fk_ev[slot], cudaEventDisableTiming));
-  if (e->fk_pin_ints[slot] < n_all) {
-    cudaFreeHost(e->fk_pin[slot]);
-    e->fk_pin[slot] = nullptr, e->fk_pin_ints[slot] = 0;
-    const size_t cap = std::max<size_t>(n_all, 8192);
-    CK(cudaMallocHost(&e->fk_pin[slot], cap * sizeof(int)));
-    e->fk_pin_ints[slot] = cap;
+  if (chunks > 0 && e->gdn_scratch_bytes < sd::gdn_two_phase_packed_scratch((int)chunks, d.h)) {
+    CK(cudaStreamSynchronize(st));
+    cudaFree(e->gdn_scratch);
+    const size_t bytes = std::max(sd::gdn_two_phase_packed_scratch((int)chunks, d.h), e->gdn_scratch_bytes * 5 / 4);
+    e->gdn_scratch = nullptr, e->gdn_scratch_bytes = 0;
+    CK(cudaMalloc(&e->gdn_scratch, bytes));
+    e->gdn_scratch_bytes = bytes;
   }
-  int* tpos = e->fk_pin[slot];
-  int* tstart = tpos + T;
-  int* soff = tstart + T;
-  int* slen = soff + nq;
-  int* blk = slen + nq;
-  int* grows = tpos + n_idx;
-  {
-    int t = 0, k = 0;
-    long long r = 0;
-    for (int b = 0; b < nq; b++) {
-      soff[b] = t, slen[b] = lens[b];
-      for (int j = 0; j < lens[b]; j++) tpos[t + j] = p + j, tstart[t + j] = t;
-      for (int q0 = 0; q0 < lens[b]; q0 += 64, k++) blk[2 * k] = b, blk[2 * k + 1] = q0;
-      for (int j = 0; j < nrows[b]; j++, r++) {
-        if (rows[r] < 0 || rows[r] >= lens[b])
-          return e->fail(SD_ERR_INVALID, "question %d: row %d out of range for %d tokens", b, rows[r], lens[b]);
-        grows[r] = t + rows[r];
-      }
-      t += lens[b];
-    }
-  }
-  if (ids_host) memcpy(grows + R, ids_host, T * sizeof(uint32_t));
-  if (e->fk_meta_ints < n_all) {
-    CK(cudaStreamSynchronize(st));  // the old arrays may still be read by queued work
+  if (e->fk_meta_ints < ints) {
+    CK(cudaStreamSynchronize(st));
     cudaFree(e->fk_meta);
+    const size_t cap = std::max<size_t>({ints, e->fk_meta_ints * 5 / 4, 32768});
     e->fk_meta = nullptr, e->fk_meta_ints = 0;
-    const size_t cap = std::max<size_t>(n_all, 8192);
     CK(cudaMalloc(&e->fk_meta, cap * sizeof(int)));
     e->fk_meta_ints = cap;
   }
@@ -853,25 +850,252 @@ int fork_enqueue(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids_hos
   if (e->fk_kv_halves < kv) {
     CK(cudaStreamSynchronize(st));
     cudaFree(e->fk_kv);
+    const size_t cap = std::max<size_t>({kv, e->fk_kv_halves * 5 / 4, (size_t)2 * d.hk * 1024 * d.hd});
     e->fk_kv = nullptr, e->fk_kv_halves = 0;
-    const size_t cap = std::max<size_t>(kv, (size_t)2 * d.hk * 1024 * d.hd);
     CK(cudaMalloc(&e->fk_kv, cap * sizeof(__half)));
     e->fk_kv_halves = cap;
   }
+  return SD_OK;
+}
+
+// Grows pinned staging slot `slot` to `ints` ints, after its previous upload (event) is done.
+int ensure_pin_slot(sd_engine* e, int slot, size_t ints) {
+  if (e->fk_ev[slot]) CK(cudaEventSynchronize(e->fk_ev[slot]));
+  else CK(cudaEventCreateWithFlags(&e->fk_ev[slot], cudaEventDisableTiming));
+  if (e->fk_pin_ints[slot] < ints) {
+    cudaFreeHost(e->fk_pin[slot]);
+    const size_t cap = std::max<size_t>({ints, e->fk_pin_ints[slot] * 5 / 4, 32768});
+    e->fk_pin[slot] = nullptr, e->fk_pin_ints[slot] = 0;
+    CK(cudaMallocHost(&e->fk_pin[slot], cap * sizeof(int)));
+    e->fk_pin_ints[slot] = cap;
+  }
+  return SD_OK;
+}
+
+// Validates a packed pass and enqueues it on the engine's stream: one upload (through a pinned ring
+// slot) carries the per-layer tables of each sequence's snapshot buffers (and of its new snapshot,
+// with `keep`), the index arrays, the global rows and, from the host, the ids; ids already on the
+// device are read in place. Then the layers. caches: one per sequence, entries may be null (a fresh
+// sequence; the whole array may be null); `fork` names the call in errors and requires every
+// sequence to continue a snapshot. `timed` brackets the layers with the engine's events. *R_out: rows;
+// snaps_out (with keep): the new snapshots.
+int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* caches, bool fork, const uint32_t* ids_host,
+                   const uint32_t* ids_dev, const int32_t* lens, int32_t nq, const int32_t* rows, const int32_t* nrows,
+                   bool keep, sd_snapshot** snaps_out, bool has_out, bool timed, long long* R_out) {
+  if (nq <= 0 || (!ids_host && !ids_dev) || !lens || !nrows) return e->fail(SD_ERR_INVALID, "%s: no sequences", fn);
+  if (nq > 4096) return e->fail(SD_ERR_INVALID, "%s: %d sequences in one call (at most 4096)", fn, nq);
+  if (e->trace_host) return e->fail(SD_ERR_INVALID, "%s: per-layer tracing is for sd_forward only", fn);
+  if (keep && !snaps_out) return e->fail(SD_ERR_INVALID, "%s: keep without a snapshot output", fn);
+  long long T = 0, R = 0;
+  int max_len = 0, max_p = 0, max_rows = 0, nblk = 0, chunks = 0, max_chunks = 0;
+  double pairs = 0;
+  for (int b = 0; b < nq; b++) {
+    const sd_snapshot* c = caches ? caches[b] : nullptr;
+    if (!c && fork) return e->fail(SD_ERR_INVALID, "%s: question %d has no snapshot (the questions continue one)", fn, b);
+    if (c && c->owner != e) return e->fail(SD_ERR_INVALID, "snapshot belongs to another engine");
+    const int p = c ? c->len : 0;
+    if (lens[b] <= 0 || p + lens[b] > SD_CONTEXT)
+      return e->fail(SD_ERR_INVALID, "sequence %d: context of %d tokens: must be %d to %d", b, p + lens[b], p + 1, SD_CONTEXT);
+    if (nrows[b] < 0) return e->fail(SD_ERR_INVALID, "sequence %d: negative row count", b);
+    T += lens[b];
+    R += nrows[b];
+    max_len = std::max(max_len, (int)lens[b]);
+    max_p = std::max(max_p, p);
+    max_rows = std::max(max_rows, p + (int)lens[b]);
+    pairs += (double)lens[b] * p + (double)lens[b] * (lens[b] + 1) / 2;
+    nblk += (lens[b] + 63) / 64;
+    chunks += (lens[b] + 63) / 64;
+    max_chunks = std::max(max_chunks, ((int)lens[b] + 63) / 64);
+  }
+  if (T > (1 << 16)) return e->fail(SD_ERR_INVALID, "%s: %lld tokens in one call (at most 65536)", fn, T);
+  if (R > 0 && (!rows || !has_out)) return e->fail(SD_ERR_INVALID, "rows given without an output buffer");
+  if (ids_host)
+    for (long long i = 0; i < T; i++)
+      if (ids_host[i] >= (uint32_t)e->vocab)
+        return e->fail(SD_ERR_INVALID, "token id %u out of range (vocab %d)", ids_host[i], e->vocab);
+  // long sequences (more than two 64-token chunks): the two-phase scan
+  const bool two_phase = max_chunks > 2;
+  // staged layout: pointer tables (8-byte words): states[n_lin][nq], hists[n_lin][nq], k[n_full][nq],
+  // v[n_full][nq], with keep the same four for the new snapshots; then ints: tpos[T], tstart[T],
+  // tseq[T], seq_off[nq], seq_len[nq], plen[nq], blk[2 nblk], rows[R], with the two-phase scan
+  // chunk_tab[2 chunks], chunk0[nq], order[nq]; then ids[T] (host ids)
+  const size_t per_set = (size_t)(2 * e->n_lin + 2 * e->n_full) * nq;
+  const size_t i0 = 2 * per_set * (keep ? 2 : 1);  // ints before the index arrays
+  const size_t n_idx = i0 + 3 * (size_t)T + 3 * (size_t)nq + 2 * (size_t)nblk;
+  const size_t n_gdn = two_phase ? 2 * (size_t)chunks + 2 * (size_t)nq : 0;
+  const size_t n_all = packed_ints(e, T, nq, nblk, R, keep, two_phase ? chunks : -1, ids_host != nullptr);
+  {  // rows in range
+    long long r = 0;
+    for (int b = 0; b < nq; b++)
+      for (int j = 0; j < nrows[b]; j++, r++)
+        if (rows[r] < 0 || rows[r] >= lens[b])
+          return e->fail(SD_ERR_INVALID, "sequence %d: row %d out of range for %d tokens", b, rows[r], lens[b]);
+  }
+  cudaSetDevice(e->device);
+  int rc;
+  if ((rc = ensure_pool(e, (int)T)) != SD_OK || (rc = ensure_packed(e, T, n_all, two_phase ? chunks : 0)) != SD_OK) return rc;
+  const sd::Dims& d = e->dm;
+  cudaStream_t st = e->stream;
+  // the new snapshots (stream-ordered allocations, before the upload that names them)
+  std::vector<std::unique_ptr<sd_snapshot>> fresh;
+  if (keep) {
+    fresh.resize(nq);
+    for (int b = 0; b < nq; b++) {
+      const int p = caches && caches[b] ? caches[b]->len : 0;
+      if ((rc = alloc_snapshot(e, p + lens[b], &fresh[b])) != SD_OK) return rc;
+    }
+  }
+  const int slot = e->fk_next;
+  e->fk_next = (slot + 1) % sd_engine::kForkSlots;
+  if ((rc = ensure_pin_slot(e, slot, n_all)) != SD_OK) return rc;
+  {
+    const void** pt = reinterpret_cast<const void**>(e->fk_pin[slot]);
+    const size_t kb = (size_t)2 * e->n_lin * nq, vb = kb + (size_t)e->n_full * nq;
+    for (int b = 0; b < nq; b++) {
+      const sd_snapshot* c = caches ? caches[b] : nullptr;
+      for (int i = 0; i < e->n_lin; i++) {
+        pt[(size_t)i * nq + b] = c ? c->state[i] : nullptr;
+        pt[(size_t)(e->n_lin + i) * nq + b] = c ? c->hist[i] : nullptr;
+      }
+      for (int i = 0; i < e->n_full; i++) {
+        pt[kb + (size_t)i * nq + b] = c ? c->k[i] : nullptr;
+        pt[vb + (size_t)i * nq + b] = c ? c->v[i] : nullptr;
+      }
+      if (keep) {
+        const sd_snapshot* o = fresh[b].get();
+        for (int i = 0; i < e->n_lin; i++) {
+          pt[per_set + (size_t)i * nq + b] = o->state[i];
+          pt[per_set + (size_t)(e->n_lin + i) * nq + b] = o->hist[i];
+        }
+        for (int i = 0; i < e->n_full; i++) {
+          pt[per_set + kb + (size_t)i * nq + b] = o->k[i];
+          pt[per_set + vb + (size_t)i * nq + b] = o->v[i];
+        }
+      }
+    }
+  }
+  int* tpos = e->fk_pin[slot] + i0;
+  int* tstart = tpos + T;
+  int* tseq = tstart + T;
+  int* soff = tseq + T;
+  int* slen = soff + nq;
+  int* plen = slen + nq;
+  int* blk = plen + nq;
+  int* grows = e->fk_pin[slot] + n_idx;
+  int* ctab = grows + R;
+  int* c0 = ctab + 2 * (size_t)chunks;
+  int* order = c0 + nq;
+  {
+    int t = 0, k = 0, ch = 0;
+    long long r = 0;
+    for (int b = 0; b < nq; b++) {
+      const int p = caches && caches[b] ? caches[b]->len : 0;
+      soff[b] = t, slen[b] = lens[b], plen[b] = p;
+      for (int j = 0; j < lens[b]; j++) tpos[t + j] = p + j, tstart[t + j] = t, tseq[t + j] = b;
+      for (int q0 = 0; q0 < lens[b]; q0 += 64, k++) blk[2 * k] = b, blk[2 * k + 1] = q0;
+      for (int j = 0; j < nrows[b]; j++, r++) grows[r] = t + rows[r];
+      if (two_phase) {
+        c0[b] = ch;
+        for (int q0 = 0; q0 < lens[b]; q0 += 64, ch++) ctab[2 * ch] = t + q0, ctab[2 * ch + 1] = std::min(64, (int)lens[b] - q0);
+        order[b] = b;
+      }
+      t += lens[b];
+    }
+    if (two_phase) std::stable_sort(order, order + nq, [&](int a, int b) { return lens[a] > lens[b]; });
+  }
+  if (ids_host) memcpy(e->fk_pin[slot] + n_idx + R + n_gdn, ids_host, T * sizeof(uint32_t));
   CK(cudaMemcpyAsync(e->fk_meta, e->fk_pin[slot], n_all * sizeof(int), cudaMemcpyHostToDevice, st));
   CK(cudaEventRecord(e->fk_ev[slot], st));
   if (timed) CK(cudaEventRecord(e->ev0, st));
   const int* dm = e->fk_meta;
-  const uint32_t* ids = ids_host ? reinterpret_cast<const uint32_t*>(dm + n_idx + R) : ids_dev;
-  Fork fk{cache, ids, dm + n_idx, dm, dm + T, dm + 2 * T, dm + 2 * T + nq, dm + 2 * T + 2 * nq, nq, nblk, max_len,
-          tail_pairs, e->fk_kv, e->fk_kv + (size_t)d.hk * T * d.hd};
-  rc = run_layers(e, (int)T, p, true, (int)R, &fk);
+  const void* const* dp = reinterpret_cast<const void* const*>(dm);
+  const int* di = dm + i0;
+  const uint32_t* ids = ids_host ? reinterpret_cast<const uint32_t*>(dm + n_idx + R + n_gdn) : ids_dev;
+  Fork fk;
+  fk.ids = ids;
+  fk.rows = dm + n_idx;
+  fk.states = reinterpret_cast<const float* const*>(dp);
+  fk.hists = reinterpret_cast<const __half* const*>(dp + (size_t)e->n_lin * nq);
+  fk.kp = reinterpret_cast<const __half* const*>(dp + (size_t)2 * e->n_lin * nq);
+  fk.vp = reinterpret_cast<const __half* const*>(dp + (size_t)(2 * e->n_lin + e->n_full) * nq);
+  if (keep) {
+    void* const* op = const_cast<void* const*>(dp + per_set);
+    fk.s_out = reinterpret_cast<float* const*>(op);
+    fk.h_out = reinterpret_cast<__half* const*>(op + (size_t)e->n_lin * nq);
+    fk.k_out = reinterpret_cast<__half* const*>(op + (size_t)2 * e->n_lin * nq);
+    fk.v_out = reinterpret_cast<__half* const*>(op + (size_t)(2 * e->n_lin + e->n_full) * nq);
+  }
+  fk.tpos = di, fk.tstart = di + T, fk.tseq = di + 2 * T;
+  fk.seq_off = di + 3 * T, fk.seq_len = fk.seq_off + nq, fk.plen = fk.seq_len + nq, fk.blk = fk.plen + nq;
+  if (two_phase) {
+    fk.chunk_tab = dm + n_idx + R;
+    fk.chunk0 = fk.chunk_tab + 2 * (size_t)chunks;
+    fk.order = fk.chunk0 + nq;
+    fk.chunks = chunks;
+    fk.two_phase = true;
+  }
+  fk.nseq = nq, fk.nblk = nblk, fk.max_len = max_len, fk.max_p = max_p, fk.max_rows = max_rows, fk.pairs = pairs;
+  fk.kt = e->fk_kv, fk.vt = e->fk_kv + (size_t)d.hk * T * d.hd;
+  rc = run_layers(e, (int)T, max_p, true, (int)R, &fk);
   if (rc != SD_OK) {
     cudaStreamSynchronize(st);
-    return rc;
+    return rc;  // the new snapshots are freed with `fresh`
   }
   if (timed) CK(cudaEventRecord(e->ev1, st));
+  if (keep)
+    for (int b = 0; b < nq; b++) {
+      e->live.push_back(fresh[b].get());
+      snaps_out[b] = fresh[b].release();
+    }
   *R_out = R;
+  return SD_OK;
+}
+
+// A packed pass with host buffers: enqueue, copy the rows out, wait, and un-rotate the rows of a
+// rotated torso (src/engine.rs:652-660). On a failure after the enqueue the new snapshots are freed.
+int batch_host(sd_engine* e, const char* fn, const sd_snapshot* const* caches, bool fork, const uint32_t* ids,
+               const int32_t* lens, int32_t nq, const int32_t* rows, const int32_t* nrows, bool keep, float* hidden_out,
+               sd_snapshot** snaps_out, double* gpu_ms_out) {
+  if (!ids) return e->fail(SD_ERR_INVALID, "%s: no token ids", fn);
+  long long R = 0;
+  int rc = packed_enqueue(e, fn, caches, fork, ids, nullptr, lens, nq, rows, nrows, keep, snaps_out, hidden_out != nullptr,
+                          true, &R);
+  if (rc != SD_OK) return rc;
+  const sd::Dims& d = e->dm;
+  cudaStream_t st = e->stream;
+  auto drop = [&]() {
+    if (keep)
+      for (int b = 0; b < nq; b++) {
+        delete snaps_out[b];
+        snaps_out[b] = nullptr;
+      }
+  };
+  if ((rc = ensure_pinned(e, 1, (int)R)) != SD_OK) {
+    drop();
+    return rc;
+  }
+  if (R > 0 && cudaMemcpyAsync(e->p_out, e->out, (size_t)R * d.d * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+    drop();
+    return e->fail(SD_ERR_CUDA, "%s: copying the rows out", fn);
+  }
+  if ((rc = sync_engine(e)) != SD_OK) {
+    drop();
+    return rc;
+  }
+  if (gpu_ms_out) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev0, e->ev1);
+    *gpu_ms_out = ms;
+  }
+  if (R > 0) {
+    memcpy(hidden_out, e->p_out, (size_t)R * d.d * 4);
+    if ((int)e->unrotate.size() == d.d)
+      for (long long r = 0; r < R; r++) {
+        float* row = hidden_out + (size_t)r * d.d;
+        fwht(row, d.d);
+        for (int c = 0; c < d.d; c++) row[c] = (float)((double)row[c] * e->unrotate[c]);
+      }
+  }
   return SD_OK;
 }
 
@@ -978,6 +1202,31 @@ void sd_engine_destroy(sd_engine* e) {
   delete e;
 }
 
+int sd_engine_reserve(sd_engine* e, int32_t max_tokens, int32_t max_seqs, int32_t max_rows) {
+  if (!e) return SD_ERR_INVALID;
+  if (max_tokens <= 0 || max_tokens > (1 << 16) || max_seqs <= 0 || max_seqs > 4096 || max_rows < 0)
+    return e->fail(SD_ERR_INVALID, "sd_engine_reserve: tokens 1..65536, sequences 1..4096, rows >= 0");
+  cudaSetDevice(e->device);
+  const long long T = max_tokens, nq = max_seqs, chunks = T / 64 + nq;
+  const size_t ints = packed_ints(e, T, nq, chunks, max_rows, true, chunks, true);
+  int rc;
+  if ((rc = ensure_pool(e, max_tokens)) != SD_OK || (rc = ensure_packed(e, T, ints, chunks)) != SD_OK ||
+      (rc = ensure_pinned(e, max_tokens, max_rows)) != SD_OK)
+    return rc;
+  for (int s = 0; s < sd_engine::kForkSlots; s++)
+    if ((rc = ensure_pin_slot(e, s, ints)) != SD_OK) return rc;
+  // the snapshots of such a pass (kept by the pool once freed): max_seqs states and histories, and
+  // K/V for max_tokens rows
+  const sd::Dims& d = e->dm;
+  const size_t snap_bytes = (size_t)max_seqs * e->n_lin * ((size_t)d.h * d.dk * d.dv * 4 + (size_t)3 * d.C() * 2) +
+                            (size_t)2 * e->n_full * d.hk * max_tokens * d.hd * 2;
+  void* prime = nullptr;
+  CK(cudaMallocFromPoolAsync(&prime, snap_bytes, e->snap_pool, e->stream));
+  CK(cudaFreeAsync(prime, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  return SD_OK;
+}
+
 int sd_engine_hidden_size(const sd_engine* e) { return e ? e->dm.d : 0; }
 int sd_engine_num_layers(const sd_engine* e) { return e ? e->n_layers : 0; }
 const char* sd_engine_last_error(const sd_engine* e) { return e ? e->err.c_str() : g_last_error.c_str(); }
@@ -1055,36 +1304,55 @@ int sd_forward(sd_engine* e, const uint32_t* ids, int32_t l, const int32_t* rows
 int sd_forward_fork(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids, const int32_t* lens, int32_t nq,
                     const int32_t* rows, const int32_t* nrows, float* hidden_out, double* gpu_ms_out) {
   if (!e) return SD_ERR_INVALID;
-  long long R = 0;
-  int rc = fork_enqueue(e, cache, ids, nullptr, lens, nq, rows, nrows, hidden_out != nullptr, true, &R);
-  if (rc != SD_OK) return rc;
-  const sd::Dims& d = e->dm;
-  cudaStream_t st = e->stream;
-  if ((rc = ensure_pinned(e, 1, (int)R)) != SD_OK) return rc;
-  if (R > 0) CK(cudaMemcpyAsync(e->p_out, e->out, (size_t)R * d.d * 4, cudaMemcpyDeviceToHost, st));
-  if ((rc = sync_engine(e)) != SD_OK) return rc;
-  if (gpu_ms_out) {
-    float ms = 0.0f;
-    cudaEventElapsedTime(&ms, e->ev0, e->ev1);
-    *gpu_ms_out = ms;
-  }
-  if (R > 0) {
-    memcpy(hidden_out, e->p_out, (size_t)R * d.d * 4);
-    if ((int)e->unrotate.size() == d.d)  // a rotated torso (src/engine.rs:652-660)
-      for (long long r = 0; r < R; r++) {
-        float* row = hidden_out + (size_t)r * d.d;
-        fwht(row, d.d);
-        for (int c = 0; c < d.d; c++) row[c] = (float)((double)row[c] * e->unrotate[c]);
-      }
-  }
-  return SD_OK;
+  if (!cache) return e->fail(SD_ERR_INVALID, "sd_forward_fork: no snapshot (the questions continue one)");
+  if (nq <= 0 || nq > 4096) return e->fail(SD_ERR_INVALID, "sd_forward_fork: %d questions (1 to 4096)", nq);
+  const std::vector<const sd_snapshot*> caches(nq, cache);
+  return sd_forward_fork_multi(e, caches.data(), ids, lens, nq, rows, nrows, hidden_out, gpu_ms_out);
+}
+
+int sd_forward_fork_multi(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids, const int32_t* lens,
+                          int32_t nq, const int32_t* rows, const int32_t* nrows, float* hidden_out, double* gpu_ms_out) {
+  if (!e) return SD_ERR_INVALID;
+  if (!caches) return e->fail(SD_ERR_INVALID, "sd_forward_fork: no snapshots (the questions continue one)");
+  return batch_host(e, "sd_forward_fork", caches, true, ids, lens, nq, rows, nrows, false, hidden_out, nullptr, gpu_ms_out);
+}
+
+int sd_forward_batch(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids, const int32_t* lens, int32_t nseq,
+                     const int32_t* rows, const int32_t* nrows, int32_t keep, float* hidden_out, sd_snapshot** snapshots_out,
+                     double* gpu_ms_out) {
+  if (!e) return SD_ERR_INVALID;
+  return batch_host(e, "sd_forward_batch", caches, false, ids, lens, nseq, rows, nrows, keep != 0, hidden_out, snapshots_out,
+                    gpu_ms_out);
 }
 
 int sd_forward_fork_dev(sd_engine* e, const sd_snapshot* cache, const uint32_t* ids_dev, const int32_t* lens, int32_t nq,
                         const int32_t* rows, const int32_t* nrows, float* hidden_dev) {
   if (!e) return SD_ERR_INVALID;
+  if (!cache) return e->fail(SD_ERR_INVALID, "sd_forward_fork: no snapshot (the questions continue one)");
+  if (nq <= 0 || nq > 4096) return e->fail(SD_ERR_INVALID, "sd_forward_fork: %d questions (1 to 4096)", nq);
+  const std::vector<const sd_snapshot*> caches(nq, cache);
+  return sd_forward_fork_multi_dev(e, caches.data(), ids_dev, lens, nq, rows, nrows, hidden_dev);
+}
+
+int sd_forward_fork_multi_dev(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids_dev, const int32_t* lens,
+                              int32_t nq, const int32_t* rows, const int32_t* nrows, float* hidden_dev) {
+  if (!e) return SD_ERR_INVALID;
+  if (!caches) return e->fail(SD_ERR_INVALID, "sd_forward_fork: no snapshots (the questions continue one)");
   long long R = 0;
-  int rc = fork_enqueue(e, cache, nullptr, ids_dev, lens, nq, rows, nrows, hidden_dev != nullptr, false, &R);
+  int rc = packed_enqueue(e, "sd_forward_fork", caches, true, nullptr, ids_dev, lens, nq, rows, nrows, false, nullptr,
+                          hidden_dev != nullptr, false, &R);
+  if (rc != SD_OK) return rc;
+  if (R > 0) CK(cudaMemcpyAsync(hidden_dev, e->out, (size_t)R * e->dm.d * 4, cudaMemcpyDeviceToDevice, e->stream));
+  return SD_OK;
+}
+
+int sd_forward_batch_dev(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids_dev, const int32_t* lens,
+                         int32_t nseq, const int32_t* rows, const int32_t* nrows, int32_t keep, float* hidden_dev,
+                         sd_snapshot** snapshots_out) {
+  if (!e) return SD_ERR_INVALID;
+  long long R = 0;
+  int rc = packed_enqueue(e, "sd_forward_batch", caches, false, nullptr, ids_dev, lens, nseq, rows, nrows, keep != 0,
+                          snapshots_out, hidden_dev != nullptr, false, &R);
   if (rc != SD_OK) return rc;
   if (R > 0) CK(cudaMemcpyAsync(hidden_dev, e->out, (size_t)R * e->dm.d * 4, cudaMemcpyDeviceToDevice, e->stream));
   return SD_OK;

@@ -135,6 +135,10 @@ struct GdnArgs {
   const int *seq_off = nullptr, *seq_len = nullptr;
   long long state_bstride = -1;  // elements between sequences' states (-1: h * 128 * 128; 0: one shared state)
   int store_state = 1;           // write the final state back
+  // per-sequence states instead of `state` (packed mode): initial states (read only; a null entry:
+  // zeros) and where the final ones go (null table or entry: not stored)
+  const float* const* states = nullptr;
+  float* const* states_out = nullptr;
 };
 
 template <int DVS, typename TIn>
@@ -157,7 +161,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
   const float* gg = a.g + t_base * H + h;
   float* og = a.o + t_base * H * DK + h * DK + c0;
   const long long sb = a.state_bstride < 0 ? (long long)H * DK * DK : a.state_bstride;
-  float* stg = a.state + b * sb + (long long)h * DK * DK + c0;
+  const long long hoff = (long long)h * DK * DK + c0;
+  const float* sin = a.states ? (a.states[b] ? a.states[b] + hoff : nullptr) : (a.load_state ? a.state + b * sb + hoff : nullptr);
+  float* sout = a.states ? (a.states_out && a.states_out[b] ? a.states_out[b] + hoff : nullptr)
+                         : (a.store_state ? a.state + b * sb + hoff : nullptr);
 
   // State slice: warp w owns key rows 16w..16w+15, all DVS columns (m16n8 accumulator layout).
   float sacc[DVS / 8][4];
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
 #pragma unroll
     for (int r = 0; r < 4; r++) {
       const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
-      sacc[nt][r] = a.load_state ? stg[row * DK + col] : 0.0f;
+      sacc[nt][r] = sin ? sin[row * DK + col] : 0.0f;
     }
   auto write_state_f16 = [&]() {
 #pragma unroll
@@ -476,13 +483,13 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
     __syncthreads();
   }
   // final state (f32)
-  if (a.store_state) {
+  if (sout) {
 #pragma unroll
     for (int nt = 0; nt < DVS / 8; nt++)
 #pragma unroll
       for (int r = 0; r < 4; r++) {
         const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
-        stg[row * DK + col] = sacc[nt][r];
+        sout[row * DK + col] = sacc[nt][r];
       }
   }
 }
@@ -518,18 +525,20 @@ struct PrepSmem {
   float beta[CH], g[CH], G[CH];
 };
 
-// Phase 1: grid (chunks, heads). Inputs f16 rows as in the chunked kernel (one sequence).
+// Phase 1: grid (chunks, heads). Inputs f16 rows as in the chunked kernel: one sequence of l tokens,
+// or (chunk_tab non-null) packed sequences whose chunk c starts at token chunk_tab[2c] and holds
+// chunk_tab[2c + 1] tokens. Record (c, h) is rec[h * chunks + c].
 __global__ void __launch_bounds__(256, 1) gdn_prep_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
                                                           int qk_stride, const __half* __restrict__ v, int v_stride,
                                                           const float* __restrict__ beta, const float* __restrict__ gl, int l,
-                                                          int H, ChunkRec* __restrict__ rec) {
+                                                          int H, const int* __restrict__ chunk_tab, ChunkRec* __restrict__ rec) {
   extern __shared__ __align__(16) uint8_t prep_smem_raw[];
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(prep_smem_raw);
   const int c = blockIdx.x, h = blockIdx.y;
-  const int t0 = c * CH, n = min(CH, l - t0);
+  const int t0 = chunk_tab ? chunk_tab[2 * c] : c * CH, n = chunk_tab ? chunk_tab[2 * c + 1] : min(CH, l - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g8 = lane >> 2, tq = lane & 3;
   const int mt = warp & 3;
-  ChunkRec& R = rec[(size_t)h * ((l + CH - 1) / CH) + c];
+  ChunkRec& R = rec[(size_t)h * gridDim.x + c];
   const float qscale = rsqrtf((float)DK);
 
   // 1. q^, k^ (normalised), v: each warp loads its 8 rows at once, then reduces
@@ -736,10 +745,22 @@ struct ScanSmem {
   __half ds[CH * LV];
 };
 
-// Phase 2: grid (heads x 128/DVS). Walks the chunks in order; the next chunk's record is prefetched.
+// Packed sequences of the two-phase scan: sequence b is tokens seq_off[b] .. + seq_len[b], its chunks
+// are records chunk0[b] .. of every head; it starts from s_in[b] (null: zeros) and its final state
+// goes to s_out[b] (null table or entry: not stored). CTA row y takes sequence order[y] (longest first).
+struct ScanPacked {
+  const int *seq_off = nullptr, *seq_len = nullptr, *chunk0 = nullptr, *order = nullptr;
+  const float* const* s_in = nullptr;
+  float* const* s_out = nullptr;
+  int total_chunks = 0;
+};
+
+// Phase 2: grid (heads x 128/DVS, sequences). Walks the chunks in order; the next chunk's record is
+// prefetched. One sequence: `state` in (with load_state) and out; packed: `ps`.
 template <int DVS>
-__global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const ChunkRec* __restrict__ rec, int nchunks, int l, int H,
-                                                          float* __restrict__ state, int load_state, float* __restrict__ o) {
+__global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const ChunkRec* __restrict__ rec, int nchunks_one, int l, int H,
+                                                          float* __restrict__ state, int load_state, float* __restrict__ o,
+                                                          const ScanPacked ps) {
   constexpr int LV = ScanSmem<DVS>::LV;
   constexpr int NT = DVS / 16;
   extern __shared__ __align__(16) uint8_t scan_smem_raw[];
@@ -748,9 +769,27 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const ChunkRec* __rest
   const int h = blockIdx.x / NS, c0 = (blockIdx.x % NS) * DVS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g8 = lane >> 2, tq = lane & 3;
   const int mt = warp & 3, nbase = (warp >> 2) * (DVS / 2);
-  float* stg = state + (long long)h * DK * DK + c0;
-  float* og = o + h * DK + c0;
-  const ChunkRec* rh = rec + (size_t)h * nchunks;
+  const long long hoff = (long long)h * DK * DK + c0;
+  const float* sin;
+  float* sout;
+  const ChunkRec* rh;
+  int nchunks;
+  long long tb = 0;  // first token of the sequence
+  if (ps.seq_off) {
+    const int b = ps.order[blockIdx.y];
+    tb = ps.seq_off[b];
+    l = ps.seq_len[b];
+    nchunks = (l + CH - 1) / CH;
+    rh = rec + (size_t)h * ps.total_chunks + ps.chunk0[b];
+    sin = ps.s_in && ps.s_in[b] ? ps.s_in[b] + hoff : nullptr;
+    sout = ps.s_out && ps.s_out[b] ? ps.s_out[b] + hoff : nullptr;
+  } else {
+    nchunks = nchunks_one;
+    rh = rec + (size_t)h * nchunks;
+    sin = load_state ? state + hoff : nullptr;
+    sout = state + hoff;
+  }
+  float* og = o + tb * H * DK + h * DK + c0;
 
   auto prefetch = [&](int c, int b) {
     const ChunkRec& R = rh[c];
@@ -779,7 +818,7 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const ChunkRec* __rest
 #pragma unroll
     for (int r = 0; r < 4; r++) {
       const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
-      sacc[nt][r] = load_state ? stg[row * DK + col] : 0.0f;
+      sacc[nt][r] = sin ? sin[row * DK + col] : 0.0f;
     }
   auto write_state_f16 = [&]() {
 #pragma unroll
@@ -872,13 +911,14 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const ChunkRec* __rest
     __syncthreads();  // done with the old f16 state, delta and this chunk's buffers
     write_state_f16();
   }
+  if (sout)
 #pragma unroll
-  for (int nt = 0; nt < DVS / 8; nt++)
+    for (int nt = 0; nt < DVS / 8; nt++)
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-      const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
-      stg[row * DK + col] = sacc[nt][r];
-    }
+      for (int r = 0; r < 4; r++) {
+        const int row = warp * 16 + g8 + (r >> 1) * 8, col = nt * 8 + 2 * tq + (r & 1);
+        sout[row * DK + col] = sacc[nt][r];
+      }
 }
 
 size_t gdn_two_phase_scratch(int l, int h) { return (size_t)((l + CH - 1) / CH) * h * sizeof(ChunkRec); }
@@ -902,10 +942,47 @@ cudaError_t launch_gdn_two_phase(const __half* q, const __half* k, int qk_stride
   }
   const int nchunks = (l + CH - 1) / CH;
   ChunkRec* rec = reinterpret_cast<ChunkRec*>(scratch);
-  gdn_prep_kernel<<<dim3(nchunks, h), 256, sizeof(PrepSmem), st>>>(q, k, qk_stride, v, v_stride, beta, g, l, h, rec);
+  gdn_prep_kernel<<<dim3(nchunks, h), 256, sizeof(PrepSmem), st>>>(q, k, qk_stride, v, v_stride, beta, g, l, h, nullptr, rec);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  gdn_scan_kernel<DVS><<<h * (DK / DVS), 256, sizeof(ScanSmem<DVS>), st>>>(rec, nchunks, l, h, state, load_state ? 1 : 0, o);
+  gdn_scan_kernel<DVS><<<h * (DK / DVS), 256, sizeof(ScanSmem<DVS>), st>>>(rec, nchunks, l, h, state, load_state ? 1 : 0, o,
+                                                                          ScanPacked{});
+  return cudaGetLastError();
+}
+
+size_t gdn_two_phase_packed_scratch(int chunks, int h) { return (size_t)chunks * h * sizeof(ChunkRec); }
+
+// Packed sequences, f16 q/k/v rows (token-major, sequence b at tokens seq_off[b] .. + seq_len[b]):
+// phase 1 over every (chunk, head) of every sequence, then the scan over (head, slice, sequence).
+// Device arrays: chunk_tab [chunks][2] (first token, tokens) of every chunk, sequences' chunks
+// consecutive from chunk0[b]; order: the sequences longest first; s_in / s_out as ScanPacked.
+cudaError_t launch_gdn_two_phase_packed(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
+                                        const float* beta, const float* g, const float* const* s_in, float* const* s_out,
+                                        float* o, const int* seq_off, const int* seq_len, const int* chunk0, const int* order,
+                                        const int* chunk_tab, int nseq, int chunks, int h, void* scratch, size_t scratch_bytes,
+                                        cudaStream_t st) {
+  if (nseq <= 0 || chunks <= 0 || h <= 0 || scratch_bytes < gdn_two_phase_packed_scratch(chunks, h) || nseq > 65535)
+    return cudaErrorInvalidValue;
+  constexpr int DVS = 32;
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gdn_scan_kernel<DVS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(ScanSmem<DVS>));
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  ChunkRec* rec = reinterpret_cast<ChunkRec*>(scratch);
+  gdn_prep_kernel<<<dim3(chunks, h), 256, sizeof(PrepSmem), st>>>(q, k, qk_stride, v, v_stride, beta, g, 0, h, chunk_tab, rec);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  ScanPacked ps;
+  ps.seq_off = seq_off, ps.seq_len = seq_len, ps.chunk0 = chunk0, ps.order = order, ps.s_in = s_in, ps.s_out = s_out;
+  ps.total_chunks = chunks;
+  gdn_scan_kernel<DVS><<<dim3(h * (DK / DVS), nseq), 256, sizeof(ScanSmem<DVS>), st>>>(rec, 0, 0, h, nullptr, 0, o, ps);
   return cudaGetLastError();
 }
 
@@ -965,16 +1042,19 @@ cudaError_t preload_gdn() {
 }
 
 // The chunked scan over `nseq` packed sequences of different lengths (sequence b: tokens seq_off[b] ..
-// + seq_len[b], device arrays), all starting from one shared state, which is read and not written:
-// continuations of one prefix, as a batched fork runs them.
+// + seq_len[b], device arrays), sequence b starting from states[b] (a device array of pointers, the
+// same one for every continuation of one prefix; a null entry: zeros), which is read and not written;
+// the final state of sequence b goes to states_out[b] (null table or entry: not stored). Continuations
+// of snapshots, as a batched fork runs them (one CTA walks all chunks of its sequence: for short ones).
 cudaError_t launch_gdn_chunked_packed(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
-                                      const float* beta, const float* g, const float* state, float* o, const int* seq_off,
-                                      const int* seq_len, int nseq, int h, cudaStream_t st) {
-  if (nseq <= 0 || h <= 0) return cudaErrorInvalidValue;
-  GdnArgs<__half> a{q, k, v, qk_stride, v_stride, 0, 0, beta, g, const_cast<float*>(state), o, 1, 0, h};
+                                      const float* beta, const float* g, const float* const* states, float* const* states_out,
+                                      float* o, const int* seq_off, const int* seq_len, int nseq, int h, cudaStream_t st) {
+  if (nseq <= 0 || h <= 0 || !states || nseq > 65535) return cudaErrorInvalidValue;
+  GdnArgs<__half> a{q, k, v, qk_stride, v_stride, 0, 0, beta, g, nullptr, o, 1, 0, h};
   a.seq_off = seq_off;
   a.seq_len = seq_len;
-  a.state_bstride = 0;
+  a.states = states;
+  a.states_out = states_out;
   a.store_state = 0;
   return (long long)nseq * h >= 128 ? launch_chunk<64>(a, nseq, st) : launch_chunk<32>(a, nseq, st);
 }

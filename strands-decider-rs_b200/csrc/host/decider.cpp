@@ -79,70 +79,112 @@ struct sd_decider {
     return it == cfg.temperature_by_kind.end() ? cfg.temperature : it->second;
   }
 
-  // `Decider::run` (src/lib.rs:156-208): the answers, in question order, and the usage count.
-  sd::pj::Value run(const sd::pj::Value& state, const std::vector<std::pair<std::string, sd::prompt::Question>>& named) {
+  // A request ready for the torso: its questions rendered, the state and the questions tokenized,
+  // the option tokens located (the part of `Decider::run`, src/lib.rs:156-184, before the forwards).
+  struct Prepared {
+    std::vector<std::pair<std::string, sd::prompt::Question>> named;
+    std::vector<sd::prompt::Rendered> rendered;
+    sd::Encoding st;
+    std::vector<sd::Encoding> qs;
+    std::vector<std::vector<size_t>> options;
+  };
+
+  Prepared prepare(const sd::pj::Value& state, const std::vector<std::pair<std::string, sd::prompt::Question>>& named) const {
     using namespace sd;
     if (!state.is_content()) throw std::runtime_error("state must be a string, object or array");
     if (named.empty()) throw std::runtime_error("ask at least one question");
     for (const auto& q : named) q.second.validate();
-    std::vector<prompt::Rendered> rendered;
-    for (const auto& q : named) rendered.push_back(prompt::render_question(q.second));
-    const Encoding st = tok->encode(prompt::render_state(state));
-    std::vector<Encoding> qs;
+    Prepared p;
+    p.named = named;
+    for (const auto& q : named) p.rendered.push_back(prompt::render_question(q.second));
+    p.st = tok->encode(prompt::render_state(state));
     size_t longest = 0;
-    for (const auto& r : rendered) {
-      qs.push_back(tok->encode(r.text));
-      longest = std::max(longest, qs.back().ids.size());
+    for (const auto& r : p.rendered) {
+      p.qs.push_back(tok->encode(r.text));
+      longest = std::max(longest, p.qs.back().ids.size());
     }
-    const size_t ns = st.ids.size();
+    const size_t ns = p.st.ids.size();
     if (ns + longest > cfg.max_length)
       throw std::runtime_error("prompt of " + std::to_string(ns + longest) + " tokens (" + std::to_string(ns) + " state + " +
                                std::to_string(longest) + " question) exceeds the context window of " +
                                std::to_string(cfg.max_length) + " tokens");
-    std::vector<std::vector<size_t>> options;
-    for (size_t i = 0; i < qs.size(); i++) options.push_back(prompt::option_token_index(qs[i].offsets, rendered[i].spans));
-    const int d = sd_engine_hidden_size(engine);
+    for (size_t i = 0; i < p.qs.size(); i++) p.options.push_back(prompt::option_token_index(p.qs[i].offsets, p.rendered[i].spans));
+    return p;
+  }
+
+  // The pointer head over question i's hidden rows (its options', then its last token's).
+  std::vector<double> head_probs(const Prepared& p, size_t i, const float* hidden, size_t nrows) const {
+    std::vector<double> probs(nrows - 1);
+    if (sd_head_probs(head, hidden, (int32_t)nrows, sd_engine_hidden_size(engine), temperature(p.rendered[i].kind),
+                      probs.data()) != SD_OK)
+      throw std::runtime_error(sd_last_error());
+    return probs;
+  }
+
+  // `Response::to_json` (src/lib.rs:78-87) from each question's probabilities; usage as the official
+  // engine counts it: chunks of questions, each with the state once.
+  sd::pj::Value respond(const Prepared& p, const std::vector<std::vector<double>>& probs) const {
+    using namespace sd;
     pj::Value answers = pj::Value::object();
-    auto answer = [&](size_t i, const float* hidden, size_t nrows) {
-      std::vector<double> probs(nrows - 1);
-      if (sd_head_probs(head, hidden, (int32_t)nrows, d, temperature(rendered[i].kind), probs.data()) != SD_OK)
-        throw std::runtime_error(sd_last_error());
-      answers.set(named[i].first, prompt::to_answer(rendered[i], probs, cfg.ordinal_smoothing));
-    };
-    auto check = [&](int rc) {
-      if (rc != SD_OK) throw std::runtime_error(sd_engine_last_error(engine));
-    };
-    if (qs.size() == 1) {
-      std::vector<uint32_t> ids(st.ids);
-      ids.insert(ids.end(), qs[0].ids.begin(), qs[0].ids.end());
+    for (size_t i = 0; i < p.qs.size(); i++)
+      answers.set(p.named[i].first, prompt::to_answer(p.rendered[i], probs[i], cfg.ordinal_smoothing));
+    size_t input_tokens = 0;
+    for (size_t c = 0; c < p.qs.size(); c += kMaxBatch) {
+      const size_t e = std::min(p.qs.size(), c + kMaxBatch);
+      input_tokens += p.st.ids.size();
+      for (size_t i = c; i < e; i++) input_tokens += p.qs[i].ids.size();
+    }
+    pj::Value usage = pj::Value::object();
+    usage.set("input_tokens", pj::Value::integer((long long)input_tokens));
+    usage.set("output_tokens", pj::Value::integer((long long)p.named.size()));
+    pj::Value resp = pj::Value::object();
+    resp.set("model", pj::Value::str("strands-decider-rs-0.1.0"));
+    resp.set("answers", answers);
+    resp.set("usage", usage);
+    return resp;
+  }
+
+  void check(int rc) const {
+    if (rc != SD_OK) throw std::runtime_error(sd_engine_last_error(engine));
+  }
+
+  // `Decider::run` (src/lib.rs:156-208): the answers, in question order, and the usage count.
+  sd::pj::Value run(const sd::pj::Value& state, const std::vector<std::pair<std::string, sd::prompt::Question>>& named) {
+    const Prepared p = prepare(state, named);
+    const size_t ns = p.st.ids.size();
+    const int d = sd_engine_hidden_size(engine);
+    std::vector<std::vector<double>> probs(p.qs.size());
+    if (p.qs.size() == 1) {
+      std::vector<uint32_t> ids(p.st.ids);
+      ids.insert(ids.end(), p.qs[0].ids.begin(), p.qs[0].ids.end());
       std::vector<int32_t> rows;
-      for (size_t o : options[0]) rows.push_back((int32_t)(ns + o));
+      for (size_t o : p.options[0]) rows.push_back((int32_t)(ns + o));
       rows.push_back((int32_t)ids.size() - 1);
       std::vector<float> hidden(rows.size() * (size_t)d);
       check(sd_forward(engine, ids.data(), (int32_t)ids.size(), rows.data(), (int32_t)rows.size(), nullptr, 0, hidden.data(),
                        nullptr, nullptr));
-      answer(0, hidden.data(), rows.size());
+      probs[0] = head_probs(p, 0, hidden.data(), rows.size());
     } else {
       sd_snapshot* prefix = nullptr;
-      check(sd_forward(engine, st.ids.data(), (int32_t)ns, nullptr, 0, nullptr, 1, nullptr, &prefix, nullptr));
+      check(sd_forward(engine, p.st.ids.data(), (int32_t)ns, nullptr, 0, nullptr, 1, nullptr, &prefix, nullptr));
       try {
-        for (size_t c = 0; c < qs.size(); c += kMaxBatch) {
-          const size_t e = std::min(qs.size(), c + kMaxBatch);
+        for (size_t c = 0; c < p.qs.size(); c += kMaxBatch) {
+          const size_t e = std::min(p.qs.size(), c + kMaxBatch);
           std::vector<uint32_t> ids;
           std::vector<int32_t> lens, rows, nrows;
           for (size_t i = c; i < e; i++) {
-            ids.insert(ids.end(), qs[i].ids.begin(), qs[i].ids.end());
-            lens.push_back((int32_t)qs[i].ids.size());
-            for (size_t o : options[i]) rows.push_back((int32_t)o);
-            rows.push_back((int32_t)qs[i].ids.size() - 1);
-            nrows.push_back((int32_t)options[i].size() + 1);
+            ids.insert(ids.end(), p.qs[i].ids.begin(), p.qs[i].ids.end());
+            lens.push_back((int32_t)p.qs[i].ids.size());
+            for (size_t o : p.options[i]) rows.push_back((int32_t)o);
+            rows.push_back((int32_t)p.qs[i].ids.size() - 1);
+            nrows.push_back((int32_t)p.options[i].size() + 1);
           }
           std::vector<float> hidden(rows.size() * (size_t)d);
           check(sd_forward_fork(engine, prefix, ids.data(), lens.data(), (int32_t)lens.size(), rows.data(), nrows.data(),
                                 hidden.data(), nullptr));
           size_t at = 0;
           for (size_t i = c; i < e; i++) {
-            answer(i, hidden.data() + at * d, (size_t)nrows[i - c]);
+            probs[i] = head_probs(p, i, hidden.data() + at * d, (size_t)nrows[i - c]);
             at += nrows[i - c];
           }
         }
@@ -152,21 +194,157 @@ struct sd_decider {
       }
       sd_snapshot_free(prefix);
     }
-    // usage as the official engine counts it: chunks of questions, each with the state once
-    size_t input_tokens = 0;
-    for (size_t c = 0; c < qs.size(); c += kMaxBatch) {
-      const size_t e = std::min(qs.size(), c + kMaxBatch);
-      input_tokens += ns;
-      for (size_t i = c; i < e; i++) input_tokens += qs[i].ids.size();
+    return respond(p, probs);
+  }
+
+  // Many requests at once, as a server answers concurrent ones: every request's first forward (its
+  // state, kept as a snapshot; or, with a single question, state and question together, as
+  // `Decider::run` does) in packed passes (sd_forward_batch), then every question continuing its
+  // request's snapshot in packed forks (sd_forward_fork_multi). Each request's answers equal its own
+  // `run` up to f32 summation order. out[i]: the response, or {"error": message} for a request that
+  // failed (invalid, too long, or a failed pass of the torso).
+  std::vector<sd::pj::Value> run_batch(const std::vector<const sd::pj::Value*>& states,
+                                       const std::vector<std::vector<std::pair<std::string, sd::prompt::Question>>>& named,
+                                       std::vector<std::string> errors) {
+    using namespace sd;
+    constexpr size_t kPassTokens = 65536, kPassSeqs = 4096;  // the packed passes' limits
+    const size_t n = states.size();
+    const int d = sd_engine_hidden_size(engine);
+    std::vector<Prepared> prep(n);
+    std::vector<std::vector<std::vector<double>>> probs(n);
+    std::vector<sd_snapshot*> snaps(n, nullptr);
+    for (size_t r = 0; r < n; r++) {
+      if (!errors[r].empty()) continue;
+      try {
+        prep[r] = prepare(*states[r], named[r]);
+        probs[r].resize(prep[r].qs.size());
+      } catch (const std::exception& e) {
+        errors[r] = e.what();
+      }
     }
-    pj::Value usage = pj::Value::object();
-    usage.set("input_tokens", pj::Value::integer((long long)input_tokens));
-    usage.set("output_tokens", pj::Value::integer((long long)named.size()));
-    pj::Value resp = pj::Value::object();  // Response::to_json (src/lib.rs:78-87)
-    resp.set("model", pj::Value::str("strands-decider-rs-0.1.0"));
-    resp.set("answers", answers);
-    resp.set("usage", usage);
-    return resp;
+    auto fail_all = [&](const std::vector<size_t>& group, const std::string& msg) {
+      for (size_t r : group) errors[r] = msg;
+    };
+    // pass 1: one sequence per request
+    {
+      std::vector<size_t> group;
+      size_t tokens = 0;
+      auto flush = [&]() {
+        if (group.empty()) return;
+        std::vector<uint32_t> ids;
+        std::vector<int32_t> lens, rows, nrows;
+        for (size_t r : group) {
+          const Prepared& p = prep[r];
+          const size_t ns = p.st.ids.size();
+          ids.insert(ids.end(), p.st.ids.begin(), p.st.ids.end());
+          if (p.qs.size() == 1) {
+            ids.insert(ids.end(), p.qs[0].ids.begin(), p.qs[0].ids.end());
+            for (size_t o : p.options[0]) rows.push_back((int32_t)(ns + o));
+            rows.push_back((int32_t)(ns + p.qs[0].ids.size()) - 1);
+            nrows.push_back((int32_t)p.options[0].size() + 1);
+            lens.push_back((int32_t)(ns + p.qs[0].ids.size()));
+          } else {
+            nrows.push_back(0);
+            lens.push_back((int32_t)ns);
+          }
+        }
+        std::vector<float> hidden(rows.size() * (size_t)d);
+        std::vector<sd_snapshot*> out(group.size(), nullptr);
+        const int rc = sd_forward_batch(engine, nullptr, ids.data(), lens.data(), (int32_t)lens.size(), rows.data(), nrows.data(),
+                                        1, hidden.data(), out.data(), nullptr);
+        if (rc != SD_OK) {
+          fail_all(group, sd_engine_last_error(engine));
+        } else {
+          size_t at = 0;
+          for (size_t g = 0; g < group.size(); g++) {
+            const size_t r = group[g];
+            if (prep[r].qs.size() == 1) {
+              sd_snapshot_free(out[g]);
+              try {
+                probs[r][0] = head_probs(prep[r], 0, hidden.data() + at * d, (size_t)nrows[g]);
+              } catch (const std::exception& e) {
+                errors[r] = e.what();
+              }
+              at += nrows[g];
+            } else {
+              snaps[r] = out[g];
+            }
+          }
+        }
+        group.clear();
+        tokens = 0;
+      };
+      for (size_t r = 0; r < n; r++) {
+        if (!errors[r].empty()) continue;
+        const Prepared& p = prep[r];
+        const size_t len = p.st.ids.size() + (p.qs.size() == 1 ? p.qs[0].ids.size() : 0);
+        if (tokens + len > kPassTokens || group.size() == kPassSeqs) flush();
+        group.push_back(r);
+        tokens += len;
+      }
+      flush();
+    }
+    // pass 2: every question of the requests with several, each continuing its request's snapshot
+    {
+      std::vector<std::pair<size_t, size_t>> group;  // (request, question)
+      size_t tokens = 0;
+      auto flush = [&]() {
+        if (group.empty()) return;
+        std::vector<const sd_snapshot*> caches;
+        std::vector<uint32_t> ids;
+        std::vector<int32_t> lens, rows, nrows;
+        for (const auto& rq : group) {
+          const Prepared& p = prep[rq.first];
+          const Encoding& q = p.qs[rq.second];
+          caches.push_back(snaps[rq.first]);
+          ids.insert(ids.end(), q.ids.begin(), q.ids.end());
+          lens.push_back((int32_t)q.ids.size());
+          for (size_t o : p.options[rq.second]) rows.push_back((int32_t)o);
+          rows.push_back((int32_t)q.ids.size() - 1);
+          nrows.push_back((int32_t)p.options[rq.second].size() + 1);
+        }
+        std::vector<float> hidden(rows.size() * (size_t)d);
+        const int rc = sd_forward_fork_multi(engine, caches.data(), ids.data(), lens.data(), (int32_t)lens.size(), rows.data(),
+                                             nrows.data(), hidden.data(), nullptr);
+        size_t at = 0;
+        for (size_t g = 0; g < group.size(); g++) {
+          const size_t r = group[g].first;
+          if (rc != SD_OK) {
+            errors[r] = sd_engine_last_error(engine);
+          } else if (errors[r].empty()) {
+            try {
+              probs[r][group[g].second] = head_probs(prep[r], group[g].second, hidden.data() + at * d, (size_t)nrows[g]);
+            } catch (const std::exception& e) {
+              errors[r] = e.what();
+            }
+          }
+          at += nrows[g];
+        }
+        group.clear();
+        tokens = 0;
+      };
+      for (size_t r = 0; r < n; r++) {
+        if (!snaps[r]) continue;
+        for (size_t i = 0; i < prep[r].qs.size(); i++) {
+          const size_t len = prep[r].qs[i].ids.size();
+          if (tokens + len > kPassTokens || group.size() == kPassSeqs) flush();
+          group.emplace_back(r, i);
+          tokens += len;
+        }
+      }
+      flush();
+    }
+    for (sd_snapshot* s : snaps) sd_snapshot_free(s);
+    std::vector<pj::Value> out(n);
+    for (size_t r = 0; r < n; r++) {
+      if (errors[r].empty()) {
+        out[r] = respond(prep[r], probs[r]);
+      } else {
+        out[r] = pj::Value::object();
+        out[r].set("error", pj::Value::str(errors[r]));
+      }
+    }
+    return out;
   }
 };
 
@@ -285,6 +463,27 @@ int sd_decider_load(const char* model_dir, int device, sd_decider** out) {
 
 void sd_decider_free(sd_decider* d) { delete d; }
 
+// `Request::from_json` (src/lib.rs:46-63): the state, and the questions in order.
+static const sd::pj::Value* parse_request(const sd::pj::Value& req,
+                                          std::vector<std::pair<std::string, sd::prompt::Question>>& named) {
+  using namespace sd;
+  const pj::Value* state = req.kind == pj::Value::Object ? req.get("state") : nullptr;
+  if (!state || !state->is_content()) throw std::runtime_error("state must be a string, object or array");
+  const pj::Value* images = req.get("images");
+  if (images && images->kind == pj::Value::Array && !images->arr.empty())
+    throw std::runtime_error("this engine has no vision tower; images are not supported");
+  const pj::Value* qs = req.get("questions");
+  if (!qs || qs->kind != pj::Value::Object || qs->obj.empty()) throw std::runtime_error("questions must be a non-empty object");
+  for (const auto& kv : qs->obj) {
+    try {
+      named.emplace_back(kv.first, prompt::Question::from_json(kv.second));
+    } catch (const std::exception& e) {
+      throw std::runtime_error("question " + kv.first + ": " + e.what());
+    }
+  }
+  return state;
+}
+
 const char* sd_decider_last_error(const sd_decider* d) { return d ? d->err.c_str() : g_host_error.c_str(); }
 
 int sd_decider_ask_all(sd_decider* d, const char* request_json, char** response_json) {
@@ -292,24 +491,38 @@ int sd_decider_ask_all(sd_decider* d, const char* request_json, char** response_
   *response_json = nullptr;
   try {
     using namespace sd;
-    // `Request::from_json` (src/lib.rs:46-63)
     const pj::Value req = pj::parse(request_json);
-    const pj::Value* state = req.get("state");
-    if (!state || !state->is_content()) throw std::runtime_error("state must be a string, object or array");
-    const pj::Value* images = req.get("images");
-    if (images && images->kind == pj::Value::Array && !images->arr.empty())
-      throw std::runtime_error("this engine has no vision tower; images are not supported");
-    const pj::Value* qs = req.get("questions");
-    if (!qs || qs->kind != pj::Value::Object || qs->obj.empty()) throw std::runtime_error("questions must be a non-empty object");
     std::vector<std::pair<std::string, prompt::Question>> named;
-    for (const auto& kv : qs->obj) {
+    const pj::Value* state = parse_request(req, named);
+    *response_json = dup_string(pj::dumps(d->run(*state, named)));
+    return SD_OK;
+  } catch (const std::exception& e) {
+    return host_fail(&d->err, e.what());
+  }
+}
+
+int sd_decider_ask_batch(sd_decider* d, const char* requests_json, char** responses_json) {
+  if (!d || !requests_json || !responses_json)
+    return host_fail(d ? &d->err : nullptr, "sd_decider_ask_batch: null argument");
+  *responses_json = nullptr;
+  try {
+    using namespace sd;
+    const pj::Value reqs = pj::parse(requests_json);
+    if (reqs.kind != pj::Value::Array) throw std::runtime_error("requests must be a JSON array");
+    const size_t n = reqs.arr.size();
+    std::vector<const pj::Value*> states(n, nullptr);
+    std::vector<std::vector<std::pair<std::string, prompt::Question>>> named(n);
+    std::vector<std::string> errors(n);
+    for (size_t r = 0; r < n; r++) {
       try {
-        named.emplace_back(kv.first, prompt::Question::from_json(kv.second));
+        states[r] = parse_request(reqs.arr[r], named[r]);
       } catch (const std::exception& e) {
-        throw std::runtime_error("question " + kv.first + ": " + e.what());
+        errors[r] = e.what();
       }
     }
-    *response_json = dup_string(pj::dumps(d->run(*state, named)));
+    pj::Value out = pj::Value::array();
+    for (auto& v : d->run_batch(states, named, errors)) out.arr.push_back(std::move(v));
+    *responses_json = dup_string(pj::dumps(out));
     return SD_OK;
   } catch (const std::exception& e) {
     return host_fail(&d->err, e.what());

@@ -144,12 +144,14 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
 // pre-conv rows before the sequence, `hist` [3][C]) up front, so all its loads are in flight at
 // once, then computes its outputs from registers. With `tstart` (the first token of each token's
 // sequence, for several sequences packed back to back) a tap before its token's sequence start reads
-// the history; without it all l tokens are one sequence. The output is stored as f16 (the reference
+// the history, that sequence's own when `hseq` gives one per sequence (hseq[tseq[t]]); without it all
+// l tokens are one sequence. The output is stored as f16 (the reference
 // keeps f32): the chunked scan that reads it rounds q, k and v to f16 tensor-core operands anyway,
 // after normalising q and k in f32.
 constexpr int kConvT = 8;
 __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ big, int stride, const float4* __restrict__ cw,
                                                    const __half* __restrict__ hist, int l, int C, const int* __restrict__ tstart,
+                                                   const __half* const* __restrict__ hseq, const int* __restrict__ tseq,
                                                    __half* __restrict__ out) {
   const int c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   const int t0 = blockIdx.y * kConvT;
@@ -160,9 +162,10 @@ __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ bi
     const int t = t0 - 3 + r;
     raw[r] = (t >= 0 && t < l) ? *reinterpret_cast<const uint4*>(big + (size_t)t * stride + c8) : make_uint4(0, 0, 0, 0);
   }
-  uint4 hs[3];
+  uint4 hs[3] = {};
+  if (!hseq)
 #pragma unroll
-  for (int j = 0; j < 3; j++) hs[j] = *reinterpret_cast<const uint4*>(hist + (size_t)j * C + c8);
+    for (int j = 0; j < 3; j++) hs[j] = *reinterpret_cast<const uint4*>(hist + (size_t)j * C + c8);
   int st[kConvT];
 #pragma unroll
   for (int i = 0; i < kConvT; i++) st[i] = (tstart && t0 + i < l) ? tstart[t0 + i] : 0;
@@ -180,7 +183,13 @@ __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ bi
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const int tt = t - 3 + j, hr = 3 + tt - st[i];  // history row when tt is before the sequence
-      src[j] = tt >= st[i] ? raw[i + j] : (hr == 0 ? hs[0] : (hr == 1 ? hs[1] : hs[2]));
+      if (tt >= st[i]) {
+        src[j] = raw[i + j];
+      } else if (hseq) {  // the sequence's own history; none (a fresh sequence): zeros
+        const __half* hp = hseq[tseq[t]];
+        src[j] = hp ? *reinterpret_cast<const uint4*>(hp + (size_t)hr * C + c8) : make_uint4(0, 0, 0, 0);
+      }
+      else src[j] = hr == 0 ? hs[0] : (hr == 1 ? hs[1] : hs[2]);
     }
     float x[4][8];
 #pragma unroll
@@ -222,6 +231,49 @@ __global__ void hist_update_kernel(const __half* __restrict__ big, int stride, _
   }
 #pragma unroll
   for (int r = 0; r < 3; r++) hist[(size_t)r * C + c] = v[r];
+}
+
+// hist_update_kernel for packed sequences: grid (channel blocks, sequences).
+__global__ void hist_pack_kernel(const __half* __restrict__ big, int stride, int C, const int* __restrict__ seq_off,
+                                 const int* __restrict__ seq_len, const __half* const* __restrict__ h_in,
+                                 __half* const* __restrict__ h_out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+  __half* dst = h_out[b];
+  if (c >= C || !dst) return;
+  const __half* old = h_in ? h_in[b] : nullptr;
+  const int off = seq_off[b], l = seq_len[b];
+#pragma unroll
+  for (int r = 0; r < 3; r++) {
+    const int src = l - 3 + r;
+    dst[(size_t)r * C + c] = src >= 0 ? big[(size_t)(off + src) * stride + c]
+                                      : (old ? old[(size_t)(src + 3) * C + c] : __float2half(0.0f));
+  }
+}
+
+// A sequence's keys and values into its snapshot: grid (row blocks of 8, kv heads, sequences), a warp
+// per row, 16 bytes per lane (head dim 256).
+__global__ void kv_pack_kernel(const __half* __restrict__ kt, const __half* __restrict__ vt, int T, int hd,
+                               const int* __restrict__ seq_off, const int* __restrict__ seq_len, const int* __restrict__ plen,
+                               const __half* const* __restrict__ kp, const __half* const* __restrict__ vp,
+                               __half* const* __restrict__ k_out, __half* const* __restrict__ v_out) {
+  const int b = blockIdx.z, kh = blockIdx.y;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  __half *dk = k_out[b], *dv = v_out[b];
+  const int p = plen[b], n = p + seq_len[b];
+  if (!dk || row >= n) return;
+  const __half *sk, *sv;
+  if (row < p) {
+    sk = kp[b] + ((size_t)kh * p + row) * hd;
+    sv = vp[b] + ((size_t)kh * p + row) * hd;
+  } else {
+    sk = kt + ((size_t)kh * T + seq_off[b] + row - p) * hd;
+    sv = vt + ((size_t)kh * T + seq_off[b] + row - p) * hd;
+  }
+  const size_t o = ((size_t)kh * n + row) * hd;
+  for (int c = lane * 8; c < hd; c += 256) {
+    *reinterpret_cast<uint4*>(dk + o + c) = *reinterpret_cast<const uint4*>(sk + c);
+    *reinterpret_cast<uint4*>(dv + o + c) = *reinterpret_cast<const uint4*>(sv + c);
+  }
 }
 
 // The per-token gates of the gated delta rule (src/kernels.rs:289-292): beta = sigmoid(b) and the log
@@ -390,15 +442,32 @@ cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const i
 }
 
 cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, __half* qkvc,
-                        const int* tstart, cudaStream_t st) {
-  if (C % 8 || stride % 8) return cudaErrorInvalidValue;
+                        const int* tstart, const __half* const* hseq, const int* tseq, cudaStream_t st) {
+  if (C % 8 || stride % 8 || (hseq && (!tstart || !tseq))) return cudaErrorInvalidValue;
   dim3 grid((C / 8 + 127) / 128, (l + kConvT - 1) / kConvT);
-  conv_kernel<<<grid, 128, 0, st>>>(big, stride, reinterpret_cast<const float4*>(conv_w), hist, l, C, tstart, qkvc);
+  conv_kernel<<<grid, 128, 0, st>>>(big, stride, reinterpret_cast<const float4*>(conv_w), hist, l, C, tstart, hseq, tseq, qkvc);
   return cudaGetLastError();
 }
 
 cudaError_t launch_hist_update(const __half* big, int stride, __half* hist, int l, int C, cudaStream_t st) {
   hist_update_kernel<<<(C + 255) / 256, 256, 0, st>>>(big, stride, hist, l, C);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_hist_pack(const __half* big, int stride, int C, const int* seq_off, const int* seq_len,
+                             const __half* const* h_in, __half* const* h_out, int nseq, cudaStream_t st) {
+  if (nseq <= 0 || nseq > 65535 || !h_out) return cudaErrorInvalidValue;
+  hist_pack_kernel<<<dim3((C + 255) / 256, nseq), 256, 0, st>>>(big, stride, C, seq_off, seq_len, h_in, h_out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_kv_pack(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
+                           const int* plen, const __half* const* kp, const __half* const* vp, __half* const* k_out,
+                           __half* const* v_out, int nseq, int max_rows, cudaStream_t st) {
+  if (nseq <= 0 || nseq > 65535 || hk <= 0 || hk > 65535 || hd % 8 || max_rows <= 0 || !k_out || !v_out)
+    return cudaErrorInvalidValue;
+  kv_pack_kernel<<<dim3((max_rows + 7) / 8, hk, nseq), 256, 0, st>>>(kt, vt, T, hd, seq_off, seq_len, plen, kp, vp, k_out,
+                                                                     v_out);
   return cudaGetLastError();
 }
 
@@ -436,7 +505,8 @@ cudaError_t preload_kernels() {
   const void* fns[] = {(const void*)embed_norm_kernel, (const void*)add_norm_kernel,   (const void*)final_norm_kernel,
                        (const void*)conv_kernel,       (const void*)hist_update_kernel, (const void*)gdn_gates_kernel,
                        (const void*)gdn_recurrent_kernel, (const void*)gnorm_kernel,  (const void*)qk_prep_kernel,
-                       (const void*)trace_kernel,      (const void*)add_bias_kernel};
+                       (const void*)trace_kernel,      (const void*)add_bias_kernel,    (const void*)hist_pack_kernel,
+                       (const void*)kv_pack_kernel};
   for (const void* f : fns) {
     cudaError_t e = cudaFuncGetAttributes(&a, f);
     if (e != cudaSuccess) return e;

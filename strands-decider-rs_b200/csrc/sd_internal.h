@@ -55,8 +55,18 @@ cudaError_t launch_add_norm(float* x, const __half* y, const float* w, int l, in
 cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int l, int d, float* out,
                               int* err, cudaStream_t st);
 cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, __half* qkvc,
-                        const int* tstart, cudaStream_t st);
+                        const int* tstart, const __half* const* hseq, const int* tseq, cudaStream_t st);
 cudaError_t launch_hist_update(const __half* big, int stride, __half* hist, int l, int C, cudaStream_t st);
+// packed sequences: the conv history after each sequence (its last 3 conv input rows, earlier ones
+// from its old history h_in[b], null: zeros) to h_out[b] (null entry: skipped)
+cudaError_t launch_hist_pack(const __half* big, int stride, int C, const int* seq_off, const int* seq_len,
+                             const __half* const* h_in, __half* const* h_out, int nseq, cudaStream_t st);
+// packed sequences: each sequence's keys and values, its prefix (kp[b] / vp[b], [hk][plen[b]][hd]) then
+// its own rows (kt / vt, [hk][T][hd] at seq_off[b]), to k_out[b] / v_out[b] ([hk][plen + len][hd];
+// null entry: skipped). max_rows: the largest plen + len.
+cudaError_t launch_kv_pack(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
+                           const int* plen, const __half* const* kp, const __half* const* vp, __half* const* k_out,
+                           __half* const* v_out, int nseq, int max_rows, cudaStream_t st);
 // gates: beta = sigmoid(b), g = log decay = negA softplus(a + dt_bias), both [l][h]
 cudaError_t launch_gdn_gates(const __half* big, int stride, int aoff, int boff, const float* neg_a, const float* dt_bias,
                              int l, int h, float* beta, float* g, cudaStream_t st);
@@ -69,9 +79,20 @@ cudaError_t launch_gdn_recurrent(const float* q, const float* k, int qk_stride, 
 cudaError_t launch_gdn_chunked(const void* q, const void* k, int qk_stride, const void* v, int v_stride, long long seq_qk,
                                long long seq_v, bool in_f16, const float* beta, const float* g, float* state, bool load_state,
                                float* o, int l, int h, int batch, cudaStream_t st);
+// packed sequences (token-major; sequence b at seq_off[b] .. + seq_len[b]), each from states[b] (null
+// entry: zeros) to states_out[b] (null table or entry: not stored); one CTA walks a sequence's chunks
 cudaError_t launch_gdn_chunked_packed(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
-                                      const float* beta, const float* g, const float* state, float* o, const int* seq_off,
-                                      const int* seq_len, int nseq, int h, cudaStream_t st);
+                                      const float* beta, const float* g, const float* const* states, float* const* states_out,
+                                      float* o, const int* seq_off, const int* seq_len, int nseq, int h, cudaStream_t st);
+// the two-phase scan over packed sequences (long ones): chunk_tab [chunks][2] (first token, tokens),
+// chunk0[b] the first chunk of sequence b, order the sequences longest first; scratch holds
+// gdn_two_phase_packed_scratch(chunks, h) bytes
+size_t gdn_two_phase_packed_scratch(int chunks, int h);
+cudaError_t launch_gdn_two_phase_packed(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
+                                        const float* beta, const float* g, const float* const* s_in, float* const* s_out,
+                                        float* o, const int* seq_off, const int* seq_len, const int* chunk0, const int* order,
+                                        const int* chunk_tab, int nseq, int chunks, int h, void* scratch, size_t scratch_bytes,
+                                        cudaStream_t st);
 // two-phase chunked scan for one long sequence (f16 rows): all chunks' intra-chunk work in parallel,
 // then the state scan; `scratch` holds gdn_two_phase_scratch(l, h) bytes of per-chunk records
 size_t gdn_two_phase_scratch(int l, int h);
@@ -96,6 +117,11 @@ struct AttnPacked {
   const __half* kt = nullptr;    // [hk][T][hd] keys and values of the packed tokens
   const __half* vt = nullptr;
   int T = 0;
+  // prefixes of their own (one snapshot per sequence): [hk][plen[b]][hd] keys and values of each
+  // sequence's prefix; null: every sequence continues the one prefix passed to the launch
+  const __half* const* kp = nullptr;
+  const __half* const* vp = nullptr;
+  const int* plen = nullptr;
 };
 cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, const __half* gate, int gstride, int goff,
                              int gstep, __half* out, int l, int p, int lt, int hq, int hk, int hd, int splits, float* ws,

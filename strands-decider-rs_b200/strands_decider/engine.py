@@ -51,6 +51,11 @@ def lib() -> C.CDLL:
         L.sd_forward_dev.argtypes = [vp, vp, i32, vp, i32, vp, i32, vp, C.POINTER(vp)]
         L.sd_forward_fork.argtypes = [vp, vp, vp, vp, i32, vp, vp, vp, C.POINTER(C.c_double)]
         L.sd_forward_fork_dev.argtypes = [vp, vp, vp, vp, i32, vp, vp, vp]
+        L.sd_forward_fork_multi.argtypes = [vp, vp, vp, vp, i32, vp, vp, vp, C.POINTER(C.c_double)]
+        L.sd_forward_fork_multi_dev.argtypes = [vp, vp, vp, vp, i32, vp, vp, vp]
+        L.sd_forward_batch.argtypes = [vp, vp, vp, vp, i32, vp, vp, i32, vp, vp, C.POINTER(C.c_double)]
+        L.sd_engine_reserve.argtypes = [vp, i32, i32, i32]
+        L.sd_forward_batch_dev.argtypes = [vp, vp, vp, vp, i32, vp, vp, i32, vp, vp]
         L.sd_engine_synchronize.argtypes = [vp]
         L.sd_engine_stream.restype = vp
         L.sd_engine_stream.argtypes = [vp]
@@ -80,6 +85,7 @@ def lib() -> C.CDLL:
         L.sd_decider_load.argtypes = [cp, C.c_int, C.POINTER(vp)]
         L.sd_decider_free.argtypes = [vp]
         L.sd_decider_ask_all.argtypes = [vp, cp, C.POINTER(vp)]
+        L.sd_decider_ask_batch.argtypes = [vp, cp, C.POINTER(vp)]
         L.sd_decider_last_error.argtypes = [vp]
         L.sd_decider_last_error.restype = cp
         L.sd_host_last_error.restype = cp
@@ -179,10 +185,11 @@ class Engine:
         out.trace = tr
         return out
 
-    def forward_fork(self, cache: Snapshot, ids_list, rows_list, timed: bool = False):
+    def forward_fork(self, cache, ids_list, rows_list, timed: bool = False):
         """`sd_forward_fork`: every question (ids_list[b], its rows rows_list[b]) continued from the
-        snapshot ``cache`` in one pass. Returns the hidden rows of each question ([rows, d] f32 each)
-        and, with ``timed``, the pass's device time in ms."""
+        snapshot ``cache`` in one pass; ``cache`` a list of snapshots, one per question
+        (`sd_forward_fork_multi`): questions of several requests in one pass. Returns the hidden
+        rows of each question ([rows, d] f32 each) and, with ``timed``, the pass's device time in ms."""
         lens = np.array([len(x) for x in ids_list], np.int32)
         nrows = np.array([len(r) for r in rows_list], np.int32)
         ids = np.ascontiguousarray(np.concatenate([np.asarray(x, np.uint32) for x in ids_list]), np.uint32)
@@ -191,21 +198,76 @@ class Engine:
         d = self.hidden_size()
         hidden = np.zeros((int(nrows.sum()), d), np.float32)
         ms = C.c_double(0.0)
-        _check(lib().sd_forward_fork(self._h, cache._h, _ptr(ids), _ptr(lens), len(lens), _ptr(rows) if len(rows) else None,
-                                     _ptr(nrows), _ptr(hidden) if len(rows) else None, C.byref(ms)),
-               "sd_forward_fork", self._h)
+        if isinstance(cache, (list, tuple)):
+            caches = (C.c_void_p * len(cache))(*[c._h for c in cache])
+            _check(lib().sd_forward_fork_multi(self._h, caches, _ptr(ids), _ptr(lens), len(lens),
+                                               _ptr(rows) if len(rows) else None, _ptr(nrows),
+                                               _ptr(hidden) if len(rows) else None, C.byref(ms)),
+                   "sd_forward_fork_multi", self._h)
+        else:
+            _check(lib().sd_forward_fork(self._h, cache._h, _ptr(ids), _ptr(lens), len(lens), _ptr(rows) if len(rows) else None,
+                                         _ptr(nrows), _ptr(hidden) if len(rows) else None, C.byref(ms)),
+                   "sd_forward_fork", self._h)
         outs = np.split(hidden, np.cumsum(nrows)[:-1]) if len(nrows) > 1 else [hidden]
         return (outs, ms.value) if timed else outs
 
-    def forward_fork_dev(self, cache: Snapshot, ids_dev: int, lens, rows_list, hidden_dev: int | None):
+    def forward_fork_dev(self, cache, ids_dev: int, lens, rows_list, hidden_dev: int | None):
         """`sd_forward_fork_dev`: the fork with the questions' ids on the GPU (back to back, lens[b]
-        each), hidden rows to ``hidden_dev``, queued on the engine's stream."""
+        each), hidden rows to ``hidden_dev``, queued on the engine's stream; ``cache`` a snapshot or
+        one per question (`sd_forward_fork_multi_dev`)."""
         lens = np.ascontiguousarray(lens, np.int32)
         nrows = np.array([len(r) for r in rows_list], np.int32)
         rows = np.ascontiguousarray(np.concatenate([np.asarray(r, np.int32) for r in rows_list] + [np.zeros(0, np.int32)]),
                                     np.int32)
-        _check(lib().sd_forward_fork_dev(self._h, cache._h, ids_dev, _ptr(lens), len(lens), _ptr(rows) if len(rows) else None,
-                                         _ptr(nrows), hidden_dev), "sd_forward_fork_dev", self._h)
+        if isinstance(cache, (list, tuple)):
+            caches = (C.c_void_p * len(cache))(*[c._h for c in cache])
+            _check(lib().sd_forward_fork_multi_dev(self._h, caches, ids_dev, _ptr(lens), len(lens),
+                                                   _ptr(rows) if len(rows) else None, _ptr(nrows), hidden_dev),
+                   "sd_forward_fork_multi_dev", self._h)
+        else:
+            _check(lib().sd_forward_fork_dev(self._h, cache._h, ids_dev, _ptr(lens), len(lens),
+                                             _ptr(rows) if len(rows) else None, _ptr(nrows), hidden_dev),
+                   "sd_forward_fork_dev", self._h)
+
+    def reserve(self, max_tokens: int, max_seqs: int, max_rows: int):
+        """`sd_engine_reserve`: size the working memory for passes up to these bounds up front."""
+        _check(lib().sd_engine_reserve(self._h, max_tokens, max_seqs, max_rows), "sd_engine_reserve", self._h)
+
+    def forward_batch(self, caches, ids_list, rows_list, keep: bool = False, timed: bool = False):
+        """`sd_forward_batch`: sequence b (ids_list[b], rows rows_list[b]) continuing caches[b] (None:
+        a fresh sequence; ``caches`` None: all fresh), all in one pass. Returns the hidden rows of
+        each sequence, the new snapshots (with ``keep``; else None) and, with ``timed``, the device
+        time in ms."""
+        n = len(ids_list)
+        lens = np.array([len(x) for x in ids_list], np.int32)
+        nrows = np.array([len(r) for r in rows_list], np.int32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(x, np.uint32) for x in ids_list]), np.uint32)
+        rows = np.ascontiguousarray(np.concatenate([np.asarray(r, np.int32) for r in rows_list] + [np.zeros(0, np.int32)]),
+                                    np.int32)
+        hidden = np.zeros((int(nrows.sum()), self.hidden_size()), np.float32)
+        cs = None if caches is None else (C.c_void_p * n)(*[c._h if c is not None else None for c in caches])
+        out = (C.c_void_p * n)()
+        ms = C.c_double(0.0)
+        _check(lib().sd_forward_batch(self._h, cs, _ptr(ids), _ptr(lens), n, _ptr(rows) if len(rows) else None, _ptr(nrows),
+                                      int(keep), _ptr(hidden) if len(rows) else None, out if keep else None, C.byref(ms)),
+               "sd_forward_batch", self._h)
+        outs = np.split(hidden, np.cumsum(nrows)[:-1]) if n > 1 else [hidden]
+        snaps = [Snapshot(out[b]) for b in range(n)] if keep else None
+        return (outs, snaps, ms.value) if timed else (outs, snaps)
+
+    def forward_batch_dev(self, caches, ids_dev: int, lens, rows_list, hidden_dev: int | None, keep: bool = False):
+        """`sd_forward_batch_dev`: the batch with the ids on the GPU (back to back), rows to
+        ``hidden_dev``, queued on the engine's stream. Returns the new snapshots (with ``keep``)."""
+        n = len(lens)
+        lens = np.ascontiguousarray(lens, np.int32)
+        nrows = np.array([len(r) for r in rows_list], np.int32)
+        rows = np.ascontiguousarray(np.concatenate([np.asarray(r, np.int32) for r in rows_list] + [np.zeros(0, np.int32)]),
+                                    np.int32)
+        cs = None if caches is None else (C.c_void_p * n)(*[c._h if c is not None else None for c in caches])
+        out = (C.c_void_p * n)()
+        _check(lib().sd_forward_batch_dev(self._h, cs, ids_dev, _ptr(lens), n, _ptr(rows) if len(rows) else None, _ptr(nrows),
+                                          int(keep), hidden_dev, out if keep else None), "sd_forward_batch_dev", self._h)
+        return [Snapshot(out[b]) for b in range(n)] if keep else None
 
     def forward_dev(self, ids_dev: int, n_ids: int, rows_dev: int | None, n_rows: int, cache: Snapshot | None = None,
                     keep: bool = False, hidden_dev: int | None = None) -> Snapshot | None:
@@ -355,6 +417,18 @@ class NativeDecider:
         out = C.c_void_p()
         L = lib()
         if L.sd_decider_ask_all(self._h, json.dumps(request).encode(), C.byref(out)) != SD_OK:
+            raise Error(L.sd_decider_last_error(self._h).decode(errors="replace"))
+        try:
+            return json.loads(C.string_at(out.value).decode())
+        finally:
+            L.sd_string_free(out)
+
+    def ask_batch(self, requests: list) -> list:
+        """`sd_decider_ask_batch`: many requests at once (their states in packed passes, then all their
+        questions in packed forks); a response body per request, or {"error": message}."""
+        out = C.c_void_p()
+        L = lib()
+        if L.sd_decider_ask_batch(self._h, json.dumps(requests).encode(), C.byref(out)) != SD_OK:
             raise Error(L.sd_decider_last_error(self._h).decode(errors="replace"))
         try:
             return json.loads(C.string_at(out.value).decode())

@@ -27,3 +27,53 @@ def test_native_decider_matches_python(small_model):
     with pytest.raises(Exception, match="questions must be a non-empty object"):
         nat.ask_all({"state": "x", "questions": {}})
     nat.close()
+
+
+def _close_answers(a, b, tol=2e-3):
+    """Two response bodies from different batchings: same keys, labels and choices, numbers within tol."""
+    assert a.keys() == b.keys()
+    assert a["model"] == b["model"] and a["usage"] == b["usage"]
+    for name in a["answers"]:
+        x, y = a["answers"][name], b["answers"][name]
+        assert x.keys() == y.keys() and x["type"] == y["type"]
+        for k in x:
+            if isinstance(x[k], float):
+                assert abs(x[k] - y[k]) <= tol, (name, k)
+            elif k == "probabilities":
+                assert x[k].keys() == y[k].keys()
+                assert max(abs(x[k][o] - y[k][o]) for o in x[k]) <= tol
+            elif k != "choice":
+                assert x[k] == y[k], (name, k)
+
+
+def test_native_decider_batch_matches_one_by_one(small_model):
+    """sd_decider_ask_batch: many requests (one question, several, invalid ones) in packed passes give
+    each request's own ask_all answers; the failures come back in place as {"error": ...}."""
+    from strands_decider import NativeDecider
+    nat = NativeDecider.load(small_model)
+    rng = np.random.default_rng(7)
+    words = ["payout", "refund", "charged", "twice", "help", "urgent", "billing", "login", "error", "slow", "café", "日本"]
+    qs = {"urgent": {"type": "noul", "instructions": "Does this convey urgency?"},
+          "team": {"type": "choice", "instructions": "Which team?", "criteria": {"billing": "money", "tech": "", "sales": None}},
+          "mood": {"type": "score", "instructions": "How upset?", "criteria": ["calm", "annoyed", "furious"]}}
+    requests = []
+    for i in range(10):
+        state = " ".join(rng.choice(words, int(rng.integers(3, 400))))
+        names = list(qs)[: 1 + i % 3]
+        requests.append({"state": state, "questions": {n: qs[n] for n in names}})
+    requests.insert(3, {"state": "x", "questions": {}})
+    requests.insert(7, {"state": 5, "questions": qs})
+    requests.append({"state": "word " * 5000, "questions": qs})  # past the context window
+    got = nat.ask_batch(requests)
+    assert len(got) == len(requests)
+    for req, g in zip(requests, got):
+        try:
+            want = nat.ask_all(req)
+        except Exception as e:
+            assert g == {"error": str(e)}
+            continue
+        _close_answers(g, want)
+    assert nat.ask_batch([]) == []
+    with pytest.raises(Exception, match="JSON array"):
+        nat.ask_batch({"state": "x"})
+    nat.close()

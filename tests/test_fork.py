@@ -117,3 +117,80 @@ def test_fork_errors(engines, small_model):
     # the engine still works after the rejected calls
     assert gpu.forward_fork(snap, [q], [[9]])[0].shape == (1, gpu.hidden_size())
     snap.close()
+
+
+def test_fork_across_snapshots_matches_serial(engines):
+    """sd_forward_fork_multi: questions of several requests (snapshots of 3 to 1100 tokens, the
+    longest with its keys split across CTAs) in one pass, interleaved, each equal to its own serial
+    continuation."""
+    gpu, _ = engines
+    rng = np.random.default_rng(27)
+    snaps = [gpu.forward(rng.integers(0, 8000, n), [], keep=True).snapshot for n in (3, 64, 300, 1100)]
+    order = [2, 0, 3, 1, 2, 3, 0, 1, 3]
+    qs, rows = _questions(rng, [5, 63, 64, 65, 1, 130, 30, 12, 77])
+    got = gpu.forward_fork([snaps[i] for i in order], qs, rows)
+    for i, q, r, g in zip(order, qs, rows, got):
+        want = gpu.forward(q, r, cache=snaps[i]).hidden
+        assert g.shape == want.shape
+        assert np.abs(g - want).max() < 2e-2
+    # the same questions through one call per snapshot agree (a batch of another size takes other
+    # GEMM split-K and attention key-split plans, so f32 summation orders differ: parity tolerance)
+    for s in range(4):
+        idx = [j for j, i in enumerate(order) if i == s]
+        one = gpu.forward_fork(snaps[s], [qs[j] for j in idx], [rows[j] for j in idx])
+        for j, g in zip(idx, one):
+            assert np.abs(g - got[j]).max() < 2e-2
+    for s in snaps:
+        s.close()
+
+
+def test_fork_across_snapshots_matches_oracle(engines):
+    gpu, cpu = engines
+    rng = np.random.default_rng(28)
+    states = [rng.integers(0, 8000, n) for n in (40, 150)]
+    snaps = [gpu.forward(s, [], keep=True).snapshot for s in states]
+    qs, rows = _questions(rng, [20, 66, 9])
+    order = [1, 0, 1]
+    got = gpu.forward_fork([snaps[i] for i in order], qs, rows)
+    for i, q, r, g in zip(order, qs, rows, got):
+        want = cpu.forward(np.concatenate([states[i], q]), [len(states[i]) + k for k in r])[0]
+        assert np.abs(g - want).max() < 2e-2
+    for s in snaps:
+        s.close()
+
+
+def test_fork_across_snapshots_dev_matches_host(engines):
+    import torch
+    gpu, _ = engines
+    rng = np.random.default_rng(29)
+    snaps = [gpu.forward(rng.integers(0, 8000, n), [], keep=True).snapshot for n in (100, 700)]
+    qs, rows = _questions(rng, [50, 3, 90, 64])
+    caches = [snaps[0], snaps[1], snaps[1], snaps[0]]
+    want = np.concatenate(gpu.forward_fork(caches, qs, rows))
+    ids_d = torch.from_numpy(np.concatenate(qs).astype(np.int32)).cuda()
+    hid = torch.empty((len(want), gpu.hidden_size()), dtype=torch.float32, device="cuda")
+    gpu.forward_fork_dev(caches, ids_d.data_ptr(), [len(q) for q in qs], rows, hid.data_ptr())
+    gpu.synchronize()
+    assert np.array_equal(hid.cpu().numpy(), want)
+    for s in snaps:
+        s.close()
+
+
+def test_fork_across_snapshots_errors(engines, small_model):
+    from strands_decider.engine import Engine, Error, Snapshot
+    gpu, _ = engines
+    rng = np.random.default_rng(30)
+    a = gpu.forward(rng.integers(0, 8000, 50), [], keep=True).snapshot
+    b = gpu.forward(rng.integers(0, 8000, 4000), [], keep=True).snapshot
+    q = rng.integers(0, 8000, 10)
+    with pytest.raises(Error):
+        gpu.forward_fork([a, Snapshot(None)], [q, q], [[9], [9]])  # one question without a snapshot
+    with pytest.raises(Error):
+        gpu.forward_fork([a, b], [q, rng.integers(0, 8000, 200)], [[9], [0]])  # past the context of b
+    other = Engine.load(small_model)
+    c = other.forward(q, [], keep=True).snapshot
+    with pytest.raises(Error):
+        gpu.forward_fork([a, c], [q, q], [[9], [9]])  # another engine's snapshot
+    assert len(gpu.forward_fork([a, b], [q, q[:5]], [[9], [4]])) == 2
+    for s in (a, b, c):
+        s.close()
