@@ -528,7 +528,7 @@ struct PrepSmem {
 // Phase 1: grid (chunks, heads). Inputs f16 rows as in the chunked kernel: one sequence of l tokens,
 // or (chunk_tab non-null) packed sequences whose chunk c starts at token chunk_tab[2c] and holds
 // chunk_tab[2c + 1] tokens. Record (c, h) is rec[h * chunks + c].
-__global__ void __launch_bounds__(256, 1) gdn_prep_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
+__global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
                                                           int qk_stride, const __half* __restrict__ v, int v_stride,
                                                           const float* __restrict__ beta, const float* __restrict__ gl, int l,
                                                           int H, const int* __restrict__ chunk_tab, ChunkRec* __restrict__ rec) {

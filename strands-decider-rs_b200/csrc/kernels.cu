@@ -139,71 +139,60 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
 }
 
 // conv (src/kernels.rs:152-171): depthwise causal conv (4 taps) over the C = q,k,v channels of the
-// in_proj output, then SiLU, f16 out. Each thread owns 8 channels (16-byte loads and stores) and
-// kConvT consecutive tokens: it loads the kConvT + 3 input rows and the 3 history rows (the last 3
-// pre-conv rows before the sequence, `hist` [3][C]) up front, so all its loads are in flight at
-// once, then computes its outputs from registers. With `tstart` (the first token of each token's
-// sequence, for several sequences packed back to back) a tap before its token's sequence start reads
-// the history, that sequence's own when `hseq` gives one per sequence (hseq[tseq[t]]); without it all
-// l tokens are one sequence. The output is stored as f16 (the reference
-// keeps f32): the chunked scan that reads it rounds q, k and v to f16 tensor-core operands anyway,
-// after normalising q and k in f32.
+// in_proj output, then SiLU, f16 out. Each thread owns 4 channels (8-byte loads and stores) and
+// kConvT consecutive tokens: it loads the kConvT + 3 input rows up front, so all its loads are in
+// flight at once, then computes its outputs from registers (about 70 registers, so 7 CTAs of 128
+// threads share an SM and keep enough loads in flight for HBM). A tap before the sequence reads the
+// history (the last 3 pre-conv rows before it, `hist` [3][C]). With `tstart` (the first token of each
+// token's sequence, for several sequences packed back to back) a tap before its token's sequence
+// start reads the history, that sequence's own when `hseq` gives one per sequence (hseq[tseq[t]]; a
+// null entry: zeros, a fresh sequence); without it all l tokens are one sequence. The output is
+// stored as f16 (the reference keeps f32): the chunked scan that reads it rounds q, k and v to f16
+// tensor-core operands anyway, after normalising q and k in f32.
 constexpr int kConvT = 8;
 __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ big, int stride, const float4* __restrict__ cw,
                                                    const __half* __restrict__ hist, int l, int C, const int* __restrict__ tstart,
                                                    const __half* const* __restrict__ hseq, const int* __restrict__ tseq,
                                                    __half* __restrict__ out) {
-  const int c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int c4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   const int t0 = blockIdx.y * kConvT;
-  if (c8 >= C || t0 >= l) return;
-  uint4 raw[kConvT + 3];  // input rows t0 - 3 .. t0 + kConvT - 1 (zero outside 0 .. l - 1)
+  if (c4 >= C || t0 >= l) return;
+  uint2 raw[kConvT + 3];  // input rows t0 - 3 .. t0 + kConvT - 1 (zero outside 0 .. l - 1)
 #pragma unroll
   for (int r = 0; r < kConvT + 3; r++) {
     const int t = t0 - 3 + r;
-    raw[r] = (t >= 0 && t < l) ? *reinterpret_cast<const uint4*>(big + (size_t)t * stride + c8) : make_uint4(0, 0, 0, 0);
+    raw[r] = (t >= 0 && t < l) ? *reinterpret_cast<const uint2*>(big + (size_t)t * stride + c4) : make_uint2(0, 0);
   }
-  uint4 hs[3] = {};
-  if (!hseq)
+  float w[4][4];
 #pragma unroll
-    for (int j = 0; j < 3; j++) hs[j] = *reinterpret_cast<const uint4*>(hist + (size_t)j * C + c8);
-  int st[kConvT];
-#pragma unroll
-  for (int i = 0; i < kConvT; i++) st[i] = (tstart && t0 + i < l) ? tstart[t0 + i] : 0;
-  float w[8][4];
-#pragma unroll
-  for (int c = 0; c < 8; c++) {
-    const float4 k = cw[c8 + c];
+  for (int c = 0; c < 4; c++) {
+    const float4 k = cw[c4 + c];
     w[c][0] = k.x, w[c][1] = k.y, w[c][2] = k.z, w[c][3] = k.w;
   }
 #pragma unroll
   for (int i = 0; i < kConvT; i++) {
     const int t = t0 + i;
     if (t >= l) break;
-    uint4 src[4];
+    const int st = tstart ? tstart[t] : 0;
+    float x[4][4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const int tt = t - 3 + j, hr = 3 + tt - st[i];  // history row when tt is before the sequence
-      if (tt >= st[i]) {
-        src[j] = raw[i + j];
-      } else if (hseq) {  // the sequence's own history; none (a fresh sequence): zeros
-        const __half* hp = hseq[tseq[t]];
-        src[j] = hp ? *reinterpret_cast<const uint4*>(hp + (size_t)hr * C + c8) : make_uint4(0, 0, 0, 0);
+      const int tt = t - 3 + j;
+      uint2 src = raw[i + j];
+      if (tt < st) {  // before the sequence: history row 3 + tt - st
+        const __half* hp = hseq ? hseq[tseq[t]] : hist;
+        src = hp ? *reinterpret_cast<const uint2*>(hp + (size_t)(3 + tt - st) * C + c4) : make_uint2(0, 0);
       }
-      else src[j] = hr == 0 ? hs[0] : (hr == 1 ? hs[1] : hs[2]);
-    }
-    float x[4][8];
+      const __half2* h2 = reinterpret_cast<const __half2*>(&src);
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const __half2* h2 = reinterpret_cast<const __half2*>(&src[j]);
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
+      for (int c = 0; c < 2; c++) {
         const float2 f = __half22float2(h2[c]);
         x[j][2 * c] = f.x, x[j][2 * c + 1] = f.y;
       }
     }
-    uint32_t o[4];
+    uint32_t o[2];
 #pragma unroll
-    for (int c = 0; c < 8; c += 2) {
+    for (int c = 0; c < 4; c += 2) {
       float r[2];
 #pragma unroll
       for (int u = 0; u < 2; u++) {
@@ -215,7 +204,7 @@ __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ bi
       const __half2 hv = __floats2half2_rn(r[0], r[1]);
       o[c / 2] = *reinterpret_cast<const uint32_t*>(&hv);
     }
-    *reinterpret_cast<uint4*>(out + (size_t)t * C + c8) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint2*>(out + (size_t)t * C + c4) = make_uint2(o[0], o[1]);
   }
 }
 
@@ -444,7 +433,7 @@ cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const i
 cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, __half* qkvc,
                         const int* tstart, const __half* const* hseq, const int* tseq, cudaStream_t st) {
   if (C % 8 || stride % 8 || (hseq && (!tstart || !tseq))) return cudaErrorInvalidValue;
-  dim3 grid((C / 8 + 127) / 128, (l + kConvT - 1) / kConvT);
+  dim3 grid((C / 4 + 127) / 128, (l + kConvT - 1) / kConvT);
   conv_kernel<<<grid, 128, 0, st>>>(big, stride, reinterpret_cast<const float4*>(conv_w), hist, l, C, tstart, hseq, tseq, qkvc);
   return cudaGetLastError();
 }
