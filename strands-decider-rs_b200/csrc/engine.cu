@@ -670,7 +670,7 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
                            e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, e->beta, e->decay,
                            fk->states + (size_t)Lw.slot * fk->nseq, fk->s_out ? fk->s_out + (size_t)Lw.slot * fk->nseq : nullptr,
                            e->of, fk->seq_off, fk->seq_len, fk->chunk0, fk->order, fk->chunk_tab, fk->nseq, fk->chunks, d.h,
-                           e->gdn_scratch, e->gdn_scratch_bytes, st)));
+                           e->gdn_scratch, e->gdn_scratch_bytes, e->num_sms, st)));
         else if (fk)
           LK(SD_PROF_GDN, gdn_bytes,
              sd::launch_gdn_chunked_packed(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, e->beta,

@@ -960,21 +960,9 @@ cudaError_t launch_gdn_two_phase_packed(const __half* q, const __half* k, int qk
                                         const float* beta, const float* g, const float* const* s_in, float* const* s_out,
                                         float* o, const int* seq_off, const int* seq_len, const int* chunk0, const int* order,
                                         const int* chunk_tab, int nseq, int chunks, int h, void* scratch, size_t scratch_bytes,
-                                        cudaStream_t st) {
+                                        int num_sms, cudaStream_t st) {
   if (nseq <= 0 || chunks <= 0 || h <= 0 || scratch_bytes < gdn_two_phase_packed_scratch(chunks, h) || nseq > 65535)
     return cudaErrorInvalidValue;
-  constexpr int DVS = 32;
-  static bool attr[kMaxDevices] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  if (!attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gdn_scan_kernel<DVS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(ScanSmem<DVS>));
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
-  }
   ChunkRec* rec = reinterpret_cast<ChunkRec*>(scratch);
   gdn_prep_kernel<<<dim3(chunks, h), 256, sizeof(PrepSmem), st>>>(q, k, qk_stride, v, v_stride, beta, g, 0, h, chunk_tab, rec);
   cudaError_t e = cudaGetLastError();
@@ -982,7 +970,12 @@ cudaError_t launch_gdn_two_phase_packed(const __half* q, const __half* k, int qk
   ScanPacked ps;
   ps.seq_off = seq_off, ps.seq_len = seq_len, ps.chunk0 = chunk0, ps.order = order, ps.s_in = s_in, ps.s_out = s_out;
   ps.total_chunks = chunks;
-  gdn_scan_kernel<DVS><<<dim3(h * (DK / DVS), nseq), 256, sizeof(ScanSmem<DVS>), st>>>(rec, 0, 0, h, nullptr, 0, o, ps);
+  // value slices of 64 columns once two CTAs per head and sequence fill the SMs (half the CTAs
+  // re-reading each chunk's record), else of 32 (more CTAs for a few sequences)
+  if ((long long)nseq * h * 2 >= num_sms)
+    gdn_scan_kernel<64><<<dim3(h * 2, nseq), 256, sizeof(ScanSmem<64>), st>>>(rec, 0, 0, h, nullptr, 0, o, ps);
+  else
+    gdn_scan_kernel<32><<<dim3(h * 4, nseq), 256, sizeof(ScanSmem<32>), st>>>(rec, 0, 0, h, nullptr, 0, o, ps);
   return cudaGetLastError();
 }
 
@@ -1036,7 +1029,9 @@ cudaError_t preload_gdn() {
       (e = cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem))) !=
           cudaSuccess ||
       (e = cudaFuncSetAttribute(gdn_scan_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(ScanSmem<32>))) != cudaSuccess)
+                                (int)sizeof(ScanSmem<32>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_scan_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(ScanSmem<64>))) != cudaSuccess)
     return e;
   return cudaFuncGetAttributes(&a, gdn_scan_kernel<32>);
 }

@@ -92,7 +92,7 @@ cudaError_t launch_gdn_two_phase_packed(const __half* q, const __half* k, int qk
                                         const float* beta, const float* g, const float* const* s_in, float* const* s_out,
                                         float* o, const int* seq_off, const int* seq_len, const int* chunk0, const int* order,
                                         const int* chunk_tab, int nseq, int chunks, int h, void* scratch, size_t scratch_bytes,
-                                        cudaStream_t st);
+                                        int num_sms, cudaStream_t st);
 // two-phase chunked scan for one long sequence (f16 rows): all chunks' intra-chunk work in parallel,
 // then the state scan; `scratch` holds gdn_two_phase_scratch(l, h) bytes of per-chunk records
 size_t gdn_two_phase_scratch(int l, int h);
