@@ -88,13 +88,24 @@ SD_DEV float swiglu(float gate, float up) {
 
 struct TileGrid {
   int ntiles, mtiles, splits, kps, KT;
+  int mmajor;  // tile order: 0, weight tiles outermost; 1, token tiles outermost
   __host__ __device__ int count() const { return ntiles * mtiles * splits; }
-  // consecutive tiles share the weight tile (same n-tile, all m-tiles and splits next to each other)
+  // Consecutive tiles share the weight tile (same n-tile, all m-tiles and splits next to each other),
+  // so the CTAs running at once read a few weight tiles and every activation tile: right while the
+  // activations stay in L2. With mmajor they share the token tile instead (all n-tiles of one m-tile
+  // next to each other): the activations stream from HBM once while the weights stay in L2.
   __device__ void decode(int t, int& nt, int& mt, int& sp, int& kt0, int& nk) const {
-    nt = t / (mtiles * splits);
-    const int r = t % (mtiles * splits);
-    mt = r / splits;
-    sp = r % splits;
+    if (mmajor) {
+      mt = t / (ntiles * splits);
+      const int r = t % (ntiles * splits);
+      nt = r / splits;
+      sp = r % splits;
+    } else {
+      nt = t / (mtiles * splits);
+      const int r = t % (mtiles * splits);
+      mt = r / splits;
+      sp = r % splits;
+    }
     kt0 = sp * kps;
     nk = max(0, min(KT, kt0 + kps) - kt0);
   }
@@ -555,6 +566,20 @@ void gemm_plan(const QWeight& w, int M, int num_sms, int* bn_out, int* splits_ou
   *kps_out = split_kps(KT, best_s);
 }
 
+// Tile order from the HBM traffic it implies: an operand that does not fit in (a share of) L2 is read
+// from HBM once per tile of the other operand's axis unless its own tiles are the outer loop. The
+// share is a quarter of the 126 MB L2 (each die's half holds the lines it reads fastest): on B200 at
+// M = 16384 the token-major order measured 1122 vs 849 TFLOP/s (down, K = 6144: 201 MB of
+// activations) and 1124 vs 1036 (gate_up, K = 2048: 67 MB), and the same at M = 1536.
+bool gemm_token_major(const QWeight& w, int M) {
+  constexpr double kL2 = 32e6;  // bytes of L2 an operand may occupy and still be re-read from L2
+  const double act = (double)M * w.k * 2, wts = (double)w.bytes;
+  const double ntiles = w.npad / kBM, mtiles = (M + 191) / 192;
+  const double weight_major = wts + (act > kL2 ? act * ntiles : act);
+  const double token_major = act + (wts > kL2 ? wts * mtiles : wts);
+  return token_major < weight_major;
+}
+
 cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
                     size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch) {
   if (nlaunch) *nlaunch = 0;
@@ -572,7 +597,7 @@ cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half*
   }
   CUtensorMap map;
   if (make_act_map(&map, act, M, w.k, lda, bn) != 0) return cudaErrorInvalidValue;
-  TileGrid tg{w.npad / kBM, (M + bn - 1) / bn, splits, kps, KT};
+  TileGrid tg{w.npad / kBM, (M + bn - 1) / bn, splits, kps, KT, gemm_token_major(w, M) ? 1 : 0};
   if (nlaunch) *nlaunch = splits == 1 ? 1 : 2;
   if (splits == 1)
     return silu ? launch_epi<kEpiSilu>(bn, map, w, M, tg, num_sms, y, ldy, nullptr, err, st)
