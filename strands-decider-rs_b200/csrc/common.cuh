@@ -102,6 +102,13 @@ SD_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+SD_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 SD_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
                "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
@@ -202,10 +209,26 @@ SD_DEV uint64_t sw128_desc(const void* smem_tile) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand tile stored with the 128-byte swizzle: each
+// row (one k) holds 64 consecutive f16 of the M or N dimension, 8-row groups are 1024 bytes apart, and
+// the next 64 of M or N start `lbo_bytes` further on.
+SD_DEV uint64_t sw128_mn_desc(const void* smem_tile, uint32_t lbo_bytes) {
+  uint64_t addr = smem_u32(smem_tile);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;                      // start address
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;  // leading byte offset: next 64 of M or N
+  d |= (uint64_t)(1024 >> 4) << 32;                  // stride byte offset: next 8 rows of K
+  d |= (uint64_t)1 << 46;                            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                            // SWIZZLE_128B
+  return d;
+}
+
 // Instruction descriptor, kind::f16: f16 A and B (K-major), f32 accumulator, M x N.
 __host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
+// The same with B MN-major (B stored k rows of N values).
+__host__ __device__ constexpr uint32_t idesc_f16_bmn(int m, int n) { return idesc_f16(m, n) | (1u << 16); }
 
 // ---------------------------------------------------------------------------------------------
 // int4 dequantisation. Weight words are stored with the even elements of an 8-element group in

@@ -610,7 +610,8 @@ struct Fork {
   __half* const* v_out = nullptr;
   const int *tpos, *tstart, *tseq, *seq_off, *seq_len, *plen, *blk;
   const int *chunk_tab = nullptr, *chunk0 = nullptr, *order = nullptr;
-  int nseq, nblk, max_len, max_p, max_rows, chunks = 0;
+  const int* blk128 = nullptr;  // (sequence, first query) per 128-query block, most keys first (the tcgen05 kernel)
+  int nseq, nblk, max_len, max_p, max_rows, chunks = 0, nblk128 = 0;
   bool two_phase = false;
   double pairs;       // causal (query, key) pairs of every sequence: len p + len (len + 1) / 2
   __half *kt, *vt;    // [hk][l][hd] K and V of the packed tokens
@@ -697,12 +698,21 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
           sd::AttnPacked pk;
           pk.blk = fk->blk, pk.seq_off = fk->seq_off, pk.seq_len = fk->seq_len, pk.kt = fk->kt, pk.vt = fk->vt, pk.T = l;
           pk.kp = fk->kp + (size_t)Lw.slot * fk->nseq, pk.vp = fk->vp + (size_t)Lw.slot * fk->nseq, pk.plen = fk->plen;
-          int splits = sd::attention_splits_packed(fk->nblk, fk->max_p, fk->max_len, d.hq, e->num_sms);
-          while (splits > 1 && sd::attention_split_bytes(l, d.hq, splits) > e->ws_bytes) splits--;
-          LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * fk->pairs,
-             (*nl = splits > 1 ? 2 : 1,
-              sd::launch_attention_packed(e->q, nullptr, nullptr, e->big, N, d.hd, 2 * d.hd, e->o, l, fk->max_p, fk->max_p,
-                                          d.hq, d.hk, d.hd, pk, fk->nblk, splits, e->ws, e->ws_bytes, st)));
+          if (fk->max_p == 0 && fk->max_len >= 128 && d.hd == 256) {
+            // fresh sequences (prefills): the tcgen05 kernel over 128-query blocks
+            sd::AttnTcArgs ta;
+            ta.blk = fk->blk128, ta.seq_off = fk->seq_off, ta.seq_len = fk->seq_len, ta.hq = d.hq, ta.hk = d.hk;
+            ta.gate = e->big, ta.gstride = N, ta.goff = d.hd, ta.gstep = 2 * d.hd, ta.out = e->o, ta.err = e->d_err;
+            LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * fk->pairs,
+               sd::launch_attention_tc(e->q, l, fk->kt, fk->vt, l, l, ta, fk->nblk128, st));
+          } else {
+            int splits = sd::attention_splits_packed(fk->nblk, fk->max_p, fk->max_len, d.hq, e->num_sms);
+            while (splits > 1 && sd::attention_split_bytes(l, d.hq, splits) > e->ws_bytes) splits--;
+            LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * fk->pairs,
+               (*nl = splits > 1 ? 2 : 1,
+                sd::launch_attention_packed(e->q, nullptr, nullptr, e->big, N, d.hd, 2 * d.hd, e->o, l, fk->max_p, fk->max_p,
+                                            d.hq, d.hk, d.hd, pk, fk->nblk, splits, e->ws, e->ws_bytes, st)));
+          }
           if (fk->k_out)  // the sequences' keys and values (prefix and own) into their new snapshots
             LK(SD_PROF_OTHER, 8.0 * d.hk * d.hd * (L + fk->max_p),
                sd::launch_kv_pack(fk->kt, fk->vt, l, d.hk, d.hd, fk->seq_off, fk->seq_len, fk->plen,
@@ -715,12 +725,20 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
            sd::launch_qk_prep(e->big, N, Lw.q_norm, Lw.k_norm, e->rope, l, p, SD_CONTEXT, d, nullptr, e->q, e->kc[Lw.slot],
                               e->vc[Lw.slot], st));
         const double pairs = L * p + L * (L + 1) / 2;  // causal (query, key) pairs
-        int splits = sd::attention_splits(l, p, d.hq, e->num_sms);  // keys split for short continuations
-        while (splits > 1 && sd::attention_split_bytes(l, d.hq, splits) > e->ws_bytes) splits--;
-        LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * pairs,
-           (*nl = splits > 1 ? 2 : 1,  // with split keys, a second kernel merges the splits
-            sd::launch_attention(e->q, e->kc[Lw.slot], e->vc[Lw.slot], e->big, N, d.hd, 2 * d.hd, e->o, l, p, SD_CONTEXT,
-                                 d.hq, d.hk, d.hd, splits, e->ws, e->ws_bytes, st)));
+        if (l >= 128 && d.hd == 256) {  // query blocks of 128: the tcgen05 kernel
+          sd::AttnTcArgs ta;
+          ta.l = l, ta.p = p, ta.hq = d.hq, ta.hk = d.hk;
+          ta.gate = e->big, ta.gstride = N, ta.goff = d.hd, ta.gstep = 2 * d.hd, ta.out = e->o, ta.err = e->d_err;
+          LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * pairs,
+             sd::launch_attention_tc(e->q, l, e->kc[Lw.slot], e->vc[Lw.slot], SD_CONTEXT, p + l, ta, (l + 127) / 128, st));
+        } else {
+          int splits = sd::attention_splits(l, p, d.hq, e->num_sms);  // keys split for short continuations
+          while (splits > 1 && sd::attention_split_bytes(l, d.hq, splits) > e->ws_bytes) splits--;
+          LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * pairs,
+             (*nl = splits > 1 ? 2 : 1,  // with split keys, a second kernel merges the splits
+              sd::launch_attention(e->q, e->kc[Lw.slot], e->vc[Lw.slot], e->big, N, d.hd, 2 * d.hd, e->o, l, p, SD_CONTEXT,
+                                   d.hq, d.hk, d.hd, splits, e->ws, e->ws_bytes, st)));
+        }
         MM(Lw.o_proj, e->o, d.hq * d.hd, e->y, d.d, false);
         }
       }
@@ -887,7 +905,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   if (e->trace_host) return e->fail(SD_ERR_INVALID, "%s: per-layer tracing is for sd_forward only", fn);
   if (keep && !snaps_out) return e->fail(SD_ERR_INVALID, "%s: keep without a snapshot output", fn);
   long long T = 0, R = 0;
-  int max_len = 0, max_p = 0, max_rows = 0, nblk = 0, chunks = 0, max_chunks = 0;
+  int max_len = 0, max_p = 0, max_rows = 0, nblk = 0, nblk128 = 0, chunks = 0, max_chunks = 0;
   double pairs = 0;
   for (int b = 0; b < nq; b++) {
     const sd_snapshot* c = caches ? caches[b] : nullptr;
@@ -904,6 +922,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
     max_rows = std::max(max_rows, p + (int)lens[b]);
     pairs += (double)lens[b] * p + (double)lens[b] * (lens[b] + 1) / 2;
     nblk += (lens[b] + 63) / 64;
+    nblk128 += (lens[b] + 127) / 128;
     chunks += (lens[b] + 63) / 64;
     max_chunks = std::max(max_chunks, ((int)lens[b] + 63) / 64);
   }
@@ -921,9 +940,9 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   // chunk_tab[2 chunks], chunk0[nq], order[nq]; then ids[T] (host ids)
   const size_t per_set = (size_t)(2 * e->n_lin + 2 * e->n_full) * nq;
   const size_t i0 = 2 * per_set * (keep ? 2 : 1);  // ints before the index arrays
-  const size_t n_idx = i0 + 3 * (size_t)T + 3 * (size_t)nq + 2 * (size_t)nblk;
+  const size_t n_idx = i0 + 3 * (size_t)T + 3 * (size_t)nq + 2 * (size_t)nblk + 2 * (size_t)nblk128;
   const size_t n_gdn = two_phase ? 2 * (size_t)chunks + 2 * (size_t)nq : 0;
-  const size_t n_all = packed_ints(e, T, nq, nblk, R, keep, two_phase ? chunks : -1, ids_host != nullptr);
+  const size_t n_all = packed_ints(e, T, nq, nblk + nblk128, R, keep, two_phase ? chunks : -1, ids_host != nullptr);
   {  // rows in range
     long long r = 0;
     for (int b = 0; b < nq; b++)
@@ -981,6 +1000,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   int* slen = soff + nq;
   int* plen = slen + nq;
   int* blk = plen + nq;
+  int* blk128 = blk + 2 * (size_t)nblk;
   int* grows = e->fk_pin[slot] + n_idx;
   int* ctab = grows + R;
   int* c0 = ctab + 2 * (size_t)chunks;
@@ -1002,6 +1022,16 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
       t += lens[b];
     }
     if (two_phase) std::stable_sort(order, order + nq, [&](int a, int b) { return lens[a] > lens[b]; });
+    // 128-query blocks, those with the most keys (latest queries) first
+    int k2 = 0;
+    for (int b = 0; b < nq; b++)
+      for (int q0 = 0; q0 < lens[b]; q0 += 128, k2++) blk128[2 * k2] = b, blk128[2 * k2 + 1] = q0;
+    std::vector<std::pair<int, int>> bl(nblk128);
+    for (int i = 0; i < nblk128; i++) bl[i] = {blk128[2 * i], blk128[2 * i + 1]};
+    std::stable_sort(bl.begin(), bl.end(), [&](const std::pair<int, int>& x, const std::pair<int, int>& y) {
+      return std::min(x.second + 128, (int)lens[x.first]) > std::min(y.second + 128, (int)lens[y.first]);
+    });
+    for (int i = 0; i < nblk128; i++) blk128[2 * i] = bl[i].first, blk128[2 * i + 1] = bl[i].second;
   }
   if (ids_host) memcpy(e->fk_pin[slot] + n_idx + R + n_gdn, ids_host, T * sizeof(uint32_t));
   CK(cudaMemcpyAsync(e->fk_meta, e->fk_pin[slot], n_all * sizeof(int), cudaMemcpyHostToDevice, st));
@@ -1027,6 +1057,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   }
   fk.tpos = di, fk.tstart = di + T, fk.tseq = di + 2 * T;
   fk.seq_off = di + 3 * T, fk.seq_len = fk.seq_off + nq, fk.plen = fk.seq_len + nq, fk.blk = fk.plen + nq;
+  fk.blk128 = fk.blk + 2 * (size_t)nblk, fk.nblk128 = nblk128;
   if (two_phase) {
     fk.chunk_tab = dm + n_idx + R;
     fk.chunk0 = fk.chunk_tab + 2 * (size_t)chunks;
@@ -1152,6 +1183,7 @@ int sd_engine_create(const char* model_dir, int device, sd_engine** out) {
   }
   cudaError_t ce;
   if ((ce = sd::preload_gemm()) != cudaSuccess || (ce = sd::preload_attention()) != cudaSuccess ||
+      (ce = sd::preload_attention_tc()) != cudaSuccess ||
       (ce = sd::preload_gdn()) != cudaSuccess || (ce = sd::preload_kernels()) != cudaSuccess) {
     set_global_error(std::string("sd_engine_create: loading the kernels: ") + cudaGetErrorString(ce));
     sd_engine_destroy(e);
@@ -1208,7 +1240,7 @@ int sd_engine_reserve(sd_engine* e, int32_t max_tokens, int32_t max_seqs, int32_
     return e->fail(SD_ERR_INVALID, "sd_engine_reserve: tokens 1..65536, sequences 1..4096, rows >= 0");
   cudaSetDevice(e->device);
   const long long T = max_tokens, nq = max_seqs, chunks = T / 64 + nq;
-  const size_t ints = packed_ints(e, T, nq, chunks, max_rows, true, chunks, true);
+  const size_t ints = packed_ints(e, T, nq, 2 * chunks, max_rows, true, chunks, true);  // 64- and 128-query blocks
   int rc;
   if ((rc = ensure_pool(e, max_tokens)) != SD_OK || (rc = ensure_packed(e, T, ints, chunks)) != SD_OK ||
       (rc = ensure_pinned(e, max_tokens, max_rows)) != SD_OK)
@@ -1537,6 +1569,14 @@ int sd_attention(const void* q, const void* k, const void* v, const void* gate, 
   if (!q || !k || !v || !out || l <= 0 || p < 0 || p + l > lt || hk <= 0 || hq % hk) {
     set_global_error("sd_attention: bad arguments");
     return SD_ERR_INVALID;
+  }
+  if (l >= 128 && hd == 256) {  // query blocks of 128: the tcgen05 kernel
+    sd::AttnTcArgs ta;
+    ta.l = l, ta.p = p, ta.hq = hq, ta.hk = hk, ta.gate = (const __half*)gate, ta.gstride = gstride, ta.goff = goff,
+    ta.gstep = gstep, ta.out = (__half*)out;
+    return op_result(sd::launch_attention_tc((const __half*)q, l, (const __half*)k, (const __half*)v, lt, p + l, ta,
+                                             (l + 127) / 128, (cudaStream_t)stream),
+                     "sd_attention");
   }
   return op_result(sd::launch_attention((const __half*)q, (const __half*)k, (const __half*)v, (const __half*)gate, gstride, goff,
                                         gstep, (__half*)out, l, p, lt, hq, hk, hd, 1, nullptr, 0, (cudaStream_t)stream),

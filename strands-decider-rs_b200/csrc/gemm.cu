@@ -498,6 +498,22 @@ int make_act_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, 
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+// A 3-D f16 tensor map [z][y][x] (x contiguous, y rows `ystride` elements apart, z slabs `zstride`
+// elements apart; dims x, y, z) with boxes of 64 x box_y x 1 and the 128-byte swizzle. Coordinates
+// outside the dims read zeros.
+int make_map_3d(CUtensorMap* map, const void* ptr, int x, int y, int z, long long ystride, long long zstride, int box_y) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  cuuint64_t dims[3] = {(cuuint64_t)x, (cuuint64_t)y, (cuuint64_t)z};
+  cuuint64_t strides[2] = {(cuuint64_t)ystride * 2, (cuuint64_t)zstride * 2};
+  cuuint32_t box[3] = {64u, (cuuint32_t)box_y, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
 template <int BN, int EPI>
 static cudaError_t launch_bn(const CUtensorMap& map, const QWeight& w, int M, const TileGrid& tg, int num_sms, __half* y,
                              int ldy, float* ws, int* err, cudaStream_t st) {

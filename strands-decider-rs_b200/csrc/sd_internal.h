@@ -39,6 +39,7 @@ void gemm_plan(const QWeight& w, int M, int num_sms, int* bn, int* splits, int* 
 cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
                     size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch = nullptr);
 int make_act_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
+int make_map_3d(CUtensorMap* map, const void* ptr, int x, int y, int z, long long ystride, long long zstride, int box_y);
 
 // Model dims the kernels are specialised for (src/kernels.rs:813-835).
 struct Dims {
@@ -130,6 +131,23 @@ cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, 
 cudaError_t launch_attention_packed(const __half* q, const __half* k, const __half* v, const __half* gate, int gstride,
                                     int goff, int gstep, __half* out, int T, int p, int lt, int hq, int hk, int hd,
                                     const AttnPacked& pk, int nblk, int splits, float* ws, size_t ws_bytes, cudaStream_t st);
+// attn_tc.cu: the same attention on tcgen05 for query blocks of 128 (head dim 256). Single sequence
+// (blk null): l queries after p cached keys, query t at row t of q, keys rows 0 .. p + l - 1. Packed
+// (blk non-null): [nblk][2] (sequence, first query, a multiple of 128), sequence b at rows seq_off[b]
+// .. + seq_len[b] of q, the keys and out, with no prefix.
+struct AttnTcArgs {
+  const int* blk = nullptr;
+  const int* seq_off = nullptr;
+  const int* seq_len = nullptr;
+  int l = 0, p = 0, hq = 0, hk = 0;
+  const __half* gate = nullptr;
+  int gstride = 0, goff = 0, gstep = 0;
+  __half* out = nullptr;
+  int* err = nullptr;  // a bounded wait that gave up records its code here
+};
+cudaError_t launch_attention_tc(const __half* q, int qrows, const __half* k, const __half* v, int krows, int krows_valid,
+                                const AttnTcArgs& a, int nblk, cudaStream_t st);
+cudaError_t preload_attention_tc();
 int attention_splits_packed(int nblk, int p, int max_len, int hq, int num_sms);
 int attention_splits(int l, int p, int hq, int num_sms);
 size_t attention_split_bytes(int l, int hq, int splits);

@@ -91,6 +91,41 @@ def test_attention_matches_oracle(torch, l, p, splits):
     assert np.abs(got - want).max() < 4e-3
 
 
+@pytest.mark.parametrize("l,p,hq,hk,gated", [(128, 0, 8, 2, True), (2048, 0, 8, 2, True), (200, 700, 8, 2, True),
+                                             (1000, 3000, 8, 2, True), (513, 17, 16, 2, False), (130, 1, 4, 4, True)])
+def test_attention_tc_matches_oracle(torch, l, p, hq, hk, gated):
+    """sd_attention on query blocks of 128 (the tcgen05 kernel: l >= 128) against the oracle and against
+    the mma.sync kernel (sd_attention_split with one split) on the same inputs: prefills, continuations
+    of long prefixes, ragged last blocks, other head ratios, no gate."""
+    from strands_decider.engine import attention
+    rng = np.random.default_rng(l * 3 + p)
+    hd, lt = 256, 4096
+    q = rng.standard_normal((hq, l, hd)).astype(np.float16)
+    kc = np.full((hk, lt, hd), np.nan, np.float16)  # rows past the valid keys must never be read
+    vc = np.full((hk, lt, hd), np.nan, np.float16)
+    kc[:, :p + l] = rng.standard_normal((hk, p + l, hd))
+    vc[:, :p + l] = rng.standard_normal((hk, p + l, hd))
+    gw = 3 * hq * hd
+    gate = rng.standard_normal((l, gw)).astype(np.float16)
+    if gated:
+        want = oracle.attn(q, kc[:, :p + l], vc[:, :p + l], gate, gw, hd, 2 * hd, p=p).astype(np.float32)
+    else:
+        want = oracle.attn(q, kc[:, :p + l], vc[:, :p + l], None, 0, 0, 0, p=p).astype(np.float32)
+    qd, kd, vd, gd = (dev(torch, x.view(np.uint16)) for x in (q, kc, vc, gate))
+    ws = torch.empty(32 << 20, dtype=torch.uint8, device="cuda")
+    outs = []
+    for splits in (None, 1):
+        out = torch.zeros((l, hq * hd), dtype=torch.float16, device="cuda")
+        attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), gd.data_ptr() if gated else None, gw, hd, 2 * hd, out.data_ptr(),
+                  l, p, lt, hq, hk, hd, splits=splits, ws=ws.data_ptr(), ws_bytes=ws.numel())
+        torch.cuda.synchronize()
+        outs.append(out.cpu().numpy().astype(np.float32))
+    tc, legacy = outs
+    assert np.isfinite(tc).all()
+    assert np.abs(tc - want).max() < 4e-3
+    assert np.abs(tc - legacy).max() < 4e-3
+
+
 def _gdn_inputs(rng, b, l, h):
     q = rng.standard_normal((b, l, h, 128)).astype(np.float32)
     k = rng.standard_normal((b, l, h, 128)).astype(np.float32)
