@@ -414,7 +414,7 @@ def run_kernel_workload(args):
     dequantizing matmul shape. Inputs are seeded synthetic tensors with the configs' shapes."""
     import torch
     from strands_decider import model as M
-    from strands_decider.engine import QWeight, attention, gdn
+    from strands_decider.engine import QWeight, attention_batch, gdn
     torch.cuda.set_device(0)
     hbm, tf_burst, tf_sus, src = peaks()
     g = torch.Generator(device="cuda").manual_seed(args.seed)
@@ -439,10 +439,9 @@ def run_kernel_workload(args):
         gate = torch.randn(B, S, hq * 2 * hd, generator=g, device="cuda").half()
         o = torch.empty(B, S, hq * hd, device="cuda").half()
 
-        def fn():
-            for b in range(B):
-                attention(q[b].data_ptr(), k[b].data_ptr(), v[b].data_ptr(), gate[b].data_ptr(), hq * 2 * hd, hd, 2 * hd,
-                          o[b].data_ptr(), S, 0, S, hq, hk, hd)
+        def fn():  # the batch in one launch (sd_attention_batch)
+            attention_batch(q.data_ptr(), k.data_ptr(), v.data_ptr(), gate.data_ptr(), hq * 2 * hd, hd, 2 * hd, o.data_ptr(), B,
+                            S, 0, S, hq, hk, hd)
         ms = timed(fn, args.steps, args.warmup)
         work = 4.0 * hd * hq * B * S * (S + 1) / 2
         line = {"metric": "attention TFLOP/s (config 2)", "value": work / ms / 1e9, "unit": "TFLOP/s", "ms_per_step": ms,

@@ -186,10 +186,18 @@ int sd_attention(const void* q_dev, const void* k_dev, const void* v_dev, const 
                  int32_t goff, int32_t gstep, void* out_dev, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk,
                  int32_t hd, void* stream);
 
-/* sd_attention with the keys split across `splits` CTAs per (query block, head) (0: the engine's
- * choice, which splits only when the query blocks x heads leave SMs idle, as for a short continuation
- * over a long prefix); each split's partial result is merged by a second kernel. ws_dev: f32
- * workspace of splits x hq x l x (hd + 2) floats (16-byte aligned; unused with one split). */
+/* sd_attention over `batch` independent sequences in one launch (the reference dispatches `attn` once
+ * per sequence): q_dev [batch][hq][l][hd], k_dev/v_dev [batch][hk][lt][hd], gate rows and out rows
+ * batch-major ([batch][l][gstride], [batch][l][hq * hd]); everything else as sd_attention. */
+int sd_attention_batch(const void* q_dev, const void* k_dev, const void* v_dev, const void* gate_dev, int32_t gstride,
+                       int32_t goff, int32_t gstep, void* out_dev, int32_t batch, int32_t l, int32_t p, int32_t lt, int32_t hq,
+                       int32_t hk, int32_t hd, void* stream);
+
+/* sd_attention on the mma.sync kernel with the keys split across `splits` CTAs per (query block,
+ * head) (0: the engine's choice, which splits only when the query blocks x heads leave SMs idle, as
+ * for a short continuation over a long prefix); each split's partial result is merged by a second
+ * kernel. ws_dev: f32 workspace of splits x hq x l x (hd + 2) floats (16-byte aligned; unused with one
+ * split). sd_attention itself takes the tcgen05 kernel for l >= 128 (query blocks of 128). */
 int sd_attention_split(const void* q_dev, const void* k_dev, const void* v_dev, const void* gate_dev, int32_t gstride,
                        int32_t goff, int32_t gstep, void* out_dev, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk,
                        int32_t hd, int32_t splits, void* ws_dev, size_t ws_bytes, void* stream);

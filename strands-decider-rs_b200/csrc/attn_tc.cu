@@ -3,17 +3,22 @@
 // V / (1 + exp(-gate)) ), f32 scores and accumulation, probabilities rounded to f16 as the P operand
 // of the PV product, as attn.cu computes them.
 //
-// One CTA per (128 queries, q head); six warps:
-//   warp 0     TMA: the Q tile once (128 x 256 f16, four 64-column boxes), then per block of 64 keys
-//              its K tile and its V tile (64 x 256 each) into two-deep rings of their own;
-//   warp 1     one thread issues tcgen05.mma: S_j = Q K_j^T (M 128, N 64, K 256: 16 MMAs, both
+// One CTA per (128 queries, q head), keys in blocks of 128; six warps:
+//   warp 0     TMA: the Q tile (128 x 256 f16, four 64-column boxes) once, then the K and V tiles of
+//              every key block into one ring of nine 16 KB slots, in the order the MMAs read them
+//              (K_0, K_1, V_0, K_2, V_1, ...): a K tile as four boxes of 128 keys x 64 columns, a V
+//              tile as four chunks of 32 keys x 256 columns, so a slot frees as soon as the MMAs of
+//              its part are done and the next tiles stream in behind them;
+//   warp 1     one thread issues tcgen05.mma: S_j = Q K_j^T (M 128, N 128, K 256: 16 MMAs, both
 //              operands K-major from shared memory) into one of two S buffers in TMEM, then
-//              O += P_{j-1} V_{j-1} (M 128, N 256, K 64: 4 MMAs, P from TMEM, V MN-major from shared
+//              O += P_{j-1} V_{j-1} (M 128, N 256, K 128: 8 MMAs, P from TMEM, V MN-major from shared
 //              memory), so the softmax of block j overlaps the PV product of block j-1;
-//   warps 2-5  softmax, one thread per query row (its TMEM lane): S row out of TMEM, causal mask,
-//              row max, probabilities, row sum in registers, no shuffles; P (f16) into one of two P
-//              buffers in TMEM. At the end: O out of TMEM, / row sum, sigmoid gate, f16 rows out.
-// Tensor memory (512 columns): S 2 x 64, P 2 x 32, O 256.
+//   warps 2-5  softmax, one thread per query row (its TMEM lane): the S row out of TMEM, causal mask,
+//              row max, probabilities and row sum in registers, no shuffles; P (f16) written over
+//              the first half of the same S buffer. At the end: O out of TMEM, / row sum, sigmoid
+//              gate, f16 rows out.
+// Tensor memory (512 columns): S/P 2 x 128, O 256. An S buffer is rewritten (S_{j+2}) only after the
+// PV product that read its P (PV_j) has completed.
 //
 // The running max is updated lazily: probabilities are taken against the max used so far, m_used,
 // and O (in TMEM) is rescaled only when a row's max grows past m_used + 8 (then P <= e^8, well inside
@@ -28,30 +33,31 @@
 namespace sd {
 
 namespace {
-constexpr int TQ = 128, TK = 64, HD = 256;
-constexpr int kQBox = TQ * 64 * 2;    // 16 KB: 128 rows x 64 columns
-constexpr int kKVBox = TK * 64 * 2;   // 8 KB: 64 rows x 64 columns
-constexpr int kQBytes = 4 * kQBox;    // 64 KB
-constexpr int kKVBytes = 4 * kKVBox;  // 32 KB
-constexpr int kOffK = kQBytes, kOffV = kOffK + 2 * kKVBytes, kOffBar = kOffV + 2 * kKVBytes;
+constexpr int TQ = 128, TK = 128, HD = 256;
+constexpr int kQBox = TQ * 64 * 2;  // 16 KB: 128 rows x 64 columns
+constexpr int kQBytes = 4 * kQBox;  // 64 KB
+constexpr int kSlot = 16384;        // one ring slot: a K box (128 keys x 64) or a V chunk (32 keys x 256)
+constexpr int kVSub = 4096;         // a V chunk's 64-column part (32 keys x 64)
+constexpr int kSlots = 9;
+constexpr int kOffRing = kQBytes, kOffBar = kOffRing + kSlots * kSlot;
 // barriers
 enum {
   BQ_FULL = 0,
-  BK_FULL = 1,    // [2] K tile landed (TMA bytes)
-  BK_EMPTY = 3,   // [2] S MMAs that read it completed
-  BV_FULL = 5,    // [2]
-  BV_EMPTY = 7,   // [2] PV MMAs that read it completed
-  BS_FULL = 9,    // [2] S_j in TMEM
-  BS_EMPTY = 11,  // [2] the softmax warps read S_j (4 arrivals)
-  BP_FULL = 13,   // [2] P_j in TMEM and O rescaled (4 arrivals)
-  BPV_DONE = 15,  // [2] PV_j completed (P buffer free, O updated)
-  BO_FULL = 17,   // every PV completed
-  BMMA_END = 18,  // every MMA issued completed (teardown)
-  kBars = 19
+  B_FULL = 1,                // [kSlots] a slot's tile part landed (TMA bytes)
+  B_EMPTY = 1 + kSlots,      // [kSlots] the MMAs that read it completed
+  BS_FULL = 1 + 2 * kSlots,  // [2] S_j in TMEM
+  BP_FULL = BS_FULL + 2,     // [2] P_j in TMEM and O rescaled (4 arrivals)
+  BPV_DONE = BP_FULL + 2,    // [2] PV_j completed (its S buffer free, O updated)
+  BO_FULL = BPV_DONE + 2,    // every PV completed
+  BMMA_END = BO_FULL + 1,    // every MMA issued completed (teardown)
+  kBars = BMMA_END + 1
 };
 constexpr int kSmem = kOffBar + kBars * 8 + 16 + 1024;
-constexpr uint32_t kColS = 0, kColP = 128, kColO = 256, kTmemCols = 512;
-constexpr float kLazy = 8.0f;  // rescale O once a row max grows past the one in use by this much
+constexpr uint32_t kColO = 256, kTmemCols = 512;  // S/P buffers at columns 0 and 128
+// Scores are handled in the log2 domain: y = s / 16 * log2(e), probabilities 2^(y - m).
+constexpr float kScaleL2 = 0.0625f * 1.4426950408889634f;
+constexpr float kLazy = 8.0f * 1.4426950408889634f;  // rescale O once a row max grows past the one in use by e^8
+constexpr int kThreads = 192;
 
 __device__ int g_attn_tc_err;  // error slot of calls without one
 
@@ -61,22 +67,29 @@ SD_DEV bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort, int* e
 SD_DEV bool wait_bar_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
   return mbar_wait_warp(bar, parity, abort, err ? err : &g_attn_tc_err, code);
 }
+SD_DEV float ex2(float x) {  // 2^x (the hardware's approximate exponential, as __expf uses)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 SD_DEV uint32_t pack_h2f(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 }  // namespace
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const AttnTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base + kOffRing;
   uint64_t* bar = reinterpret_cast<uint64_t*>(base + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, kh = h / (a.hq / a.hk);
+  const int bz = blockIdx.z;  // batch element (single-sequence mode): q / k / v slabs bz * heads + head
 
   // this CTA's queries: q0 .. q0 + nq - 1 of their sequence (positions p + q0 + i), rows tok0 + i of
   // q / gate / out; the sequence's keys are rows kbase .. of the K/V tensors
@@ -99,15 +112,14 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[BQ_FULL], 1);
-    for (int s = 0; s < 2; s++) {
-      mbar_init(&bar[BK_FULL + s], 1);
-      mbar_init(&bar[BK_EMPTY + s], 1);
-      mbar_init(&bar[BV_FULL + s], 1);
-      mbar_init(&bar[BV_EMPTY + s], 1);
-      mbar_init(&bar[BS_FULL + s], 1);
-      mbar_init(&bar[BS_EMPTY + s], 4);
-      mbar_init(&bar[BP_FULL + s], 4);
-      mbar_init(&bar[BPV_DONE + s], 1);
+    for (int s = 0; s < kSlots; s++) {
+      mbar_init(&bar[B_FULL + s], 1);
+      mbar_init(&bar[B_EMPTY + s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&bar[BS_FULL + b], 1);
+      mbar_init(&bar[BP_FULL + b], 4);
+      mbar_init(&bar[BPV_DONE + b], 1);
     }
     mbar_init(&bar[BO_FULL], 1);
     mbar_init(&bar[BMMA_END], 1);
@@ -129,60 +141,86 @@ __global__ void __launch_bounds__(192, 1)
       prefetch_tmap(&kmap);
       prefetch_tmap(&vmap);
       mbar_arrive_expect_tx(&bar[BQ_FULL], kQBytes);
-      for (int c = 0; c < 4; c++) tma_load_3d(base + c * kQBox, &qmap, &bar[BQ_FULL], c * 64, tok0, h);
-      int kissued = 0, vissued = 0;
+      for (int c = 0; c < 4; c++) tma_load_3d(base + c * kQBox, &qmap, &bar[BQ_FULL], c * 64, tok0, bz * a.hq + h);
+      // ring items in MMA order: K_0, then per block j >= 1 K_j and V_{j-1}, then V_{nkb-1}
+      int it = 0;
       bool ok = true;
-      for (int j = 0; j < nkb && ok; j++) {
-        const int s = j & 1;
-        if (j >= 2 && !(ok = wait_bar(&bar[BK_EMPTY + s], ((j >> 1) - 1) & 1, abort, a.err, kErrTimeoutEmpty))) break;
-        mbar_arrive_expect_tx(&bar[BK_FULL + s], kKVBytes);
-        for (int c = 0; c < 4; c++)
-          tma_load_3d(base + kOffK + s * kKVBytes + c * kKVBox, &kmap, &bar[BK_FULL + s], c * 64, kbase + j * TK, kh);
-        kissued++;
-        if (j >= 2 && !(ok = wait_bar(&bar[BV_EMPTY + s], ((j >> 1) - 1) & 1, abort, a.err, kErrTimeoutEmpty))) break;
-        mbar_arrive_expect_tx(&bar[BV_FULL + s], kKVBytes);
-        for (int c = 0; c < 4; c++)
-          tma_load_3d(base + kOffV + s * kKVBytes + c * kKVBox, &vmap, &bar[BV_FULL + s], c * 64, kbase + j * TK, kh);
-        vissued++;
+      auto slot_wait = [&]() -> int {  // the next slot, once its previous tile part is consumed
+        const int s = it % kSlots, u = it / kSlots;
+        if (u >= 1 && !wait_bar(&bar[B_EMPTY + s], (u - 1) & 1, abort, a.err, kErrTimeoutEmpty)) return -1;
+        return s;
+      };
+      for (int j = 0; j <= nkb && ok; j++) {
+        if (j < nkb)
+          for (int c = 0; c < 4 && ok; c++, it++) {  // K_j box c: keys j*128 .., columns 64c ..
+            const int s = slot_wait();
+            if (s < 0) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bar[B_FULL + s], kSlot);
+            tma_load_3d(ring + s * kSlot, &kmap, &bar[B_FULL + s], c * 64, kbase + j * TK, bz * a.hk + kh);
+          }
+        if (j >= 1)
+          for (int c = 0; c < 4 && ok; c++, it++) {  // V_{j-1} chunk c: keys (j-1)*128 + 32c .., all columns
+            const int s = slot_wait();
+            if (s < 0) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bar[B_FULL + s], kSlot);
+            for (int hb = 0; hb < 4; hb++)
+              tma_load_3d(ring + s * kSlot + hb * kVSub, &vmap, &bar[B_FULL + s], hb * 64, kbase + (j - 1) * TK + c * 32,
+                          bz * a.hk + kh);
+          }
       }
       // no copy may land after the CTA has left: wait (bounded) for the last ones issued
       mbar_drain(&bar[BQ_FULL], 0);
-      for (int j = max(0, kissued - 2); j < kissued; j++) mbar_drain(&bar[BK_FULL + (j & 1)], (j >> 1) & 1);
-      for (int j = max(0, vissued - 2); j < vissued; j++) mbar_drain(&bar[BV_FULL + (j & 1)], (j >> 1) & 1);
+      for (int i = max(0, it - kSlots); i < it; i++) mbar_drain(&bar[B_FULL + i % kSlots], (i / kSlots) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idS = idesc_f16(TQ, TK), idPV = idesc_f16_bmn(TQ, HD);
+      // descriptors of the first box of each tile; a box, a k step or a slot is an add to the start
+      // address field (16-byte units)
+      const uint64_t qd0 = sw128_desc(base), rd0 = sw128_desc(ring), vd0 = sw128_mn_desc(ring, kVSub);
       bool ok = wait_bar(&bar[BQ_FULL], 0, abort, a.err, kErrTimeoutFull);
       tc_fence_after();
+      int it = 0;
       for (int j = 0; j <= nkb && ok; j++) {
-        if (j < nkb) {  // S_j = Q K_j^T
-          const int s = j & 1;
-          if (!(ok = wait_bar(&bar[BK_FULL + s], (j >> 1) & 1, abort, a.err, kErrTimeoutFull))) break;
-          if (j >= 2 && !(ok = wait_bar(&bar[BS_EMPTY + s], ((j >> 1) - 1) & 1, abort, a.err, kErrTimeoutEmpty))) break;
-          tc_fence_after();
-          const uint8_t* kt = base + kOffK + s * kKVBytes;
+        if (j < nkb) {  // S_j = Q K_j^T into buffer j & 1, once PV_{j-2} (which read its P) is done
+          const int b = j & 1;
+          if (j >= 2 && !(ok = wait_bar(&bar[BPV_DONE + b], ((j >> 1) - 1) & 1, abort, a.err, kErrTimeoutEmpty))) break;
+          for (int c = 0; c < 4; c++, it++) {
+            const int s = it % kSlots;
+            if (!(ok = wait_bar(&bar[B_FULL + s], (it / kSlots) & 1, abort, a.err, kErrTimeoutFull))) break;
+            tc_fence_after();
+            const uint64_t kd = rd0 + (uint64_t)(s * (kSlot >> 4));
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; kk++) {  // K 16 per MMA: +32 bytes within a 64-column box
-            const uint64_t qd = sw128_desc(base + (kk >> 2) * kQBox) + 2 * (kk & 3);
-            const uint64_t kd = sw128_desc(kt + (kk >> 2) * kKVBox) + 2 * (kk & 3);
-            tc_mma_f16(tmem + kColS + s * TK, qd, kd, idS, kk > 0);
+            for (int k4 = 0; k4 < 4; k4++)  // K 16 per MMA: +32 bytes within the 64-column box
+              tc_mma_f16(tmem + b * TK, qd0 + (uint64_t)(c * (kQBox >> 4) + 2 * k4), kd + (uint64_t)(2 * k4), idS,
+                         (c | k4) != 0);
+            tc_commit(&bar[B_EMPTY + s]);
           }
-          tc_commit(&bar[BK_EMPTY + s]);
-          tc_commit(&bar[BS_FULL + s]);
+          if (!ok) break;
+          tc_commit(&bar[BS_FULL + b]);
         }
         if (j >= 1) {  // O += P_{j-1} V_{j-1}
-          const int jj = j - 1, s = jj & 1;
-          if (!(ok = wait_bar(&bar[BP_FULL + s], (jj >> 1) & 1, abort, a.err, kErrTimeoutFull))) break;
-          if (!(ok = wait_bar(&bar[BV_FULL + s], (jj >> 1) & 1, abort, a.err, kErrTimeoutFull))) break;
-          tc_fence_after();
-          const uint8_t* vt = base + kOffV + s * kKVBytes;
+          const int jj = j - 1, b = jj & 1;
+          if (!(ok = wait_bar(&bar[BP_FULL + b], (jj >> 1) & 1, abort, a.err, kErrTimeoutFull))) break;
+          for (int c = 0; c < 4; c++, it++) {
+            const int s = it % kSlots;
+            if (!(ok = wait_bar(&bar[B_FULL + s], (it / kSlots) & 1, abort, a.err, kErrTimeoutFull))) break;
+            tc_fence_after();
+            const uint64_t vd = vd0 + (uint64_t)(s * (kSlot >> 4));
 #pragma unroll
-          for (int kk = 0; kk < TK / 16; kk++)  // K 16 per MMA: 16 key rows of V (two 1024-byte groups)
-            tc_mma_f16_ts(tmem + kColO, tmem + kColP + s * (TK / 2) + kk * 8, sw128_mn_desc(vt + kk * 2048, kKVBox), idPV,
-                          (jj | kk) != 0);
-          tc_commit(&bar[BV_EMPTY + s]);
-          tc_commit(&bar[BPV_DONE + s]);
+            for (int k2 = 0; k2 < 2; k2++)  // K 16 per MMA: 8 TMEM columns of P, 16 key rows of V (2048 bytes)
+              tc_mma_f16_ts(tmem + kColO, tmem + b * TK + (c * 2 + k2) * 8, vd + (uint64_t)(k2 * (2048 >> 4)), idPV,
+                            (jj | c | k2) != 0);
+            tc_commit(&bar[B_EMPTY + s]);
+          }
+          if (!ok) break;
+          tc_commit(&bar[BPV_DONE + b]);
         }
       }
       if (ok) tc_commit(&bar[BO_FULL]);
@@ -198,29 +236,32 @@ __global__ void __launch_bounds__(192, 1)
     float m_used = -INFINITY, lsum = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkb && ok; j++) {
-      const int s = j & 1;
-      if (!(ok = wait_bar_warp(&bar[BS_FULL + s], (j >> 1) & 1, abort, a.err, kErrTimeoutFull))) break;
+      const int b = j & 1;
+      const uint32_t sb = tmem + lanes + b * TK;
+      if (!(ok = wait_bar_warp(&bar[BS_FULL + b], (j >> 1) & 1, abort, a.err, kErrTimeoutFull))) break;
       tc_fence_after();
       uint32_t sv[TK];
-      tmem_ld32(tmem + lanes + kColS + s * TK, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld32(tmem + lanes + kColS + s * TK + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-      tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[BS_EMPTY + s]);
-      // scores (1/sqrt(256) = 1/16, exact), causal mask, row max
-      float x[TK];
-      float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < TK; c++) {
-        const float v = __uint_as_float(sv[c]) * 0.0625f;
-        x[c] = j * TK + c <= pos ? v : -INFINITY;
-        mx = fmaxf(mx, x[c]);
+      for (int c = 0; c < TK; c += 32) tmem_ld32(sb + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
+      tc_wait_ld();
+      // causal mask (only where the block reaches past a row of this warp), row max of the raw
+      // scores; in the log2 domain y = s * kScaleL2 (1/16 = 1/sqrt(256) and log2(e))
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (j * TK + TK - 1 <= p + q0 + (warp & 3) * 32) {  // every key of the block is visible to the warp
+#pragma unroll
+        for (int c = 0; c < TK; c++) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sv[c]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < TK; c++) {
+          if (j * TK + c > pos) sv[c] = __float_as_uint(-INFINITY);
+          m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sv[c]));
+        }
       }
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * kScaleL2;
       const bool resc = mx > m_used + kLazy;  // first block: m_used = -inf
       float alpha = 1.0f;
       if (resc) {
-        alpha = j == 0 ? 0.0f : __expf(m_used - mx);
+        alpha = j == 0 ? 0.0f : ex2(m_used - mx);
         m_used = mx;
         lsum *= alpha;
       }
@@ -239,29 +280,29 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_wait_st();
       }
-      // probabilities against m_used, rounded to f16 for the PV product; the row sum in f32
-      uint32_t pk[TK / 2];
-      float ps = 0.0f;
+      // probabilities 2^(y - m_used), rounded to f16 for the PV product (packed in place over the
+      // scores already read); the row sum in f32
+      float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < TK; c += 2) {
-        const float p0 = __expf(x[c] - m_used), p1 = __expf(x[c + 1] - m_used);
-        ps += p0 + p1;
-        pk[c / 2] = pack_h2f(p0, p1);
+        const float p0 = ex2(fmaf(__uint_as_float(sv[c]), kScaleL2, -m_used));
+        const float p1 = ex2(fmaf(__uint_as_float(sv[c + 1]), kScaleL2, -m_used));
+        ps4[(c >> 1) & 3] += p0 + p1;
+        sv[c / 2] = pack_h2f(p0, p1);
       }
-      lsum += ps;
-      // P buffer s was read by PV_{j-2}
-      if (j >= 2 && !(ok = wait_bar_warp(&bar[BPV_DONE + s], ((j >> 1) - 1) & 1, abort, a.err, kErrTimeoutAccum))) break;
-      tc_fence_after();
-      tmem_st32(tmem + lanes + kColP + s * (TK / 2), pk);
+      lsum += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
+      // P over the first 64 columns of this S buffer (its scores are all in registers now)
+      tmem_st32(sb, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tmem_st32(sb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[BP_FULL + s]);
+      if (lane == 0) mbar_arrive(&bar[BP_FULL + b]);
     }
     if (ok && wait_bar_warp(&bar[BO_FULL], 0, abort, a.err, kErrTimeoutAccum)) {
       tc_fence_after();
       const float il = 1.0f / lsum;
-      const int t = tok0 + r;
+      const size_t t = (size_t)bz * a.l + tok0 + r;  // row of gate / out
 #pragma unroll 1
       for (int c0 = 0; c0 < HD; c0 += 32) {
         uint32_t o[32];
@@ -273,7 +314,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int c = 0; c < 32; c += 8) {
             float g[8];
             if (a.gate) {
-              const uint4 gr = *reinterpret_cast<const uint4*>(a.gate + (size_t)t * a.gstride + a.goff + h * a.gstep + c0 + c);
+              const uint4 gr = *reinterpret_cast<const uint4*>(a.gate + t * a.gstride + a.goff + h * a.gstep + c0 + c);
               const __half2* g2 = reinterpret_cast<const __half2*>(&gr);
 #pragma unroll
               for (int i = 0; i < 4; i++) {
@@ -291,7 +332,7 @@ __global__ void __launch_bounds__(192, 1)
               hv[(c + i) / 2] = pack_h2f(x0, x1);
             }
           }
-          uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)t * a.hq * HD + h * HD + c0);
+          uint4* dst = reinterpret_cast<uint4*>(a.out + t * a.hq * HD + h * HD + c0);
 #pragma unroll
           for (int k4 = 0; k4 < 4; k4++) dst[k4] = make_uint4(hv[4 * k4], hv[4 * k4 + 1], hv[4 * k4 + 2], hv[4 * k4 + 3]);
         }
@@ -310,12 +351,13 @@ cudaError_t preload_attention_tc() {
   return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
 }
 
-// Query blocks of 128 for the tensor-core kernel; q [hq][qrows][256], k / v [hk][krows][256] with
-// krows_valid rows readable per head (later rows read zeros).
+// Query blocks of 128 for the tensor-core kernel; q [batch][hq][qrows][256], k / v [batch][hk][krows][256]
+// with krows_valid rows readable per head (later rows read zeros); gate / out rows batch-major.
 cudaError_t launch_attention_tc(const __half* q, int qrows, const __half* k, const __half* v, int krows, int krows_valid,
                                 const AttnTcArgs& a, int nblk, cudaStream_t st) {
   if (nblk <= 0 || nblk > 65535 || a.hq <= 0 || a.hq > 65535 || a.hk <= 0 || a.hq % a.hk || qrows <= 0 || krows_valid <= 0 ||
-      krows_valid > krows || ((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16)
+      krows_valid > krows || ((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16 || a.batch < 1 || a.batch > 65535 ||
+      (a.blk && a.batch != 1))
     return cudaErrorInvalidValue;
   if (a.gate && (a.gstride % 8 || a.goff % 8 || a.gstep % 8 || (uintptr_t)a.gate % 16)) return cudaErrorInvalidValue;
   static bool attr[kMaxDevices] = {};  // the shared-memory size, once per device
@@ -328,11 +370,11 @@ cudaError_t launch_attention_tc(const __half* q, int qrows, const __half* k, con
     attr[dev] = true;
   }
   CUtensorMap qm, km, vm;
-  if (make_map_3d(&qm, q, HD, qrows, a.hq, HD, (long long)qrows * HD, TQ) != 0 ||
-      make_map_3d(&km, k, HD, krows_valid, a.hk, HD, (long long)krows * HD, TK) != 0 ||
-      make_map_3d(&vm, v, HD, krows_valid, a.hk, HD, (long long)krows * HD, TK) != 0)
+  if (make_map_3d(&qm, q, HD, qrows, a.batch * a.hq, HD, (long long)qrows * HD, TQ) != 0 ||
+      make_map_3d(&km, k, HD, krows_valid, a.batch * a.hk, HD, (long long)krows * HD, TK) != 0 ||
+      make_map_3d(&vm, v, HD, krows_valid, a.batch * a.hk, HD, (long long)krows * HD, 32) != 0)
     return cudaErrorInvalidValue;
-  attn_tc_kernel<<<dim3(nblk, a.hq), 192, kSmem, st>>>(qm, km, vm, a);
+  attn_tc_kernel<<<dim3(nblk, a.hq, a.batch), kThreads, kSmem, st>>>(qm, km, vm, a);
   return cudaGetLastError();
 }
 

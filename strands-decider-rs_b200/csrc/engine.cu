@@ -1583,6 +1583,33 @@ int sd_attention(const void* q, const void* k, const void* v, const void* gate, 
                    "sd_attention");
 }
 
+int sd_attention_batch(const void* q, const void* k, const void* v, const void* gate, int32_t gstride, int32_t goff,
+                       int32_t gstep, void* out, int32_t batch, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk,
+                       int32_t hd, void* stream) {
+  if (!q || !k || !v || !out || batch < 1 || l <= 0 || p < 0 || p + l > lt || hk <= 0 || hq % hk) {
+    set_global_error("sd_attention_batch: bad arguments");
+    return SD_ERR_INVALID;
+  }
+  if (l < 128 || hd != 256) {  // the mma.sync kernel, one sequence at a time
+    for (int b = 0; b < batch; b++) {
+      const size_t qo = (size_t)b * hq * l * hd, ko = (size_t)b * hk * lt * hd, go = (size_t)b * l * gstride,
+                   oo = (size_t)b * l * hq * hd;
+      const int rc = op_result(sd::launch_attention((const __half*)q + qo, (const __half*)k + ko, (const __half*)v + ko,
+                                                    gate ? (const __half*)gate + go : nullptr, gstride, goff, gstep,
+                                                    (__half*)out + oo, l, p, lt, hq, hk, hd, 1, nullptr, 0, (cudaStream_t)stream),
+                               "sd_attention_batch");
+      if (rc != SD_OK) return rc;
+    }
+    return SD_OK;
+  }
+  sd::AttnTcArgs ta;
+  ta.l = l, ta.p = p, ta.hq = hq, ta.hk = hk, ta.batch = batch, ta.gate = (const __half*)gate, ta.gstride = gstride,
+  ta.goff = goff, ta.gstep = gstep, ta.out = (__half*)out;
+  return op_result(sd::launch_attention_tc((const __half*)q, l, (const __half*)k, (const __half*)v, lt, p + l, ta,
+                                           (l + 127) / 128, (cudaStream_t)stream),
+                   "sd_attention_batch");
+}
+
 int sd_attention_split(const void* q, const void* k, const void* v, const void* gate, int32_t gstride, int32_t goff,
                        int32_t gstep, void* out, int32_t l, int32_t p, int32_t lt, int32_t hq, int32_t hk, int32_t hd,
                        int32_t splits, void* ws, size_t ws_bytes, void* stream) {

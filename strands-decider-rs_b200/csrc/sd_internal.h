@@ -140,6 +140,7 @@ struct AttnTcArgs {
   const int* seq_off = nullptr;
   const int* seq_len = nullptr;
   int l = 0, p = 0, hq = 0, hk = 0;
+  int batch = 1;  // single-sequence mode: independent sequences (blockIdx.z), q/k/v/gate/out batch-major
   const __half* gate = nullptr;
   int gstride = 0, goff = 0, gstep = 0;
   __half* out = nullptr;

@@ -70,6 +70,7 @@ def lib() -> C.CDLL:
         L.sd_head_free.argtypes = [vp]
         L.sd_head_probs.argtypes = [vp, vp, i32, i32, C.c_double, vp]
         L.sd_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]
+        L.sd_attention_batch.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp]
         L.sd_attention_split.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp,
                                          C.c_size_t, vp]
         L.sd_gdn.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32, i32, i32, C.c_int64, C.c_int64, i32, i32, vp,
@@ -342,6 +343,12 @@ class Head:
 # ---------------------------------------------------------------------------------------------
 # Kernel-level entry points on device memory (pointers as ints, e.g. torch.Tensor.data_ptr())
 # ---------------------------------------------------------------------------------------------
+
+def attention_batch(q, k, v, gate, gstride, goff, gstep, out, batch, l, p, lt, hq, hk, hd, stream=None):
+    """`sd_attention_batch`: `batch` sequences in one launch (q [batch][hq][l][hd], k/v [batch][hk][lt][hd])."""
+    _check(lib().sd_attention_batch(q, k, v, gate, gstride, goff, gstep, out, batch, l, p, lt, hq, hk, hd, stream),
+           "sd_attention_batch")
+
 
 def attention(q, k, v, gate, gstride, goff, gstep, out, l, p, lt, hq, hk, hd, stream=None, splits=None, ws=None,
               ws_bytes=0):

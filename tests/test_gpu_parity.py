@@ -126,6 +126,28 @@ def test_attention_tc_matches_oracle(torch, l, p, hq, hk, gated):
     assert np.abs(tc - legacy).max() < 4e-3
 
 
+@pytest.mark.parametrize("l,p", [(256, 0), (300, 44), (60, 10)])
+def test_attention_batch_matches_one_by_one(torch, l, p):
+    """sd_attention_batch (one launch over the batch) equals sd_attention on each sequence."""
+    from strands_decider.engine import attention, attention_batch
+    rng = np.random.default_rng(l + 7 * p)
+    B, hq, hk, hd, lt = 3, 8, 2, 256, 512
+    q = rng.standard_normal((B, hq, l, hd)).astype(np.float16)
+    kc = rng.standard_normal((B, hk, lt, hd)).astype(np.float16)
+    vc = rng.standard_normal((B, hk, lt, hd)).astype(np.float16)
+    gate = rng.standard_normal((B, l, 3 * hq * hd)).astype(np.float16)
+    qd, kd, vd, gd = (dev(torch, x.view(np.uint16)) for x in (q, kc, vc, gate))
+    out = torch.zeros((B, l, hq * hd), dtype=torch.float16, device="cuda")
+    attention_batch(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), gd.data_ptr(), 3 * hq * hd, hd, 2 * hd, out.data_ptr(), B, l, p,
+                    lt, hq, hk, hd)
+    one = torch.zeros((l, hq * hd), dtype=torch.float16, device="cuda")
+    for b in range(B):
+        attention(qd[b].data_ptr(), kd[b].data_ptr(), vd[b].data_ptr(), gd[b].data_ptr(), 3 * hq * hd, hd, 2 * hd, one.data_ptr(),
+                  l, p, lt, hq, hk, hd)
+        torch.cuda.synchronize()
+        assert torch.equal(out[b], one)
+
+
 def _gdn_inputs(rng, b, l, h):
     q = rng.standard_normal((b, l, h, 128)).astype(np.float32)
     k = rng.standard_normal((b, l, h, 128)).astype(np.float32)
