@@ -299,23 +299,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[BP_FULL + b]);
     }
-    if (ok && wait_bar_warp(&bar[BO_FULL], 0, abort, a.err, kErrTimeoutAccum)) {
+    // this row's gate, all of it at once (one memory latency, overlapping the last PV product; the
+    // registers of the scores are free now)
+    const size_t t = (size_t)bz * a.l + tok0 + r;  // row of gate / out
+    uint4 grow[HD / 8];
+    if (a.gate && r < nq) {
+      const uint4* gsrc = reinterpret_cast<const uint4*>(a.gate + t * a.gstride + a.goff + h * a.gstep);
+#pragma unroll
+      for (int i = 0; i < HD / 8; i++) grow[i] = gsrc[i];
+    }
+    // out = O / row sum x sigmoid(gate), f16, each thread its own row (staging the tile in shared
+    // memory for row-contiguous stores measured 8% slower)
+    const bool done = ok && wait_bar_warp(&bar[BO_FULL], 0, abort, a.err, kErrTimeoutAccum);
+    if (done) {
       tc_fence_after();
       const float il = 1.0f / lsum;
-      const size_t t = (size_t)bz * a.l + tok0 + r;  // row of gate / out
-#pragma unroll 1
+#pragma unroll
       for (int c0 = 0; c0 < HD; c0 += 32) {
         uint32_t o[32];
         tmem_ld32(tmem + lanes + kColO + c0, o);
         tc_wait_ld();
-        if (r < nq) {
+        {
           uint32_t hv[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
             float g[8];
             if (a.gate) {
-              const uint4 gr = *reinterpret_cast<const uint4*>(a.gate + t * a.gstride + a.goff + h * a.gstep + c0 + c);
-              const __half2* g2 = reinterpret_cast<const __half2*>(&gr);
+              const __half2* g2 = reinterpret_cast<const __half2*>(&grow[(c0 + c) / 8]);
 #pragma unroll
               for (int i = 0; i < 4; i++) {
                 const float2 f = __half22float2(g2[i]);
@@ -325,16 +335,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 8; i += 2) {
               float x0 = __uint_as_float(o[c + i]) * il, x1 = __uint_as_float(o[c + i + 1]) * il;
-              if (a.gate) {
-                x0 = x0 / (1.0f + __expf(-g[i]));
-                x1 = x1 / (1.0f + __expf(-g[i + 1]));
+              if (a.gate) {  // x sigmoid(gate) (fast division: within 2 ulp, far below the f16 rounding that follows)
+                x0 = __fdividef(x0, 1.0f + __expf(-g[i]));
+                x1 = __fdividef(x1, 1.0f + __expf(-g[i + 1]));
               }
               hv[(c + i) / 2] = pack_h2f(x0, x1);
             }
           }
-          uint4* dst = reinterpret_cast<uint4*>(a.out + t * a.hq * HD + h * HD + c0);
+          if (r < nq) {
+            uint4* dst = reinterpret_cast<uint4*>(a.out + t * a.hq * HD + h * HD + c0);
 #pragma unroll
-          for (int k4 = 0; k4 < 4; k4++) dst[k4] = make_uint4(hv[4 * k4], hv[4 * k4 + 1], hv[4 * k4 + 2], hv[4 * k4 + 3]);
+            for (int k4 = 0; k4 < 4; k4++) dst[k4] = make_uint4(hv[4 * k4], hv[4 * k4 + 1], hv[4 * k4 + 2], hv[4 * k4 + 3]);
+          }
         }
       }
     }
