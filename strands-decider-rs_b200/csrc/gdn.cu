@@ -73,6 +73,74 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ uint32_t tf32(float x) {  // round to tf32 (nearest, ties away), as the operand
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void mma1688_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                             uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The off-diagonal 16 x 16 blocks of X = (I + A)^-1 (64 x 64, rows LA floats apart, its diagonal blocks
+// already solved), level by level: X_ij = -X_ii sum_{m=j}^{i-1} A_im X_mj for i = j + dl; warp w < 4 - dl
+// takes block (w + dl, w). The products run on the tensor cores with tf32 operands and f32
+// accumulation (tf32 keeps f16's 10-bit mantissa with f32's range: T is rounded to f16 for the W and U
+// products right after). `y`: 3 x 16 x 17 floats of scratch. Every thread of the CTA calls it (it
+// synchronises the CTA between levels).
+__device__ void inverse_offdiag(const float* __restrict__ a, float* __restrict__ x, float* __restrict__ y, int warp, int lane) {
+  const int g = lane >> 2, tq = lane & 3;
+#pragma unroll 1
+  for (int dl = 1; dl < 4; dl++) {
+    if (warp < 4 - dl) {
+      const int bj = warp, bi = bj + dl;
+      float acc[2][4] = {};
+      for (int m = bj; m < bi; m++)
+#pragma unroll
+        for (int kk = 0; kk < 16; kk += 8) {
+          const float* ar = a + (bi * 16 + g) * LA + m * 16 + kk;
+          const uint32_t a0 = tf32(ar[tq]), a1 = tf32(ar[8 * LA + tq]), a2 = tf32(ar[tq + 4]), a3 = tf32(ar[8 * LA + tq + 4]);
+#pragma unroll
+          for (int nt = 0; nt < 2; nt++) {
+            const float* xr = x + (m * 16 + kk + tq) * LA + bj * 16 + nt * 8 + g;
+            mma1688_tf32(acc[nt], a0, a1, a2, a3, tf32(xr[0]), tf32(xr[4 * LA]));
+          }
+        }
+      float* yw = y + warp * 272;  // this block's sum, 16 x 16 (row stride 17)
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++) {
+        yw[g * 17 + nt * 8 + 2 * tq] = acc[nt][0];
+        yw[g * 17 + nt * 8 + 2 * tq + 1] = acc[nt][1];
+        yw[(g + 8) * 17 + nt * 8 + 2 * tq] = acc[nt][2];
+        yw[(g + 8) * 17 + nt * 8 + 2 * tq + 1] = acc[nt][3];
+      }
+      __syncwarp();
+      float z[2][4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 16; kk += 8) {
+        const float* xr = x + (bi * 16 + g) * LA + bi * 16 + kk;
+        const uint32_t a0 = tf32(xr[tq]), a1 = tf32(xr[8 * LA + tq]), a2 = tf32(xr[tq + 4]), a3 = tf32(xr[8 * LA + tq + 4]);
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+          mma1688_tf32(z[nt], a0, a1, a2, a3, tf32(yw[(kk + tq) * 17 + nt * 8 + g]), tf32(yw[(kk + tq + 4) * 17 + nt * 8 + g]));
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++) {
+        float* xo = x + (bi * 16 + g) * LA + bj * 16 + nt * 8 + 2 * tq;
+        xo[0] = -z[nt][0];
+        xo[1] = -z[nt][1];
+        xo[8 * LA] = -z[nt][2];
+        xo[8 * LA + 1] = -z[nt][3];
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // Fragment addresses (lane-dependent) for the m16n8k16 operands from padded row-major tiles.
 // A from [m][k]; B from [n][k] (non-transposed) or [k][n] (transposed); A from [k][m] (transposed).
 __device__ __forceinline__ uint32_t a_addr(const __half* base, int ld, int m0, int k0, int lane) {
@@ -323,29 +391,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(const GdnArgs<TIn> a)
       for (int r = 0; r < 16; r++) sm.x[(o + r) * LA + o + c] = xc[r];
     }
     __syncthreads();
-#pragma unroll 1
-    for (int dl = 1; dl < 4; dl++) {
-      const int npair = 4 - dl;
-      for (int e = threadIdx.x; e < npair * 256; e += 256) {
-        const int pr = e >> 8, r = (e >> 4) & 15, c = e & 15;
-        const int bi = dl + pr, bj = pr;
-        float s = 0.0f;
-        for (int m = bj; m < bi; m++)
-#pragma unroll
-          for (int q = 0; q < 16; q++) s += sm.a[(bi * 16 + r) * LA + m * 16 + q] * sm.x[(m * 16 + q) * LA + bj * 16 + c];
-        sm.y[pr * 272 + r * 17 + c] = s;
-      }
-      __syncthreads();
-      for (int e = threadIdx.x; e < npair * 256; e += 256) {
-        const int pr = e >> 8, r = (e >> 4) & 15, c = e & 15;
-        const int bi = dl + pr, bj = pr;
-        float s = 0.0f;
-#pragma unroll
-        for (int q = 0; q < 16; q++) s += sm.x[(bi * 16 + r) * LA + bi * 16 + q] * sm.y[pr * 272 + q * 17 + c];
-        sm.x[(bi * 16 + r) * LA + bj * 16 + c] = -s;
-      }
-      __syncthreads();
-    }
+    inverse_offdiag(sm.a, sm.x, sm.y, warp, lane);
     // T1 = T diag(beta Gamma), T2 = T diag(beta) (lower triangular, f16)
     for (int e = threadIdx.x; e < CH * CH; e += 256) {
       const int i = e >> 6, j = e & 63;
@@ -601,7 +647,10 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const __half* __restri
     for (int j = 0; j < 4; j++) q2[j] = __hmul2(q2[j], gi);
     *reinterpret_cast<uint4*>(&R.qg[r * DK + c8]) = qv;
   }
-  if (threadIdx.x < CH) R.dsc[threadIdx.x] = __expf(sm.G[CH - 1] - sm.G[threadIdx.x]);
+  if (threadIdx.x < CH) {
+    R.dsc[threadIdx.x] = __expf(sm.G[CH - 1] - sm.G[threadIdx.x]);
+    sm.g[threadIdx.x] = sm.beta[threadIdx.x] * __expf(sm.G[threadIdx.x]);  // beta_j Gamma_j, for T1 (read after a barrier)
+  }
   if (threadIdx.x == 0) R.gc = __expf(sm.G[CH - 1]);
 
   // 2. A and P
@@ -630,11 +679,12 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const __half* __restri
 #pragma unroll
     for (int nt = 0; nt < 4; nt++)
 #pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const int i = mt * 16 + g8 + (r >> 1) * 8, j = nb + nt * 8 + 2 * tq + (r & 1);
-        const float e = j <= i ? __expf(sm.G[i] - sm.G[j]) : 0.0f;
-        sm.a[i * LA + j] = j < i ? sm.beta[i] * e * kk[nt][r] : 0.0f;
-        R.p[i * CH + j] = __float2half_rn(e * qk[nt][r]);
+      for (int hf = 0; hf < 2; hf++) {  // elements (i, j) and (i, j + 1)
+        const int i = mt * 16 + g8 + hf * 8, j = nb + nt * 8 + 2 * tq;
+        const float e0 = j <= i ? __expf(sm.G[i] - sm.G[j]) : 0.0f, e1 = j + 1 <= i ? __expf(sm.G[i] - sm.G[j + 1]) : 0.0f;
+        sm.a[i * LA + j] = j < i ? sm.beta[i] * e0 * kk[nt][2 * hf] : 0.0f;
+        sm.a[i * LA + j + 1] = j + 1 < i ? sm.beta[i] * e1 * kk[nt][2 * hf + 1] : 0.0f;
+        *reinterpret_cast<__half2*>(&R.p[i * CH + j]) = __floats2half2_rn(e0 * qk[nt][2 * hf], e1 * qk[nt][2 * hf + 1]);
       }
   }
   __syncthreads();
@@ -657,41 +707,12 @@ __global__ void __launch_bounds__(256, 2) gdn_prep_kernel(const __half* __restri
     for (int r = 0; r < 16; r++) sm.x[(o + r) * LA + o + cc] = xc[r];
   }
   __syncthreads();
-#pragma unroll 1
-  for (int dl = 1; dl < 4; dl++) {
-    const int npair = 4 - dl;
-    for (int e = threadIdx.x; e < npair * 256; e += 256) {
-      const int pr = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      const int bi = dl + pr, bj = pr;
-      float s0 = 0.0f, s1 = 0.0f;
-      for (int m = bj; m < bi; m++)
-#pragma unroll
-        for (int qq = 0; qq < 16; qq += 2) {
-          s0 += sm.a[(bi * 16 + r) * LA + m * 16 + qq] * sm.x[(m * 16 + qq) * LA + bj * 16 + cc];
-          s1 += sm.a[(bi * 16 + r) * LA + m * 16 + qq + 1] * sm.x[(m * 16 + qq + 1) * LA + bj * 16 + cc];
-        }
-      sm.y[pr * 272 + r * 17 + cc] = s0 + s1;
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < npair * 256; e += 256) {
-      const int pr = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      const int bi = dl + pr, bj = pr;
-      float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-      for (int qq = 0; qq < 16; qq += 2) {
-        s0 += sm.x[(bi * 16 + r) * LA + bi * 16 + qq] * sm.y[pr * 272 + qq * 17 + cc];
-        s1 += sm.x[(bi * 16 + r) * LA + bi * 16 + qq + 1] * sm.y[pr * 272 + (qq + 1) * 17 + cc];
-      }
-      sm.x[(bi * 16 + r) * LA + bj * 16 + cc] = -(s0 + s1);
-    }
-    __syncthreads();
-  }
+  inverse_offdiag(sm.a, sm.x, sm.y, warp, lane);
   for (int e = threadIdx.x; e < CH * CH; e += 256) {
     const int i = e >> 6, j = e & 63;
     const float t = j <= i ? sm.x[i * LA + j] : 0.0f;
-    const float bj = sm.beta[j];
-    sm.t1[i * L64 + j] = __float2half_rn(t * bj * __expf(sm.G[j]));
-    sm.t2[i * L64 + j] = __float2half_rn(t * bj);
+    sm.t1[i * L64 + j] = __float2half_rn(t * sm.g[j]);  // beta_j Gamma_j
+    sm.t2[i * L64 + j] = __float2half_rn(t * sm.beta[j]);
   }
   __syncthreads();
   // 4. W = T1 K^ (f16) and U = T2 V (f32), 64 x 128 each
