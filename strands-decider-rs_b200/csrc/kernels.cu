@@ -395,6 +395,73 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const __half* __restrict__
   else ko[((size_t)(s - hq) * lt + krow) * HD + d] = __float2half_rn(r);
 }
 
+// qk_prep_kernel with one warp per (token, head) row: lane i holds elements 8i .. 8i + 7 (16-byte loads
+// and stores), the row's mean square is a warp reduction, and a RoPE partner (d -/+ rd/2) lives rd/16
+// lanes away (a shuffle). Needs rd / 2 a multiple of 8. Rows: token-major, (hq + hk) per token.
+__global__ void __launch_bounds__(256) qk_prep_warp_kernel(const __half* __restrict__ big, int stride,
+                                                           const float* __restrict__ qw, const float* __restrict__ kw,
+                                                           const float2* __restrict__ rope, int l, int p, int lt, int hq,
+                                                           int hk, int rd, const int* __restrict__ tpos,
+                                                           __half* __restrict__ qo, __half* __restrict__ ko,
+                                                           __half* __restrict__ vo) {
+  constexpr int HD = 256;
+  const int lane = threadIdx.x & 31;
+  const long long rowid = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int heads = hq + hk;
+  if (rowid >= (long long)l * heads) return;
+  const int t = (int)(rowid / heads), s = (int)(rowid % heads);
+  const bool isq = s < hq;
+  const int pos = tpos ? tpos[t] : p + t;  // RoPE position
+  const int krow = tpos ? t : pos;         // K/V row
+  const __half* row = big + (size_t)t * stride;
+  const int koff = hq * HD * 2, voff = koff + hk * HD;
+  const int d0 = lane * 8;
+  if (!isq) {
+    const int kh = s - hq;
+    *reinterpret_cast<uint4*>(vo + ((size_t)kh * lt + krow) * HD + d0) =
+        *reinterpret_cast<const uint4*>(row + voff + kh * HD + d0);
+  }
+  const uint4 raw = *reinterpret_cast<const uint4*>(row + (isq ? s * 2 * HD : koff + (s - hq) * HD) + d0);
+  const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const float2 f = __half22float2(h2[i]);
+    v[2 * i] = f.x, v[2 * i + 1] = f.y;
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) ss += v[i] * v[i];
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)HD + 1e-6f);
+  const float* w = isq ? qw : kw;
+  float n[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) n[i] = v[i] * inv * w[d0 + i];
+  // RoPE on the first rd elements: partner d + rd/2 (first half) or d - rd/2 (second half)
+  const int rd2 = rd / 2, lofs = rd2 / 8;
+  const int src = d0 < rd2 ? lane + lofs : (d0 < rd ? lane - lofs : lane);
+  float r[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float partner = __shfl_sync(0xffffffffu, n[i], src);
+    r[i] = n[i];
+    if (d0 < rd) {
+      const float2 cs = rope[(size_t)pos * rd2 + ((d0 + i) % rd2)];
+      r[i] = d0 < rd2 ? n[i] * cs.x - partner * cs.y : n[i] * cs.x + partner * cs.y;
+    }
+  }
+  uint4 out;
+  uint32_t* o32 = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const __half2 hv = __floats2half2_rn(r[2 * i], r[2 * i + 1]);
+    o32[i] = *reinterpret_cast<const uint32_t*>(&hv);
+  }
+  if (isq) *reinterpret_cast<uint4*>(qo + ((size_t)s * l + t) * HD + d0) = out;
+  else *reinterpret_cast<uint4*>(ko + ((size_t)(s - hq) * lt + krow) * HD + d0) = out;
+}
+
 __global__ void trace_kernel(const float* __restrict__ x, const __half* __restrict__ y, int n, float* __restrict__ out) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = x[i] + __half2float(y[i]);
 }
@@ -482,6 +549,12 @@ cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff
 cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,
                            int lt, const Dims& dm, const int* tpos, __half* q, __half* kc, __half* vc, cudaStream_t st) {
   if (dm.hd != 256) return cudaErrorInvalidValue;
+  if ((dm.rd / 2) % 8 == 0 && dm.rd <= 256 && stride % 8 == 0) {  // a warp per row
+    const long long rows = (long long)l * (dm.hq + dm.hk);
+    qk_prep_warp_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(big, stride, qw, kw, reinterpret_cast<const float2*>(rope), l,
+                                                                     p, lt, dm.hq, dm.hk, dm.rd, tpos, q, kc, vc);
+    return cudaGetLastError();
+  }
   dim3 grid(l, dm.hq + dm.hk);
   qk_prep_kernel<<<grid, 256, 0, st>>>(big, stride, qw, kw, reinterpret_cast<const float2*>(rope), l, p, lt, dm.hq, dm.hk,
                                        dm.rd, tpos, q, kc, vc);
@@ -495,7 +568,7 @@ cudaError_t preload_kernels() {
                        (const void*)conv_kernel,       (const void*)hist_update_kernel, (const void*)gdn_gates_kernel,
                        (const void*)gdn_recurrent_kernel, (const void*)gnorm_kernel,  (const void*)qk_prep_kernel,
                        (const void*)trace_kernel,      (const void*)add_bias_kernel,    (const void*)hist_pack_kernel,
-                       (const void*)kv_pack_kernel};
+                       (const void*)kv_pack_kernel,    (const void*)qk_prep_warp_kernel};
   for (const void* f : fns) {
     cudaError_t e = cudaFuncGetAttributes(&a, f);
     if (e != cudaSuccess) return e;
