@@ -185,9 +185,30 @@ def model_path(world, rank):
     return path
 
 
-def step_requests(step: int, rank: int, world: int, per: int):
-    base = (step * world + rank) * per
-    return [(base + j) % N_REQUESTS for j in range(per)]
+def request_tokens(i: int, seed: int = 0) -> int:
+    """Tokens of request i of the sweep (its state and its questions), from the lengths alone."""
+    rng = np.random.default_rng([seed, i])
+    qlens = rng.integers(QLEN[0], QLEN[1] + 1, 3)
+    s = min(int(rng.integers(64, 4097)), CONTEXT - int(qlens.max()))
+    return s + int(qlens.sum())
+
+
+def step_requests(step: int, rank: int, world: int, per: int, seed: int = 0):
+    """This rank's requests of step `step`: the step takes the next world x per requests of the sweep
+    and shares them out as a server balances concurrent requests over its GPUs, longest first to the
+    rank with the fewest tokens so far (each rank gets `per`), so that no rank waits on another
+    holding all the long states."""
+    base = step * world * per
+    ids = [(base + j) % N_REQUESTS for j in range(world * per)]
+    if world == 1:
+        return ids
+    load = [0] * world
+    mine = [[] for _ in range(world)]
+    for i in sorted(ids, key=lambda i: -request_tokens(i, seed)):
+        r = min((r for r in range(world) if len(mine[r]) < per), key=lambda r: load[r])
+        mine[r].append(i)
+        load[r] += request_tokens(i, seed)
+    return sorted(mine[rank])
 
 
 def cpu_baseline(path: str, seed: int = 0, state_len: int = 96):
@@ -254,7 +275,7 @@ def run_ours(args, world, rank, local):
     reqs = {}
     staged = {}
     for s in range(steps_all + 1):
-        for i in step_requests(s, rank, world, per):
+        for i in step_requests(s, rank, world, per, args.seed):
             if i in reqs:
                 continue
             sids, qs, _ = request(i, args.seed)
@@ -266,7 +287,7 @@ def run_ours(args, world, rank, local):
     # the states and the questions of a step's requests back to back in HBM, for the passes across requests
     step_s, step_q = {}, {}
     for s in range(steps_all + 1):
-        ii = step_requests(s, rank, world, per)
+        ii = step_requests(s, rank, world, per, args.seed)
         step_s[s] = torch.cat([staged[i][0] for i in ii])
         step_q[s] = torch.cat([staged[i][1] for i in ii])
     hidden_dev = torch.empty((per * 12, 2048), dtype=torch.float32, device="cuda")
@@ -279,7 +300,7 @@ def run_ours(args, world, rank, local):
     # requests run as one packed pass (sd_forward_batch, a snapshot each), then their questions as
     # one batched fork (each continuing its own request's snapshot)
     def one_step_dev(s):
-        ii = step_requests(s, rank, world, per)
+        ii = step_requests(s, rank, world, per, args.seed)
         slens = [staged[i][0].numel() for i in ii]
         snaps = eng.forward_batch_dev(None, step_s[s].data_ptr(), slens, [[]] * len(ii), None, keep=True)
         caches, lens, rows = [], [], []
@@ -299,7 +320,7 @@ def run_ours(args, world, rank, local):
 
     def one_step_host(s):
         nonlocal h2d, d2h
-        ii = step_requests(s, rank, world, per)
+        ii = step_requests(s, rank, world, per, args.seed)
         states = [reqs[i][0] for i in ii]
         _, snaps = eng.forward_batch(None, states, [[]] * len(ii), keep=True)
         h2d += sum(x.nbytes for x in states)
