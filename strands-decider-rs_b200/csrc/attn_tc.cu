@@ -99,8 +99,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     q0 = a.blk[2 * blockIdx.x + 1];
     nq = min(TQ, a.seq_len[sq] - q0);
     tok0 = a.seq_off[sq] + q0;
-    kbase = a.seq_off[sq];
-    p = 0;
+    kbase = a.kbase_tab ? a.kbase_tab[sq] : a.seq_off[sq];
+    p = a.plen ? a.plen[sq] : 0;
   } else {
     q0 = (gridDim.x - 1 - blockIdx.x) * TQ;  // longest (latest) query blocks first
     nq = min(TQ, a.l - q0);

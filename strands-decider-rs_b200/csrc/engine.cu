@@ -152,6 +152,10 @@ struct sd_engine {
   size_t fk_meta_ints = 0;
   __half* fk_kv = nullptr;
   size_t fk_kv_halves = 0;
+  // continuations' keys and values gathered per sequence (prefix then own rows) for the tcgen05
+  // attention: [2][hk][ktot][hd], grown as needed
+  __half* fk_gather = nullptr;
+  size_t fk_gather_halves = 0;
   // pinned staging of fk_meta: a ring of slots, each reused once the copy out of it (event) is done
   static constexpr int kForkSlots = 4;
   int* fk_pin[kForkSlots] = {};
@@ -611,6 +615,8 @@ struct Fork {
   const int *tpos, *tstart, *tseq, *seq_off, *seq_len, *plen, *blk;
   const int *chunk_tab = nullptr, *chunk0 = nullptr, *order = nullptr;
   const int* blk128 = nullptr;  // (sequence, first query) per 128-query block, most keys first (the tcgen05 kernel)
+  const int* gofs = nullptr;    // first row of each sequence in the gathered keys (prefix + own rows)
+  int ktot = 0;                 // rows per head of the gathered keys
   int nseq, nblk, max_len, max_p, max_rows, chunks = 0, nblk128 = 0;
   bool two_phase = false;
   double pairs;       // causal (query, key) pairs of every sequence: len p + len (len + 1) / 2
@@ -705,6 +711,21 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
             ta.gate = e->big, ta.gstride = N, ta.goff = d.hd, ta.gstep = 2 * d.hd, ta.out = e->o, ta.err = e->d_err;
             LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * fk->pairs,
                sd::launch_attention_tc(e->q, l, fk->kt, fk->vt, l, l, ta, fk->nblk128, st));
+          } else if (fk->max_p > 0 && d.hd == 256 && fk->ktot > 0) {
+            // continuations (questions over snapshots): each sequence's prefix and own keys gathered into
+            // one tensor, then the tcgen05 kernel with per-sequence key rows and prefix lengths
+            __half* gk = e->fk_gather;
+            __half* gv = gk + (size_t)d.hk * fk->ktot * d.hd;
+            LK(SD_PROF_OTHER, 8.0 * d.hk * d.hd * (double)fk->ktot,
+               sd::launch_kv_gather(fk->kt, fk->vt, l, d.hk, d.hd, fk->seq_off, fk->seq_len, fk->plen,
+                                    fk->kp + (size_t)Lw.slot * fk->nseq, fk->vp + (size_t)Lw.slot * fk->nseq, fk->gofs,
+                                    fk->ktot, gk, gv, fk->nseq, fk->max_rows, st));
+            sd::AttnTcArgs ta;
+            ta.blk = fk->blk128, ta.seq_off = fk->seq_off, ta.seq_len = fk->seq_len, ta.hq = d.hq, ta.hk = d.hk;
+            ta.kbase_tab = fk->gofs, ta.plen = fk->plen;
+            ta.gate = e->big, ta.gstride = N, ta.goff = d.hd, ta.gstep = 2 * d.hd, ta.out = e->o, ta.err = e->d_err;
+            LK(SD_PROF_ATTN, 4.0 * d.hd * d.hq * fk->pairs,
+               sd::launch_attention_tc(e->q, l, gk, gv, fk->ktot, fk->ktot, ta, fk->nblk128, st));
           } else {
             int splits = sd::attention_splits_packed(fk->nblk, fk->max_p, fk->max_len, d.hq, e->num_sms);
             while (splits > 1 && sd::attention_split_bytes(l, d.hq, splits) > e->ws_bytes) splits--;
@@ -838,7 +859,7 @@ int check_forward_args(sd_engine* e, int l, int nrows, const sd_snapshot* cache,
 size_t packed_ints(const sd_engine* e, long long T, long long nq, long long nblk, long long R, bool keep, long long chunks,
                    bool host_ids) {
   const size_t per_set = (size_t)(2 * e->n_lin + 2 * e->n_full) * nq;
-  return 2 * per_set * (keep ? 2 : 1) + 3 * (size_t)T + 3 * (size_t)nq + 2 * (size_t)nblk + (size_t)R +
+  return 2 * per_set * (keep ? 2 : 1) + 3 * (size_t)T + 4 * (size_t)nq + 2 * (size_t)nblk + (size_t)R +
          (chunks >= 0 ? 2 * (size_t)chunks + 2 * (size_t)nq : 0) + (host_ids ? (size_t)T : 0);
 }
 
@@ -873,6 +894,20 @@ int ensure_packed(sd_engine* e, long long T, size_t ints, long long chunks) {
     CK(cudaMalloc(&e->fk_kv, cap * sizeof(__half)));
     e->fk_kv_halves = cap;
   }
+  return SD_OK;
+}
+
+// Grows the gathered keys of continuations (sd_forward_fork and friends) to `ktot` rows per head, by at
+// least a quarter at a time, after the queued work that may use the old buffer.
+int ensure_gather(sd_engine* e, long long ktot) {
+  const size_t need = 2 * (size_t)e->dm.hk * ktot * e->dm.hd;
+  if (ktot <= 0 || e->fk_gather_halves >= need) return SD_OK;
+  CK(cudaStreamSynchronize(e->stream));
+  cudaFree(e->fk_gather);
+  const size_t cap = std::max(need, e->fk_gather_halves * 5 / 4);
+  e->fk_gather = nullptr, e->fk_gather_halves = 0;
+  CK(cudaMalloc(&e->fk_gather, cap * sizeof(__half)));
+  e->fk_gather_halves = cap;
   return SD_OK;
 }
 
@@ -927,6 +962,11 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
     max_chunks = std::max(max_chunks, ((int)lens[b] + 63) / 64);
   }
   if (T > (1 << 16)) return e->fail(SD_ERR_INVALID, "%s: %lld tokens in one call (at most 65536)", fn, T);
+  long long ktot_ll = 0;  // rows of the gathered keys (continuations: every prefix with its own rows)
+  if (max_p > 0)
+    for (int b = 0; b < nq; b++) ktot_ll += (caches && caches[b] ? caches[b]->len : 0) + lens[b];
+  if (ktot_ll > (1 << 24)) return e->fail(SD_ERR_INVALID, "%s: %lld key rows in one call", fn, ktot_ll);
+  const int ktot = (int)ktot_ll;
   if (R > 0 && (!rows || !has_out)) return e->fail(SD_ERR_INVALID, "rows given without an output buffer");
   if (ids_host)
     for (long long i = 0; i < T; i++)
@@ -940,7 +980,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   // chunk_tab[2 chunks], chunk0[nq], order[nq]; then ids[T] (host ids)
   const size_t per_set = (size_t)(2 * e->n_lin + 2 * e->n_full) * nq;
   const size_t i0 = 2 * per_set * (keep ? 2 : 1);  // ints before the index arrays
-  const size_t n_idx = i0 + 3 * (size_t)T + 3 * (size_t)nq + 2 * (size_t)nblk + 2 * (size_t)nblk128;
+  const size_t n_idx = i0 + 3 * (size_t)T + 4 * (size_t)nq + 2 * (size_t)nblk + 2 * (size_t)nblk128;
   const size_t n_gdn = two_phase ? 2 * (size_t)chunks + 2 * (size_t)nq : 0;
   const size_t n_all = packed_ints(e, T, nq, nblk + nblk128, R, keep, two_phase ? chunks : -1, ids_host != nullptr);
   {  // rows in range
@@ -952,7 +992,9 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   }
   cudaSetDevice(e->device);
   int rc;
-  if ((rc = ensure_pool(e, (int)T)) != SD_OK || (rc = ensure_packed(e, T, n_all, two_phase ? chunks : 0)) != SD_OK) return rc;
+  if ((rc = ensure_pool(e, (int)T)) != SD_OK || (rc = ensure_packed(e, T, n_all, two_phase ? chunks : 0)) != SD_OK ||
+      (rc = ensure_gather(e, ktot)) != SD_OK)
+    return rc;
   const sd::Dims& d = e->dm;
   cudaStream_t st = e->stream;
   // the new snapshots (stream-ordered allocations, before the upload that names them)
@@ -1001,6 +1043,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   int* plen = slen + nq;
   int* blk = plen + nq;
   int* blk128 = blk + 2 * (size_t)nblk;
+  int* gofs = blk128 + 2 * (size_t)nblk128;
   int* grows = e->fk_pin[slot] + n_idx;
   int* ctab = grows + R;
   int* c0 = ctab + 2 * (size_t)chunks;
@@ -1022,16 +1065,19 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
       t += lens[b];
     }
     if (two_phase) std::stable_sort(order, order + nq, [&](int a, int b) { return lens[a] > lens[b]; });
-    // 128-query blocks, those with the most keys (latest queries) first
+    // 128-query blocks, those with the most keys (latest queries, longest prefixes) first
     int k2 = 0;
     for (int b = 0; b < nq; b++)
       for (int q0 = 0; q0 < lens[b]; q0 += 128, k2++) blk128[2 * k2] = b, blk128[2 * k2 + 1] = q0;
     std::vector<std::pair<int, int>> bl(nblk128);
     for (int i = 0; i < nblk128; i++) bl[i] = {blk128[2 * i], blk128[2 * i + 1]};
-    std::stable_sort(bl.begin(), bl.end(), [&](const std::pair<int, int>& x, const std::pair<int, int>& y) {
-      return std::min(x.second + 128, (int)lens[x.first]) > std::min(y.second + 128, (int)lens[y.first]);
-    });
+    auto keys = [&](const std::pair<int, int>& x) { return plen[x.first] + std::min(x.second + 128, (int)lens[x.first]); };
+    std::stable_sort(bl.begin(), bl.end(),
+                     [&](const std::pair<int, int>& x, const std::pair<int, int>& y) { return keys(x) > keys(y); });
     for (int i = 0; i < nblk128; i++) blk128[2 * i] = bl[i].first, blk128[2 * i + 1] = bl[i].second;
+    // the gathered keys: sequence b at rows gofs[b] .. + plen[b] + lens[b]
+    long long g = 0;
+    for (int b = 0; b < nq; b++) gofs[b] = (int)g, g += plen[b] + lens[b];
   }
   if (ids_host) memcpy(e->fk_pin[slot] + n_idx + R + n_gdn, ids_host, T * sizeof(uint32_t));
   CK(cudaMemcpyAsync(e->fk_meta, e->fk_pin[slot], n_all * sizeof(int), cudaMemcpyHostToDevice, st));
@@ -1058,6 +1104,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   fk.tpos = di, fk.tstart = di + T, fk.tseq = di + 2 * T;
   fk.seq_off = di + 3 * T, fk.seq_len = fk.seq_off + nq, fk.plen = fk.seq_len + nq, fk.blk = fk.plen + nq;
   fk.blk128 = fk.blk + 2 * (size_t)nblk, fk.nblk128 = nblk128;
+  fk.gofs = fk.blk128 + 2 * (size_t)nblk128, fk.ktot = ktot;
   if (two_phase) {
     fk.chunk_tab = dm + n_idx + R;
     fk.chunk0 = fk.chunk_tab + 2 * (size_t)chunks;
@@ -1223,6 +1270,7 @@ void sd_engine_destroy(sd_engine* e) {
   cudaFreeHost(e->p_out);
   cudaFree(e->fk_meta);
   cudaFree(e->fk_kv);
+  cudaFree(e->fk_gather);
   for (int i = 0; i < sd_engine::kForkSlots; i++) {
     cudaFreeHost(e->fk_pin[i]);
     if (e->fk_ev[i]) cudaEventDestroy(e->fk_ev[i]);
@@ -1247,6 +1295,8 @@ int sd_engine_reserve(sd_engine* e, int32_t max_tokens, int32_t max_seqs, int32_
     return rc;
   for (int s = 0; s < sd_engine::kForkSlots; s++)
     if ((rc = ensure_pin_slot(e, s, ints)) != SD_OK) return rc;
+  // continuations' gathered keys: every sequence a whole context at most (capped at 2^20 rows a head)
+  if ((rc = ensure_gather(e, std::min<long long>((long long)max_seqs * SD_CONTEXT, 1 << 20))) != SD_OK) return rc;
   // the snapshots of such a pass (kept by the pool once freed): max_seqs states and histories, and
   // K/V for max_tokens rows
   const sd::Dims& d = e->dm;

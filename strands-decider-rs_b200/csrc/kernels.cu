@@ -265,6 +265,30 @@ __global__ void kv_pack_kernel(const __half* __restrict__ kt, const __half* __re
   }
 }
 
+// kv_pack_kernel into one gathered tensor: sequence b's rows at gofs[b] of every head's ktot rows.
+__global__ void kv_gather_kernel(const __half* __restrict__ kt, const __half* __restrict__ vt, int T, int hd,
+                                 const int* __restrict__ seq_off, const int* __restrict__ seq_len, const int* __restrict__ plen,
+                                 const __half* const* __restrict__ kp, const __half* const* __restrict__ vp,
+                                 const int* __restrict__ gofs, int ktot, __half* __restrict__ gk, __half* __restrict__ gv) {
+  const int b = blockIdx.z, kh = blockIdx.y;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int p = plen[b], n = p + seq_len[b];
+  if (row >= n) return;
+  const __half *sk, *sv;
+  if (row < p) {
+    sk = kp[b] + ((size_t)kh * p + row) * hd;
+    sv = vp[b] + ((size_t)kh * p + row) * hd;
+  } else {
+    sk = kt + ((size_t)kh * T + seq_off[b] + row - p) * hd;
+    sv = vt + ((size_t)kh * T + seq_off[b] + row - p) * hd;
+  }
+  const size_t o = ((size_t)kh * ktot + gofs[b] + row) * hd;
+  for (int c = lane * 8; c < hd; c += 256) {
+    *reinterpret_cast<uint4*>(gk + o + c) = *reinterpret_cast<const uint4*>(sk + c);
+    *reinterpret_cast<uint4*>(gv + o + c) = *reinterpret_cast<const uint4*>(sv + c);
+  }
+}
+
 // The per-token gates of the gated delta rule (src/kernels.rs:289-292): beta = sigmoid(b) and the log
 // decay g = negA * softplus(a + dt_bias), softplus(x) = x above 20 (the decay is exp(g)).
 __global__ void gdn_gates_kernel(const __half* __restrict__ big, int stride, int aoff, int boff, const float* __restrict__ neg_a,
@@ -517,6 +541,15 @@ cudaError_t launch_hist_pack(const __half* big, int stride, int C, const int* se
   return cudaGetLastError();
 }
 
+cudaError_t launch_kv_gather(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
+                             const int* plen, const __half* const* kp, const __half* const* vp, const int* gofs, int ktot,
+                             __half* gk, __half* gv, int nseq, int max_rows, cudaStream_t st) {
+  if (nseq <= 0 || nseq > 65535 || hk <= 0 || hk > 65535 || hd % 8 || max_rows <= 0 || max_rows > ktot) return cudaErrorInvalidValue;
+  kv_gather_kernel<<<dim3((max_rows + 7) / 8, hk, nseq), 256, 0, st>>>(kt, vt, T, hd, seq_off, seq_len, plen, kp, vp, gofs, ktot,
+                                                                       gk, gv);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_kv_pack(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
                            const int* plen, const __half* const* kp, const __half* const* vp, __half* const* k_out,
                            __half* const* v_out, int nseq, int max_rows, cudaStream_t st) {
@@ -568,7 +601,7 @@ cudaError_t preload_kernels() {
                        (const void*)conv_kernel,       (const void*)hist_update_kernel, (const void*)gdn_gates_kernel,
                        (const void*)gdn_recurrent_kernel, (const void*)gnorm_kernel,  (const void*)qk_prep_kernel,
                        (const void*)trace_kernel,      (const void*)add_bias_kernel,    (const void*)hist_pack_kernel,
-                       (const void*)kv_pack_kernel,    (const void*)qk_prep_warp_kernel};
+                       (const void*)kv_pack_kernel,    (const void*)qk_prep_warp_kernel, (const void*)kv_gather_kernel};
   for (const void* f : fns) {
     cudaError_t e = cudaFuncGetAttributes(&a, f);
     if (e != cudaSuccess) return e;

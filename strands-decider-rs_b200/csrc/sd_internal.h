@@ -65,6 +65,12 @@ cudaError_t launch_hist_pack(const __half* big, int stride, int C, const int* se
 // packed sequences: each sequence's keys and values, its prefix (kp[b] / vp[b], [hk][plen[b]][hd]) then
 // its own rows (kt / vt, [hk][T][hd] at seq_off[b]), to k_out[b] / v_out[b] ([hk][plen + len][hd];
 // null entry: skipped). max_rows: the largest plen + len.
+// packed sequences: each sequence's keys and values, its prefix (kp[b] / vp[b], [hk][plen[b]][hd]) then
+// its own rows (kt / vt, [hk][T][hd] at seq_off[b]), gathered into gk / gv [hk][ktot][hd] at rows
+// gofs[b] .. + plen[b] + seq_len[b]. max_rows: the largest plen + len.
+cudaError_t launch_kv_gather(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
+                             const int* plen, const __half* const* kp, const __half* const* vp, const int* gofs, int ktot,
+                             __half* gk, __half* gv, int nseq, int max_rows, cudaStream_t st);
 cudaError_t launch_kv_pack(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
                            const int* plen, const __half* const* kp, const __half* const* vp, __half* const* k_out,
                            __half* const* v_out, int nseq, int max_rows, cudaStream_t st);
@@ -141,6 +147,11 @@ struct AttnTcArgs {
   const int* seq_len = nullptr;
   int l = 0, p = 0, hq = 0, hk = 0;
   int batch = 1;  // single-sequence mode: independent sequences (blockIdx.z), q/k/v/gate/out batch-major
+  // packed mode with prefixes (continuations): sequence b's keys are rows kbase_tab[b] .. of the K/V
+  // tensors, its plen[b]-row prefix first, and its query i sits at position plen[b] + i (null: rows
+  // seq_off[b] .., no prefix)
+  const int* kbase_tab = nullptr;
+  const int* plen = nullptr;
   const __half* gate = nullptr;
   int gstride = 0, goff = 0, gstep = 0;
   __half* out = nullptr;
