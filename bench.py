@@ -10,15 +10,15 @@ then each question continued from the snapshot, hidden rows at the option tokens
 then the pointer head. A step is a batch of --requests-per-step requests per GPU (weak scaling:
 each rank takes its own requests, no collective on the data path): the states of all of them in one
 packed pass, a snapshot each (sd_forward_batch), then their questions in one batched fork, each
-continuing its own request's snapshot (sd_forward_fork_multi), as a server answers concurrent
-requests.
+continuing its own request's snapshot (sd_forward_fork_multi), then the pointer head of every
+question on the GPU (f64), as a server answers concurrent requests.
 
 `value`: device-resident inputs (token ids and rows staged in HBM before the timed region),
-passes queued with sd_forward_batch_dev / sd_forward_fork_multi_dev, hidden rows left in HBM; CUDA
-events on the engine's stream.
-`e2e`: the same requests through the C ABI with host buffers (sd_forward_batch / sd_forward_fork_multi:
-ids host->device, hidden rows device->host, synchronous per call) and the pointer head on the host
-(sd_head_probs).
+passes queued with sd_forward_batch_dev / sd_forward_fork_multi_dev / sd_head_probs_dev,
+probabilities left in HBM; CUDA events on the engine's stream.
+`e2e`: the same requests through the C ABI with host buffers (sd_forward_batch, then
+sd_forward_fork_multi_probs: ids host->device, each question's probabilities device->host,
+synchronous per call).
 `roofline`: the dominant kernel (the dequantizing GEMM), from per-launch CUDA events on the engine's
 stream over a profiled pass of the same steps.
 """
@@ -291,6 +291,7 @@ def run_ours(args, world, rank, local):
         step_s[s] = torch.cat([staged[i][0] for i in ii])
         step_q[s] = torch.cat([staged[i][1] for i in ii])
     hidden_dev = torch.empty((per * 12, 2048), dtype=torch.float32, device="cuda")
+    probs_dev = torch.empty(per * 12, dtype=torch.float64, device="cuda")
     # working memory for the largest pass of any step, up front (as a server sizes it at start-up)
     eng.reserve(max(max(t.numel() for t in step_s.values()), max(t.numel() for t in step_q.values())), per * 3, per * 12)
     torch.cuda.synchronize()
@@ -312,6 +313,7 @@ def run_ours(args, world, rank, local):
             rows += qr
             n_tok += qd.numel()
         eng.forward_fork_dev(caches, step_q[s].data_ptr(), lens, rows, hidden_dev.data_ptr())
+        eng.head_probs_dev(head, hidden_dev.data_ptr(), [len(r) for r in rows], 1.0, probs_dev.data_ptr())
         for snap in snaps:
             snap.close()
         return len(lens), n_tok
@@ -330,11 +332,10 @@ def run_ours(args, world, rank, local):
             caches += [snap] * len(qs)
             qids += [q for q, _ in qs]
             qrows += [r for _, r in qs]
-        outs = eng.forward_fork(caches, qids, qrows)
-        for q, r, hidden in zip(qids, qrows, outs):
-            head.probs(hidden, 2048, 1.0)
+        outs = eng.forward_fork_probs(caches, qids, qrows, head, 1.0)
+        for q, r, probs in zip(qids, qrows, outs):
             h2d += q.nbytes + r.nbytes
-            d2h += hidden.nbytes
+            d2h += probs.nbytes
         for snap in snaps:
             snap.close()
         return len(outs)
@@ -403,7 +404,7 @@ def run_ours(args, world, rank, local):
                    "parallelism": f"replicas x{world} (requests sharded, no collective)"},
         "prefill_tok_s": tok_all / t_dev,
         "e2e": {"value": qh_all / t_host, "unit": "questions/s", "h2d_bytes_per_step": int(h2d_step),
-                "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward_batch (the step's states, one snapshot each) + sd_forward_fork_multi (the step's questions, each from its request's snapshot; host ids in, host hidden rows out) + sd_head_probs"},
+                "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward_batch (the step's states, one snapshot each) + sd_forward_fork_multi_probs (the step's questions, each from its request's snapshot, and the pointer head on the GPU; host ids in, host probabilities out)"},
         "gpu_launches": int(launches),
         "roofline": {"kernel": "gemm_q4_tc (dequantizing tcgen05 GEMM)", "bound": "tensor", "achieved": gemm_tflops,
                      "peak": tf_sus, "unit": "TFLOP/s", "frac": gemm_tflops / tf_sus,

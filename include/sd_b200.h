@@ -138,6 +138,22 @@ int sd_engine_profile_get(sd_engine* e, int32_t kind, double* ms, int64_t* launc
 int sd_head_load(const char* safetensors_path, sd_head** out);
 void sd_head_free(sd_head* h);
 int sd_head_probs(const sd_head* h, const float* hidden, int32_t n_rows, int32_t d, double temperature, double* probs_out);
+/* `Head::probs` on the GPU, for many questions at once, asynchronous on the engine's stream (f64 as
+ * on the host; sums in tree order, so equal to sd_head_probs to f64 rounding). hidden_dev holds the
+ * questions' rows back to back as the engine's _dev calls write them (question i: n_rows[i] rows,
+ * options then answer, hidden_size f32 each; a rotated torso's rows are mapped back on the device);
+ * temperatures[i] (host) is question i's; probs_dev gets sum(n_rows[i] - 1) f64, question after
+ * question. The head's weights go to the engine's device on first use. */
+int sd_head_probs_dev(sd_engine* e, const sd_head* h, const float* hidden_dev, const int32_t* n_rows, int32_t n_questions,
+                      const double* temperatures, double* probs_dev);
+/* sd_forward_fork_multi with the pointer head on the GPU: the questions' hidden rows never leave the
+ * device, only their probabilities come back (probs_out, host, sum(n_rows[i] - 1) f64; every
+ * question needs 2 or more rows: its options and its answer). Synchronous. The question loop of
+ * `Decider::run` (`src/lib.rs:191-198`: a forward from the prefix snapshot, then `Head::probs`, per
+ * question) as one call. */
+int sd_forward_fork_multi_probs(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids, const int32_t* lens,
+                                int32_t n_questions, const int32_t* rows, const int32_t* n_rows, const sd_head* h,
+                                const double* temperatures, double* probs_out);
 
 /* The Decider on the engine (the reference's `Decider`, `src/lib.rs:100-209`): tokenizer, prompt,
  * torso, pointer head and answers in the library (C++). */

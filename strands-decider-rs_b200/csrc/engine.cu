@@ -110,6 +110,10 @@ struct sd_qweight {
 struct sd_head {
   std::vector<float> nw, nb, qw, qb, kw, kb;
   int dim = 0, d = 0;
+  // the weights on each device that ran the head there ([qw | kw | nw | nb | qb | kb] f32), uploaded
+  // on first use
+  mutable std::mutex mu;
+  mutable float* dev[sd::kMaxDevices] = {};
 };
 
 struct sd_engine {
@@ -170,6 +174,13 @@ struct sd_engine {
   int p_row_cap = 0;  // rows of p_rows and p_out
   float* trace_host = nullptr;
   size_t trace_floats = 0;
+  // the pointer head on the device: question table, xn, proj and probabilities (grown as needed),
+  // the rotated torso's per-channel factors, and pinned staging of the probabilities
+  void* hd_buf = nullptr;
+  size_t hd_bytes = 0;
+  double* d_unrot = nullptr;
+  double* hd_pin = nullptr;
+  size_t hd_pin_doubles = 0;
   std::string err;
   // launches of this library's kernels since creation
   long long launches = 0;
@@ -1177,6 +1188,82 @@ int batch_host(sd_engine* e, const char* fn, const sd_snapshot* const* caches, b
   return SD_OK;
 }
 
+// The head's weights on the engine's device, uploaded on first use.
+int head_weights(sd_engine* e, const sd_head* h, sd::HeadWeights* hw) {
+  std::lock_guard<std::mutex> lock(h->mu);
+  float*& p = h->dev[e->device];
+  const size_t w = (size_t)h->dim * h->d;
+  if (!p) {
+    std::vector<float> all;
+    all.reserve(2 * w + 2 * (size_t)h->d + 2 * (size_t)h->dim);
+    for (const auto* v : {&h->qw, &h->kw, &h->nw, &h->nb, &h->qb, &h->kb}) all.insert(all.end(), v->begin(), v->end());
+    float* dp = nullptr;
+    CK(cudaMalloc(&dp, all.size() * sizeof(float)));
+    if (cudaMemcpy(dp, all.data(), all.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaFree(dp);
+      return e->fail(SD_ERR_CUDA, "uploading the head");
+    }
+    p = dp;
+  }
+  hw->qw = p, hw->kw = p + w, hw->nw = p + 2 * w, hw->nb = hw->nw + h->d, hw->qb = hw->nb + h->d, hw->kb = hw->qb + h->dim;
+  return SD_OK;
+}
+
+// Queues the pointer head over the hidden rows at `hidden` (question after question, nrows[i] rows
+// each: options, then the answer) on the engine's stream; the probabilities go to probs_dev, or to
+// the engine's own buffer when probs_dev is null (*probs_at, *n_probs either way).
+int enqueue_head(sd_engine* e, const char* fn, const sd_head* h, const float* hidden, const int32_t* nrows, int nq,
+                 const double* temps, double* probs_dev, double** probs_at, long long* n_probs) {
+  if (!h || !nrows || !temps || nq <= 0) return e->fail(SD_ERR_INVALID, "%s: bad arguments", fn);
+  if (h->d != e->dm.d) return e->fail(SD_ERR_INVALID, "%s: head of width %d on a torso of %d", fn, h->d, e->dm.d);
+  std::vector<sd::HeadQuestion> qs(nq);
+  long long R = 0, P = 0;
+  for (int i = 0; i < nq; i++) {
+    if (nrows[i] < 2) return e->fail(SD_ERR_INVALID, "%s: question %d has %d rows (options and the answer: 2 or more)", fn, i, nrows[i]);
+    qs[i].row0 = (int)R, qs[i].nrows = nrows[i], qs[i].prob0 = (int)P, qs[i].pad = 0;
+    qs[i].scale = std::pow((double)h->dim, -0.5) / std::max(temps[i], 1e-6);
+    R += nrows[i];
+    P += nrows[i] - 1;
+  }
+  if (R > (1 << 24)) return e->fail(SD_ERR_INVALID, "%s: %lld rows", fn, R);
+  cudaSetDevice(e->device);
+  sd::HeadWeights hw;
+  int rc = head_weights(e, h, &hw);
+  if (rc != SD_OK) return rc;
+  if (!e->unrotate.empty() && !e->d_unrot) {
+    CK(cudaMalloc(&e->d_unrot, e->unrotate.size() * sizeof(double)));
+    CK(cudaMemcpy(e->d_unrot, e->unrotate.data(), e->unrotate.size() * sizeof(double), cudaMemcpyHostToDevice));
+  }
+  auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+  const size_t tb = up((size_t)nq * sizeof(sd::HeadQuestion)), xb = up((size_t)R * h->d * 8), pb = up((size_t)R * h->dim * 8),
+               ob = up((size_t)P * 8);
+  if (e->hd_bytes < tb + xb + pb + ob) {
+    CK(cudaStreamSynchronize(e->stream));
+    cudaFree(e->hd_buf);
+    e->hd_buf = nullptr, e->hd_bytes = 0;
+    const size_t want = std::max<size_t>(tb + xb + pb + ob, (size_t)4 << 20);
+    CK(cudaMalloc(&e->hd_buf, want));
+    e->hd_bytes = want;
+  }
+  char* base = (char*)e->hd_buf;
+  auto* dq = (sd::HeadQuestion*)base;
+  auto* xn = (double*)(base + tb);
+  auto* proj = (double*)(base + tb + xb);
+  double* probs = probs_dev ? probs_dev : (double*)(base + tb + xb + pb);
+  // a pageable source: staged before the call returns, so `qs` may go
+  CK(cudaMemcpyAsync(dq, qs.data(), (size_t)nq * sizeof(sd::HeadQuestion), cudaMemcpyHostToDevice, e->stream));
+  const double* unrot = (int)e->unrotate.size() == h->d ? e->d_unrot : nullptr;
+  const double bytes = (double)R * h->d * 4 + 2.0 * h->dim * h->d * 4 + (double)P * 8;
+  cudaError_t ce = launch(e, SD_PROF_OTHER, bytes, [&](int* nl) -> cudaError_t {
+    *nl = 3;
+    return sd::launch_head(hidden, (int)R, dq, nq, h->d, h->dim, unrot, hw, xn, proj, probs, e->stream);
+  });
+  if (ce != cudaSuccess) return e->fail(SD_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(ce));
+  if (probs_at) *probs_at = probs;
+  if (n_probs) *n_probs = P;
+  return SD_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1231,7 +1318,8 @@ int sd_engine_create(const char* model_dir, int device, sd_engine** out) {
   cudaError_t ce;
   if ((ce = sd::preload_gemm()) != cudaSuccess || (ce = sd::preload_attention()) != cudaSuccess ||
       (ce = sd::preload_attention_tc()) != cudaSuccess ||
-      (ce = sd::preload_gdn()) != cudaSuccess || (ce = sd::preload_kernels()) != cudaSuccess) {
+      (ce = sd::preload_gdn()) != cudaSuccess || (ce = sd::preload_kernels()) != cudaSuccess ||
+      (ce = sd::preload_head()) != cudaSuccess) {
     set_global_error(std::string("sd_engine_create: loading the kernels: ") + cudaGetErrorString(ce));
     sd_engine_destroy(e);
     return SD_ERR_CUDA;
@@ -1271,6 +1359,9 @@ void sd_engine_destroy(sd_engine* e) {
   cudaFree(e->fk_meta);
   cudaFree(e->fk_kv);
   cudaFree(e->fk_gather);
+  cudaFree(e->hd_buf);
+  cudaFree(e->d_unrot);
+  cudaFreeHost(e->hd_pin);
   for (int i = 0; i < sd_engine::kForkSlots; i++) {
     cudaFreeHost(e->fk_pin[i]);
     if (e->fk_ev[i]) cudaEventDestroy(e->fk_ev[i]);
@@ -1539,7 +1630,15 @@ int sd_head_load(const char* path, sd_head** out) {
   return SD_OK;
 }
 
-void sd_head_free(sd_head* h) { delete h; }
+void sd_head_free(sd_head* h) {
+  if (!h) return;
+  for (int dv = 0; dv < sd::kMaxDevices; dv++)
+    if (h->dev[dv]) {
+      cudaSetDevice(dv);
+      cudaFree(h->dev[dv]);
+    }
+  delete h;
+}
 
 int sd_head_probs(const sd_head* h, const float* hidden, int32_t nrows, int32_t d, double temperature, double* probs) {
   if (!h || !hidden || !probs || nrows < 2 || d != h->d) {
@@ -1602,6 +1701,44 @@ int sd_head_probs(const sd_head* h, const float* hidden, int32_t nrows, int32_t 
     z += probs[i];
   }
   for (int i = 0; i < nopt; i++) probs[i] /= z;
+  return SD_OK;
+}
+
+int sd_head_probs_dev(sd_engine* e, const sd_head* h, const float* hidden_dev, const int32_t* nrows, int32_t nq,
+                      const double* temperatures, double* probs_dev) {
+  if (!e) return SD_ERR_INVALID;
+  if (!hidden_dev || !probs_dev) return e->fail(SD_ERR_INVALID, "sd_head_probs_dev: null device buffer");
+  return enqueue_head(e, "sd_head_probs_dev", h, hidden_dev, nrows, nq, temperatures, probs_dev, nullptr, nullptr);
+}
+
+int sd_forward_fork_multi_probs(sd_engine* e, const sd_snapshot* const* caches, const uint32_t* ids, const int32_t* lens,
+                                int32_t nq, const int32_t* rows, const int32_t* nrows, const sd_head* h,
+                                const double* temperatures, double* probs_out) {
+  if (!e) return SD_ERR_INVALID;
+  const char* fn = "sd_forward_fork_multi_probs";
+  if (!caches) return e->fail(SD_ERR_INVALID, "%s: no snapshots (the questions continue one)", fn);
+  if (!ids || !probs_out || !rows || !nrows) return e->fail(SD_ERR_INVALID, "%s: null argument", fn);
+  if (!h || !temperatures) return e->fail(SD_ERR_INVALID, "%s: no head", fn);
+  if (h->d != e->dm.d) return e->fail(SD_ERR_INVALID, "%s: head of width %d on a torso of %d", fn, h->d, e->dm.d);
+  for (int i = 0; i < nq; i++)
+    if (nrows[i] < 2) return e->fail(SD_ERR_INVALID, "%s: question %d has %d rows (options and the answer: 2 or more)", fn, i, nrows[i]);
+  long long R = 0;
+  int rc = packed_enqueue(e, fn, caches, true, ids, nullptr, lens, nq, rows, nrows, false, nullptr, true, true, &R);
+  if (rc != SD_OK) return rc;
+  double* probs = nullptr;
+  long long P = 0;
+  if ((rc = enqueue_head(e, fn, h, e->out, nrows, nq, temperatures, nullptr, &probs, &P)) != SD_OK) return rc;
+  if (e->hd_pin_doubles < (size_t)P) {
+    CK(cudaStreamSynchronize(e->stream));
+    cudaFreeHost(e->hd_pin);
+    e->hd_pin = nullptr, e->hd_pin_doubles = 0;
+    const size_t cap = std::max<size_t>((size_t)P, 4096);
+    CK(cudaMallocHost(&e->hd_pin, cap * sizeof(double)));
+    e->hd_pin_doubles = cap;
+  }
+  CK(cudaMemcpyAsync(e->hd_pin, probs, (size_t)P * sizeof(double), cudaMemcpyDeviceToHost, e->stream));
+  if ((rc = sync_engine(e)) != SD_OK) return rc;
+  memcpy(probs_out, e->hd_pin, (size_t)P * sizeof(double));
   return SD_OK;
 }
 

@@ -200,8 +200,8 @@ struct sd_decider {
   // Many requests at once, as a server answers concurrent ones: every request's first forward (its
   // state, kept as a snapshot; or, with a single question, state and question together, as
   // `Decider::run` does) in packed passes (sd_forward_batch), then every question continuing its
-  // request's snapshot in packed forks (sd_forward_fork_multi). Each request's answers equal its own
-  // `run` up to f32 summation order. out[i]: the response, or {"error": message} for a request that
+  // request's snapshot in packed forks with the pointer head on the GPU (sd_forward_fork_multi_probs).
+  // Each request's answers equal its own `run` up to f32 summation order. out[i]: the response, or {"error": message} for a request that
   // failed (invalid, too long, or a failed pass of the torso).
   std::vector<sd::pj::Value> run_batch(const std::vector<const sd::pj::Value*>& states,
                                        const std::vector<std::vector<std::pair<std::string, sd::prompt::Question>>>& named,
@@ -293,6 +293,7 @@ struct sd_decider {
         std::vector<const sd_snapshot*> caches;
         std::vector<uint32_t> ids;
         std::vector<int32_t> lens, rows, nrows;
+        std::vector<double> temps;
         for (const auto& rq : group) {
           const Prepared& p = prep[rq.first];
           const Encoding& q = p.qs[rq.second];
@@ -302,23 +303,21 @@ struct sd_decider {
           for (size_t o : p.options[rq.second]) rows.push_back((int32_t)o);
           rows.push_back((int32_t)q.ids.size() - 1);
           nrows.push_back((int32_t)p.options[rq.second].size() + 1);
+          temps.push_back(temperature(p.rendered[rq.second].kind));
         }
-        std::vector<float> hidden(rows.size() * (size_t)d);
-        const int rc = sd_forward_fork_multi(engine, caches.data(), ids.data(), lens.data(), (int32_t)lens.size(), rows.data(),
-                                             nrows.data(), hidden.data(), nullptr);
+        // the fork and the pointer head on the GPU: only the probabilities come back
+        std::vector<double> all(rows.size() - group.size());
+        const int rc = sd_forward_fork_multi_probs(engine, caches.data(), ids.data(), lens.data(), (int32_t)lens.size(),
+                                                   rows.data(), nrows.data(), head, temps.data(), all.data());
         size_t at = 0;
         for (size_t g = 0; g < group.size(); g++) {
           const size_t r = group[g].first;
           if (rc != SD_OK) {
             errors[r] = sd_engine_last_error(engine);
           } else if (errors[r].empty()) {
-            try {
-              probs[r][group[g].second] = head_probs(prep[r], group[g].second, hidden.data() + at * d, (size_t)nrows[g]);
-            } catch (const std::exception& e) {
-              errors[r] = e.what();
-            }
+            probs[r][group[g].second].assign(all.begin() + at, all.begin() + at + nrows[g] - 1);
           }
-          at += nrows[g];
+          at += nrows[g] - 1;
         }
         group.clear();
         tokens = 0;

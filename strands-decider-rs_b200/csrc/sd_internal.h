@@ -164,6 +164,23 @@ int attention_splits_packed(int nblk, int p, int max_len, int hq, int num_sms);
 int attention_splits(int l, int p, int hq, int num_sms);
 size_t attention_split_bytes(int l, int hq, int splits);
 
+// The pointer head on the device (head.cu). Question q's rows are row0 .. row0 + nrows - 1 of the
+// hidden rows (its options, then its answer row); its nrows - 1 probabilities go to probs[prob0 ..];
+// scale = dim^-1/2 / max(temperature, 1e-6).
+struct HeadQuestion {
+  int row0, nrows, prob0, pad;
+  double scale;
+};
+struct HeadWeights {
+  const float *nw = nullptr, *nb = nullptr, *qw = nullptr, *qb = nullptr, *kw = nullptr, *kb = nullptr;
+};
+// xn [nrows_total][d] and proj [nrows_total][dim] f64 are working memory; unrot (d f64, or null)
+// maps a rotated torso's rows back to the head's basis first.
+cudaError_t launch_head(const float* hidden, int nrows_total, const HeadQuestion* qs, int nq, int d, int dim,
+                        const double* unrot, const HeadWeights& hw, double* xn, double* proj, double* probs,
+                        cudaStream_t st);
+cudaError_t preload_head();
+
 // Load every kernel of a file on the current device (first-use module loads happen at engine
 // creation, not inside a timed forward).
 cudaError_t preload_gemm();

@@ -69,6 +69,8 @@ def lib() -> C.CDLL:
         L.sd_head_load.argtypes = [cp, C.POINTER(vp)]
         L.sd_head_free.argtypes = [vp]
         L.sd_head_probs.argtypes = [vp, vp, i32, i32, C.c_double, vp]
+        L.sd_head_probs_dev.argtypes = [vp, vp, vp, vp, i32, vp, vp]
+        L.sd_forward_fork_multi_probs.argtypes = [vp, vp, vp, vp, i32, vp, vp, vp, vp, vp]
         L.sd_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]
         L.sd_attention_batch.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp]
         L.sd_attention_split.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp,
@@ -229,6 +231,31 @@ class Engine:
             _check(lib().sd_forward_fork_dev(self._h, cache._h, ids_dev, _ptr(lens), len(lens),
                                              _ptr(rows) if len(rows) else None, _ptr(nrows), hidden_dev),
                    "sd_forward_fork_dev", self._h)
+
+    def forward_fork_probs(self, caches, ids_list, rows_list, head: "Head", temperatures):
+        """`sd_forward_fork_multi_probs`: question b (ids_list[b], its option rows then its answer
+        row in rows_list[b]) continued from caches[b], then the pointer head on the GPU; returns each
+        question's probabilities (f64, len(rows_list[b]) - 1 each)."""
+        lens = np.array([len(x) for x in ids_list], np.int32)
+        nrows = np.array([len(r) for r in rows_list], np.int32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(x, np.uint32) for x in ids_list]), np.uint32)
+        rows = np.ascontiguousarray(np.concatenate([np.asarray(r, np.int32) for r in rows_list]), np.int32)
+        temps = np.ascontiguousarray(np.broadcast_to(np.asarray(temperatures, np.float64), (len(lens),)))
+        probs = np.zeros(int(nrows.sum()) - len(lens), np.float64)
+        caches = (C.c_void_p * len(caches))(*[c._h for c in caches])
+        _check(lib().sd_forward_fork_multi_probs(self._h, caches, _ptr(ids), _ptr(lens), len(lens), _ptr(rows), _ptr(nrows),
+                                                 head._h, _ptr(temps), _ptr(probs)),
+               "sd_forward_fork_multi_probs", self._h)
+        return np.split(probs, np.cumsum(nrows - 1)[:-1]) if len(lens) > 1 else [probs]
+
+    def head_probs_dev(self, head: "Head", hidden_dev: int, nrows, temperatures, probs_dev: int):
+        """`sd_head_probs_dev`: the pointer head over questions' rows already on the GPU (question b:
+        nrows[b] rows at ``hidden_dev``, back to back), probabilities to ``probs_dev`` (f64), queued on
+        the engine's stream."""
+        nrows = np.ascontiguousarray(nrows, np.int32)
+        temps = np.ascontiguousarray(np.broadcast_to(np.asarray(temperatures, np.float64), (len(nrows),)))
+        _check(lib().sd_head_probs_dev(self._h, head._h, hidden_dev, _ptr(nrows), len(nrows), _ptr(temps), probs_dev),
+               "sd_head_probs_dev", self._h)
 
     def reserve(self, max_tokens: int, max_seqs: int, max_rows: int):
         """`sd_engine_reserve`: size the working memory for passes up to these bounds up front."""
