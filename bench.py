@@ -266,7 +266,9 @@ def run_ours(args, world, rank, local):
 
     path = model_path(world, rank)
     torch.cuda.set_device(local)
+    t_load = time.perf_counter()
     eng = Engine.load(path, local)
+    t_load = time.perf_counter() - t_load
     head = Head.load(os.path.join(path, "head.safetensors"))
     stream = torch.cuda.ExternalStream(eng.stream)
     per = args.requests_per_step
@@ -403,6 +405,7 @@ def run_ours(args, world, rank, local):
                    "sweep_clipped_requests": clips, "l2": "inputs larger than L2 (0.8 GB of weights streamed per forward)",
                    "parallelism": f"replicas x{world} (requests sharded, no collective)"},
         "prefill_tok_s": tok_all / t_dev,
+        "engine_load_s": round(t_load, 3),
         "e2e": {"value": qh_all / t_host, "unit": "questions/s", "h2d_bytes_per_step": int(h2d_step),
                 "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward_batch (the step's states, one snapshot each) + sd_forward_fork_multi_probs (the step's questions, each from its request's snapshot, and the pointer head on the GPU; host ids in, host probabilities out)"},
         "gpu_launches": int(launches),

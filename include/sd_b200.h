@@ -171,9 +171,10 @@ void sd_decider_free(sd_decider* d);
 int sd_decider_ask_all(sd_decider* d, const char* request_json, char** response_json);
 /* Many requests at once (a JSON array of requests as sd_decider_ask_all takes them), as a server
  * answers concurrent ones: the requests' states in packed passes (sd_forward_batch), then all their
- * questions in packed forks (sd_forward_fork_multi). Writes a JSON array in the same order: each
- * request's response body, equal to its own sd_decider_ask_all up to f32 summation order, or
- * {"error": message} for a request that failed. The call itself fails only on a malformed array. */
+ * questions in packed forks with the pointer head on the GPU (sd_forward_fork_multi_probs). Writes a
+ * JSON array in the same order: each request's response body, equal to its own sd_decider_ask_all up
+ * to f32 summation order, or {"error": message} for a request that failed. The call itself fails
+ * only on a malformed array. */
 int sd_decider_ask_batch(sd_decider* d, const char* requests_json, char** responses_json);
 const char* sd_decider_last_error(const sd_decider* d);
 const char* sd_host_last_error(void);
@@ -260,6 +261,16 @@ void sd_qweight_free(sd_qweight* w);
  * 0 bytes disables split-K). Results do not depend on the split count's summation order run to run. */
 int sd_matmul(const sd_qweight* w, const void* act_dev, int32_t m, void* y_dev, int32_t ldy, int32_t silu, void* ws_dev,
               size_t ws_bytes, void* stream);
+
+/* `decode_scales` (`src/model.rs:219-236`) on the device: src_dev holds n 4-byte row headers (m as
+ * fp16 bits, j as u16) then n rows of g codes (`sign << 7 | k`); dst_dev gets [n][g] fp16 with
+ * |scale| = fp16(f32(m 2^(-k j / 4096))), the power in f64 from a host table as the reference builds
+ * it, so bit-identical to the host decode. Synchronous (the headers are read to size the table).
+ * sd_engine_create uses the same kernels for the embedding's 8-bit scale codes (`embed_parts`,
+ * `src/model.rs:260-283`) and for packed shards (`unpack_shard`, `src/model.rs:239-258`: a shard
+ * whose manifest entry has `wire` and whose converted weights.<i>.bin is absent is read from its
+ * `path` and unpacked on the device). */
+int sd_decode_scales(const void* src_dev, int32_t n, int32_t g, void* dst_dev, void* stream);
 
 #ifdef __cplusplus
 }

@@ -51,32 +51,9 @@ struct LayerW {
   const float *q_norm = nullptr, *k_norm = nullptr, *bias = nullptr;
 };
 
-float half_bits_to_float(uint16_t h) {
-  __half_raw r;
-  r.x = h;
-  return __half2float(__half(r));
-}
-
-uint16_t float_to_half_bits(float f) {
-  __half_raw r = __half(__float2half_rn(f));
-  return r.x;
-}
-
-// `decode_scales` (src/model.rs:219-236): n rows of g codes, each row after a 4-byte header (m as
-// fp16 bits, j as u16); |scale| = fp16(f32(m * 2^(-k j / 4096))) with the power in f64.
-void decode_scales(const uint8_t* src, int n, int g, uint16_t* dst) {
-  const uint8_t* codes = src + 4 * (size_t)n;
-  for (int r = 0; r < n; r++) {
-    const uint16_t mb = (uint16_t)(src[4 * r] | (src[4 * r + 1] << 8));
-    const uint16_t j = (uint16_t)(src[4 * r + 2] | (src[4 * r + 3] << 8));
-    const double m = (double)half_bits_to_float(mb);
-    for (int i = 0; i < g; i++) {
-      const uint8_t c = codes[(size_t)r * g + i];
-      const int k = c & 127;
-      const uint16_t mag = float_to_half_bits((float)(m * std::pow(2.0, -(double)(k * j) / 4096.0)));
-      dst[(size_t)r * g + i] = (uint16_t)(mag | ((uint16_t)(c & 128) << 8));
-    }
-  }
+bool file_exists(const std::string& path) {
+  struct stat st;
+  return stat(path.c_str(), &st) == 0;
 }
 
 bool read_file(const std::string& path, std::string& out) {
@@ -357,29 +334,83 @@ int load_engine(sd_engine* e, const std::string& dir) {
   const size_t chunk = 64ull << 20;
   CK(cudaMallocHost(&pinned, chunk));
   std::unique_ptr<uint8_t, void (*)(uint8_t*)> pin_guard(pinned, [](uint8_t* p) { cudaFreeHost(p); });
+  // Reads `bytes` bytes of `path` into device memory at `dev` through the pinned chunk; `jmax_at`
+  // (optional): per chunk, the largest u16 at row offsets of `row_bytes` + `jmax_off` (the embedding
+  // rows' scale-code headers) is folded into *jmax.
+  auto upload = [&](const std::string& path, FILE* f, uint8_t* dev, uint64_t bytes, size_t row_bytes, size_t jmax_off,
+                    int* jmax) -> int {
+    const size_t step = row_bytes ? chunk / row_bytes * row_bytes : chunk;
+    for (uint64_t off = 0; off < bytes; off += step) {
+      const size_t n = (size_t)std::min<uint64_t>(step, bytes - off);
+      if (fread(pinned, 1, n, f) != n)
+        return e->fail(SD_ERR_IO, "%s: %llu bytes, expected %llu", path.c_str(), (unsigned long long)off,
+                       (unsigned long long)bytes);
+      if (jmax)
+        for (size_t r = 0; r + row_bytes <= n; r += row_bytes)
+          *jmax = std::max(*jmax, (int)(pinned[r + jmax_off + 2] | (pinned[r + jmax_off + 3] << 8)));
+      CK(cudaMemcpy(dev + off, pinned, n, cudaMemcpyHostToDevice));
+    }
+    return SD_OK;
+  };
   for (size_t i = 0; i < shards.size(); i++) {
     const uint64_t start = (uint64_t)shards[i].at("start").integer(), bytes = (uint64_t)shards[i].at("bytes").integer();
     std::string path = dir + "/weights." + std::to_string(i) + ".bin";
+    const auto* wire = shards[i].get("wire");
+    const bool packed = wire && !wire->is_null() && !file_exists(path);
+    if (packed) path = dir + "/" + shards[i].at("path").str;
     FILE* f = fopen(path.c_str(), "rb");
     if (!f) return e->fail(SD_ERR_IO, "%s: cannot open", path.c_str());
+    std::unique_ptr<FILE, int (*)(FILE*)> f_guard(f, fclose);
     uint8_t* dev = nullptr;
     cudaError_t ce = cudaMalloc(&dev, std::max<uint64_t>(bytes, 16));
-    if (ce != cudaSuccess) {
-      fclose(f);
-      return e->fail(SD_ERR_CUDA, "shard %zu: %s", i, cudaGetErrorString(ce));
-    }
+    if (ce != cudaSuccess) return e->fail(SD_ERR_CUDA, "shard %zu: %s", i, cudaGetErrorString(ce));
     e->shards.push_back(dev);
     e->shard_ranges.push_back({start, bytes});
-    for (uint64_t off = 0; off < bytes; off += chunk) {
-      const size_t n = (size_t)std::min<uint64_t>(chunk, bytes - off);
-      if (fread(pinned, 1, n, f) != n) {
-        fclose(f);
-        return e->fail(SD_ERR_IO, "%s: %llu bytes, the manifest says %llu", path.c_str(), (unsigned long long)off,
-                       (unsigned long long)bytes);
-      }
-      CK(cudaMemcpy(dev + off, pinned, n, cudaMemcpyHostToDevice));
+    if (!packed) {
+      int rc = upload(path, f, dev, bytes, 0, 0, nullptr);
+      if (rc != SD_OK) return rc;
+      continue;
     }
-    fclose(f);
+    // a packed shard (`unpack_shard`, src/model.rs:239-258): its tensors back to back, scales as 8-bit
+    // codes; uploaded as is, then each tensor goes to its offset, the codes decoded on the device
+    const uint64_t wbytes = (uint64_t)wire->integer();
+    if (path.size() > 3 && path.compare(path.size() - 3, 3, ".gz") == 0)
+      return e->fail(SD_ERR_FORMAT, "%s: a compressed shard (decompress it first)", path.c_str());
+    uint8_t* wdev = nullptr;
+    CK(cudaMalloc(&wdev, std::max<uint64_t>(wbytes, 16)));
+    std::unique_ptr<uint8_t, cudaError_t (*)(void*)> w_guard(wdev, cudaFree);
+    int rc = upload(path, f, wdev, wbytes, 0, 0, nullptr);
+    if (rc != SD_OK) return rc;
+    CK(cudaMemset(dev, 0, bytes));
+    for (const auto& kv : tensors.obj) {
+      const auto& t = kv.second;
+      const auto* tw = t.get("wire");
+      if (!tw || tw->is_null()) continue;
+      const uint64_t off = t.get("offset") ? (uint64_t)t.at("offset").integer() : 0;
+      const uint64_t tb = t.get("bytes") ? (uint64_t)t.at("bytes").integer() : 0;
+      if (off < start || off >= start + bytes) continue;
+      if (off + tb > start + bytes) return e->fail(SD_ERR_FORMAT, "packed shard: %s out of range", kv.first.c_str());
+      const uint64_t w = (uint64_t)tw->integer();
+      const bool u8 = t.get("u8") && t.at("u8").boolean();
+      uint8_t* dst = dev + (off - start);
+      if (u8) {
+        const auto& shape = t.at("shape").arr;
+        if (shape.size() != 2) return e->fail(SD_ERR_FORMAT, "packed shard: %s: 8-bit scales need a 2-D shape", kv.first.c_str());
+        const uint64_t n = (uint64_t)shape[0].integer(), g = (uint64_t)shape[1].integer();
+        if (w + 4 * n + n * g > wbytes || 2 * n * g > tb)
+          return e->fail(SD_ERR_FORMAT, "packed shard: %s out of range", kv.first.c_str());
+        // the rows' largest j bounds the power table (headers: m, j as u16 each)
+        std::vector<uint8_t> hdr(4 * n);
+        CK(cudaMemcpy(hdr.data(), wdev + w, hdr.size(), cudaMemcpyDeviceToHost));
+        int jmax = 0;
+        for (uint64_t r = 0; r < n; r++) jmax = std::max(jmax, (int)(hdr[4 * r + 2] | (hdr[4 * r + 3] << 8)));
+        CK(sd::decode_scales_dev(wdev + w, 4, wdev + w + 4 * n, g, (long long)n, (int)g, jmax, (uint16_t*)dst, g, e->stream));
+      } else {
+        if (w + tb > wbytes) return e->fail(SD_ERR_FORMAT, "packed shard: %s out of range", kv.first.c_str());
+        CK(cudaMemcpyAsync(dst, wdev + w, tb, cudaMemcpyDeviceToDevice, e->stream));
+      }
+    }
+    CK(cudaStreamSynchronize(e->stream));
   }
   auto tensor_ptr = [&](const std::string& name, const sd::json::Value** meta) -> const uint8_t* {
     const auto* t = tensors.get(name);
@@ -476,34 +507,31 @@ int load_engine(sd_engine* e, const std::string& dir) {
     const size_t rb = (wrb && !wrb->is_null()) ? (size_t)wrb->integer() : (size_t)emb->at("row_bytes").integer();
     if (qb != (size_t)d.d / 32 * 4 * e->embed_bits || sb != (size_t)d.d / 32 * 2)
       return e->fail(SD_ERR_FORMAT, "embed part sizes do not match the hidden size");
+    if (rb < qb + (u8 ? 4 + sb / 2 : sb)) return e->fail(SD_ERR_FORMAT, "embedding rows of %zu bytes are shorter than their parts", rb);
     std::string path = dir + "/" + emb->at("rows").str;
     FILE* f = fopen(path.c_str(), "rb");
     if (!f) return e->fail(SD_ERR_IO, "%s: cannot open", path.c_str());
+    std::unique_ptr<FILE, int (*)(FILE*)> f_guard(f, fclose);
     struct stat stbuf;
-    if (fstat(fileno(f), &stbuf) != 0 || (size_t)stbuf.st_size != (size_t)e->vocab * rb) {
-      fclose(f);
+    if (fstat(fileno(f), &stbuf) != 0 || (size_t)stbuf.st_size != (size_t)e->vocab * rb)
       return e->fail(SD_ERR_IO, "%s: %lld bytes, expected %d rows of %zu", path.c_str(), (long long)stbuf.st_size, e->vocab, rb);
-    }
-    std::vector<uint8_t> hq((size_t)e->vocab * qb), hs((size_t)e->vocab * sb);
-    std::vector<uint8_t> rows(rb * 4096);
-    for (int r0 = 0; r0 < e->vocab; r0 += 4096) {
-      const int n = std::min(4096, e->vocab - r0);
-      if (fread(rows.data(), 1, rb * n, f) != rb * n) {
-        fclose(f);
-        return e->fail(SD_ERR_IO, "%s: short read", path.c_str());
-      }
-      for (int r = 0; r < n; r++) {
-        const uint8_t* row = rows.data() + rb * r;
-        memcpy(hq.data() + (size_t)(r0 + r) * qb, row, qb);
-        if (u8) decode_scales(row + qb, 1, (int)sb / 2, reinterpret_cast<uint16_t*>(hs.data() + (size_t)(r0 + r) * sb));
-        else memcpy(hs.data() + (size_t)(r0 + r) * sb, row + qb, sb);
-      }
-    }
-    fclose(f);
-    CK(cudaMalloc(&e->embed_q, hq.size()));
-    CK(cudaMalloc(&e->embed_s, hs.size()));
-    CK(cudaMemcpy(e->embed_q, hq.data(), hq.size(), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(e->embed_s, hs.data(), hs.size(), cudaMemcpyHostToDevice));
+    // the rows file goes up as is; the parts are split out (and 8-bit scale codes decoded,
+    // `decode_scales`, src/model.rs:219-236) on the device
+    uint8_t* raw = nullptr;
+    CK(cudaMalloc(&raw, (size_t)e->vocab * rb));
+    std::unique_ptr<uint8_t, cudaError_t (*)(void*)> raw_guard(raw, cudaFree);
+    int jmax = 0;
+    int rc = upload(path, f, raw, (uint64_t)e->vocab * rb, rb, qb, u8 ? &jmax : nullptr);
+    if (rc != SD_OK) return rc;
+    CK(cudaMalloc(&e->embed_q, (size_t)e->vocab * qb));
+    CK(cudaMalloc(&e->embed_s, (size_t)e->vocab * sb));
+    CK(sd::split_rows_dev(raw, rb, 0, qb, e->vocab, e->embed_q, e->stream));
+    if (u8)
+      CK(sd::decode_scales_dev(raw + qb, rb, raw + qb + 4, rb, e->vocab, (int)sb / 2, jmax,
+                               reinterpret_cast<uint16_t*>(e->embed_s), sb / 2, e->stream));
+    else
+      CK(sd::split_rows_dev(raw, rb, qb, sb, e->vocab, reinterpret_cast<uint8_t*>(e->embed_s), e->stream));
+    CK(cudaStreamSynchronize(e->stream));
   }
 
   // recurrent state, conv history, K/V caches (src/engine.rs:251-257), RoPE table (:259-269)
@@ -1749,6 +1777,24 @@ static int op_result(cudaError_t ce, const char* what) {
   if (ce == cudaSuccess) return SD_OK;
   set_global_error(std::string(what) + ": " + cudaGetErrorString(ce));
   return ce == cudaErrorInvalidValue ? SD_ERR_INVALID : SD_ERR_CUDA;
+}
+
+int sd_decode_scales(const void* src_dev, int32_t n, int32_t g, void* dst_dev, void* stream) {
+  if (!src_dev || !dst_dev || n < 0 || g <= 0 || g > (1 << 20)) {
+    set_global_error("sd_decode_scales: bad arguments");
+    return SD_ERR_INVALID;
+  }
+  if (n == 0) return SD_OK;
+  const uint8_t* src = (const uint8_t*)src_dev;
+  std::vector<uint8_t> hdr((size_t)4 * n);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t ce = cudaMemcpyAsync(hdr.data(), src, hdr.size(), cudaMemcpyDeviceToHost, st);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+  if (ce != cudaSuccess) return op_result(ce, "sd_decode_scales");
+  int jmax = 0;
+  for (int32_t r = 0; r < n; r++) jmax = std::max(jmax, (int)(hdr[4 * (size_t)r + 2] | (hdr[4 * (size_t)r + 3] << 8)));
+  return op_result(sd::decode_scales_dev(src, 4, src + 4 * (size_t)n, g, n, g, jmax, (uint16_t*)dst_dev, g, st),
+                   "sd_decode_scales");
 }
 
 int sd_attention(const void* q, const void* k, const void* v, const void* gate, int32_t gstride, int32_t goff, int32_t gstep,

@@ -63,14 +63,14 @@ cudaError_t launch_hist_update(const __half* big, int stride, __half* hist, int 
 cudaError_t launch_hist_pack(const __half* big, int stride, int C, const int* seq_off, const int* seq_len,
                              const __half* const* h_in, __half* const* h_out, int nseq, cudaStream_t st);
 // packed sequences: each sequence's keys and values, its prefix (kp[b] / vp[b], [hk][plen[b]][hd]) then
-// its own rows (kt / vt, [hk][T][hd] at seq_off[b]), to k_out[b] / v_out[b] ([hk][plen + len][hd];
-// null entry: skipped). max_rows: the largest plen + len.
-// packed sequences: each sequence's keys and values, its prefix (kp[b] / vp[b], [hk][plen[b]][hd]) then
 // its own rows (kt / vt, [hk][T][hd] at seq_off[b]), gathered into gk / gv [hk][ktot][hd] at rows
 // gofs[b] .. + plen[b] + seq_len[b]. max_rows: the largest plen + len.
 cudaError_t launch_kv_gather(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
                              const int* plen, const __half* const* kp, const __half* const* vp, const int* gofs, int ktot,
                              __half* gk, __half* gv, int nseq, int max_rows, cudaStream_t st);
+// packed sequences: each sequence's keys and values, its prefix (kp[b] / vp[b], [hk][plen[b]][hd]) then
+// its own rows (kt / vt, [hk][T][hd] at seq_off[b]), to k_out[b] / v_out[b] ([hk][plen + len][hd];
+// null entry: skipped). max_rows: the largest plen + len.
 cudaError_t launch_kv_pack(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
                            const int* plen, const __half* const* kp, const __half* const* vp, __half* const* k_out,
                            __half* const* v_out, int nseq, int max_rows, cudaStream_t st);
@@ -180,6 +180,15 @@ cudaError_t launch_head(const float* hidden, int nrows_total, const HeadQuestion
                         const double* unrot, const HeadWeights& hw, double* xn, double* proj, double* probs,
                         cudaStream_t st);
 cudaError_t preload_head();
+
+// The wire format on the device (wire.cu). decode_scales_dev: n rows of g 8-bit scale codes (row r's
+// 4-byte header at hdr + r hdr_stride, its codes at codes + r code_stride) to fp16 bits at dst + r
+// dst_stride; jmax bounds the rows' j. split_rows_dev: bytes [off, off + len) of n rows of `stride`
+// bytes to a dense [n][len] array. Both are stream-ordered.
+cudaError_t decode_scales_dev(const uint8_t* hdr, size_t hdr_stride, const uint8_t* codes, size_t code_stride, long long n,
+                              int g, int jmax, uint16_t* dst, size_t dst_stride, cudaStream_t st);
+cudaError_t split_rows_dev(const uint8_t* src, size_t stride, size_t off, size_t len, long long n, uint8_t* dst,
+                           cudaStream_t st);
 
 // Load every kernel of a file on the current device (first-use module loads happen at engine
 // creation, not inside a timed forward).

@@ -70,6 +70,7 @@ def lib() -> C.CDLL:
         L.sd_head_free.argtypes = [vp]
         L.sd_head_probs.argtypes = [vp, vp, i32, i32, C.c_double, vp]
         L.sd_head_probs_dev.argtypes = [vp, vp, vp, vp, i32, vp, vp]
+        L.sd_decode_scales.argtypes = [vp, i32, i32, vp, vp]
         L.sd_forward_fork_multi_probs.argtypes = [vp, vp, vp, vp, i32, vp, vp, vp, vp, vp]
         L.sd_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]
         L.sd_attention_batch.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp]
@@ -397,6 +398,12 @@ def gdn(q, k, qk_stride, v, v_stride, beta, g, state, load_state, o, l, h, batch
         algo = GDN_SERIAL if serial else GDN_CHUNKED
     _check(lib().sd_gdn(q, k, qk_stride, v, v_stride, beta, g, state, int(load_state), o, l, h, batch, seq_qk, seq_v,
                         int(in_f16), int(algo), scratch, scratch_bytes, stream), "sd_gdn")
+
+
+def decode_scales(src, n, g, dst, stream=None):
+    """`decode_scales` (`src/model.rs:219-236`) on the device: n headers then n x g codes at ``src``,
+    [n][g] fp16 to ``dst`` (device pointers)."""
+    _check(lib().sd_decode_scales(src, n, g, dst, stream), "sd_decode_scales")
 
 
 def gdn_scratch_bytes(l: int, h: int) -> int:

@@ -423,3 +423,80 @@ def ensure_model(path: str, **kw) -> str:
     from .tokenizer import write_synthetic_tokenizer
     write_synthetic_tokenizer(os.path.join(path, "tokenizer.json"), seed=kw.get("seed", 0))
     return path
+
+
+# ---------------------------------------------------------------------------------------------
+# The packed download format
+# ---------------------------------------------------------------------------------------------
+
+def write_packed(src: str, packed: str, unpacked: str) -> None:
+    """From the GPU-layout model at ``src``, two directories holding the same weights.
+
+    ``packed`` keeps its shard in the reference's packed download format, which `unpack_shard`
+    (`src/model.rs:239-258`) converts:
+    - tensors back to back, with a gap of 0-2 bytes after each (unaligned offsets);
+    - every 2-D scale tensor (``*.s``) stored as 8-bit codes (``u8``);
+    - the manifest's shard entry naming the packed file (``path``) and its size (``wire``);
+    - no ``weights.0.bin``.
+
+    ``unpacked`` is in GPU layout, with the scales the codes decode to: what the reference's
+    download writes. The other files are symlinked to ``src``."""
+    m = read_manifest(src)
+    if len(m["shards"]) != 1:
+        raise ValueError("one shard expected")
+    with open(os.path.join(src, "weights.0.bin"), "rb") as f:
+        data = bytearray(f.read())
+    wire = bytearray()
+    tensors = json.loads(json.dumps(m["tensors"]))
+    order = sorted((t["offset"], name) for name, t in m["tensors"].items() if t.get("bytes", 0) > 0)
+    for i, (off, name) in enumerate(order):
+        t = tensors[name]
+        raw = bytes(data[off:off + t["bytes"]])
+        t["wire"] = len(wire)
+        if name.endswith(".s") and len(t["shape"]) == 2:
+            enc, dec = encode_scales_u8(np.frombuffer(raw, np.float16).reshape(t["shape"]))
+            t["u8"] = True
+            wire += enc
+            data[off:off + t["bytes"]] = dec.tobytes()
+        else:
+            wire += raw
+        wire += b"\x5a" * (i % 3)
+    for out in (packed, unpacked):
+        os.makedirs(out, exist_ok=True)
+        for f in os.listdir(src):
+            if f not in ("manifest.json", "weights.0.bin") and not os.path.exists(os.path.join(out, f)):
+                os.symlink(os.path.abspath(os.path.join(src, f)), os.path.join(out, f))
+    with open(os.path.join(packed, "weights.0.wire"), "wb") as f:
+        f.write(wire)
+    mp = json.loads(json.dumps(m))
+    mp["tensors"] = tensors
+    mp["shards"] = [{"path": "weights.0.wire", "start": 0, "bytes": m["shards"][0]["bytes"], "wire": len(wire)}]
+    with open(os.path.join(packed, "manifest.json"), "w") as f:
+        json.dump(mp, f)
+    with open(os.path.join(unpacked, "weights.0.bin"), "wb") as f:
+        f.write(data)
+    with open(os.path.join(unpacked, "manifest.json"), "w") as f:
+        json.dump(m, f)
+
+
+def unpack_shard(wire: bytes, shard: dict, tensors: dict) -> bytes:
+    """`unpack_shard` (`src/model.rs:239-258`) in numpy: each tensor with a ``wire`` offset in the
+    shard's range goes to its offset, 8-bit scale codes decoded (`decode_scales`); the rest is zero."""
+    out = bytearray(shard["bytes"])
+    for name, t in tensors.items():
+        w = t.get("wire")
+        if w is None or not (shard["start"] <= t.get("offset", 0) < shard["start"] + shard["bytes"]):
+            continue
+        o = t["offset"] - shard["start"]
+        if t.get("u8"):
+            n, g = t["shape"]
+            src = wire[w:w + 4 * n + n * g]
+            if len(src) != 4 * n + n * g:
+                raise ValueError(f"packed shard: {name} out of range")
+            out[o:o + t["bytes"]] = decode_scales_u8(bytes(src), n, g).tobytes()
+        else:
+            src = wire[w:w + t["bytes"]]
+            if len(src) != t["bytes"]:
+                raise ValueError(f"packed shard: {name} out of range")
+            out[o:o + t["bytes"]] = src
+    return bytes(out)
