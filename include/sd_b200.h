@@ -187,6 +187,13 @@ int sd_tokenizer_load(const char* tokenizer_json_path, sd_tokenizer** out);
 void sd_tokenizer_free(sd_tokenizer* t);
 int sd_tokenizer_encode(const sd_tokenizer* t, const char* text, size_t len, uint32_t* ids, uint32_t* offsets, int64_t cap,
                         int64_t* n_out);
+/* Many texts (texts[i], lens[i] bytes) encoded on up to `threads` host threads (0: one per hardware
+ * thread, at most 16), as a server tokenizes concurrent requests; sd_decider_ask_batch prepares its
+ * requests the same way. counts[i] gets text i's token count; ids and offsets are written text after
+ * text, at most `cap` tokens in all. Equal to n sd_tokenizer_encode calls. A text that fails fails
+ * the call (the first by index names it). */
+int sd_tokenizer_encode_batch(const sd_tokenizer* t, const char* const* texts, const size_t* lens, int64_t n, int32_t threads,
+                              uint32_t* ids, uint32_t* offsets, int64_t cap, int64_t* counts);
 /* Prompt rendering (`src/prompt.rs:159-200`) of {"state": content, "questions": [question, ...]}:
  * writes {"state": text, "questions": [{"text": text, "spans": [[begin, end], ...]}]} (byte ranges of
  * the option lines) to *out_json (free with sd_string_free). */

@@ -11,7 +11,9 @@
 #include <sstream>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
+#include <atomic>
 
 #include "prompt.h"
 #include "pyjson.h"
@@ -29,6 +31,26 @@ int host_fail(std::string* slot, const std::string& msg) {
   if (slot) *slot = msg;
   g_host_error = msg;
   return SD_ERR_INVALID;
+}
+
+// fn(i) for i in [0, n) on up to `threads` host threads (0: one per hardware thread, at most 16);
+// fn must not throw.
+template <class F>
+void parallel_for(size_t n, int threads, F&& fn) {
+  size_t t = threads > 0 ? (size_t)threads : std::min<size_t>(16, std::max(1u, std::thread::hardware_concurrency()));
+  t = std::min(t, n);
+  if (t <= 1) {
+    for (size_t i = 0; i < n; i++) fn(i);
+    return;
+  }
+  std::atomic<size_t> next{0};
+  auto work = [&]() {
+    for (size_t i; (i = next.fetch_add(1)) < n;) fn(i);
+  };
+  std::vector<std::thread> pool;
+  for (size_t k = 1; k < t; k++) pool.emplace_back(work);
+  work();
+  for (auto& th : pool) th.join();
 }
 
 bool read_file(const std::string& path, std::string& out, std::string& err) {
@@ -213,15 +235,16 @@ struct sd_decider {
     std::vector<Prepared> prep(n);
     std::vector<std::vector<std::vector<double>>> probs(n);
     std::vector<sd_snapshot*> snaps(n, nullptr);
-    for (size_t r = 0; r < n; r++) {
-      if (!errors[r].empty()) continue;
+    // rendering and tokenizing, request by request on the host threads (the tokenizer is read-only)
+    parallel_for(n, 0, [&](size_t r) {
+      if (!errors[r].empty()) return;
       try {
         prep[r] = prepare(*states[r], named[r]);
         probs[r].resize(prep[r].qs.size());
       } catch (const std::exception& e) {
         errors[r] = e.what();
       }
-    }
+    });
     auto fail_all = [&](const std::vector<size_t>& group, const std::string& msg) {
       for (size_t r : group) errors[r] = msg;
     };
@@ -383,6 +406,34 @@ int sd_tokenizer_encode(const sd_tokenizer* t, const char* text, size_t len, uin
   } catch (const std::exception& e) {
     return host_fail(nullptr, e.what());
   }
+}
+
+int sd_tokenizer_encode_batch(const sd_tokenizer* t, const char* const* texts, const size_t* lens, int64_t n, int32_t threads,
+                              uint32_t* ids, uint32_t* offsets, int64_t cap, int64_t* counts) {
+  if (!t || n < 0 || (n > 0 && (!texts || !lens || !counts)))
+    return host_fail(nullptr, "sd_tokenizer_encode_batch: null argument");
+  for (int64_t i = 0; i < n; i++)
+    if (!texts[i] && lens[i]) return host_fail(nullptr, "sd_tokenizer_encode_batch: null text");
+  std::vector<sd::Encoding> enc((size_t)n);
+  std::vector<std::string> errs((size_t)n);
+  parallel_for((size_t)n, threads, [&](size_t i) {
+    try {
+      enc[i] = t->tok->encode(std::string(texts[i] ? texts[i] : "", lens[i]));
+    } catch (const std::exception& e) {
+      errs[i] = e.what();
+    }
+  });
+  for (int64_t i = 0; i < n; i++)
+    if (!errs[i].empty()) return host_fail(nullptr, "text " + std::to_string(i) + ": " + errs[i]);
+  int64_t at = 0;
+  for (int64_t i = 0; i < n; i++) {
+    counts[i] = (int64_t)enc[i].ids.size();
+    for (size_t k = 0; k < enc[i].ids.size() && at < cap; k++, at++) {
+      if (ids) ids[at] = enc[i].ids[k];
+      if (offsets) offsets[2 * at] = enc[i].offsets[k].first, offsets[2 * at + 1] = enc[i].offsets[k].second;
+    }
+  }
+  return SD_OK;
 }
 
 int sd_prompt_render(const char* request_json, char** out_json) {

@@ -24,6 +24,8 @@ def lib():
     L.sd_tokenizer_free.argtypes = [C.c_void_p]
     L.sd_tokenizer_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, C.c_void_p, C.c_void_p, C.c_int64,
                                       C.POINTER(C.c_int64)]
+    L.sd_tokenizer_encode_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p,
+                                            C.c_void_p, C.c_int64, C.c_void_p]
     L.sd_prompt_render.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
     L.sd_string_free.argtypes = [C.c_void_p]
     L.sd_host_last_error.restype = C.c_char_p
@@ -48,6 +50,25 @@ class CppTokenizer:
         if rc != 0:
             raise ValueError(self.L.sd_host_last_error().decode())
         return list(ids[:n.value]), [(offs[2 * i], offs[2 * i + 1]) for i in range(n.value)]
+
+    def encode_batch(self, texts, threads=0, cap=None):
+        bs = [t if isinstance(t, bytes) else t.encode() for t in texts]
+        n = len(bs)
+        ptrs = (C.c_char_p * n)(*bs)
+        lens = (C.c_size_t * n)(*[len(b) for b in bs])
+        cap = sum(4 * len(b) + 8 for b in bs) if cap is None else cap
+        ids = (C.c_uint32 * max(cap, 1))()
+        offs = (C.c_uint32 * max(2 * cap, 1))()
+        counts = (C.c_int64 * max(n, 1))()
+        rc = self.L.sd_tokenizer_encode_batch(self.h, ptrs, lens, n, threads, ids, offs, cap, counts)
+        if rc != 0:
+            raise ValueError(self.L.sd_host_last_error().decode())
+        out, at = [], 0
+        for i in range(n):
+            c = counts[i]
+            out.append((list(ids[at:min(at + c, cap)]), [(offs[2 * k], offs[2 * k + 1]) for k in range(at, min(at + c, cap))], c))
+            at += c
+        return out
 
     def close(self):
         self.L.sd_tokenizer_free(self.h)
@@ -92,6 +113,23 @@ def test_tokenizer_matches_the_mirror(tokenizers):
         ids, offs = cpp.encode(t)
         assert ids == e.ids, t
         assert offs == [tuple(o) for o in e.offsets], t
+
+
+@pytest.mark.parametrize("threads", [1, 4, 0])
+def test_tokenizer_batch_matches_one_by_one(tokenizers, threads):
+    """sd_tokenizer_encode_batch on host threads = sd_tokenizer_encode text by text (ids, offsets,
+    counts), including empty texts; a cap cuts the written tokens, not the counts."""
+    _, cpp = tokenizers
+    texts = list(_texts(3, 300)) + ["", "".join(_texts(4, 200))]
+    got = cpp.encode_batch(texts, threads)
+    for t, (ids, offs, c) in zip(texts, got):
+        want_ids, want_offs = cpp.encode(t)
+        assert (ids, offs, c) == (want_ids, want_offs, len(want_ids)), t
+    short = cpp.encode_batch(texts[:5], threads, cap=7)
+    assert [c for _, _, c in short] == [len(cpp.encode(t)[0]) for t in texts[:5]]
+    assert sum(len(i) for i, _, _ in short) == min(7, sum(c for _, _, c in short))
+    with pytest.raises(ValueError, match="text 1: text is not UTF-8"):
+        cpp.encode_batch(["ok", b"bad \xff\xfe", b"\xff"], threads)
 
 
 def test_tokenizer_on_long_text(tokenizers):
