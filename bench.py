@@ -136,6 +136,44 @@ def peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+class PassRoofline:
+    """The aggregate roofline of the sweep: for each packed pass, the slower of its bytes at the
+    measured HBM bandwidth and its FLOPs at the measured sustained tensor peak, summed over the
+    passes. A pass streams every layer weight once (int4 g32: 0.5625 B per weight), moves each
+    GEMM's f16 activations in and out, reads and writes the gated-delta states of its sequences
+    (written only when kept) and their K/V rows; FLOPs are the GEMMs (2 N K per token), causal
+    attention (4 hd hq per query-key pair, over the prefix too) and the chunked gated-delta rule
+    (8 C dk + 6 dk^2 + 2 C^2 / 3 per token and head, C = 64)."""
+
+    def __init__(self, path: str):
+        from strands_decider import model
+        m = model.read_manifest(path)
+        c = m["config"]
+        self.n_lin = sum(t == "linear_attention" for t in c["layer_types"])
+        self.n_full = sum(t == "full_attention" for t in c["layer_types"])
+        mats = [(t["N"], t["K"]) for n, t in m["tensors"].items() if n.endswith(".q") and n != "embed.q"]
+        self.weight_bytes = sum(nn * k for nn, k in mats) * 0.5625
+        self.flop_tok = 2.0 * sum(nn * k for nn, k in mats)
+        self.act_tok = 2.0 * sum(nn + k for nn, k in mats)
+        self.h, self.dk, self.dv = c["linear_num_key_heads"], c["linear_key_head_dim"], c["linear_value_head_dim"]
+        self.hq, self.hk, self.hd = c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"]
+        C = 64
+        self.gdn_flop_tok = (8 * C * self.dk + 6 * self.dk * self.dk + 2 * C * C / 3) * self.h * self.n_lin
+        self.gdn_bytes_tok = (3 * self.h * self.dk * 2 + 8 * self.h + 4 * self.h * self.dv) * self.n_lin
+        self.state_bytes = self.h * self.dk * self.dv * 4 * self.n_lin
+        self.kv_tok = 2 * self.hk * self.hd * 2 * self.n_full
+        self.bound_s = 0.0
+
+    def add(self, seqs, keep: bool, hbm_gbs: float, tflops: float):
+        """One pass over sequences (prefix length, new tokens)."""
+        tok = sum(l for _, l in seqs)
+        pairs = sum(l * p + l * (l + 1) / 2 for p, l in seqs)
+        flops = self.flop_tok * tok + 4.0 * self.hd * self.hq * pairs * self.n_full + self.gdn_flop_tok * tok
+        nbytes = (self.weight_bytes + (self.act_tok + self.gdn_bytes_tok + self.kv_tok) * tok
+                  + self.state_bytes * len(seqs) * (2 if keep else 1) + self.kv_tok * sum(p for p, _ in seqs))
+        self.bound_s += max(nbytes / (hbm_gbs * 1e9), flops / (tflops * 1e12))
+
+
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -302,6 +340,9 @@ def run_ours(args, world, rank, local):
     # a snapshot, then its questions continued from the snapshot. The states of all the step's
     # requests run as one packed pass (sd_forward_batch, a snapshot each), then their questions as
     # one batched fork (each continuing its own request's snapshot)
+    hbm_gbs, _, tf_sustained, _ = peaks()
+    roof = PassRoofline(path)
+
     def one_step_dev(s):
         ii = step_requests(s, rank, world, per, args.seed)
         slens = [staged[i][0].numel() for i in ii]
@@ -381,6 +422,11 @@ def run_ours(args, world, rank, local):
     prof = eng.profile_get()
     eng.profile(False)
 
+    for s in range(args.steps):  # the timed steps' passes, counted outside the timed region
+        ii = step_requests(args.warmup + s, rank, world, per, args.seed)
+        roof.add([(0, staged[i][0].numel()) for i in ii], True, hbm_gbs, tf_sustained)
+        roof.add([(staged[i][0].numel(), n) for i in ii for n in staged[i][2]], False, hbm_gbs, tf_sustained)
+    bound_all = sum_over_ranks(world, roof.bound_s)
     t_dev = max_over_ranks(world, ms_dev) / 1e3
     t_host = max_over_ranks(world, ms_host) / 1e3
     q_all = sum_over_ranks(world, q_dev)
@@ -406,6 +452,8 @@ def run_ours(args, world, rank, local):
                    "parallelism": f"replicas x{world} (requests sharded, no collective)"},
         "prefill_tok_s": tok_all / t_dev,
         "engine_load_s": round(t_load, 3),
+        "aggregate_roofline": {"bound_ms_per_step": 1e3 * bound_all / world / args.steps, "frac": bound_all / world / t_dev,
+                               "basis": "per packed pass max(bytes / measured HBM, FLOPs / measured sustained bf16), summed over the timed passes"},
         "e2e": {"value": qh_all / t_host, "unit": "questions/s", "h2d_bytes_per_step": int(h2d_step),
                 "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward_batch (the step's states, one snapshot each) + sd_forward_fork_multi_probs (the step's questions, each from its request's snapshot, and the pointer head on the GPU; host ids in, host probabilities out)"},
         "gpu_launches": int(launches),
