@@ -44,6 +44,31 @@ def test_matmul_matches_oracle(torch, m, n, k):
         assert err.max() <= 2e-3 + 2e-3 * np.abs(want).max(), (ws_bytes, err.max())
 
 
+@pytest.mark.parametrize("m,n,k,silu", [(2500, 2048, 2048, False), (1000, 8256, 2048, False), (777, 12288, 2048, True),
+                                         (4097, 384, 192, False)])
+def test_matmul_large_m(torch, m, n, k, silu):
+    """Large token counts without split-K: many waves of persistent tiles, an odd count of 128-row
+    weight tiles, an odd k-tile count, and the SwiGLU epilogue."""
+    from strands_decider.engine import QWeight
+    rng = np.random.default_rng(m + n + k)
+    packed, scales = M._quant_tensor(rng, n, k, 4, 1.0 / np.sqrt(k))
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    want = oracle.matmul(a, packed, scales, n, k, 4, variant=2).astype(np.float32)
+    if silu:
+        g, u = want[:, :n // 2], want[:, n // 2:]
+        want = (g / (1 + np.exp(-g)) * u).astype(np.float16).astype(np.float32)
+    q_d, s_d, a_d = dev(torch, packed), dev(torch, scales.view(np.uint16)), dev(torch, a.view(np.uint16))
+    w = QWeight(q_d.data_ptr(), s_d.data_ptr(), n, k, interleave=silu)
+    nout = n // 2 if silu else n
+    y = torch.full((m, nout), float("nan"), dtype=torch.float16, device="cuda")
+    w.matmul(a_d.data_ptr(), m, y.data_ptr(), nout, silu=silu, ws_dev=None, ws_bytes=0)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy().astype(np.float32)
+    assert np.isfinite(got).all()
+    tol = (4e-3 if silu else 2e-3) * (1 + np.abs(want).max())
+    assert np.abs(got - want).max() <= tol
+
+
 @pytest.mark.parametrize("m", [5, 64, 100, 200, 328])
 def test_matmul_swiglu_epilogue(torch, m):
     from strands_decider.engine import QWeight
