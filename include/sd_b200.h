@@ -143,7 +143,8 @@ int sd_head_probs(const sd_head* h, const float* hidden, int32_t n_rows, int32_t
  * questions' rows back to back as the engine's _dev calls write them (question i: n_rows[i] rows,
  * options then answer, hidden_size f32 each; a rotated torso's rows are mapped back on the device);
  * temperatures[i] (host) is question i's; probs_dev gets sum(n_rows[i] - 1) f64, question after
- * question. The head's weights go to the engine's device on first use. */
+ * question (at most 65535 questions per call). The head's weights go to the engine's device on first
+ * use; sd_head_free releases them (after the device's queued work). */
 int sd_head_probs_dev(sd_engine* e, const sd_head* h, const float* hidden_dev, const int32_t* n_rows, int32_t n_questions,
                       const double* temperatures, double* probs_dev);
 /* sd_forward_fork_multi with the pointer head on the GPU: the questions' hidden rows never leave the

@@ -1243,6 +1243,7 @@ int head_weights(sd_engine* e, const sd_head* h, sd::HeadWeights* hw) {
 int enqueue_head(sd_engine* e, const char* fn, const sd_head* h, const float* hidden, const int32_t* nrows, int nq,
                  const double* temps, double* probs_dev, double** probs_at, long long* n_probs) {
   if (!h || !nrows || !temps || nq <= 0) return e->fail(SD_ERR_INVALID, "%s: bad arguments", fn);
+  if (nq > 65535) return e->fail(SD_ERR_INVALID, "%s: %d questions in one call (at most 65535)", fn, nq);
   if (h->d != e->dm.d) return e->fail(SD_ERR_INVALID, "%s: head of width %d on a torso of %d", fn, h->d, e->dm.d);
   std::vector<sd::HeadQuestion> qs(nq);
   long long R = 0, P = 0;
