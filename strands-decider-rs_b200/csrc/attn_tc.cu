@@ -88,21 +88,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y, kh = h / (a.hq / a.hk);
-  const int bz = blockIdx.z;  // batch element (single-sequence mode): q / k / v slabs bz * heads + head
+  // Blocks are dispatched in linear order (x fastest). The query-block index is made the slowest
+  // varying one, so the longest query blocks of every head and batch element start first and the
+  // short ones fill the tail (the x order alone would run all of one head's blocks before the next
+  // head's longest).
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int hb = gridDim.y * gridDim.z, bx = lin / hb;
+  const int h = (lin % hb) % gridDim.y, kh = h / (a.hq / a.hk);
+  const int bz = (lin % hb) / gridDim.y;  // batch element (single-sequence mode): q / k / v slabs bz * heads + head
 
   // this CTA's queries: q0 .. q0 + nq - 1 of their sequence (positions p + q0 + i), rows tok0 + i of
   // q / gate / out; the sequence's keys are rows kbase .. of the K/V tensors
   int q0, nq, tok0, kbase, p;
   if (a.blk) {
-    const int sq = a.blk[2 * blockIdx.x];
-    q0 = a.blk[2 * blockIdx.x + 1];
+    const int sq = a.blk[2 * bx];
+    q0 = a.blk[2 * bx + 1];
     nq = min(TQ, a.seq_len[sq] - q0);
     tok0 = a.seq_off[sq] + q0;
     kbase = a.kbase_tab ? a.kbase_tab[sq] : a.seq_off[sq];
     p = a.plen ? a.plen[sq] : 0;
   } else {
-    q0 = (gridDim.x - 1 - blockIdx.x) * TQ;  // longest (latest) query blocks first
+    q0 = (gridDim.x - 1 - bx) * TQ;  // longest (latest) query blocks first
     nq = min(TQ, a.l - q0);
     tok0 = q0;
     kbase = 0;
