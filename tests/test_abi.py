@@ -59,3 +59,22 @@ def test_head_load_errors(tmp_path):
         E.Head.load(str(p))
     with pytest.raises(E.Error):
         E.Head.load(str(tmp_path / "missing.safetensors"))
+
+
+def test_new_entry_points_reject_bad_arguments_without_touching_a_gpu():
+    """The device-side head, the fork-with-head and the scale decoder validate their arguments on the
+    host: a null engine, null buffers or impossible sizes come back as SD_ERR_INVALID with a message."""
+    L = E.lib()
+    L.sd_last_error.restype = ctypes.c_char_p
+    buf = (ctypes.c_uint8 * 64)()
+    # no engine
+    assert L.sd_head_probs_dev(None, None, None, None, 1, None, None) == -1
+    assert L.sd_forward_fork_multi_probs(None, None, None, None, 1, None, None, None, None, None) == -1
+    # decode_scales: null buffers, negative rows, zero or huge group
+    assert L.sd_decode_scales(None, 1, 64, buf, None) == -1
+    assert L.sd_decode_scales(buf, -1, 64, buf, None) == -1
+    assert L.sd_decode_scales(buf, 1, 0, buf, None) == -1
+    assert L.sd_decode_scales(buf, 1, 1 << 21, buf, None) == -1
+    assert b"sd_decode_scales" in L.sd_last_error()
+    # no rows at all is a no-op, not an error
+    assert L.sd_decode_scales(buf, 0, 64, buf, None) == 0
