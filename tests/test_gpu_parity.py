@@ -323,6 +323,25 @@ def test_snapshot_of_continuation(engines):
     assert np.abs(got - want).max() < 2e-2
 
 
+def test_full_context_forward(engines):
+    """The maximum context (4096 tokens, `src/engine.rs:532`): one forward of all of it, the same
+    tokens as a 4000-token snapshot plus a 96-token continuation ending exactly at the limit (the
+    reference's prefix forward == full forward invariant, `tests/engine_parity.rs:59-85`), and the
+    same sequence packed beside a short one in one batch."""
+    gpu, _ = engines
+    rng = np.random.default_rng(4096)
+    ids = rng.integers(0, 8000, 4096)
+    rows = [0, 2047, 4000, 4095]
+    full = gpu.forward(ids, rows).hidden
+    assert np.isfinite(full).all()
+    snap = gpu.forward(ids[:4000], [], keep=True).snapshot
+    cont = gpu.forward(ids[4000:], [0, 95], cache=snap).hidden
+    assert np.abs(cont - full[2:]).max() < 2e-2
+    snap.close()
+    outs, _ = gpu.forward_batch(None, [rng.integers(0, 8000, 37), ids], [[36], rows])
+    assert np.abs(outs[1] - full).max() < 2e-2
+
+
 def test_engine_errors(engines):
     from strands_decider.engine import Error
     gpu, _ = engines
