@@ -35,6 +35,22 @@ def test_fork_matches_serial_continuations(engines):
     snap.close()
 
 
+def test_fork_up_to_the_context_limit(engines):
+    """Questions after a 4000-token snapshot, the longest ending exactly at the 4096-token context:
+    the batched fork equals the serial continuations and, for the longest, the full forward."""
+    gpu, _ = engines
+    rng = np.random.default_rng(23)
+    state = rng.integers(0, 8000, 4000)
+    snap = gpu.forward(state, [], keep=True).snapshot
+    qs, rows = _questions(rng, [96, 50, 130 - 34, 1])
+    got = gpu.forward_fork(snap, qs, rows)
+    for q, r, g in zip(qs, rows, got):
+        assert np.abs(g - gpu.forward(q, r, cache=snap).hidden).max() < 2e-2
+    full = gpu.forward(np.concatenate([state, qs[0]]), [4000 + i for i in rows[0]]).hidden
+    assert np.abs(got[0] - full).max() < 2e-2
+    snap.close()
+
+
 def test_fork_matches_oracle(engines):
     gpu, cpu = engines
     rng = np.random.default_rng(22)

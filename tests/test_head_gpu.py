@@ -47,6 +47,26 @@ def test_head_dev_matches_oracle(parts):
         assert abs(g.sum() - 1.0) < 1e-12
 
 
+def test_head_dev_many_questions(parts):
+    """2000 questions of 2 to 12 rows in one call (grids of thousands of blocks), each against the
+    host head."""
+    import torch
+    eng, head, _ = parts
+    rng = np.random.default_rng(12)
+    nrows = rng.integers(2, 13, 2000).tolist()
+    temps = rng.uniform(0.5, 2.0, 2000).tolist()
+    hidden = rng.standard_normal((sum(nrows), 2048)).astype(np.float32)
+    hd = torch.from_numpy(hidden).cuda()
+    pd = torch.full((sum(nrows) - len(nrows),), float("nan"), dtype=torch.float64, device="cuda")
+    eng.head_probs_dev(head, hd.data_ptr(), nrows, temps, pd.data_ptr())
+    eng.synchronize()
+    got = np.split(pd.cpu().numpy(), np.cumsum(np.array(nrows) - 1)[:-1])
+    row0 = np.concatenate([[0], np.cumsum(nrows)[:-1]])
+    for i in range(0, 2000, 7):
+        want = head.probs(hidden[row0[i]:row0[i] + nrows[i]], 2048, temps[i])
+        np.testing.assert_allclose(got[i], want, rtol=RTOL, atol=ATOL)
+
+
 def test_fork_probs_matches_fork_then_host_head(parts, small_model):
     """sd_forward_fork_multi_probs = sd_forward_fork_multi (the same pass, so the same hidden rows)
     followed by the host head, across two snapshots."""
