@@ -77,3 +77,26 @@ def test_native_decider_batch_matches_one_by_one(small_model):
     with pytest.raises(Exception, match="JSON array"):
         nat.ask_batch({"state": "x"})
     nat.close()
+
+
+def test_native_decider_batch_spans_several_passes(small_model):
+    """Twenty requests of ~3500-token states (over 65536 tokens in all, so the states run in more
+    than one packed pass) and one to three questions each, prepared on host threads: every
+    request's answers match its own ask_all."""
+    from strands_decider import NativeDecider
+    nat = NativeDecider.load(small_model)
+    rng = np.random.default_rng(11)
+    words = ["payout", "refund", "charged", "twice", "help", "urgent", "billing", "login", "error", "slow"]
+    qs = {"urgent": {"type": "noul", "instructions": "Does this convey urgency?"},
+          "team": {"type": "choice", "instructions": "Which team?", "criteria": {"billing": "money", "tech": "", "sales": None}},
+          "mood": {"type": "score", "instructions": "How upset?", "criteria": ["calm", "annoyed", "furious"]}}
+    requests = []
+    for i in range(20):
+        state = " ".join(rng.choice(words, 1300))
+        names = list(qs)[: 1 + i % 3]
+        requests.append({"state": state, "questions": {n: qs[n] for n in names}})
+    got = nat.ask_batch(requests)
+    assert sum(g["usage"]["input_tokens"] for g in got) > 65536
+    for req, g in zip(requests, got):
+        _close_answers(g, nat.ask_all(req))
+    nat.close()
