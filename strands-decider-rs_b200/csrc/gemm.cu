@@ -42,14 +42,17 @@ constexpr int kTileBytes = kTileCodes + kTileScales;
 constexpr int kHalfCodes = kTileCodes / 2;  // codes of k-group 0 of every row, then of k-group 1
 constexpr int kACols = kBK / 2;             // TMEM columns of one dequantized k-tile (f16 pairs)
 
-template <int BN>
+// WIDE: two k-tiles per stage at BN 192 (two stages, two dequantization groups; the TMEM A ring keeps
+// its four k-tiles), so the MMA thread waits and commits once per 8 MMAs. Measured on B200: +3% on the
+// gate_up GEMM with its SwiGLU epilogue, -2% on the down projection, so only the SwiGLU GEMM uses it.
+template <int BN, int WIDE = 0>
 struct GemmCfg {
   // k-tiles per stage, stages, dequantization groups (no more than stages), raw ring slots of one
   // stage's packed weights each (deeper for short prompts, whose weights stream from HBM once)
-  static constexpr int KS = BN >= 192 ? 1 : 2;
-  static constexpr int S = BN >= 64 ? 4 : 6;
-  static constexpr int NG = 4;
-  static constexpr int SR = BN >= 192 ? 16 : (BN >= 128 ? 8 : 12);
+  static constexpr int KS = BN >= 192 && !WIDE ? 1 : 2;
+  static constexpr int S = WIDE ? 2 : (BN >= 64 ? 4 : 6);
+  static constexpr int NG = WIDE ? 2 : 4;
+  static constexpr int SR = WIDE ? 8 : (BN >= 192 ? 16 : (BN >= 128 ? 8 : 12));
   static constexpr int kRawSlot = KS * kTileBytes;
   static constexpr int kWarps = 2 + 4 * NG + 4 + 1;
   static constexpr int kThreads = 32 * kWarps;
@@ -79,6 +82,9 @@ struct GemmCfg {
 };
 
 enum Epi { kEpiStore = 0, kEpiSilu = 1, kEpiPartial = 2 };
+// The configuration a kernel instantiation uses.
+template <int BN, int EPI>
+using CfgOf = GemmCfg<BN, (EPI == kEpiSilu && BN >= 192) ? 1 : 0>;
 
 // The SwiGLU of one output: gate and up are each rounded to f16 first, as the reference stores them.
 SD_DEV float swiglu(float gate, float up) {
@@ -115,10 +121,10 @@ struct TileGrid {
 // Every role walks the same sequence: tiles with work, their stages (KS k-tiles each, the last one of a
 // tile possibly fewer) and k-tiles, so stage and k-tile counters agree between roles.
 template <int BN, int EPI>
-__global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
+__global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
     gemm_q4_tc(const __grid_constant__ CUtensorMap act_map, const uint8_t* __restrict__ wt, int M, int N, TileGrid tg,
                __half* __restrict__ y, int ldy, float* __restrict__ ws, int* err) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = CfgOf<BN, EPI>;
   constexpr int KS = Cfg::KS, S = Cfg::S, SR = Cfg::SR, NG = Cfg::NG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -517,7 +523,7 @@ int make_map_3d(CUtensorMap* map, const void* ptr, int x, int y, int z, long lon
 template <int BN, int EPI>
 static cudaError_t launch_bn(const CUtensorMap& map, const QWeight& w, int M, const TileGrid& tg, int num_sms, __half* y,
                              int ldy, float* ws, int* err, cudaStream_t st) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = CfgOf<BN, EPI>;
   auto kern = gemm_q4_tc<BN, EPI>;
   static bool attr_set[kMaxDevices] = {};  // per instantiation and device
   int dev = 0;
@@ -628,11 +634,14 @@ cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half*
 
 template <int BN>
 static cudaError_t preload_bn() {
-  for (auto kern : {gemm_q4_tc<BN, kEpiStore>, gemm_q4_tc<BN, kEpiSilu>, gemm_q4_tc<BN, kEpiPartial>}) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<BN>::kSmem);
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(gemm_q4_tc<BN, kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)CfgOf<BN, kEpiStore>::kSmem)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gemm_q4_tc<BN, kEpiSilu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)CfgOf<BN, kEpiSilu>::kSmem)) != cudaSuccess)
+    return e;
+  return cudaFuncSetAttribute(gemm_q4_tc<BN, kEpiPartial>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)CfgOf<BN, kEpiPartial>::kSmem);
 }
 
 // Loads every GEMM kernel on the current device (and sets its shared-memory size), so that no launch
