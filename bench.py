@@ -194,24 +194,23 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(world, x: float) -> float:
+def _reduce(world, x: float, op: str) -> float:
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    # NCCL reduces device tensors; the CPU (gloo) process groups of the tests reduce host ones
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if dist.get_backend() == "nccl" else "cpu")
+    dist.all_reduce(t, op=getattr(dist.ReduceOp, op))
     return float(t.item())
+
+
+def max_over_ranks(world, x: float) -> float:
+    return _reduce(world, x, "MAX")
 
 
 def sum_over_ranks(world, x: float) -> float:
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return _reduce(world, x, "SUM")
 
 
 def model_path(world, rank):

@@ -244,13 +244,16 @@ size_t sd_gdn_scratch_bytes(int32_t l, int32_t h);
  * device memory while they run, such as a serving process whose GPU memory is all reserved when it
  * starts, or a latency path that cannot take cudaMalloc's implicit device synchronisation. This entry
  * point has no counterpart in the reference. It calls no cudaMalloc, cudaFree or other allocating
- * routine: its per-chunk scratch is one fixed 24 MiB device array inside the library, which every
- * GPU that loads the library holds until the process exits. Limit: ceil(l / 64) * h chunk records
+ * routine: its per-chunk scratch is one fixed 24 MiB device array inside the library. CUDA loads the
+ * library's modules lazily, so a device commits those 24 MiB, and the library looks the array's
+ * address up for it, when the gated-delta module first loads there: at sd_engine_create on that
+ * device, or else at the first sd_gdn or sd_gdn_noalloc call on it. Make one of these happen at
+ * start-up, before the process reserves the rest of its GPU memory and before any stream capture;
+ * the device then holds the array until the process exits. Limit: ceil(l / 64) * h chunk records
  * must fit that array (sd_gdn_noalloc_max_tokens(h) tokens; 1088 for 16 heads); larger calls fail
- * with SD_ERR_INVALID and say why. The first call on a device looks the array's address up for that
- * device (make it before any stream capture). All calls on a device share the array, and each call
- * writes every record it reads, so nothing carries over between calls; two calls whose work
- * overlaps on the GPU (different streams, no ordering between them) race on it. */
+ * with SD_ERR_INVALID and say why. All calls on a device share the array, and each call writes
+ * every record it reads, so nothing carries over between calls; two calls whose work overlaps on
+ * the GPU (different streams, no ordering between them) race on it. */
 int sd_gdn_noalloc(const void* q_dev, const void* k_dev, int32_t qk_stride, const void* v_dev, int32_t v_stride,
                    const void* beta_dev, const void* g_dev, void* state_dev, int32_t load_state, void* o_dev, int32_t l,
                    int32_t h, void* stream);

@@ -942,7 +942,70 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const ChunkRec* __rest
       }
 }
 
-size_t gdn_two_phase_scratch(int l, int h) { return (size_t)((l + CH - 1) / CH) * h * sizeof(ChunkRec); }
+// The fixed scratch array of sd_gdn_noalloc (the two-phase scan's per-chunk records, for callers that
+// cannot allocate). It belongs to this file's module: under CUDA's lazy module loading the module, and
+// with it these 24 MiB, is loaded on a device the first time anything in it is used there, which the
+// engine does at creation (preload_gdn) and a bare caller at its first sd_gdn / sd_gdn_noalloc call.
+constexpr size_t kNoAllocScratchBytes = (size_t)24 << 20;
+static __device__ __align__(256) unsigned char g_gdn_noalloc_scratch[kNoAllocScratchBytes];
+
+// The array's device address on the current device. Host code cannot use the symbol itself (on the
+// host it names a stand-in, not device memory), so the address is looked up once per device, with
+// that device current, and cached.
+static cudaError_t noalloc_scratch(void** out) {
+  static void* addr[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> g(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_gdn_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return cudaSuccess;
+}
+
+// Sets the dynamic shared-memory size of every gated-delta kernel on the current device, once per
+// device. Host threads that drive different streams may reach a device's first launch together, so
+// the flag is taken under a lock.
+static cudaError_t set_gdn_attrs() {
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(gdn_chunk_kernel<32, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(GdnSmem<32>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_chunk_kernel<64, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(GdnSmem<64>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_chunk_kernel<32, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(GdnSmem<32>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_chunk_kernel<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(GdnSmem<64>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem))) !=
+          cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_scan_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(ScanSmem<32>))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gdn_scan_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(ScanSmem<64>))) != cudaSuccess)
+    return e;
+  return cudaSuccess;
+}
+static cudaError_t ensure_gdn_attrs() {
+  static bool done[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> g(mu);
+  if (done[dev]) return cudaSuccess;
+  if ((e = set_gdn_attrs()) == cudaSuccess) done[dev] = true;
+  return e;
+}
+
+size_t gdn_two_phase_scratch(int l, int h) { return (size_t)(((long long)l + CH - 1) / CH) * h * sizeof(ChunkRec); }
 
 // One sequence, f16 q/k/v rows: phase 1 over all (chunk, head), then the scan over (head, slice).
 cudaError_t launch_gdn_two_phase(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
@@ -950,21 +1013,12 @@ cudaError_t launch_gdn_two_phase(const __half* q, const __half* k, int qk_stride
                                  void* scratch, size_t scratch_bytes, cudaStream_t st) {
   if (l <= 0 || h <= 0 || scratch_bytes < gdn_two_phase_scratch(l, h)) return cudaErrorInvalidValue;
   constexpr int DVS = 32;
-  static bool attr[kMaxDevices] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  if (!attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gdn_scan_kernel<DVS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(ScanSmem<DVS>));
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
-  }
-  const int nchunks = (l + CH - 1) / CH;
+  cudaError_t e = ensure_gdn_attrs();
+  if (e != cudaSuccess) return e;
+  const int nchunks = (int)(((long long)l + CH - 1) / CH);
   ChunkRec* rec = reinterpret_cast<ChunkRec*>(scratch);
   gdn_prep_kernel<<<dim3(nchunks, h), 256, sizeof(PrepSmem), st>>>(q, k, qk_stride, v, v_stride, beta, g, l, h, nullptr, rec);
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   gdn_scan_kernel<DVS><<<h * (DK / DVS), 256, sizeof(ScanSmem<DVS>), st>>>(rec, nchunks, l, h, state, load_state ? 1 : 0, o,
                                                                           ScanPacked{});
@@ -1004,15 +1058,8 @@ template <int DVS, typename TIn>
 static cudaError_t launch_chunk(const GdnArgs<TIn>& a, int batch, cudaStream_t st) {
   auto kern = gdn_chunk_kernel<DVS, TIn>;
   const int smem = (int)sizeof(GdnSmem<DVS>);
-  static bool attr[kMaxDevices] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  if (!attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
-  }
+  cudaError_t e = ensure_gdn_attrs();
+  if (e != cudaSuccess) return e;
   dim3 grid(a.h * (DK / DVS), batch);
   kern<<<grid, 256, smem, st>>>(a);
   return cudaGetLastError();
@@ -1035,26 +1082,14 @@ cudaError_t launch_gdn_chunked(const void* q, const void* k, int qk_stride, cons
   return wide ? launch_chunk<64>(a, batch, st) : launch_chunk<32>(a, batch, st);
 }
 
-// Loads the gated-delta kernels on the current device (see preload_gemm).
+// Loads the gated-delta kernels on the current device (see preload_gemm), and with them this file's
+// module, so the fixed scratch of sd_gdn_noalloc is committed and its address known from engine
+// creation on, not at a first call made after the process has reserved its memory.
 cudaError_t preload_gdn() {
-  cudaFuncAttributes a;
-  cudaError_t e;
-  if ((e = cudaFuncSetAttribute(gdn_chunk_kernel<32, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(GdnSmem<32>))) != cudaSuccess ||
-      (e = cudaFuncSetAttribute(gdn_chunk_kernel<64, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(GdnSmem<64>))) != cudaSuccess ||
-      (e = cudaFuncSetAttribute(gdn_chunk_kernel<32, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(GdnSmem<32>))) != cudaSuccess ||
-      (e = cudaFuncSetAttribute(gdn_chunk_kernel<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(GdnSmem<64>))) != cudaSuccess ||
-      (e = cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem))) !=
-          cudaSuccess ||
-      (e = cudaFuncSetAttribute(gdn_scan_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(ScanSmem<32>))) != cudaSuccess ||
-      (e = cudaFuncSetAttribute(gdn_scan_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(ScanSmem<64>))) != cudaSuccess)
-    return e;
-  return cudaFuncGetAttributes(&a, gdn_scan_kernel<32>);
+  cudaError_t e = ensure_gdn_attrs();
+  void* scratch = nullptr;
+  if (e == cudaSuccess) e = noalloc_scratch(&scratch);
+  return e;
 }
 
 // The chunked scan over `nseq` packed sequences of different lengths (sequence b: tokens seq_off[b] ..
@@ -1078,36 +1113,14 @@ cudaError_t launch_gdn_chunked_packed(const __half* q, const __half* k, int qk_s
 }  // namespace sd
 
 // ---------------------------------------------------------------------------------------------
-// The two-phase scan without allocation. Its per-chunk records live in one fixed device array
-// compiled into the library: every GPU that loads the library holds these 24 MiB until the process
-// exits, and every call on a device uses the same array.
+// The two-phase scan without allocation. Its per-chunk records live in the fixed device array above
+// (g_gdn_noalloc_scratch): a device holds these 24 MiB from the moment this file's module loads there
+// (engine creation, or the first gated-delta call) until the process exits, and every call on a
+// device uses the same array.
 // ---------------------------------------------------------------------------------------------
 namespace sd {
 namespace {
-constexpr size_t kNoAllocScratchBytes = (size_t)24 << 20;
 constexpr int kNoAllocRecords = (int)(kNoAllocScratchBytes / sizeof(ChunkRec));
-static __device__ __align__(256) unsigned char g_gdn_noalloc_scratch[kNoAllocScratchBytes];
-
-// The array's device address on the current device. Host code cannot use the symbol itself (on the
-// host it names a stand-in, not device memory), so the address is looked up once per device, with
-// that device current, and cached.
-cudaError_t noalloc_scratch(void** out) {
-  static void* addr[kMaxDevices] = {};
-  static std::mutex mu;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> g(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_gdn_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    addr[dev] = p;
-  }
-  *out = addr[dev];
-  return cudaSuccess;
-}
 }  // namespace
 }  // namespace sd
 
@@ -1124,9 +1137,9 @@ extern "C" int sd_gdn_noalloc(const void* q, const void* k, int32_t qk_stride, c
     sd::set_last_error("sd_gdn_noalloc: bad arguments");
     return SD_ERR_INVALID;
   }
-  const long long records = (long long)((l + 63) / 64) * h;
+  const long long chunks = ((long long)l + 63) / 64, records = chunks * h;
   if (records > sd::kNoAllocRecords) {
-    sd::set_last_error("sd_gdn_noalloc: " + std::to_string(h) + " heads x " + std::to_string((l + 63) / 64) +
+    sd::set_last_error("sd_gdn_noalloc: " + std::to_string(h) + " heads x " + std::to_string(chunks) +
                        " chunks of 64 tokens need " + std::to_string(records) + " chunk records; the fixed scratch holds " +
                        std::to_string(sd::kNoAllocRecords) + " (at most " + std::to_string(sd_gdn_noalloc_max_tokens(h)) +
                        " tokens for " + std::to_string(h) + " heads)");

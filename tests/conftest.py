@@ -25,6 +25,14 @@ def small_model():
 
 
 @pytest.fixture(scope="session")
+def full_model():
+    """The benchmarked model: production dims, 24 layers ([3 gated-delta, 1 attention] x 6), the
+    248320-row int3 embedding; seed 0, as bench.py generates it."""
+    from strands_decider import model
+    return model.ensure_model(os.path.join(MODELS, "full_s0"), seed=0)
+
+
+@pytest.fixture(scope="session")
 def small_model_u8():
     """As small_model, with the embedding's scales stored as 8-bit codes (`src/model.rs:219-236`)."""
     from strands_decider import model
