@@ -232,8 +232,10 @@ int sd_attention_split(const void* q_dev, const void* k_dev, const void* v_dev, 
  * f32, or f16 when in_f16; seq_qk/seq_v: elements between sequences. beta_dev and g_dev (the log decay:
  * the decay is exp(g)) [batch][l][h] f32; state_dev [batch][h][128][128] f32 (read when load_state,
  * always written); o_dev [batch][l][h * 128] f32. algo 0: the chunked scan (64-token chunks, one
- * pass); 1: the token-serial recurrence (f32, batch 1); 2: the two-phase chunked scan (f16, batch 1;
- * needs scratch_dev of sd_gdn_scratch_bytes(l, h) bytes). */
+ * pass; with f16 inputs the fused tcgen05 kernel, which needs 16-byte aligned q/k/v and strides of
+ * multiples of 8 elements); 1: the token-serial recurrence (f32, batch 1); 2: the two-phase chunked
+ * scan (f16, batch 1; needs scratch_dev of sd_gdn_scratch_bytes(l, h) bytes); 3: the single-pass
+ * chunked scan on mma.sync (f16). */
 int sd_gdn(const void* q_dev, const void* k_dev, int32_t qk_stride, const void* v_dev, int32_t v_stride,
            const void* beta_dev, const void* g_dev, void* state_dev, int32_t load_state, void* o_dev, int32_t l,
            int32_t h, int32_t batch, int64_t seq_qk, int64_t seq_v, int32_t in_f16, int32_t algo, void* scratch_dev,

@@ -127,6 +127,14 @@ static void dequant_row(const OrMat* w, int n, float* out, int f16_math) {
  * matmul_tiled (src/kernels.rs:640-709): f16 dequant; each output accumulates vec4 dots block by
  * block in K order.
  * ------------------------------------------------------------------------------------------- */
+/* Perturbation probe (off by default): with it set, every matmul adds its f32 partial sums in the
+ * opposite order (the tiled kernel's K groups from the last; the GEMV's eight split-K lanes from the
+ * last). The result differs from the reference only by f32 summation order; the tests use the
+ * difference to measure how far the model's f16 activations drift under such a change, the floor
+ * below which no implementation that is not bit-identical can agree with the reference. */
+static int g_sum_reversed = 0;
+void or_set_sum_reversed(int on) { g_sum_reversed = on != 0; }
+
 static inline float dot4(const float* a, const float* b) {
   return a[0] * b[0] + a[1] * b[1] + a[2] * b[2] + a[3] * b[3];
 }
@@ -142,7 +150,8 @@ static void matmul_gemv(const float* A, int m, const OrMat* w, uint16_t* Y) {
       for (int r = 0; r < m; r++) {
         const float* a = A + (size_t)r * K;
         float tot = 0.0f;
-        for (int s = 0; s < 8; s++) {
+        for (int s0 = 0; s0 < 8; s0++) {
+          const int s = g_sum_reversed ? 7 - s0 : s0;
           float acc = 0.0f;
           for (int b = s; b < nb; b += 8) {
             const float* ab = a + b * 32;
@@ -175,7 +184,8 @@ static void matmul_tiled(const float* A, int m, const OrMat* w, uint16_t* Y) {
     for (int n = 0; n < N; n++) {
       dequant_row(w, n, wr, 1);
       for (int r = 0; r < m; r++) acc[r] = 0.0f;
-      for (int k4 = 0; k4 < K / 4; k4++) {
+      for (int i4 = 0; i4 < K / 4; i4++) {
+        const int k4 = g_sum_reversed ? K / 4 - 1 - i4 : i4;
         const float* wk = wr + 4 * k4;
         const float* ak = At + (size_t)k4 * m * 4;
         for (int r = 0; r < m; r++) acc[r] += dot4(ak + 4 * r, wk);

@@ -63,6 +63,8 @@ typedef struct OrSnapshot OrSnapshot;
 OrEngine* or_engine_create(const OrModel* m);
 void or_engine_destroy(OrEngine* e);
 void or_set_threads(int n);
+/* Perturbation probe: every matmul adds its f32 partial sums in the opposite order (off by default). */
+void or_set_sum_reversed(int on);
 
 /* Engine::forward (src/engine.rs:529-662): returns 0 or a negative error. hidden: [nrows][d] f32.
  * trace (optional): [n_layers][l][d] f32, the residual stream after each layer (x + y). */

@@ -70,6 +70,7 @@ def lib():
         _lib.or_f16_to_f32.restype = C.c_float
         _lib.or_f16_to_f32.argtypes = [C.c_uint16]
         _lib.or_set_threads.argtypes = [C.c_int]
+        _lib.or_set_sum_reversed.argtypes = [C.c_int]
     return _lib
 
 
@@ -79,6 +80,11 @@ def _p(a: np.ndarray | None):
 
 def set_threads(n: int) -> None:
     lib().or_set_threads(n)
+
+
+def set_sum_reversed(on: bool) -> None:
+    """Perturbation probe: every matmul adds its f32 partial sums in the opposite order."""
+    lib().or_set_sum_reversed(int(on))
 
 
 def decode_scales(src: bytes, n: int, g: int) -> np.ndarray:

@@ -1875,12 +1875,29 @@ int sd_gdn(const void* q, const void* k, int32_t qk_stride, const void* v, int32
            int64_t seq_v, int32_t in_f16, int32_t algo, void* scratch, size_t scratch_bytes, void* stream) {
   const size_t align = in_f16 ? 8 : 16;
   if (!q || !k || !v || !beta || !g || !state || !o || l <= 0 || h <= 0 || batch <= 0 || qk_stride % 4 ||
-      (size_t)q % align || (size_t)k % align || algo < 0 || algo > 2 || (algo == 1 && (in_f16 || batch != 1)) ||
-      (algo == 2 && (!in_f16 || batch != 1 || !scratch || scratch_bytes < sd::gdn_two_phase_scratch(l, h)))) {
+      (size_t)q % align || (size_t)k % align || algo < 0 || algo > 3 || (algo == 1 && (in_f16 || batch != 1)) ||
+      (algo == 2 && (!in_f16 || batch != 1 || !scratch || scratch_bytes < sd::gdn_two_phase_scratch(l, h))) ||
+      (algo == 3 && !in_f16)) {
     set_global_error("sd_gdn: bad arguments");
     return SD_ERR_INVALID;
   }
   cudaStream_t st = (cudaStream_t)stream;
+  if (algo == 0 && in_f16) {
+    // the fused tcgen05 scan: its TMA reads need 16-byte aligned rows and sequences
+    if ((size_t)v % 16 || (size_t)q % 16 || (size_t)k % 16 || qk_stride % 8 || v_stride % 8 || seq_qk % 8 || seq_v % 8 ||
+        (batch > 1 && (seq_qk < (int64_t)l * qk_stride || seq_v < (int64_t)l * v_stride))) {
+      set_global_error("sd_gdn: the tcgen05 scan needs 16-byte aligned q/k/v, strides that are multiples of 8 elements "
+                       "and sequences that do not overlap");
+      return SD_ERR_INVALID;
+    }
+    sd::GdnTcArgs a;
+    a.beta = (const float*)beta, a.g = (const float*)g, a.o = (float*)o, a.h = h, a.l = l;
+    a.state = (float*)state, a.load_state = load_state != 0, a.store_state = 1;
+    return op_result(sd::launch_gdn_tc((const __half*)q, (const __half*)k, qk_stride, (const __half*)v, v_stride,
+                                       batch > 1 ? seq_qk : (int64_t)l * qk_stride, batch > 1 ? seq_v : (int64_t)l * v_stride,
+                                       l, a, batch * h, st),
+                     "sd_gdn");
+  }
   if (algo == 1)
     return op_result(sd::launch_gdn_recurrent((const float*)q, (const float*)k, qk_stride, (const float*)v, v_stride,
                                               (const float*)beta, (const float*)g, (float*)state, load_state != 0, (float*)o,

@@ -1,0 +1,718 @@
+// The gated delta rule (the reference's `Gdn` kernels, src/kernels.rs:257-302) as one fused chunked
+// scan on the 5th-generation tensor cores.
+//
+// Per token and head (src/kernels.rs:282-297): q^ = q rsqrt(|q|^2 + 1e-6) / sqrt(DK),
+// k^ = k rsqrt(|k|^2 + 1e-6), S <- gamma S, delta = beta (v - S^T k^), S += k^ delta^T, o = S^T q^.
+// Chunks of C = 64 tokens from the entry state S (DK x DV, f32), with G_i = sum_{j<=i} g_j and
+// Gamma_i = exp(G_i) (the WY form of the chunk, as gdn.cu states it):
+//   A_ij = beta_i e^{G_i - G_j} k^_i.k^_j (j < i),  T = (I + A)^-1,  T1 = T diag(beta Gamma),  T2 = T diag(beta)
+//   W = T1 K^,  U = T2 V,  delta = U - W S,  P_ij = e^{G_i - G_j} q^_i.k^_j (j <= i)
+//   O = Gamma Q^ S + P delta,   S' = Gamma_C S + K^T diag(e^{G_C - G_i}) delta
+//
+// One CTA walks one (sequence, head) over all 128 value columns. The state S is the f32 accumulator
+// of its own update in tensor memory. The chunk's products are tcgen05 MMAs of M = 128 that stack two
+// 64-row operands: [K^; Q^] K^T gives A and P at once, [Gamma Q^; -W] S gives Gamma Q^ S and -W S
+// (accumulated onto [0; U], so that the second half is delta), and [P; *] delta adds P delta to the
+// first half. The state-independent work of chunk c + 1 (normalisation, A and P, the triangular
+// inverse, W and U) runs beside the state chain of chunk c:
+//   warp 0      TMA: the raw k and q rows of each chunk (into the chunk's tile, normalised in place)
+//               and its v rows, two chunks ahead at most;
+//   warp 1      one thread issues the state chain's MMAs: [Gamma Q^; -W] S, K^T Ds, P delta;
+//   warps 2-5   the chain: S out of tensor memory (its f16 copy, the operand of the next chunk, and
+//               Gamma_C S back), delta (f16, and decayed as Ds), O rows to global memory;
+//   warps 6-9   the chunk preparation: q^, k^, the gates and G, A and P from [K^; Q^] K^T, the
+//               inverse (f32; 16 x 16 diagonal blocks by substitution, the rest on tf32 mma.sync),
+//               T1 and T2 (f16), W out of tensor memory; their first thread issues [K^; Q^] K^T,
+//               W = [T1; *] K^ and U = [0; T2] V.
+// Rounding points are those of the two-phase scan (gdn.cu): f16 q^, k^, T1, T2, W, P, delta, Ds and
+// the state operand; f32 accumulation, U and the state.
+//
+// Every wait is bounded (2 s, common.cuh): a wait that runs out records an error code and the CTA
+// winds down (each MMA issuer waits for its own MMAs, the TMA thread for its copies) without hanging.
+#include <mutex>
+
+#include "common.cuh"
+#include "sd_internal.h"
+
+namespace sd {
+
+namespace {
+constexpr int CH = 64, DK = 128;
+constexpr int kThreads = 320;
+constexpr int kBox = 192 * 128;                       // one 64-column half of a chunk tile: K^ rows 0-63, Q^ 64-127, W 128-191
+constexpr int kTile = 2 * kBox;                       // 48 KB
+constexpr int kOffKQW = 0;                            // [2] chunk tiles
+constexpr int kOffV = kOffKQW + 2 * kTile;            // V: 64 tokens x 128 values, two 8 KB halves
+constexpr int kOffS16 = kOffV + 16384;                // S (f16): 128 keys x 128 values, two 16 KB halves
+constexpr int kOffT1 = kOffS16 + 32768;               // 8 KB tiles, in this order: T1 | P1 | P0 | Z | T2
+constexpr int kOffP1 = kOffT1 + 8192;
+constexpr int kOffP0 = kOffP1 + 8192;
+constexpr int kOffZ = kOffP0 + 8192;
+constexpr int kOffT2 = kOffZ + 8192;
+constexpr int LA = CH + 1;                            // row stride (floats) of the f32 64 x 64 tiles
+constexpr int kOffA = kOffT2 + 8192;                  // A (f32)
+constexpr int kOffX = kOffA + CH * LA * 4;            // T = (I + A)^-1 (f32)
+constexpr int kOffY = kOffX + CH * LA * 4;            // 3 x 16 x 17 floats of the inverse's scratch
+constexpr int kOffSmall = kOffY + 3 * 16 * 17 * 4;    // beta[2][64], G[2][64], g[64]
+constexpr int kOffBar = kOffSmall + 5 * CH * 4;
+enum {
+  B_KQ_FULL = 0,     // [2] the chunk's k and q rows landed (TMA bytes)
+  B_KQ_EMPTY = 2,    // [2] the chain's MMAs of the chunk completed: its tile is free
+  B_V_FULL = 4,      // [2] the chunk's v rows landed
+  B_U_DONE = 6,      // [2] U = [0; T2] V completed (V, T1 and T2 free; the chain may accumulate)
+  B_DAP_FULL = 8,    // [2] [K^; Q^] K^T in tensor memory
+  B_W_FULL = 10,     // [2] W in tensor memory
+  B_WQ_READY = 12,   // [2] -W, Gamma Q^ and P written (shared memory), W read out
+  B_G_READY = 14,    // [2] the chunk's G written
+  B_S16_READY = 16,  // [2] the entry state's f16 copy written and Gamma_C S back in tensor memory
+  B_X_FULL = 18,     // [2] [Gamma Q^; -W] S accumulated
+  B_D_READY = 20,    // [2] delta and Ds written
+  B_S_FULL = 22,     // [2] the state update completed
+  B_O_FULL = 24,     // [2] P delta accumulated (O complete); P and delta free
+  B_O_READ = 26,     // [2] O read out of tensor memory
+  B_END_PREP = 28,   // every MMA of the preparation completed (teardown)
+  B_END_CHAIN = 29,  // every MMA of the chain completed (teardown)
+  kBars = 30
+};
+constexpr int kSmem = kOffBar + kBars * 8 + 16 + 1024;
+static_assert(kSmem <= 232448, "shared memory");
+constexpr uint32_t kColS = 0, kColX = 128, kColDAP = 384, kTmemCols = 512;
+constexpr uint32_t kIdS = idesc_f16(128, 128) | (1u << 15) | (1u << 16);  // both operands MN-major
+constexpr uint32_t kIdB = idesc_f16_bmn(128, 128);                        // B MN-major
+constexpr uint32_t kIdAP = idesc_f16(128, 64);                            // both K-major
+constexpr int kPrepBar = 1;                                               // named barrier of the preparation warps
+
+__device__ int g_gdn_tc_err;  // error slot of calls without one
+
+// Byte offset of 16-byte piece `c` of row `r` in a tile stored with the 128-byte swizzle (rows of
+// 128 bytes; the tile starts on a 1024-byte boundary).
+SD_DEV uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+SD_DEV void prep_sync() { asm volatile("bar.sync %0, 128;" ::"n"(kPrepBar) : "memory"); }
+
+SD_DEV uint32_t pack_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+SD_DEV uint32_t tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+SD_DEV void mma1688_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// X = (I + A)^-1 for the strictly lower triangular 64 x 64 A (rows LA floats apart), by the four
+// preparation warps (w = 0..3): the 16 x 16 diagonal blocks by forward substitution (warp w, lane =
+// column), then the blocks below the diagonal level by level, X_ij = -X_ii sum_{m=j}^{i-1} A_im X_mj for
+// i = j + dl (warp w < 4 - dl takes block (w + dl, w)), on the tensor cores with tf32 operands and f32
+// accumulation. Blocks above the diagonal are not written (never read).
+SD_DEV void tri_inverse(const float* __restrict__ a, float* __restrict__ x, float* __restrict__ y, int w, int lane) {
+  if (lane < 16) {
+    const int o = w * 16, c = lane;
+    float xc[16];
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+      float v0 = r == c ? 1.0f : 0.0f, v1 = 0.0f;
+#pragma unroll
+      for (int j = 0; j < r; j++)
+        if (j >= c) {
+          if (j & 1) v1 -= a[(o + r) * LA + o + j] * xc[j];
+          else v0 -= a[(o + r) * LA + o + j] * xc[j];
+        }
+      xc[r] = r >= c ? v0 + v1 : 0.0f;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; r++) x[(o + r) * LA + o + c] = xc[r];
+  }
+  prep_sync();
+  const int g = lane >> 2, tq = lane & 3;
+#pragma unroll 1
+  for (int dl = 1; dl < 4; dl++) {
+    if (w < 4 - dl) {
+      const int bj = w, bi = bj + dl;
+      float acc[2][4] = {};
+      for (int m = bj; m < bi; m++)
+#pragma unroll
+        for (int kk = 0; kk < 16; kk += 8) {
+          const float* ar = a + (bi * 16 + g) * LA + m * 16 + kk;
+          const uint32_t a0 = tf32(ar[tq]), a1 = tf32(ar[8 * LA + tq]), a2 = tf32(ar[tq + 4]), a3 = tf32(ar[8 * LA + tq + 4]);
+#pragma unroll
+          for (int nt = 0; nt < 2; nt++) {
+            const float* xr = x + (m * 16 + kk + tq) * LA + bj * 16 + nt * 8 + g;
+            mma1688_tf32(acc[nt], a0, a1, a2, a3, tf32(xr[0]), tf32(xr[4 * LA]));
+          }
+        }
+      float* yw = y + w * 272;  // this block's sum, 16 x 16 (row stride 17)
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++) {
+        yw[g * 17 + nt * 8 + 2 * tq] = acc[nt][0];
+        yw[g * 17 + nt * 8 + 2 * tq + 1] = acc[nt][1];
+        yw[(g + 8) * 17 + nt * 8 + 2 * tq] = acc[nt][2];
+        yw[(g + 8) * 17 + nt * 8 + 2 * tq + 1] = acc[nt][3];
+      }
+      __syncwarp();
+      float z[2][4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 16; kk += 8) {
+        const float* xr = x + (bi * 16 + g) * LA + bi * 16 + kk;
+        const uint32_t a0 = tf32(xr[tq]), a1 = tf32(xr[8 * LA + tq]), a2 = tf32(xr[tq + 4]), a3 = tf32(xr[8 * LA + tq + 4]);
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+          mma1688_tf32(z[nt], a0, a1, a2, a3, tf32(yw[(kk + tq) * 17 + nt * 8 + g]), tf32(yw[(kk + tq + 4) * 17 + nt * 8 + g]));
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++) {
+        float* xo = x + (bi * 16 + g) * LA + bj * 16 + nt * 8 + 2 * tq;
+        xo[0] = -z[nt][0];
+        xo[1] = -z[nt][1];
+        xo[8 * LA] = -z[nt][2];
+        xo[8 * LA + 1] = -z[nt][3];
+      }
+    }
+    prep_sync();
+  }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gdn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                  const __grid_constant__ CUtensorMap vmap, const GdnTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kBars);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* sbeta = reinterpret_cast<float*>(base + kOffSmall);  // [2][64]
+  float* sG = sbeta + 2 * CH;                                  // [2][64]
+  float* sg = sG + 2 * CH;                                     // [64]
+  int* err = a.err ? a.err : &g_gdn_tc_err;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = a.h;
+
+  // this CTA's walk: sequence b (its tokens tok0 .. tok0 + L - 1 of the gates and outputs; of the
+  // q/k/v maps rows y0 .. in slab z), head hd
+  const int hd = blockIdx.x % H;
+  int b, L, z;
+  long long tok0, y0;
+  const float* sin;
+  float* sout;
+  const long long hoff = (long long)hd * DK * DK;
+  if (a.seq_off) {
+    b = a.order ? a.order[blockIdx.x / H] : blockIdx.x / H;
+    tok0 = a.seq_off[b];
+    L = a.seq_len[b];
+    z = 0;
+    y0 = tok0;
+    sin = a.s_in && a.s_in[b] ? a.s_in[b] + hoff : nullptr;
+    sout = a.s_out && a.s_out[b] ? a.s_out[b] + hoff : nullptr;
+  } else {
+    b = blockIdx.x / H;
+    L = a.l;
+    tok0 = (long long)b * a.l;
+    z = b;
+    y0 = 0;
+    const long long sb = (long long)H * DK * DK;
+    sin = a.load_state ? a.state + b * sb + hoff : nullptr;
+    sout = a.store_state ? a.state + b * sb + hoff : nullptr;
+  }
+  const int nch = (L + CH - 1) / CH;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kBars; i++) {
+      const bool four = (i >= B_S16_READY && i < B_S16_READY + 2) || (i >= B_D_READY && i < B_D_READY + 2) ||
+                        (i >= B_O_READ && i < B_O_READ + 2);
+      mbar_init(&bar[i], four ? 4 : 1);
+    }
+    *abort = 0;
+    fence_mbar_init();
+  }
+  // the zero tile (rows 64-127 of U's [0; T2] operand)
+  for (int i = threadIdx.x; i < 8192 / 16; i += kThreads) reinterpret_cast<uint4*>(base + kOffZ)[i] = make_uint4(0, 0, 0, 0);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (nch == 0) {
+    // nothing to walk: the final state is the initial one
+  } else if (warp == 0) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      prefetch_tmap(&qmap);
+      prefetch_tmap(&kmap);
+      prefetch_tmap(&vmap);
+      bool ok = true;
+      int nkq = 0, nv = 0;
+      for (int c = 0; c < nch && ok; c++) {
+        const int s = c & 1;
+        if (c >= 2 && !(ok = mbar_wait(&bar[B_KQ_EMPTY + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty))) break;
+        uint8_t* t = base + kOffKQW + s * kTile;
+        const int y = (int)(y0 + (long long)c * CH), x = hd * DK;
+        mbar_arrive_expect_tx(&bar[B_KQ_FULL + s], 4 * 8192);
+        for (int hb = 0; hb < 2; hb++) {
+          tma_load_3d(t + hb * kBox, &kmap, &bar[B_KQ_FULL + s], x + hb * 64, y, z);
+          tma_load_3d(t + hb * kBox + 64 * 128, &qmap, &bar[B_KQ_FULL + s], x + hb * 64, y, z);
+        }
+        nkq++;
+        if (c >= 1 && !(ok = mbar_wait(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty))) break;
+        mbar_arrive_expect_tx(&bar[B_V_FULL + s], 2 * 8192);
+        for (int hb = 0; hb < 2; hb++) tma_load_3d(base + kOffV + hb * 8192, &vmap, &bar[B_V_FULL + s], x + hb * 64, y, z);
+        nv++;
+      }
+      // no copy may land after the CTA has left: wait (bounded) for the last ones issued
+      for (int c = max(0, nkq - 2); c < nkq; c++) mbar_drain(&bar[B_KQ_FULL + (c & 1)], (c >> 1) & 1);
+      if (nv > 0) mbar_drain(&bar[B_V_FULL + ((nv - 1) & 1)], ((nv - 1) >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- the chain's MMAs
+    if (lane == 0) {
+      bool ok = true;
+      for (int c = 0; c < nch && ok; c++) {
+        const int s = c & 1;
+        const uint32_t ph = (c >> 1) & 1;
+        uint8_t* t = base + kOffKQW + s * kTile;
+        const uint32_t dx = tmem + kColX + s * 128;
+        if (!(ok = mbar_wait(&bar[B_WQ_READY + s], ph, abort, err, kErrTimeoutFull) &&
+                   mbar_wait(&bar[B_U_DONE + s], ph, abort, err, kErrTimeoutFull) &&
+                   mbar_wait(&bar[B_S16_READY + s], ph, abort, err, kErrTimeoutFull)))
+          break;
+        tc_fence_after();
+        {  // [Gamma Q^; -W] S onto [0; U]: rows 0-63 Gamma Q^ S, rows 64-127 delta
+          const uint64_t ad = sw128_desc(t + 64 * 128), bd = sw128_mn_desc(base + kOffS16, 16384);
+#pragma unroll
+          for (int ks = 0; ks < 8; ks++)
+            tc_mma_f16(dx, ad + (uint64_t)((ks >> 2) * (kBox >> 4) + 2 * (ks & 3)), bd + (uint64_t)(128 * ks), kIdB, 1);
+        }
+        tc_commit(&bar[B_X_FULL + s]);
+        if (!(ok = mbar_wait(&bar[B_D_READY + s], ph, abort, err, kErrTimeoutFull))) break;
+        tc_fence_after();
+        {  // S += K^T Ds
+          const uint64_t ad = sw128_mn_desc(t, kBox), bd = sw128_mn_desc(t + 128 * 128, kBox);
+#pragma unroll
+          for (int ks = 0; ks < 4; ks++) tc_mma_f16(tmem + kColS, ad + (uint64_t)(128 * ks), bd + (uint64_t)(128 * ks), kIdS, 1);
+        }
+        tc_commit(&bar[B_S_FULL + s]);
+        {  // O = Gamma Q^ S + P delta (rows 0-63; the operand's rows 64-127 are whatever follows P)
+          const uint64_t ad = sw128_desc(base + (s ? kOffP1 : kOffP0)), bd = sw128_mn_desc(t + 64 * 128, kBox);
+#pragma unroll
+          for (int ks = 0; ks < 4; ks++) tc_mma_f16(dx, ad + (uint64_t)(2 * ks), bd + (uint64_t)(128 * ks), kIdB, 1);
+        }
+        tc_commit(&bar[B_O_FULL + s]);
+        tc_commit(&bar[B_KQ_EMPTY + s]);
+      }
+      tc_commit(&bar[B_END_CHAIN]);
+      mbar_drain(&bar[B_END_CHAIN], 0);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- the chain
+    const int q4 = warp & 3;                       // TMEM lanes 32 q4 .. + 31
+    const int r = q4 * 32 + lane;                  // S: key row r; D_X: row r
+    const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+    // the entry state into tensor memory (zeros without one)
+    for (int cb = 0; cb < 4; cb++) {
+      uint32_t v[32];
+      if (sin) {
+        const float4* src = reinterpret_cast<const float4*>(sin + (size_t)r * DK + cb * 32);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float4 f = src[i];
+          v[4 * i] = __float_as_uint(f.x), v[4 * i + 1] = __float_as_uint(f.y);
+          v[4 * i + 2] = __float_as_uint(f.z), v[4 * i + 3] = __float_as_uint(f.w);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = 0u;
+      }
+      tmem_st32(tmem + lanes + kColS + cb * 32, v);
+    }
+    tc_wait_st();
+    bool ok = true;
+    auto read_o = [&](int c) {  // O rows (D_X rows 0-63) of chunk c to global memory, then release D_X
+      const int s = c & 1;
+      if (!(ok = mbar_wait_warp(&bar[B_O_FULL + s], (c >> 1) & 1, abort, err, kErrTimeoutAccum))) return;
+      tc_fence_after();
+      const int n = min(CH, L - c * CH);
+      if (q4 < 2) {
+        // tcgen05.ld and wait::ld are warp-collective (.sync.aligned): every lane of the warp executes
+        // the same loads, and only the stores are limited to the chunk's rows
+        float* dst = a.o + (size_t)(tok0 + c * CH + r) * H * DK + hd * DK;
+        for (int cb = 0; cb < 4; cb++) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lanes + kColX + s * 128 + cb * 32, v);
+          tc_wait_ld();
+          if (r < n) {
+            float4* d4 = reinterpret_cast<float4*>(dst + cb * 32);
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+              d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]), __uint_as_float(v[4 * i + 2]),
+                                  __uint_as_float(v[4 * i + 3]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_O_READ + s]);
+    };
+    for (int c = 0; c < nch && ok; c++) {
+      const int s = c & 1;
+      const uint32_t ph = (c >> 1) & 1;
+      uint8_t* t = base + kOffKQW + s * kTile;
+      // (1) the entry state S_{c-1}: its f16 copy (the operand of [Gamma Q^; -W] S), Gamma_C S back
+      if (c >= 1 && !(ok = mbar_wait_warp(&bar[B_S_FULL + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutAccum)))
+        break;
+      if (!(ok = mbar_wait_warp(&bar[B_G_READY + s], ph, abort, err, kErrTimeoutFull))) break;
+      tc_fence_after();
+      const float gc = __expf(sG[s * CH + CH - 1]);
+      for (int cb = 0; cb < 4; cb++) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lanes + kColS + cb * 32, v);
+        tc_wait_ld();
+        uint8_t* dst = base + kOffS16 + (cb >> 1) * 16384;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          uint4 u;
+          u.x = pack_h2(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1]));
+          u.y = pack_h2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
+          u.z = pack_h2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
+          u.w = pack_h2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
+          *reinterpret_cast<uint4*>(dst + swz(r, (cb & 1) * 4 + j)) = u;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * gc);
+        tmem_st32(tmem + lanes + kColS + cb * 32, v);
+      }
+      tc_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_S16_READY + s]);
+      // (2) O of the previous chunk (its MMA was issued right after the state update just waited for)
+      if (c >= 1) {
+        read_o(c - 1);
+        if (!ok) break;
+      }
+      // (3) delta = D_X rows 64-127: delta (f16, over Gamma Q^) and Ds = delta e^{G_C - G_i} (over -W)
+      if (!(ok = mbar_wait_warp(&bar[B_X_FULL + s], ph, abort, err, kErrTimeoutAccum))) break;
+      tc_fence_after();
+      if (q4 >= 2) {
+        const int i = r - 64;
+        const float sc = __expf(sG[s * CH + CH - 1] - sG[s * CH + i]);
+        for (int cb = 0; cb < 4; cb++) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lanes + kColX + s * 128 + cb * 32, v);
+          tc_wait_ld();
+          uint8_t* box = t + (cb >> 1) * kBox;
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            uint4 u, w;
+            u.x = pack_h2(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1]));
+            u.y = pack_h2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
+            u.z = pack_h2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
+            u.w = pack_h2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
+            w.x = pack_h2(__uint_as_float(v[8 * j]) * sc, __uint_as_float(v[8 * j + 1]) * sc);
+            w.y = pack_h2(__uint_as_float(v[8 * j + 2]) * sc, __uint_as_float(v[8 * j + 3]) * sc);
+            w.z = pack_h2(__uint_as_float(v[8 * j + 4]) * sc, __uint_as_float(v[8 * j + 5]) * sc);
+            w.w = pack_h2(__uint_as_float(v[8 * j + 6]) * sc, __uint_as_float(v[8 * j + 7]) * sc);
+            *reinterpret_cast<uint4*>(box + swz(64 + i, (cb & 1) * 4 + j)) = u;
+            *reinterpret_cast<uint4*>(box + swz(128 + i, (cb & 1) * 4 + j)) = w;
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_D_READY + s]);
+    }
+    if (ok) read_o(nch - 1);
+    // the final state
+    if (ok && sout) {
+      const int c = nch - 1;
+      if ((ok = mbar_wait_warp(&bar[B_S_FULL + (c & 1)], (c >> 1) & 1, abort, err, kErrTimeoutAccum))) {
+        tc_fence_after();
+        for (int cb = 0; cb < 4; cb++) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lanes + kColS + cb * 32, v);
+          tc_wait_ld();
+          float4* d4 = reinterpret_cast<float4*>(sout + (size_t)r * DK + cb * 32);
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]), __uint_as_float(v[4 * i + 2]),
+                                __uint_as_float(v[4 * i + 3]));
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- the chunk preparation
+    const int pw = warp - 6;                  // 0..3
+    const int pt = threadIdx.x - 6 * 32;      // 0..127
+    const int q4 = warp & 3;                  // TMEM lanes 32 q4 .. + 31: warps 6, 7 -> Q rows; 8, 9 -> K rows
+    const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+    float* sa = reinterpret_cast<float*>(base + kOffA);
+    float* sx = reinterpret_cast<float*>(base + kOffX);
+    float* sy = reinterpret_cast<float*>(base + kOffY);
+    const float qscale = rsqrtf((float)DK);
+    bool ok = true;
+    // the gates of chunk c (beta for threads 0-63, g for 64-127), loaded one chunk ahead
+    auto gate = [&](int c) -> float {
+      const int i = pt & 63;
+      if (c >= nch || c * CH + i >= L) return 0.0f;
+      const long long t = tok0 + c * CH + i;
+      return pt < 64 ? a.beta[t * H + hd] : a.g[t * H + hd];
+    };
+    float gnext = gate(0);
+    for (int c = 0; c < nch; c++) {
+      const int s = c & 1;
+      const uint32_t ph = (c >> 1) & 1;
+      uint8_t* t = base + kOffKQW + s * kTile;
+      const uint32_t dx = tmem + kColX + s * 128;
+      const float gcur = gnext;
+      gnext = gate(c + 1);
+      // (1) the chunk's k and q rows; the gates and G (G[s] and beta[s] are free: the chain's last use
+      // of them, chunk c - 2, came before its MMAs released the tile this chunk was loaded into)
+      if (ok) ok = mbar_wait_warp(&bar[B_KQ_FULL + s], ph, abort, err, kErrTimeoutFull);
+      if (pt < 64) sbeta[s * CH + pt] = gcur;
+      else sg[pt - 64] = gcur;
+      prep_sync();
+      if (pw == 0) {
+        const float x0 = sg[2 * lane], x1 = sg[2 * lane + 1];
+        float sum = x0 + x1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float u = __shfl_up_sync(0xffffffffu, sum, o);
+          if (lane >= o) sum += u;
+        }
+        const float before = sum - (x0 + x1);
+        sG[s * CH + 2 * lane] = before + x0;
+        sG[s * CH + 2 * lane + 1] = sum;
+      }
+      // (2) q^, k^ in place (rows 0-63 K, 64-127 Q; lane l: 4 values of one 64-column half)
+      if (ok) {
+        const int hb = lane >> 4, pc = (lane & 15) >> 1, hh = lane & 1;
+#pragma unroll 1
+        for (int r0 = pw; r0 < 128; r0 += 32) {
+          uint2 raw[8];
+#pragma unroll
+          for (int u = 0; u < 8; u++)
+            raw[u] = *reinterpret_cast<const uint2*>(t + hb * kBox + swz(r0 + 4 * u, pc) + hh * 8);
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            const int row = r0 + 4 * u;
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&raw[u].x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&raw[u].y));
+            const float ss = warp_sum(f0.x * f0.x + f0.y * f0.y + f1.x * f1.x + f1.y * f1.y);
+            const float sc = row < 64 ? rsqrtf(ss + 1e-6f) : rsqrtf(ss + 1e-6f) * qscale;
+            uint2 o;
+            o.x = pack_h2(f0.x * sc, f0.y * sc);
+            o.y = pack_h2(f1.x * sc, f1.y * sc);
+            *reinterpret_cast<uint2*>(t + hb * kBox + swz(row, pc) + hh * 8) = o;
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      prep_sync();
+      if (pt == 0) {
+        mbar_arrive(&bar[B_G_READY + s]);
+        if (ok) {  // [K^; Q^] K^T: rows 0-63 K^ K^T, rows 64-127 Q^ K^T
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(t);
+#pragma unroll
+          for (int ks = 0; ks < 8; ks++) {
+            const uint64_t o = (uint64_t)((ks >> 2) * (kBox >> 4) + 2 * (ks & 3));
+            tc_mma_f16(tmem + kColDAP, ad + o, ad + o, kIdAP, ks > 0);
+          }
+          tc_commit(&bar[B_DAP_FULL + s]);
+        }
+      }
+      // (3) A (K rows) and P (Q rows) from the products; Gamma Q^ over Q^
+      if (ok) ok = mbar_wait_warp(&bar[B_DAP_FULL + s], ph, abort, err, kErrTimeoutAccum);
+      if (ok && q4 >= 2 && c >= 2)  // P[s] is free once the chain's P delta of chunk c - 2 has completed
+        ok = mbar_wait_warp(&bar[B_O_FULL + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty);
+      if (ok) {
+        tc_fence_after();
+        uint32_t v[64];
+        tmem_ld32(tmem + lanes + kColDAP, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tmem + lanes + kColDAP + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tc_wait_ld();
+        const float* G = sG + s * CH;
+        if (q4 < 2) {  // K row i
+          const int i = q4 * 32 + lane;
+          const float gi = G[i], bi = sbeta[s * CH + i];
+#pragma unroll
+          for (int j = 0; j < CH; j++) sa[i * LA + j] = j < i ? bi * __expf(gi - G[j]) * __uint_as_float(v[j]) : 0.0f;
+        } else {  // Q row i: P row i (f16), then Gamma_i q^_i in place
+          const int i = (q4 - 2) * 32 + lane;
+          const float gi = G[i];
+          uint8_t* pt_ = base + (s ? kOffP1 : kOffP0);
+#pragma unroll
+          for (int j8 = 0; j8 < 8; j8++) {
+            float p[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+              const int j = j8 * 8 + e;
+              p[e] = j <= i ? __expf(gi - G[j]) * __uint_as_float(v[j]) : 0.0f;
+            }
+            *reinterpret_cast<uint4*>(pt_ + swz(i, j8)) =
+                make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
+          }
+          const float ga = __expf(gi);
+#pragma unroll
+          for (int hb = 0; hb < 2; hb++)
+#pragma unroll
+            for (int j8 = 0; j8 < 8; j8++) {
+              uint4* qp = reinterpret_cast<uint4*>(t + hb * kBox + swz(64 + i, j8));
+              uint4 u = *qp;
+              uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+              for (int e = 0; e < 4; e++) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+                w[e] = pack_h2(f.x * ga, f.y * ga);
+              }
+              *qp = u;
+            }
+        }
+      }
+      tc_fence_before();
+      prep_sync();
+      // (4) T = (I + A)^-1
+      tri_inverse(sa, sx, sy, pw, lane);
+      // (5) T1 = T diag(beta Gamma), T2 = T diag(beta) (f16), once U of chunk c - 1 has read T2 (and W
+      // of chunk c - 1, issued before it, T1)
+      if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
+      if (ok) {
+        const int i = pt >> 1, j0 = (pt & 1) * 32;
+        const float* G = sG + s * CH;
+        const float* be = sbeta + s * CH;
+#pragma unroll
+        for (int j8 = 0; j8 < 4; j8++) {
+          float t1[8], t2[8];
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            const int j = j0 + j8 * 8 + e;
+            const float tv = j <= i ? sx[i * LA + j] : 0.0f;
+            t2[e] = tv * be[j];
+            t1[e] = t2[e] * __expf(G[j]);
+          }
+          const int pc = (j0 >> 3) + j8;
+          *reinterpret_cast<uint4*>(base + kOffT1 + swz(i, pc)) =
+              make_uint4(pack_h2(t1[0], t1[1]), pack_h2(t1[2], t1[3]), pack_h2(t1[4], t1[5]), pack_h2(t1[6], t1[7]));
+          *reinterpret_cast<uint4*>(base + kOffT2 + swz(i, pc)) =
+              make_uint4(pack_h2(t2[0], t2[1]), pack_h2(t2[2], t2[3]), pack_h2(t2[4], t2[5]), pack_h2(t2[6], t2[7]));
+        }
+      }
+      fence_proxy_async_smem();
+      prep_sync();
+      if (pt == 0 && ok) {  // W = [T1; *] K^ into D_X[s], once the chain has read chunk c - 2's O out of it
+        if (c >= 2) ok = mbar_wait(&bar[B_O_READ + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty);
+        if (ok) {
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(base + kOffT1), bd = sw128_mn_desc(t, kBox);
+#pragma unroll
+          for (int ks = 0; ks < 4; ks++) tc_mma_f16(dx, ad + (uint64_t)(2 * ks), bd + (uint64_t)(128 * ks), kIdB, ks > 0);
+          tc_commit(&bar[B_W_FULL + s]);
+        }
+      }
+      // (6) -W (D_X rows 0-63) over rows 128-191 of the tile
+      if (ok && q4 < 2) {
+        ok = mbar_wait_warp(&bar[B_W_FULL + s], ph, abort, err, kErrTimeoutAccum);
+        if (ok) {
+          tc_fence_after();
+          const int i = q4 * 32 + lane;
+          for (int cb = 0; cb < 4; cb++) {
+            uint32_t v[32];
+            tmem_ld32(dx + lanes + cb * 32, v);
+            tc_wait_ld();
+            uint8_t* box = t + (cb >> 1) * kBox;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+              *reinterpret_cast<uint4*>(box + swz(128 + i, (cb & 1) * 4 + j)) =
+                  make_uint4(pack_h2(-__uint_as_float(v[8 * j]), -__uint_as_float(v[8 * j + 1])),
+                             pack_h2(-__uint_as_float(v[8 * j + 2]), -__uint_as_float(v[8 * j + 3])),
+                             pack_h2(-__uint_as_float(v[8 * j + 4]), -__uint_as_float(v[8 * j + 5])),
+                             pack_h2(-__uint_as_float(v[8 * j + 6]), -__uint_as_float(v[8 * j + 7])));
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      // every preparation warp takes the same path through the barriers; a warp that gave up tells the others
+      if (!__all_sync(0xffffffffu, ok)) *abort = 1;
+      prep_sync();
+      ok = ok && !*abort;
+      if (pt == 0 && ok) {  // U = [0; T2] V into D_X[s] (rows 0-63 zero: the start of Gamma Q^ S)
+        mbar_arrive(&bar[B_WQ_READY + s]);
+        ok = mbar_wait(&bar[B_V_FULL + s], ph, abort, err, kErrTimeoutFull);
+        if (ok) {
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(base + kOffZ), bd = sw128_mn_desc(base + kOffV, 8192);
+#pragma unroll
+          for (int ks = 0; ks < 4; ks++) tc_mma_f16(dx, ad + (uint64_t)(2 * ks), bd + (uint64_t)(128 * ks), kIdB, ks > 0);
+          tc_commit(&bar[B_U_DONE + s]);
+        }
+      }
+      if (!__all_sync(0xffffffffu, ok)) *abort = 1;
+      prep_sync();
+      if (*abort) ok = false;
+    }
+    if (pt == 0) {
+      tc_commit(&bar[B_END_PREP]);
+      mbar_drain(&bar[B_END_PREP], 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  // the walk of an empty sequence: the final state is the initial one
+  if (nch == 0 && sout && warp >= 2 && warp < 6) {
+    const int r = (warp & 3) * 32 + lane;
+    for (int cv = 0; cv < DK; cv++) sout[(size_t)r * DK + cv] = sin ? sin[(size_t)r * DK + cv] : 0.0f;
+  }
+}
+
+cudaError_t preload_gdn_tc() {
+  return cudaFuncSetAttribute(gdn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+}
+
+cudaError_t launch_gdn_tc(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride, long long seq_qk,
+                          long long seq_v, int rows, const GdnTcArgs& a, int walks, cudaStream_t st) {
+  if (walks <= 0 || a.h <= 0 || rows <= 0 || qk_stride % 8 || v_stride % 8 || seq_qk % 8 || seq_v % 8 ||
+      ((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16 || (!a.seq_off && (a.l <= 0 || walks % a.h)))
+    return cudaErrorInvalidValue;
+  static bool attr[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (!attr[dev]) {
+      if ((e = preload_gdn_tc()) != cudaSuccess) return e;
+      attr[dev] = true;
+    }
+  }
+  const int zdim = a.seq_off ? 1 : walks / a.h;
+  CUtensorMap qm, km, vm;
+  if (make_map_3d(&qm, q, a.h * DK, rows, zdim, qk_stride, a.seq_off ? (long long)rows * qk_stride : seq_qk, CH) != 0 ||
+      make_map_3d(&km, k, a.h * DK, rows, zdim, qk_stride, a.seq_off ? (long long)rows * qk_stride : seq_qk, CH) != 0 ||
+      make_map_3d(&vm, v, a.h * DK, rows, zdim, v_stride, a.seq_off ? (long long)rows * v_stride : seq_v, CH) != 0)
+    return cudaErrorInvalidValue;
+  gdn_tc_kernel<<<walks, kThreads, kSmem, st>>>(qm, km, vm, a);
+  return cudaGetLastError();
+}
+
+}  // namespace sd

@@ -106,6 +106,27 @@ size_t gdn_two_phase_scratch(int l, int h);
 cudaError_t launch_gdn_two_phase(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride,
                                  const float* beta, const float* g, float* state, bool load_state, float* o, int l, int h,
                                  void* scratch, size_t scratch_bytes, cudaStream_t st);
+// gdn_tc.cu: the fused chunked scan on tcgen05 (f16 q/k/v rows, head h at h * 128), one CTA per
+// (sequence, head). Packed (seq_off non-null): sequence order[y] (null: y) is tokens seq_off[b] ..
+// + seq_len[b], from s_in[b] (null table or entry: zeros) to s_out[b] (null: not stored). Batch:
+// `walks / h` sequences of l tokens, sequence b at slab b of the q/k/v maps (seq_qk / seq_v elements
+// apart) and tokens b * l .. of beta, g and o; state [b][h][128][128] read when load_state, written
+// when store_state. beta, g [token][h]; o [token][h * 128] f32.
+struct GdnTcArgs {
+  const float *beta = nullptr, *g = nullptr;
+  float* o = nullptr;
+  int h = 0, l = 0;
+  const int *seq_off = nullptr, *seq_len = nullptr, *order = nullptr;
+  const float* const* s_in = nullptr;
+  float* const* s_out = nullptr;
+  float* state = nullptr;
+  int load_state = 0, store_state = 1;
+  int* err = nullptr;  // a bounded wait that gave up records its code here
+};
+// rows: the token rows of the q/k/v maps (packed: all packed tokens; batch: l)
+cudaError_t launch_gdn_tc(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride, long long seq_qk,
+                          long long seq_v, int rows, const GdnTcArgs& a, int walks, cudaStream_t st);
+cudaError_t preload_gdn_tc();
 cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff, const float* w, int l, int h, __half* out,
                          cudaStream_t st);
 cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,

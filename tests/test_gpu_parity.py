@@ -227,6 +227,33 @@ def test_gdn_chunked_matches_oracle(torch, b, l, in_f16, load):
         assert np.abs(got_o[i] - o_want).max() < 3e-2
 
 
+@pytest.mark.parametrize("b,l,load,algo", [(1, 1, True, 0), (2, 7, True, 0), (1, 63, False, 0), (3, 64, True, 0),
+                                            (2, 65, False, 0), (4, 129, True, 0), (1, 1000, True, 0), (2, 130, True, 3)])
+def test_gdn_f16_scans_match_oracle(torch, b, l, load, algo):
+    """The f16 single-pass scans: algo 0 (the fused tcgen05 kernel: one CTA per sequence and head, all
+    value columns) and 3 (mma.sync), over ragged last chunks, a single token, exact chunk multiples,
+    batches with and without an entry state, against the oracle's recurrence: relative error below
+    5e-3, and the batch's other sequences untouched by each one's padding rows."""
+    from strands_decider.engine import gdn
+    h = 16
+    q, k, v, beta, g, s0 = _gdn_inputs(np.random.default_rng(7 * l + b + algo), b, l, h)
+    q, k, v = (x.astype(np.float16) for x in (q, k, v))
+    qd, kd, vd, bd, gd = (dev(torch, x) for x in (q, k, v, beta, g))
+    sd_ = dev(torch, s0.copy())
+    od = torch.full((b, l, h * 128), float("nan"), dtype=torch.float32, device="cuda")
+    gdn(qd.data_ptr(), kd.data_ptr(), h * 128, vd.data_ptr(), h * 128, bd.data_ptr(), gd.data_ptr(), sd_.data_ptr(), load,
+        od.data_ptr(), l, h, batch=b, seq_qk=l * h * 128, seq_v=l * h * 128, in_f16=True, algo=algo)
+    torch.cuda.synchronize()
+    got_o, got_s = od.cpu().numpy(), sd_.cpu().numpy()
+    assert np.isfinite(got_o).all() and np.isfinite(got_s).all()
+    for i in range(b):
+        o_want, s_want = oracle.gdn(q[i].astype(np.float32), k[i].astype(np.float32), v[i].astype(np.float32), beta[i],
+                                    np.exp(g[i]), s0[i] if load else None)
+        eo = np.linalg.norm(got_o[i] - o_want) / np.linalg.norm(o_want)
+        es = np.linalg.norm(got_s[i] - s_want) / np.linalg.norm(s_want)
+        assert eo < 5e-3 and es < 5e-3, (i, eo, es)
+
+
 @pytest.mark.parametrize("l,load", [(333, False), (64, True), (65, True), (1000, True)])
 def test_gdn_two_phase_matches_oracle(torch, l, load):
     """The two-phase scan (all chunks' intra-chunk products in parallel, then the state walk) against
