@@ -25,6 +25,7 @@ stream over a profiled pass of the same steps.
 from __future__ import annotations
 
 import argparse
+import functools
 import json
 import os
 import statistics
@@ -230,13 +231,26 @@ def request_tokens(i: int, seed: int = 0) -> int:
     return s + int(qlens.sum())
 
 
+@functools.lru_cache(maxsize=4)
+def sweep_order(seed: int = 0):
+    """The order in which the bench takes the sweep's requests: sorted by state length, then visited in
+    bit-reversed rank order (a van der Corput sequence over the length quantiles), so that any run of
+    consecutive requests, the timed steps among them, spreads evenly over the sweep's length
+    distribution (160 requests: mean state within 0.5% of the sweep's 2080 tokens)."""
+    lens = [request_tokens(i, seed) for i in range(N_REQUESTS)]
+    srt = sorted(range(N_REQUESTS), key=lambda i: (lens[i], i))
+    bits = (N_REQUESTS - 1).bit_length()
+    return [srt[int(format(k, f"0{bits}b")[::-1], 2)] for k in range(N_REQUESTS)]
+
+
 def step_requests(step: int, rank: int, world: int, per: int, seed: int = 0):
     """This rank's requests of step `step`: the step takes the next world x per requests of the sweep
-    and shares them out as a server balances concurrent requests over its GPUs, longest first to the
-    rank with the fewest tokens so far (each rank gets `per`), so that no rank waits on another
-    holding all the long states."""
+    (in sweep_order) and shares them out as a server balances concurrent requests over its GPUs,
+    longest first to the rank with the fewest tokens so far (each rank gets `per`), so that no rank
+    waits on another holding all the long states."""
     base = step * world * per
-    ids = [(base + j) % N_REQUESTS for j in range(world * per)]
+    order = sweep_order(seed)
+    ids = [order[(base + j) % N_REQUESTS] for j in range(world * per)]
     if world == 1:
         return ids
     load = [0] * world
@@ -444,6 +458,8 @@ def run_ours(args, world, rank, local):
     a = prof["attention"]
     d = prof["gdn"]
     mean_state, mean_tok_q, clips = sweep_stats(args.seed)
+    timed_ids = [i for st_ in range(args.warmup, args.warmup + args.steps) for i in step_requests(st_, rank, world, per, args.seed)]
+    sample_mean_state = sum(staged[i][0].numel() for i in timed_ids) / max(1, len(timed_ids))
     line = {
         "metric": "answered questions/s", "value": q_all / t_dev, "unit": "questions/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True,
@@ -452,6 +468,8 @@ def run_ours(args, world, rank, local):
                                "+ 3 questions of 42-84 tokens (noul/choice/score), random non-special ids",
                    "model": "random-init 2B hybrid (24 layers: 18 gated-delta + 6 attention, int4 g32 weights, int3 embedding)",
                    "requests_per_step_per_gpu": per, "requests_timed": int(q_all // 3), "sweep_mean_state_tokens": round(mean_state, 1),
+                   "sample_mean_state_tokens": round(sample_mean_state, 1),
+                   "sample": "the requests in sweep_order (length quantiles in bit-reversed order), so the timed ones spread over the sweep's length distribution",
                    "sweep_clipped_requests": clips, "l2": "inputs larger than L2 (0.8 GB of weights streamed per forward)",
                    "parallelism": f"replicas x{world} (requests sharded, no collective)"},
         "prefill_tok_s": tok_all / t_dev,
@@ -473,6 +491,17 @@ def run_ours(args, world, rank, local):
                         "unit": "TFLOP/s" if k in ("gemm", "attention") else "GB/s"} for k, v in prof.items()},
         "clocks": clk,
     }
+    if world == 1 and not args.no_configs:
+        # the other configurations of the reference's benchmark, beside the sweep (one GPU)
+        cf = {}
+        cf["1_ask_all"] = config1_ask_all(path, steps=20, warmup=3)
+        cf["2_attention"] = kernel_attention(10, 3, args.seed)
+        cf["3_gdn"] = kernel_gdn(10, 3, args.seed)
+        cf["4_fork"] = config4_fork(eng, head, steps=20, warmup=3)
+        cf["5_sweep"] = {"questions_per_s": q_all / t_dev, "e2e_questions_per_s": qh_all / t_host,
+                         "sample": f"{int(q_all // 3)} requests in sweep_order (mean state "
+                                   f"{sample_mean_state:.0f} tokens; the sweep's {mean_state:.0f})"}
+        line["configs"] = cf
     if world == 1 and not args.no_cpu_baseline:
         path = model_path(1, 0)
         dt, tok = cpu_baseline(path, args.seed)
@@ -484,87 +513,195 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
-def run_kernel_workload(args):
-    """Isolated kernel workloads (not the headline; used for kernel rooflines and ncu captures):
-    attention = config 2 (B=4, S=2048, causal GQA 8/2 heads x 256, gated), gdn = config 3 (B=16,
-    L=1024, 16 heads of 128x128, f16 q/k/v, beta = sigmoid(N(0,1)), g = -softplus(N(0,1))), gemm = one
-    dequantizing matmul shape. Inputs are seeded synthetic tensors with the configs' shapes."""
+def _timed_launches(fn, steps, warmup, flush=None, stream=None):
+    """Median device time (ms) of `steps` launches of fn after `warmup`, each timed alone with CUDA
+    events on the launching stream, with L2 flushed (a 256 MB write) before each."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def kernel_attention(steps, warmup, seed=0):
+    """Config 2: B=4, S=2048, causal GQA 8/2 heads x 256, gated, one sd_attention_batch launch.
+    FLOPs = 4 HD HQ B S(S+1)/2 = 6.875e10 (tensor-bound)."""
+    import torch
+    from strands_decider.engine import attention_batch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    B, S, hq, hk, hd = 4, 2048, 8, 2, 256
+    q = torch.randn(B, hq, S, hd, generator=g, device="cuda").half()
+    k = torch.randn(B, hk, S, hd, generator=g, device="cuda").half()
+    v = torch.randn(B, hk, S, hd, generator=g, device="cuda").half()
+    gate = torch.randn(B, S, hq * 2 * hd, generator=g, device="cuda").half()
+    o = torch.empty(B, S, hq * hd, device="cuda").half()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def fn():
+        attention_batch(q.data_ptr(), k.data_ptr(), v.data_ptr(), gate.data_ptr(), hq * 2 * hd, hd, 2 * hd, o.data_ptr(), B, S,
+                        0, S, hq, hk, hd)
+    ms = _timed_launches(fn, steps, warmup, flush)
+    work = 4.0 * hd * hq * B * S * (S + 1) / 2
+    _, tf_burst, _, src = peaks()
+    return {"us": ms * 1e3, "flops": work, "achieved": work / ms / 1e9, "unit": "TFLOP/s", "peak": tf_burst,
+            "frac": work / ms / 1e9 / tf_burst, "peak_source": f"{src} bf16 burst",
+            "workload": "config 2: B=4 S=2048 HQ=8 HK=2 HD=256 causal, gated (sd_attention_batch, one launch)",
+            "l2": "flushed before each timed launch"}
+
+
+def kernel_gdn(steps, warmup, seed=0, algo=0):
+    """Config 3: B=16, L=1024, 16 heads of 128 x 128, f16 q/k/v, beta = sigmoid(N(0,1)), g =
+    -softplus(N(0,1)), the chunked scan with the final states written. Algorithmic bytes: q, k, v f16 +
+    beta, g f32 + o f32 + final state f32 = 354.4 MB (HBM-bound)."""
+    import torch
+    from strands_decider.engine import gdn
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    B, L, H = 16, 1024, 16
+    x = torch.randn(B, L, 3, H * 128, generator=g, device="cuda").half()
+    beta = torch.sigmoid(torch.randn(B, L, H, generator=g, device="cuda"))
+    gl = -torch.nn.functional.softplus(torch.randn(B, L, H, generator=g, device="cuda"))
+    st = torch.zeros(B, H, 128, 128, device="cuda")
+    o = torch.empty(B, L, H * 128, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    qp = x.data_ptr()
+
+    def fn():
+        gdn(qp, qp + H * 128 * 2, 3 * H * 128, qp + 2 * H * 128 * 2, 3 * H * 128, beta.data_ptr(), gl.data_ptr(),
+            st.data_ptr(), 0, o.data_ptr(), L, H, batch=B, seq_qk=L * 3 * H * 128, seq_v=L * 3 * H * 128, in_f16=True, algo=algo)
+    ms = _timed_launches(fn, steps, warmup, flush)
+    byts = B * L * H * (3 * 128 * 2 + 8 + 128 * 4) + B * H * 128 * 128 * 4
+    hbm, _, _, src = peaks()
+    return {"us": ms * 1e3, "bytes": byts, "achieved": byts / ms / 1e6, "unit": "GB/s", "peak": hbm,
+            "frac": byts / ms / 1e6 / hbm, "peak_source": f"{src} HBM copy",
+            "workload": "config 3: B=16 L=1024 H=16 DK=DV=128, f16 q/k/v, fused tcgen05 chunked scan" if algo == 0 else
+                        f"config 3 through sd_gdn algo {algo}", "l2": "flushed before each timed launch"}
+
+
+def kernel_gemm(m, n, k, steps, warmup, seed=0):
     import torch
     from strands_decider import model as M
-    from strands_decider.engine import QWeight, attention_batch, gdn
+    from strands_decider.engine import QWeight
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    rng = np.random.default_rng(seed)
+    silu = n == 12288
+    packed, scales = M._quant_tensor(rng, n, k, 4, 1.0 / np.sqrt(k))
+    qd = torch.from_numpy(packed).cuda()
+    sd = torch.from_numpy(scales.view(np.uint16)).cuda()
+    w = QWeight(qd.data_ptr(), sd.data_ptr(), n, k, interleave=silu)
+    a = torch.randn(m, k, generator=g, device="cuda").half()
+    y = torch.empty(m, n, device="cuda").half()
+    ws = torch.empty(16 << 20, dtype=torch.float32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def fn():
+        w.matmul(a.data_ptr(), m, y.data_ptr(), n // 2 if silu else n, silu=silu, ws_dev=ws.data_ptr(), ws_bytes=ws.numel() * 4)
+    ms = _timed_launches(fn, steps, warmup, flush)
+    fl = 2.0 * m * n * k
+    _, tf_burst, _, src = peaks()
+    return {"us": ms * 1e3, "achieved": fl / ms / 1e9, "unit": "TFLOP/s", "peak": tf_burst, "frac": fl / ms / 1e9 / tf_burst,
+            "peak_source": f"{src} bf16 burst", "bound": "tensor" if m > 71 else "hbm", "weight_gbs": n * k * 0.5625 / ms / 1e6,
+            "workload": f"gemm m={m} n={n} k={k}" + (" (SwiGLU epilogue)" if silu else ""), "l2": "flushed before each timed launch"}
+
+
+WORDS = ("payout", "failing", "account", "billing", "urgent", "refund", "customer", "support", "invoice", "delay",
+         "error", "card", "bank", "transfer", "status", "pending", "help", "days", "please", "order", "ticket",
+         "escalate", "charge", "merchant", "dashboard", "settings", "email", "phone", "reply", "waiting")
+
+
+def config1_request(path, n_tokens=128, seed=1):
+    """Config 1's System One request: a state of random words rendering to n_tokens tokens (or just
+    over) and three questions (noul; choice over 3; score over 3)."""
+    from strands_decider import prompt
+    from strands_decider.tokenizer import Tokenizer
+    with open(os.path.join(path, "tokenizer.json"), encoding="utf-8") as f:
+        tok = Tokenizer.from_json(f.read())
+    rng = np.random.default_rng(seed)
+    words = []
+    while len(tok.encode(prompt.render_state(" ".join(words))).ids) < n_tokens:
+        words.append(WORDS[int(rng.integers(len(WORDS)))])
+    state = " ".join(words)
+    return {"state": state, "questions": {
+        "urgent": {"type": "noul", "instructions": "Does this convey urgency?"},
+        "team": {"type": "choice", "instructions": "Which team should handle this?",
+                 "criteria": {"billing": "payments and invoices", "technical": "errors and outages", "sales": "plans and pricing"}},
+        "mood": {"type": "score", "instructions": "How frustrated is the writer?", "criteria": ["calm", "frustrated", "very angry"]}}}, \
+        len(tok.encode(prompt.render_state(state)).ids)
+
+
+def config1_ask_all(path, steps, warmup):
+    """Config 1: one `ask_all` (sd_decider_ask_all: System One JSON in, the response JSON out, batch 1)
+    on a 128-token state with 3 questions: wall-clock latency per call (tokenizer, prompt, the state's
+    forward, the batched fork of the questions, the head, the answers)."""
+    from strands_decider.engine import NativeDecider
+    req, ntok = config1_request(path)
+    dec = NativeDecider.load(path)
+    for _ in range(warmup):
+        dec.ask_all(req)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        dec.ask_all(req)
+        ts.append(time.perf_counter() - t0)
+    dec.close()
+    lat = statistics.median(ts)
+    return {"latency_ms": lat * 1e3, "questions_per_s": 3 / lat, "state_tokens": ntok, "calls": steps,
+            "path": "sd_decider_ask_all: JSON request in, JSON response out (host tokenizer and prompt in C++)"}
+
+
+def config4_fork(eng, head, steps, warmup, seed=4):
+    """Config 4: a 512-token state encoded once (kept as a snapshot), then 64 questions of 24-48 random
+    non-special tokens continued from it in one batched fork (sd_forward_fork_multi_probs: host ids in,
+    each question's probabilities out; the pointer head on the GPU over 2 option rows + the answer
+    row). Questions/s from the wall time of the fork calls (host copies included)."""
+    rng = np.random.default_rng(seed)
+
+    def ids(n):
+        x = rng.integers(0, VOCAB - len(SPECIAL), n)
+        return (x + (x >= SPECIAL[0]) * len(SPECIAL)).astype(np.uint32)
+    snap = eng.forward(ids(512), [], keep=True).snapshot
+    qs = [ids(int(n)) for n in rng.integers(24, 49, 64)]
+    rows = [np.array([len(q) // 3, 2 * len(q) // 3, len(q) - 1], np.int32) for q in qs]
+    for _ in range(warmup):
+        eng.forward_fork_probs([snap] * 64, qs, rows, head, 1.0)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        eng.forward_fork_probs([snap] * 64, qs, rows, head, 1.0)
+        ts.append(time.perf_counter() - t0)
+    snap.close()
+    t = statistics.median(ts)
+    return {"ms_per_fork": t * 1e3, "questions_per_s": 64 / t, "question_tokens": int(sum(len(q) for q in qs)),
+            "path": "sd_forward_fork_multi_probs over one 512-token snapshot (64 questions, one packed pass + head)"}
+
+
+def run_kernel_workload(args):
+    """Isolated kernel workloads (not the headline; used for kernel rooflines and ncu captures):
+    attention = config 2, gdn = config 3, gemm = one dequantizing matmul shape. Inputs are seeded
+    synthetic tensors with the configs' shapes."""
+    import torch
     torch.cuda.set_device(0)
-    hbm, tf_burst, tf_sus, src = peaks()
-    g = torch.Generator(device="cuda").manual_seed(args.seed)
-
-    def timed(fn, steps, warmup):
-        for _ in range(warmup):
-            fn()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / steps
-
     if args.workload == "attention":
-        B, S, hq, hk, hd = 4, 2048, 8, 2, 256
-        q = torch.randn(B, hq, S, hd, generator=g, device="cuda").half()
-        k = torch.randn(B, hk, S, hd, generator=g, device="cuda").half()
-        v = torch.randn(B, hk, S, hd, generator=g, device="cuda").half()
-        gate = torch.randn(B, S, hq * 2 * hd, generator=g, device="cuda").half()
-        o = torch.empty(B, S, hq * hd, device="cuda").half()
-
-        def fn():  # the batch in one launch (sd_attention_batch)
-            attention_batch(q.data_ptr(), k.data_ptr(), v.data_ptr(), gate.data_ptr(), hq * 2 * hd, hd, 2 * hd, o.data_ptr(), B,
-                            S, 0, S, hq, hk, hd)
-        ms = timed(fn, args.steps, args.warmup)
-        work = 4.0 * hd * hq * B * S * (S + 1) / 2
-        line = {"metric": "attention TFLOP/s (config 2)", "value": work / ms / 1e9, "unit": "TFLOP/s", "ms_per_step": ms,
-                "roofline": {"bound": "tensor", "achieved": work / ms / 1e9, "peak": tf_burst, "unit": "TFLOP/s",
-                             "frac": work / ms / 1e9 / tf_burst, "peak_source": f"{src} bf16 burst"},
-                "config": {"workload": "config 2: B=4 S=2048 HQ=8 HK=2 HD=256 causal, gated", "flops_per_step": work}}
+        r = kernel_attention(args.steps, args.warmup, args.seed)
+        metric = "attention TFLOP/s (config 2)"
     elif args.workload == "gdn":
-        B, L, H = 16, 1024, 16
-        x = torch.randn(B, L, 3, H * 128, generator=g, device="cuda").half()
-        beta = torch.sigmoid(torch.randn(B, L, H, generator=g, device="cuda"))
-        gl = -torch.nn.functional.softplus(torch.randn(B, L, H, generator=g, device="cuda"))
-        st = torch.zeros(B, H, 128, 128, device="cuda")
-        o = torch.empty(B, L, H * 128, device="cuda")
-        qp = x.data_ptr()
-
-        def fn():
-            gdn(qp, qp + H * 128 * 2, 3 * H * 128, qp + 2 * H * 128 * 2, 3 * H * 128, beta.data_ptr(), gl.data_ptr(),
-                st.data_ptr(), 0, o.data_ptr(), L, H, batch=B, seq_qk=L * 3 * H * 128, seq_v=L * 3 * H * 128, in_f16=True)
-        ms = timed(fn, args.steps, args.warmup)
-        byts = B * L * H * (3 * 128 * 2 + 8 + 128 * 4) + B * H * 128 * 128 * 4
-        line = {"metric": "gated delta rule GB/s (config 3)", "value": byts / ms / 1e6, "unit": "GB/s", "ms_per_step": ms,
-                "roofline": {"bound": "hbm", "achieved": byts / ms / 1e6, "peak": hbm, "unit": "GB/s",
-                             "frac": byts / ms / 1e6 / hbm, "peak_source": f"{src} HBM copy"},
-                "config": {"workload": "config 3: B=16 L=1024 H=16 DK=DV=128, f16 q/k/v, chunked scan", "bytes_per_step": byts}}
+        r = kernel_gdn(args.steps, args.warmup, args.seed, args.gdn_algo)
+        metric = "gated delta rule GB/s (config 3)"
     else:
-        m, n, k = args.m, args.n, args.k
-        rng = np.random.default_rng(args.seed)
-        silu = n == 12288
-        packed, scales = M._quant_tensor(rng, n, k, 4, 1.0 / np.sqrt(k))
-        qd = torch.from_numpy(packed).cuda()
-        sd = torch.from_numpy(scales.view(np.uint16)).cuda()
-        w = QWeight(qd.data_ptr(), sd.data_ptr(), n, k, interleave=silu)
-        a = torch.randn(m, k, generator=g, device="cuda").half()
-        y = torch.empty(m, n, device="cuda").half()
-        ws = torch.empty(16 << 20, dtype=torch.float32, device="cuda")
-
-        def fn():
-            w.matmul(a.data_ptr(), m, y.data_ptr(), n // 2 if silu else n, silu=silu, ws_dev=ws.data_ptr(), ws_bytes=ws.numel() * 4)
-        ms = timed(fn, args.steps, args.warmup)
-        fl = 2.0 * m * n * k
-        line = {"metric": "dequantizing GEMM TFLOP/s", "value": fl / ms / 1e9, "unit": "TFLOP/s", "ms_per_step": ms,
-                "roofline": {"bound": "tensor" if m > 71 else "hbm", "achieved": fl / ms / 1e9, "peak": tf_burst,
-                             "unit": "TFLOP/s", "frac": fl / ms / 1e9 / tf_burst, "peak_source": f"{src} bf16 burst"},
-                "config": {"workload": f"gemm m={m} n={n} k={k}" + (" (SwiGLU epilogue)" if silu else ""),
-                           "weight_gbs": n * k * 0.5625 / ms / 1e6}}
-    line.update({"steps": args.steps, "warmup": args.warmup, "n_gpus": 1, "data": "synthetic", "dtype": "f16"})
+        r = kernel_gemm(args.m, args.n, args.k, args.steps, args.warmup, args.seed)
+        metric = "dequantizing GEMM TFLOP/s"
+    line = {"metric": metric, "value": r["achieved"], "unit": r["unit"], "us_per_launch": r["us"],
+            "roofline": {k: r[k] for k in ("achieved", "peak", "unit", "frac", "peak_source")}, "config": r,
+            "steps": args.steps, "warmup": args.warmup, "n_gpus": 1, "data": "synthetic", "dtype": "f16"}
     print(json.dumps(line), flush=True)
 
 
@@ -582,6 +719,8 @@ def main():
     ap.add_argument("--m", type=int, default=2048)
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--gdn-algo", type=int, default=0, help="sd_gdn algo for --workload gdn (0: the fused tcgen05 scan)")
+    ap.add_argument("--no-configs", action="store_true", help="skip configs 1-4 beside the sweep (N=1 only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

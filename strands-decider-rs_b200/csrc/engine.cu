@@ -96,6 +96,9 @@ struct sd_head {
 struct sd_engine {
   int device = 0;
   int num_sms = 148;
+  // the gated-delta layers on the fused tcgen05 scan (gdn_tc.cu); SD_GDN_KERNEL=legacy at engine
+  // creation selects the mma.sync scans (single-pass and two-phase) instead, for comparisons
+  bool gdn_tc = true;
   cudaStream_t stream = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   sd::Dims dm;
@@ -710,7 +713,22 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
         // one chunk: the single-pass scan; longer: the two-phase scan (chunks in parallel, then the state walk);
         // packed sequences, each from its snapshot's state (or zeros): short ones with the single-pass
         // scan, long ones with the two-phase scan
-        if (fk && fk->two_phase)
+        if (e->gdn_tc) {  // the fused tcgen05 scan: one CTA per (sequence, head)
+          sd::GdnTcArgs ga;
+          ga.beta = e->beta, ga.g = e->decay, ga.o = e->of, ga.h = d.h, ga.err = e->d_err;
+          int walks = d.h;
+          if (fk) {
+            ga.seq_off = fk->seq_off, ga.seq_len = fk->seq_len, ga.order = fk->order;
+            ga.s_in = fk->states + (size_t)Lw.slot * fk->nseq;
+            ga.s_out = fk->s_out ? fk->s_out + (size_t)Lw.slot * fk->nseq : nullptr;
+            walks = fk->nseq * d.h;
+          } else {
+            ga.l = l, ga.state = e->state[Lw.slot], ga.load_state = has_cache, ga.store_state = 1;
+          }
+          LK(SD_PROF_GDN, gdn_bytes,
+             sd::launch_gdn_tc(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, (long long)l * C,
+                               (long long)l * C, l, ga, walks, st));
+        } else if (fk && fk->two_phase)
           LK(SD_PROF_GDN, gdn_bytes,
              (*nl = 2, sd::launch_gdn_two_phase_packed(
                            e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, e->beta, e->decay,
@@ -1318,6 +1336,7 @@ int sd_engine_create(const char* model_dir, int device, sd_engine** out) {
   auto* e = new sd_engine();
   e->device = device;
   e->num_sms = prop.multiProcessorCount;
+  if (const char* k = getenv("SD_GDN_KERNEL")) e->gdn_tc = strcmp(k, "legacy") != 0;
   cudaSetDevice(device);
   if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess || cudaEventCreate(&e->ev0) != cudaSuccess ||
       cudaEventCreate(&e->ev1) != cudaSuccess) {
@@ -1347,7 +1366,8 @@ int sd_engine_create(const char* model_dir, int device, sd_engine** out) {
   cudaError_t ce;
   if ((ce = sd::preload_gemm()) != cudaSuccess || (ce = sd::preload_attention()) != cudaSuccess ||
       (ce = sd::preload_attention_tc()) != cudaSuccess ||
-      (ce = sd::preload_gdn()) != cudaSuccess || (ce = sd::preload_kernels()) != cudaSuccess ||
+      (ce = sd::preload_gdn()) != cudaSuccess || (ce = sd::preload_gdn_tc()) != cudaSuccess ||
+      (ce = sd::preload_kernels()) != cudaSuccess ||
       (ce = sd::preload_head()) != cudaSuccess) {
     set_global_error(std::string("sd_engine_create: loading the kernels: ") + cudaGetErrorString(ce));
     sd_engine_destroy(e);

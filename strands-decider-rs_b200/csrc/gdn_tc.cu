@@ -15,15 +15,17 @@
 // (accumulated onto [0; U], so that the second half is delta), and [P; *] delta adds P delta to the
 // first half. The state-independent work of chunk c + 1 (normalisation, A and P, the triangular
 // inverse, W and U) runs beside the state chain of chunk c:
-//   warp 0      TMA: the raw k and q rows of each chunk (into the chunk's tile, normalised in place)
-//               and its v rows, two chunks ahead at most;
-//   warp 1      one thread issues the state chain's MMAs: [Gamma Q^; -W] S, K^T Ds, P delta;
-//   warps 2-5   the chain: S out of tensor memory (its f16 copy, the operand of the next chunk, and
-//               Gamma_C S back), delta (f16, and decayed as Ds), O rows to global memory;
-//   warps 6-9   the chunk preparation: q^, k^, the gates and G, A and P from [K^; Q^] K^T, the
+//   warps 0-3   the chain: S out of tensor memory (its f16 copy, the operand of the next chunk, and
+//               Gamma_C S back), delta (f16, and decayed as Ds), O rows to global memory; one thread
+//               issues the chain's MMAs ([Gamma Q^; -W] S, K^T Ds, P delta) and the v rows' TMA, one
+//               the k and q rows' TMA (into the chunk's tile, where they are normalised in place), two
+//               chunks ahead at most;
+//   warps 4-11  the chunk preparation: q^, k^, the gates and G, A and P from [K^; Q^] K^T, the
 //               inverse (f32; 16 x 16 diagonal blocks by substitution, the rest on tf32 mma.sync),
 //               T1 and T2 (f16), W out of tensor memory; their first thread issues [K^; Q^] K^T,
 //               W = [T1; *] K^ and U = [0; T2] V.
+// Each group keeps its warps on the same path through its named barrier whatever happens (a wait
+// that gives up marks the CTA aborted and the group skips the work that follows, not the barriers).
 // Rounding points are those of the two-phase scan (gdn.cu): f16 q^, k^, T1, T2, W, P, delta, Ds and
 // the state operand; f32 accumulation, U and the state.
 //
@@ -38,7 +40,7 @@ namespace sd {
 
 namespace {
 constexpr int CH = 64, DK = 128;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
 constexpr int kBox = 192 * 128;                       // one 64-column half of a chunk tile: K^ rows 0-63, Q^ 64-127, W 128-191
 constexpr int kTile = 2 * kBox;                       // 48 KB
 constexpr int kOffKQW = 0;                            // [2] chunk tiles
@@ -52,27 +54,24 @@ constexpr int kOffT2 = kOffZ + 8192;
 constexpr int LA = CH + 1;                            // row stride (floats) of the f32 64 x 64 tiles
 constexpr int kOffA = kOffT2 + 8192;                  // A (f32)
 constexpr int kOffX = kOffA + CH * LA * 4;            // T = (I + A)^-1 (f32)
-constexpr int kOffY = kOffX + CH * LA * 4;            // 3 x 16 x 17 floats of the inverse's scratch
-constexpr int kOffSmall = kOffY + 3 * 16 * 17 * 4;    // beta[2][64], G[2][64], g[64]
+constexpr int kOffY = kOffX + CH * LA * 4;            // 6 x 16 x 9 floats of the inverse's scratch
+constexpr int kOffSmall = kOffY + 6 * 16 * 9 * 4;     // beta[2][64], G[2][64], g[64]
 constexpr int kOffBar = kOffSmall + 5 * CH * 4;
 enum {
   B_KQ_FULL = 0,     // [2] the chunk's k and q rows landed (TMA bytes)
-  B_KQ_EMPTY = 2,    // [2] the chain's MMAs of the chunk completed: its tile is free
-  B_V_FULL = 4,      // [2] the chunk's v rows landed
-  B_U_DONE = 6,      // [2] U = [0; T2] V completed (V, T1 and T2 free; the chain may accumulate)
-  B_DAP_FULL = 8,    // [2] [K^; Q^] K^T in tensor memory
-  B_W_FULL = 10,     // [2] W in tensor memory
-  B_WQ_READY = 12,   // [2] -W, Gamma Q^ and P written (shared memory), W read out
-  B_G_READY = 14,    // [2] the chunk's G written
-  B_S16_READY = 16,  // [2] the entry state's f16 copy written and Gamma_C S back in tensor memory
-  B_X_FULL = 18,     // [2] [Gamma Q^; -W] S accumulated
-  B_D_READY = 20,    // [2] delta and Ds written
-  B_S_FULL = 22,     // [2] the state update completed
-  B_O_FULL = 24,     // [2] P delta accumulated (O complete); P and delta free
-  B_O_READ = 26,     // [2] O read out of tensor memory
-  B_END_PREP = 28,   // every MMA of the preparation completed (teardown)
-  B_END_CHAIN = 29,  // every MMA of the chain completed (teardown)
-  kBars = 30
+  B_V_FULL = 2,      // [2] the chunk's v rows landed
+  B_U_DONE = 4,      // [2] U = [0; T2] V completed (V, T1 and T2 free; the chain may accumulate)
+  B_DAP_FULL = 6,    // [2] [K^; Q^] K^T in tensor memory
+  B_W_FULL = 8,      // [2] W in tensor memory
+  B_WQ_READY = 10,   // [2] -W, Gamma Q^ and P written (shared memory), W read out
+  B_G_READY = 12,    // [2] the chunk's G written
+  B_X_FULL = 14,     // [2] [Gamma Q^; -W] S accumulated
+  B_S_FULL = 16,     // [2] the state update completed
+  B_O_FULL = 18,     // [2] P delta accumulated (O complete): every MMA of the chunk has completed
+  B_O_READ = 20,     // [2] O read out of tensor memory (4 arrivals)
+  B_END_PREP = 22,   // every MMA of the preparation completed (teardown)
+  B_END_CHAIN = 23,  // every MMA of the chain completed (teardown)
+  kBars = 24
 };
 constexpr int kSmem = kOffBar + kBars * 8 + 16 + 1024;
 static_assert(kSmem <= 232448, "shared memory");
@@ -81,6 +80,7 @@ constexpr uint32_t kIdS = idesc_f16(128, 128) | (1u << 15) | (1u << 16);  // bot
 constexpr uint32_t kIdB = idesc_f16_bmn(128, 128);                        // B MN-major
 constexpr uint32_t kIdAP = idesc_f16(128, 64);                            // both K-major
 constexpr int kPrepBar = 1;                                               // named barrier of the preparation warps
+constexpr int kChainBar = 2;                                              // named barrier of the chain warps
 
 __device__ int g_gdn_tc_err;  // error slot of calls without one
 
@@ -88,7 +88,8 @@ __device__ int g_gdn_tc_err;  // error slot of calls without one
 // 128 bytes; the tile starts on a 1024-byte boundary).
 SD_DEV uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-SD_DEV void prep_sync() { asm volatile("bar.sync %0, 128;" ::"n"(kPrepBar) : "memory"); }
+SD_DEV void prep_sync() { asm volatile("bar.sync %0, 256;" ::"n"(kPrepBar) : "memory"); }
+SD_DEV void chain_sync() { asm volatile("bar.sync %0, 128;" ::"n"(kChainBar) : "memory"); }
 
 SD_DEV uint32_t pack_h2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
@@ -107,14 +108,15 @@ SD_DEV void mma1688_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, u
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// X = (I + A)^-1 for the strictly lower triangular 64 x 64 A (rows LA floats apart), by the four
-// preparation warps (w = 0..3): the 16 x 16 diagonal blocks by forward substitution (warp w, lane =
-// column), then the blocks below the diagonal level by level, X_ij = -X_ii sum_{m=j}^{i-1} A_im X_mj for
-// i = j + dl (warp w < 4 - dl takes block (w + dl, w)), on the tensor cores with tf32 operands and f32
-// accumulation. Blocks above the diagonal are not written (never read).
-SD_DEV void tri_inverse(const float* __restrict__ a, float* __restrict__ x, float* __restrict__ y, int w, int lane) {
-  if (lane < 16) {
-    const int o = w * 16, c = lane;
+// X = (I + A)^-1 for the strictly lower triangular 64 x 64 A (rows LA floats apart), by the eight
+// preparation warps (w = 0..7): the 16 x 16 diagonal blocks by forward substitution (warp w < 4,
+// lane = column), then the blocks below the diagonal level by level, X_ij = -X_ii sum_{m=j}^{i-1} A_im
+// X_mj for i = j + dl (warps w and w + 4 take the two 8-column halves of block (w + dl, w), w < 4 - dl),
+// on the tensor cores with tf32 operands and f32 accumulation. Blocks above the diagonal are not
+// written (never read). `y`: 6 x 16 x 9 floats of scratch.
+SD_DEV void tri_inverse(const float* __restrict__ a, float* __restrict__ x, float* __restrict__ y, int pw, int lane) {
+  if (pw < 4 && lane < 16) {
+    const int o = pw * 16, c = lane;
     float xc[16];
 #pragma unroll
     for (int r = 0; r < 16; r++) {
@@ -131,49 +133,38 @@ SD_DEV void tri_inverse(const float* __restrict__ a, float* __restrict__ x, floa
     for (int r = 0; r < 16; r++) x[(o + r) * LA + o + c] = xc[r];
   }
   prep_sync();
-  const int g = lane >> 2, tq = lane & 3;
+  const int g = lane >> 2, tq = lane & 3, w = pw & 3, nt = pw >> 2;
 #pragma unroll 1
   for (int dl = 1; dl < 4; dl++) {
     if (w < 4 - dl) {
       const int bj = w, bi = bj + dl;
-      float acc[2][4] = {};
+      float acc[4] = {};
       for (int m = bj; m < bi; m++)
 #pragma unroll
         for (int kk = 0; kk < 16; kk += 8) {
           const float* ar = a + (bi * 16 + g) * LA + m * 16 + kk;
-          const uint32_t a0 = tf32(ar[tq]), a1 = tf32(ar[8 * LA + tq]), a2 = tf32(ar[tq + 4]), a3 = tf32(ar[8 * LA + tq + 4]);
-#pragma unroll
-          for (int nt = 0; nt < 2; nt++) {
-            const float* xr = x + (m * 16 + kk + tq) * LA + bj * 16 + nt * 8 + g;
-            mma1688_tf32(acc[nt], a0, a1, a2, a3, tf32(xr[0]), tf32(xr[4 * LA]));
-          }
+          const float* xr = x + (m * 16 + kk + tq) * LA + bj * 16 + nt * 8 + g;
+          mma1688_tf32(acc, tf32(ar[tq]), tf32(ar[8 * LA + tq]), tf32(ar[tq + 4]), tf32(ar[8 * LA + tq + 4]), tf32(xr[0]),
+                       tf32(xr[4 * LA]));
         }
-      float* yw = y + w * 272;  // this block's sum, 16 x 16 (row stride 17)
-#pragma unroll
-      for (int nt = 0; nt < 2; nt++) {
-        yw[g * 17 + nt * 8 + 2 * tq] = acc[nt][0];
-        yw[g * 17 + nt * 8 + 2 * tq + 1] = acc[nt][1];
-        yw[(g + 8) * 17 + nt * 8 + 2 * tq] = acc[nt][2];
-        yw[(g + 8) * 17 + nt * 8 + 2 * tq + 1] = acc[nt][3];
-      }
+      float* yw = y + (w + 3 * nt) * 144;  // this warp's 16 x 8 part of the sum (row stride 9; w < 3)
+      yw[g * 9 + 2 * tq] = acc[0];
+      yw[g * 9 + 2 * tq + 1] = acc[1];
+      yw[(g + 8) * 9 + 2 * tq] = acc[2];
+      yw[(g + 8) * 9 + 2 * tq + 1] = acc[3];
       __syncwarp();
-      float z[2][4] = {};
+      float z[4] = {};
 #pragma unroll
       for (int kk = 0; kk < 16; kk += 8) {
         const float* xr = x + (bi * 16 + g) * LA + bi * 16 + kk;
-        const uint32_t a0 = tf32(xr[tq]), a1 = tf32(xr[8 * LA + tq]), a2 = tf32(xr[tq + 4]), a3 = tf32(xr[8 * LA + tq + 4]);
-#pragma unroll
-        for (int nt = 0; nt < 2; nt++)
-          mma1688_tf32(z[nt], a0, a1, a2, a3, tf32(yw[(kk + tq) * 17 + nt * 8 + g]), tf32(yw[(kk + tq + 4) * 17 + nt * 8 + g]));
+        mma1688_tf32(z, tf32(xr[tq]), tf32(xr[8 * LA + tq]), tf32(xr[tq + 4]), tf32(xr[8 * LA + tq + 4]),
+                     tf32(yw[(kk + tq) * 9 + g]), tf32(yw[(kk + tq + 4) * 9 + g]));
       }
-#pragma unroll
-      for (int nt = 0; nt < 2; nt++) {
-        float* xo = x + (bi * 16 + g) * LA + bj * 16 + nt * 8 + 2 * tq;
-        xo[0] = -z[nt][0];
-        xo[1] = -z[nt][1];
-        xo[8 * LA] = -z[nt][2];
-        xo[8 * LA + 1] = -z[nt][3];
-      }
+      float* xo = x + (bi * 16 + g) * LA + bj * 16 + nt * 8 + 2 * tq;
+      xo[0] = -z[0];
+      xo[1] = -z[1];
+      xo[8 * LA] = -z[2];
+      xo[8 * LA + 1] = -z[3];
     }
     prep_sync();
   }
@@ -225,17 +216,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nch = (L + CH - 1) / CH;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kBars; i++) {
-      const bool four = (i >= B_S16_READY && i < B_S16_READY + 2) || (i >= B_D_READY && i < B_D_READY + 2) ||
-                        (i >= B_O_READ && i < B_O_READ + 2);
-      mbar_init(&bar[i], four ? 4 : 1);
-    }
+    for (int i = 0; i < kBars; i++) mbar_init(&bar[i], i >= B_O_READ && i < B_O_READ + 2 ? 4 : 1);
     *abort = 0;
     fence_mbar_init();
   }
   // the zero tile (rows 64-127 of U's [0; T2] operand)
   for (int i = threadIdx.x; i < 8192 / 16; i += kThreads) reinterpret_cast<uint4*>(base + kOffZ)[i] = make_uint4(0, 0, 0, 0);
-  if (warp == 1) {
+  if (warp == 0) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -247,79 +234,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (nch == 0) {
     // nothing to walk: the final state is the initial one
-  } else if (warp == 0) {
-    // ---------------------------------------------------------------- TMA
-    if (lane == 0) {
+  } else if (warp < 4) {
+    // ---------------------------------------------------------------- the chain (and the copies)
+    const int q4 = warp;                           // TMEM lanes 32 q4 .. + 31
+    const int r = q4 * 32 + lane;                  // S: key row r; D_X: row r
+    const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+    const int x = hd * DK;
+    // TMA of chunk c's k and q rows into its tile, and of its v rows
+    auto load_kq = [&](int c) {
+      const int s = c & 1, y = (int)(y0 + (long long)c * CH);
+      uint8_t* t = base + kOffKQW + s * kTile;
+      mbar_arrive_expect_tx(&bar[B_KQ_FULL + s], 4 * 8192);
+      for (int hb = 0; hb < 2; hb++) {
+        tma_load_3d(t + hb * kBox, &kmap, &bar[B_KQ_FULL + s], x + hb * 64, y, z);
+        tma_load_3d(t + hb * kBox + 64 * 128, &qmap, &bar[B_KQ_FULL + s], x + hb * 64, y, z);
+      }
+    };
+    auto load_v = [&](int c) {
+      const int s = c & 1, y = (int)(y0 + (long long)c * CH);
+      mbar_arrive_expect_tx(&bar[B_V_FULL + s], 2 * 8192);
+      for (int hb = 0; hb < 2; hb++) tma_load_3d(base + kOffV + hb * 8192, &vmap, &bar[B_V_FULL + s], x + hb * 64, y, z);
+    };
+    int nkq = 0, nv = 0;  // copies issued (warp 0 lane 0: k/q; warp 2 lane 0: v)
+    if (warp == 0 && lane == 0) {
       prefetch_tmap(&qmap);
       prefetch_tmap(&kmap);
       prefetch_tmap(&vmap);
-      bool ok = true;
-      int nkq = 0, nv = 0;
-      for (int c = 0; c < nch && ok; c++) {
-        const int s = c & 1;
-        if (c >= 2 && !(ok = mbar_wait(&bar[B_KQ_EMPTY + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty))) break;
-        uint8_t* t = base + kOffKQW + s * kTile;
-        const int y = (int)(y0 + (long long)c * CH), x = hd * DK;
-        mbar_arrive_expect_tx(&bar[B_KQ_FULL + s], 4 * 8192);
-        for (int hb = 0; hb < 2; hb++) {
-          tma_load_3d(t + hb * kBox, &kmap, &bar[B_KQ_FULL + s], x + hb * 64, y, z);
-          tma_load_3d(t + hb * kBox + 64 * 128, &qmap, &bar[B_KQ_FULL + s], x + hb * 64, y, z);
-        }
-        nkq++;
-        if (c >= 1 && !(ok = mbar_wait(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty))) break;
-        mbar_arrive_expect_tx(&bar[B_V_FULL + s], 2 * 8192);
-        for (int hb = 0; hb < 2; hb++) tma_load_3d(base + kOffV + hb * 8192, &vmap, &bar[B_V_FULL + s], x + hb * 64, y, z);
-        nv++;
-      }
-      // no copy may land after the CTA has left: wait (bounded) for the last ones issued
-      for (int c = max(0, nkq - 2); c < nkq; c++) mbar_drain(&bar[B_KQ_FULL + (c & 1)], (c >> 1) & 1);
-      if (nv > 0) mbar_drain(&bar[B_V_FULL + ((nv - 1) & 1)], ((nv - 1) >> 1) & 1);
+      for (; nkq < min(2, nch); nkq++) load_kq(nkq);
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- the chain's MMAs
-    if (lane == 0) {
-      bool ok = true;
-      for (int c = 0; c < nch && ok; c++) {
-        const int s = c & 1;
-        const uint32_t ph = (c >> 1) & 1;
-        uint8_t* t = base + kOffKQW + s * kTile;
-        const uint32_t dx = tmem + kColX + s * 128;
-        if (!(ok = mbar_wait(&bar[B_WQ_READY + s], ph, abort, err, kErrTimeoutFull) &&
-                   mbar_wait(&bar[B_U_DONE + s], ph, abort, err, kErrTimeoutFull) &&
-                   mbar_wait(&bar[B_S16_READY + s], ph, abort, err, kErrTimeoutFull)))
-          break;
-        tc_fence_after();
-        {  // [Gamma Q^; -W] S onto [0; U]: rows 0-63 Gamma Q^ S, rows 64-127 delta
-          const uint64_t ad = sw128_desc(t + 64 * 128), bd = sw128_mn_desc(base + kOffS16, 16384);
-#pragma unroll
-          for (int ks = 0; ks < 8; ks++)
-            tc_mma_f16(dx, ad + (uint64_t)((ks >> 2) * (kBox >> 4) + 2 * (ks & 3)), bd + (uint64_t)(128 * ks), kIdB, 1);
-        }
-        tc_commit(&bar[B_X_FULL + s]);
-        if (!(ok = mbar_wait(&bar[B_D_READY + s], ph, abort, err, kErrTimeoutFull))) break;
-        tc_fence_after();
-        {  // S += K^T Ds
-          const uint64_t ad = sw128_mn_desc(t, kBox), bd = sw128_mn_desc(t + 128 * 128, kBox);
-#pragma unroll
-          for (int ks = 0; ks < 4; ks++) tc_mma_f16(tmem + kColS, ad + (uint64_t)(128 * ks), bd + (uint64_t)(128 * ks), kIdS, 1);
-        }
-        tc_commit(&bar[B_S_FULL + s]);
-        {  // O = Gamma Q^ S + P delta (rows 0-63; the operand's rows 64-127 are whatever follows P)
-          const uint64_t ad = sw128_desc(base + (s ? kOffP1 : kOffP0)), bd = sw128_mn_desc(t + 64 * 128, kBox);
-#pragma unroll
-          for (int ks = 0; ks < 4; ks++) tc_mma_f16(dx, ad + (uint64_t)(2 * ks), bd + (uint64_t)(128 * ks), kIdB, 1);
-        }
-        tc_commit(&bar[B_O_FULL + s]);
-        tc_commit(&bar[B_KQ_EMPTY + s]);
-      }
-      tc_commit(&bar[B_END_CHAIN]);
-      mbar_drain(&bar[B_END_CHAIN], 0);
-    }
-  } else if (warp < 6) {
-    // ---------------------------------------------------------------- the chain
-    const int q4 = warp & 3;                       // TMEM lanes 32 q4 .. + 31
-    const int r = q4 * 32 + lane;                  // S: key row r; D_X: row r
-    const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+    if (warp == 2 && lane == 0) load_v(nv++);
     // the entry state into tensor memory (zeros without one)
     for (int cb = 0; cb < 4; cb++) {
       uint32_t v[32];
@@ -339,12 +282,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_wait_st();
     bool ok = true;
-    auto read_o = [&](int c) {  // O rows (D_X rows 0-63) of chunk c to global memory, then release D_X
+    // O rows (D_X rows 0-63, warps 0 and 1) of chunk c to global memory, then D_X[c & 1] is released;
+    // the MMAs of chunk c have all completed, so its tile takes chunk c + 2's k and q rows
+    auto read_o = [&](int c) {
       const int s = c & 1;
-      if (!(ok = mbar_wait_warp(&bar[B_O_FULL + s], (c >> 1) & 1, abort, err, kErrTimeoutAccum))) return;
-      tc_fence_after();
-      const int n = min(CH, L - c * CH);
-      if (q4 < 2) {
+      if (ok) ok = mbar_wait_warp(&bar[B_O_FULL + s], (c >> 1) & 1, abort, err, kErrTimeoutAccum);
+      if (ok && q4 < 2) {
+        tc_fence_after();
+        const int n = min(CH, L - c * CH);
         // tcgen05.ld and wait::ld are warp-collective (.sync.aligned): every lane of the warp executes
         // the same loads, and only the stores are limited to the chunk's rows
         float* dst = a.o + (size_t)(tok0 + c * CH + r) * H * DK + hd * DK;
@@ -361,52 +306,67 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (ok && warp == 0 && lane == 0 && c + 2 < nch) load_kq(nkq++);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_O_READ + s]);
     };
-    for (int c = 0; c < nch && ok; c++) {
+    for (int c = 0; c < nch; c++) {
       const int s = c & 1;
       const uint32_t ph = (c >> 1) & 1;
       uint8_t* t = base + kOffKQW + s * kTile;
+      const uint32_t dx = tmem + kColX + s * 128;
       // (1) the entry state S_{c-1}: its f16 copy (the operand of [Gamma Q^; -W] S), Gamma_C S back
-      if (c >= 1 && !(ok = mbar_wait_warp(&bar[B_S_FULL + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutAccum)))
-        break;
-      if (!(ok = mbar_wait_warp(&bar[B_G_READY + s], ph, abort, err, kErrTimeoutFull))) break;
-      tc_fence_after();
-      const float gc = __expf(sG[s * CH + CH - 1]);
-      for (int cb = 0; cb < 4; cb++) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lanes + kColS + cb * 32, v);
-        tc_wait_ld();
-        uint8_t* dst = base + kOffS16 + (cb >> 1) * 16384;
+      if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_S_FULL + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutAccum);
+      if (ok) ok = mbar_wait_warp(&bar[B_G_READY + s], ph, abort, err, kErrTimeoutFull);
+      if (ok) {
+        tc_fence_after();
+        const float gc = __expf(sG[s * CH + CH - 1]);
+        for (int cb = 0; cb < 4; cb++) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lanes + kColS + cb * 32, v);
+          tc_wait_ld();
+          uint8_t* dst = base + kOffS16 + (cb >> 1) * 16384;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          uint4 u;
-          u.x = pack_h2(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1]));
-          u.y = pack_h2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
-          u.z = pack_h2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
-          u.w = pack_h2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
-          *reinterpret_cast<uint4*>(dst + swz(r, (cb & 1) * 4 + j)) = u;
+          for (int j = 0; j < 4; j++) {
+            uint4 u;
+            u.x = pack_h2(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1]));
+            u.y = pack_h2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
+            u.z = pack_h2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
+            u.w = pack_h2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
+            *reinterpret_cast<uint4*>(dst + swz(r, (cb & 1) * 4 + j)) = u;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * gc);
+          tmem_st32(tmem + lanes + kColS + cb * 32, v);
         }
-#pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * gc);
-        tmem_st32(tmem + lanes + kColS + cb * 32, v);
+        tc_wait_st();
       }
-      tc_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_S16_READY + s]);
-      // (2) O of the previous chunk (its MMA was issued right after the state update just waited for)
-      if (c >= 1) {
-        read_o(c - 1);
-        if (!ok) break;
+      if (!__all_sync(0xffffffffu, ok)) *abort = 1;
+      chain_sync();
+      ok = ok && !*abort;
+      if (warp == 2) {  // [Gamma Q^; -W] S onto [0; U] (rows 0-63 Gamma Q^ S, rows 64-127 delta), then v of chunk c + 1
+        if (ok) ok = mbar_wait_warp(&bar[B_WQ_READY + s], ph, abort, err, kErrTimeoutFull);
+        if (ok) ok = mbar_wait_warp(&bar[B_U_DONE + s], ph, abort, err, kErrTimeoutFull);
+        if (ok && lane == 0) {
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(t + 64 * 128), bd = sw128_mn_desc(base + kOffS16, 16384);
+#pragma unroll
+          for (int ks = 0; ks < 8; ks++)
+            tc_mma_f16(dx, ad + (uint64_t)((ks >> 2) * (kBox >> 4) + 2 * (ks & 3)), bd + (uint64_t)(128 * ks), kIdB, 1);
+          tc_commit(&bar[B_X_FULL + s]);
+          if (c + 1 < nch) load_v(nv++);  // the v buffer is free: U of chunk c has completed
+        }
       }
-      // (3) delta = D_X rows 64-127: delta (f16, over Gamma Q^) and Ds = delta e^{G_C - G_i} (over -W)
-      if (!(ok = mbar_wait_warp(&bar[B_X_FULL + s], ph, abort, err, kErrTimeoutAccum))) break;
-      tc_fence_after();
-      if (q4 >= 2) {
+      // (2) O of the previous chunk (its MMA was issued right after the state update just waited for)
+      if (c >= 1) read_o(c - 1);
+      // (3) delta = D_X rows 64-127 (warps 2 and 3): delta (f16, over Gamma Q^) and Ds = delta e^{G_C - G_i}
+      // (over -W)
+      if (ok) ok = mbar_wait_warp(&bar[B_X_FULL + s], ph, abort, err, kErrTimeoutAccum);
+      if (ok && q4 >= 2) {
+        tc_fence_after();
         const int i = r - 64;
         const float sc = __expf(sG[s * CH + CH - 1] - sG[s * CH + i]);
         for (int cb = 0; cb < 4; cb++) {
@@ -432,10 +392,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_D_READY + s]);
+      if (!__all_sync(0xffffffffu, ok)) *abort = 1;
+      chain_sync();
+      ok = ok && !*abort;
+      if (warp == 2 && lane == 0 && ok) {  // S += K^T Ds, then O += [P; *] delta
+        tc_fence_after();
+        {
+          const uint64_t ad = sw128_mn_desc(t, kBox), bd = sw128_mn_desc(t + 128 * 128, kBox);
+#pragma unroll
+          for (int ks = 0; ks < 4; ks++) tc_mma_f16(tmem + kColS, ad + (uint64_t)(128 * ks), bd + (uint64_t)(128 * ks), kIdS, 1);
+        }
+        tc_commit(&bar[B_S_FULL + s]);
+        {  // the operand's rows 64-127 are whatever follows P
+          const uint64_t ad = sw128_desc(base + (s ? kOffP1 : kOffP0)), bd = sw128_mn_desc(t + 64 * 128, kBox);
+#pragma unroll
+          for (int ks = 0; ks < 4; ks++) tc_mma_f16(dx, ad + (uint64_t)(2 * ks), bd + (uint64_t)(128 * ks), kIdB, 1);
+        }
+        tc_commit(&bar[B_O_FULL + s]);
+      }
     }
-    if (ok) read_o(nch - 1);
+    read_o(nch - 1);
     // the final state
     if (ok && sout) {
       const int c = nch - 1;
@@ -453,11 +429,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // teardown: every MMA this group issued has completed, and no copy lands after the CTA has left
+    if (warp == 2 && lane == 0) {
+      tc_commit(&bar[B_END_CHAIN]);
+      mbar_drain(&bar[B_END_CHAIN], 0);
+      if (nv > 0) mbar_drain(&bar[B_V_FULL + ((nv - 1) & 1)], ((nv - 1) >> 1) & 1);
+    }
+    if (warp == 0 && lane == 0)
+      for (int c = max(0, nkq - 2); c < nkq; c++) mbar_drain(&bar[B_KQ_FULL + (c & 1)], (c >> 1) & 1);
   } else {
     // ---------------------------------------------------------------- the chunk preparation
-    const int pw = warp - 6;                  // 0..3
-    const int pt = threadIdx.x - 6 * 32;      // 0..127
-    const int q4 = warp & 3;                  // TMEM lanes 32 q4 .. + 31: warps 6, 7 -> Q rows; 8, 9 -> K rows
+    const int pw = warp - 4;                  // 0..7
+    const int pt = threadIdx.x - 4 * 32;      // 0..255
+    const int q4 = warp & 3;                  // TMEM lanes 32 q4 .. + 31: K rows for q4 0, 1; Q rows for 2, 3
+    const int colh = pw >> 2;                 // the half of the columns this warp takes of its lanes' rows
     const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
     float* sa = reinterpret_cast<float*>(base + kOffA);
     float* sx = reinterpret_cast<float*>(base + kOffX);
@@ -467,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the gates of chunk c (beta for threads 0-63, g for 64-127), loaded one chunk ahead
     auto gate = [&](int c) -> float {
       const int i = pt & 63;
-      if (c >= nch || c * CH + i >= L) return 0.0f;
+      if (pt >= 128 || c >= nch || c * CH + i >= L) return 0.0f;
       const long long t = tok0 + c * CH + i;
       return pt < 64 ? a.beta[t * H + hd] : a.g[t * H + hd];
     };
@@ -483,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // of them, chunk c - 2, came before its MMAs released the tile this chunk was loaded into)
       if (ok) ok = mbar_wait_warp(&bar[B_KQ_FULL + s], ph, abort, err, kErrTimeoutFull);
       if (pt < 64) sbeta[s * CH + pt] = gcur;
-      else sg[pt - 64] = gcur;
+      else if (pt < 128) sg[pt - 64] = gcur;
       prep_sync();
       if (pw == 0) {
         const float x0 = sg[2 * lane], x1 = sg[2 * lane + 1];
@@ -497,27 +482,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         sG[s * CH + 2 * lane] = before + x0;
         sG[s * CH + 2 * lane + 1] = sum;
       }
-      // (2) q^, k^ in place (rows 0-63 K, 64-127 Q; lane l: 4 values of one 64-column half)
+      // (2) q^, k^ in place: thread pt takes one 64-column half (pt & 1) of row pt >> 1 (rows 0-63 K,
+      // 64-127 Q); the two halves' sums of squares meet through one shuffle
       if (ok) {
-        const int hb = lane >> 4, pc = (lane & 15) >> 1, hh = lane & 1;
-#pragma unroll 1
-        for (int r0 = pw; r0 < 128; r0 += 32) {
-          uint2 raw[8];
+        const int row = pt >> 1, hb = pt & 1;
+        uint8_t* rp = t + hb * kBox;
+        uint4 raw[8];
 #pragma unroll
-          for (int u = 0; u < 8; u++)
-            raw[u] = *reinterpret_cast<const uint2*>(t + hb * kBox + swz(r0 + 4 * u, pc) + hh * 8);
+        for (int j = 0; j < 8; j++) raw[j] = *reinterpret_cast<const uint4*>(rp + swz(row, j));
+        float ss = 0.0f;
 #pragma unroll
-          for (int u = 0; u < 8; u++) {
-            const int row = r0 + 4 * u;
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&raw[u].x));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&raw[u].y));
-            const float ss = warp_sum(f0.x * f0.x + f0.y * f0.y + f1.x * f1.x + f1.y * f1.y);
-            const float sc = row < 64 ? rsqrtf(ss + 1e-6f) : rsqrtf(ss + 1e-6f) * qscale;
-            uint2 o;
-            o.x = pack_h2(f0.x * sc, f0.y * sc);
-            o.y = pack_h2(f1.x * sc, f1.y * sc);
-            *reinterpret_cast<uint2*>(t + hb * kBox + swz(row, pc) + hh * 8) = o;
+        for (int j = 0; j < 8; j++) {
+          const uint32_t* w = reinterpret_cast<const uint32_t*>(&raw[j]);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
           }
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        const float sc = row < 64 ? rsqrtf(ss + 1e-6f) : rsqrtf(ss + 1e-6f) * qscale;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          uint32_t* w = reinterpret_cast<uint32_t*>(&raw[j]);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+            w[e] = pack_h2(f.x * sc, f.y * sc);
+          }
+          *reinterpret_cast<uint4*>(rp + swz(row, j)) = raw[j];
         }
       }
       fence_proxy_async_smem();
@@ -535,52 +528,56 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit(&bar[B_DAP_FULL + s]);
         }
       }
-      // (3) A (K rows) and P (Q rows) from the products; Gamma Q^ over Q^
+      // (3) A (K rows) and P (Q rows) from the products, each warp 32 of the 64 columns of its lanes'
+      // rows; Gamma Q^ over Q^ (each warp one 64-column half)
       if (ok) ok = mbar_wait_warp(&bar[B_DAP_FULL + s], ph, abort, err, kErrTimeoutAccum);
       if (ok && q4 >= 2 && c >= 2)  // P[s] is free once the chain's P delta of chunk c - 2 has completed
         ok = mbar_wait_warp(&bar[B_O_FULL + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty);
       if (ok) {
         tc_fence_after();
-        uint32_t v[64];
-        tmem_ld32(tmem + lanes + kColDAP, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld32(tmem + lanes + kColDAP + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        uint32_t v[32];
+        tmem_ld32(tmem + lanes + kColDAP + 32 * colh, v);
         tc_wait_ld();
         const float* G = sG + s * CH;
+        const int j0 = 32 * colh;
         if (q4 < 2) {  // K row i
           const int i = q4 * 32 + lane;
           const float gi = G[i], bi = sbeta[s * CH + i];
 #pragma unroll
-          for (int j = 0; j < CH; j++) sa[i * LA + j] = j < i ? bi * __expf(gi - G[j]) * __uint_as_float(v[j]) : 0.0f;
-        } else {  // Q row i: P row i (f16), then Gamma_i q^_i in place
+          for (int jj = 0; jj < 32; jj++) {
+            const int j = j0 + jj;
+            sa[i * LA + j] = j < i ? bi * __expf(gi - G[j]) * __uint_as_float(v[jj]) : 0.0f;
+          }
+        } else {  // Q row i: its P columns (f16), then Gamma_i q^_i over one half of the row
           const int i = (q4 - 2) * 32 + lane;
           const float gi = G[i];
           uint8_t* pt_ = base + (s ? kOffP1 : kOffP0);
 #pragma unroll
-          for (int j8 = 0; j8 < 8; j8++) {
+          for (int j8 = 0; j8 < 4; j8++) {
             float p[8];
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-              const int j = j8 * 8 + e;
-              p[e] = j <= i ? __expf(gi - G[j]) * __uint_as_float(v[j]) : 0.0f;
+              const int j = j0 + j8 * 8 + e;
+              p[e] = j <= i ? __expf(gi - G[j]) * __uint_as_float(v[j8 * 8 + e]) : 0.0f;
             }
-            *reinterpret_cast<uint4*>(pt_ + swz(i, j8)) =
+            *reinterpret_cast<uint4*>(pt_ + swz(i, 4 * colh + j8)) =
                 make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
           }
           const float ga = __expf(gi);
+          uint8_t* qb = t + colh * kBox;
+          uint4 u[8];
 #pragma unroll
-          for (int hb = 0; hb < 2; hb++)
+          for (int j8 = 0; j8 < 8; j8++) u[j8] = *reinterpret_cast<const uint4*>(qb + swz(64 + i, j8));
 #pragma unroll
-            for (int j8 = 0; j8 < 8; j8++) {
-              uint4* qp = reinterpret_cast<uint4*>(t + hb * kBox + swz(64 + i, j8));
-              uint4 u = *qp;
-              uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+          for (int j8 = 0; j8 < 8; j8++) {
+            uint32_t* w = reinterpret_cast<uint32_t*>(&u[j8]);
 #pragma unroll
-              for (int e = 0; e < 4; e++) {
-                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-                w[e] = pack_h2(f.x * ga, f.y * ga);
-              }
-              *qp = u;
+            for (int e = 0; e < 4; e++) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+              w[e] = pack_h2(f.x * ga, f.y * ga);
             }
+            *reinterpret_cast<uint4*>(qb + swz(64 + i, j8)) = u[j8];
+          }
         }
       }
       tc_fence_before();
@@ -588,14 +585,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (4) T = (I + A)^-1
       tri_inverse(sa, sx, sy, pw, lane);
       // (5) T1 = T diag(beta Gamma), T2 = T diag(beta) (f16), once U of chunk c - 1 has read T2 (and W
-      // of chunk c - 1, issued before it, T1)
+      // of chunk c - 1, issued before it, T1); thread pt: row pt >> 2, columns 16 (pt & 3) ..
       if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
       if (ok) {
-        const int i = pt >> 1, j0 = (pt & 1) * 32;
+        const int i = pt >> 2, j0 = (pt & 3) * 16;
         const float* G = sG + s * CH;
         const float* be = sbeta + s * CH;
 #pragma unroll
-        for (int j8 = 0; j8 < 4; j8++) {
+        for (int j8 = 0; j8 < 2; j8++) {
           float t1[8], t2[8];
 #pragma unroll
           for (int e = 0; e < 8; e++) {
@@ -623,20 +620,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit(&bar[B_W_FULL + s]);
         }
       }
-      // (6) -W (D_X rows 0-63) over rows 128-191 of the tile
+      ok = __all_sync(0xffffffffu, ok);  // the issuing thread's warp agrees again before the warp-wide waits
+      // (6) -W (D_X rows 0-63) over rows 128-191 of the tile, each warp one 64-column half
       if (ok && q4 < 2) {
         ok = mbar_wait_warp(&bar[B_W_FULL + s], ph, abort, err, kErrTimeoutAccum);
         if (ok) {
           tc_fence_after();
           const int i = q4 * 32 + lane;
-          for (int cb = 0; cb < 4; cb++) {
+          uint8_t* box = t + colh * kBox;
+          for (int cb = 0; cb < 2; cb++) {
             uint32_t v[32];
-            tmem_ld32(dx + lanes + cb * 32, v);
+            tmem_ld32(dx + lanes + (2 * colh + cb) * 32, v);
             tc_wait_ld();
-            uint8_t* box = t + (cb >> 1) * kBox;
 #pragma unroll
             for (int j = 0; j < 4; j++)
-              *reinterpret_cast<uint4*>(box + swz(128 + i, (cb & 1) * 4 + j)) =
+              *reinterpret_cast<uint4*>(box + swz(128 + i, cb * 4 + j)) =
                   make_uint4(pack_h2(-__uint_as_float(v[8 * j]), -__uint_as_float(v[8 * j + 1])),
                              pack_h2(-__uint_as_float(v[8 * j + 2]), -__uint_as_float(v[8 * j + 3])),
                              pack_h2(-__uint_as_float(v[8 * j + 4]), -__uint_as_float(v[8 * j + 5])),
@@ -672,12 +670,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
   // the walk of an empty sequence: the final state is the initial one
-  if (nch == 0 && sout && warp >= 2 && warp < 6) {
+  if (nch == 0 && sout && warp < 4) {
     const int r = (warp & 3) * 32 + lane;
     for (int cv = 0; cv < DK; cv++) sout[(size_t)r * DK + cv] = sin ? sin[(size_t)r * DK + cv] : 0.0f;
   }

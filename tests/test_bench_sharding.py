@@ -29,12 +29,24 @@ def test_steps_are_partitions(bench, world):
     for step in range(4):
         parts = [bench.step_requests(step, r, world, per) for r in range(world)]
         flat = sorted(i for p in parts for i in p)
-        assert flat == [(step * world * per + j) % bench.N_REQUESTS for j in range(world * per)]
+        order = bench.sweep_order()
+        assert flat == sorted(order[(step * world * per + j) % bench.N_REQUESTS] for j in range(world * per))
         assert all(len(p) == per for p in parts)
 
 
 def test_one_rank_takes_the_step_in_order(bench):
-    assert bench.step_requests(3, 0, 1, 8) == list(range(24, 32))
+    assert bench.step_requests(3, 0, 1, 8) == bench.sweep_order()[24:32]
+
+
+def test_sweep_order_is_a_representative_permutation(bench):
+    """Every request once; the 160 requests of the default timed steps have the sweep's mean state
+    length within 1%."""
+    order = bench.sweep_order()
+    assert sorted(order) == list(range(bench.N_REQUESTS))
+    mean_all, _, _ = bench.sweep_stats()
+    state = lambda i: len(bench.request(i)[0])  # noqa: E731
+    sample = [state(i) for i in order[24:184]]
+    assert abs(sum(sample) / len(sample) - mean_all) < 0.01 * mean_all
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
