@@ -26,6 +26,12 @@ SD_DEV unsigned long long global_ns() {
 
 SD_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
+// The first 1024-byte aligned address at or after p, for p in shared memory. It is p plus an offset
+// (not an integer round trip) so that the compiler still knows the result, and every pointer made
+// from it, to be shared memory: it then emits shared loads and stores instead of generic ones, which
+// take the longer path through the L1 and the long scoreboard.
+SD_DEV uint8_t* smem_align1024(uint8_t* p) { return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u); }
+
 // ---------------------------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------------------------

@@ -96,9 +96,10 @@ struct sd_head {
 struct sd_engine {
   int device = 0;
   int num_sms = 148;
-  // the gated-delta layers on the fused tcgen05 scan (gdn_tc.cu); SD_GDN_KERNEL=legacy at engine
-  // creation selects the mma.sync scans (single-pass and two-phase) instead, for comparisons
-  bool gdn_tc = true;
+  // which scan the gated-delta layers take: 0 the faster by gdn_pick's estimate, 1 always the fused
+  // tcgen05 scan (gdn_tc.cu), 2 always the mma.sync scans (single-pass and two-phase); set once at
+  // engine creation from SD_GDN_KERNEL (unset, "tc" or "legacy"), for comparisons
+  int gdn_mode = 0;
   cudaStream_t stream = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   sd::Dims dm;
@@ -665,6 +666,20 @@ struct Fork {
   __half *kt, *vt;    // [hk][l][hd] K and V of the packed tokens
 };
 
+// Whether a gated-delta layer over `walks` (sequence, head) walks, the longest of max_chunks 64-token
+// chunks and chunks x heads chunk records in all, takes the fused tcgen05 scan rather than the
+// two-phase one. Estimates from B200 timings: the fused scan walks about 8.5 us per chunk, one CTA
+// per walk and SM, so a wave lasts its longest walk; the two-phase scan's preparation does about two
+// chunk records per SM each 21 us, then its walk takes about 4 us per chunk of the longest sequence.
+static bool gdn_pick_tc(const sd_engine* e, long long walks, long long max_chunks, long long records, bool two_phase_ok) {
+  if (e->gdn_mode) return e->gdn_mode == 1;
+  if (!two_phase_ok) return true;
+  const long long sms = std::max(1, e->num_sms);
+  const double fused = (double)((walks + sms - 1) / sms) * max_chunks * 8.5;
+  const double two_phase = (double)((records + 2 * sms - 1) / (2 * sms)) * 21.0 + max_chunks * 4.0;
+  return fused <= two_phase;
+}
+
 // The layer loop (src/engine.rs:446-522), launched on the engine's stream. With `fk`, the l tokens are
 // a batched fork's packed sequences (each at position p + its index within its sequence).
 int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork* fk = nullptr) {
@@ -713,7 +728,10 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
         // one chunk: the single-pass scan; longer: the two-phase scan (chunks in parallel, then the state walk);
         // packed sequences, each from its snapshot's state (or zeros): short ones with the single-pass
         // scan, long ones with the two-phase scan
-        if (e->gdn_tc) {  // the fused tcgen05 scan: one CTA per (sequence, head)
+        const long long max_chunks = fk ? (fk->max_len + 63) / 64 : (l + 63) / 64;
+        const bool use_tc = fk ? gdn_pick_tc(e, (long long)fk->nseq * d.h, max_chunks, (long long)fk->chunks * d.h, fk->two_phase)
+                               : gdn_pick_tc(e, d.h, max_chunks, max_chunks * d.h, l > 64);
+        if (use_tc) {  // the fused tcgen05 scan: one CTA per (sequence, head)
           sd::GdnTcArgs ga;
           ga.beta = e->beta, ga.g = e->decay, ga.o = e->of, ga.h = d.h, ga.err = e->d_err;
           int walks = d.h;
@@ -1336,7 +1354,7 @@ int sd_engine_create(const char* model_dir, int device, sd_engine** out) {
   auto* e = new sd_engine();
   e->device = device;
   e->num_sms = prop.multiProcessorCount;
-  if (const char* k = getenv("SD_GDN_KERNEL")) e->gdn_tc = strcmp(k, "legacy") != 0;
+  if (const char* k = getenv("SD_GDN_KERNEL")) e->gdn_mode = strcmp(k, "tc") == 0 ? 1 : strcmp(k, "legacy") == 0 ? 2 : 0;
   cudaSetDevice(device);
   if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess || cudaEventCreate(&e->ev0) != cudaSuccess ||
       cudaEventCreate(&e->ev1) != cudaSuccess) {

@@ -55,8 +55,8 @@ constexpr int LA = CH + 1;                            // row stride (floats) of 
 constexpr int kOffA = kOffT2 + 8192;                  // A (f32)
 constexpr int kOffX = kOffA + CH * LA * 4;            // T = (I + A)^-1 (f32)
 constexpr int kOffY = kOffX + CH * LA * 4;            // 6 x 16 x 9 floats of the inverse's scratch
-constexpr int kOffSmall = kOffY + 6 * 16 * 9 * 4;     // beta[2][64], G[2][64], g[64]
-constexpr int kOffBar = kOffSmall + 5 * CH * 4;
+constexpr int kOffSmall = kOffY + 6 * 16 * 9 * 4;     // beta[2][64], G[2][64], g[64], decay tables E[64], Gam[64], F[4][64]
+constexpr int kOffBar = kOffSmall + 11 * CH * 4;
 enum {
   B_KQ_FULL = 0,     // [2] the chunk's k and q rows landed (TMA bytes)
   B_V_FULL = 2,      // [2] the chunk's v rows landed
@@ -91,16 +91,22 @@ SD_DEV uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) <
 SD_DEV void prep_sync() { asm volatile("bar.sync %0, 256;" ::"n"(kPrepBar) : "memory"); }
 SD_DEV void chain_sync() { asm volatile("bar.sync %0, 128;" ::"n"(kChainBar) : "memory"); }
 
+// e^x as one ex2.approx.ftz (results below 2^-126 flush to zero). __expf without -ftz becomes a
+// longer sequence that keeps denormal results, and the preparation takes thousands per chunk.
+SD_DEV float fexp(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+  return y;
+}
+
 SD_DEV uint32_t pack_h2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-SD_DEV uint32_t tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
+// A tf32 operand: the f32 bits as they are (the tensor cores read the top 19 bits, so this truncates
+// the mantissa to 10 bits; T is rounded to f16 right after its products, which is coarser).
+SD_DEV uint32_t tf32(float x) { return __float_as_uint(x); }
 SD_DEV void mma1688_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -176,13 +182,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     gdn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap, const GdnTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = smem_align1024(smem_raw);
   uint64_t* bar = reinterpret_cast<uint64_t*>(base + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sbeta = reinterpret_cast<float*>(base + kOffSmall);  // [2][64]
   float* sG = sbeta + 2 * CH;                                  // [2][64]
   float* sg = sG + 2 * CH;                                     // [64]
+  // the chunk's decays, made once per chunk so that the A and P rows need few exponentials: with
+  // block b = i / 16 of row i and M_b = G_{16 b}, e^{G_i - G_j} = E_i F_{b,j} for j < 16 b, where
+  // E_i = e^{G_i - M_b} and F_{b,j} = e^{M_b - G_j} are both at most 1 (G never increases), so neither
+  // factor can overflow; pairs within one block take their own exponential. Gam_j = e^{G_j}.
+  float* sE = sg + CH;                                         // [64]
+  float* sGam = sE + CH;                                       // [64]
+  float* sF = sGam + CH;                                       // [4][64]
   int* err = a.err ? a.err : &g_gdn_tc_err;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = a.h;
@@ -321,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) ok = mbar_wait_warp(&bar[B_G_READY + s], ph, abort, err, kErrTimeoutFull);
       if (ok) {
         tc_fence_after();
-        const float gc = __expf(sG[s * CH + CH - 1]);
+        const float gc = fexp(sG[s * CH + CH - 1]);
         for (int cb = 0; cb < 4; cb++) {
           uint32_t v[32];
           tmem_ld32(tmem + lanes + kColS + cb * 32, v);
@@ -368,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && q4 >= 2) {
         tc_fence_after();
         const int i = r - 64;
-        const float sc = __expf(sG[s * CH + CH - 1] - sG[s * CH + i]);
+        const float sc = fexp(sG[s * CH + CH - 1] - sG[s * CH + i]);
         for (int cb = 0; cb < 4; cb++) {
           uint32_t v[32];
           tmem_ld32(tmem + lanes + kColX + s * 128 + cb * 32, v);
@@ -501,15 +514,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-        const float sc = row < 64 ? rsqrtf(ss + 1e-6f) : rsqrtf(ss + 1e-6f) * qscale;
+        // the scale in f16 and the products on the f16 pipe (one rounding each, as in f32; it keeps
+        // the f32 -> f16 conversions, which share a narrow pipe with the exponentials, to one per row)
+        const __half2 sc = __float2half2_rn(row < 64 ? rsqrtf(ss + 1e-6f) : rsqrtf(ss + 1e-6f) * qscale);
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-          uint32_t* w = reinterpret_cast<uint32_t*>(&raw[j]);
+          __half2* w = reinterpret_cast<__half2*>(&raw[j]);
 #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-            w[e] = pack_h2(f.x * sc, f.y * sc);
-          }
+          for (int e = 0; e < 4; e++) w[e] = __hmul2(w[e], sc);
           *reinterpret_cast<uint4*>(rp + swz(row, j)) = raw[j];
         }
       }
@@ -528,6 +540,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit(&bar[B_DAP_FULL + s]);
         }
       }
+      {  // the decay tables (beside the product)
+        const float* G = sG + s * CH;
+        const int b4 = pt >> 6, j = pt & 63;
+        sF[pt] = j < 16 * b4 ? fexp(G[16 * b4] - G[j]) : 0.0f;
+        if (pt < 64) sE[pt] = fexp(G[pt] - G[pt & ~15]);
+        else if (pt < 128) sGam[pt - 64] = fexp(G[pt - 64]);
+      }
+      prep_sync();
       // (3) A (K rows) and P (Q rows) from the products, each warp 32 of the 64 columns of its lanes'
       // rows; Gamma Q^ over Q^ (each warp one 64-column half)
       if (ok) ok = mbar_wait_warp(&bar[B_DAP_FULL + s], ph, abort, err, kErrTimeoutAccum);
@@ -540,42 +560,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_wait_ld();
         const float* G = sG + s * CH;
         const int j0 = 32 * colh;
-        if (q4 < 2) {  // K row i
-          const int i = q4 * 32 + lane;
-          const float gi = G[i], bi = sbeta[s * CH + i];
+        // G of this warp's 32 columns into registers first: the stores below go to shared memory too,
+        // and loads interleaved with them could not be moved ahead of them
+        float gj[32];
 #pragma unroll
-          for (int jj = 0; jj < 32; jj++) {
-            const int j = j0 + jj;
-            sa[i * LA + j] = j < i ? bi * __expf(gi - G[j]) * __uint_as_float(v[jj]) : 0.0f;
+        for (int j4 = 0; j4 < 8; j4++) {
+          const float4 f = *reinterpret_cast<const float4*>(G + j0 + 4 * j4);
+          gj[4 * j4] = f.x, gj[4 * j4 + 1] = f.y, gj[4 * j4 + 2] = f.z, gj[4 * j4 + 3] = f.w;
+        }
+        // the decays of row i's 32 columns j (two 16-column blocks): E_i F_{b,j} in the blocks before
+        // row i's, e^{G_i - G_j} in its own (the only exponentials), zero after it
+        const int i = (q4 & 1) * 32 + lane, bi_ = i >> 4;
+        const float gi = G[i], ei = sE[i];
+        float dec[32];
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+          const int bj = (j0 >> 4) + hf;
+          if (bj < bi_) {
+#pragma unroll
+            for (int e = 0; e < 16; e++) dec[16 * hf + e] = ei * sF[bi_ * CH + 16 * bj + e];
+          } else if (bj == bi_) {
+#pragma unroll
+            for (int e = 0; e < 16; e++) dec[16 * hf + e] = 16 * bj + e <= i ? fexp(gi - gj[16 * hf + e]) : 0.0f;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; e++) dec[16 * hf + e] = 0.0f;
           }
+        }
+        if (q4 < 2) {  // K row i
+          const float bi = sbeta[s * CH + i];
+          float av[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; jj++) av[jj] = j0 + jj < i ? bi * dec[jj] * __uint_as_float(v[jj]) : 0.0f;
+#pragma unroll
+          for (int jj = 0; jj < 32; jj++) sa[i * LA + j0 + jj] = av[jj];
         } else {  // Q row i: its P columns (f16), then Gamma_i q^_i over one half of the row
-          const int i = (q4 - 2) * 32 + lane;
-          const float gi = G[i];
           uint8_t* pt_ = base + (s ? kOffP1 : kOffP0);
 #pragma unroll
           for (int j8 = 0; j8 < 4; j8++) {
             float p[8];
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-              const int j = j0 + j8 * 8 + e;
-              p[e] = j <= i ? __expf(gi - G[j]) * __uint_as_float(v[j8 * 8 + e]) : 0.0f;
-            }
+            for (int e = 0; e < 8; e++) p[e] = dec[j8 * 8 + e] * __uint_as_float(v[j8 * 8 + e]);
             *reinterpret_cast<uint4*>(pt_ + swz(i, 4 * colh + j8)) =
                 make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
           }
-          const float ga = __expf(gi);
+          const __half2 ga = __float2half2_rn(sGam[i]);  // Gamma_i (below f16's range: zero, as its terms)
           uint8_t* qb = t + colh * kBox;
           uint4 u[8];
 #pragma unroll
           for (int j8 = 0; j8 < 8; j8++) u[j8] = *reinterpret_cast<const uint4*>(qb + swz(64 + i, j8));
 #pragma unroll
           for (int j8 = 0; j8 < 8; j8++) {
-            uint32_t* w = reinterpret_cast<uint32_t*>(&u[j8]);
+            __half2* w = reinterpret_cast<__half2*>(&u[j8]);
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-              w[e] = pack_h2(f.x * ga, f.y * ga);
-            }
+            for (int e = 0; e < 4; e++) w[e] = __hmul2(w[e], ga);
             *reinterpret_cast<uint4*>(qb + swz(64 + i, j8)) = u[j8];
           }
         }
@@ -589,17 +627,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
       if (ok) {
         const int i = pt >> 2, j0 = (pt & 3) * 16;
-        const float* G = sG + s * CH;
         const float* be = sbeta + s * CH;
+        float tv[16], bj[16], gj[16];  // loaded before any store (see the A and P loops)
+#pragma unroll
+        for (int e = 0; e < 16; e++) tv[e] = j0 + e <= i ? sx[i * LA + j0 + e] : 0.0f;
+#pragma unroll
+        for (int j4 = 0; j4 < 4; j4++) {
+          const float4 f = *reinterpret_cast<const float4*>(be + j0 + 4 * j4);
+          const float4 h = *reinterpret_cast<const float4*>(sGam + j0 + 4 * j4);
+          bj[4 * j4] = f.x, bj[4 * j4 + 1] = f.y, bj[4 * j4 + 2] = f.z, bj[4 * j4 + 3] = f.w;
+          gj[4 * j4] = h.x, gj[4 * j4 + 1] = h.y, gj[4 * j4 + 2] = h.z, gj[4 * j4 + 3] = h.w;
+        }
 #pragma unroll
         for (int j8 = 0; j8 < 2; j8++) {
           float t1[8], t2[8];
 #pragma unroll
           for (int e = 0; e < 8; e++) {
-            const int j = j0 + j8 * 8 + e;
-            const float tv = j <= i ? sx[i * LA + j] : 0.0f;
-            t2[e] = tv * be[j];
-            t1[e] = t2[e] * __expf(G[j]);
+            const int k = j8 * 8 + e;
+            t2[e] = tv[k] * bj[k];
+            t1[e] = t2[e] * gj[k];  // Gamma_j
           }
           const int pc = (j0 >> 3) + j8;
           *reinterpret_cast<uint4*>(base + kOffT1 + swz(i, pc)) =
