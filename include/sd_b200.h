@@ -110,6 +110,14 @@ int sd_forward_dev(sd_engine* e, const uint32_t* ids_dev, int32_t n_ids, const i
                    const sd_snapshot* cache, int32_t keep, float* hidden_dev, sd_snapshot** snapshot_out);
 /* Waits for the engine's queued work; returns the first error a kernel reported since the last call. */
 int sd_engine_synchronize(sd_engine* e);
+/* A self-test of the failure path that no valid input reaches (this call has no counterpart in the
+ * reference, which returns device errors as `Err`, src/engine.rs:648-651): on the engine's stream, one
+ * warp of a small kernel waits on a barrier phase that nothing completes and gives up after limit_us
+ * microseconds (1..1000000), recording a timeout in the engine's error word and setting its CTA's abort
+ * flag, while a second warp waiting with the kernels' full 2 s limit leaves on that flag, as every
+ * warp-specialised kernel of the library does. Nothing faults; the call returns SD_ERR_KERNEL with the
+ * timeout's message, as a forward whose kernel gave up would, and the engine stays usable. */
+int sd_engine_selftest_wait(sd_engine* e, int32_t limit_us);
 /* The engine's CUDA stream (a cudaStream_t), for callers that order their own work after it. */
 void* sd_engine_stream(const sd_engine* e);
 /* Kernels of this library the engine has launched since it was created. */
@@ -266,6 +274,14 @@ int32_t sd_gdn_noalloc_max_tokens(int32_t h);
  * layout, made from the reference layout on the device: q_dev [n][k/32][16 bytes], s_dev [n][k/32] f16.
  * `interleave` stores rows (j, n/2 + j) next to each other (gate_up for the fused SwiGLU). */
 int sd_qweight_create(const void* q_dev, const void* s_dev, int32_t n, int32_t k, int32_t interleave, sd_qweight** out);
+/* sd_qweight_create for the reference's other symmetric formats (`src/kernels.rs:545-586`, served there by
+ * `matmul_gemv`): bits 2, 3 or 4 (q_dev [n][k/32][4 * bits bytes]: int4 as 4 words of 8 nibbles, int2 as 2
+ * words of 16 two-bit fields, int3 as those 2 words plus a word of high bits), one f16 scale per `group`
+ * weights (a multiple of 32) indexed by the global block (row * k/32 + block) / (group / 32). The weight is
+ * repacked into the int4 tile layout with the same values ((q - 2^(bits-1)) * scale); asymmetric weights
+ * are not supported. */
+int sd_qweight_create_format(const void* q_dev, const void* s_dev, int32_t n, int32_t k, int32_t bits, int32_t group,
+                             int32_t interleave, sd_qweight** out);
 void sd_qweight_free(sd_qweight* w);
 
 /* `matmul_gemv`/`matmul_tiled`/`matmul_coop` (`src/kernels.rs:590-804`): y_dev[m][ldy] =

@@ -65,26 +65,33 @@ SD_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // another thread of the CTA has given up (*abort set): records `code` in *err and returns false. Each
 // poll sleeps in hardware until the phase completes (or kSuspendNs), then the clock and the abort flag
 // are read.
-SD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+SD_DEV bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       *abort = 1;
       atomicCAS(err, 0, code);
       return false;
     }
   }
 }
+SD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+  return mbar_wait_for(bar, parity, abort, err, code, kWaitLimitNs);
+}
 
 // mbar_wait for a whole warp: every lane polls (one try_wait instruction for the warp), so each
 // lane has the barrier's acquire ordering. The lanes leave together: a lane that gave up (timeout or
 // abort) makes the whole warp give up.
-SD_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
-  const bool ok = mbar_wait(bar, parity, abort, err, code);
+SD_DEV bool mbar_wait_warp_for(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code,
+                               unsigned long long limit_ns) {
+  const bool ok = mbar_wait_for(bar, parity, abort, err, code, limit_ns);
   return __all_sync(0xffffffffu, ok);
+}
+SD_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+  return mbar_wait_warp_for(bar, parity, abort, err, code, kWaitLimitNs);
 }
 
 // Waits (bounded, ignoring the abort flag) for a phase that asynchronous copies or MMAs this CTA

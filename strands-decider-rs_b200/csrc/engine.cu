@@ -445,11 +445,15 @@ int load_engine(sd_engine* e, const std::string& dir) {
     const int group = (int)(t->get("group") ? t->at("group").integer() : 32);
     const bool asym = t->get("asym") ? t->at("asym").boolean() : false;
     const int n = (int)t->at("N").integer(), k = (int)t->at("K").integer();
-    if (bits != 4 || group != 32 || asym || k % 64 || (interleave && n % 2)) {
-      if (rc == SD_OK) rc = e->fail(SD_ERR_FORMAT, "%s: only int4 group-32 symmetric matmul weights are supported", name.c_str());
+    if (bits < 2 || bits > 4 || group < 32 || group % 32 || asym || k % 64 || (interleave && n % 2)) {
+      if (rc == SD_OK)
+        rc = e->fail(SD_ERR_FORMAT,
+                     "%s: matmul weights must be symmetric int2, int3 or int4 with groups of a multiple of 32 and K a "
+                     "multiple of 64 (asymmetric weights are not supported)",
+                     name.c_str());
       return;
     }
-    cudaError_t ce = sd::repack_weight(q, reinterpret_cast<const __half*>(s), n, k, interleave, w, e->stream);
+    cudaError_t ce = sd::repack_weight(q, reinterpret_cast<const __half*>(s), n, k, interleave, w, e->stream, bits, group);
     if (ce != cudaSuccess && rc == SD_OK) rc = e->fail(SD_ERR_CUDA, "%s: %s", name.c_str(), cudaGetErrorString(ce));
   };
   for (int i = 0; i < e->n_layers; i++) {
@@ -1625,6 +1629,17 @@ int sd_engine_synchronize(sd_engine* e) {
   return sync_engine(e);
 }
 
+int sd_engine_selftest_wait(sd_engine* e, int32_t limit_us) {
+  if (!e) return SD_ERR_INVALID;
+  if (limit_us < 1 || limit_us > 1000000) return e->fail(SD_ERR_INVALID, "selftest: limit_us must be 1..1000000");
+  cudaSetDevice(e->device);
+  int rc = sync_engine(e);  // earlier work first, so that its errors stay its own
+  if (rc != SD_OK) return rc;
+  const cudaError_t ce = sd::launch_wait_probe(e->d_err, (unsigned long long)limit_us * 1000ull, e->stream);
+  if (ce != cudaSuccess) return e->fail(SD_ERR_CUDA, "selftest: %s", cudaGetErrorString(ce));
+  return sync_engine(e);
+}
+
 void* sd_engine_stream(const sd_engine* e) { return e ? (void*)e->stream : nullptr; }
 int64_t sd_engine_launches(const sd_engine* e) { return e ? e->launches : 0; }
 
@@ -1954,13 +1969,19 @@ int sd_gdn(const void* q, const void* k, int32_t qk_stride, const void* v, int32
 size_t sd_gdn_scratch_bytes(int32_t l, int32_t h) { return l > 0 && h > 0 ? sd::gdn_two_phase_scratch(l, h) : 0; }
 
 int sd_qweight_create(const void* q, const void* s, int32_t n, int32_t k, int32_t interleave, sd_qweight** out) {
-  if (!q || !s || !out || n <= 0 || k <= 0 || k % 64 || (interleave && n % 2)) {
-    set_global_error("sd_qweight_create: bad arguments (k must be a multiple of 64)");
+  return sd_qweight_create_format(q, s, n, k, 4, 32, interleave, out);
+}
+
+int sd_qweight_create_format(const void* q, const void* s, int32_t n, int32_t k, int32_t bits, int32_t group,
+                             int32_t interleave, sd_qweight** out) {
+  if (!q || !s || !out || n <= 0 || k <= 0 || k % 64 || (interleave && n % 2) || bits < 2 || bits > 4 || group < 32 ||
+      group % 32) {
+    set_global_error("sd_qweight_create: bad arguments (k a multiple of 64; bits 2, 3 or 4; group a multiple of 32)");
     return SD_ERR_INVALID;
   }
   auto w = std::make_unique<sd_qweight>();
   cudaGetDevice(&w->device);
-  cudaError_t ce = sd::repack_weight((const uint8_t*)q, (const __half*)s, n, k, interleave != 0, &w->w, nullptr);
+  cudaError_t ce = sd::repack_weight((const uint8_t*)q, (const __half*)s, n, k, interleave != 0, &w->w, nullptr, bits, group);
   if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
   if (ce != cudaSuccess) return op_result(ce, "sd_qweight_create");
   *out = w.release();

@@ -431,14 +431,28 @@ __global__ void gemm_finish(const float* __restrict__ ws, int splits, int M, int
   }
 }
 
-// Reference layout (n rows of k/32 blocks of 16 bytes; scales [n][k/32]) -> tile layout
-// [npad/128][k/64][2048 code bytes of k-group 0 (16 per row) + 2048 of k-group 1 + 512 scale bytes
-// (2 per row)], so that 32 consecutive rows read by a warp are contiguous, with the nibbles of each
-// 8-element word reordered to (even elements low half, odd elements high half). `interleave` maps output row 2j
-// to source row j and 2j+1 to source row n/2 + j (gate_up: gate j next to up j).
+// Reference layout -> tile layout. The reference stores each row as k/32 blocks of 32 codes of `bits`
+// bits (src/kernels.rs:545-586: int4 as 4 words of 8 nibbles; int2 as 2 words of 16 two-bit fields;
+// int3 as those 2 words for the low two bits and a third word for the high bits) with one f16 scale
+// per `group` weights, taken by the global block index (row * k/32 + block) / (group / 32). A
+// symmetric code q means (q - 2^(bits-1)) * scale; as the int4 code q + 8 - 2^(bits-1) (0..15) it means
+// the same value under the int4 rule (code - 8) * scale, and each 32-block gets its own copy of its
+// group's scale, so every symmetric format becomes the GEMM's one format without changing a value.
+// Tile layout: [npad/128][k/64][2048 code bytes of k-group 0 (16 per row) + 2048 of k-group 1 + 512
+// scale bytes (2 per row)], so that 32 consecutive rows read by a warp are contiguous, with the nibbles
+// of each 8-element word reordered to (even elements low half, odd elements high half). `interleave`
+// maps output row 2j to source row j and 2j+1 to source row n/2 + j (gate_up: gate j next to up j).
+SD_DEV uint32_t code_at(const uint8_t* blk, int bits, int e) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(blk);
+  if (bits == 4) return (w[e >> 3] >> (4 * (e & 7))) & 15u;
+  uint32_t c = (w[e >> 4] >> (2 * (e & 15))) & 3u;
+  if (bits == 3) c |= ((w[2] >> e) & 1u) << 2;
+  return c;
+}
 __global__ void repack_q4(const uint8_t* __restrict__ q, const __half* __restrict__ s, int n, int k, int npad, int interleave,
-                          uint8_t* __restrict__ out) {
-  const int KT = k / kBK;
+                          int bits, int group, uint8_t* __restrict__ out) {
+  const int KT = k / kBK, nb = k / 32, bb = 4 * bits, gpb = group / 32;
+  const uint32_t shift = 8u - (1u << (bits - 1));
   const int64_t total = (int64_t)npad * KT;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
     const int row = (int)(idx / KT), kt = (int)(idx % KT);
@@ -453,19 +467,20 @@ __global__ void repack_q4(const uint8_t* __restrict__ q, const __half* __restric
       dsc[0] = dsc[1] = __float2half(0.0f);
       continue;
     }
-    const uint32_t* sw = reinterpret_cast<const uint32_t*>(q + ((size_t)src * (k / 32) + 2 * kt) * 16);
-    for (int i = 0; i < 8; i++) {
-      const uint32_t w = sw[i];
-      uint32_t o = 0;
-      for (int e = 0; e < 8; e++) {
-        const uint32_t nib = (w >> (4 * e)) & 15u;
-        const int pos = (e & 1) ? (4 + (e >> 1)) : (e >> 1);
-        o |= nib << (4 * pos);
+    for (int hb = 0; hb < 2; hb++) {  // the two 32-blocks of this k-tile
+      const size_t blk = (size_t)src * nb + 2 * kt + hb;
+      const uint8_t* bp = q + blk * bb;
+      for (int i = 0; i < 4; i++) {
+        uint32_t o = 0;
+        for (int e = 0; e < 8; e++) {
+          const uint32_t c4 = code_at(bp, bits, 8 * i + e) + shift;
+          const int pos = (e & 1) ? (4 + (e >> 1)) : (e >> 1);
+          o |= c4 << (4 * pos);
+        }
+        (hb ? dst1 : dst0)[i] = o;
       }
-      (i < 4 ? dst0 : dst1)[i & 3] = o;
+      dsc[hb] = s[blk / gpb];
     }
-    dsc[0] = s[(size_t)src * (k / 32) + 2 * kt];
-    dsc[1] = s[(size_t)src * (k / 32) + 2 * kt + 1];
   }
 }
 
@@ -656,7 +671,9 @@ cudaError_t preload_gemm() {
   return cudaFuncGetAttributes(&a, repack_q4);
 }
 
-cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool interleave, QWeight* out, cudaStream_t st) {
+cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool interleave, QWeight* out, cudaStream_t st,
+                          int bits, int group) {
+  if ((bits != 2 && bits != 3 && bits != 4) || group < 32 || group % 32) return cudaErrorInvalidValue;
   out->n = n;
   out->k = k;
   out->npad = (n + kBM - 1) / kBM * kBM;
@@ -666,7 +683,7 @@ cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool 
   if (e != cudaSuccess) return e;
   out->bytes = bytes;
   const int64_t total = (int64_t)out->npad * (k / kBK);
-  repack_q4<<<(int)std::min<int64_t>((total + 255) / 256, 8192), 256, 0, st>>>(q, s, n, k, out->npad, interleave ? 1 : 0,
+  repack_q4<<<(int)std::min<int64_t>((total + 255) / 256, 8192), 256, 0, st>>>(q, s, n, k, out->npad, interleave ? 1 : 0, bits, group,
                                                                                out->tiles);
   return cudaGetLastError();
 }

@@ -596,6 +596,31 @@ cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const
   return cudaGetLastError();
 }
 
+// A self-test of the kernels' failure path, which no input can reach: warp 0 waits on an mbarrier
+// phase that nothing completes, with a short limit, and gives up (the error code into *err, the CTA's
+// abort flag set), while warp 1 waits on another such phase with the kernels' full 2 s limit and must
+// leave as soon as it sees the abort flag, as every role of the tcgen05 kernels does. Nothing faults
+// and nothing is left waiting: the kernel returns and the host reads the code.
+__global__ void wait_probe_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ uint64_t bar[2];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) mbar_wait_warp_for(&bar[0], 0, &abort_flag, err, kErrTimeoutFull, limit_ns);
+  else mbar_wait_warp(&bar[1], 0, &abort_flag, err, kErrTimeoutEmpty);
+  __syncthreads();
+}
+
+cudaError_t launch_wait_probe(int* err, unsigned long long limit_ns, cudaStream_t st) {
+  wait_probe_kernel<<<1, 64, 0, st>>>(err, limit_ns);
+  return cudaGetLastError();
+}
+
 // Loads the row-wise kernels on the current device (see preload_gemm).
 cudaError_t preload_kernels() {
   cudaFuncAttributes a;

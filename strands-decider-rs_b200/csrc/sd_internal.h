@@ -32,7 +32,10 @@ struct QWeight {
   bool interleaved = false;
 };
 
-cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool interleave, QWeight* out, cudaStream_t st);
+// q, s in the reference's layout: `bits` (2, 3 or 4) bit symmetric codes, one f16 scale per `group`
+// weights (a multiple of 32); every format becomes the int4 tile layout, values unchanged.
+cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool interleave, QWeight* out, cudaStream_t st,
+                          int bits = 4, int group = 32);
 void gemm_plan(const QWeight& w, int M, int num_sms, int* bn, int* splits, int* kps);
 // y[M][ldy] = act[M][K] W^T, or SwiGLU of interleaved gate/up rows into y[M][N/2] when silu; ws is
 // the f32 split-K workspace (M * N floats; smaller disables split-K); *nlaunch gets the kernel count.
@@ -132,6 +135,8 @@ cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff
 cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,
                            int lt, const Dims& dm, const int* tpos, __half* q, __half* kc, __half* vc, cudaStream_t st);
 cudaError_t launch_trace(const float* x, const __half* y, int n, float* out, cudaStream_t st);
+// the failure path's self-test: a bounded wait that runs out after limit_ns (see kernels.cu)
+cudaError_t launch_wait_probe(int* err, unsigned long long limit_ns, cudaStream_t st);
 cudaError_t launch_add_bias(__half* y, const float* bias, int l, int d, cudaStream_t st);
 
 // attn.cu: causal GQA attention with the sigmoid output gate (src/kernels.rs:453-541).

@@ -84,6 +84,8 @@ def lib() -> C.CDLL:
         L.sd_gdn_scratch_bytes.restype = C.c_size_t
         L.sd_gdn_scratch_bytes.argtypes = [i32, i32]
         L.sd_qweight_create.argtypes = [vp, vp, i32, i32, i32, C.POINTER(vp)]
+        L.sd_engine_selftest_wait.argtypes = [vp, i32]
+        L.sd_qweight_create_format.argtypes = [vp, vp, i32, i32, i32, i32, i32, C.POINTER(vp)]
         L.sd_qweight_free.argtypes = [vp]
         L.sd_matmul.argtypes = [vp, vp, i32, vp, i32, i32, vp, C.c_size_t, vp]
         L.sd_decider_load.argtypes = [cp, C.c_int, C.POINTER(vp)]
@@ -306,6 +308,10 @@ class Engine:
                                     int(keep), hidden_dev, C.byref(snap)), "sd_forward_dev", self._h)
         return Snapshot(snap.value) if keep else None
 
+    def selftest_wait(self, limit_us: int):
+        """`sd_engine_selftest_wait`: a bounded wait that runs out on purpose; raises the kernel error."""
+        _check(lib().sd_engine_selftest_wait(self._h, limit_us), "selftest", self._h)
+
     def synchronize(self):
         _check(lib().sd_engine_synchronize(self._h), "sd_engine_synchronize", self._h)
 
@@ -421,9 +427,12 @@ def gdn_noalloc_max_tokens(h: int) -> int:
 
 
 class QWeight:
-    def __init__(self, q_dev: int, s_dev: int, n: int, k: int, interleave: bool = False):
+    def __init__(self, q_dev: int, s_dev: int, n: int, k: int, interleave: bool = False, bits: int = 4, group: int = 32):
+        """A weight in the reference's block-quantized layout (symmetric int2/int3/int4, one f16 scale per
+        `group` weights), repacked for the GEMM (`sd_qweight_create_format`)."""
         h = C.c_void_p()
-        _check(lib().sd_qweight_create(q_dev, s_dev, n, k, int(interleave), C.byref(h)), "sd_qweight_create")
+        _check(lib().sd_qweight_create_format(q_dev, s_dev, n, k, bits, group, int(interleave), C.byref(h)),
+               "sd_qweight_create")
         self._h = h.value
         self.n, self.k = n, k
 

@@ -255,10 +255,10 @@ class _ShardWriter:
         self.tensors[name] = t
         self.off += len(raw)
 
-    def add_matmul(self, rng, name: str, n: int, k: int, std: float, bits: int = 4):
-        packed, scales = _quant_tensor(rng, n, k, bits, std)
-        self.add(f"{name}.q", packed, N=n, K=k, bits=bits, group=32, asym=False)
-        self.add(f"{name}.s", scales, N=n, K=k, bits=bits, group=32, asym=False)
+    def add_matmul(self, rng, name: str, n: int, k: int, std: float, bits: int = 4, group: int = 32):
+        packed, scales = _quant_tensor(rng, n, k, bits, std, group=group)
+        self.add(f"{name}.q", packed, N=n, K=k, bits=bits, group=group, asym=False)
+        self.add(f"{name}.s", scales, N=n, K=k, bits=bits, group=group, asym=False)
 
     def close(self) -> int:
         self.f.close()
@@ -266,7 +266,8 @@ class _ShardWriter:
 
 
 def write_synthetic(path: str, seed: int = 0, n_layers: int = PROD_LAYERS, vocab: int = PROD_VOCAB,
-                    embed_bits: int = 3, embed_u8: bool = False, layer_types: list | None = None) -> dict:
+                    embed_bits: int = 3, embed_u8: bool = False, layer_types: list | None = None,
+                    matmul_formats: list | None = None) -> dict:
     """Writes a complete model directory with seeded random-init weights in the reference's format.
 
     The dims are the production ones (:data:`PROD`); ``n_layers``/``vocab`` shrink test models. The
@@ -289,6 +290,14 @@ def write_synthetic(path: str, seed: int = 0, n_layers: int = PROD_LAYERS, vocab
         return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
 
     sw = _ShardWriter(os.path.join(path, "weights.0.bin"))
+    if matmul_formats:  # (bits, group) of the layer matmuls, in turn (the reference's other formats)
+        fmts = iter(matmul_formats * 1000)
+        plain_add = sw.add_matmul
+
+        def add_fmt(rng_, name, n, k, std):
+            bits, group = next(fmts)
+            plain_add(rng_, name, n, k, std, bits=bits, group=group)
+        sw.add_matmul = add_fmt
     for li, kind in enumerate(types):
         pre = f"layers.{li}."
         sw.add(pre + "in_norm", norm_w(d))
