@@ -291,6 +291,14 @@ void sd_qweight_free(sd_qweight* w);
 int sd_matmul(const sd_qweight* w, const void* act_dev, int32_t m, void* y_dev, int32_t ldy, int32_t silu, void* ws_dev,
               size_t ws_bytes, void* stream);
 
+/* The standalone calls (sd_gdn, sd_attention*, sd_matmul) return once their kernels are queued; a
+ * kernel that gave up (one of its bounded waits ran out, 2 s) records an error code on the device
+ * instead of faulting. sd_op_status synchronises `stream`, reads and clears those codes on the
+ * current device and returns SD_ERR_KERNEL (message: which call, which code) if any was set, else
+ * SD_OK. No counterpart in the reference (its kernels have no such waits). The engine's calls check
+ * their own error word and need no sd_op_status. */
+int sd_op_status(void* stream);
+
 /* `decode_scales` (`src/model.rs:219-236`) on the device: src_dev holds n 4-byte row headers (m as
  * fp16 bits, j as u16) then n rows of g codes (`sign << 7 | k`); dst_dev gets [n][g] fp16 with
  * |scale| = fp16(f32(m 2^(-k j / 4096))), the power in f64 from a host table as the reference builds

@@ -396,4 +396,11 @@ cudaError_t launch_attention_tc(const __half* q, int qrows, const __half* k, con
   return cudaGetLastError();
 }
 
+cudaError_t take_attn_tc_err(int* code) {
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_attn_tc_err, sizeof(int));
+  const int zero = 0;
+  if (e == cudaSuccess && *code != 0) e = cudaMemcpyToSymbol(g_attn_tc_err, &zero, sizeof(int));
+  return e;
+}
+
 }  // namespace sd

@@ -1937,9 +1937,9 @@ int sd_gdn(const void* q, const void* k, int32_t qk_stride, const void* v, int32
   cudaStream_t st = (cudaStream_t)stream;
   if (algo == 0 && in_f16) {
     // the fused tcgen05 scan: its TMA reads need 16-byte aligned rows and sequences
-    if ((size_t)v % 16 || (size_t)q % 16 || (size_t)k % 16 || qk_stride % 8 || v_stride % 8 || seq_qk % 8 || seq_v % 8 ||
-        (batch > 1 && (seq_qk < (int64_t)l * qk_stride || seq_v < (int64_t)l * v_stride))) {
-      set_global_error("sd_gdn: the tcgen05 scan needs 16-byte aligned q/k/v, strides that are multiples of 8 elements "
+    if ((size_t)v % 16 || (size_t)q % 16 || (size_t)k % 16 || (size_t)o % 16 || qk_stride % 8 || v_stride % 8 || seq_qk % 8 ||
+        seq_v % 8 || (batch > 1 && (seq_qk < (int64_t)l * qk_stride || seq_v < (int64_t)l * v_stride))) {
+      set_global_error("sd_gdn: the tcgen05 scan needs 16-byte aligned q/k/v/o, strides that are multiples of 8 elements "
                        "and sequences that do not overlap");
       return SD_ERR_INVALID;
     }
@@ -1998,6 +1998,16 @@ void sd_qweight_free(sd_qweight* w) {
   delete w;
 }
 
+// sd_matmul's error word on device `dev` (allocated by the first sd_matmul there, `create`; never
+// freed: one int per device)
+static int* matmul_err_word(int dev, bool create) {
+  static int* word[sd::kMaxDevices] = {};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  if (create && !word[dev] && cudaMalloc(&word[dev], sizeof(int)) == cudaSuccess) cudaMemset(word[dev], 0, sizeof(int));
+  return word[dev];
+}
+
 int sd_matmul(const sd_qweight* w, const void* act, int32_t m, void* y, int32_t ldy, int32_t silu, void* ws, size_t ws_bytes,
               void* stream) {
   if (!w || !act || !y || m <= 0 || (silu && !w->w.interleaved)) {
@@ -2014,17 +2024,37 @@ int sd_matmul(const sd_qweight* w, const void* act, int32_t m, void* y, int32_t 
   }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
+  if (dev < 0 || dev >= sd::kMaxDevices) return op_result(cudaErrorInvalidDevice, "sd_matmul");
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  static int* err_word[sd::kMaxDevices] = {};
-  static std::mutex mu;
-  {
-    std::lock_guard<std::mutex> g(mu);
-    if (!err_word[dev] && cudaMalloc(&err_word[dev], sizeof(int)) == cudaSuccess) cudaMemset(err_word[dev], 0, sizeof(int));
-  }
-  if (!err_word[dev]) return op_result(cudaErrorMemoryAllocation, "sd_matmul");
+  int* err_word = matmul_err_word(dev, true);
+  if (!err_word) return op_result(cudaErrorMemoryAllocation, "sd_matmul");
   return op_result(sd::gemm_q4(w->w, (const __half*)act, m, w->w.k, (__half*)y, ldy, silu != 0, (float*)ws, ws_bytes,
-                               err_word[dev], sms, (cudaStream_t)stream),
+                               err_word, sms, (cudaStream_t)stream),
                    "sd_matmul");
+}
+
+int sd_op_status(void* stream) {
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return op_result(e, "sd_op_status");
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return op_result(e, "sd_op_status");
+  int codes[3] = {0, 0, 0};
+  const char* names[3] = {"sd_gdn (tcgen05 scan)", "sd_attention (tcgen05)", "sd_matmul"};
+  if ((e = sd::take_gdn_tc_err(&codes[0])) != cudaSuccess || (e = sd::take_attn_tc_err(&codes[1])) != cudaSuccess)
+    return op_result(e, "sd_op_status");
+  if (int* w = dev >= 0 && dev < sd::kMaxDevices ? matmul_err_word(dev, false) : nullptr) {
+    if ((e = cudaMemcpy(&codes[2], w, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess) return op_result(e, "sd_op_status");
+    if (codes[2] != 0 && (e = cudaMemset(w, 0, sizeof(int))) != cudaSuccess) return op_result(e, "sd_op_status");
+  }
+  for (int i = 0; i < 3; i++)
+    if (codes[i] != 0) {
+      char msg[256];
+      snprintf(msg, sizeof(msg), "%s: a kernel reported error %d (%s)", names[i], codes[i],
+               codes[i] == sd::kErrBadShape ? "token id or row out of range" : "a bounded wait ran out");
+      set_global_error(msg);
+      return SD_ERR_KERNEL;
+    }
+  return SD_OK;
 }
 
 }  // extern "C"

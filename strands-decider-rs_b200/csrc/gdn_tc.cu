@@ -21,7 +21,8 @@
 //               the k and q rows' TMA (into the chunk's tile, where they are normalised in place), two
 //               chunks ahead at most;
 //   warps 4-11  the chunk preparation: q^, k^, the gates and G, A and P from [K^; Q^] K^T, the
-//               inverse (f32; 16 x 16 diagonal blocks by substitution, the rest on tf32 mma.sync),
+//               inverse (f32; 8 x 8 diagonal blocks by substitution, then doubled blocks, the larger
+//               products on tf32 mma.sync),
 //               T1 and T2 (f16), W out of tensor memory; their first thread issues [K^; Q^] K^T,
 //               W = [T1; *] K^ and U = [0; T2] V.
 // Each group keeps its warps on the same path through its named barrier whatever happens (a wait
@@ -51,11 +52,14 @@ constexpr int kOffP1 = kOffT1 + 8192;
 constexpr int kOffP0 = kOffP1 + 8192;
 constexpr int kOffZ = kOffP0 + 8192;
 constexpr int kOffT2 = kOffZ + 8192;
-constexpr int LA = CH + 1;                            // row stride (floats) of the f32 64 x 64 tiles
+// row stride (floats) of the f32 64 x 64 tiles: 4 mod 32 banks, so the tf32 MMA fragments' loads (rows g,
+// columns t of an 8 x 4 lane grid) hit 32 different banks, and a row per lane stores 16-byte vectors
+// at the minimum of four wavefronts
+constexpr int LA = CH + 4;
 constexpr int kOffA = kOffT2 + 8192;                  // A (f32)
 constexpr int kOffX = kOffA + CH * LA * 4;            // T = (I + A)^-1 (f32)
-constexpr int kOffY = kOffX + CH * LA * 4;            // 6 x 16 x 9 floats of the inverse's scratch
-constexpr int kOffSmall = kOffY + 6 * 16 * 9 * 4;     // beta[2][64], G[2][64], g[64], decay tables E[64], Gam[64], F[4][64]
+constexpr int kOffY = kOffX + CH * LA * 4;            // 32 x 40 floats of the inverse's scratch
+constexpr int kOffSmall = kOffY + 32 * 40 * 4;        // beta[2][64], G[2][64], g[64], decay tables E[64], Gam[64], F[4][64]
 constexpr int kOffBar = kOffSmall + 11 * CH * 4;
 enum {
   B_KQ_FULL = 0,     // [2] the chunk's k and q rows landed (TMA bytes)
@@ -68,7 +72,7 @@ enum {
   B_X_FULL = 14,     // [2] [Gamma Q^; -W] S accumulated
   B_S_FULL = 16,     // [2] the state update completed
   B_O_FULL = 18,     // [2] P delta accumulated (O complete): every MMA of the chunk has completed
-  B_O_READ = 20,     // [2] O read out of tensor memory (4 arrivals)
+  B_O_READ = 20,     // [2] O read out of tensor memory and stored (2 arrivals)
   B_END_PREP = 22,   // every MMA of the preparation completed (teardown)
   B_END_CHAIN = 23,  // every MMA of the chain completed (teardown)
   kBars = 24
@@ -114,73 +118,96 @@ SD_DEV void mma1688_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, u
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// One 16 x 8 tile of a product of f32 matrices in shared memory on the tensor cores (tf32 operands: the
+// top 19 bits of each f32, so the mantissa is truncated to 10 bits; f32 accumulation):
+// acc += L[r0 .. r0 + 16)[k0 .. k1) R[k0 .. k1)[c0 .. c0 + 8), k1 - k0 a multiple of 8.
+SD_DEV void mm_tile(float (&acc)[4], const float* __restrict__ L, int ldl, const float* __restrict__ R, int ldr, int r0, int c0,
+                    int k0, int k1, int g, int tq) {
+  for (int k = k0; k < k1; k += 8) {
+    const float* lp = L + (r0 + g) * ldl + k;
+    const float* rp = R + (k + tq) * ldr + c0 + g;
+    mma1688_tf32(acc, tf32(lp[tq]), tf32(lp[8 * ldl + tq]), tf32(lp[tq + 4]), tf32(lp[8 * ldl + tq + 4]), tf32(rp[0]),
+                 tf32(rp[4 * ldr]));
+  }
+}
+SD_DEV void st_tile(float* __restrict__ D, int ldd, int r0, int c0, const float (&acc)[4], float sign, int g, int tq) {
+  D[(r0 + g) * ldd + c0 + 2 * tq] = sign * acc[0];
+  D[(r0 + g) * ldd + c0 + 2 * tq + 1] = sign * acc[1];
+  D[(r0 + g + 8) * ldd + c0 + 2 * tq] = sign * acc[2];
+  D[(r0 + g + 8) * ldd + c0 + 2 * tq + 1] = sign * acc[3];
+}
+
 // X = (I + A)^-1 for the strictly lower triangular 64 x 64 A (rows LA floats apart), by the eight
-// preparation warps (w = 0..7): the 16 x 16 diagonal blocks by forward substitution (warp w < 4,
-// lane = column), then the blocks below the diagonal level by level, X_ij = -X_ii sum_{m=j}^{i-1} A_im
-// X_mj for i = j + dl (warps w and w + 4 take the two 8-column halves of block (w + dl, w), w < 4 - dl),
-// on the tensor cores with tf32 operands and f32 accumulation. Blocks above the diagonal are not
-// written (never read). `y`: 6 x 16 x 9 floats of scratch.
-SD_DEV void tri_inverse(const float* __restrict__ a, float* __restrict__ x, float* __restrict__ y, int pw, int lane) {
-  if (pw < 4 && lane < 16) {
-    const int o = pw * 16, c = lane;
-    float xc[16];
+// preparation warps (pw = 0..7, pt = 0..255), doubling the inverted blocks: the eight 8 x 8 diagonal
+// blocks by forward substitution (warp pw, lane = column), then the lower-left block of each 2s x 2s
+// diagonal block from its two s x s halves, X_10 = -X_11 (A_10 X_00), for s = 8 (four blocks, on the
+// CUDA cores), 16 (two blocks) and 32 (one block), the last two on the tensor cores. X's blocks above
+// the diagonal must hold zeros (the products read whole s x s blocks): they are never written here,
+// so zeroing X once when the kernel starts keeps them zero. `y`: 32 x 40 floats of scratch (row strides
+// of 24 and 40: 8 mod 32 banks for the B fragments' loads).
+SD_DEV void tri_inverse(const float* __restrict__ a, float* __restrict__ x, float* __restrict__ y, int pw, int pt, int lane) {
+  if (lane < 8) {
+    const int o = pw * 8, c = lane;
+    float xc[8];
 #pragma unroll
-    for (int r = 0; r < 16; r++) {
-      float v0 = r == c ? 1.0f : 0.0f, v1 = 0.0f;
+    for (int r = 0; r < 8; r++) {  // branch-free: xc[j] is zero above the diagonal (j < c)
+      float v = r == c ? 1.0f : 0.0f;
 #pragma unroll
-      for (int j = 0; j < r; j++)
-        if (j >= c) {
-          if (j & 1) v1 -= a[(o + r) * LA + o + j] * xc[j];
-          else v0 -= a[(o + r) * LA + o + j] * xc[j];
-        }
-      xc[r] = r >= c ? v0 + v1 : 0.0f;
+      for (int j = 0; j < r; j++) v -= a[(o + r) * LA + o + j] * xc[j];
+      xc[r] = r >= c ? v : 0.0f;
     }
 #pragma unroll
-    for (int r = 0; r < 16; r++) x[(o + r) * LA + o + c] = xc[r];
+    for (int r = 0; r < 8; r++) x[(o + r) * LA + o + c] = xc[r];
   }
   prep_sync();
-  const int g = lane >> 2, tq = lane & 3, w = pw & 3, nt = pw >> 2;
-#pragma unroll 1
-  for (int dl = 1; dl < 4; dl++) {
-    if (w < 4 - dl) {
-      const int bj = w, bi = bj + dl;
+  {  // s = 8: thread pt takes element (i, j) of block b = pt / 64 (rows 16 b + 8 .., columns 16 b ..)
+    const int b = pt >> 6, i = (pt >> 3) & 7, jj = pt & 7, o = 16 * b;
+    float t = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 8; m++) t += a[(o + 8 + i) * LA + o + m] * x[(o + m) * LA + o + jj];
+    y[b * 64 + i * 8 + jj] = t;
+    prep_sync();
+    float z = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 8; m++) z += x[(o + 8 + i) * LA + o + 8 + m] * y[b * 64 + m * 8 + jj];
+    x[(o + 8 + i) * LA + o + jj] = -z;
+  }
+  prep_sync();
+  const int g = lane >> 2, tq = lane & 3;
+  {  // s = 16: warps 0-3, block b = pw / 2 (rows 32 b + 16 .., columns 32 b ..), 8 columns each
+    const int b = (pw >> 1) & 1, c0 = 8 * (pw & 1), o = 32 * b;
+    float* yb = y + b * 16 * 24;
+    if (pw < 4) {
       float acc[4] = {};
-      for (int m = bj; m < bi; m++)
-#pragma unroll
-        for (int kk = 0; kk < 16; kk += 8) {
-          const float* ar = a + (bi * 16 + g) * LA + m * 16 + kk;
-          const float* xr = x + (m * 16 + kk + tq) * LA + bj * 16 + nt * 8 + g;
-          mma1688_tf32(acc, tf32(ar[tq]), tf32(ar[8 * LA + tq]), tf32(ar[tq + 4]), tf32(ar[8 * LA + tq + 4]), tf32(xr[0]),
-                       tf32(xr[4 * LA]));
-        }
-      float* yw = y + (w + 3 * nt) * 144;  // this warp's 16 x 8 part of the sum (row stride 9; w < 3)
-      yw[g * 9 + 2 * tq] = acc[0];
-      yw[g * 9 + 2 * tq + 1] = acc[1];
-      yw[(g + 8) * 9 + 2 * tq] = acc[2];
-      yw[(g + 8) * 9 + 2 * tq + 1] = acc[3];
-      __syncwarp();
-      float z[4] = {};
-#pragma unroll
-      for (int kk = 0; kk < 16; kk += 8) {
-        const float* xr = x + (bi * 16 + g) * LA + bi * 16 + kk;
-        mma1688_tf32(z, tf32(xr[tq]), tf32(xr[8 * LA + tq]), tf32(xr[tq + 4]), tf32(xr[8 * LA + tq + 4]),
-                     tf32(yw[(kk + tq) * 9 + g]), tf32(yw[(kk + tq + 4) * 9 + g]));
-      }
-      float* xo = x + (bi * 16 + g) * LA + bj * 16 + nt * 8 + 2 * tq;
-      xo[0] = -z[0];
-      xo[1] = -z[1];
-      xo[8 * LA] = -z[2];
-      xo[8 * LA + 1] = -z[3];
+      mm_tile(acc, a + (o + 16) * LA + o, LA, x + o * LA + o, LA, 0, c0, 0, 16, g, tq);
+      st_tile(yb, 24, 0, c0, acc, 1.0f, g, tq);
     }
     prep_sync();
+    if (pw < 4) {
+      float acc[4] = {};
+      mm_tile(acc, x + (o + 16) * LA + o + 16, LA, yb, 24, 0, c0, 0, 16, g, tq);
+      st_tile(x + (o + 16) * LA + o, LA, 0, c0, acc, -1.0f, g, tq);
+    }
   }
+  prep_sync();
+  {  // s = 32: eight warps, a 16 x 8 tile each of the 32 x 32 block (rows 32 .., columns 0 ..)
+    const int r0 = 16 * (pw & 1), c0 = 8 * (pw >> 1);
+    float acc[4] = {};
+    mm_tile(acc, a + 32 * LA, LA, x, LA, r0, c0, 0, 32, g, tq);
+    st_tile(y, 40, r0, c0, acc, 1.0f, g, tq);
+    prep_sync();
+    float acc2[4] = {};
+    mm_tile(acc2, x + 32 * LA + 32, LA, y, 40, r0, c0, 0, 32, g, tq);
+    st_tile(x + 32 * LA, LA, r0, c0, acc2, -1.0f, g, tq);
+  }
+  prep_sync();
 }
 
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                  const __grid_constant__ CUtensorMap vmap, const GdnTcArgs a) {
+                  const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap, const GdnTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = smem_align1024(smem_raw);
   uint64_t* bar = reinterpret_cast<uint64_t*>(base + kOffBar);
@@ -229,12 +256,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nch = (L + CH - 1) / CH;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kBars; i++) mbar_init(&bar[i], i >= B_O_READ && i < B_O_READ + 2 ? 4 : 1);
+    for (int i = 0; i < kBars; i++) mbar_init(&bar[i], i >= B_O_READ && i < B_O_READ + 2 ? 2 : 1);
     *abort = 0;
     fence_mbar_init();
   }
-  // the zero tile (rows 64-127 of U's [0; T2] operand)
+  // the zero tile (rows 64-127 of U's [0; T2] operand), and X (T = (I + A)^-1), whose blocks above the
+  // diagonal the inverse reads and never writes
   for (int i = threadIdx.x; i < 8192 / 16; i += kThreads) reinterpret_cast<uint4*>(base + kOffZ)[i] = make_uint4(0, 0, 0, 0);
+  for (int i = threadIdx.x; i < CH * LA; i += kThreads) reinterpret_cast<float*>(base + kOffX)[i] = 0.0f;
   if (warp == 0) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -273,6 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&qmap);
       prefetch_tmap(&kmap);
       prefetch_tmap(&vmap);
+      prefetch_tmap(&omap);
       for (; nkq < min(2, nch); nkq++) load_kq(nkq);
     }
     if (warp == 2 && lane == 0) load_v(nv++);
@@ -296,13 +326,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_wait_st();
     bool ok = true;
     // O rows (D_X rows 0-63, warps 0 and 1) of chunk c to global memory, then D_X[c & 1] is released;
-    // the MMAs of chunk c have all completed, so its tile takes chunk c + 2's k and q rows
+    // the MMAs of chunk c have all completed, so its tile takes chunk c + 2's k and q rows. A warp whose
+    // 32 rows all lie in the sequence stores them as four 32 x 32 blocks through shared memory (the T1
+    // tile, 4 KB per warp: free from W of chunk c until the preparation of chunk c + 1 writes T1, which
+    // waits for this read-out) with the TMA, in whole 128-byte lines: lane-per-row stores from the
+    // registers would write 32 rows' 16-byte pieces per instruction and hold up the shared-memory
+    // traffic of the preparation warps beside them. The ragged rows of a last chunk are stored directly.
     auto read_o = [&](int c) {
       const int s = c & 1;
       if (ok) ok = mbar_wait_warp(&bar[B_O_FULL + s], (c >> 1) & 1, abort, err, kErrTimeoutAccum);
+      if (ok && warp == 0 && lane == 0 && c + 2 < nch) load_kq(nkq++);
       if (ok && q4 < 2) {
         tc_fence_after();
         const int n = min(CH, L - c * CH);
+        const bool whole = n >= 32 * (q4 + 1);
+        uint8_t* stage = base + kOffT1 + q4 * 4096;
         // tcgen05.ld and wait::ld are warp-collective (.sync.aligned): every lane of the warp executes
         // the same loads, and only the stores are limited to the chunk's rows
         float* dst = a.o + (size_t)(tok0 + c * CH + r) * H * DK + hd * DK;
@@ -310,7 +348,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v[32];
           tmem_ld32(tmem + lanes + kColX + s * 128 + cb * 32, v);
           tc_wait_ld();
-          if (r < n) {
+          if (whole) {
+            if (cb > 0) {  // the previous block's store has read the staging
+              if (lane == 0) bulk_wait_read();
+              __syncwarp();
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+              *reinterpret_cast<uint4*>(stage + lane * 128 + ((i ^ (lane & 7)) << 4)) =
+                  make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&omap, stage, hd * DK + cb * 32, (int)(tok0 + c * CH + q4 * 32));
+              bulk_commit();
+            }
+          } else if (r < n) {
             float4* d4 = reinterpret_cast<float4*>(dst + cb * 32);
 #pragma unroll
             for (int i = 0; i < 8; i++)
@@ -318,17 +371,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   __uint_as_float(v[4 * i + 3]));
           }
         }
+        if (whole && lane == 0) bulk_wait_read();
       }
-      if (ok && warp == 0 && lane == 0 && c + 2 < nch) load_kq(nkq++);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_O_READ + s]);
+      // warps 0 and 1 only: warps 2 and 3 read their rows (delta) before the chunk's last MMAs were
+      // issued, and warp 2 reaches this point only after the next chunk's preparation, which waits here
+      if (lane == 0 && q4 < 2) mbar_arrive(&bar[B_O_READ + s]);
     };
     for (int c = 0; c < nch; c++) {
       const int s = c & 1;
       const uint32_t ph = (c >> 1) & 1;
       uint8_t* t = base + kOffKQW + s * kTile;
       const uint32_t dx = tmem + kColX + s * 128;
+      // (0) O of the previous chunk first (the next chunk's preparation waits for it before it writes T1)
+      if (c >= 1) read_o(c - 1);
       // (1) the entry state S_{c-1}: its f16 copy (the operand of [Gamma Q^; -W] S), Gamma_C S back
       if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_S_FULL + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutAccum);
       if (ok) ok = mbar_wait_warp(&bar[B_G_READY + s], ph, abort, err, kErrTimeoutFull);
@@ -373,8 +430,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c + 1 < nch) load_v(nv++);  // the v buffer is free: U of chunk c has completed
         }
       }
-      // (2) O of the previous chunk (its MMA was issued right after the state update just waited for)
-      if (c >= 1) read_o(c - 1);
       // (3) delta = D_X rows 64-127 (warps 2 and 3): delta (f16, over Gamma Q^) and Ds = delta e^{G_C - G_i}
       // (over -W)
       if (ok) ok = mbar_wait_warp(&bar[B_X_FULL + s], ph, abort, err, kErrTimeoutAccum);
@@ -425,6 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     read_o(nch - 1);
+    if (q4 < 2 && lane == 0) bulk_wait_all();  // the output stores have completed
     // the final state
     if (ok && sout) {
       const int c = nch - 1;
@@ -593,7 +649,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int jj = 0; jj < 32; jj++) av[jj] = j0 + jj < i ? bi * dec[jj] * __uint_as_float(v[jj]) : 0.0f;
 #pragma unroll
-          for (int jj = 0; jj < 32; jj++) sa[i * LA + j0 + jj] = av[jj];
+          for (int j4 = 0; j4 < 8; j4++)
+            *reinterpret_cast<float4*>(sa + i * LA + j0 + 4 * j4) = make_float4(av[4 * j4], av[4 * j4 + 1], av[4 * j4 + 2], av[4 * j4 + 3]);
         } else {  // Q row i: its P columns (f16), then Gamma_i q^_i over one half of the row
           uint8_t* pt_ = base + (s ? kOffP1 : kOffP0);
 #pragma unroll
@@ -621,16 +678,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       prep_sync();
       // (4) T = (I + A)^-1
-      tri_inverse(sa, sx, sy, pw, lane);
+      tri_inverse(sa, sx, sy, pw, pt, lane);
       // (5) T1 = T diag(beta Gamma), T2 = T diag(beta) (f16), once U of chunk c - 1 has read T2 (and W
       // of chunk c - 1, issued before it, T1); thread pt: row pt >> 2, columns 16 (pt & 3) ..
       if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
+      // ... and once the chain has stored chunk c - 1's O through T1
+      if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_O_READ + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
       if (ok) {
         const int i = pt >> 2, j0 = (pt & 3) * 16;
         const float* be = sbeta + s * CH;
         float tv[16], bj[16], gj[16];  // loaded before any store (see the A and P loops)
 #pragma unroll
-        for (int e = 0; e < 16; e++) tv[e] = j0 + e <= i ? sx[i * LA + j0 + e] : 0.0f;
+        for (int j4 = 0; j4 < 4; j4++) {  // T is lower triangular: its entries above the diagonal are zeros
+          const float4 f = *reinterpret_cast<const float4*>(sx + i * LA + j0 + 4 * j4);
+          tv[4 * j4] = f.x, tv[4 * j4 + 1] = f.y, tv[4 * j4 + 2] = f.z, tv[4 * j4 + 3] = f.w;
+        }
 #pragma unroll
         for (int j4 = 0; j4 < 4; j4++) {
           const float4 f = *reinterpret_cast<const float4*>(be + j0 + 4 * j4);
@@ -727,6 +789,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+cudaError_t take_gdn_tc_err(int* code) {
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_gdn_tc_err, sizeof(int));
+  const int zero = 0;
+  if (e == cudaSuccess && *code != 0) e = cudaMemcpyToSymbol(g_gdn_tc_err, &zero, sizeof(int));
+  return e;
+}
+
 cudaError_t preload_gdn_tc() {
   return cudaFuncSetAttribute(gdn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
 }
@@ -734,7 +803,7 @@ cudaError_t preload_gdn_tc() {
 cudaError_t launch_gdn_tc(const __half* q, const __half* k, int qk_stride, const __half* v, int v_stride, long long seq_qk,
                           long long seq_v, int rows, const GdnTcArgs& a, int walks, cudaStream_t st) {
   if (walks <= 0 || a.h <= 0 || rows <= 0 || qk_stride % 8 || v_stride % 8 || seq_qk % 8 || seq_v % 8 ||
-      ((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16 || (!a.seq_off && (a.l <= 0 || walks % a.h)))
+      ((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)a.o) % 16 || (!a.seq_off && (a.l <= 0 || walks % a.h)))
     return cudaErrorInvalidValue;
   static bool attr[kMaxDevices] = {};
   static std::mutex mu;
@@ -750,12 +819,15 @@ cudaError_t launch_gdn_tc(const __half* q, const __half* k, int qk_stride, const
     }
   }
   const int zdim = a.seq_off ? 1 : walks / a.h;
-  CUtensorMap qm, km, vm;
+  CUtensorMap qm, km, vm, om;
+  // the outputs: rows of h * DK floats, one per token (packed: `rows` tokens; else walks / h sequences of l)
+  const long long orows = a.seq_off ? (long long)rows : (long long)(walks / a.h) * a.l;
   if (make_map_3d(&qm, q, a.h * DK, rows, zdim, qk_stride, a.seq_off ? (long long)rows * qk_stride : seq_qk, CH) != 0 ||
       make_map_3d(&km, k, a.h * DK, rows, zdim, qk_stride, a.seq_off ? (long long)rows * qk_stride : seq_qk, CH) != 0 ||
-      make_map_3d(&vm, v, a.h * DK, rows, zdim, v_stride, a.seq_off ? (long long)rows * v_stride : seq_v, CH) != 0)
+      make_map_3d(&vm, v, a.h * DK, rows, zdim, v_stride, a.seq_off ? (long long)rows * v_stride : seq_v, CH) != 0 ||
+      make_map_f32(&om, a.o, orows, a.h * DK, (long long)a.h * DK, 32) != 0)
     return cudaErrorInvalidValue;
-  gdn_tc_kernel<<<walks, kThreads, kSmem, st>>>(qm, km, vm, a);
+  gdn_tc_kernel<<<walks, kThreads, kSmem, st>>>(qm, km, vm, om, a);
   return cudaGetLastError();
 }
 

@@ -535,6 +535,21 @@ int make_map_3d(CUtensorMap* map, const void* ptr, int x, int y, int z, long lon
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+// A 2-D f32 tensor map over rows x cols (row-major, rows `ld` elements apart) with boxes of
+// 32 x box_rows and the 128-byte swizzle (a box row is one 128-byte line). Stores clip at the dims.
+int make_map_f32(CUtensorMap* map, const void* ptr, long long rows, int cols, long long ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {32u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
 template <int BN, int EPI>
 static cudaError_t launch_bn(const CUtensorMap& map, const QWeight& w, int M, const TileGrid& tg, int num_sms, __half* y,
                              int ldy, float* ws, int* err, cudaStream_t st) {

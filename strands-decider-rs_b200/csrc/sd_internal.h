@@ -43,6 +43,11 @@ cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half*
                     size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch = nullptr);
 int make_act_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
 int make_map_3d(CUtensorMap* map, const void* ptr, int x, int y, int z, long long ystride, long long zstride, int box_y);
+// The error words of the standalone calls' kernels (no engine: the C ABI's sd_attention*, sd_gdn):
+// read and cleared by sd_op_status.
+cudaError_t take_gdn_tc_err(int* code);
+cudaError_t take_attn_tc_err(int* code);
+int make_map_f32(CUtensorMap* map, const void* ptr, long long rows, int cols, long long ld, int box_rows);
 
 // Model dims the kernels are specialised for (src/kernels.rs:813-835).
 struct Dims {

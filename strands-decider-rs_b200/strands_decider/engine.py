@@ -85,6 +85,7 @@ def lib() -> C.CDLL:
         L.sd_gdn_scratch_bytes.argtypes = [i32, i32]
         L.sd_qweight_create.argtypes = [vp, vp, i32, i32, i32, C.POINTER(vp)]
         L.sd_engine_selftest_wait.argtypes = [vp, i32]
+        L.sd_op_status.argtypes = [vp]
         L.sd_qweight_create_format.argtypes = [vp, vp, i32, i32, i32, i32, i32, C.POINTER(vp)]
         L.sd_qweight_free.argtypes = [vp]
         L.sd_matmul.argtypes = [vp, vp, i32, vp, i32, i32, vp, C.c_size_t, vp]
@@ -404,6 +405,12 @@ def gdn(q, k, qk_stride, v, v_stride, beta, g, state, load_state, o, l, h, batch
         algo = GDN_SERIAL if serial else GDN_CHUNKED
     _check(lib().sd_gdn(q, k, qk_stride, v, v_stride, beta, g, state, int(load_state), o, l, h, batch, seq_qk, seq_v,
                         int(in_f16), int(algo), scratch, scratch_bytes, stream), "sd_gdn")
+
+
+def op_status(stream=None):
+    """`sd_op_status`: synchronises ``stream`` and raises if a kernel of a standalone call (gdn,
+    attention, matmul) gave up on a bounded wait since the last check."""
+    _check(lib().sd_op_status(stream), "sd_op_status")
 
 
 def decode_scales(src, n, g, dst, stream=None):

@@ -17,6 +17,19 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (runs the CUDA path through the C ABI)")
 
 
+@pytest.fixture(autouse=True)
+def _kernel_status(request):
+    """After every GPU test: no kernel of a standalone call gave up on a bounded wait (sd_op_status)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from strands_decider import engine
+    engine.op_status()
+
+
 @pytest.fixture(scope="session")
 def small_model():
     """Production dims, 4 layers (3 gated-delta + 1 full attention), an 8192-row vocabulary."""

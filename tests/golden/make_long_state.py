@@ -70,17 +70,20 @@ def main():
     _, snap_r, tr_r = eng.forward(state, list(STATE_ROWS), keep=True, trace=True)
     drift_state = np.abs(tr_r[:, list(STATE_ROWS), :] - trace_rows).max(axis=(1, 2))
     del tr_r
-    _, _, trq_r = eng.forward(question, list(Q_ROWS), cache=snap_r, trace=True)
+    hidden_q_r, _, trq_r = eng.forward(question, list(Q_ROWS), cache=snap_r, trace=True)
     drift_q = np.abs(trq_r[:, [Q_ROWS[-1]], :] - trace_q).max(axis=(1, 2))
+    drift_p = float(np.abs(oracle.head_probs(hidden_q_r, tensors, 1.0) - probs).max())
     oracle.set_sum_reversed(False)
     t2 = time.time()
     out = os.path.join(HERE, "long_state_s0.npz")
     np.savez_compressed(out, fingerprint=np.array(fingerprint(path)), state=state, question=question,
                         state_rows=np.array(STATE_ROWS, np.int32), q_rows=np.array(Q_ROWS, np.int32),
                         hidden_state=hidden_s, trace_state=trace_rows, hidden_q=hidden_q, trace_q=trace_q, probs=probs,
-                        drift_state=drift_state.astype(np.float32), drift_q=drift_q.astype(np.float32))
+                        drift_state=drift_state.astype(np.float32), drift_q=drift_q.astype(np.float32),
+                        drift_p=np.float32(drift_p))
     print(f"state forward {t1 - t0:.0f} s, question and drift {t2 - t1:.0f} s -> {out} ({os.path.getsize(out) / 1e3:.0f} KB); "
-          f"sum-order drift at the last layer {drift_state[-1]:.2e} (state), {drift_q[-1]:.2e} (question)")
+          f"sum-order drift at the last layer {drift_state[-1]:.2e} (state), {drift_q[-1]:.2e} (question); "
+          f"of the probabilities {drift_p:.2e}")
 
 
 if __name__ == "__main__":

@@ -242,9 +242,10 @@ def test_long_state_and_continuation_match_fixture(full_model, long_state):
     head = Head.load(os.path.join(full_model, "head.safetensors"))
     probs = gpu.forward_fork_probs([snaps[0]], [question], [qrows], head, 1.0)[0]
     dp = float(np.abs(probs - fx["probs"]).max())
-    assert dp < PROB_TOL and np.argmax(probs) == np.argmax(fx["probs"])
+    p_tol = max(PROB_TOL, DRIFT_FACTOR * float(fx["drift_p"]))
+    assert dp < p_tol and np.argmax(probs) == np.argmax(fx["probs"]), (dp, float(fx["drift_p"]))
     snaps[0].close()
     gpu.close()
     print(f"3000-token state (24 layers): worst per-layer max-abs {per_layer.max():.2e} (state rows; the oracle's "
           f"sum-order drift {fx['drift_state'].max():.2e}), {per_layer_q.max():.2e} (question; drift "
-          f"{fx['drift_q'].max():.2e}); fork hidden {err_q:.2e}; |dp| {dp:.2e}")
+          f"{fx['drift_q'].max():.2e}); fork hidden {err_q:.2e}; |dp| {dp:.2e} (drift {float(fx['drift_p']):.2e})")
