@@ -672,14 +672,15 @@ struct Fork {
 
 // Whether a gated-delta layer over `walks` (sequence, head) walks, the longest of max_chunks 64-token
 // chunks and chunks x heads chunk records in all, takes the fused tcgen05 scan rather than the
-// two-phase one. Estimates from B200 timings: the fused scan walks about 8.5 us per chunk, one CTA
-// per walk and SM, so a wave lasts its longest walk; the two-phase scan's preparation does about two
+// two-phase one. Estimates from B200 timings: the fused scan walks about 6 us per chunk (config 3,
+// B = 16, L = 1024: 204 us for two waves of 16 chunks), one CTA per walk and SM, so a wave lasts its
+// longest walk; the two-phase scan's preparation does about two
 // chunk records per SM each 21 us, then its walk takes about 4 us per chunk of the longest sequence.
 static bool gdn_pick_tc(const sd_engine* e, long long walks, long long max_chunks, long long records, bool two_phase_ok) {
   if (e->gdn_mode) return e->gdn_mode == 1;
   if (!two_phase_ok) return true;
   const long long sms = std::max(1, e->num_sms);
-  const double fused = (double)((walks + sms - 1) / sms) * max_chunks * 8.5;
+  const double fused = (double)((walks + sms - 1) / sms) * max_chunks * 6.0;
   const double two_phase = (double)((records + 2 * sms - 1) / (2 * sms)) * 21.0 + max_chunks * 4.0;
   return fused <= two_phase;
 }

@@ -7,6 +7,7 @@
 // Gamma_i = exp(G_i) (the WY form of the chunk, as gdn.cu states it):
 //   A_ij = beta_i e^{G_i - G_j} k^_i.k^_j (j < i),  T = (I + A)^-1,  T1 = T diag(beta Gamma),  T2 = T diag(beta)
 //   W = T1 K^,  U = T2 V,  delta = U - W S,  P_ij = e^{G_i - G_j} q^_i.k^_j (j <= i)
+//   (k^ = rk k, q^ = rq q: the norms below)
 //   O = Gamma Q^ S + P delta,   S' = Gamma_C S + K^T diag(e^{G_C - G_i}) delta
 //
 // One CTA walks one (sequence, head) over all 128 value columns. The state S is the f32 accumulator
@@ -14,21 +15,22 @@
 // 64-row operands: [K^; Q^] K^T gives A and P at once, [Gamma Q^; -W] S gives Gamma Q^ S and -W S
 // (accumulated onto [0; U], so that the second half is delta), and [P; *] delta adds P delta to the
 // first half. The state-independent work of chunk c + 1 (normalisation, A and P, the triangular
-// inverse, W and U) runs beside the state chain of chunk c:
-//   warps 0-3   the chain: S out of tensor memory (its f16 copy, the operand of the next chunk, and
-//               Gamma_C S back), delta (f16, and decayed as Ds), O rows to global memory; one thread
-//               issues the chain's MMAs ([Gamma Q^; -W] S, K^T Ds, P delta) and the v rows' TMA, one
-//               the k and q rows' TMA (into the chunk's tile, where they are normalised in place), two
-//               chunks ahead at most;
-//   warps 4-11  the chunk preparation: q^, k^, the gates and G, A and P from [K^; Q^] K^T, the
+// inverse, T1 and T2) runs beside the state chain of chunk c:
+//   warps 0-3   the chain: O rows to global memory, S out of tensor memory (its f16 copy, the operand
+//               of the next chunk, and Gamma_C S back), -W out of tensor memory, delta (f16, and
+//               decayed as Ds); one thread issues U = [0; T2] V and the chain's MMAs ([Gamma Q^; -W] S,
+//               K^T Ds, P delta) and the v rows' TMA, one the k and q rows' TMA (into the chunk's
+//               tile), two chunks ahead at most;
+//   warps 4-11  the chunk preparation: the norms of q and k, the gates and G, A and P from [K; Q] K^T, the
 //               inverse (f32; 8 x 8 diagonal blocks by substitution, then doubled blocks, the larger
-//               products on tf32 mma.sync),
-//               T1 and T2 (f16), W out of tensor memory; their first thread issues [K^; Q^] K^T,
-//               W = [T1; *] K^ and U = [0; T2] V.
+//               products on tf32 mma.sync), T1 and T2 (f16); their first thread issues [K; Q] K^T and
+//               W = [T1; *] K, after which the chunk passes to the chain.
 // Each group keeps its warps on the same path through its named barrier whatever happens (a wait
 // that gives up marks the CTA aborted and the group skips the work that follows, not the barriers).
-// Rounding points are those of the two-phase scan (gdn.cu): f16 q^, k^, T1, T2, W, P, delta, Ds and
-// the state operand; f32 accumulation, U and the state.
+// The tile keeps k and q as loaded (f16): their norms, rk_i = rsqrt(|k_i|^2 + 1e-6) and
+// rq_i = rsqrt(|q_i|^2 + 1e-6) / sqrt(DK), scale the f32 products instead (A and P by rows and columns,
+// T1 by columns, Ds by rows, Gamma q^ = Gamma_i rq_i q_i), so no rounded q^ or k^ is formed. Rounded
+// to f16: T1, T2, W, P, Gamma q^, delta, Ds and the state operand; f32 accumulation, U and the state.
 //
 // Every wait is bounded (2 s, common.cuh): a wait that runs out records an error code and the CTA
 // winds down (each MMA issuer waits for its own MMAs, the TMA thread for its copies) without hanging.
@@ -56,18 +58,18 @@ constexpr int kOffT2 = kOffZ + 8192;
 // columns t of an 8 x 4 lane grid) hit 32 different banks, and a row per lane stores 16-byte vectors
 // at the minimum of four wavefronts
 constexpr int LA = CH + 4;
-constexpr int kOffA = kOffT2 + 8192;                  // A (f32)
-constexpr int kOffX = kOffA + CH * LA * 4;            // T = (I + A)^-1 (f32)
-constexpr int kOffY = kOffX + CH * LA * 4;            // 32 x 40 floats of the inverse's scratch
-constexpr int kOffSmall = kOffY + 32 * 40 * 4;        // beta[2][64], G[2][64], g[64], decay tables E[64], Gam[64], F[4][64]
-constexpr int kOffBar = kOffSmall + 11 * CH * 4;
+constexpr int kOffA = kOffT2 + 8192;                  // A (f32), replaced in place by T = (I + A)^-1
+constexpr int kOffY = kOffA + CH * LA * 4;            // 32 x 40 floats of the inverse's scratch
+constexpr int kOffSmall = kOffY + 32 * 40 * 4;        // beta[2][64], G[2][64], g[64], decay tables E[64], Gam[64], F[4][64],
+                                                      // row norms N[2][128]
+constexpr int kOffBar = kOffSmall + 15 * CH * 4;
 enum {
   B_KQ_FULL = 0,     // [2] the chunk's k and q rows landed (TMA bytes)
   B_V_FULL = 2,      // [2] the chunk's v rows landed
-  B_U_DONE = 4,      // [2] U = [0; T2] V completed (V, T1 and T2 free; the chain may accumulate)
+  B_U_DONE = 4,      // [2] U = [0; T2] V completed (T1 and T2 free; W read out before it)
   B_DAP_FULL = 6,    // [2] [K^; Q^] K^T in tensor memory
   B_W_FULL = 8,      // [2] W in tensor memory
-  B_WQ_READY = 10,   // [2] -W, Gamma Q^ and P written (shared memory), W read out
+  B_WQ_READY = 10,   // [2] Gamma Q^, P, T1 and T2 written (shared memory) and W issued
   B_G_READY = 12,    // [2] the chunk's G written
   B_X_FULL = 14,     // [2] [Gamma Q^; -W] S accumulated
   B_S_FULL = 16,     // [2] the state update completed
@@ -137,18 +139,20 @@ SD_DEV void st_tile(float* __restrict__ D, int ldd, int r0, int c0, const float 
   D[(r0 + g + 8) * ldd + c0 + 2 * tq + 1] = sign * acc[3];
 }
 
-// X = (I + A)^-1 for the strictly lower triangular 64 x 64 A (rows LA floats apart), by the eight
-// preparation warps (pw = 0..7, pt = 0..255), doubling the inverted blocks: the eight 8 x 8 diagonal
-// blocks by forward substitution (warp pw, lane = column), then the lower-left block of each 2s x 2s
-// diagonal block from its two s x s halves, X_10 = -X_11 (A_10 X_00), for s = 8 (four blocks, on the
-// CUDA cores), 16 (two blocks) and 32 (one block), the last two on the tensor cores. X's blocks above
-// the diagonal must hold zeros (the products read whole s x s blocks): they are never written here,
-// so zeroing X once when the kernel starts keeps them zero. `y`: 32 x 40 floats of scratch (row strides
+// X = (I + A)^-1 for the strictly lower triangular 64 x 64 A (rows LA floats apart), in place, by the
+// eight preparation warps (pw = 0..7, pt = 0..255), doubling the inverted blocks: the eight 8 x 8
+// diagonal blocks by forward substitution (warp pw, lane = column), then the lower-left block of each
+// 2s x 2s diagonal block from its two s x s halves, X_10 = -X_11 (A_10 X_00), for s = 8 (four blocks,
+// on the CUDA cores), 16 (two blocks) and 32 (one block), the last two on the tensor cores. Each A_10
+// is read (into Y) before X_10 replaces it, and no level reads an A block an earlier level replaced.
+// The array must hold zeros above the diagonal (the products read whole s x s blocks; A's rows are
+// written whole, zeros included, and no level writes there). `y`: 32 x 40 floats of scratch (row strides
 // of 24 and 40: 8 mod 32 banks for the B fragments' loads).
-SD_DEV void tri_inverse(const float* __restrict__ a, float* __restrict__ x, float* __restrict__ y, int pw, int pt, int lane) {
+SD_DEV void tri_inverse(float* a, float* y, int pw, int pt, int lane) {
+  float* x = a;
+  const int o = pw * 8, c = lane;
+  float xc[8];
   if (lane < 8) {
-    const int o = pw * 8, c = lane;
-    float xc[8];
 #pragma unroll
     for (int r = 0; r < 8; r++) {  // branch-free: xc[j] is zero above the diagonal (j < c)
       float v = r == c ? 1.0f : 0.0f;
@@ -156,6 +160,9 @@ SD_DEV void tri_inverse(const float* __restrict__ a, float* __restrict__ x, floa
       for (int j = 0; j < r; j++) v -= a[(o + r) * LA + o + j] * xc[j];
       xc[r] = r >= c ? v : 0.0f;
     }
+  }
+  __syncwarp();  // the block's A read before its T is written over it
+  if (lane < 8) {
 #pragma unroll
     for (int r = 0; r < 8; r++) x[(o + r) * LA + o + c] = xc[r];
   }
@@ -223,6 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* sE = sg + CH;                                         // [64]
   float* sGam = sE + CH;                                       // [64]
   float* sF = sGam + CH;                                       // [4][64]
+  // rsqrt(|k_i|^2 + 1e-6) (rows 0-63) and rsqrt(|q_i|^2 + 1e-6) / sqrt(DK) (rows 64-127) of chunk c
+  // (sN[c & 1]): the tile keeps the raw k and q, and the products take these as row and column scales
+  float* sN = sF + 4 * CH;                                     // [2][128]
   int* err = a.err ? a.err : &g_gdn_tc_err;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = a.h;
@@ -260,10 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort = 0;
     fence_mbar_init();
   }
-  // the zero tile (rows 64-127 of U's [0; T2] operand), and X (T = (I + A)^-1), whose blocks above the
-  // diagonal the inverse reads and never writes
+  // the zero tile (rows 0-63 of U's [0; T2] operand)
   for (int i = threadIdx.x; i < 8192 / 16; i += kThreads) reinterpret_cast<uint4*>(base + kOffZ)[i] = make_uint4(0, 0, 0, 0);
-  for (int i = threadIdx.x; i < CH * LA; i += kThreads) reinterpret_cast<float*>(base + kOffX)[i] = 0.0f;
   if (warp == 0) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -417,26 +425,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ok)) *abort = 1;
       chain_sync();
       ok = ok && !*abort;
-      if (warp == 2) {  // [Gamma Q^; -W] S onto [0; U] (rows 0-63 Gamma Q^ S, rows 64-127 delta), then v of chunk c + 1
+      // (2) -W (D_X rows 0-63, warps 0 and 1) over rows 128-191 of the tile, once W has completed; the
+      // preparation has gone on to the next chunk
+      if (ok && q4 < 2) {
+        ok = mbar_wait_warp(&bar[B_W_FULL + s], ph, abort, err, kErrTimeoutAccum);
+        if (ok) {
+          tc_fence_after();
+          for (int cb = 0; cb < 4; cb++) {
+            uint32_t v[32];
+            tmem_ld32(dx + lanes + cb * 32, v);
+            tc_wait_ld();
+            uint8_t* box = t + (cb >> 1) * kBox;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+              *reinterpret_cast<uint4*>(box + swz(128 + r, (cb & 1) * 4 + j)) =
+                  make_uint4(pack_h2(-__uint_as_float(v[8 * j]), -__uint_as_float(v[8 * j + 1])),
+                             pack_h2(-__uint_as_float(v[8 * j + 2]), -__uint_as_float(v[8 * j + 3])),
+                             pack_h2(-__uint_as_float(v[8 * j + 4]), -__uint_as_float(v[8 * j + 5])),
+                             pack_h2(-__uint_as_float(v[8 * j + 6]), -__uint_as_float(v[8 * j + 7])));
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      if (!__all_sync(0xffffffffu, ok)) *abort = 1;
+      chain_sync();
+      ok = ok && !*abort;
+      if (warp == 2) {  // U = [0; T2] V into D_X[s] (rows 0-63 zero), then [Gamma Q^; -W] S onto it (rows
+                        // 0-63 Gamma Q^ S, rows 64-127 delta)
         if (ok) ok = mbar_wait_warp(&bar[B_WQ_READY + s], ph, abort, err, kErrTimeoutFull);
-        if (ok) ok = mbar_wait_warp(&bar[B_U_DONE + s], ph, abort, err, kErrTimeoutFull);
+        if (ok) ok = mbar_wait_warp(&bar[B_V_FULL + s], ph, abort, err, kErrTimeoutFull);
         if (ok && lane == 0) {
           tc_fence_after();
+          {
+            const uint64_t ad = sw128_desc(base + kOffZ), bd = sw128_mn_desc(base + kOffV, 8192);
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) tc_mma_f16(dx, ad + (uint64_t)(2 * ks), bd + (uint64_t)(128 * ks), kIdB, ks > 0);
+          }
+          tc_commit(&bar[B_U_DONE + s]);
           const uint64_t ad = sw128_desc(t + 64 * 128), bd = sw128_mn_desc(base + kOffS16, 16384);
 #pragma unroll
           for (int ks = 0; ks < 8; ks++)
             tc_mma_f16(dx, ad + (uint64_t)((ks >> 2) * (kBox >> 4) + 2 * (ks & 3)), bd + (uint64_t)(128 * ks), kIdB, 1);
           tc_commit(&bar[B_X_FULL + s]);
-          if (c + 1 < nch) load_v(nv++);  // the v buffer is free: U of chunk c has completed
         }
       }
       // (3) delta = D_X rows 64-127 (warps 2 and 3): delta (f16, over Gamma Q^) and Ds = delta e^{G_C - G_i}
       // (over -W)
       if (ok) ok = mbar_wait_warp(&bar[B_X_FULL + s], ph, abort, err, kErrTimeoutAccum);
+      if (ok && warp == 2 && lane == 0 && c + 1 < nch) load_v(nv++);  // the v buffer is free: U has completed
       if (ok && q4 >= 2) {
         tc_fence_after();
         const int i = r - 64;
-        const float sc = fexp(sG[s * CH + CH - 1] - sG[s * CH + i]);
+        const float sc = fexp(sG[s * CH + CH - 1] - sG[s * CH + i]) * sN[s * 128 + i];  // K^T Ds = K^T (rk Ds)
         for (int cb = 0; cb < 4; cb++) {
           uint32_t v[32];
           tmem_ld32(tmem + lanes + kColX + s * 128 + cb * 32, v);
@@ -514,48 +555,72 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int colh = pw >> 2;                 // the half of the columns this warp takes of its lanes' rows
     const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
     float* sa = reinterpret_cast<float*>(base + kOffA);
-    float* sx = reinterpret_cast<float*>(base + kOffX);
     float* sy = reinterpret_cast<float*>(base + kOffY);
     const float qscale = rsqrtf((float)DK);
     bool ok = true;
-    // the gates of chunk c (beta for threads 0-63, g for 64-127), loaded one chunk ahead
-    auto gate = [&](int c) -> float {
-      const int i = pt & 63;
-      if (pt >= 128 || c >= nch || c * CH + i >= L) return 0.0f;
-      const long long t = tok0 + c * CH + i;
-      return pt < 64 ? a.beta[t * H + hd] : a.g[t * H + hd];
+    // the gates of chunk c, loaded one chunk ahead: g of positions 2 lane and 2 lane + 1 in every warp
+    // (each warp scans G itself), beta by threads 0-63
+    auto gates = [&](int c, float& g0, float& g1, float& bt) {
+      g0 = g1 = bt = 0.0f;
+      if (c >= nch) return;
+      const long long t = tok0 + (long long)c * CH;
+      const int n = min(CH, L - c * CH);
+      if (2 * lane < n) g0 = a.g[(t + 2 * lane) * H + hd];
+      if (2 * lane + 1 < n) g1 = a.g[(t + 2 * lane + 1) * H + hd];
+      if (pt < n && pt < 64) bt = a.beta[(t + pt) * H + hd];
     };
-    float gnext = gate(0);
+    float gn0, gn1, bn;
+    gates(0, gn0, gn1, bn);
     for (int c = 0; c < nch; c++) {
       const int s = c & 1;
       const uint32_t ph = (c >> 1) & 1;
       uint8_t* t = base + kOffKQW + s * kTile;
       const uint32_t dx = tmem + kColX + s * 128;
-      const float gcur = gnext;
-      gnext = gate(c + 1);
-      // (1) the chunk's k and q rows; the gates and G (G[s] and beta[s] are free: the chain's last use
-      // of them, chunk c - 2, came before its MMAs released the tile this chunk was loaded into)
+      const float g0 = gn0, g1 = gn1, bc = bn;
+      gates(c + 1, gn0, gn1, bn);
+      // (1) the chunk's raw k and q rows: [K; Q] K^T at once (rows 0-63 K K^T, rows 64-127 Q K^T); the
+      // gates, G and the decay tables, and the rows' norms beside it (G[s], beta[s] and N[s] are free:
+      // the chain's last use of them, chunk c - 2, came before the chunk c - 1 read-out that the
+      // preparation of chunk c - 1 waited for)
       if (ok) ok = mbar_wait_warp(&bar[B_KQ_FULL + s], ph, abort, err, kErrTimeoutFull);
-      if (pt < 64) sbeta[s * CH + pt] = gcur;
-      else if (pt < 128) sg[pt - 64] = gcur;
-      prep_sync();
-      if (pw == 0) {
-        const float x0 = sg[2 * lane], x1 = sg[2 * lane + 1];
-        float sum = x0 + x1;
+      if (pt == 0 && ok) {
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(t);
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+          const uint64_t o = (uint64_t)((ks >> 2) * (kBox >> 4) + 2 * (ks & 3));
+          tc_mma_f16(tmem + kColDAP, ad + o, ad + o, kIdAP, ks > 0);
+        }
+        tc_commit(&bar[B_DAP_FULL + s]);
+      }
+      if (pt < 64) sbeta[s * CH + pt] = bc;
+      {  // G = inclusive prefix sums of g (every warp: lane l holds G_{2l}, G_{2l+1}), then the decays
+        float sum = g0 + g1;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const float u = __shfl_up_sync(0xffffffffu, sum, o);
           if (lane >= o) sum += u;
         }
-        const float before = sum - (x0 + x1);
-        sG[s * CH + 2 * lane] = before + x0;
-        sG[s * CH + 2 * lane + 1] = sum;
+        const float G0 = sum - g1, G1 = sum;
+        if (pw == 0) {
+          sG[s * CH + 2 * lane] = G0;
+          sG[s * CH + 2 * lane + 1] = G1;
+        }
+        auto g_at = [&](int j) {
+          const float u0 = __shfl_sync(0xffffffffu, G0, j >> 1), u1 = __shfl_sync(0xffffffffu, G1, j >> 1);
+          return (j & 1) ? u1 : u0;
+        };
+        const int b4 = pt >> 6, j = pt & 63;
+        const float gj = g_at(j), gm = g_at(16 * b4), gb = g_at(j & ~15);
+        sF[pt] = j < 16 * b4 ? fexp(gm - gj) : 0.0f;
+        if (pt < 64) sE[pt] = fexp(gj - gb);
+        else if (pt < 128) sGam[j] = fexp(gj);
       }
-      // (2) q^, k^ in place: thread pt takes one 64-column half (pt & 1) of row pt >> 1 (rows 0-63 K,
-      // 64-127 Q); the two halves' sums of squares meet through one shuffle
+      // (2) the row norms: thread pt takes one 64-column half (pt & 1) of row pt >> 1 (rows 0-63 k,
+      // 64-127 q); the two halves' sums of squares meet through one shuffle
       if (ok) {
         const int row = pt >> 1, hb = pt & 1;
-        uint8_t* rp = t + hb * kBox;
+        const uint8_t* rp = t + hb * kBox;
         uint4 raw[8];
 #pragma unroll
         for (int j = 0; j < 8; j++) raw[j] = *reinterpret_cast<const uint4*>(rp + swz(row, j));
@@ -570,40 +635,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-        // the scale in f16 and the products on the f16 pipe (one rounding each, as in f32; it keeps
-        // the f32 -> f16 conversions, which share a narrow pipe with the exponentials, to one per row)
-        const __half2 sc = __float2half2_rn(row < 64 ? rsqrtf(ss + 1e-6f) : rsqrtf(ss + 1e-6f) * qscale);
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-          __half2* w = reinterpret_cast<__half2*>(&raw[j]);
-#pragma unroll
-          for (int e = 0; e < 4; e++) w[e] = __hmul2(w[e], sc);
-          *reinterpret_cast<uint4*>(rp + swz(row, j)) = raw[j];
-        }
-      }
-      fence_proxy_async_smem();
-      prep_sync();
-      if (pt == 0) {
-        mbar_arrive(&bar[B_G_READY + s]);
-        if (ok) {  // [K^; Q^] K^T: rows 0-63 K^ K^T, rows 64-127 Q^ K^T
-          tc_fence_after();
-          const uint64_t ad = sw128_desc(t);
-#pragma unroll
-          for (int ks = 0; ks < 8; ks++) {
-            const uint64_t o = (uint64_t)((ks >> 2) * (kBox >> 4) + 2 * (ks & 3));
-            tc_mma_f16(tmem + kColDAP, ad + o, ad + o, kIdAP, ks > 0);
-          }
-          tc_commit(&bar[B_DAP_FULL + s]);
-        }
-      }
-      {  // the decay tables (beside the product)
-        const float* G = sG + s * CH;
-        const int b4 = pt >> 6, j = pt & 63;
-        sF[pt] = j < 16 * b4 ? fexp(G[16 * b4] - G[j]) : 0.0f;
-        if (pt < 64) sE[pt] = fexp(G[pt] - G[pt & ~15]);
-        else if (pt < 128) sGam[pt - 64] = fexp(G[pt - 64]);
+        if (hb == 0) sN[s * 128 + row] = row < 64 ? rsqrtf(ss + 1e-6f) : rsqrtf(ss + 1e-6f) * qscale;
       }
       prep_sync();
+      if (pt == 0) mbar_arrive(&bar[B_G_READY + s]);
       // (3) A (K rows) and P (Q rows) from the products, each warp 32 of the 64 columns of its lanes'
       // rows; Gamma Q^ over Q^ (each warp one 64-column half)
       if (ok) ok = mbar_wait_warp(&bar[B_DAP_FULL + s], ph, abort, err, kErrTimeoutAccum);
@@ -643,25 +678,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 16; e++) dec[16 * hf + e] = 0.0f;
           }
         }
-        if (q4 < 2) {  // K row i
-          const float bi = sbeta[s * CH + i];
-          float av[32];
+        const float* nk = sN + s * 128 + j0;  // the column norms rk_j
+        if (q4 < 2) {  // K row i: A_ij = beta_i rk_i rk_j e^{G_i - G_j} k_i.k_j
+          const float bi = sbeta[s * CH + i] * sN[s * 128 + i];
 #pragma unroll
-          for (int jj = 0; jj < 32; jj++) av[jj] = j0 + jj < i ? bi * dec[jj] * __uint_as_float(v[jj]) : 0.0f;
+          for (int j4 = 0; j4 < 8; j4++) {
+            const float4 f = *reinterpret_cast<const float4*>(nk + 4 * j4);
+            const float r4[4] = {f.x, f.y, f.z, f.w};
+            float av[4];
 #pragma unroll
-          for (int j4 = 0; j4 < 8; j4++)
-            *reinterpret_cast<float4*>(sa + i * LA + j0 + 4 * j4) = make_float4(av[4 * j4], av[4 * j4 + 1], av[4 * j4 + 2], av[4 * j4 + 3]);
-        } else {  // Q row i: its P columns (f16), then Gamma_i q^_i over one half of the row
+            for (int e = 0; e < 4; e++) {
+              const int jj = 4 * j4 + e;
+              av[e] = j0 + jj < i ? bi * r4[e] * dec[jj] * __uint_as_float(v[jj]) : 0.0f;
+            }
+            *reinterpret_cast<float4*>(sa + i * LA + j0 + 4 * j4) = make_float4(av[0], av[1], av[2], av[3]);
+          }
+        } else {  // Q row i: its P columns (f16, P_ij = rq_i rk_j e^{G_i - G_j} q_i.k_j), then Gamma_i rq_i q_i
+                  // over one half of the row
           uint8_t* pt_ = base + (s ? kOffP1 : kOffP0);
+          const float rq = sN[s * 128 + 64 + i];
 #pragma unroll
           for (int j8 = 0; j8 < 4; j8++) {
+            const float4 f0 = *reinterpret_cast<const float4*>(nk + 8 * j8), f1 = *reinterpret_cast<const float4*>(nk + 8 * j8 + 4);
+            const float r8[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
             float p[8];
 #pragma unroll
-            for (int e = 0; e < 8; e++) p[e] = dec[j8 * 8 + e] * __uint_as_float(v[j8 * 8 + e]);
+            for (int e = 0; e < 8; e++) p[e] = rq * r8[e] * dec[j8 * 8 + e] * __uint_as_float(v[j8 * 8 + e]);
             *reinterpret_cast<uint4*>(pt_ + swz(i, 4 * colh + j8)) =
                 make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
           }
-          const __half2 ga = __float2half2_rn(sGam[i]);  // Gamma_i (below f16's range: zero, as its terms)
+          const __half2 ga = __float2half2_rn(sGam[i] * rq);  // (below f16's range: zero, as its terms)
           uint8_t* qb = t + colh * kBox;
           uint4 u[8];
 #pragma unroll
@@ -678,8 +724,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       prep_sync();
       // (4) T = (I + A)^-1
-      tri_inverse(sa, sx, sy, pw, pt, lane);
-      // (5) T1 = T diag(beta Gamma), T2 = T diag(beta) (f16), once U of chunk c - 1 has read T2 (and W
+      tri_inverse(sa, sy, pw, pt, lane);
+      // (5) T1 = T diag(beta Gamma rk), T2 = T diag(beta) (f16), once U of chunk c - 1 has read T2 (and W
       // of chunk c - 1, issued before it, T1); thread pt: row pt >> 2, columns 16 (pt & 3) ..
       if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
       // ... and once the chain has stored chunk c - 1's O through T1
@@ -690,15 +736,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         float tv[16], bj[16], gj[16];  // loaded before any store (see the A and P loops)
 #pragma unroll
         for (int j4 = 0; j4 < 4; j4++) {  // T is lower triangular: its entries above the diagonal are zeros
-          const float4 f = *reinterpret_cast<const float4*>(sx + i * LA + j0 + 4 * j4);
+          const float4 f = *reinterpret_cast<const float4*>(sa + i * LA + j0 + 4 * j4);
           tv[4 * j4] = f.x, tv[4 * j4 + 1] = f.y, tv[4 * j4 + 2] = f.z, tv[4 * j4 + 3] = f.w;
         }
 #pragma unroll
         for (int j4 = 0; j4 < 4; j4++) {
           const float4 f = *reinterpret_cast<const float4*>(be + j0 + 4 * j4);
           const float4 h = *reinterpret_cast<const float4*>(sGam + j0 + 4 * j4);
+          const float4 nk = *reinterpret_cast<const float4*>(sN + s * 128 + j0 + 4 * j4);
           bj[4 * j4] = f.x, bj[4 * j4 + 1] = f.y, bj[4 * j4 + 2] = f.z, bj[4 * j4 + 3] = f.w;
-          gj[4 * j4] = h.x, gj[4 * j4 + 1] = h.y, gj[4 * j4 + 2] = h.z, gj[4 * j4 + 3] = h.w;
+          gj[4 * j4] = h.x * nk.x, gj[4 * j4 + 1] = h.y * nk.y, gj[4 * j4 + 2] = h.z * nk.z, gj[4 * j4 + 3] = h.w * nk.w;
         }
 #pragma unroll
         for (int j8 = 0; j8 < 2; j8++) {
@@ -707,7 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 8; e++) {
             const int k = j8 * 8 + e;
             t2[e] = tv[k] * bj[k];
-            t1[e] = t2[e] * gj[k];  // Gamma_j
+            t1[e] = t2[e] * gj[k];  // Gamma_j rk_j (W = T diag(beta Gamma) K^ = T1 K)
           }
           const int pc = (j0 >> 3) + j8;
           *reinterpret_cast<uint4*>(base + kOffT1 + swz(i, pc)) =
@@ -726,47 +773,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int ks = 0; ks < 4; ks++) tc_mma_f16(dx, ad + (uint64_t)(2 * ks), bd + (uint64_t)(128 * ks), kIdB, ks > 0);
           tc_commit(&bar[B_W_FULL + s]);
+          // the chain takes the chunk from here: -W out of W, then U and the state products
+          mbar_arrive(&bar[B_WQ_READY + s]);
         }
       }
-      ok = __all_sync(0xffffffffu, ok);  // the issuing thread's warp agrees again before the warp-wide waits
-      // (6) -W (D_X rows 0-63) over rows 128-191 of the tile, each warp one 64-column half
-      if (ok && q4 < 2) {
-        ok = mbar_wait_warp(&bar[B_W_FULL + s], ph, abort, err, kErrTimeoutAccum);
-        if (ok) {
-          tc_fence_after();
-          const int i = q4 * 32 + lane;
-          uint8_t* box = t + colh * kBox;
-          for (int cb = 0; cb < 2; cb++) {
-            uint32_t v[32];
-            tmem_ld32(dx + lanes + (2 * colh + cb) * 32, v);
-            tc_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-              *reinterpret_cast<uint4*>(box + swz(128 + i, cb * 4 + j)) =
-                  make_uint4(pack_h2(-__uint_as_float(v[8 * j]), -__uint_as_float(v[8 * j + 1])),
-                             pack_h2(-__uint_as_float(v[8 * j + 2]), -__uint_as_float(v[8 * j + 3])),
-                             pack_h2(-__uint_as_float(v[8 * j + 4]), -__uint_as_float(v[8 * j + 5])),
-                             pack_h2(-__uint_as_float(v[8 * j + 6]), -__uint_as_float(v[8 * j + 7])));
-          }
-        }
-      }
-      fence_proxy_async_smem();
       tc_fence_before();
       // every preparation warp takes the same path through the barriers; a warp that gave up tells the others
-      if (!__all_sync(0xffffffffu, ok)) *abort = 1;
-      prep_sync();
-      ok = ok && !*abort;
-      if (pt == 0 && ok) {  // U = [0; T2] V into D_X[s] (rows 0-63 zero: the start of Gamma Q^ S)
-        mbar_arrive(&bar[B_WQ_READY + s]);
-        ok = mbar_wait(&bar[B_V_FULL + s], ph, abort, err, kErrTimeoutFull);
-        if (ok) {
-          tc_fence_after();
-          const uint64_t ad = sw128_desc(base + kOffZ), bd = sw128_mn_desc(base + kOffV, 8192);
-#pragma unroll
-          for (int ks = 0; ks < 4; ks++) tc_mma_f16(dx, ad + (uint64_t)(2 * ks), bd + (uint64_t)(128 * ks), kIdB, ks > 0);
-          tc_commit(&bar[B_U_DONE + s]);
-        }
-      }
       if (!__all_sync(0xffffffffu, ok)) *abort = 1;
       prep_sync();
       if (*abort) ok = false;

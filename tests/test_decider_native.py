@@ -29,8 +29,11 @@ def test_native_decider_matches_python(small_model):
     nat.close()
 
 
-def _close_answers(a, b, tol=2e-3):
-    """Two response bodies from different batchings: same keys, labels and choices, numbers within tol."""
+def _close_answers(a, b, tol=3e-3):
+    """Two response bodies from different batchings: same keys, labels and choices, numbers within tol.
+    A request alone and the same request in a packed batch can take different gated-delta kernels (the
+    fused scan or the two-phase one, chosen per layer by the batch's shape), whose f16 rounding points
+    differ; each is checked against the oracle on its own."""
     assert a.keys() == b.keys()
     assert a["model"] == b["model"] and a["usage"] == b["usage"]
     for name in a["answers"]:
