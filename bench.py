@@ -515,7 +515,10 @@ def run_ours(args, world, rank, local):
 
 def _timed_launches(fn, steps, warmup, flush=None, stream=None):
     """Median device time (ms) of `steps` launches of fn after `warmup`, each timed alone with CUDA
-    events on the launching stream, with L2 flushed (a 256 MB write) before each."""
+    events on the launching stream, with L2 flushed (a 256 MB write) before each. A 100k-cycle spin
+    kernel (torch.cuda._sleep, ~50 us) goes between the flush and the first event, so that the host's
+    work of the call (ctypes, tensor maps, launch) is done while the device is busy and the events
+    bracket device time only."""
     import torch
     for _ in range(warmup):
         fn()
@@ -525,6 +528,7 @@ def _timed_launches(fn, steps, warmup, flush=None, stream=None):
         if flush is not None:
             flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(100_000)
         e0.record(stream)
         fn()
         e1.record(stream)

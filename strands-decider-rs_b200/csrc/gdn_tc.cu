@@ -74,7 +74,7 @@ enum {
   B_X_FULL = 14,     // [2] [Gamma Q^; -W] S accumulated
   B_S_FULL = 16,     // [2] the state update completed
   B_O_FULL = 18,     // [2] P delta accumulated (O complete): every MMA of the chunk has completed
-  B_O_READ = 20,     // [2] O read out of tensor memory and stored (2 arrivals)
+  B_O_READ = 20,     // [2] O read out of tensor memory and stored, its staging (P) read (2 arrivals)
   B_END_PREP = 22,   // every MMA of the preparation completed (teardown)
   B_END_CHAIN = 23,  // every MMA of the chain completed (teardown)
   kBars = 24
@@ -335,11 +335,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     // O rows (D_X rows 0-63, warps 0 and 1) of chunk c to global memory, then D_X[c & 1] is released;
     // the MMAs of chunk c have all completed, so its tile takes chunk c + 2's k and q rows. A warp whose
-    // 32 rows all lie in the sequence stores them as four 32 x 32 blocks through shared memory (the T1
-    // tile, 4 KB per warp: free from W of chunk c until the preparation of chunk c + 1 writes T1, which
-    // waits for this read-out) with the TMA, in whole 128-byte lines: lane-per-row stores from the
-    // registers would write 32 rows' 16-byte pieces per instruction and hold up the shared-memory
-    // traffic of the preparation warps beside them. The ragged rows of a last chunk are stored directly.
+    // 32 rows all lie in the sequence stores them as four 32 x 32 blocks through shared memory (chunk c's
+    // P tile, 4 KB per warp: free once P delta of chunk c has completed, until the preparation of chunk
+    // c + 2 writes P there, which waits for this read-out) with the TMA, in whole 128-byte lines:
+    // lane-per-row stores from the registers would write 32 rows' 16-byte pieces per instruction and hold
+    // up the shared-memory traffic of the preparation warps beside them. (Other MMAs read the tile only as
+    // the spare rows 64-127 of an M = 128 operand, whose products are not used.) The ragged rows of a
+    // last chunk are stored directly.
     auto read_o = [&](int c) {
       const int s = c & 1;
       if (ok) ok = mbar_wait_warp(&bar[B_O_FULL + s], (c >> 1) & 1, abort, err, kErrTimeoutAccum);
@@ -348,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const int n = min(CH, L - c * CH);
         const bool whole = n >= 32 * (q4 + 1);
-        uint8_t* stage = base + kOffT1 + q4 * 4096;
+        uint8_t* stage = base + (s ? kOffP1 : kOffP0) + q4 * 4096;
         // tcgen05.ld and wait::ld are warp-collective (.sync.aligned): every lane of the warp executes
         // the same loads, and only the stores are limited to the chunk's rows
         float* dst = a.o + (size_t)(tok0 + c * CH + r) * H * DK + hd * DK;
@@ -642,8 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (3) A (K rows) and P (Q rows) from the products, each warp 32 of the 64 columns of its lanes'
       // rows; Gamma Q^ over Q^ (each warp one 64-column half)
       if (ok) ok = mbar_wait_warp(&bar[B_DAP_FULL + s], ph, abort, err, kErrTimeoutAccum);
-      if (ok && q4 >= 2 && c >= 2)  // P[s] is free once the chain's P delta of chunk c - 2 has completed
-        ok = mbar_wait_warp(&bar[B_O_FULL + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty);
+      if (ok && q4 >= 2 && c >= 2)  // P[s] is free once the chain has stored chunk c - 2's O through it
+        ok = mbar_wait_warp(&bar[B_O_READ + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty);
       if (ok) {
         tc_fence_after();
         uint32_t v[32];
@@ -728,8 +730,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (5) T1 = T diag(beta Gamma rk), T2 = T diag(beta) (f16), once U of chunk c - 1 has read T2 (and W
       // of chunk c - 1, issued before it, T1); thread pt: row pt >> 2, columns 16 (pt & 3) ..
       if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
-      // ... and once the chain has stored chunk c - 1's O through T1
-      if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_O_READ + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
       if (ok) {
         const int i = pt >> 2, j0 = (pt & 3) * 16;
         const float* be = sbeta + s * CH;

@@ -409,24 +409,28 @@ __global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
 }
 
 // Split-K finish: sums the splits' f32 partials in split order (deterministic), then f16 (or the
-// SwiGLU of interleaved gate/up rows).
-__global__ void gemm_finish(const float* __restrict__ ws, int splits, int M, int N, __half* __restrict__ y, int ldy, int silu) {
-  const int64_t total = silu ? (int64_t)M * (N / 2) : (int64_t)M * N;
-  const int64_t slice = (int64_t)M * N;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+// SwiGLU of interleaved gate/up rows). Rows blockIdx.y, + gridDim.y, ...; each thread takes four
+// partial columns (16-byte loads; N is a multiple of 8) and stores four outputs, or two with SwiGLU.
+__global__ void __launch_bounds__(256) gemm_finish(const float* __restrict__ ws, int splits, int M, int N,
+                                                   __half* __restrict__ y, int ldy, int silu) {
+  const int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (n >= N) return;
+  const size_t slice = (size_t)M * N;
+  for (int m = blockIdx.y; m < M; m += gridDim.y) {
+    const float* p = ws + (size_t)m * N + n;
+    float4 s = *reinterpret_cast<const float4*>(p);
+    for (int z = 1; z < splits; z++) {
+      const float4 t = *reinterpret_cast<const float4*>(p + z * slice);
+      s.x += t.x, s.y += t.y, s.z += t.z, s.w += t.w;
+    }
     if (!silu) {
-      const int64_t m = i / N, n = i % N;
-      float s = 0.0f;
-      for (int z = 0; z < splits; z++) s += ws[z * slice + i];
-      y[m * ldy + n] = __float2half_rn(s);
-    } else {
-      const int64_t half = N / 2, m = i / half, j = i % half;
-      float gs = 0.0f, us = 0.0f;
-      for (int z = 0; z < splits; z++) {
-        gs += ws[z * slice + m * N + 2 * j];
-        us += ws[z * slice + m * N + 2 * j + 1];
-      }
-      y[m * ldy + j] = __float2half_rn(swiglu(gs, us));
+      const __half2 a = __floats2half2_rn(s.x, s.y), b = __floats2half2_rn(s.z, s.w);
+      uint2 o;
+      o.x = *reinterpret_cast<const uint32_t*>(&a);
+      o.y = *reinterpret_cast<const uint32_t*>(&b);
+      *reinterpret_cast<uint2*>(y + (size_t)m * ldy + n) = o;
+    } else {  // columns (2j, 2j + 1) are gate and up of output j = n / 2 (and j + 1)
+      *reinterpret_cast<__half2*>(y + (size_t)m * ldy + n / 2) = __floats2half2_rn(swiglu(s.x, s.y), swiglu(s.z, s.w));
     }
   }
 }
@@ -647,6 +651,7 @@ cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half*
     splits = (KT + kps - 1) / kps;
     if (splits * slice > ws_bytes) splits = 1, kps = KT;
   }
+  if (w.n % 4) splits = 1, kps = KT;  // the finish reads four partial columns at a time
   CUtensorMap map;
   if (make_act_map(&map, act, M, w.k, lda, bn) != 0) return cudaErrorInvalidValue;
   TileGrid tg{w.npad / kBM, (M + bn - 1) / bn, splits, kps, KT, gemm_token_major(w, M) ? 1 : 0};
@@ -656,9 +661,8 @@ cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half*
                 : launch_epi<kEpiStore>(bn, map, w, M, tg, num_sms, y, ldy, nullptr, err, st);
   cudaError_t e = launch_epi<kEpiPartial>(bn, map, w, M, tg, num_sms, y, ldy, ws, err, st);
   if (e != cudaSuccess) return e;
-  const int64_t total = silu ? (int64_t)M * (w.n / 2) : (int64_t)M * w.n;
-  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4096);
-  gemm_finish<<<blocks, 256, 0, st>>>(ws, splits, M, w.n, y, ldy, silu ? 1 : 0);
+  const dim3 grid((w.n / 4 + 255) / 256, std::min(M, 65535));
+  gemm_finish<<<grid, 256, 0, st>>>(ws, splits, M, w.n, y, ldy, silu ? 1 : 0);
   return cudaGetLastError();
 }
 
