@@ -697,22 +697,40 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
     LK(SD_PROF_GEMM, flops, sd::gemm_q4(w, a, l, lda, y, ldy, silu, e->ws, e->ws_bytes, e->d_err, e->num_sms, st, nl));
     return SD_OK;
   };
+  // x += f16(a W^T): the layer's output matmuls add into the residual stream in their epilogue
+  auto mm_add = [&](const QWeight& w, const __half* a, int lda) -> int {
+    const double flops = 2.0 * L * w.n * w.k;
+    LK(SD_PROF_GEMM, flops,
+       sd::gemm_q4(w, a, l, lda, nullptr, d.d, false, e->ws, e->ws_bytes, e->d_err, e->num_sms, st, nl, e->x));
+    return SD_OK;
+  };
   int rc;
 #define MM(...)                          \
   do {                                   \
     if ((rc = mm(__VA_ARGS__)) != SD_OK) \
       return rc;                         \
   } while (0)
+#define MM_ADD(...)                          \
+  do {                                       \
+    if ((rc = mm_add(__VA_ARGS__)) != SD_OK) \
+      return rc;                             \
+  } while (0)
+  // whether y holds a layer output not yet added into x (an adapter's projection: its bias is added
+  // to the f16 output first, as the reference does)
+  bool pending = false;
   const double row_bytes = (double)d.d * (4 + 2);
   LK(SD_PROF_OTHER, L * (d.d / 32 * (4.0 * e->embed_bits + 2) + row_bytes),
      sd::launch_embed_norm(fk ? fk->ids : e->d_ids, l, e->embed_q, e->embed_s, e->embed_bits, d.d, e->vocab, e->layers[0].in_norm, e->x,
                            e->h, e->d_err, st));
   for (int i = 0; i < e->n_layers; i++) {
     const LayerW& Lw = e->layers[i];
-    if (i > 0) LK(SD_PROF_OTHER, L * d.d * 12.0, sd::launch_add_norm(e->x, e->y, Lw.in_norm, l, d.d, true, e->h, st));
+    if (i > 0)
+      LK(SD_PROF_OTHER, L * d.d * (pending ? 12.0 : 6.0), sd::launch_add_norm(e->x, e->y, Lw.in_norm, l, d.d, pending, e->h, st));
+    pending = false;
     if (Lw.kind == 2) {
       MM(Lw.proj, e->h, d.d, e->y, d.d, false);
       LK(SD_PROF_OTHER, L * d.d * 4.0, sd::launch_add_bias(e->y, Lw.bias, l, d.d, st));
+      pending = true;
     } else {
       if (Lw.kind == 0) {
         const int N = Lw.in_proj.n;
@@ -774,7 +792,7 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
                                                 e->decay, e->state[Lw.slot], has_cache, e->of, l, d.h, e->gdn_scratch,
                                                 e->gdn_scratch_bytes, st)));
         LK(SD_PROF_OTHER, L * d.h * d.dv * 8.0, sd::launch_gnorm(e->of, e->big, N, C, Lw.gnorm, l, d.h, e->o, st));
-        MM(Lw.out_proj, e->o, d.h * d.dv, e->y, d.d, false);
+        MM_ADD(Lw.out_proj, e->o, d.h * d.dv);
       } else {
         const int N = Lw.qkv.n;
         MM(Lw.qkv, e->h, d.d, e->big, N, false);
@@ -820,7 +838,7 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
                                   fk->kp + (size_t)Lw.slot * fk->nseq, fk->vp + (size_t)Lw.slot * fk->nseq,
                                   fk->k_out + (size_t)Lw.slot * fk->nseq, fk->v_out + (size_t)Lw.slot * fk->nseq, fk->nseq,
                                   fk->max_rows, st));
-          MM(Lw.o_proj, e->o, d.hq * d.hd, e->y, d.d, false);
+          MM_ADD(Lw.o_proj, e->o, d.hq * d.hd);
         } else {
         LK(SD_PROF_OTHER, L * (N * 2.0 + (d.hq + 2.0 * d.hk) * d.hd * 2.0),
            sd::launch_qk_prep(e->big, N, Lw.q_norm, Lw.k_norm, e->rope, l, p, SD_CONTEXT, d, nullptr, e->q, e->kc[Lw.slot],
@@ -840,21 +858,25 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
               sd::launch_attention(e->q, e->kc[Lw.slot], e->vc[Lw.slot], e->big, N, d.hd, 2 * d.hd, e->o, l, p, SD_CONTEXT,
                                    d.hq, d.hk, d.hd, splits, e->ws, e->ws_bytes, st)));
         }
-        MM(Lw.o_proj, e->o, d.hq * d.hd, e->y, d.d, false);
+        MM_ADD(Lw.o_proj, e->o, d.hq * d.hd);
         }
       }
     }
     if (Lw.kind != 2) {
-      LK(SD_PROF_OTHER, L * d.d * 12.0, sd::launch_add_norm(e->x, e->y, Lw.post_norm, l, d.d, true, e->h, st));
+      LK(SD_PROF_OTHER, L * d.d * 6.0, sd::launch_add_norm(e->x, nullptr, Lw.post_norm, l, d.d, false, e->h, st));
       MM(Lw.gate_up, e->h, d.d, e->mid, d.inter, true);
-      MM(Lw.down, e->mid, d.inter, e->y, d.d, false);
+      MM_ADD(Lw.down, e->mid, d.inter);
     }
-    if (e->trace_dev) LK(SD_PROF_OTHER, L * d.d * 10.0, sd::launch_trace(e->x, e->y, l * d.d, e->trace_dev + (size_t)i * l * d.d, st));
+    if (e->trace_dev)
+      LK(SD_PROF_OTHER, L * d.d * 10.0,
+         sd::launch_trace(e->x, pending ? e->y : nullptr, l * d.d, e->trace_dev + (size_t)i * l * d.d, st));
   }
   if (nrows > 0)
     LK(SD_PROF_OTHER, nrows * d.d * 14.0,
-       sd::launch_final_norm(e->x, e->y, e->final_norm, fk ? fk->rows : e->d_rows, nrows, l, d.d, e->out, e->d_err, st));
+       sd::launch_final_norm(e->x, pending ? e->y : nullptr, e->final_norm, fk ? fk->rows : e->d_rows, nrows, l, d.d, e->out,
+                             e->d_err, st));
 #undef MM
+#undef MM_ADD
   return SD_OK;
 }
 

@@ -81,7 +81,10 @@ struct GemmCfg {
   static_assert(SR % NG == 0, "raw ring: each slot belongs to one group");
 };
 
-enum Epi { kEpiStore = 0, kEpiSilu = 1, kEpiPartial = 2 };
+// kEpiAdd: the f16-rounded outputs are added into the f32 rows at `ws` (ldy floats apart): the
+// residual stream x += f16(A W^T), the reference's matmul-then-add_norm (src/kernels.rs:93-120) with
+// the add done here.
+enum Epi { kEpiStore = 0, kEpiSilu = 1, kEpiPartial = 2, kEpiAdd = 3 };
 // The configuration a kernel instantiation uses.
 template <int BN, int EPI>
 using CfgOf = GemmCfg<BN, (EPI == kEpiSilu && BN >= 192) ? 1 : 0>;
@@ -320,7 +323,7 @@ __global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
       tc_fence_after();
       const uint32_t acc = tmem + buf * Cfg::kAccCols + ((uint32_t)(q * 32) << 16);
       const int n0 = nt * kBM + q * 32;  // first weight row of this warp
-      if (EPI != kEpiPartial) {
+      if (EPI == kEpiStore || EPI == kEpiSilu) {
         __half* st = reinterpret_cast<__half*>(stg);  // [32 tokens][40]
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -368,6 +371,46 @@ __global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
           }
           __syncwarp();
         }
+      } else if (EPI == kEpiAdd) {
+        float* st = reinterpret_cast<float*>(stg);  // [16 tokens][36], f16-rounded
+        // four tokens per instruction, eight lanes a token's 32 outputs (whole 128-byte lines); the x
+        // rows of the next 16 tokens are loaded while these are added, so the loads' latency overlaps
+        const int ch = (lane & 7) * 4;
+        auto x_at = [&](int mbase, int r4) -> float* {
+          const int m = mbase + 4 * r4 + (lane >> 3);
+          return m < M && n0 + ch < N ? ws + (size_t)m * ldy + n0 + ch : nullptr;  // N is a multiple of 4
+        };
+        float4 cur[4], nxt[4];
+#pragma unroll
+        for (int r4 = 0; r4 < 4; r4++)
+          if (const float* p = x_at(mt * BN, r4)) cur[r4] = *reinterpret_cast<const float4*>(p);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          const int mbase = mt * BN + c0;
+          if (mbase >= M) break;
+          if (c0 + 16 < BN) {
+#pragma unroll
+            for (int r4 = 0; r4 < 4; r4++)
+              if (const float* p = x_at(mbase + 16, r4)) nxt[r4] = *reinterpret_cast<const float4*>(p);
+          }
+          uint32_t v[16];
+          tmem_ld16(acc + c0, v);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; j++) st[j * 36 + lane] = __half2float(__float2half_rn(__uint_as_float(v[j])));
+          __syncwarp();
+#pragma unroll
+          for (int r4 = 0; r4 < 4; r4++) {
+            if (float* p = x_at(mbase, r4)) {
+              const float4 a = *reinterpret_cast<const float4*>(st + (4 * r4 + (lane >> 3)) * 36 + ch);
+              float4 xv = cur[r4];
+              xv.x += a.x, xv.y += a.y, xv.z += a.z, xv.w += a.w;
+              *reinterpret_cast<float4*>(p) = xv;
+            }
+            cur[r4] = nxt[r4];
+          }
+          __syncwarp();
+        }
       } else {
         float* st = reinterpret_cast<float*>(stg);  // [16 tokens][36]
         float* part = ws + (size_t)sp * M * N;
@@ -409,10 +452,11 @@ __global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
 }
 
 // Split-K finish: sums the splits' f32 partials in split order (deterministic), then f16 (or the
-// SwiGLU of interleaved gate/up rows). Rows blockIdx.y, + gridDim.y, ...; each thread takes four
-// partial columns (16-byte loads; N is a multiple of 8) and stores four outputs, or two with SwiGLU.
+// SwiGLU of interleaved gate/up rows, or f16 added into the f32 rows at xadd). Rows blockIdx.y,
+// + gridDim.y, ...; each thread takes four partial columns (16-byte loads; N is a multiple of 8) and
+// stores four outputs, or two with SwiGLU.
 __global__ void __launch_bounds__(256) gemm_finish(const float* __restrict__ ws, int splits, int M, int N,
-                                                   __half* __restrict__ y, int ldy, int silu) {
+                                                   __half* __restrict__ y, int ldy, int silu, float* __restrict__ xadd) {
   const int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (n >= N) return;
   const size_t slice = (size_t)M * N;
@@ -423,7 +467,13 @@ __global__ void __launch_bounds__(256) gemm_finish(const float* __restrict__ ws,
       const float4 t = *reinterpret_cast<const float4*>(p + z * slice);
       s.x += t.x, s.y += t.y, s.z += t.z, s.w += t.w;
     }
-    if (!silu) {
+    if (xadd) {
+      float4* dx = reinterpret_cast<float4*>(xadd + (size_t)m * ldy + n);
+      float4 xv = *dx;
+      xv.x += __half2float(__float2half_rn(s.x)), xv.y += __half2float(__float2half_rn(s.y));
+      xv.z += __half2float(__float2half_rn(s.z)), xv.w += __half2float(__float2half_rn(s.w));
+      *dx = xv;
+    } else if (!silu) {
       const __half2 a = __floats2half2_rn(s.x, s.y), b = __floats2half2_rn(s.z, s.w);
       uint2 o;
       o.x = *reinterpret_cast<const uint32_t*>(&a);
@@ -637,7 +687,7 @@ bool gemm_token_major(const QWeight& w, int M) {
 }
 
 cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
-                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch) {
+                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch, float* xadd) {
   if (nlaunch) *nlaunch = 0;
   if (M <= 0) return cudaSuccess;
   int bn, splits, kps;
@@ -656,13 +706,15 @@ cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half*
   if (make_act_map(&map, act, M, w.k, lda, bn) != 0) return cudaErrorInvalidValue;
   TileGrid tg{w.npad / kBM, (M + bn - 1) / bn, splits, kps, KT, gemm_token_major(w, M) ? 1 : 0};
   if (nlaunch) *nlaunch = splits == 1 ? 1 : 2;
+  if (xadd && (silu || w.n % 4 || ldy % 4 || (uintptr_t)xadd % 16)) return cudaErrorInvalidValue;
   if (splits == 1)
-    return silu ? launch_epi<kEpiSilu>(bn, map, w, M, tg, num_sms, y, ldy, nullptr, err, st)
-                : launch_epi<kEpiStore>(bn, map, w, M, tg, num_sms, y, ldy, nullptr, err, st);
+    return xadd ? launch_epi<kEpiAdd>(bn, map, w, M, tg, num_sms, nullptr, ldy, xadd, err, st)
+                : silu ? launch_epi<kEpiSilu>(bn, map, w, M, tg, num_sms, y, ldy, nullptr, err, st)
+                       : launch_epi<kEpiStore>(bn, map, w, M, tg, num_sms, y, ldy, nullptr, err, st);
   cudaError_t e = launch_epi<kEpiPartial>(bn, map, w, M, tg, num_sms, y, ldy, ws, err, st);
   if (e != cudaSuccess) return e;
   const dim3 grid((w.n / 4 + 255) / 256, std::min(M, 65535));
-  gemm_finish<<<grid, 256, 0, st>>>(ws, splits, M, w.n, y, ldy, silu ? 1 : 0);
+  gemm_finish<<<grid, 256, 0, st>>>(ws, splits, M, w.n, y, ldy, silu ? 1 : 0, xadd);
   return cudaGetLastError();
 }
 
@@ -672,7 +724,9 @@ static cudaError_t preload_bn() {
   if ((e = cudaFuncSetAttribute(gemm_q4_tc<BN, kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)CfgOf<BN, kEpiStore>::kSmem)) != cudaSuccess ||
       (e = cudaFuncSetAttribute(gemm_q4_tc<BN, kEpiSilu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)CfgOf<BN, kEpiSilu>::kSmem)) != cudaSuccess)
+                                (int)CfgOf<BN, kEpiSilu>::kSmem)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(gemm_q4_tc<BN, kEpiAdd>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)CfgOf<BN, kEpiAdd>::kSmem)) != cudaSuccess)
     return e;
   return cudaFuncSetAttribute(gemm_q4_tc<BN, kEpiPartial>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)CfgOf<BN, kEpiPartial>::kSmem);

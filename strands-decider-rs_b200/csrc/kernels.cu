@@ -107,7 +107,8 @@ __global__ void __launch_bounds__(256) add_norm_kernel(float* __restrict__ x, co
 }
 
 // The final norm (src/kernels.rs:93-120 with add and f32 out, src/engine.rs:519-522): for each
-// requested row, x += y, out = x * inv * w in f32.
+// requested row, x += y (y null: nothing to add, the last matmul added its output already),
+// out = x * inv * w in f32.
 __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, const __half* __restrict__ y,
                                                          const float* __restrict__ w, const int* __restrict__ rows, int l,
                                                          int d, float* __restrict__ out, int* err) {
@@ -124,8 +125,11 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
     const int c = threadIdx.x + 256 * i;
     float a = 0.0f;
     if (c < d) {
-      a = x[(size_t)r * d + c] + __half2float(y[(size_t)r * d + c]);
-      x[(size_t)r * d + c] = a;
+      a = x[(size_t)r * d + c];
+      if (y) {
+        a += __half2float(y[(size_t)r * d + c]);
+        x[(size_t)r * d + c] = a;
+      }
     }
     v[i] = a;
     ss += a * a;
@@ -489,7 +493,8 @@ __global__ void __launch_bounds__(256) qk_prep_warp_kernel(const __half* __restr
 }
 
 __global__ void trace_kernel(const float* __restrict__ x, const __half* __restrict__ y, int n, float* __restrict__ out) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = x[i] + __half2float(y[i]);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = y ? x[i] + __half2float(y[i]) : x[i];
 }
 
 // add_bias (src/kernels.rs:138-149): y = f16(y + c[j]).

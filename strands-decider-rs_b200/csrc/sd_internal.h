@@ -39,8 +39,9 @@ cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool 
 void gemm_plan(const QWeight& w, int M, int num_sms, int* bn, int* splits, int* kps);
 // y[M][ldy] = act[M][K] W^T, or SwiGLU of interleaved gate/up rows into y[M][N/2] when silu; ws is
 // the f32 split-K workspace (M * N floats; smaller disables split-K); *nlaunch gets the kernel count.
+// With xadd (f32 rows ldy floats apart, n a multiple of 4, no silu): x += f16(act W^T) instead of y.
 cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
-                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch = nullptr);
+                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch = nullptr, float* xadd = nullptr);
 int make_act_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
 int make_map_3d(CUtensorMap* map, const void* ptr, int x, int y, int z, long long ystride, long long zstride, int box_y);
 // The error words of the standalone calls' kernels (no engine: the C ABI's sd_attention*, sd_gdn):
@@ -139,6 +140,7 @@ cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff
                          cudaStream_t st);
 cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,
                            int lt, const Dims& dm, const int* tpos, __half* q, __half* kc, __half* vc, cudaStream_t st);
+// out = x + y (y may be null: out = x)
 cudaError_t launch_trace(const float* x, const __half* y, int n, float* out, cudaStream_t st);
 // the failure path's self-test: a bounded wait that runs out after limit_ns (see kernels.cu)
 cudaError_t launch_wait_probe(int* err, unsigned long long limit_ns, cudaStream_t st);
