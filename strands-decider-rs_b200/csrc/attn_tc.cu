@@ -62,10 +62,10 @@ constexpr int kThreads = 192;
 __device__ int g_attn_tc_err;  // error slot of calls without one
 
 SD_DEV bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
-  return mbar_wait(bar, parity, abort, err ? err : &g_attn_tc_err, code);
+  return mbar_wait<false>(bar, parity, abort, err ? err : &g_attn_tc_err, code);
 }
 SD_DEV bool wait_bar_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
-  return mbar_wait_warp(bar, parity, abort, err ? err : &g_attn_tc_err, code);
+  return mbar_wait_warp<false>(bar, parity, abort, err ? err : &g_attn_tc_err, code);
 }
 SD_DEV float ex2(float x) {  // 2^x (the hardware's approximate exponential, as __expf uses)
   float y;

@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // last chunk are stored directly.
     auto read_o = [&](int c) {
       const int s = c & 1;
-      if (ok) ok = mbar_wait_warp(&bar[B_O_FULL + s], (c >> 1) & 1, abort, err, kErrTimeoutAccum);
+      if (ok) ok = mbar_wait_warp<false>(&bar[B_O_FULL + s], (c >> 1) & 1, abort, err, kErrTimeoutAccum);
       if (ok && warp == 0 && lane == 0 && c + 2 < nch) load_kq(nkq++);
       if (ok && q4 < 2) {
         tc_fence_after();
@@ -397,8 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (0) O of the previous chunk first (the next chunk's preparation waits for it before it writes T1)
       if (c >= 1) read_o(c - 1);
       // (1) the entry state S_{c-1}: its f16 copy (the operand of [Gamma Q^; -W] S), Gamma_C S back
-      if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_S_FULL + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutAccum);
-      if (ok) ok = mbar_wait_warp(&bar[B_G_READY + s], ph, abort, err, kErrTimeoutFull);
+      if (ok && c >= 1) ok = mbar_wait_warp<false>(&bar[B_S_FULL + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutAccum);
+      if (ok) ok = mbar_wait_warp<false>(&bar[B_G_READY + s], ph, abort, err, kErrTimeoutFull);
       if (ok) {
         tc_fence_after();
         const float gc = fexp(sG[s * CH + CH - 1]);
@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (2) -W (D_X rows 0-63, warps 0 and 1) over rows 128-191 of the tile, once W has completed; the
       // preparation has gone on to the next chunk
       if (ok && q4 < 2) {
-        ok = mbar_wait_warp(&bar[B_W_FULL + s], ph, abort, err, kErrTimeoutAccum);
+        ok = mbar_wait_warp<false>(&bar[B_W_FULL + s], ph, abort, err, kErrTimeoutAccum);
         if (ok) {
           tc_fence_after();
           for (int cb = 0; cb < 4; cb++) {
@@ -455,8 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = ok && !*abort;
       if (warp == 2) {  // U = [0; T2] V into D_X[s] (rows 0-63 zero), then [Gamma Q^; -W] S onto it (rows
                         // 0-63 Gamma Q^ S, rows 64-127 delta)
-        if (ok) ok = mbar_wait_warp(&bar[B_WQ_READY + s], ph, abort, err, kErrTimeoutFull);
-        if (ok) ok = mbar_wait_warp(&bar[B_V_FULL + s], ph, abort, err, kErrTimeoutFull);
+        if (ok) ok = mbar_wait_warp<false>(&bar[B_WQ_READY + s], ph, abort, err, kErrTimeoutFull);
+        if (ok) ok = mbar_wait_warp<false>(&bar[B_V_FULL + s], ph, abort, err, kErrTimeoutFull);
         if (ok && lane == 0) {
           tc_fence_after();
           {
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // (3) delta = D_X rows 64-127 (warps 2 and 3): delta (f16, over Gamma Q^) and Ds = delta e^{G_C - G_i}
       // (over -W)
-      if (ok) ok = mbar_wait_warp(&bar[B_X_FULL + s], ph, abort, err, kErrTimeoutAccum);
+      if (ok) ok = mbar_wait_warp<false>(&bar[B_X_FULL + s], ph, abort, err, kErrTimeoutAccum);
       if (ok && warp == 2 && lane == 0 && c + 1 < nch) load_v(nv++);  // the v buffer is free: U has completed
       if (ok && q4 >= 2) {
         tc_fence_after();
@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the final state
     if (ok && sout) {
       const int c = nch - 1;
-      if ((ok = mbar_wait_warp(&bar[B_S_FULL + (c & 1)], (c >> 1) & 1, abort, err, kErrTimeoutAccum))) {
+      if ((ok = mbar_wait_warp<false>(&bar[B_S_FULL + (c & 1)], (c >> 1) & 1, abort, err, kErrTimeoutAccum))) {
         tc_fence_after();
         for (int cb = 0; cb < 4; cb++) {
           uint32_t v[32];
@@ -584,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // gates, G and the decay tables, and the rows' norms beside it (G[s], beta[s] and N[s] are free:
       // the chain's last use of them, chunk c - 2, came before the chunk c - 1 read-out that the
       // preparation of chunk c - 1 waited for)
-      if (ok) ok = mbar_wait_warp(&bar[B_KQ_FULL + s], ph, abort, err, kErrTimeoutFull);
+      if (ok) ok = mbar_wait_warp<false>(&bar[B_KQ_FULL + s], ph, abort, err, kErrTimeoutFull);
       if (pt == 0 && ok) {
         tc_fence_after();
         const uint64_t ad = sw128_desc(t);
@@ -643,9 +643,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (pt == 0) mbar_arrive(&bar[B_G_READY + s]);
       // (3) A (K rows) and P (Q rows) from the products, each warp 32 of the 64 columns of its lanes'
       // rows; Gamma Q^ over Q^ (each warp one 64-column half)
-      if (ok) ok = mbar_wait_warp(&bar[B_DAP_FULL + s], ph, abort, err, kErrTimeoutAccum);
+      if (ok) ok = mbar_wait_warp<false>(&bar[B_DAP_FULL + s], ph, abort, err, kErrTimeoutAccum);
       if (ok && q4 >= 2 && c >= 2)  // P[s] is free once the chain has stored chunk c - 2's O through it
-        ok = mbar_wait_warp(&bar[B_O_READ + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty);
+        ok = mbar_wait_warp<false>(&bar[B_O_READ + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty);
       if (ok) {
         tc_fence_after();
         uint32_t v[32];
@@ -729,7 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tri_inverse(sa, sy, pw, pt, lane);
       // (5) T1 = T diag(beta Gamma rk), T2 = T diag(beta) (f16), once U of chunk c - 1 has read T2 (and W
       // of chunk c - 1, issued before it, T1); thread pt: row pt >> 2, columns 16 (pt & 3) ..
-      if (ok && c >= 1) ok = mbar_wait_warp(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
+      if (ok && c >= 1) ok = mbar_wait_warp<false>(&bar[B_U_DONE + (s ^ 1)], ((c - 1) >> 1) & 1, abort, err, kErrTimeoutEmpty);
       if (ok) {
         const int i = pt >> 2, j0 = (pt & 3) * 16;
         const float* be = sbeta + s * CH;
@@ -766,7 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       prep_sync();
       if (pt == 0 && ok) {  // W = [T1; *] K^ into D_X[s], once the chain has read chunk c - 2's O out of it
-        if (c >= 2) ok = mbar_wait(&bar[B_O_READ + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty);
+        if (c >= 2) ok = mbar_wait<false>(&bar[B_O_READ + s], ((c >> 1) - 1) & 1, abort, err, kErrTimeoutEmpty);
         if (ok) {
           tc_fence_after();
           const uint64_t ad = sw128_desc(base + kOffT1), bd = sw128_mn_desc(t, kBox);
