@@ -81,6 +81,7 @@ SD_DEV uint32_t pack_h2f(float a, float b) {
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const AttnTcArgs a) {
+  grid_dep_wait();  // launched as a programmatic dependent (launch_dependent): inputs ready from here
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = base + kOffRing;
@@ -392,8 +393,7 @@ cudaError_t launch_attention_tc(const __half* q, int qrows, const __half* k, con
       make_map_3d(&km, k, HD, krows_valid, a.batch * a.hk, HD, (long long)krows * HD, TK) != 0 ||
       make_map_3d(&vm, v, HD, krows_valid, a.batch * a.hk, HD, (long long)krows * HD, 32) != 0)
     return cudaErrorInvalidValue;
-  attn_tc_kernel<<<dim3(nblk, a.hq, a.batch), kThreads, kSmem, st>>>(qm, km, vm, a);
-  return cudaGetLastError();
+  return launch_dependent(attn_tc_kernel, dim3(nblk, a.hq, a.batch), dim3(kThreads), kSmem, st, qm, km, vm, a);
 }
 
 cudaError_t take_attn_tc_err(int* code) {

@@ -159,6 +159,28 @@ SD_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "me
 SD_DEV void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may start
+// while the kernel before it in the stream is still running; this waits until that kernel has
+// completed and its memory operations are visible (a no-op for a kernel launched without it).
+SD_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Launches `kern` with programmatic stream serialization (it may be scheduled while the kernel before
+// it in `st` finishes: its launch, and whatever it does before grid_dep_wait, overlap that kernel's
+// tail). Every kernel launched this way calls grid_dep_wait before it touches memory that earlier work
+// in the stream writes or reads.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 SD_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------------------

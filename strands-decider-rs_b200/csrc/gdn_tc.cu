@@ -215,6 +215,7 @@ SD_DEV void tri_inverse(float* a, float* y, int pw, int pt, int lane) {
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap, const GdnTcArgs a) {
+  grid_dep_wait();  // launched as a programmatic dependent (launch_dependent): inputs ready from here
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = smem_align1024(smem_raw);
   uint64_t* bar = reinterpret_cast<uint64_t*>(base + kOffBar);
@@ -839,8 +840,7 @@ cudaError_t launch_gdn_tc(const __half* q, const __half* k, int qk_stride, const
       make_map_3d(&vm, v, a.h * DK, rows, zdim, v_stride, a.seq_off ? (long long)rows * v_stride : seq_v, CH) != 0 ||
       make_map_f32(&om, a.o, orows, a.h * DK, (long long)a.h * DK, 32) != 0)
     return cudaErrorInvalidValue;
-  gdn_tc_kernel<<<walks, kThreads, kSmem, st>>>(qm, km, vm, om, a);
-  return cudaGetLastError();
+  return launch_dependent(gdn_tc_kernel, dim3(walks), dim3(kThreads), kSmem, st, qm, km, vm, om, a);
 }
 
 }  // namespace sd

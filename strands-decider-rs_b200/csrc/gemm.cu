@@ -198,6 +198,7 @@ __global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
     // one thread: the activation k-tiles of each stage, one barrier per stage
     if (lane == 0) {
       prefetch_tmap(&act_map);
+      grid_dep_wait();  // the activations are the previous kernel's output
       int si = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < ntile_total && ok; t += gridDim.x) {
@@ -310,6 +311,7 @@ __global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
   } else if (warp < Cfg::kWarpRaw) {
     // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (weight rows of the tile), transposes
     // through shared memory and stores token rows with 16-byte stores
+    grid_dep_wait();  // the outputs (and x) may still be in use by the previous kernel until it completes
     const int q = warp & 3;
     uint8_t* stg = sstg + (warp - Cfg::kWarpEpi0) * Cfg::kStgBytesPerWarp;
     int lt = -1;
@@ -618,9 +620,20 @@ static cudaError_t launch_bn(const CUtensorMap& map, const QWeight& w, int M, co
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const int grid = std::min(tg.count(), num_sms);
-  kern<<<grid, Cfg::kThreads, Cfg::kSmem, st>>>(map, w.tiles, M, w.n, tg, y, ldy, ws, err);
-  return cudaGetLastError();
+  // launched as a programmatic dependent of the kernel before it: its set-up (barriers, TMEM, the
+  // weight tiles' first copies, which depend on nothing the stream computes) overlaps that kernel's
+  // tail; the activation loads and the epilogue wait for it (grid_dep_wait)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min(tg.count(), num_sms));
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, map, (const uint8_t*)w.tiles, M, w.n, tg, y, ldy, ws, err);
 }
 
 template <int EPI>

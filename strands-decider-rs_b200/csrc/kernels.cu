@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t* __restr
                                                          const __half* __restrict__ es, int bits, int d, int vocab,
                                                          const float* __restrict__ w, float* __restrict__ x,
                                                          __half* __restrict__ h, int* err) {
+  grid_dep_wait();
   __shared__ float red[8];
   const int t = blockIdx.x;
   uint32_t id = ids[t];
@@ -74,6 +75,7 @@ __global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t* __restr
 __global__ void __launch_bounds__(256) add_norm_kernel(float* __restrict__ x, const __half* __restrict__ y,
                                                        const float* __restrict__ w, int d, int add,
                                                        __half* __restrict__ h) {
+  grid_dep_wait();
   __shared__ float red[8];
   const int t = blockIdx.x;
   float* xr = x + (size_t)t * d;
@@ -112,6 +114,7 @@ __global__ void __launch_bounds__(256) add_norm_kernel(float* __restrict__ x, co
 __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, const __half* __restrict__ y,
                                                          const float* __restrict__ w, const int* __restrict__ rows, int l,
                                                          int d, float* __restrict__ out, int* err) {
+  grid_dep_wait();
   __shared__ float red[8];
   const int r = rows[blockIdx.x];
   if (r < 0 || r >= l) {  // rows given on the device are checked here
@@ -158,6 +161,7 @@ __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ bi
                                                    const __half* __restrict__ hist, int l, int C, const int* __restrict__ tstart,
                                                    const __half* const* __restrict__ hseq, const int* __restrict__ tseq,
                                                    __half* __restrict__ out) {
+  grid_dep_wait();
   const int c4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   const int t0 = blockIdx.y * kConvT;
   if (c4 >= C || t0 >= l) return;
@@ -215,6 +219,7 @@ __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ bi
 
 // hist_update (src/kernels.rs:173-190): the last 3 pre-conv rows of (old history ++ this call).
 __global__ void hist_update_kernel(const __half* __restrict__ big, int stride, __half* __restrict__ hist, int l, int C) {
+  grid_dep_wait();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   __half v[3];
@@ -231,6 +236,7 @@ __global__ void hist_update_kernel(const __half* __restrict__ big, int stride, _
 __global__ void hist_pack_kernel(const __half* __restrict__ big, int stride, int C, const int* __restrict__ seq_off,
                                  const int* __restrict__ seq_len, const __half* const* __restrict__ h_in,
                                  __half* const* __restrict__ h_out) {
+  grid_dep_wait();
   const int c = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
   __half* dst = h_out[b];
   if (c >= C || !dst) return;
@@ -250,6 +256,7 @@ __global__ void kv_pack_kernel(const __half* __restrict__ kt, const __half* __re
                                const int* __restrict__ seq_off, const int* __restrict__ seq_len, const int* __restrict__ plen,
                                const __half* const* __restrict__ kp, const __half* const* __restrict__ vp,
                                __half* const* __restrict__ k_out, __half* const* __restrict__ v_out) {
+  grid_dep_wait();
   const int b = blockIdx.z, kh = blockIdx.y;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   __half *dk = k_out[b], *dv = v_out[b];
@@ -275,6 +282,7 @@ __global__ void kv_gather_kernel(const __half* __restrict__ kt, const __half* __
                                  const int* __restrict__ seq_off, const int* __restrict__ seq_len, const int* __restrict__ plen,
                                  const __half* const* __restrict__ kp, const __half* const* __restrict__ vp,
                                  const int* __restrict__ gofs, int ktot, __half* __restrict__ gk, __half* __restrict__ gv) {
+  grid_dep_wait();
   const int b = blockIdx.z, kh = blockIdx.y;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int p = plen[b], n = p + seq_len[b];
@@ -299,6 +307,7 @@ __global__ void kv_gather_kernel(const __half* __restrict__ kt, const __half* __
 __global__ void gdn_gates_kernel(const __half* __restrict__ big, int stride, int aoff, int boff, const float* __restrict__ neg_a,
                                  const float* __restrict__ dtb, int l, int h, float* __restrict__ beta,
                                  float* __restrict__ gl) {
+  grid_dep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= l * h) return;
   const int t = i / h, hh = i % h;
@@ -366,6 +375,7 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(const float* __restr
 __global__ void __launch_bounds__(128) gnorm_kernel(const float* __restrict__ o, const __half* __restrict__ big, int stride,
                                                     int zoff, const float* __restrict__ w, int l, int h,
                                                     __half* __restrict__ out) {
+  grid_dep_wait();
   constexpr int DV = 128;
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= l * h) return;
@@ -397,6 +407,7 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const __half* __restrict__
                                                       const float* __restrict__ kw, const float2* __restrict__ rope, int l,
                                                       int p, int lt, int hq, int hk, int rd, const int* __restrict__ tpos,
                                                       __half* __restrict__ qo, __half* __restrict__ ko, __half* __restrict__ vo) {
+  grid_dep_wait();
   constexpr int HD = 256;
   __shared__ float red[8];
   __shared__ float nv[HD];
@@ -434,6 +445,7 @@ __global__ void __launch_bounds__(256) qk_prep_warp_kernel(const __half* __restr
                                                            int hk, int rd, const int* __restrict__ tpos,
                                                            __half* __restrict__ qo, __half* __restrict__ ko,
                                                            __half* __restrict__ vo) {
+  grid_dep_wait();
   constexpr int HD = 256;
   const int lane = threadIdx.x & 31;
   const long long rowid = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -493,12 +505,14 @@ __global__ void __launch_bounds__(256) qk_prep_warp_kernel(const __half* __restr
 }
 
 __global__ void trace_kernel(const float* __restrict__ x, const __half* __restrict__ y, int n, float* __restrict__ out) {
+  grid_dep_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     out[i] = y ? x[i] + __half2float(y[i]) : x[i];
 }
 
 // add_bias (src/kernels.rs:138-149): y = f16(y + c[j]).
 __global__ void add_bias_kernel(__half* __restrict__ y, const float* __restrict__ c, int n, int d) {
+  grid_dep_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     y[i] = __float2half_rn(__half2float(y[i]) + c[i % d]);
 }
@@ -511,50 +525,45 @@ static int blocks_for(int64_t n, int per) { return (int)std::min<int64_t>((n + p
 cudaError_t launch_embed_norm(const uint32_t* ids, int l, const uint8_t* eq, const __half* es, int bits, int d, int vocab,
                               const float* w, float* x, __half* h, int* err, cudaStream_t st) {
   if (d > 2048 || d % 32) return cudaErrorInvalidValue;
-  embed_norm_kernel<<<l, 256, 0, st>>>(ids, eq, es, bits, d, vocab, w, x, h, err);
-  return cudaGetLastError();
+  return launch_dependent(embed_norm_kernel, dim3(l), dim3(256), 0, st, ids, eq, es, bits, d, vocab, w, x, h, err);
 }
 
 cudaError_t launch_add_norm(float* x, const __half* y, const float* w, int l, int d, bool add, __half* h, cudaStream_t st) {
   if (d != 2048) return cudaErrorInvalidValue;
-  add_norm_kernel<<<l, 256, 0, st>>>(x, y, w, d, add ? 1 : 0, h);
-  return cudaGetLastError();
+  return launch_dependent(add_norm_kernel, dim3(l), dim3(256), 0, st, x, y, w, d, add ? 1 : 0, h);
 }
 
 cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int l, int d, float* out,
                               int* err, cudaStream_t st) {
   if (nrows <= 0) return cudaSuccess;
-  final_norm_kernel<<<nrows, 256, 0, st>>>(x, y, w, rows, l, d, out, err);
-  return cudaGetLastError();
+  return launch_dependent(final_norm_kernel, dim3(nrows), dim3(256), 0, st, x, y, w, rows, l, d, out, err);
 }
 
 cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, __half* qkvc,
                         const int* tstart, const __half* const* hseq, const int* tseq, cudaStream_t st) {
   if (C % 8 || stride % 8 || (hseq && (!tstart || !tseq))) return cudaErrorInvalidValue;
   dim3 grid((C / 4 + 127) / 128, (l + kConvT - 1) / kConvT);
-  conv_kernel<<<grid, 128, 0, st>>>(big, stride, reinterpret_cast<const float4*>(conv_w), hist, l, C, tstart, hseq, tseq, qkvc);
-  return cudaGetLastError();
+  return launch_dependent(conv_kernel, grid, dim3(128), 0, st, big, stride, reinterpret_cast<const float4*>(conv_w), hist, l, C,
+                          tstart, hseq, tseq, qkvc);
 }
 
 cudaError_t launch_hist_update(const __half* big, int stride, __half* hist, int l, int C, cudaStream_t st) {
-  hist_update_kernel<<<(C + 255) / 256, 256, 0, st>>>(big, stride, hist, l, C);
-  return cudaGetLastError();
+  return launch_dependent(hist_update_kernel, dim3((C + 255) / 256), dim3(256), 0, st, big, stride, hist, l, C);
 }
 
 cudaError_t launch_hist_pack(const __half* big, int stride, int C, const int* seq_off, const int* seq_len,
                              const __half* const* h_in, __half* const* h_out, int nseq, cudaStream_t st) {
   if (nseq <= 0 || nseq > 65535 || !h_out) return cudaErrorInvalidValue;
-  hist_pack_kernel<<<dim3((C + 255) / 256, nseq), 256, 0, st>>>(big, stride, C, seq_off, seq_len, h_in, h_out);
-  return cudaGetLastError();
+  return launch_dependent(hist_pack_kernel, dim3((C + 255) / 256, nseq), dim3(256), 0, st, big, stride, C, seq_off, seq_len, h_in,
+                          h_out);
 }
 
 cudaError_t launch_kv_gather(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
                              const int* plen, const __half* const* kp, const __half* const* vp, const int* gofs, int ktot,
                              __half* gk, __half* gv, int nseq, int max_rows, cudaStream_t st) {
   if (nseq <= 0 || nseq > 65535 || hk <= 0 || hk > 65535 || hd % 8 || max_rows <= 0 || max_rows > ktot) return cudaErrorInvalidValue;
-  kv_gather_kernel<<<dim3((max_rows + 7) / 8, hk, nseq), 256, 0, st>>>(kt, vt, T, hd, seq_off, seq_len, plen, kp, vp, gofs, ktot,
-                                                                       gk, gv);
-  return cudaGetLastError();
+  return launch_dependent(kv_gather_kernel, dim3((max_rows + 7) / 8, hk, nseq), dim3(256), 0, st, kt, vt, T, hd, seq_off, seq_len,
+                          plen, kp, vp, gofs, ktot, gk, gv);
 }
 
 cudaError_t launch_kv_pack(const __half* kt, const __half* vt, int T, int hk, int hd, const int* seq_off, const int* seq_len,
@@ -562,15 +571,14 @@ cudaError_t launch_kv_pack(const __half* kt, const __half* vt, int T, int hk, in
                            __half* const* v_out, int nseq, int max_rows, cudaStream_t st) {
   if (nseq <= 0 || nseq > 65535 || hk <= 0 || hk > 65535 || hd % 8 || max_rows <= 0 || !k_out || !v_out)
     return cudaErrorInvalidValue;
-  kv_pack_kernel<<<dim3((max_rows + 7) / 8, hk, nseq), 256, 0, st>>>(kt, vt, T, hd, seq_off, seq_len, plen, kp, vp, k_out,
-                                                                     v_out);
-  return cudaGetLastError();
+  return launch_dependent(kv_pack_kernel, dim3((max_rows + 7) / 8, hk, nseq), dim3(256), 0, st, kt, vt, T, hd, seq_off, seq_len,
+                          plen, kp, vp, k_out, v_out);
 }
 
 cudaError_t launch_gdn_gates(const __half* big, int stride, int aoff, int boff, const float* neg_a, const float* dt_bias,
                              int l, int h, float* beta, float* gl, cudaStream_t st) {
-  gdn_gates_kernel<<<blocks_for((int64_t)l * h, 256), 256, 0, st>>>(big, stride, aoff, boff, neg_a, dt_bias, l, h, beta, gl);
-  return cudaGetLastError();
+  return launch_dependent(gdn_gates_kernel, dim3(blocks_for((int64_t)l * h, 256)), dim3(256), 0, st, big, stride, aoff, boff, neg_a,
+                          dt_bias, l, h, beta, gl);
 }
 
 cudaError_t launch_gdn_recurrent(const float* q, const float* k, int qk_stride, const float* v, int v_stride,
@@ -582,8 +590,7 @@ cudaError_t launch_gdn_recurrent(const float* q, const float* k, int qk_stride, 
 
 cudaError_t launch_gnorm(const float* o, const __half* big, int stride, int zoff, const float* w, int l, int h, __half* out,
                          cudaStream_t st) {
-  gnorm_kernel<<<(l * h + 3) / 4, 128, 0, st>>>(o, big, stride, zoff, w, l, h, out);
-  return cudaGetLastError();
+  return launch_dependent(gnorm_kernel, dim3((l * h + 3) / 4), dim3(128), 0, st, o, big, stride, zoff, w, l, h, out);
 }
 
 cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const float* kw, const float* rope, int l, int p,
@@ -591,14 +598,12 @@ cudaError_t launch_qk_prep(const __half* big, int stride, const float* qw, const
   if (dm.hd != 256) return cudaErrorInvalidValue;
   if ((dm.rd / 2) % 8 == 0 && dm.rd <= 256 && stride % 8 == 0) {  // a warp per row
     const long long rows = (long long)l * (dm.hq + dm.hk);
-    qk_prep_warp_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(big, stride, qw, kw, reinterpret_cast<const float2*>(rope), l,
-                                                                     p, lt, dm.hq, dm.hk, dm.rd, tpos, q, kc, vc);
-    return cudaGetLastError();
+    return launch_dependent(qk_prep_warp_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, st, big, stride, qw, kw,
+                            reinterpret_cast<const float2*>(rope), l, p, lt, dm.hq, dm.hk, dm.rd, tpos, q, kc, vc);
   }
   dim3 grid(l, dm.hq + dm.hk);
-  qk_prep_kernel<<<grid, 256, 0, st>>>(big, stride, qw, kw, reinterpret_cast<const float2*>(rope), l, p, lt, dm.hq, dm.hk,
-                                       dm.rd, tpos, q, kc, vc);
-  return cudaGetLastError();
+  return launch_dependent(qk_prep_kernel, grid, dim3(256), 0, st, big, stride, qw, kw, reinterpret_cast<const float2*>(rope), l, p,
+                          lt, dm.hq, dm.hk, dm.rd, tpos, q, kc, vc);
 }
 
 // A self-test of the kernels' failure path, which no input can reach: warp 0 waits on an mbarrier
@@ -642,13 +647,11 @@ cudaError_t preload_kernels() {
 }
 
 cudaError_t launch_trace(const float* x, const __half* y, int n, float* out, cudaStream_t st) {
-  trace_kernel<<<blocks_for(n, 256), 256, 0, st>>>(x, y, n, out);
-  return cudaGetLastError();
+  return launch_dependent(trace_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, st, x, y, n, out);
 }
 
 cudaError_t launch_add_bias(__half* y, const float* bias, int l, int d, cudaStream_t st) {
-  add_bias_kernel<<<blocks_for((int64_t)l * d, 256), 256, 0, st>>>(y, bias, l * d, d);
-  return cudaGetLastError();
+  return launch_dependent(add_bias_kernel, dim3(blocks_for((int64_t)l * d, 256)), dim3(256), 0, st, y, bias, l * d, d);
 }
 
 }  // namespace sd
