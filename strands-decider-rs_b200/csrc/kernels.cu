@@ -171,6 +171,9 @@ __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ bi
     const int t = t0 - 3 + r;
     raw[r] = (t >= 0 && t < l) ? *reinterpret_cast<const uint2*>(big + (size_t)t * stride + c4) : make_uint2(0, 0);
   }
+  int tst[kConvT];  // each token's sequence start, loaded with the rows (not one dependent load per token)
+#pragma unroll
+  for (int i = 0; i < kConvT; i++) tst[i] = tstart && t0 + i < l ? tstart[t0 + i] : 0;
   float w[4][4];
 #pragma unroll
   for (int c = 0; c < 4; c++) {
@@ -181,7 +184,7 @@ __global__ void __launch_bounds__(128) conv_kernel(const __half* __restrict__ bi
   for (int i = 0; i < kConvT; i++) {
     const int t = t0 + i;
     if (t >= l) break;
-    const int st = tstart ? tstart[t] : 0;
+    const int st = tst[i];
     float x[4][4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
