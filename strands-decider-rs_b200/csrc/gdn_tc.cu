@@ -12,9 +12,9 @@
 //
 // One CTA walks one (sequence, head) over all 128 value columns. The state S is the f32 accumulator
 // of its own update in tensor memory. The chunk's products are tcgen05 MMAs of M = 128 that stack two
-// 64-row operands: [K^; Q^] K^T gives A and P at once, [Gamma Q^; -W] S gives Gamma Q^ S and -W S
+// 64-row operands: [K; Q] K^T gives A and P at once, [Gamma Q^; -W] S gives Gamma Q^ S and -W S
 // (accumulated onto [0; U], so that the second half is delta), and [P; *] delta adds P delta to the
-// first half. The state-independent work of chunk c + 1 (normalisation, A and P, the triangular
+// first half. The state-independent work of chunk c + 1 (row norms, A and P, the triangular
 // inverse, T1 and T2) runs beside the state chain of chunk c:
 //   warps 0-3   the chain: O rows to global memory, S out of tensor memory (its f16 copy, the operand
 //               of the next chunk, and Gamma_C S back), -W out of tensor memory, delta (f16, and
@@ -67,7 +67,7 @@ enum {
   B_KQ_FULL = 0,     // [2] the chunk's k and q rows landed (TMA bytes)
   B_V_FULL = 2,      // [2] the chunk's v rows landed
   B_U_DONE = 4,      // [2] U = [0; T2] V completed (T1 and T2 free; W read out before it)
-  B_DAP_FULL = 6,    // [2] [K^; Q^] K^T in tensor memory
+  B_DAP_FULL = 6,    // [2] [K; Q] K^T in tensor memory
   B_W_FULL = 8,      // [2] W in tensor memory
   B_WQ_READY = 10,   // [2] Gamma Q^, P, T1 and T2 written (shared memory) and W issued
   B_G_READY = 12,    // [2] the chunk's G written
