@@ -274,14 +274,16 @@ int32_t sd_gdn_noalloc_max_tokens(int32_t h);
  * layout, made from the reference layout on the device: q_dev [n][k/32][16 bytes], s_dev [n][k/32] f16.
  * `interleave` stores rows (j, n/2 + j) next to each other (gate_up for the fused SwiGLU). */
 int sd_qweight_create(const void* q_dev, const void* s_dev, int32_t n, int32_t k, int32_t interleave, sd_qweight** out);
-/* sd_qweight_create for the reference's other symmetric formats (`src/kernels.rs:545-586`, served there by
+/* sd_qweight_create for the reference's other formats (`src/kernels.rs:545-586`, served there by
  * `matmul_gemv`): bits 2, 3 or 4 (q_dev [n][k/32][4 * bits bytes]: int4 as 4 words of 8 nibbles, int2 as 2
  * words of 16 two-bit fields, int3 as those 2 words plus a word of high bits), one f16 scale per `group`
- * weights (a multiple of 32) indexed by the global block (row * k/32 + block) / (group / 32). The weight is
- * repacked into the int4 tile layout with the same values ((q - 2^(bits-1)) * scale); asymmetric weights
- * are not supported. */
-int sd_qweight_create_format(const void* q_dev, const void* s_dev, int32_t n, int32_t k, int32_t bits, int32_t group,
-                             int32_t interleave, sd_qweight** out);
+ * weights (a multiple of 32) indexed by the global block (row * k/32 + block) / (group / 32). b_dev null:
+ * symmetric, value (q - 2^(bits-1)) * scale; else one f16 bias per group, indexed as the scales:
+ * asymmetric, value q * scale + bias. The weight is repacked into the int4 tile layout with the same
+ * values (the dequantized weight is rounded to f16 as the tiled path rounds it; the reference's
+ * `matmul_gemv` keeps it f32). */
+int sd_qweight_create_format(const void* q_dev, const void* s_dev, const void* b_dev, int32_t n, int32_t k, int32_t bits,
+                             int32_t group, int32_t interleave, sd_qweight** out);
 void sd_qweight_free(sd_qweight* w);
 
 /* `matmul_gemv`/`matmul_tiled`/`matmul_coop` (`src/kernels.rs:590-804`): y_dev[m][ldy] =

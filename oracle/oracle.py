@@ -95,13 +95,14 @@ def decode_scales(src: bytes, n: int, g: int) -> np.ndarray:
 
 
 def matmul(a: np.ndarray, q: np.ndarray, s: np.ndarray, n: int, k: int, bits: int = 4, group: int = 32,
-           variant: int = 0) -> np.ndarray:
+           variant: int = 0, b: np.ndarray | None = None) -> np.ndarray:
     """Y = A W^T with the reference's dispatch for a.shape[0] rows (variant 0), or forced GEMV (1) /
-    tiled (2). a: f16 [m, k]."""
+    tiled (2). a: f16 [m, k]; b: the per-group f16 biases of an asymmetric weight."""
     a = np.ascontiguousarray(a, np.float16)
     q = np.ascontiguousarray(q)
     s = np.ascontiguousarray(s, np.float16)
-    w = OrMat(_p(q), _p(s), None, n, k, bits, group, 0)
+    bb = None if b is None else np.ascontiguousarray(b, np.float16)
+    w = OrMat(_p(q), _p(s), _p(bb) if bb is not None else None, n, k, bits, group, int(bb is not None))
     y = np.empty((a.shape[0], n), np.float16)
     lib().or_matmul(_p(a), a.shape[0], C.byref(w), _p(y), variant)
     return y

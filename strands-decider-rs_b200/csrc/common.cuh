@@ -308,6 +308,15 @@ SD_DEV __half2 dq_pair(uint32_t w, int i, __half2 scale2) {
   return __hmul2(v, scale2);
 }
 
+// The asymmetric format's pair: fma(q, scale, bias) in f16, one rounding, as the reference's
+// `fma(vec4<f16>(q), sc, bi)` (src/kernels.rs:572); (q + 1024) - 1024 = q exactly.
+SD_DEV __half2 dq_pair_affine(uint32_t w, int i, __half2 scale2, __half2 bias2) {
+  uint32_t t = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
+  __half2 v = *reinterpret_cast<__half2*>(&t);
+  v = __hsub2(v, __half2half2(__ushort_as_half((unsigned short)0x6400)));  // 1024.0
+  return __hfma2(v, scale2, bias2);
+}
+
 SD_DEV uint32_t h2_as_u32(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
 
 SD_DEV float warp_sum(float v) {

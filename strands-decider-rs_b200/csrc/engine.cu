@@ -445,15 +445,20 @@ int load_engine(sd_engine* e, const std::string& dir) {
     const int group = (int)(t->get("group") ? t->at("group").integer() : 32);
     const bool asym = t->get("asym") ? t->at("asym").boolean() : false;
     const int n = (int)t->at("N").integer(), k = (int)t->at("K").integer();
-    if (bits < 2 || bits > 4 || group < 32 || group % 32 || asym || k % 64 || (interleave && n % 2)) {
+    if (bits < 2 || bits > 4 || group < 32 || group % 32 || k % 64 || (interleave && n % 2)) {
       if (rc == SD_OK)
         rc = e->fail(SD_ERR_FORMAT,
-                     "%s: matmul weights must be symmetric int2, int3 or int4 with groups of a multiple of 32 and K a "
-                     "multiple of 64 (asymmetric weights are not supported)",
+                     "%s: matmul weights must be int2, int3 or int4 with groups of a multiple of 32 and K a multiple of 64",
                      name.c_str());
       return;
     }
-    cudaError_t ce = sd::repack_weight(q, reinterpret_cast<const __half*>(s), n, k, interleave, w, e->stream, bits, group);
+    const uint8_t* b = asym ? tensor_ptr(name + ".b", nullptr) : nullptr;  // the per-group f16 biases
+    if (asym && !b) {
+      if (missing.empty()) missing = name + ".b";
+      return;
+    }
+    cudaError_t ce = sd::repack_weight(q, reinterpret_cast<const __half*>(s), n, k, interleave, w, e->stream, bits, group,
+                                       reinterpret_cast<const __half*>(b));
     if (ce != cudaSuccess && rc == SD_OK) rc = e->fail(SD_ERR_CUDA, "%s: %s", name.c_str(), cudaGetErrorString(ce));
   };
   for (int i = 0; i < e->n_layers; i++) {
@@ -1992,10 +1997,10 @@ int sd_gdn(const void* q, const void* k, int32_t qk_stride, const void* v, int32
 size_t sd_gdn_scratch_bytes(int32_t l, int32_t h) { return l > 0 && h > 0 ? sd::gdn_two_phase_scratch(l, h) : 0; }
 
 int sd_qweight_create(const void* q, const void* s, int32_t n, int32_t k, int32_t interleave, sd_qweight** out) {
-  return sd_qweight_create_format(q, s, n, k, 4, 32, interleave, out);
+  return sd_qweight_create_format(q, s, nullptr, n, k, 4, 32, interleave, out);
 }
 
-int sd_qweight_create_format(const void* q, const void* s, int32_t n, int32_t k, int32_t bits, int32_t group,
+int sd_qweight_create_format(const void* q, const void* s, const void* b, int32_t n, int32_t k, int32_t bits, int32_t group,
                              int32_t interleave, sd_qweight** out) {
   if (!q || !s || !out || n <= 0 || k <= 0 || k % 64 || (interleave && n % 2) || bits < 2 || bits > 4 || group < 32 ||
       group % 32) {
@@ -2004,7 +2009,8 @@ int sd_qweight_create_format(const void* q, const void* s, int32_t n, int32_t k,
   }
   auto w = std::make_unique<sd_qweight>();
   cudaGetDevice(&w->device);
-  cudaError_t ce = sd::repack_weight((const uint8_t*)q, (const __half*)s, n, k, interleave != 0, &w->w, nullptr, bits, group);
+  cudaError_t ce = sd::repack_weight((const uint8_t*)q, (const __half*)s, n, k, interleave != 0, &w->w, nullptr, bits, group,
+                                     (const __half*)b);
   if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
   if (ce != cudaSuccess) return op_result(ce, "sd_qweight_create");
   *out = w.release();

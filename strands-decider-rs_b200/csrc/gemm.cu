@@ -38,7 +38,9 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kTileCodes = kBM * kBK / 2;          // 4096 bytes of int4 codes
 constexpr int kTileScales = kBM * (kBK / 32) * 2;  // 512 bytes of f16 scales
-constexpr int kTileBytes = kTileCodes + kTileScales;
+constexpr int kTileBytes = kTileCodes + kTileScales;  // a symmetric weight's k-tile
+constexpr int kTileBias = kBM * (kBK / 32) * 2;        // f16 biases of an asymmetric weight's k-tile
+constexpr int kTileBytesMax = kTileBytes + kTileBias;
 constexpr int kHalfCodes = kTileCodes / 2;  // codes of k-group 0 of every row, then of k-group 1
 constexpr int kACols = kBK / 2;             // TMEM columns of one dequantized k-tile (f16 pairs)
 
@@ -53,7 +55,7 @@ struct GemmCfg {
   static constexpr int S = WIDE ? 2 : (BN >= 64 ? 4 : 6);
   static constexpr int NG = WIDE ? 2 : 4;
   static constexpr int SR = WIDE ? 8 : (BN >= 192 ? 16 : (BN >= 128 ? 8 : 12));
-  static constexpr int kRawSlot = KS * kTileBytes;
+  static constexpr int kRawSlot = KS * kTileBytesMax;
   static constexpr int kWarps = 2 + 4 * NG + 4 + 1;
   static constexpr int kThreads = 32 * kWarps;
   static constexpr int kWarpAct = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 2 + 4 * NG, kWarpRaw = kWarpEpi0 + 4;
@@ -125,8 +127,8 @@ struct TileGrid {
 // tile possibly fewer) and k-tiles, so stage and k-tile counters agree between roles.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
-    gemm_q4_tc(const __grid_constant__ CUtensorMap act_map, const uint8_t* __restrict__ wt, int M, int N, TileGrid tg,
-               __half* __restrict__ y, int ldy, float* __restrict__ ws, int* err) {
+    gemm_q4_tc(const __grid_constant__ CUtensorMap act_map, const uint8_t* __restrict__ wt, int M, int N, int tile_bytes,
+               TileGrid tg, __half* __restrict__ y, int ldy, float* __restrict__ ws, int* err) {
   using Cfg = CfgOf<BN, EPI>;
   constexpr int KS = Cfg::KS, S = Cfg::S, SR = Cfg::SR, NG = Cfg::NG;
   extern __shared__ uint8_t smem_raw[];
@@ -181,15 +183,15 @@ __global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
       for (int t = blockIdx.x; t < ntile_total && ok; t += gridDim.x) {
         int nt, mt, sp, kt0, nk;
         tg.decode(t, nt, mt, sp, kt0, nk);
-        const uint8_t* wtile = wt + (size_t)nt * KT * kTileBytes;
+        const uint8_t* wtile = wt + (size_t)nt * KT * tile_bytes;
         for (int i = 0; i < nk; i += KS, si++) {
           const int rs = si % SR, kc = min(KS, nk - i);
           if (si >= SR && !mbar_wait(&raw_empty[rs], ((si / SR) & 1) ^ 1, abort, err, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)(kc * kTileBytes));
-          bulk_load(sraw + rs * Cfg::kRawSlot, wtile + (size_t)(kt0 + i) * kTileBytes, kc * kTileBytes, &raw_full[rs]);
+          mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)(kc * tile_bytes));
+          bulk_load(sraw + rs * Cfg::kRawSlot, wtile + (size_t)(kt0 + i) * tile_bytes, kc * tile_bytes, &raw_full[rs]);
         }
       }
       for (int j = max(0, si - SR); j < si; j++) mbar_drain(&raw_full[j % SR], (j / SR) & 1);
@@ -275,17 +277,28 @@ __global__ void __launch_bounds__(CfgOf<BN, EPI>::kThreads, 1)
           break;
         }
         for (int j = 0; j < kc; j++) {
-          const uint8_t* raw = sraw + rs * Cfg::kRawSlot + j * kTileBytes;
+          const uint8_t* raw = sraw + rs * Cfg::kRawSlot + j * tile_bytes;
           const uint4 c0 = *reinterpret_cast<const uint4*>(raw + r * 16);
           const uint4 c1 = *reinterpret_cast<const uint4*>(raw + kHalfCodes + r * 16);
           const __half2 sc = *reinterpret_cast<const __half2*>(raw + kTileCodes + r * 4);
           const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
           uint32_t v[32];  // column c: elements (2c, 2c + 1) of this row's 64
+          if (tile_bytes == kTileBytes) {
 #pragma unroll
-          for (int ch = 0; ch < 8; ch++) {
-            const __half2 sc2 = ch < 4 ? __low2half2(sc) : __high2half2(sc);
+            for (int ch = 0; ch < 8; ch++) {
+              const __half2 sc2 = ch < 4 ? __low2half2(sc) : __high2half2(sc);
 #pragma unroll
-            for (int e = 0; e < 4; e++) v[ch * 4 + e] = h2_as_u32(dq_pair(w[ch], e, sc2));
+              for (int e = 0; e < 4; e++) v[ch * 4 + e] = h2_as_u32(dq_pair(w[ch], e, sc2));
+            }
+          } else {  // asymmetric: q * scale + bias
+            const __half2 bi = *reinterpret_cast<const __half2*>(raw + kTileBytes + r * 4);
+#pragma unroll
+            for (int ch = 0; ch < 8; ch++) {
+              const __half2 sc2 = ch < 4 ? __low2half2(sc) : __high2half2(sc);
+              const __half2 bi2 = ch < 4 ? __low2half2(bi) : __high2half2(bi);
+#pragma unroll
+              for (int e = 0; e < 4; e++) v[ch * 4 + e] = h2_as_u32(dq_pair_affine(w[ch], e, sc2, bi2));
+            }
           }
           if (j == kc - 1) {
             // the stage's codes are in registers (the results depend on them): refill the raw slot
@@ -505,22 +518,25 @@ SD_DEV uint32_t code_at(const uint8_t* blk, int bits, int e) {
   if (bits == 3) c |= ((w[2] >> e) & 1u) << 2;
   return c;
 }
-__global__ void repack_q4(const uint8_t* __restrict__ q, const __half* __restrict__ s, int n, int k, int npad, int interleave,
-                          int bits, int group, uint8_t* __restrict__ out) {
+__global__ void repack_q4(const uint8_t* __restrict__ q, const __half* __restrict__ s, const __half* __restrict__ b, int n, int k,
+                          int npad, int interleave, int bits, int group, uint8_t* __restrict__ out) {
   const int KT = k / kBK, nb = k / 32, bb = 4 * bits, gpb = group / 32;
-  const uint32_t shift = 8u - (1u << (bits - 1));
+  const int tb = b ? kTileBytesMax : kTileBytes;
+  const uint32_t shift = b ? 0u : 8u - (1u << (bits - 1));  // asymmetric codes stay as they are
   const int64_t total = (int64_t)npad * KT;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
     const int row = (int)(idx / KT), kt = (int)(idx % KT);
     int src = row;
     if (interleave) src = (row & 1) ? (n / 2 + (row >> 1)) : (row >> 1);
-    uint8_t* tile = out + ((size_t)(row / kBM) * KT + kt) * kTileBytes;
+    uint8_t* tile = out + ((size_t)(row / kBM) * KT + kt) * tb;
     uint32_t* dst0 = reinterpret_cast<uint32_t*>(tile + (row % kBM) * 16);               // k-group 0
     uint32_t* dst1 = reinterpret_cast<uint32_t*>(tile + kHalfCodes + (row % kBM) * 16);  // k-group 1
     __half* dsc = reinterpret_cast<__half*>(tile + kTileCodes) + (row % kBM) * 2;
+    __half* dbi = reinterpret_cast<__half*>(tile + kTileBytes) + (row % kBM) * 2;  // asymmetric only
     if (row >= n) {
       for (int i = 0; i < 4; i++) dst0[i] = dst1[i] = 0;
       dsc[0] = dsc[1] = __float2half(0.0f);
+      if (b) dbi[0] = dbi[1] = __float2half(0.0f);
       continue;
     }
     for (int hb = 0; hb < 2; hb++) {  // the two 32-blocks of this k-tile
@@ -536,6 +552,7 @@ __global__ void repack_q4(const uint8_t* __restrict__ q, const __half* __restric
         (hb ? dst1 : dst0)[i] = o;
       }
       dsc[hb] = s[blk / gpb];
+      if (b) dbi[hb] = b[blk / gpb];
     }
   }
 }
@@ -633,7 +650,7 @@ static cudaError_t launch_bn(const CUtensorMap& map, const QWeight& w, int M, co
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, map, (const uint8_t*)w.tiles, M, w.n, tg, y, ldy, ws, err);
+  return cudaLaunchKernelEx(&cfg, kern, map, (const uint8_t*)w.tiles, M, w.n, w.tile_bytes, tg, y, ldy, ws, err);
 }
 
 template <int EPI>
@@ -758,19 +775,21 @@ cudaError_t preload_gemm() {
 }
 
 cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool interleave, QWeight* out, cudaStream_t st,
-                          int bits, int group) {
+                          int bits, int group, const __half* b) {
   if ((bits != 2 && bits != 3 && bits != 4) || group < 32 || group % 32) return cudaErrorInvalidValue;
   out->n = n;
   out->k = k;
   out->npad = (n + kBM - 1) / kBM * kBM;
   out->interleaved = interleave;
-  const size_t bytes = (size_t)(out->npad / kBM) * (k / kBK) * kTileBytes;
+  out->asym = b != nullptr;
+  out->tile_bytes = b ? kTileBytesMax : kTileBytes;
+  const size_t bytes = (size_t)(out->npad / kBM) * (k / kBK) * out->tile_bytes;
   cudaError_t e = cudaMalloc(&out->tiles, bytes);
   if (e != cudaSuccess) return e;
   out->bytes = bytes;
   const int64_t total = (int64_t)out->npad * (k / kBK);
-  repack_q4<<<(int)std::min<int64_t>((total + 255) / 256, 8192), 256, 0, st>>>(q, s, n, k, out->npad, interleave ? 1 : 0, bits, group,
-                                                                               out->tiles);
+  repack_q4<<<(int)std::min<int64_t>((total + 255) / 256, 8192), 256, 0, st>>>(q, s, b, n, k, out->npad, interleave ? 1 : 0, bits,
+                                                                               group, out->tiles);
   return cudaGetLastError();
 }
 

@@ -30,12 +30,15 @@ struct QWeight {
   size_t bytes = 0;
   int n = 0, k = 0, npad = 0;
   bool interleaved = false;
+  bool asym = false;     // tiles carry an f16 bias per 32-block: value = q * scale + bias
+  int tile_bytes = 0;    // bytes of one 128-row k-tile (codes, scales, and biases when asym)
 };
 
-// q, s in the reference's layout: `bits` (2, 3 or 4) bit symmetric codes, one f16 scale per `group`
-// weights (a multiple of 32); every format becomes the int4 tile layout, values unchanged.
+// q, s (and b) in the reference's layout: `bits` (2, 3 or 4) bit codes, one f16 scale (and with b,
+// asymmetric weights: one f16 bias) per `group` weights (a multiple of 32); every format becomes the
+// int4 tile layout, values unchanged.
 cudaError_t repack_weight(const uint8_t* q, const __half* s, int n, int k, bool interleave, QWeight* out, cudaStream_t st,
-                          int bits = 4, int group = 32);
+                          int bits = 4, int group = 32, const __half* b = nullptr);
 void gemm_plan(const QWeight& w, int M, int num_sms, int* bn, int* splits, int* kps);
 // y[M][ldy] = act[M][K] W^T, or SwiGLU of interleaved gate/up rows into y[M][N/2] when silu; ws is
 // the f32 split-K workspace (M * N floats; smaller disables split-K); *nlaunch gets the kernel count.

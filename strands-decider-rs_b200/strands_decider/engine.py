@@ -86,7 +86,7 @@ def lib() -> C.CDLL:
         L.sd_qweight_create.argtypes = [vp, vp, i32, i32, i32, C.POINTER(vp)]
         L.sd_engine_selftest_wait.argtypes = [vp, i32]
         L.sd_op_status.argtypes = [vp]
-        L.sd_qweight_create_format.argtypes = [vp, vp, i32, i32, i32, i32, i32, C.POINTER(vp)]
+        L.sd_qweight_create_format.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, C.POINTER(vp)]
         L.sd_qweight_free.argtypes = [vp]
         L.sd_matmul.argtypes = [vp, vp, i32, vp, i32, i32, vp, C.c_size_t, vp]
         L.sd_decider_load.argtypes = [cp, C.c_int, C.POINTER(vp)]
@@ -434,11 +434,13 @@ def gdn_noalloc_max_tokens(h: int) -> int:
 
 
 class QWeight:
-    def __init__(self, q_dev: int, s_dev: int, n: int, k: int, interleave: bool = False, bits: int = 4, group: int = 32):
-        """A weight in the reference's block-quantized layout (symmetric int2/int3/int4, one f16 scale per
-        `group` weights), repacked for the GEMM (`sd_qweight_create_format`)."""
+    def __init__(self, q_dev: int, s_dev: int, n: int, k: int, interleave: bool = False, bits: int = 4, group: int = 32,
+                 b_dev: int | None = None):
+        """A weight in the reference's block-quantized layout (int2/int3/int4, one f16 scale per `group`
+        weights, and with ``b_dev`` one f16 bias per group: asymmetric), repacked for the GEMM
+        (`sd_qweight_create_format`)."""
         h = C.c_void_p()
-        _check(lib().sd_qweight_create_format(q_dev, s_dev, n, k, bits, group, int(interleave), C.byref(h)),
+        _check(lib().sd_qweight_create_format(q_dev, s_dev, b_dev, n, k, bits, group, int(interleave), C.byref(h)),
                "sd_qweight_create")
         self._h = h.value
         self.n, self.k = n, k

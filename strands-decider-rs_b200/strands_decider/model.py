@@ -237,6 +237,14 @@ def _quant_tensor(rng, n: int, k: int, bits: int, std: float, group: int = 32):
     return pack_codes(q, bits), scales
 
 
+def _asym_bias(rng, scales: np.ndarray, bits: int) -> np.ndarray:
+    """f16 biases for asymmetric codes: -2^(bits-1) scale (the symmetric centre) plus a per-group shift
+    of up to half a scale."""
+    s = scales.astype(np.float32)
+    shift = rng.uniform(-0.5, 0.5, size=s.shape).astype(np.float32)
+    return (-(float(1 << (bits - 1))) * s + shift * s).astype(np.float16)
+
+
 class _ShardWriter:
     def __init__(self, path: str):
         self.f = open(path, "wb")
@@ -255,10 +263,12 @@ class _ShardWriter:
         self.tensors[name] = t
         self.off += len(raw)
 
-    def add_matmul(self, rng, name: str, n: int, k: int, std: float, bits: int = 4, group: int = 32):
+    def add_matmul(self, rng, name: str, n: int, k: int, std: float, bits: int = 4, group: int = 32, asym: bool = False):
         packed, scales = _quant_tensor(rng, n, k, bits, std, group=group)
-        self.add(f"{name}.q", packed, N=n, K=k, bits=bits, group=group, asym=False)
-        self.add(f"{name}.s", scales, N=n, K=k, bits=bits, group=group, asym=False)
+        self.add(f"{name}.q", packed, N=n, K=k, bits=bits, group=group, asym=asym)
+        self.add(f"{name}.s", scales, N=n, K=k, bits=bits, group=group, asym=asym)
+        if asym:  # value q * scale + bias: the symmetric values, each group shifted by up to half a scale
+            self.add(f"{name}.b", _asym_bias(rng, scales, bits), N=n, K=k, bits=bits, group=group, asym=True)
 
     def close(self) -> int:
         self.f.close()
@@ -290,13 +300,13 @@ def write_synthetic(path: str, seed: int = 0, n_layers: int = PROD_LAYERS, vocab
         return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
 
     sw = _ShardWriter(os.path.join(path, "weights.0.bin"))
-    if matmul_formats:  # (bits, group) of the layer matmuls, in turn (the reference's other formats)
+    if matmul_formats:  # (bits, group[, asym]) of the layer matmuls, in turn (the reference's other formats)
         fmts = iter(matmul_formats * 1000)
         plain_add = sw.add_matmul
 
         def add_fmt(rng_, name, n, k, std):
-            bits, group = next(fmts)
-            plain_add(rng_, name, n, k, std, bits=bits, group=group)
+            f = next(fmts)  # (bits, group) or (bits, group, asym)
+            plain_add(rng_, name, n, k, std, bits=f[0], group=f[1], asym=bool(f[2]) if len(f) > 2 else False)
         sw.add_matmul = add_fmt
     for li, kind in enumerate(types):
         pre = f"layers.{li}."

@@ -44,21 +44,24 @@ def test_matmul_matches_oracle(torch, m, n, k):
         assert err.max() <= 2e-3 + 2e-3 * np.abs(want).max(), (ws_bytes, err.max())
 
 
-@pytest.mark.parametrize("bits,group", [(3, 32), (2, 32), (4, 64), (3, 128), (2, 256)])
+@pytest.mark.parametrize("bits,group,asym", [(3, 32, False), (2, 32, False), (4, 64, False), (3, 128, False), (2, 256, False),
+                                             (4, 32, True), (3, 64, True), (2, 128, True)])
 @pytest.mark.parametrize("m", [5, 300])
-def test_matmul_other_formats_match_oracle(torch, bits, group, m):
-    """The reference's other symmetric weight formats (int3 and int2 codes, groups of 64-256 weights per
-    scale), which it serves through its GEMV with f32 dequantization (`src/engine.rs:432-441`,
-    `src/kernels.rs:545-635`): repacked into the int4 tile layout with the same values, against the
-    oracle's GEMV, at a GEMV-sized and a tile-sized m."""
+def test_matmul_other_formats_match_oracle(torch, bits, group, asym, m):
+    """The reference's other weight formats (int3 and int2 codes, groups of 64-256 weights per scale,
+    asymmetric weights q * scale + bias with an f16 bias per group), which it serves through its GEMV
+    with f32 dequantization (`src/engine.rs:432-441`, `src/kernels.rs:545-635`): repacked into the int4
+    tile layout with the same values, against the oracle's GEMV, at a GEMV-sized and a tile-sized m."""
     from strands_decider.engine import QWeight
     n, k = 1152, 2048
-    rng = np.random.default_rng(bits * 1000 + group + m)
+    rng = np.random.default_rng(bits * 1000 + group + m + 7 * asym)
     packed, scales = M._quant_tensor(rng, n, k, bits, 1.0 / np.sqrt(k), group=group)
+    bias = M._asym_bias(rng, scales, bits) if asym else None
     a = rng.standard_normal((m, k)).astype(np.float16)
-    want = oracle.matmul(a, packed, scales, n, k, bits, group=group, variant=1).astype(np.float32)
+    want = oracle.matmul(a, packed, scales, n, k, bits, group=group, variant=1, b=bias).astype(np.float32)
     q_d, s_d, a_d = dev(torch, packed), dev(torch, scales.view(np.uint16)), dev(torch, a.view(np.uint16))
-    w = QWeight(q_d.data_ptr(), s_d.data_ptr(), n, k, bits=bits, group=group)
+    b_d = dev(torch, bias.view(np.uint16)) if asym else None
+    w = QWeight(q_d.data_ptr(), s_d.data_ptr(), n, k, bits=bits, group=group, b_dev=b_d.data_ptr() if asym else None)
     y = torch.zeros((m, n), dtype=torch.float16, device="cuda")
     w.matmul(a_d.data_ptr(), m, y.data_ptr(), n)
     torch.cuda.synchronize()
