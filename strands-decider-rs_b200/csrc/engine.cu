@@ -311,9 +311,15 @@ int load_engine(sd_engine* e, const std::string& dir) {
     e->rope_theta = c.at("rope_theta").number();
     if (const auto* u = c.get("unrotate"); u && u->kind == sd::json::Value::Array)
       for (auto& x : u->arr) e->unrotate.push_back(x.number());
-    if (d.d != 2048 || d.hd != 256 || d.dk != 128 || d.dv != 128 || d.hq % d.hk || d.rd > d.hd || d.rd % 2 ||
-        d.inter % 128)
-      return e->fail(SD_ERR_FORMAT, "unsupported dims (the kernels are built for D=2048, HD=256, DK=DV=128)");
+    // The GEMM's K tile (64) and the row-wise norms (one CTA per row, up to 8192 in registers) bound
+    // the hidden size; the attention and scan tiles fix the head sizes.
+    if (d.d <= 0 || d.d % 64 || d.d > 8192 || d.hd != 256 || d.dk != 128 || d.dv != 128 || d.hq <= 0 || d.hk <= 0 ||
+        d.h <= 0 || d.hq % d.hk || d.rd > d.hd || d.rd % 2 || d.inter <= 0 || d.inter % 128)
+      return e->fail(SD_ERR_FORMAT,
+                     "unsupported dims (hidden size a multiple of 64 up to 8192, intermediate a multiple of 128, "
+                     "HD=256, DK=DV=128)");
+    if (!e->unrotate.empty() && ((int)e->unrotate.size() != d.d || (d.d & (d.d - 1))))
+      return e->fail(SD_ERR_FORMAT, "unrotate needs %d factors and a power-of-two hidden size", d.d);
     const auto& types = c.at("layer_types").arr;
     e->n_layers = (int)types.size();
     e->layers.resize(e->n_layers);

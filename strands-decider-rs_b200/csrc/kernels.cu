@@ -31,8 +31,13 @@ __device__ __forceinline__ uint32_t code_of(const uint8_t* row, int bits, int bl
   return lo;
 }
 
+// Hidden sizes the row-wise norm kernels take: a multiple of 64 up to kMaxD (one CTA of 256 threads
+// per row, each thread holding NP x 8 elements in registers; NP = ceil(d / 2048)).
+constexpr int kMaxD = 8192;
+
 // embed (src/kernels.rs:63-89) fused with layer 0's input RMSNorm (add_norm without the residual
 // add, src/kernels.rs:93-120): x[t] = dequant(table[ids[t]]) in f32, h[t] = f16(x * inv * w).
+template <int NP>
 __global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t* __restrict__ ids, const uint8_t* __restrict__ eq,
                                                          const __half* __restrict__ es, int bits, int d, int vocab,
                                                          const float* __restrict__ w, float* __restrict__ x,
@@ -48,10 +53,10 @@ __global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t* __restr
   const int nb = d / 32;
   const uint8_t* row = eq + (size_t)id * nb * 4 * bits;
   const float half = (float)(1 << (bits - 1));
-  float v[8];
+  float v[8 * NP];
   float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
+  for (int i = 0; i < 8 * NP; i++) {
     const int c = threadIdx.x + 256 * i;
     float val = 0.0f;
     if (c < d) {
@@ -64,14 +69,16 @@ __global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t* __restr
   }
   const float inv = rsqrtf(block_sum256(ss, red) / (float)d + 1e-6f);
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
+  for (int i = 0; i < 8 * NP; i++) {
     const int c = threadIdx.x + 256 * i;
     if (c < d) h[(size_t)t * d + c] = __float2half_rn(v[i] * inv * w[c]);
   }
 }
 
 // add_norm (src/kernels.rs:93-120): x += y (when add), h = f16(x * rsqrt(mean(x^2) + 1e-6) * w).
-// Thread i owns elements 8i..8i+7 (d = 2048).
+// In pass p thread i owns elements 2048p + 8i .. +7 (16- and 32-byte accesses); a pass past d
+// holds zeros.
+template <int NP>
 __global__ void __launch_bounds__(256) add_norm_kernel(float* __restrict__ x, const __half* __restrict__ y,
                                                        const float* __restrict__ w, int d, int add,
                                                        __half* __restrict__ h) {
@@ -79,38 +86,52 @@ __global__ void __launch_bounds__(256) add_norm_kernel(float* __restrict__ x, co
   __shared__ float red[8];
   const int t = blockIdx.x;
   float* xr = x + (size_t)t * d;
-  const int c0 = threadIdx.x * 8;
-  float v[8];
-  float4 a = *reinterpret_cast<const float4*>(xr + c0), b = *reinterpret_cast<const float4*>(xr + c0 + 4);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  if (add) {
-    uint4 yy = *reinterpret_cast<const uint4*>(y + (size_t)t * d + c0);
-    const __half2* y2 = reinterpret_cast<const __half2*>(&yy);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      float2 f = __half22float2(y2[i]);
-      v[2 * i] += f.x;
-      v[2 * i + 1] += f.y;
-    }
-    *reinterpret_cast<float4*>(xr + c0) = make_float4(v[0], v[1], v[2], v[3]);
-    *reinterpret_cast<float4*>(xr + c0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
-  }
+  float v[NP][8];
   float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; i++) ss += v[i] * v[i];
-  const float inv = rsqrtf(block_sum256(ss, red) / (float)d + 1e-6f);
-  float4 w0 = *reinterpret_cast<const float4*>(w + c0), w1 = *reinterpret_cast<const float4*>(w + c0 + 4);
-  const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-  uint4 o;
-  __half2* o2 = reinterpret_cast<__half2*>(&o);
+  for (int p = 0; p < NP; p++) {
+    const int c0 = 2048 * p + threadIdx.x * 8;
 #pragma unroll
-  for (int i = 0; i < 4; i++) o2[i] = __floats2half2_rn(v[2 * i] * inv * ww[2 * i], v[2 * i + 1] * inv * ww[2 * i + 1]);
-  *reinterpret_cast<uint4*>(h + (size_t)t * d + c0) = o;
+    for (int i = 0; i < 8; i++) v[p][i] = 0.0f;
+    if (c0 < d) {
+      float4 a = *reinterpret_cast<const float4*>(xr + c0), b = *reinterpret_cast<const float4*>(xr + c0 + 4);
+      v[p][0] = a.x; v[p][1] = a.y; v[p][2] = a.z; v[p][3] = a.w; v[p][4] = b.x; v[p][5] = b.y; v[p][6] = b.z; v[p][7] = b.w;
+      if (add) {
+        uint4 yy = *reinterpret_cast<const uint4*>(y + (size_t)t * d + c0);
+        const __half2* y2 = reinterpret_cast<const __half2*>(&yy);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          float2 f = __half22float2(y2[i]);
+          v[p][2 * i] += f.x;
+          v[p][2 * i + 1] += f.y;
+        }
+        *reinterpret_cast<float4*>(xr + c0) = make_float4(v[p][0], v[p][1], v[p][2], v[p][3]);
+        *reinterpret_cast<float4*>(xr + c0 + 4) = make_float4(v[p][4], v[p][5], v[p][6], v[p][7]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) ss += v[p][i] * v[p][i];
+  }
+  const float inv = rsqrtf(block_sum256(ss, red) / (float)d + 1e-6f);
+#pragma unroll
+  for (int p = 0; p < NP; p++) {
+    const int c0 = 2048 * p + threadIdx.x * 8;
+    if (c0 >= d) continue;
+    float4 w0 = *reinterpret_cast<const float4*>(w + c0), w1 = *reinterpret_cast<const float4*>(w + c0 + 4);
+    const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    uint4 o;
+    __half2* o2 = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      o2[i] = __floats2half2_rn(v[p][2 * i] * inv * ww[2 * i], v[p][2 * i + 1] * inv * ww[2 * i + 1]);
+    *reinterpret_cast<uint4*>(h + (size_t)t * d + c0) = o;
+  }
 }
 
 // The final norm (src/kernels.rs:93-120 with add and f32 out, src/engine.rs:519-522): for each
 // requested row, x += y (y null: nothing to add, the last matmul added its output already),
 // out = x * inv * w in f32.
+template <int NP>
 __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, const __half* __restrict__ y,
                                                          const float* __restrict__ w, const int* __restrict__ rows, int l,
                                                          int d, float* __restrict__ out, int* err) {
@@ -121,10 +142,10 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
     if (threadIdx.x == 0) atomicCAS(err, 0, kErrBadShape);
     return;
   }
-  float v[8];
+  float v[8 * NP];
   float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
+  for (int i = 0; i < 8 * NP; i++) {
     const int c = threadIdx.x + 256 * i;
     float a = 0.0f;
     if (c < d) {
@@ -139,7 +160,7 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
   }
   const float inv = rsqrtf(block_sum256(ss, red) / (float)d + 1e-6f);
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
+  for (int i = 0; i < 8 * NP; i++) {
     const int c = threadIdx.x + 256 * i;
     if (c < d) out[(size_t)blockIdx.x * d + c] = v[i] * inv * w[c];
   }
@@ -525,21 +546,40 @@ __global__ void add_bias_kernel(__half* __restrict__ y, const float* __restrict_
 // ---------------------------------------------------------------------------------------------
 static int blocks_for(int64_t n, int per) { return (int)std::min<int64_t>((n + per - 1) / per, 65535); }
 
+static bool norm_dim_ok(int d) { return d > 0 && d <= kMaxD && d % 64 == 0; }
+
 cudaError_t launch_embed_norm(const uint32_t* ids, int l, const uint8_t* eq, const __half* es, int bits, int d, int vocab,
                               const float* w, float* x, __half* h, int* err, cudaStream_t st) {
-  if (d > 2048 || d % 32) return cudaErrorInvalidValue;
-  return launch_dependent(embed_norm_kernel, dim3(l), dim3(256), 0, st, ids, eq, es, bits, d, vocab, w, x, h, err);
+  if (!norm_dim_ok(d)) return cudaErrorInvalidValue;
+  switch ((d + 2047) / 2048) {
+    case 1: return launch_dependent(embed_norm_kernel<1>, dim3(l), dim3(256), 0, st, ids, eq, es, bits, d, vocab, w, x, h, err);
+    case 2: return launch_dependent(embed_norm_kernel<2>, dim3(l), dim3(256), 0, st, ids, eq, es, bits, d, vocab, w, x, h, err);
+    case 3: return launch_dependent(embed_norm_kernel<3>, dim3(l), dim3(256), 0, st, ids, eq, es, bits, d, vocab, w, x, h, err);
+    default: return launch_dependent(embed_norm_kernel<4>, dim3(l), dim3(256), 0, st, ids, eq, es, bits, d, vocab, w, x, h, err);
+  }
 }
 
 cudaError_t launch_add_norm(float* x, const __half* y, const float* w, int l, int d, bool add, __half* h, cudaStream_t st) {
-  if (d != 2048) return cudaErrorInvalidValue;
-  return launch_dependent(add_norm_kernel, dim3(l), dim3(256), 0, st, x, y, w, d, add ? 1 : 0, h);
+  if (!norm_dim_ok(d)) return cudaErrorInvalidValue;
+  const int a = add ? 1 : 0;
+  switch ((d + 2047) / 2048) {
+    case 1: return launch_dependent(add_norm_kernel<1>, dim3(l), dim3(256), 0, st, x, y, w, d, a, h);
+    case 2: return launch_dependent(add_norm_kernel<2>, dim3(l), dim3(256), 0, st, x, y, w, d, a, h);
+    case 3: return launch_dependent(add_norm_kernel<3>, dim3(l), dim3(256), 0, st, x, y, w, d, a, h);
+    default: return launch_dependent(add_norm_kernel<4>, dim3(l), dim3(256), 0, st, x, y, w, d, a, h);
+  }
 }
 
 cudaError_t launch_final_norm(float* x, const __half* y, const float* w, const int* rows, int nrows, int l, int d, float* out,
                               int* err, cudaStream_t st) {
   if (nrows <= 0) return cudaSuccess;
-  return launch_dependent(final_norm_kernel, dim3(nrows), dim3(256), 0, st, x, y, w, rows, l, d, out, err);
+  if (!norm_dim_ok(d)) return cudaErrorInvalidValue;
+  switch ((d + 2047) / 2048) {
+    case 1: return launch_dependent(final_norm_kernel<1>, dim3(nrows), dim3(256), 0, st, x, y, w, rows, l, d, out, err);
+    case 2: return launch_dependent(final_norm_kernel<2>, dim3(nrows), dim3(256), 0, st, x, y, w, rows, l, d, out, err);
+    case 3: return launch_dependent(final_norm_kernel<3>, dim3(nrows), dim3(256), 0, st, x, y, w, rows, l, d, out, err);
+    default: return launch_dependent(final_norm_kernel<4>, dim3(nrows), dim3(256), 0, st, x, y, w, rows, l, d, out, err);
+  }
 }
 
 cudaError_t launch_conv(const __half* big, int stride, const float* conv_w, const __half* hist, int l, int C, __half* qkvc,
@@ -637,7 +677,10 @@ cudaError_t launch_wait_probe(int* err, unsigned long long limit_ns, cudaStream_
 // Loads the row-wise kernels on the current device (see preload_gemm).
 cudaError_t preload_kernels() {
   cudaFuncAttributes a;
-  const void* fns[] = {(const void*)embed_norm_kernel, (const void*)add_norm_kernel,   (const void*)final_norm_kernel,
+  const void* fns[] = {(const void*)embed_norm_kernel<1>, (const void*)embed_norm_kernel<2>, (const void*)embed_norm_kernel<3>,
+                       (const void*)embed_norm_kernel<4>, (const void*)add_norm_kernel<1>,   (const void*)add_norm_kernel<2>,
+                       (const void*)add_norm_kernel<3>,   (const void*)add_norm_kernel<4>,   (const void*)final_norm_kernel<1>,
+                       (const void*)final_norm_kernel<2>, (const void*)final_norm_kernel<3>, (const void*)final_norm_kernel<4>,
                        (const void*)conv_kernel,       (const void*)hist_update_kernel, (const void*)gdn_gates_kernel,
                        (const void*)gdn_recurrent_kernel, (const void*)gnorm_kernel,  (const void*)qk_prep_kernel,
                        (const void*)trace_kernel,      (const void*)add_bias_kernel,    (const void*)hist_pack_kernel,

@@ -277,17 +277,18 @@ class _ShardWriter:
 
 def write_synthetic(path: str, seed: int = 0, n_layers: int = PROD_LAYERS, vocab: int = PROD_VOCAB,
                     embed_bits: int = 3, embed_u8: bool = False, layer_types: list | None = None,
-                    matmul_formats: list | None = None) -> dict:
+                    matmul_formats: list | None = None, dims: dict | None = None) -> dict:
     """Writes a complete model directory with seeded random-init weights in the reference's format.
 
-    The dims are the production ones (:data:`PROD`); ``n_layers``/``vocab`` shrink test models. The
+    The dims are the production ones (:data:`PROD`), with ``dims`` overriding any of them (other
+    sizes of the family); ``n_layers``/``vocab`` shrink test models. The
     init keeps the residual stream O(1): embedding rows of std 1, projections into the stream sized
     to add about 0.3 RMS each (from the typical RMS of their inputs), other projections
     1/sqrt(K). Returns the manifest."""
     os.makedirs(path, exist_ok=True)
     rng = np.random.default_rng(seed)
     types = layer_types or layer_pattern(n_layers)
-    cfg = Config(layer_types=types, **PROD)
+    cfg = Config(layer_types=types, **{**PROD, **(dims or {})})
     d, i_size = cfg.hidden_size, cfg.intermediate_size
     h, dk, dv = cfg.linear_num_key_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
     hq, hk, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
