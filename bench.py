@@ -591,7 +591,7 @@ def kernel_gdn(steps, warmup, seed=0, algo=0):
                         f"config 3 through sd_gdn algo {algo}", "l2": "flushed before each timed launch"}
 
 
-def kernel_gemm(m, n, k, steps, warmup, seed=0):
+def kernel_gemm(m, n, k, steps, warmup, seed=0, algo=0):
     import torch
     from strands_decider import model as M
     from strands_decider.engine import QWeight
@@ -608,13 +608,16 @@ def kernel_gemm(m, n, k, steps, warmup, seed=0):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
     def fn():
-        w.matmul(a.data_ptr(), m, y.data_ptr(), n // 2 if silu else n, silu=silu, ws_dev=ws.data_ptr(), ws_bytes=ws.numel() * 4)
+        w.matmul_ex(a.data_ptr(), m, y.data_ptr(), n // 2 if silu else n, silu=silu, ws_dev=ws.data_ptr(),
+                    ws_bytes=ws.numel() * 4, algo=algo)
     ms = _timed_launches(fn, steps, warmup, flush)
     fl = 2.0 * m * n * k
     _, tf_burst, _, src = peaks()
     return {"us": ms * 1e3, "achieved": fl / ms / 1e9, "unit": "TFLOP/s", "peak": tf_burst, "frac": fl / ms / 1e9 / tf_burst,
             "peak_source": f"{src} bf16 burst", "bound": "tensor" if m > 71 else "hbm", "weight_gbs": n * k * 0.5625 / ms / 1e6,
-            "workload": f"gemm m={m} n={n} k={k}" + (" (SwiGLU epilogue)" if silu else ""), "l2": "flushed before each timed launch"}
+            "workload": f"gemm m={m} n={n} k={k}" + (" (SwiGLU epilogue)" if silu else "") +
+                        {0: "", 1: ", tcgen05 tiles", 2: ", small-M mma.sync kernel"}[algo],
+            "l2": "flushed before each timed launch"}
 
 
 WORDS = ("payout", "failing", "account", "billing", "urgent", "refund", "customer", "support", "invoice", "delay",
@@ -701,7 +704,7 @@ def run_kernel_workload(args):
         r = kernel_gdn(args.steps, args.warmup, args.seed, args.gdn_algo)
         metric = "gated delta rule GB/s (config 3)"
     else:
-        r = kernel_gemm(args.m, args.n, args.k, args.steps, args.warmup, args.seed)
+        r = kernel_gemm(args.m, args.n, args.k, args.steps, args.warmup, args.seed, args.gemm_algo)
         metric = "dequantizing GEMM TFLOP/s"
     line = {"metric": metric, "value": r["achieved"], "unit": r["unit"], "us_per_launch": r["us"],
             "roofline": {k: r[k] for k in ("achieved", "peak", "unit", "frac", "peak_source")}, "config": r,
@@ -723,6 +726,8 @@ def main():
     ap.add_argument("--m", type=int, default=2048)
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--gemm-algo", type=int, default=0, choices=[0, 1, 2],
+                    help="sd_matmul_ex algo for --workload gemm (0: the planner, 1: tcgen05 tiles, 2: small-M kernel)")
     ap.add_argument("--gdn-algo", type=int, default=0, help="sd_gdn algo for --workload gdn (0: the fused tcgen05 scan)")
     ap.add_argument("--no-configs", action="store_true", help="skip configs 1-4 beside the sweep (N=1 only)")
     args = ap.parse_args()

@@ -293,6 +293,17 @@ void sd_qweight_free(sd_qweight* w);
 int sd_matmul(const sd_qweight* w, const void* act_dev, int32_t m, void* y_dev, int32_t ldy, int32_t silu, void* ws_dev,
               size_t ws_bytes, void* stream);
 
+/* sd_matmul with the kernel chosen and the residual add: algo 0 is sd_matmul's choice (where k is a
+ * multiple of 128, the small-M kernel up to 16 tokens, or up to 64 with n <= 4096; else the tcgen05
+ * tiles), 1 the tcgen05 tiles,
+ * 2 the small-M kernel (mma.sync on weights dequantized in registers, K split over a thread-block
+ * cluster; up to 256 tokens, k a multiple of 128; SD_ERR_INVALID otherwise). With x_dev (f32 rows,
+ * ldy floats apart, 16-byte aligned; no silu) the f16-rounded products are added into x instead of
+ * stored to y (y_dev may then be null): `add_norm`'s residual add (src/kernels.rs:93-120) done by the
+ * matmul, as the engine runs it. Results of one algo do not change run to run. */
+int sd_matmul_ex(const sd_qweight* w, const void* act_dev, int32_t m, void* y_dev, int32_t ldy, int32_t silu, void* x_dev,
+                 void* ws_dev, size_t ws_bytes, int32_t algo, void* stream);
+
 /* The standalone calls (sd_gdn, sd_attention*, sd_matmul) return once their kernels are queued; a
  * kernel that gave up (one of its bounded waits ran out, 2 s) records an error code on the device
  * instead of faulting. sd_op_status synchronises `stream`, reads and clears those codes on the

@@ -2043,29 +2043,45 @@ static int* matmul_err_word(int dev, bool create) {
   return word[dev];
 }
 
-int sd_matmul(const sd_qweight* w, const void* act, int32_t m, void* y, int32_t ldy, int32_t silu, void* ws, size_t ws_bytes,
-              void* stream) {
-  if (!w || !act || !y || m <= 0 || (silu && !w->w.interleaved)) {
+int sd_matmul_ex(const sd_qweight* w, const void* act, int32_t m, void* y, int32_t ldy, int32_t silu, void* x, void* ws,
+                 size_t ws_bytes, int32_t algo, void* stream) {
+  if (!w || !act || (!y && !x) || m <= 0 || (silu && !w->w.interleaved) || (x && silu) || algo < 0 || algo > 2) {
     set_global_error("sd_matmul: bad arguments");
     return SD_ERR_INVALID;
   }
   // the epilogue stores 16-byte vectors: 16-byte aligned buffers, rows of whole vectors
   const int nout = silu ? w->w.n / 2 : w->w.n;
-  if (ldy < nout || ldy % 8 || w->w.n % 8 || (silu && w->w.n % 32) || ((uintptr_t)act | (uintptr_t)y) % 16 ||
+  if (ldy < nout || ldy % 8 || w->w.n % 8 || (silu && w->w.n % 32) || ((uintptr_t)act | (uintptr_t)y | (uintptr_t)x) % 16 ||
       (uintptr_t)ws % 16) {
     set_global_error("sd_matmul: ldy must be >= the output width and a multiple of 8, n a multiple of 8 (32 with "
-                     "silu), and act, y and ws 16-byte aligned");
+                     "silu), and act, y, x and ws 16-byte aligned");
     return SD_ERR_INVALID;
   }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= sd::kMaxDevices) return op_result(cudaErrorInvalidDevice, "sd_matmul");
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (algo == 2) {
+    int nt, sp, kts;
+    if (!sd::gemm_small_plan(w->w, m, sms, &nt, &sp, &kts)) {
+      set_global_error("sd_matmul: the small-M kernel takes up to 256 tokens and k a multiple of 128");
+      return SD_ERR_INVALID;
+    }
+  }
   int* err_word = matmul_err_word(dev, true);
   if (!err_word) return op_result(cudaErrorMemoryAllocation, "sd_matmul");
   return op_result(sd::gemm_q4(w->w, (const __half*)act, m, w->w.k, (__half*)y, ldy, silu != 0, (float*)ws, ws_bytes,
-                               err_word, sms, (cudaStream_t)stream),
+                               err_word, sms, (cudaStream_t)stream, nullptr, (float*)x, algo),
                    "sd_matmul");
+}
+
+int sd_matmul(const sd_qweight* w, const void* act, int32_t m, void* y, int32_t ldy, int32_t silu, void* ws, size_t ws_bytes,
+              void* stream) {
+  if (!y) {
+    set_global_error("sd_matmul: bad arguments");
+    return SD_ERR_INVALID;
+  }
+  return sd_matmul_ex(w, act, m, y, ldy, silu, nullptr, ws, ws_bytes, 0, stream);
 }
 
 int sd_op_status(void* stream) {

@@ -25,12 +25,17 @@
 //
 // Numerics: the dequantized weight is (q - 8) * scale rounded to f16, as the reference's tiled
 // kernel computes it (src/kernels.rs:671); products accumulate in f32; the output is rounded to f16.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "sd_internal.h"
+
+namespace cg = cooperative_groups;
 
 namespace sd {
 
@@ -500,6 +505,250 @@ __global__ void __launch_bounds__(256) gemm_finish(const float* __restrict__ ws,
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Small-M path: a weight-streaming GEMM on mma.sync for a few dozen tokens
+// ---------------------------------------------------------------------------------------------
+// Below about a hundred tokens the tcgen05 kernel is bound by its MMA issue (one M=128 MMA per 16 k,
+// whatever N is) and by its split-K finish, not by the weight bytes (the reference switches to its
+// GEMV below 21 rows for the same reason, src/engine.rs:425-431). This kernel dequantizes each
+// thread's weights in registers straight into the A fragments of mma.sync.m16n8k16 (f16 in, f32
+// accumulate), so nothing but the packed tile bytes moves through memory, and splits K across the
+// CTAs of a thread-block cluster, which add their partial tiles through distributed shared memory in
+// rank order: one launch, no workspace, the same sums run to run.
+//
+// A CTA of four warps takes one 128-row block of the tile layout, a range of k-tiles (one split) and
+// up to 8 NT tokens. Warp w owns rows 32w .. 32w + 31 as two 16-row MMA row groups; lane (g, t) holds
+// rows g, g + 8, g + 16, g + 24 of them. The MMA's k order is free (the sum over k is the same in any
+// order as long as A and B agree), so in each step of two k-tiles (four 32-weight k-groups) lane t
+// takes k-group t whole: one 16-byte load per row of its four 8-weight words, and word q feeds the
+// two MMAs of sub-step q, whose B fragments are then the 8 activations of that word (one 16-byte
+// load per token, through L1, where the CTA's four warps share them). Weights are streamed past L1.
+SD_DEV uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+SD_DEV uint32_t ld_stream4(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+SD_DEV void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+constexpr int kSmallThreads = 128;
+constexpr int kSmallMaxSplits = 8;  // the portable cluster size
+constexpr int kSmallMaxM = 256;  // tokens the small-M kernel takes (token blocks of 32 over the grid)
+
+// Where the planner takes the small-M kernel, from steady-state times on B200 (back-to-back launches,
+// weights cold; small-M vs tcgen05 tiles, us): up to 16 tokens on every shape (in_proj n = 8256:
+// 10.9 vs 14.4 at m = 16, 7.2 vs 12.9 at m = 1); up to 64 tokens where the output is narrow, n <= 4096
+// (down n = 2048, k = 6144: 13.3 vs 14.4 at m = 64; out_proj 2048 x 2048: 8.8 vs 10.8). The wide
+// outputs past 16 tokens stay on the tcgen05 tiles (gate_up n = 12288, m = 32: 17.7 vs 15.0).
+static bool small_wins(const QWeight& w, int M) { return M <= 16 || (M <= 64 && w.n <= 4096); }
+
+// Activations: each CTA stages its tokens' k-range in chunks of 256 (two steps) through a two-chunk
+// shared-memory ring (cp.async, issued with the weight loads of the chunk before), so the MMAs wait on
+// shared-memory latency only. A token row of a chunk is 32 16-byte units stored at u ^ bit 3 of u, in
+// rows of 34 units: a quarter warp's B loads (tokens g, g + 1; units 16 s + 4 t + q) hit 8 distinct
+// bank groups.
+constexpr int kSmallChunkK = 256;
+constexpr int kSmallRowU = kSmallChunkK / 8 + 2;
+
+template <int NT>
+struct SmallCfg {
+  static constexpr int RS = NT == 1 ? 40 : 8 * NT + 8;  // f32 row stride of the partial tile (float2 stores conflict-free)
+  static constexpr int kBuf = 8 * NT * kSmallRowU * 16;  // one chunk of activations
+  static constexpr int kRed = kBM * RS * 4;             // the partial tile (reuses the ring after the main loop)
+  static constexpr int kSmem = 2 * kBuf > kRed ? 2 * kBuf : kRed;
+};
+
+// One step's packed weights of a lane: four rows' words of its k-group, their scale pairs (and bias pairs).
+struct SmallW {
+  uint4 q[4];
+  uint32_t s[4], b[4];
+};
+
+template <bool ASYM>
+SD_DEV void small_load(SmallW& w, const uint8_t* tile, int hb, int row0) {
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const int row = row0 + 8 * r;
+    w.q[r] = ld_stream16(tile + hb * kHalfCodes + row * 16);
+    w.s[r] = ld_stream4(tile + kTileCodes + row * 4);
+    if (ASYM) w.b[r] = ld_stream4(tile + kTileBytes + row * 4);
+  }
+}
+
+SD_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// Step s (0 or 1) of the chunk in `buf`: lane (g, t) reads token 8 j + g, units 16 s + 4 t + q.
+template <int NT, bool ASYM>
+SD_DEV void small_step(const SmallW& w, int hb, const uint4* buf, int s, int g, int t, float (&c)[2][NT][4]) {
+  __half2 s2[4], b2[4];
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    s2[r] = __half2half2(__ushort_as_half((unsigned short)(w.s[r] >> (16 * hb))));
+    if (ASYM) b2[r] = __half2half2(__ushort_as_half((unsigned short)(w.b[r] >> (16 * hb))));
+  }
+  const uint4* bb = buf + g * kSmallRowU + 16 * s + 4 * t;
+  const int sw = t >> 1;  // bit 3 of the unit 16 s + 4 t + q
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    uint32_t a[2][8];
+#pragma unroll
+    for (int rg = 0; rg < 2; rg++) {
+      const uint32_t lo = reinterpret_cast<const uint32_t*>(&w.q[2 * rg])[q];
+      const uint32_t hi = reinterpret_cast<const uint32_t*>(&w.q[2 * rg + 1])[q];
+#pragma unroll
+      for (int p = 0; p < 4; p++) {  // element pair p of the word: k 8q + 2p, + 1 of this k-group
+        __half2 vl, vh;
+        if (ASYM) {
+          vl = dq_pair_affine(lo, p, s2[2 * rg], b2[2 * rg]);
+          vh = dq_pair_affine(hi, p, s2[2 * rg + 1], b2[2 * rg + 1]);
+        } else {
+          vl = dq_pair(lo, p, s2[2 * rg]);
+          vh = dq_pair(hi, p, s2[2 * rg + 1]);
+        }
+        // A fragment: {row g, k 2t}, {row g + 8, k 2t}, {row g, k 2t + 8}, {row g + 8, k 2t + 8}; pairs 0, 1
+        // are the first MMA's k 2t and 2t + 8, pairs 2, 3 the second's
+        a[rg][(p >> 1) * 4 + (p & 1) * 2 + 0] = h2_as_u32(vl);
+        a[rg][(p >> 1) * 4 + (p & 1) * 2 + 1] = h2_as_u32(vh);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+      const uint4 bv = bb[j * 8 * kSmallRowU + (q ^ sw)];  // (16 s + 4 t + q) ^ sw: 16 s + 4 t has its low bits clear
+      mma16816(c[0][j], a[0], bv.x, bv.y);
+      mma16816(c[0][j], a[0] + 4, bv.z, bv.w);
+      mma16816(c[1][j], a[1], bv.x, bv.y);
+      mma16816(c[1][j], a[1] + 4, bv.z, bv.w);
+    }
+  }
+}
+
+template <int EPI, int NT, bool ASYM>
+__global__ void __launch_bounds__(kSmallThreads) gemm_q4_small(const uint8_t* __restrict__ wt, int tile_bytes, int KT,
+                                                               int kts, const __half* __restrict__ act, int lda, int M,
+                                                               int N, __half* __restrict__ y, int ldy,
+                                                               float* __restrict__ xadd) {
+  using Cfg = SmallCfg<NT>;
+  constexpr int RS = Cfg::RS, TOK = 8 * NT;
+  extern __shared__ __align__(16) uint8_t small_smem[];
+  uint4* ring = reinterpret_cast<uint4*>(small_smem);  // [2][TOK][kSmallRowU]
+  float* red = reinterpret_cast<float*>(small_smem);   // [128][RS], after the main loop
+  const int S = gridDim.x, split = blockIdx.x, nb = blockIdx.y, m0 = blockIdx.z * TOK;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, hb = t & 1;
+  const int row0 = warp * 32 + g;
+  const int kt0 = split * kts, kt1 = min(KT, kt0 + kts);
+  const int nsteps = max(0, kt1 - kt0) / 2, nchunks = (nsteps + 1) / 2;
+  // lane t's k-group in step i: k-tile kt0 + 2 i + t / 2, half t % 2
+  const uint8_t* tile0 = wt + ((size_t)nb * KT + kt0 + (t >> 1)) * tile_bytes;
+  const size_t step_bytes = (size_t)2 * tile_bytes;
+  const int ntok = min(TOK, M - m0);
+  const int k0 = kt0 * kBK, kend = kt1 * kBK;
+
+  float c[2][NT][4];
+#pragma unroll
+  for (int rg = 0; rg < 2; rg++)
+#pragma unroll
+    for (int j = 0; j < NT; j++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) c[rg][j][e] = 0.0f;
+
+  // the weights depend on nothing the stream computes: the first two steps' loads go out before the
+  // wait for the kernel before (programmatic dependent launch)
+  SmallW w0, w1;
+  if (nsteps > 0) small_load<ASYM>(w0, tile0, hb, row0);
+  if (nsteps > 1) small_load<ASYM>(w1, tile0 + step_bytes, hb, row0);
+  grid_dep_wait();
+  // chunk ch of the activations into ring slot ch % 2 (tokens past M and k past the split stay unloaded:
+  // they only reach output columns that are never stored, or no product at all)
+  auto load_chunk = [&](int ch) {
+    uint4* dst = ring + (ch & 1) * TOK * kSmallRowU;
+    const int kc = k0 + ch * kSmallChunkK;
+    for (int idx = threadIdx.x; idx < TOK * (kSmallChunkK / 8); idx += kSmallThreads) {
+      const int tk = idx / (kSmallChunkK / 8), u = idx % (kSmallChunkK / 8);
+      if (tk < ntok && kc + 8 * u < kend)
+        cp_async16(dst + tk * kSmallRowU + (u ^ ((u >> 3) & 1)), act + (size_t)(m0 + tk) * lda + kc + 8 * u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (nchunks > 0) load_chunk(0);
+#pragma unroll 1
+  for (int ch = 0; ch < nchunks; ch++) {
+    if (ch + 1 < nchunks) {
+      load_chunk(ch + 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const uint4* buf = ring + (ch & 1) * TOK * kSmallRowU;
+    const int i = 2 * ch;
+    small_step<NT, ASYM>(w0, hb, buf, 0, g, t, c);
+    if (i + 2 < nsteps) small_load<ASYM>(w0, tile0 + (i + 2) * step_bytes, hb, row0);
+    if (i + 1 < nsteps) {
+      small_step<NT, ASYM>(w1, hb, buf, 1, g, t, c);
+      if (i + 3 < nsteps) small_load<ASYM>(w1, tile0 + (i + 3) * step_bytes, hb, row0);
+    }
+    __syncthreads();  // the slot is loaded again two chunks on
+  }
+
+  // the partial tile: C fragment {row g, tokens 2t, 2t + 1}, {row g + 8, same}
+#pragma unroll
+  for (int rg = 0; rg < 2; rg++)
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+      const int r = warp * 32 + rg * 16 + g, col = 8 * j + 2 * t;
+      *reinterpret_cast<float2*>(&red[r * RS + col]) = make_float2(c[rg][j][0], c[rg][j][1]);
+      *reinterpret_cast<float2*>(&red[(r + 8) * RS + col]) = make_float2(c[rg][j][2], c[rg][j][3]);
+    }
+  cg::cluster_group cluster = cg::this_cluster();
+  if (S > 1) cluster.sync();
+  else __syncthreads();
+
+  // rank r finishes rows [r 128 / S, (r + 1) 128 / S): the splits' partials summed in rank order
+  const float* part[kSmallMaxSplits];
+#pragma unroll
+  for (int sp = 0; sp < kSmallMaxSplits; sp++) part[sp] = sp < S ? (S > 1 ? cluster.map_shared_rank(red, sp) : red) : red;
+  const int rows = kBM / S, rb = (S > 1 ? (int)cluster.block_rank() : 0) * rows;
+  const int n0 = nb * kBM;
+  for (int e = threadIdx.x; e < (rows / 2) * ntok; e += kSmallThreads) {
+    const int rp = e % (rows / 2), tk = e / (rows / 2);
+    const int r = rb + 2 * rp, n = n0 + r;
+    float v0 = 0.0f, v1 = 0.0f;
+#pragma unroll
+    for (int sp = 0; sp < kSmallMaxSplits; sp++)
+      if (sp < S) {
+        v0 += part[sp][r * RS + tk];
+        v1 += part[sp][(r + 1) * RS + tk];
+      }
+    if (n >= N) continue;  // N is even: rows n and n + 1 are both in or both out
+    const size_t o = (size_t)(m0 + tk) * ldy;
+    if (EPI == kEpiSilu) {
+      y[o + n / 2] = __float2half_rn(swiglu(v0, v1));
+    } else if (EPI == kEpiAdd) {
+      float2* px = reinterpret_cast<float2*>(xadd + o + n);
+      float2 xv = *px;
+      xv.x += __half2float(__float2half_rn(v0));
+      xv.y += __half2float(__float2half_rn(v1));
+      *px = xv;
+    } else {
+      *reinterpret_cast<__half2*>(y + o + n) = __floats2half2_rn(v0, v1);
+    }
+  }
+  if (S > 1) cluster.sync();  // no CTA leaves while another still reads its partial tile
+}
+
 // Reference layout -> tile layout. The reference stores each row as k/32 blocks of 32 codes of `bits`
 // bits (src/kernels.rs:545-586: int4 as 4 words of 8 nibbles; int2 as 2 words of 16 two-bit fields;
 // int3 as those 2 words for the low two bits and a third word for the high bits) with one f16 scale
@@ -716,10 +965,88 @@ bool gemm_token_major(const QWeight& w, int M) {
   return token_major < weight_major;
 }
 
+// The small-M kernel's shape: NT token groups of 8 per CTA (the fewest that hold M, up to 32 tokens, then
+// CTAs over token blocks of 32), and K split in k-tile pairs over a cluster of up to 8 CTAs until
+// about two CTAs per SM are busy. False where it does not apply (K not a multiple of 128). Measured on
+// B200 (back-to-back launches, weights cold): 32-token blocks beat 64-token ones at every shape (the
+// MMAs are latency-bound at one warp per SM quarter: in_proj m = 64, 26.9 -> 21.2 us; down 18.7 ->
+// 13.3 us), and splitting to two CTAs per SM beat one and four on the wide shapes.
+bool gemm_small_plan(const QWeight& w, int M, int num_sms, int* nt_out, int* splits_out, int* kts_out) {
+  const int KT = w.k / kBK;
+  if (KT % 2 || M <= 0 || M > kSmallMaxM) return false;
+  const int nt = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+  const long ctas = (long)(w.npad / kBM) * ((M + 8 * nt - 1) / (8 * nt));
+  const int steps = KT / 2;
+  int s = 1;
+  while (s < kSmallMaxSplits && 2 * s <= steps && s * ctas < 2L * num_sms) s *= 2;
+  *nt_out = nt;
+  *splits_out = s;
+  *kts_out = 2 * ((steps + s - 1) / s);
+  return true;
+}
+
+template <int EPI, int NT, bool ASYM>
+static cudaError_t launch_small(const QWeight& w, const __half* act, int lda, int M, int S, int kts, __half* y, int ldy,
+                                float* xadd, cudaStream_t st) {
+  auto kern = gemm_q4_small<EPI, NT, ASYM>;
+  static std::atomic<bool> attr_set[kMaxDevices] = {};  // per instantiation and device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!attr_set[dev].load()) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallCfg<NT>::kSmem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev].store(true);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S, w.npad / kBM, (M + 8 * NT - 1) / (8 * NT));
+  cfg.blockDim = dim3(kSmallThreads);
+  cfg.dynamicSmemBytes = SmallCfg<NT>::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = S;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = S > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w.tiles, w.tile_bytes, w.k / kBK, kts, act,
+                            lda, M, w.n, y, ldy, xadd);
+}
+
+template <int EPI, bool ASYM>
+static cudaError_t launch_small_nt(int nt, const QWeight& w, const __half* act, int lda, int M, int S, int kts, __half* y,
+                                   int ldy, float* xadd, cudaStream_t st) {
+  switch (nt) {
+    case 1: return launch_small<EPI, 1, ASYM>(w, act, lda, M, S, kts, y, ldy, xadd, st);
+    case 2: return launch_small<EPI, 2, ASYM>(w, act, lda, M, S, kts, y, ldy, xadd, st);
+    default: return launch_small<EPI, 4, ASYM>(w, act, lda, M, S, kts, y, ldy, xadd, st);
+  }
+}
+
+template <int EPI>
+static cudaError_t launch_small_epi(int nt, const QWeight& w, const __half* act, int lda, int M, int S, int kts, __half* y,
+                                    int ldy, float* xadd, cudaStream_t st) {
+  return w.asym ? launch_small_nt<EPI, true>(nt, w, act, lda, M, S, kts, y, ldy, xadd, st)
+                : launch_small_nt<EPI, false>(nt, w, act, lda, M, S, kts, y, ldy, xadd, st);
+}
+
 cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
-                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch, float* xadd) {
+                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch, float* xadd, int algo) {
   if (nlaunch) *nlaunch = 0;
   if (M <= 0) return cudaSuccess;
+  if (xadd && (silu || w.n % 4 || ldy % 4 || (uintptr_t)xadd % 16)) return cudaErrorInvalidValue;
+  int nt, ssplits, kts;
+  if (algo != 1 && gemm_small_plan(w, M, num_sms, &nt, &ssplits, &kts) && (algo == 2 || small_wins(w, M)) &&
+      lda % 8 == 0 && (uintptr_t)act % 16 == 0) {
+    if (nlaunch) *nlaunch = 1;
+    return xadd ? launch_small_epi<kEpiAdd>(nt, w, act, lda, M, ssplits, kts, nullptr, ldy, xadd, st)
+                : silu ? launch_small_epi<kEpiSilu>(nt, w, act, lda, M, ssplits, kts, y, ldy, nullptr, st)
+                       : launch_small_epi<kEpiStore>(nt, w, act, lda, M, ssplits, kts, y, ldy, nullptr, st);
+  }
+  if (algo == 2) return cudaErrorInvalidValue;  // the small-M kernel does not take this shape
   int bn, splits, kps;
   gemm_plan(w, M, num_sms, &bn, &splits, &kps);
   const int KT = w.k / kBK;
@@ -736,7 +1063,6 @@ cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half*
   if (make_act_map(&map, act, M, w.k, lda, bn) != 0) return cudaErrorInvalidValue;
   TileGrid tg{w.npad / kBM, (M + bn - 1) / bn, splits, kps, KT, gemm_token_major(w, M) ? 1 : 0};
   if (nlaunch) *nlaunch = splits == 1 ? 1 : 2;
-  if (xadd && (silu || w.n % 4 || ldy % 4 || (uintptr_t)xadd % 16)) return cudaErrorInvalidValue;
   if (splits == 1)
     return xadd ? launch_epi<kEpiAdd>(bn, map, w, M, tg, num_sms, nullptr, ldy, xadd, err, st)
                 : silu ? launch_epi<kEpiSilu>(bn, map, w, M, tg, num_sms, y, ldy, nullptr, err, st)
@@ -770,6 +1096,18 @@ cudaError_t preload_gemm() {
       (e = preload_bn<192>()) != cudaSuccess)
     return e;
   cudaFuncAttributes a;
+  const void* small[] = {
+      (const void*)gemm_q4_small<kEpiStore, 1, false>, (const void*)gemm_q4_small<kEpiStore, 2, false>,
+      (const void*)gemm_q4_small<kEpiStore, 4, false>, (const void*)gemm_q4_small<kEpiSilu, 1, false>,
+      (const void*)gemm_q4_small<kEpiSilu, 2, false>,  (const void*)gemm_q4_small<kEpiSilu, 4, false>,
+      (const void*)gemm_q4_small<kEpiAdd, 1, false>,   (const void*)gemm_q4_small<kEpiAdd, 2, false>,
+      (const void*)gemm_q4_small<kEpiAdd, 4, false>,   (const void*)gemm_q4_small<kEpiStore, 1, true>,
+      (const void*)gemm_q4_small<kEpiStore, 2, true>,  (const void*)gemm_q4_small<kEpiStore, 4, true>,
+      (const void*)gemm_q4_small<kEpiSilu, 1, true>,   (const void*)gemm_q4_small<kEpiSilu, 2, true>,
+      (const void*)gemm_q4_small<kEpiSilu, 4, true>,   (const void*)gemm_q4_small<kEpiAdd, 1, true>,
+      (const void*)gemm_q4_small<kEpiAdd, 2, true>,    (const void*)gemm_q4_small<kEpiAdd, 4, true>};
+  for (const void* f : small)
+    if ((e = cudaFuncGetAttributes(&a, f)) != cudaSuccess) return e;
   if ((e = cudaFuncGetAttributes(&a, gemm_finish)) != cudaSuccess) return e;
   return cudaFuncGetAttributes(&a, repack_q4);
 }

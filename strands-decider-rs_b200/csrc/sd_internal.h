@@ -43,8 +43,13 @@ void gemm_plan(const QWeight& w, int M, int num_sms, int* bn, int* splits, int* 
 // y[M][ldy] = act[M][K] W^T, or SwiGLU of interleaved gate/up rows into y[M][N/2] when silu; ws is
 // the f32 split-K workspace (M * N floats; smaller disables split-K); *nlaunch gets the kernel count.
 // With xadd (f32 rows ldy floats apart, n a multiple of 4, no silu): x += f16(act W^T) instead of y.
+// algo: 0, the planner's choice (the small-M mma.sync kernel where K is a multiple of 128 and M <= 16,
+// or M <= 64 with n <= 4096; else the tcgen05 tiles); 1, the tcgen05 tiles; 2, the small-M kernel (up
+// to 256 tokens).
 cudaError_t gemm_q4(const QWeight& w, const __half* act, int M, int lda, __half* y, int ldy, bool silu, float* ws,
-                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch = nullptr, float* xadd = nullptr);
+                    size_t ws_bytes, int* err, int num_sms, cudaStream_t st, int* nlaunch = nullptr, float* xadd = nullptr,
+                    int algo = 0);
+bool gemm_small_plan(const QWeight& w, int M, int num_sms, int* nt, int* splits, int* kts);
 int make_act_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
 int make_map_3d(CUtensorMap* map, const void* ptr, int x, int y, int z, long long ystride, long long zstride, int box_y);
 // The error words of the standalone calls' kernels (no engine: the C ABI's sd_attention*, sd_gdn):

@@ -89,6 +89,7 @@ def lib() -> C.CDLL:
         L.sd_qweight_create_format.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, C.POINTER(vp)]
         L.sd_qweight_free.argtypes = [vp]
         L.sd_matmul.argtypes = [vp, vp, i32, vp, i32, i32, vp, C.c_size_t, vp]
+        L.sd_matmul_ex.argtypes = [vp, vp, i32, vp, i32, i32, vp, vp, C.c_size_t, i32, vp]
         L.sd_decider_load.argtypes = [cp, C.c_int, C.POINTER(vp)]
         L.sd_decider_free.argtypes = [vp]
         L.sd_decider_ask_all.argtypes = [vp, cp, C.POINTER(vp)]
@@ -448,6 +449,13 @@ class QWeight:
     def matmul(self, act_dev: int, m: int, y_dev: int, ldy: int, silu: bool = False, ws_dev: int | None = None,
                ws_bytes: int = 0, stream=None):
         _check(lib().sd_matmul(self._h, act_dev, m, y_dev, ldy, int(silu), ws_dev, ws_bytes, stream), "sd_matmul")
+
+    def matmul_ex(self, act_dev: int, m: int, y_dev: int | None, ldy: int, silu: bool = False, x_dev: int | None = None,
+                  ws_dev: int | None = None, ws_bytes: int = 0, algo: int = 0, stream=None):
+        """`sd_matmul_ex`: algo 0 (the planner), 1 (tcgen05 tiles), 2 (the small-M kernel); with x_dev the
+        f16-rounded products are added into the f32 rows at x_dev (ldy floats apart)."""
+        _check(lib().sd_matmul_ex(self._h, act_dev, m, y_dev, ldy, int(silu), x_dev, ws_dev, ws_bytes, algo, stream),
+               "sd_matmul")
 
     def __del__(self):
         try:

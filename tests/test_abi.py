@@ -78,3 +78,7 @@ def test_new_entry_points_reject_bad_arguments_without_touching_a_gpu():
     assert b"sd_decode_scales" in L.sd_last_error()
     # no rows at all is a no-op, not an error
     assert L.sd_decode_scales(buf, 0, 64, buf, None) == 0
+    # sd_matmul_ex: no weight, no output, an unknown algo
+    assert L.sd_matmul_ex(None, buf, 4, buf, 64, 0, None, None, 0, 0, None) == -1
+    assert L.sd_matmul_ex(None, buf, 4, None, 64, 0, None, None, 0, 3, None) == -1
+    assert b"sd_matmul" in L.sd_last_error()

@@ -44,6 +44,80 @@ def test_matmul_matches_oracle(torch, m, n, k):
         assert err.max() <= 2e-3 + 2e-3 * np.abs(want).max(), (ws_bytes, err.max())
 
 
+@pytest.mark.parametrize("m", [1, 8, 9, 33, 64, 100, 128, 256])
+@pytest.mark.parametrize("n,k", [(8256, 2048), (2048, 6144), (384, 256)])
+def test_matmul_small_m_kernel(torch, m, n, k):
+    """The small-M kernel (sd_matmul_ex algo 2: mma.sync on weights dequantized in registers, K split over
+    a cluster) against the oracle's f16-dequant matmul and against the tcgen05 tiles (algo 1); the
+    planner's choice (algo 0) is one of the two, bit for bit (the small-M kernel up to 16 tokens, and up
+    to 64 for outputs of at most 4096); two runs agree bit for bit (the cluster adds its splits in rank
+    order). Shapes: in_proj, down (the deepest K split), and a short K with a ragged 128-row block."""
+    from strands_decider.engine import QWeight
+    rng = np.random.default_rng(m * 11 + n + k)
+    packed, scales = M._quant_tensor(rng, n, k, 4, 1.0 / np.sqrt(k))
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    want = oracle.matmul(a, packed, scales, n, k, 4, variant=2).astype(np.float32)
+    q_d, s_d, a_d = dev(torch, packed), dev(torch, scales.view(np.uint16)), dev(torch, a.view(np.uint16))
+    w = QWeight(q_d.data_ptr(), s_d.data_ptr(), n, k)
+    ws = torch.zeros(16 << 20, dtype=torch.float32, device="cuda")
+    outs = {}
+    for algo in (2, 2, 1, 0):
+        y = torch.full((m, n), float("nan"), dtype=torch.float16, device="cuda")
+        w.matmul_ex(a_d.data_ptr(), m, y.data_ptr(), n, ws_dev=ws.data_ptr(), ws_bytes=ws.numel() * 4, algo=algo)
+        torch.cuda.synchronize()
+        got = y.cpu().numpy()
+        if algo == 2 and 2 in outs:
+            assert np.array_equal(got.view(np.uint16), outs[2].view(np.uint16))
+        outs[algo] = got
+    small = outs[2].astype(np.float32)
+    assert np.isfinite(small).all()
+    tol = 2e-3 + 2e-3 * np.abs(want).max()
+    assert np.abs(small - want).max() <= tol
+    assert np.abs(small - outs[1].astype(np.float32)).max() <= tol
+    pick = 2 if (m <= 16 or (m <= 64 and n <= 4096)) else 1
+    assert np.array_equal(outs[0].view(np.uint16), outs[pick].view(np.uint16))
+
+
+@pytest.mark.parametrize("m", [5, 40, 128, 200])
+@pytest.mark.parametrize("epi", ["silu", "add"])
+def test_matmul_small_m_epilogues(torch, m, epi):
+    """The small-M kernel's other epilogues: SwiGLU of interleaved gate/up rows, and the f16-rounded
+    products added into f32 residual rows (x += f16(a W^T), `add_norm`'s add, src/kernels.rs:93-120),
+    against the oracle and against the tcgen05 tiles."""
+    from strands_decider.engine import QWeight
+    n, k = 2048, 2048
+    rng = np.random.default_rng(m + (epi == "add"))
+    packed, scales = M._quant_tensor(rng, n, k, 4, 1.0 / np.sqrt(k))
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    want = oracle.matmul(a, packed, scales, n, k, 4, variant=2).astype(np.float32)
+    q_d, s_d, a_d = dev(torch, packed), dev(torch, scales.view(np.uint16)), dev(torch, a.view(np.uint16))
+    silu = epi == "silu"
+    w = QWeight(q_d.data_ptr(), s_d.data_ptr(), n, k, interleave=silu)
+    got = {}
+    if silu:
+        g, u = want[:, :n // 2], want[:, n // 2:]
+        g, u = g.astype(np.float16).astype(np.float32), u.astype(np.float16).astype(np.float32)
+        want = g / (1 + np.exp(-g)) * u
+        for algo in (1, 2):
+            y = torch.full((m, n // 2), float("nan"), dtype=torch.float16, device="cuda")
+            w.matmul_ex(a_d.data_ptr(), m, y.data_ptr(), n // 2, silu=True, algo=algo)
+            torch.cuda.synchronize()
+            got[algo] = y.cpu().numpy().astype(np.float32)
+        tol = 4e-3 * (1 + np.abs(want).max())
+    else:
+        x0 = rng.standard_normal((m, n)).astype(np.float32)
+        want = x0 + want.astype(np.float16).astype(np.float32)
+        for algo in (1, 2):
+            x = dev(torch, x0)
+            w.matmul_ex(a_d.data_ptr(), m, None, n, x_dev=x.data_ptr(), algo=algo)
+            torch.cuda.synchronize()
+            got[algo] = x.cpu().numpy()
+        tol = 2e-3 + 2e-3 * np.abs(want).max()
+    assert np.isfinite(got[2]).all()
+    assert np.abs(got[2] - want).max() <= tol
+    assert np.abs(got[2] - got[1]).max() <= tol
+
+
 @pytest.mark.parametrize("bits,group,asym", [(3, 32, False), (2, 32, False), (4, 64, False), (3, 128, False), (2, 256, False),
                                              (4, 32, True), (3, 64, True), (2, 128, True)])
 @pytest.mark.parametrize("m", [5, 300])
