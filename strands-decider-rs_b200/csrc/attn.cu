@@ -14,6 +14,8 @@
 // the prefix's (from the cache) and then its own (from tail buffers), never another sequence's.
 #include <algorithm>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "sd_internal.h"
 
@@ -339,7 +341,7 @@ cudaError_t launch_attention(const __half* q, const __half* k, const __half* v, 
                              size_t ws_bytes, cudaStream_t st) {
   if (hd != HD || hq % hk != 0 || l <= 0 || splits < 1) return cudaErrorInvalidValue;
   if (splits > 1 && (!ws || ws_bytes < attention_split_bytes(l, hq, splits))) return cudaErrorInvalidValue;
-  static bool attr[kMaxDevices] = {};
+  static std::atomic<bool> attr[kMaxDevices] = {};  // setting it twice is harmless; the flag only saves the call
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
@@ -364,7 +366,7 @@ cudaError_t launch_attention_packed(const __half* q, const __half* k, const __ha
                                     const AttnPacked& pk, int nblk, int splits, float* ws, size_t ws_bytes, cudaStream_t st) {
   if (hd != HD || hq % hk != 0 || T <= 0 || nblk <= 0 || splits < 1 || !pk.blk) return cudaErrorInvalidValue;
   if (splits > 1 && (!ws || ws_bytes < attention_split_bytes(T, hq, splits))) return cudaErrorInvalidValue;
-  static bool attr[kMaxDevices] = {};
+  static std::atomic<bool> attr[kMaxDevices] = {};  // setting it twice is harmless; the flag only saves the call
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;

@@ -27,6 +27,8 @@
 //
 // Keys of a block past the queries' reach are masked; K/V rows past the valid range read zeros (the
 // tensor maps end there), so a masked key never brings a non-finite value into the PV product.
+#include <atomic>
+
 #include "common.cuh"
 #include "sd_internal.h"
 
@@ -379,7 +381,7 @@ cudaError_t launch_attention_tc(const __half* q, int qrows, const __half* k, con
       (a.blk && a.batch != 1))
     return cudaErrorInvalidValue;
   if (a.gate && (a.gstride % 8 || a.goff % 8 || a.gstep % 8 || (uintptr_t)a.gate % 16)) return cudaErrorInvalidValue;
-  static bool attr[kMaxDevices] = {};  // the shared-memory size, once per device
+  static std::atomic<bool> attr[kMaxDevices] = {};  // the shared-memory size, once per device (setting it twice is harmless)
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;

@@ -877,7 +877,7 @@ static cudaError_t launch_bn(const CUtensorMap& map, const QWeight& w, int M, co
                              int ldy, float* ws, int* err, cudaStream_t st) {
   using Cfg = CfgOf<BN, EPI>;
   auto kern = gemm_q4_tc<BN, EPI>;
-  static bool attr_set[kMaxDevices] = {};  // per instantiation and device
+  static std::atomic<bool> attr_set[kMaxDevices] = {};  // per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
