@@ -8,17 +8,19 @@ state of 64-4096 random non-special token ids (clipped so state + longest questi
 runs as the reference's `Decider::run` does (src/lib.rs:185-198): the state once with a snapshot,
 then each question continued from the snapshot, hidden rows at the option tokens and the last token,
 then the pointer head. A step is a batch of --requests-per-step requests per GPU (weak scaling:
-each rank takes its own requests, no collective on the data path): the states of all of them in one
-packed pass, a snapshot each (sd_forward_batch), then their questions in one batched fork, each
-continuing its own request's snapshot (sd_forward_fork_multi), then the pointer head of every
-question on the GPU (f64), as a server answers concurrent requests.
+each rank takes its own requests, no collective on the data path): the states of all of them and
+their questions in one packed tree pass, each question continuing its own request's state within the
+pass (sd_forward_tree: every layer writes the states' recurrent state, conv history and K/V before
+the questions read them), then the pointer head of every question on the GPU (f64), as a server
+answers concurrent requests. `--two-pass` runs the states as one packed pass kept as snapshots
+(sd_forward_batch), then the questions as one batched fork (sd_forward_fork_multi) instead.
 
 `value`: device-resident inputs (token ids and rows staged in HBM before the timed region),
-passes queued with sd_forward_batch_dev / sd_forward_fork_multi_dev / sd_head_probs_dev,
-probabilities left in HBM; CUDA events on the engine's stream.
-`e2e`: the same requests through the C ABI with host buffers (sd_forward_batch, then
-sd_forward_fork_multi_probs: ids host->device, each question's probabilities device->host,
-synchronous per call).
+passes queued with sd_forward_tree_dev / sd_head_probs_dev (or the two passes), probabilities left
+in HBM; CUDA events on the engine's stream.
+`e2e`: the same requests through the C ABI with host buffers (sd_forward_tree_probs, or
+sd_forward_batch then sd_forward_fork_multi_probs: ids host->device, each question's probabilities
+device->host, synchronous per call).
 `roofline`: the dominant kernel (the dequantizing GEMM), from per-launch CUDA events on the engine's
 stream over a profiled pass of the same steps.
 """
@@ -343,15 +345,17 @@ def run_ours(args, world, rank, local):
                          torch.from_numpy(np.concatenate([q for q, _ in qs]).view(np.int32)).cuda(),
                          [len(q) for q, _ in qs], [list(r) for _, r in qs])
     # the states and the questions of a step's requests back to back in HBM, for the passes across requests
-    step_s, step_q = {}, {}
+    # (the tree pass: all states, then all questions)
+    step_s, step_q, step_t = {}, {}, {}
     for s in range(steps_all + 1):
         ii = step_requests(s, rank, world, per, args.seed)
         step_s[s] = torch.cat([staged[i][0] for i in ii])
         step_q[s] = torch.cat([staged[i][1] for i in ii])
+        step_t[s] = torch.cat([step_s[s], step_q[s]])
     hidden_dev = torch.empty((per * 12, 2048), dtype=torch.float32, device="cuda")
     probs_dev = torch.empty(per * 12, dtype=torch.float64, device="cuda")
     # working memory for the largest pass of any step, up front (as a server sizes it at start-up)
-    eng.reserve(max(max(t.numel() for t in step_s.values()), max(t.numel() for t in step_q.values())), per * 3, per * 12)
+    eng.reserve(max(t.numel() for t in step_t.values()), per * 4, per * 12)
     torch.cuda.synchronize()
 
     # a request as the Decider runs it (`Decider::run`, src/lib.rs:156-208): the state once, kept as
@@ -364,6 +368,17 @@ def run_ours(args, world, rank, local):
     def one_step_dev(s):
         ii = step_requests(s, rank, world, per, args.seed)
         slens = [staged[i][0].numel() for i in ii]
+        if not args.two_pass:  # the states and their questions in one tree pass, then the head
+            lens, rows, parents = list(slens), [[] for _ in ii], [-1] * len(ii)
+            for j, i in enumerate(ii):
+                _, _, ql, qr = staged[i]
+                lens += ql
+                rows += qr
+                parents += [j] * len(ql)
+            eng.forward_tree_dev(None, parents, step_t[s].data_ptr(), lens, rows, hidden_dev.data_ptr())
+            qrows = rows[len(ii):]
+            eng.head_probs_dev(head, hidden_dev.data_ptr(), [len(r) for r in qrows], 1.0, probs_dev.data_ptr())
+            return len(qrows), sum(lens)
         snaps = eng.forward_batch_dev(None, step_s[s].data_ptr(), slens, [[]] * len(ii), None, keep=True)
         caches, lens, rows = [], [], []
         n_tok = sum(slens)
@@ -385,6 +400,19 @@ def run_ours(args, world, rank, local):
         nonlocal h2d, d2h
         ii = step_requests(s, rank, world, per, args.seed)
         states = [reqs[i][0] for i in ii]
+        if not args.two_pass:
+            qids, qrows, parents = [], [], [-1] * len(ii)
+            for j, i in enumerate(ii):
+                qs = reqs[i][1]
+                qids += [q for q, _ in qs]
+                qrows += [r for _, r in qs]
+                parents += [j] * len(qs)
+            outs = eng.forward_tree_probs(None, parents, states + qids, [[] for _ in ii] + qrows, head, 1.0)
+            h2d += sum(x.nbytes for x in states)
+            for q, r, probs in zip(qids, qrows, outs):
+                h2d += q.nbytes + r.nbytes
+                d2h += probs.nbytes
+            return len(outs)
         _, snaps = eng.forward_batch(None, states, [[]] * len(ii), keep=True)
         h2d += sum(x.nbytes for x in states)
         caches, qids, qrows = [], [], []
@@ -442,8 +470,13 @@ def run_ours(args, world, rank, local):
 
     for s in range(args.steps):  # the timed steps' passes, counted outside the timed region
         ii = step_requests(args.warmup + s, rank, world, per, args.seed)
-        roof.add([(0, staged[i][0].numel()) for i in ii], True, hbm_gbs, tf_sustained)
-        roof.add([(staged[i][0].numel(), n) for i in ii for n in staged[i][2]], False, hbm_gbs, tf_sustained)
+        roots = [(0, staged[i][0].numel()) for i in ii]
+        qs_ = [(staged[i][0].numel(), n) for i in ii for n in staged[i][2]]
+        if args.two_pass:
+            roof.add(roots, True, hbm_gbs, tf_sustained)
+            roof.add(qs_, False, hbm_gbs, tf_sustained)
+        else:
+            roof.add(roots + qs_, True, hbm_gbs, tf_sustained)
     bound_all = sum_over_ranks(world, roof.bound_s)
     t_dev = max_over_ranks(world, ms_dev) / 1e3
     t_host = max_over_ranks(world, ms_host) / 1e3
@@ -477,7 +510,7 @@ def run_ours(args, world, rank, local):
         "aggregate_roofline": {"bound_ms_per_step": 1e3 * bound_all / world / args.steps, "frac": bound_all / world / t_dev,
                                "basis": "per packed pass max(bytes / measured HBM, FLOPs / measured sustained bf16), summed over the timed passes"},
         "e2e": {"value": qh_all / t_host, "unit": "questions/s", "h2d_bytes_per_step": int(h2d_step),
-                "d2h_bytes_per_step": int(d2h_step), "path": "sd_forward_batch (the step's states, one snapshot each) + sd_forward_fork_multi_probs (the step's questions, each from its request's snapshot, and the pointer head on the GPU; host ids in, host probabilities out)"},
+                "d2h_bytes_per_step": int(d2h_step), "path": ("sd_forward_batch (the step's states, one snapshot each) + sd_forward_fork_multi_probs (the step's questions, each from its request's snapshot, and the pointer head on the GPU; host ids in, host probabilities out)" if args.two_pass else "sd_forward_tree_probs (the step's states and their questions in one packed pass, each question continuing its request's state, and the pointer head on the GPU; host ids in, host probabilities out)")},
         "gpu_launches": int(launches),
         "roofline": {"kernel": "gemm_q4_tc (dequantizing tcgen05 GEMM)", "bound": "tensor", "achieved": gemm_tflops,
                      "peak": tf_sus, "unit": "TFLOP/s", "frac": gemm_tflops / tf_sus,
@@ -726,6 +759,8 @@ def main():
     ap.add_argument("--m", type=int, default=2048)
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--two-pass", action="store_true",
+                    help="sweep: the states as one pass kept as snapshots, then the questions as one fork (not one tree pass)")
     ap.add_argument("--gemm-algo", type=int, default=0, choices=[0, 1, 2],
                     help="sd_matmul_ex algo for --workload gemm (0: the planner, 1: tcgen05 tiles, 2: small-M kernel)")
     ap.add_argument("--gdn-algo", type=int, default=0, help="sd_gdn algo for --workload gdn (0: the fused tcgen05 scan)")

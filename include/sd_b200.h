@@ -164,6 +164,31 @@ int sd_forward_fork_multi_probs(sd_engine* e, const sd_snapshot* const* caches, 
                                 int32_t n_questions, const int32_t* rows, const int32_t* n_rows, const sd_head* h,
                                 const double* temperatures, double* probs_out);
 
+/* A request's state and its questions in one packed pass (instead of a forward, then a fork): sequence
+ * b continues caches[b] (caches may be null; null entries: a fresh sequence) or, with parent[b] >= 0,
+ * the earlier sequence parent[b] of the same call, which must itself have no parent (parent[b] = -1
+ * otherwise; a sequence with a parent has no snapshot of its own). Each layer writes the parents'
+ * recurrent states, conv histories and keys/values before their children read them, so the children
+ * see what a kept snapshot of the parent would hold (`Engine::forward` with a cache,
+ * src/engine.rs:529-662, and the question loop of `Decider::ask_all`, src/lib.rs:192-198). No
+ * snapshots come out. rows / nrows: output rows per sequence (indices into its own tokens; a
+ * parent's may be none); hidden_out [sum nrows][d] f32. */
+int sd_forward_tree(sd_engine* e, const sd_snapshot* const* caches, const int32_t* parent, const uint32_t* ids,
+                    const int32_t* lens, int32_t nseq, const int32_t* rows, const int32_t* nrows, float* hidden_out);
+
+/* sd_forward_tree with the ids on the GPU and the rows written to hidden_dev, queued on the engine's
+ * stream (as sd_forward_batch_dev). */
+int sd_forward_tree_dev(sd_engine* e, const sd_snapshot* const* caches, const int32_t* parent, const uint32_t* ids_dev,
+                        const int32_t* lens, int32_t nseq, const int32_t* rows, const int32_t* nrows, float* hidden_dev);
+
+/* sd_forward_tree, then the pointer head on the GPU over the sequences that have rows (nrows[b] = 0,
+ * or 2 or more: the options, then the answer row), as sd_forward_fork_multi_probs; probs_out gets
+ * their probabilities in sequence order (nrows[b] - 1 each). temperatures: one per sequence (those
+ * of sequences without rows are not read). */
+int sd_forward_tree_probs(sd_engine* e, const sd_snapshot* const* caches, const int32_t* parent, const uint32_t* ids,
+                          const int32_t* lens, int32_t nseq, const int32_t* rows, const int32_t* nrows, const sd_head* h,
+                          const double* temperatures, double* probs_out);
+
 /* The Decider on the engine (the reference's `Decider`, `src/lib.rs:100-209`): tokenizer, prompt,
  * torso, pointer head and answers in the library (C++). */
 typedef struct sd_decider sd_decider;

@@ -652,7 +652,9 @@ cudaError_t launch(sd_engine* e, int kind, double units, F&& fn) {
 // sequence b continuing snapshot b (the same one for every question of one request, one per request
 // when several requests run together, or none: a fresh sequence), whose states, conv histories and
 // prefix K/V are read in place and never written; with `keep`, each sequence's new state, history
-// and K/V go to a new snapshot of its own. Device arrays: per-layer tables of each sequence's
+// and K/V go to a new snapshot of its own. In a tree pass a sequence may instead continue an earlier
+// sequence of the same pass (a request's questions after its state): the parent's new snapshot is
+// written layer by layer before the children read it. Device arrays: per-layer tables of each sequence's
 // snapshot buffers (null entries: no source snapshot); tpos (position of each packed token), tstart
 // (first token of each token's sequence), tseq (its sequence); seq_off / seq_len / plen (prefix
 // length) per sequence; blk (sequence, first query) per 64-query attention block; for the two-phase
@@ -677,6 +679,11 @@ struct Fork {
   int ktot = 0;                 // rows per head of the gathered keys
   int nseq, nblk, max_len, max_p, max_rows, chunks = 0, nblk128 = 0;
   bool two_phase = false;
+  // a tree pass: sequences nroot .. of gorder continue sequences of the same pass (their parents, in
+  // gorder's first nroot entries), reading the parents' new snapshot buffers of each layer
+  bool tree = false;
+  const int* gorder = nullptr;  // [nseq]: the roots, then the children, each longest first
+  int nroot = 0;
   double pairs;       // causal (query, key) pairs of every sequence: len p + len (len + 1) / 2
   __half *kt, *vt;    // [hk][l][hd] K and V of the packed tokens
 };
@@ -747,14 +754,20 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
         const int N = Lw.in_proj.n;
         __half* hist = fk ? nullptr : e->hist[Lw.slot];
         MM(Lw.in_proj, e->h, d.d, e->big, N, false);
+        // the new snapshots' conv histories; in a tree pass before the conv, whose children read
+        // their parents' (only parents have new snapshots there)
+        auto pack_hist = [&]() -> int {
+          LK(SD_PROF_OTHER, fk->nseq * C * 12.0,
+             sd::launch_hist_pack(e->big, N, C, fk->seq_off, fk->seq_len, fk->hists + (size_t)Lw.slot * fk->nseq,
+                                  fk->h_out + (size_t)Lw.slot * fk->nseq, fk->nseq, st));
+          return SD_OK;
+        };
+        if (fk && fk->tree && (rc = pack_hist()) != SD_OK) return rc;
         LK(SD_PROF_OTHER, L * C * 4.0,
            sd::launch_conv(e->big, N, Lw.conv, hist, l, C, e->qkvc, fk ? fk->tstart : nullptr,
                            fk ? fk->hists + (size_t)Lw.slot * fk->nseq : nullptr, fk ? fk->tseq : nullptr, st));
         if (!fk) LK(SD_PROF_OTHER, C * 12.0, sd::launch_hist_update(e->big, N, hist, l, C, st));
-        else if (fk->h_out)
-          LK(SD_PROF_OTHER, fk->nseq * C * 12.0,
-             sd::launch_hist_pack(e->big, N, C, fk->seq_off, fk->seq_len, fk->hists + (size_t)Lw.slot * fk->nseq,
-                                  fk->h_out + (size_t)Lw.slot * fk->nseq, fk->nseq, st));
+        else if (fk->h_out && !fk->tree && (rc = pack_hist()) != SD_OK) return rc;
         const int aoff = C + d.h * d.dv, boff = aoff + d.h;
         LK(SD_PROF_OTHER, L * d.h * 12.0,
            sd::launch_gdn_gates(e->big, N, aoff, boff, Lw.neg_a, Lw.dt_bias, l, d.h, e->beta, e->decay, st));
@@ -763,9 +776,24 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
         // packed sequences, each from its snapshot's state (or zeros): short ones with the single-pass
         // scan, long ones with the two-phase scan
         const long long max_chunks = fk ? (fk->max_len + 63) / 64 : (l + 63) / 64;
-        const bool use_tc = fk ? gdn_pick_tc(e, (long long)fk->nseq * d.h, max_chunks, (long long)fk->chunks * d.h, fk->two_phase)
+        const bool use_tc = fk ? fk->tree || gdn_pick_tc(e, (long long)fk->nseq * d.h, max_chunks, (long long)fk->chunks * d.h,
+                                                         fk->two_phase)
                                : gdn_pick_tc(e, d.h, max_chunks, max_chunks * d.h, l > 64);
-        if (use_tc) {  // the fused tcgen05 scan: one CTA per (sequence, head)
+        if (fk && fk->tree) {  // the fused scan over the roots, then over the children from the roots' new states
+          sd::GdnTcArgs ga;
+          ga.beta = e->beta, ga.g = e->decay, ga.o = e->of, ga.h = d.h, ga.err = e->d_err;
+          ga.seq_off = fk->seq_off, ga.seq_len = fk->seq_len;
+          ga.s_in = fk->states + (size_t)Lw.slot * fk->nseq;
+          ga.s_out = fk->s_out + (size_t)Lw.slot * fk->nseq;
+          ga.order = fk->gorder;
+          LK(SD_PROF_GDN, gdn_bytes,
+             sd::launch_gdn_tc(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, (long long)l * C,
+                               (long long)l * C, l, ga, fk->nroot * d.h, st));
+          ga.order = fk->gorder + fk->nroot;
+          LK(SD_PROF_GDN, 0.0,
+             sd::launch_gdn_tc(e->qkvc, e->qkvc + d.h * d.dk, C, e->qkvc + 2 * d.h * d.dk, C, (long long)l * C,
+                               (long long)l * C, l, ga, (fk->nseq - fk->nroot) * d.h, st));
+        } else if (use_tc) {  // the fused tcgen05 scan: one CTA per (sequence, head)
           sd::GdnTcArgs ga;
           ga.beta = e->beta, ga.g = e->decay, ga.o = e->of, ga.h = d.h, ga.err = e->d_err;
           int walks = d.h;
@@ -813,6 +841,17 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
           sd::AttnPacked pk;
           pk.blk = fk->blk, pk.seq_off = fk->seq_off, pk.seq_len = fk->seq_len, pk.kt = fk->kt, pk.vt = fk->vt, pk.T = l;
           pk.kp = fk->kp + (size_t)Lw.slot * fk->nseq, pk.vp = fk->vp + (size_t)Lw.slot * fk->nseq, pk.plen = fk->plen;
+          // the sequences' keys and values (prefix and own) into their new snapshots; in a tree pass
+          // first, since the children's prefixes are their parents' new snapshots
+          auto pack_kv = [&]() -> int {
+            LK(SD_PROF_OTHER, 8.0 * d.hk * d.hd * (L + fk->max_p),
+               sd::launch_kv_pack(fk->kt, fk->vt, l, d.hk, d.hd, fk->seq_off, fk->seq_len, fk->plen,
+                                  fk->kp + (size_t)Lw.slot * fk->nseq, fk->vp + (size_t)Lw.slot * fk->nseq,
+                                  fk->k_out + (size_t)Lw.slot * fk->nseq, fk->v_out + (size_t)Lw.slot * fk->nseq, fk->nseq,
+                                  fk->max_rows, st));
+            return SD_OK;
+          };
+          if (fk->tree && (rc = pack_kv()) != SD_OK) return rc;
           if (fk->max_p == 0 && fk->max_len >= 128 && d.hd == 256) {
             // fresh sequences (prefills): the tcgen05 kernel over 128-query blocks
             sd::AttnTcArgs ta;
@@ -843,12 +882,7 @@ int run_layers(sd_engine* e, int l, int p, bool has_cache, int nrows, const Fork
                 sd::launch_attention_packed(e->q, nullptr, nullptr, e->big, N, d.hd, 2 * d.hd, e->o, l, fk->max_p, fk->max_p,
                                             d.hq, d.hk, d.hd, pk, fk->nblk, splits, e->ws, e->ws_bytes, st)));
           }
-          if (fk->k_out)  // the sequences' keys and values (prefix and own) into their new snapshots
-            LK(SD_PROF_OTHER, 8.0 * d.hk * d.hd * (L + fk->max_p),
-               sd::launch_kv_pack(fk->kt, fk->vt, l, d.hk, d.hd, fk->seq_off, fk->seq_len, fk->plen,
-                                  fk->kp + (size_t)Lw.slot * fk->nseq, fk->vp + (size_t)Lw.slot * fk->nseq,
-                                  fk->k_out + (size_t)Lw.slot * fk->nseq, fk->v_out + (size_t)Lw.slot * fk->nseq, fk->nseq,
-                                  fk->max_rows, st));
+          if (fk->k_out && !fk->tree && (rc = pack_kv()) != SD_OK) return rc;
           MM_ADD(Lw.o_proj, e->o, d.hq * d.hd);
         } else {
         LK(SD_PROF_OTHER, L * (N * 2.0 + (d.hq + 2.0 * d.hk) * d.hd * 2.0),
@@ -1044,10 +1078,12 @@ int ensure_pin_slot(sd_engine* e, int slot, size_t ints) {
 // device are read in place. Then the layers. caches: one per sequence, entries may be null (a fresh
 // sequence; the whole array may be null); `fork` names the call in errors and requires every
 // sequence to continue a snapshot. `timed` brackets the layers with the engine's events. *R_out: rows;
-// snaps_out (with keep): the new snapshots.
+// snaps_out (with keep): the new snapshots. parent (may be null): per sequence -1, or the index of an
+// earlier sequence without a parent that this one continues (no snapshot of its own then; no keep).
 int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* caches, bool fork, const uint32_t* ids_host,
                    const uint32_t* ids_dev, const int32_t* lens, int32_t nq, const int32_t* rows, const int32_t* nrows,
-                   bool keep, sd_snapshot** snaps_out, bool has_out, bool timed, long long* R_out) {
+                   bool keep, sd_snapshot** snaps_out, bool has_out, bool timed, long long* R_out,
+                   const int32_t* parent = nullptr) {
   if (nq <= 0 || (!ids_host && !ids_dev) || !lens || !nrows) return e->fail(SD_ERR_INVALID, "%s: no sequences", fn);
   if (nq > 4096) return e->fail(SD_ERR_INVALID, "%s: %d sequences in one call (at most 4096)", fn, nq);
   if (e->trace_host) return e->fail(SD_ERR_INVALID, "%s: per-layer tracing is for sd_forward only", fn);
@@ -1055,11 +1091,23 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   long long T = 0, R = 0;
   int max_len = 0, max_p = 0, max_rows = 0, nblk = 0, nblk128 = 0, chunks = 0, max_chunks = 0;
   double pairs = 0;
+  std::vector<int> pl(nq, 0);   // prefix length of each sequence
+  std::vector<char> has_child(nq, 0);
+  bool tree = false;
+  int nroot = 0;
   for (int b = 0; b < nq; b++) {
-    const sd_snapshot* c = caches ? caches[b] : nullptr;
-    if (!c && fork) return e->fail(SD_ERR_INVALID, "%s: question %d has no snapshot (the questions continue one)", fn, b);
+    const int par = parent ? parent[b] : -1;
+    if (par < -1 || par >= b || (par >= 0 && parent[par] >= 0))
+      return e->fail(SD_ERR_INVALID, "%s: sequence %d: parent %d (an earlier sequence without a parent, or -1)", fn, b, par);
+    if (par >= 0 && caches && caches[b])
+      return e->fail(SD_ERR_INVALID, "%s: sequence %d continues both a snapshot and sequence %d", fn, b, par);
+    if (par >= 0) tree = true, has_child[par] = 1;
+    else nroot++;
+    const sd_snapshot* c = par < 0 && caches ? caches[b] : nullptr;
+    if (!c && par < 0 && fork) return e->fail(SD_ERR_INVALID, "%s: question %d has no snapshot (the questions continue one)", fn, b);
     if (c && c->owner != e) return e->fail(SD_ERR_INVALID, "snapshot belongs to another engine");
-    const int p = c ? c->len : 0;
+    const int p = par >= 0 ? pl[par] + lens[par] : (c ? c->len : 0);
+    pl[b] = p;
     if (lens[b] <= 0 || p + lens[b] > SD_CONTEXT)
       return e->fail(SD_ERR_INVALID, "sequence %d: context of %d tokens: must be %d to %d", b, p + lens[b], p + 1, SD_CONTEXT);
     if (nrows[b] < 0) return e->fail(SD_ERR_INVALID, "sequence %d: negative row count", b);
@@ -1075,9 +1123,10 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
     max_chunks = std::max(max_chunks, ((int)lens[b] + 63) / 64);
   }
   if (T > (1 << 16)) return e->fail(SD_ERR_INVALID, "%s: %lld tokens in one call (at most 65536)", fn, T);
+  if (tree && keep) return e->fail(SD_ERR_INVALID, "%s: keep with parents in the pass", fn);
   long long ktot_ll = 0;  // rows of the gathered keys (continuations: every prefix with its own rows)
   if (max_p > 0)
-    for (int b = 0; b < nq; b++) ktot_ll += (caches && caches[b] ? caches[b]->len : 0) + lens[b];
+    for (int b = 0; b < nq; b++) ktot_ll += pl[b] + lens[b];
   if (ktot_ll > (1 << 24)) return e->fail(SD_ERR_INVALID, "%s: %lld key rows in one call", fn, ktot_ll);
   const int ktot = (int)ktot_ll;
   if (R > 0 && (!rows || !has_out)) return e->fail(SD_ERR_INVALID, "rows given without an output buffer");
@@ -1085,17 +1134,20 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
     for (long long i = 0; i < T; i++)
       if (ids_host[i] >= (uint32_t)e->vocab)
         return e->fail(SD_ERR_INVALID, "token id %u out of range (vocab %d)", ids_host[i], e->vocab);
-  // long sequences (more than two 64-token chunks): the two-phase scan
-  const bool two_phase = max_chunks > 2;
+  // long sequences (more than two 64-token chunks): the two-phase scan (a tree pass: the fused scan,
+  // roots then children)
+  const bool two_phase = !tree && max_chunks > 2;
+  const bool outs = keep || tree;  // tables of new snapshots (a tree: the parents', written in the pass)
   // staged layout: pointer tables (8-byte words): states[n_lin][nq], hists[n_lin][nq], k[n_full][nq],
   // v[n_full][nq], with keep the same four for the new snapshots; then ints: tpos[T], tstart[T],
   // tseq[T], seq_off[nq], seq_len[nq], plen[nq], blk[2 nblk], rows[R], with the two-phase scan
   // chunk_tab[2 chunks], chunk0[nq], order[nq]; then ids[T] (host ids)
   const size_t per_set = (size_t)(2 * e->n_lin + 2 * e->n_full) * nq;
-  const size_t i0 = 2 * per_set * (keep ? 2 : 1);  // ints before the index arrays
+  const size_t i0 = 2 * per_set * (outs ? 2 : 1);  // ints before the index arrays
   const size_t n_idx = i0 + 3 * (size_t)T + 4 * (size_t)nq + 2 * (size_t)nblk + 2 * (size_t)nblk128;
   const size_t n_gdn = two_phase ? 2 * (size_t)chunks + 2 * (size_t)nq : 0;
-  const size_t n_all = packed_ints(e, T, nq, nblk + nblk128, R, keep, two_phase ? chunks : -1, ids_host != nullptr);
+  const size_t n_base = packed_ints(e, T, nq, nblk + nblk128, R, outs, two_phase ? chunks : -1, ids_host != nullptr);
+  const size_t n_all = n_base + (tree ? (size_t)nq : 0);  // a tree: gorder last
   {  // rows in range
     long long r = 0;
     for (int b = 0; b < nq; b++)
@@ -1111,13 +1163,13 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   const sd::Dims& d = e->dm;
   cudaStream_t st = e->stream;
   // the new snapshots (stream-ordered allocations, before the upload that names them)
+  // (a tree: the parents' new snapshots, freed after the pass in stream order)
   std::vector<std::unique_ptr<sd_snapshot>> fresh;
-  if (keep) {
+  if (outs) {
     fresh.resize(nq);
-    for (int b = 0; b < nq; b++) {
-      const int p = caches && caches[b] ? caches[b]->len : 0;
-      if ((rc = alloc_snapshot(e, p + lens[b], &fresh[b])) != SD_OK) return rc;
-    }
+    for (int b = 0; b < nq; b++)
+      if (keep || has_child[b])
+        if ((rc = alloc_snapshot(e, pl[b] + lens[b], &fresh[b])) != SD_OK) return rc;
   }
   const int slot = e->fk_next;
   e->fk_next = (slot + 1) % sd_engine::kForkSlots;
@@ -1126,7 +1178,9 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
     const void** pt = reinterpret_cast<const void**>(e->fk_pin[slot]);
     const size_t kb = (size_t)2 * e->n_lin * nq, vb = kb + (size_t)e->n_full * nq;
     for (int b = 0; b < nq; b++) {
-      const sd_snapshot* c = caches ? caches[b] : nullptr;
+      const int par = parent ? parent[b] : -1;
+      // a child reads its parent's new snapshot (written earlier in each layer)
+      const sd_snapshot* c = par >= 0 ? fresh[par].get() : (caches ? caches[b] : nullptr);
       for (int i = 0; i < e->n_lin; i++) {
         pt[(size_t)i * nq + b] = c ? c->state[i] : nullptr;
         pt[(size_t)(e->n_lin + i) * nq + b] = c ? c->hist[i] : nullptr;
@@ -1135,15 +1189,15 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
         pt[kb + (size_t)i * nq + b] = c ? c->k[i] : nullptr;
         pt[vb + (size_t)i * nq + b] = c ? c->v[i] : nullptr;
       }
-      if (keep) {
-        const sd_snapshot* o = fresh[b].get();
+      if (outs) {
+        const sd_snapshot* o = fresh[b].get();  // null: nothing written for this sequence
         for (int i = 0; i < e->n_lin; i++) {
-          pt[per_set + (size_t)i * nq + b] = o->state[i];
-          pt[per_set + (size_t)(e->n_lin + i) * nq + b] = o->hist[i];
+          pt[per_set + (size_t)i * nq + b] = o ? o->state[i] : nullptr;
+          pt[per_set + (size_t)(e->n_lin + i) * nq + b] = o ? o->hist[i] : nullptr;
         }
         for (int i = 0; i < e->n_full; i++) {
-          pt[per_set + kb + (size_t)i * nq + b] = o->k[i];
-          pt[per_set + vb + (size_t)i * nq + b] = o->v[i];
+          pt[per_set + kb + (size_t)i * nq + b] = o ? o->k[i] : nullptr;
+          pt[per_set + vb + (size_t)i * nq + b] = o ? o->v[i] : nullptr;
         }
       }
     }
@@ -1165,7 +1219,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
     int t = 0, k = 0, ch = 0;
     long long r = 0;
     for (int b = 0; b < nq; b++) {
-      const int p = caches && caches[b] ? caches[b]->len : 0;
+      const int p = pl[b];
       soff[b] = t, slen[b] = lens[b], plen[b] = p;
       for (int j = 0; j < lens[b]; j++) tpos[t + j] = p + j, tstart[t + j] = t, tseq[t + j] = b;
       for (int q0 = 0; q0 < lens[b]; q0 += 64, k++) blk[2 * k] = b, blk[2 * k + 1] = q0;
@@ -1193,6 +1247,17 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
     for (int b = 0; b < nq; b++) gofs[b] = (int)g, g += plen[b] + lens[b];
   }
   if (ids_host) memcpy(e->fk_pin[slot] + n_idx + R + n_gdn, ids_host, T * sizeof(uint32_t));
+  if (tree) {  // the scan's walk order: the roots, then the children, each longest first
+    int* go = e->fk_pin[slot] + n_base;
+    int k = 0;
+    for (int b = 0; b < nq; b++)
+      if (parent[b] < 0) go[k++] = b;
+    for (int b = 0; b < nq; b++)
+      if (parent[b] >= 0) go[k++] = b;
+    auto longer = [&](int a, int b) { return lens[a] > lens[b]; };
+    std::stable_sort(go, go + nroot, longer);
+    std::stable_sort(go + nroot, go + nq, longer);
+  }
   CK(cudaMemcpyAsync(e->fk_meta, e->fk_pin[slot], n_all * sizeof(int), cudaMemcpyHostToDevice, st));
   CK(cudaEventRecord(e->fk_ev[slot], st));
   if (timed) CK(cudaEventRecord(e->ev0, st));
@@ -1207,7 +1272,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
   fk.hists = reinterpret_cast<const __half* const*>(dp + (size_t)e->n_lin * nq);
   fk.kp = reinterpret_cast<const __half* const*>(dp + (size_t)2 * e->n_lin * nq);
   fk.vp = reinterpret_cast<const __half* const*>(dp + (size_t)(2 * e->n_lin + e->n_full) * nq);
-  if (keep) {
+  if (outs) {
     void* const* op = const_cast<void* const*>(dp + per_set);
     fk.s_out = reinterpret_cast<float* const*>(op);
     fk.h_out = reinterpret_cast<__half* const*>(op + (size_t)e->n_lin * nq);
@@ -1225,6 +1290,7 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
     fk.chunks = chunks;
     fk.two_phase = true;
   }
+  if (tree) fk.tree = true, fk.gorder = dm + n_base, fk.nroot = nroot;
   fk.nseq = nq, fk.nblk = nblk, fk.max_len = max_len, fk.max_p = max_p, fk.max_rows = max_rows, fk.pairs = pairs;
   fk.kt = e->fk_kv, fk.vt = e->fk_kv + (size_t)d.hk * T * d.hd;
   rc = run_layers(e, (int)T, max_p, true, (int)R, &fk);
@@ -1246,11 +1312,11 @@ int packed_enqueue(sd_engine* e, const char* fn, const sd_snapshot* const* cache
 // rotated torso (src/engine.rs:652-660). On a failure after the enqueue the new snapshots are freed.
 int batch_host(sd_engine* e, const char* fn, const sd_snapshot* const* caches, bool fork, const uint32_t* ids,
                const int32_t* lens, int32_t nq, const int32_t* rows, const int32_t* nrows, bool keep, float* hidden_out,
-               sd_snapshot** snaps_out, double* gpu_ms_out) {
+               sd_snapshot** snaps_out, double* gpu_ms_out, const int32_t* parent = nullptr) {
   if (!ids) return e->fail(SD_ERR_INVALID, "%s: no token ids", fn);
   long long R = 0;
   int rc = packed_enqueue(e, fn, caches, fork, ids, nullptr, lens, nq, rows, nrows, keep, snaps_out, hidden_out != nullptr,
-                          true, &R);
+                          true, &R, parent);
   if (rc != SD_OK) return rc;
   const sd::Dims& d = e->dm;
   cudaStream_t st = e->stream;
@@ -1636,6 +1702,18 @@ int sd_forward_batch_dev(sd_engine* e, const sd_snapshot* const* caches, const u
   return SD_OK;
 }
 
+int sd_forward_tree_dev(sd_engine* e, const sd_snapshot* const* caches, const int32_t* parent, const uint32_t* ids_dev,
+                        const int32_t* lens, int32_t nseq, const int32_t* rows, const int32_t* nrows, float* hidden_dev) {
+  if (!e) return SD_ERR_INVALID;
+  if (!parent) return e->fail(SD_ERR_INVALID, "sd_forward_tree: no parent table");
+  long long R = 0;
+  int rc = packed_enqueue(e, "sd_forward_tree", caches, false, nullptr, ids_dev, lens, nseq, rows, nrows, false, nullptr,
+                          hidden_dev != nullptr, false, &R, parent);
+  if (rc != SD_OK) return rc;
+  if (R > 0) CK(cudaMemcpyAsync(hidden_dev, e->out, (size_t)R * e->dm.d * 4, cudaMemcpyDeviceToDevice, e->stream));
+  return SD_OK;
+}
+
 int sd_forward_dev(sd_engine* e, const uint32_t* ids_dev, int32_t l, const int32_t* rows_dev, int32_t nrows,
                    const sd_snapshot* cache, int32_t keep, float* hidden_dev, sd_snapshot** snapshot_out) {
   if (!e) return SD_ERR_INVALID;
@@ -1844,6 +1922,54 @@ int sd_forward_fork_multi_probs(sd_engine* e, const sd_snapshot* const* caches, 
   double* probs = nullptr;
   long long P = 0;
   if ((rc = enqueue_head(e, fn, h, e->out, nrows, nq, temperatures, nullptr, &probs, &P)) != SD_OK) return rc;
+  if (e->hd_pin_doubles < (size_t)P) {
+    CK(cudaStreamSynchronize(e->stream));
+    cudaFreeHost(e->hd_pin);
+    e->hd_pin = nullptr, e->hd_pin_doubles = 0;
+    const size_t cap = std::max<size_t>((size_t)P, 4096);
+    CK(cudaMallocHost(&e->hd_pin, cap * sizeof(double)));
+    e->hd_pin_doubles = cap;
+  }
+  CK(cudaMemcpyAsync(e->hd_pin, probs, (size_t)P * sizeof(double), cudaMemcpyDeviceToHost, e->stream));
+  if ((rc = sync_engine(e)) != SD_OK) return rc;
+  memcpy(probs_out, e->hd_pin, (size_t)P * sizeof(double));
+  return SD_OK;
+}
+
+int sd_forward_tree(sd_engine* e, const sd_snapshot* const* caches, const int32_t* parent, const uint32_t* ids,
+                    const int32_t* lens, int32_t nseq, const int32_t* rows, const int32_t* nrows, float* hidden_out) {
+  if (!e) return SD_ERR_INVALID;
+  if (!parent) return e->fail(SD_ERR_INVALID, "sd_forward_tree: no parent table");
+  return batch_host(e, "sd_forward_tree", caches, false, ids, lens, nseq, rows, nrows, false, hidden_out, nullptr, nullptr,
+                    parent);
+}
+
+int sd_forward_tree_probs(sd_engine* e, const sd_snapshot* const* caches, const int32_t* parent, const uint32_t* ids,
+                          const int32_t* lens, int32_t nseq, const int32_t* rows, const int32_t* nrows, const sd_head* h,
+                          const double* temperatures, double* probs_out) {
+  if (!e) return SD_ERR_INVALID;
+  const char* fn = "sd_forward_tree_probs";
+  if (!parent || !ids || !lens || !nrows || !probs_out) return e->fail(SD_ERR_INVALID, "%s: null argument", fn);
+  if (!h || !temperatures) return e->fail(SD_ERR_INVALID, "%s: no head", fn);
+  if (h->d != e->dm.d) return e->fail(SD_ERR_INVALID, "%s: head of width %d on a torso of %d", fn, h->d, e->dm.d);
+  if (nseq <= 0 || nseq > 4096) return e->fail(SD_ERR_INVALID, "%s: %d sequences", fn, nseq);
+  // the head runs over the sequences with rows (their options and the answer row), in order
+  std::vector<int32_t> hn;
+  std::vector<double> ht;
+  for (int i = 0; i < nseq; i++) {
+    if (nrows[i] == 0) continue;
+    if (nrows[i] < 2) return e->fail(SD_ERR_INVALID, "%s: sequence %d has %d rows (none, or options and the answer)", fn, i, nrows[i]);
+    hn.push_back(nrows[i]);
+    ht.push_back(temperatures[i]);
+  }
+  if (hn.empty()) return e->fail(SD_ERR_INVALID, "%s: no sequence has rows", fn);
+  if (!rows) return e->fail(SD_ERR_INVALID, "%s: null argument", fn);
+  long long R = 0;
+  int rc = packed_enqueue(e, fn, caches, false, ids, nullptr, lens, nseq, rows, nrows, false, nullptr, true, true, &R, parent);
+  if (rc != SD_OK) return rc;
+  double* probs = nullptr;
+  long long P = 0;
+  if ((rc = enqueue_head(e, fn, h, e->out, hn.data(), (int32_t)hn.size(), ht.data(), nullptr, &probs, &P)) != SD_OK) return rc;
   if (e->hd_pin_doubles < (size_t)P) {
     CK(cudaStreamSynchronize(e->stream));
     cudaFreeHost(e->hd_pin);

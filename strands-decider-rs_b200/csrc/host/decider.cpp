@@ -170,6 +170,13 @@ struct sd_decider {
     if (rc != SD_OK) throw std::runtime_error(sd_engine_last_error(engine));
   }
 
+  // Whether a request fits one tree pass (at most 65536 tokens and 4096 sequences per pass).
+  static bool fits_tree(const Prepared& p) {
+    size_t tokens = p.st.ids.size();
+    for (const auto& q : p.qs) tokens += q.ids.size();
+    return tokens <= 65536 && p.qs.size() < 4096;
+  }
+
   // `Decider::run` (src/lib.rs:156-208): the answers, in question order, and the usage count.
   sd::pj::Value run(const sd::pj::Value& state, const std::vector<std::pair<std::string, sd::prompt::Question>>& named) {
     const Prepared p = prepare(state, named);
@@ -186,6 +193,26 @@ struct sd_decider {
       check(sd_forward(engine, ids.data(), (int32_t)ids.size(), rows.data(), (int32_t)rows.size(), nullptr, 0, hidden.data(),
                        nullptr, nullptr));
       probs[0] = head_probs(p, 0, hidden.data(), rows.size());
+    } else if (fits_tree(p)) {
+      // the state and every question in one packed pass, each question continuing the state
+      std::vector<uint32_t> ids(p.st.ids);
+      std::vector<int32_t> lens{(int32_t)ns}, parent{-1}, rows, nrows{0};
+      for (size_t i = 0; i < p.qs.size(); i++) {
+        ids.insert(ids.end(), p.qs[i].ids.begin(), p.qs[i].ids.end());
+        lens.push_back((int32_t)p.qs[i].ids.size());
+        parent.push_back(0);
+        for (size_t o : p.options[i]) rows.push_back((int32_t)o);
+        rows.push_back((int32_t)p.qs[i].ids.size() - 1);
+        nrows.push_back((int32_t)p.options[i].size() + 1);
+      }
+      std::vector<float> hidden(rows.size() * (size_t)d);
+      check(sd_forward_tree(engine, nullptr, parent.data(), ids.data(), lens.data(), (int32_t)lens.size(), rows.data(),
+                            nrows.data(), hidden.data()));
+      size_t at = 0;
+      for (size_t i = 0; i < p.qs.size(); i++) {
+        probs[i] = head_probs(p, i, hidden.data() + at * d, (size_t)nrows[i + 1]);
+        at += nrows[i + 1];
+      }
     } else {
       sd_snapshot* prefix = nullptr;
       check(sd_forward(engine, p.st.ids.data(), (int32_t)ns, nullptr, 0, nullptr, 1, nullptr, &prefix, nullptr));

@@ -140,8 +140,10 @@ class Decider:
 
     def _run(self, state, named) -> Response:
         """`Decider::run` (`src/lib.rs:156-208`): one forward for a single question; otherwise the
-        state once with a snapshot, then the questions continued from it, MAX_BATCH at a time in one
-        batched fork each (`sd_forward_fork`; the reference runs them one after another)."""
+        state and every question in one tree pass, each question continuing the state
+        (`sd_forward_tree`; the reference runs the state with a snapshot, then the questions one after
+        another), or, past one pass's limits, the state once with a snapshot, then the questions
+        continued from it, MAX_BATCH at a time in one batched fork each (`sd_forward_fork`)."""
         t0 = time.perf_counter()
         rendered, sids, qencs, options = self.encode(state, named)
         t1 = time.perf_counter()
@@ -154,6 +156,12 @@ class Decider:
             out = self.engine.forward(ids, rows)
             probs = self.head.probs(out.hidden, d, self._temperature(rendered[0]))
             answers.append((named[0][0], prompt.to_answer(rendered[0], probs, smooth)))
+        elif len(sids) + sum(len(q.ids) for q in qencs) <= 65536 and len(qencs) < 4096:
+            rows = [[]] + [list(options[i]) + [len(qencs[i].ids) - 1] for i in range(len(qencs))]
+            hidden = self.engine.forward_tree(None, [-1] + [0] * len(qencs), [sids] + [q.ids for q in qencs], rows)
+            for i in range(len(qencs)):
+                probs = self.head.probs(hidden[i + 1], d, self._temperature(rendered[i]))
+                answers.append((named[i][0], prompt.to_answer(rendered[i], probs, smooth)))
         else:
             prefix = self.engine.forward(sids, [], keep=True).snapshot
             try:

@@ -72,6 +72,9 @@ def lib() -> C.CDLL:
         L.sd_head_probs_dev.argtypes = [vp, vp, vp, vp, i32, vp, vp]
         L.sd_decode_scales.argtypes = [vp, i32, i32, vp, vp]
         L.sd_forward_fork_multi_probs.argtypes = [vp, vp, vp, vp, i32, vp, vp, vp, vp, vp]
+        L.sd_forward_tree.argtypes = [vp, vp, vp, vp, vp, i32, vp, vp, vp]
+        L.sd_forward_tree_probs.argtypes = [vp, vp, vp, vp, vp, i32, vp, vp, vp, vp, vp]
+        L.sd_forward_tree_dev.argtypes = [vp, vp, vp, vp, vp, i32, vp, vp, vp]
         L.sd_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]
         L.sd_attention_batch.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp]
         L.sd_attention_split.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp,
@@ -252,6 +255,54 @@ class Engine:
                                                  head._h, _ptr(temps), _ptr(probs)),
                "sd_forward_fork_multi_probs", self._h)
         return np.split(probs, np.cumsum(nrows - 1)[:-1]) if len(lens) > 1 else [probs]
+
+    def _tree_args(self, caches, parents, ids_list, rows_list):
+        n = len(ids_list)
+        lens = np.array([len(x) for x in ids_list], np.int32)
+        nrows = np.array([len(r) for r in rows_list], np.int32)
+        par = np.ascontiguousarray(parents, np.int32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(x, np.uint32) for x in ids_list]), np.uint32)
+        rows = np.ascontiguousarray(np.concatenate([np.asarray(r, np.int32) for r in rows_list] + [np.zeros(0, np.int32)]),
+                                    np.int32)
+        cs = None if caches is None else (C.c_void_p * n)(*[c._h if c is not None else None for c in caches])
+        return n, lens, nrows, par, ids, rows, cs
+
+    def forward_tree(self, caches, parents, ids_list, rows_list):
+        """`sd_forward_tree`: one packed pass in which sequence b continues caches[b] (None: fresh) or,
+        with parents[b] >= 0, the earlier sequence parents[b] of the same pass (a request's questions
+        after its state). Returns the hidden rows of each sequence."""
+        n, lens, nrows, par, ids, rows, cs = self._tree_args(caches, parents, ids_list, rows_list)
+        hidden = np.zeros((int(nrows.sum()), self.hidden_size()), np.float32)
+        _check(lib().sd_forward_tree(self._h, cs, _ptr(par), _ptr(ids), _ptr(lens), n, _ptr(rows) if len(rows) else None,
+                                     _ptr(nrows), _ptr(hidden) if len(rows) else None),
+               "sd_forward_tree", self._h)
+        return np.split(hidden, np.cumsum(nrows)[:-1]) if n > 1 else [hidden]
+
+    def forward_tree_dev(self, caches, parents, ids_dev: int, lens, rows_list, hidden_dev: int | None):
+        """`sd_forward_tree_dev`: forward_tree with the ids already on the GPU (int32, back to back) and
+        the rows written to ``hidden_dev``, queued on the engine's stream."""
+        n = len(lens)
+        lens = np.ascontiguousarray(lens, np.int32)
+        nrows = np.array([len(r) for r in rows_list], np.int32)
+        par = np.ascontiguousarray(parents, np.int32)
+        rows = np.ascontiguousarray(np.concatenate([np.asarray(r, np.int32) for r in rows_list] + [np.zeros(0, np.int32)]),
+                                    np.int32)
+        cs = None if caches is None else (C.c_void_p * n)(*[c._h if c is not None else None for c in caches])
+        _check(lib().sd_forward_tree_dev(self._h, cs, _ptr(par), ids_dev, _ptr(lens), n, _ptr(rows) if len(rows) else None,
+                                         _ptr(nrows), hidden_dev),
+               "sd_forward_tree_dev", self._h)
+
+    def forward_tree_probs(self, caches, parents, ids_list, rows_list, head: "Head", temperatures):
+        """`sd_forward_tree_probs`: the tree pass of forward_tree, then the pointer head on the GPU over
+        the sequences with rows (options then the answer row); returns their probabilities in order."""
+        n, lens, nrows, par, ids, rows, cs = self._tree_args(caches, parents, ids_list, rows_list)
+        temps = np.ascontiguousarray(np.broadcast_to(np.asarray(temperatures, np.float64), (n,)))
+        asked = nrows[nrows > 0]
+        probs = np.zeros(int(asked.sum()) - len(asked), np.float64)
+        _check(lib().sd_forward_tree_probs(self._h, cs, _ptr(par), _ptr(ids), _ptr(lens), n, _ptr(rows), _ptr(nrows),
+                                           head._h, _ptr(temps), _ptr(probs)),
+               "sd_forward_tree_probs", self._h)
+        return np.split(probs, np.cumsum(asked - 1)[:-1]) if len(asked) > 1 else [probs]
 
     def head_probs_dev(self, head: "Head", hidden_dev: int, nrows, temperatures, probs_dev: int):
         """`sd_head_probs_dev`: the pointer head over questions' rows already on the GPU (question b:
