@@ -246,10 +246,11 @@ struct sd_decider {
     return respond(p, probs);
   }
 
-  // Many requests at once, as a server answers concurrent ones: every request's first forward (its
-  // state, kept as a snapshot; or, with a single question, state and question together, as
-  // `Decider::run` does) in packed passes (sd_forward_batch), then every question continuing its
-  // request's snapshot in packed forks with the pointer head on the GPU (sd_forward_fork_multi_probs).
+  // Many requests at once, as a server answers concurrent ones: whole requests in packed tree passes
+  // (sd_forward_tree_probs: each request's state, or with a single question state and question
+  // together as `Decider::run` does, then its questions continuing it in the same pass), with the
+  // pointer head on the GPU. A request too long for one pass takes two: its state kept as a snapshot
+  // (sd_forward_batch), then its questions continuing it in packed forks (sd_forward_fork_multi_probs).
   // Each request's answers equal its own `run` up to f32 summation order. out[i]: the response, or {"error": message} for a request that
   // failed (invalid, too long, or a failed pass of the torso).
   std::vector<sd::pj::Value> run_batch(const std::vector<const sd::pj::Value*>& states,
@@ -275,7 +276,76 @@ struct sd_decider {
     auto fail_all = [&](const std::vector<size_t>& group, const std::string& msg) {
       for (size_t r : group) errors[r] = msg;
     };
-    // pass 1: one sequence per request
+    // tree passes: whole requests, as many as one pass holds
+    {
+      std::vector<size_t> group;
+      size_t tokens = 0, seqs = 0;
+      auto flush = [&]() {
+        if (group.empty()) return;
+        std::vector<uint32_t> ids;
+        std::vector<int32_t> lens, parent, rows, nrows;
+        std::vector<double> temps;
+        std::vector<std::pair<size_t, size_t>> asked;  // (request, question) of each sequence with rows
+        for (size_t r : group) {
+          const Prepared& p = prep[r];
+          const size_t ns = p.st.ids.size();
+          const int32_t root = (int32_t)lens.size();
+          ids.insert(ids.end(), p.st.ids.begin(), p.st.ids.end());
+          parent.push_back(-1);
+          if (p.qs.size() == 1) {
+            ids.insert(ids.end(), p.qs[0].ids.begin(), p.qs[0].ids.end());
+            for (size_t o : p.options[0]) rows.push_back((int32_t)(ns + o));
+            rows.push_back((int32_t)(ns + p.qs[0].ids.size()) - 1);
+            nrows.push_back((int32_t)p.options[0].size() + 1);
+            lens.push_back((int32_t)(ns + p.qs[0].ids.size()));
+            temps.push_back(temperature(p.rendered[0].kind));
+            asked.emplace_back(r, 0);
+            continue;
+          }
+          lens.push_back((int32_t)ns);
+          nrows.push_back(0);
+          temps.push_back(1.0);
+          for (size_t i = 0; i < p.qs.size(); i++) {
+            ids.insert(ids.end(), p.qs[i].ids.begin(), p.qs[i].ids.end());
+            lens.push_back((int32_t)p.qs[i].ids.size());
+            parent.push_back(root);
+            for (size_t o : p.options[i]) rows.push_back((int32_t)o);
+            rows.push_back((int32_t)p.qs[i].ids.size() - 1);
+            nrows.push_back((int32_t)p.options[i].size() + 1);
+            temps.push_back(temperature(p.rendered[i].kind));
+            asked.emplace_back(r, i);
+          }
+        }
+        std::vector<double> all(rows.size() - asked.size());
+        const int rc = sd_forward_tree_probs(engine, nullptr, parent.data(), ids.data(), lens.data(), (int32_t)lens.size(),
+                                             rows.data(), nrows.data(), head, temps.data(), all.data());
+        if (rc != SD_OK) {
+          fail_all(group, sd_engine_last_error(engine));
+        } else {
+          size_t at = 0;
+          for (const auto& rq : asked) {
+            const size_t k = prep[rq.first].options[rq.second].size();
+            probs[rq.first][rq.second].assign(all.begin() + at, all.begin() + at + k);
+            at += k;
+          }
+        }
+        group.clear();
+        tokens = seqs = 0;
+      };
+      for (size_t r = 0; r < n; r++) {
+        if (!errors[r].empty() || !fits_tree(prep[r])) continue;
+        const Prepared& p = prep[r];
+        size_t len = p.st.ids.size();
+        for (const auto& q : p.qs) len += q.ids.size();
+        const size_t ns = p.qs.size() == 1 ? 1 : 1 + p.qs.size();
+        if (tokens + len > kPassTokens || seqs + ns > kPassSeqs) flush();
+        group.push_back(r);
+        tokens += len;
+        seqs += ns;
+      }
+      flush();
+    }
+    // requests too long for one tree pass. pass 1: one sequence per request
     {
       std::vector<size_t> group;
       size_t tokens = 0;
@@ -325,7 +395,7 @@ struct sd_decider {
         tokens = 0;
       };
       for (size_t r = 0; r < n; r++) {
-        if (!errors[r].empty()) continue;
+        if (!errors[r].empty() || fits_tree(prep[r])) continue;
         const Prepared& p = prep[r];
         const size_t len = p.st.ids.size() + (p.qs.size() == 1 ? p.qs[0].ids.size() : 0);
         if (tokens + len > kPassTokens || group.size() == kPassSeqs) flush();
